@@ -1,0 +1,278 @@
+/*
+ * opt_decode.c -- oracle for the opt-125m greedy decode (TEST INFRASTRUCTURE ONLY; see
+ * oracle.h).  Restates rust/npu-whisper/src/bin/opt125m_decode.rs:
+ *   Lin::load (41-60) / Lin::fwd (106-124), Opt::step (252-293), Opt::generate (296-315).
+ *
+ * Two numerics modes:
+ *  OR_MODE_REF_F32  the reference host path run with OPT_INT8: f32 activations, the six
+ *                   Lin layers int8 (per-output-column scale), f32 LM head, f32 KV.
+ *  OR_MODE_DEVICE   the B200 engine's numerics: LN outputs / attention context / FFN hidden
+ *                   rounded to bf16 before each GEMV, K and V stored as bf16, q scaled then
+ *                   rounded to bf16, every int8 GEMV computed as the exact integer dot of the
+ *                   22-bit fixed-point activation (or_limbs) rounded once to f32, int8 LM head
+ *                   (same quantiser, per vocab row), residual stream f32.
+ *
+ * The GEMVs are parallelised over output columns with OpenMP; each output keeps the
+ * reference's k-ascending summation order, so results do not depend on the thread count.
+ */
+#include "oracle.h"
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+typedef struct {
+    const float *w;  /* F32 mode: the unquantised [K,N] weight */
+    int8_t *q;       /* REF: [K,N] (reference layout); DEVICE: [N,K] (output-major) */
+    float *scale;    /* [N] */
+    const float *bias;
+    int K, N;
+} lin_t;
+
+struct or_opt {
+    or_opt_cfg cfg;
+    or_opt_weights w;
+    int mode, nthreads;
+    lin_t *lins;           /* [L][6]: q k v o fc1 fc2 */
+    int8_t *lm_q;          /* DEVICE: [V,D] */
+    float *lm_scale;       /* DEVICE: [V] */
+    float *kc, *vc;        /* [L][max_ctx][D] (DEVICE: values already bf16-rounded) */
+    int max_ctx;
+};
+
+static void lin_init(lin_t *l, const float *w, const float *b, int K, int N, int mode) {
+    l->K = K; l->N = N; l->bias = b; l->w = w;
+    if (mode == OR_MODE_F32) return;
+    l->q = (int8_t *)malloc((size_t)K * N);
+    l->scale = (float *)malloc(sizeof(float) * (size_t)N);
+    or_quant_i8_cols(w, K, N, l->q, l->scale);
+    if (mode == OR_MODE_DEVICE) {       /* transpose to [N,K] for the exact dot */
+        int8_t *t = (int8_t *)malloc((size_t)K * N);
+        for (int k = 0; k < K; k++)
+            for (int n = 0; n < N; n++) t[(size_t)n * K + k] = l->q[(size_t)k * N + n];
+        free(l->q);
+        l->q = t;
+    }
+}
+
+or_opt *or_opt_create(const or_opt_cfg *cfg, const or_opt_weights *w, int mode, int nthreads) {
+    or_opt *m = (or_opt *)calloc(1, sizeof(or_opt));
+    m->cfg = *cfg; m->w = *w; m->mode = mode; m->nthreads = nthreads > 0 ? nthreads : 1;
+    int L = cfg->n_layers, D = cfg->d_model, F = cfg->ffn;
+    m->lins = (lin_t *)calloc((size_t)L * 6, sizeof(lin_t));
+    for (int l = 0; l < L; l++) {
+        const or_opt_layer *ly = &w->layers[l];
+        lin_t *p = m->lins + l * 6;
+        lin_init(p + 0, ly->wq, ly->bq, D, D, mode);
+        lin_init(p + 1, ly->wk, ly->bk, D, D, mode);
+        lin_init(p + 2, ly->wv, ly->bv, D, D, mode);
+        lin_init(p + 3, ly->wo, ly->bo, D, D, mode);
+        lin_init(p + 4, ly->w1, ly->b1, D, F, mode);
+        lin_init(p + 5, ly->w2, ly->b2, F, D, mode);
+    }
+    if (mode == OR_MODE_DEVICE) {
+        /* The tied LM head as an int8 linear [D -> V]: output channel v is embedding row v,
+         * quantised with the Lin::load rule (per output channel, half away from zero). */
+        int V = cfg->vocab;
+        m->lm_q = (int8_t *)malloc((size_t)V * D);
+        m->lm_scale = (float *)malloc(sizeof(float) * (size_t)V);
+        for (int v = 0; v < V; v++) {
+            const float *row = w->emb_tok + (size_t)v * D;
+            float amax = 0.0f;
+            for (int d = 0; d < D; d++) amax = fmaxf(amax, fabsf(row[d]));
+            float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+            m->lm_scale[v] = s;
+            for (int d = 0; d < D; d++) {
+                float q = roundf(row[d] / s);
+                q = q < -127.0f ? -127.0f : (q > 127.0f ? 127.0f : q);
+                m->lm_q[(size_t)v * D + d] = (int8_t)q;
+            }
+        }
+    }
+    m->max_ctx = cfg->max_pos;
+    m->kc = (float *)malloc(sizeof(float) * (size_t)L * m->max_ctx * D);
+    m->vc = (float *)malloc(sizeof(float) * (size_t)L * m->max_ctx * D);
+    return m;
+}
+
+void or_opt_free(or_opt *m) {
+    if (!m) return;
+    for (int i = 0; i < m->cfg.n_layers * 6; i++) { free(m->lins[i].q); free(m->lins[i].scale); }
+    free(m->lins); free(m->lm_q); free(m->lm_scale); free(m->kc); free(m->vc); free(m);
+}
+
+const int8_t *or_opt_qweight(const or_opt *m, int layer, int which, float const **scale) {
+    if (which == 6) { if (scale) *scale = m->lm_scale; return m->lm_q; }
+    const lin_t *l = &m->lins[layer * 6 + which];
+    if (scale) *scale = l->scale;
+    return l->q;
+}
+
+/* Lin::fwd (int8 branch) parallel over blocks of output columns, k-outer inside a block. */
+static void lin_fwd_ref(const or_opt *m, const lin_t *l, const float *x, float *y) {
+    int K = l->K, N = l->N;
+    const int BLK = 256;
+    int nblk = (N + BLK - 1) / BLK;
+#pragma omp parallel for num_threads(m->nthreads) schedule(static)
+    for (int bi = 0; bi < nblk; bi++) {
+        int n0 = bi * BLK, n1 = n0 + BLK < N ? n0 + BLK : N;
+        for (int n = n0; n < n1; n++) y[n] = 0.0f;
+        for (int k = 0; k < K; k++) {
+            float a = x[k];
+            const int8_t *wr = l->q + (size_t)k * N;
+            for (int n = n0; n < n1; n++) { float p = a * (float)wr[n]; y[n] = y[n] + p; }
+        }
+        for (int n = n0; n < n1; n++) { float t = y[n] * l->scale[n]; y[n] = t + l->bias[n]; }
+    }
+}
+
+/* exact limbed int8 GEMV on an output-major [N,K] weight (device numerics) */
+static void gemv_exact(const or_opt *m, const int8_t *wq, const float *scale, const float *bias,
+                       int K, int N, const float *x, float *y) {
+    int8_t *a = (int8_t *)malloc((size_t)K * 3);
+    int8_t *b = a + K, *c = b + K;
+    int s = or_limbs(x, K, a, b, c);
+#pragma omp parallel for num_threads(m->nthreads) schedule(static)
+    for (int n = 0; n < N; n++) {
+        const int8_t *w = wq + (size_t)n * K;
+        int64_t A = 0, B = 0, C = 0;
+        for (int k = 0; k < K; k++) { A += a[k] * w[k]; B += b[k] * w[k]; C += c[k] * w[k]; }
+        int64_t S = A * 65536 + B * 256 + C;
+        float t = ldexpf((float)S, -s);
+        t = t * scale[n];
+        y[n] = t + (bias ? bias[n] : 0.0f);
+    }
+    free(a);
+}
+
+/* Lin::fwd f32 branch (opt125m_decode.rs:125-128): y = x.W + b, k ascending. */
+static void lin_fwd_f32(const or_opt *m, const lin_t *l, const float *x, float *y) {
+    int K = l->K, N = l->N;
+#pragma omp parallel for num_threads(m->nthreads) schedule(static)
+    for (int n = 0; n < N; n++) {
+        float s = 0.0f;
+        for (int k = 0; k < K; k++) s += x[k] * l->w[(size_t)k * N + n];
+        y[n] = s + l->bias[n];
+    }
+}
+
+static void lin_apply(const or_opt *m, const lin_t *l, const float *x, float *y) {
+    if (m->mode == OR_MODE_F32) lin_fwd_f32(m, l, x, y);
+    else if (m->mode == OR_MODE_DEVICE) gemv_exact(m, l->q, l->scale, l->bias, l->K, l->N, x, y);
+    else lin_fwd_ref(m, l, x, y);
+}
+
+/* Opt::step (opt125m_decode.rs:252-293) for one token at position `pos`. */
+static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_logits) {
+    const or_opt_cfg *c = &m->cfg;
+    int D = c->d_model, H = c->n_heads, HD = c->head_dim, F = c->ffn, V = c->vocab;
+    int dev = m->mode == OR_MODE_DEVICE;
+    float *x = (float *)malloc(sizeof(float) * (size_t)(8 * D + F + pos + 1));
+    float *h = x + D, *q = h + D, *kn = q + D, *vn = kn + D, *ctx = vn + D, *o = ctx + D,
+          *xr = o + D, *f = xr + D, *sc = f + F;
+    const float scale = 0.125f;   /* (HD as f32).powf(-0.5) for HD = 64 */
+    for (int d = 0; d < D; d++)
+        x[d] = m->w.emb_tok[(size_t)id * D + d] + m->w.emb_pos[(size_t)(pos + 2) * D + d];
+    for (int l = 0; l < c->n_layers; l++) {
+        const or_opt_layer *ly = &m->w.layers[l];
+        lin_t *lin = m->lins + l * 6;
+        or_layer_norm(x, ly->ln1_w, ly->ln1_b, 1, D, c->eps, h);
+        if (dev) or_bf16_round_n(h, h, (size_t)D);
+        lin_apply(m, &lin[0], h, q);
+        lin_apply(m, &lin[1], h, kn);
+        lin_apply(m, &lin[2], h, vn);
+        for (int d = 0; d < D; d++) q[d] = q[d] * scale;
+        if (dev) { or_bf16_round_n(q, q, D); or_bf16_round_n(kn, kn, D); or_bf16_round_n(vn, vn, D); }
+        float *kc = m->kc + (size_t)l * m->max_ctx * D, *vc = m->vc + (size_t)l * m->max_ctx * D;
+        memcpy(kc + (size_t)pos * D, kn, sizeof(float) * D);
+        memcpy(vc + (size_t)pos * D, vn, sizeof(float) * D);
+        int tk = pos + 1;
+        for (int hh = 0; hh < H; hh++) {
+            int c0 = hh * HD;
+            if (!dev) {
+                /* reference: sc = q.k^T; mx; e = exp(sc - mx); sum; sc /= sum; ctx = sc.v */
+                float mx = -INFINITY;
+                for (int j = 0; j < tk; j++) {
+                    float s = 0.0f;
+                    for (int d = 0; d < HD; d++) s += q[c0 + d] * kc[(size_t)j * D + c0 + d];
+                    sc[j] = s; mx = fmaxf(mx, s);
+                }
+                float sum = 0.0f;
+                for (int j = 0; j < tk; j++) { float e = expf(sc[j] - mx); sc[j] = e; sum += e; }
+                for (int j = 0; j < tk; j++) sc[j] = sc[j] / sum;
+                for (int d = 0; d < HD; d++) {
+                    float s = 0.0f;
+                    for (int j = 0; j < tk; j++) s += sc[j] * vc[(size_t)j * D + c0 + d];
+                    ctx[c0 + d] = s;
+                }
+            } else {
+                /* device numerics: f32 scores and softmax; sums taken exactly (f64) and
+                 * rounded once, ctx rounded to bf16 for the output projection. */
+                float mx = -INFINITY;
+                for (int j = 0; j < tk; j++) {
+                    double s = 0.0;
+                    for (int d = 0; d < HD; d++) s += (double)q[c0 + d] * (double)kc[(size_t)j * D + c0 + d];
+                    sc[j] = (float)s; mx = fmaxf(mx, sc[j]);
+                }
+                double sum = 0.0;
+                for (int j = 0; j < tk; j++) { sc[j] = expf(sc[j] - mx); sum += sc[j]; }
+                for (int d = 0; d < HD; d++) {
+                    double s = 0.0;
+                    for (int j = 0; j < tk; j++) s += (double)sc[j] * (double)vc[(size_t)j * D + c0 + d];
+                    ctx[c0 + d] = or_bf16_round((float)(s / sum));
+                }
+            }
+        }
+        lin_apply(m, &lin[3], ctx, o);
+        for (int d = 0; d < D; d++) xr[d] = x[d] + o[d];
+        or_layer_norm(xr, ly->ln2_w, ly->ln2_b, 1, D, c->eps, h);
+        if (dev) or_bf16_round_n(h, h, (size_t)D);
+        lin_apply(m, &lin[4], h, f);
+        for (int i = 0; i < F; i++) f[i] = f[i] > 0.0f ? f[i] : 0.0f;
+        if (dev) or_bf16_round_n(f, f, (size_t)F);
+        lin_apply(m, &lin[5], f, o);
+        for (int d = 0; d < D; d++) x[d] = xr[d] + o[d];
+    }
+    if (want_logits) {
+        or_layer_norm(x, m->w.lnf_w, m->w.lnf_b, 1, D, c->eps, h);
+        if (dev) {
+            or_bf16_round_n(h, h, (size_t)D);
+            gemv_exact(m, m->lm_q, m->lm_scale, NULL, D, V, h, logits);
+        } else {
+#pragma omp parallel for num_threads(m->nthreads) schedule(static)
+            for (int v = 0; v < V; v++) {
+                const float *e = m->w.emb_tok + (size_t)v * D;
+                float s = 0.0f;
+                for (int d = 0; d < D; d++) s += h[d] * e[d];
+                logits[v] = s;
+            }
+        }
+    }
+    free(x);
+}
+
+/* Opt::generate (opt125m_decode.rs:296-315): prefill token by token, then greedy with
+ * max_by(partial_cmp) (last maximum wins).  With force_ids, step g feeds force_ids[g]
+ * instead of the argmax (teacher forcing, so logits stay comparable across numerics
+ * modes after a near-tie flips a token).  Logits are only needed for the last prompt
+ * token and each decoded token, so earlier prompt steps skip the LM head. */
+int or_opt_generate(or_opt *m, const int64_t *prompt, int n_prompt, int n_new,
+                    const int64_t *force_ids, int64_t *out_ids, float *logits_out) {
+    int V = m->cfg.vocab;
+    if (n_prompt < 1 || n_prompt + n_new > m->max_ctx) return -1;
+    float *logits = (float *)malloc(sizeof(float) * (size_t)V);
+    for (int p = 0; p < n_prompt; p++) opt_step(m, prompt[p], p, logits, p == n_prompt - 1);
+    int pos = n_prompt;
+    for (int g = 0; g < n_new; g++) {
+        int64_t next = or_argmax_last(logits, (size_t)V);
+        out_ids[g] = next;
+        if (logits_out) memcpy(logits_out + (size_t)g * V, logits, sizeof(float) * V);
+        if (g + 1 == n_new) break;
+        opt_step(m, force_ids ? force_ids[g] : next, pos, logits, 1);
+        pos++;
+    }
+    free(logits);
+    return 0;
+}

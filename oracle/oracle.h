@@ -1,0 +1,139 @@
+/*
+ * oracle.h -- CPU restatement of xdna-engine's host math for the fused transformer
+ * hot path.  TEST INFRASTRUCTURE ONLY: the parity tests, `__graft_entry__.smoke()` and
+ * the `cpu_baseline` / `--impl reference` legs of bench.py link this library as the
+ * checker.  The product (libxdna_b200.so) never links, loads or calls it.
+ *
+ * Every function names the reference file:line it restates (paths are relative to the
+ * xdna-engine source tree).  The reference is Rust (no toolchain here) plus numpy
+ * goldens, so this is a restatement, not a build of the reference; it is pinned against
+ * the reference's own known-answer tests and numpy goldens (tests/golden/).
+ */
+#ifndef XDNA_ORACLE_H
+#define XDNA_ORACLE_H
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- bf16 (rust/npu-xrt/src/lib.rs:809-818, rust/npu-asr-host/src/lib.rs:12-19) ---- */
+uint16_t or_f32_to_bf16_bits(float x);
+float or_bf16_bits_to_f32(uint16_t b);
+float or_bf16_round(float x);
+void or_bf16_round_n(const float *x, float *y, size_t n);
+void or_f32_to_bf16_n(const float *x, uint16_t *y, size_t n);
+
+/* ---- int8 weight quantisation ---------------------------------------------------- */
+/* per-output-column symmetric int8 of a [K,N] row-major weight, f32::round (half away
+ * from zero): rust/npu-whisper/src/bin/opt125m_decode.rs:41-60 */
+void or_quant_i8_cols(const float *w, int K, int N, int8_t *q, float *scale);
+/* per-output-row int8 of an [M,K] weight with np.round (half to even):
+ * route_b_kernels/decode_fused/gen_decode.py:158-165 (qrow) */
+void or_quant_i8_rows(const float *w, int M, int K, int8_t *q, float *scale);
+/* int8 GEMV exactly as Lin::fwd (opt125m_decode.rs:106-124): k-outer, f32 mul+add */
+void or_lin_i8_fwd(const float *x, const int8_t *q, const float *scale, const float *bias,
+                   int K, int N, float *y);
+
+/* ---- bfp16ebs8 block format (route_b_kernels/ffn_bfp16/golden_ffn_gemm.py:25-60) ---- */
+/* quantise `n` values in blocks of 8 (n % 8 == 0) -> fp32 values on the block grid */
+void or_bfp16_blocks(const float *x, float *y, size_t n);
+/* storage split: shared exponent e (quantum 2^(e-6)) and signed mantissa m (int16:
+ * the reference does not clamp, so |m| can reach 128) */
+void or_bfp16_pack(const float *x, size_t n, int16_t *mant, int8_t *exp);
+
+/* ---- norms -------------------------------------------------------------------------- */
+/* rust/npu-asr-host/src/lib.rs:79-110 (population var, f32 index-order sums) */
+void or_layer_norm(const float *x, const float *g, const float *b, int T, int D, float eps,
+                   float *y);
+/* rust/npu-asr/src/ctx_decode.rs:617-640: the f64 input normalisation of fused_norm_gemv */
+void or_ln_normalize_f64(const float *x, int K, float eps, float *y);
+void or_rms_normalize_f64(const float *x, int K, float eps, float *y);
+/* rust/npu-gemma/src/lib.rs:55-64: x * rsqrt(mean(x^2)+eps) * (1+w) */
+void or_gemma_rmsnorm(const float *x, const float *w, int D, float eps, float *y);
+
+/* ---- activations ---------------------------------------------------------------------- */
+float or_fast_exp_nonpos(float x);                 /* npu-asr-host/src/lib.rs:38-58 */
+float or_gelu_erf(float x);                        /* npu-asr-host/src/lib.rs:464-495 */
+float or_gelu_tanh(float x);                       /* gen_decode.py:509, npu-gemma lib.rs:68-77 */
+float or_sigmoid(float x);                         /* npu-asr-host/src/lib.rs:401-409 */
+float or_silu(float x);
+
+/* ---- attention ------------------------------------------------------------------------ */
+/* npu-asr-host/src/lib.rs:189-326: q,k,v [T, H*hd]; keys j >= valid_len masked */
+void or_mha(const float *q, const float *k, const float *v, int T, int H, int hd,
+            int round_probs, int valid_len, float *out);
+/* route_b_kernels/mha_decode/mha_decode.cc:90-168: single-query online softmax over
+ * a head's keys in tiles of `tkv` (the tile order the device kernel also follows) */
+void or_mha_tile_online(const float *q, const float *k, const float *v, int s, int hd,
+                        float scale, float *ctx);
+
+/* ---- greedy selection (rust/npu-whisper/src/bin/opt125m_decode.rs:303; whisper.rs:749-757) */
+int64_t or_argmax_last(const float *x, size_t n);   /* max_by(partial_cmp): last max wins */
+int64_t or_argmax_first(const float *x, size_t n);  /* strict '>': first max wins */
+
+/* ---- KV indexing (rust/npu-xrt/src/lib.rs:992-1004; whisper_decoder.rs:550-570) ---- */
+uint32_t or_kv_byte_offset(uint32_t base, uint32_t n_preceding, uint32_t head_dim);
+uint32_t or_softmax_len(uint32_t n_preceding);
+/* paged layout used by the device: page = [K|V][H][page_tokens][hd] bf16 */
+size_t or_paged_kv_index(const int32_t *page_table, int page_tokens, int H, int hd,
+                         int kv, int head, int pos, int d);
+
+/* ---- fixed-point activation limbs (device GEMV numerics; defined by this engine) ---- */
+/* x -> X = rint(x * 2^s) with s = 22 - E, max|x| < 2^E; X = a*2^16 + b*2^8 + c,
+ * a,b,c in [-128,127].  Returns s. */
+int or_limbs(const float *x, int K, int8_t *a, int8_t *b, int8_t *c);
+/* exact int8 dot of a limbed activation with an int8 weight column, rounded once to f32,
+ * then * scale + bias (separate f32 multiply and add). */
+void or_gemv_i8_exact(const float *x, const int8_t *wq_nk, const float *scale,
+                      const float *bias, int K, int N, float *y);
+
+/* ---- opt-125m greedy decode (rust/npu-whisper/src/bin/opt125m_decode.rs:252-315) ---- */
+typedef struct {
+    int n_layers, d_model, n_heads, head_dim, ffn, vocab, max_pos;
+    float eps;
+} or_opt_cfg;
+
+typedef struct {               /* layouts follow the reference's npy arrays */
+    const float *ln1_w, *ln1_b;          /* [D] */
+    const float *wq, *wk, *wv, *wo;      /* [D, D] as [K, N] */
+    const float *bq, *bk, *bv, *bo;      /* [D] */
+    const float *ln2_w, *ln2_b;          /* [D] */
+    const float *w1, *b1;                /* [D, F], [F] */
+    const float *w2, *b2;                /* [F, D], [D] */
+} or_opt_layer;
+
+typedef struct {
+    const float *emb_tok;      /* [V, D]; the LM head is tied: logits = x . emb_tok[v] */
+    const float *emb_pos;      /* [max_pos + 2, D] (position offset +2) */
+    const float *lnf_w, *lnf_b;
+    const or_opt_layer *layers;
+} or_opt_weights;
+
+enum {
+    OR_MODE_REF_F32 = 0,  /* the reference host path with OPT_INT8: f32 activations, int8
+                             Lin layers, f32 LM head (opt125m_decode.rs:106-124, 252-293) */
+    OR_MODE_DEVICE = 1,   /* the B200 engine's numerics: bf16 activations into every GEMV,
+                             bf16 KV cache, exact limbed int8 GEMV, int8 LM head */
+    OR_MODE_F32 = 2       /* the reference host path without OPT_INT8: every Lin is the f32
+                             x.W + b (opt125m_decode.rs:125-128); used to pin the model
+                             composition against the HF OPT implementation */
+};
+
+typedef struct or_opt or_opt;
+or_opt *or_opt_create(const or_opt_cfg *cfg, const or_opt_weights *w, int mode, int nthreads);
+void or_opt_free(or_opt *m);
+/* prefill prompt token by token, then greedy-decode n_new tokens (Opt::generate).
+ * force_ids (optional, [n_new]) replaces the fed-back argmax by force_ids[g] (teacher
+ * forcing); out_ids still receives each step's argmax.  logits_out (optional) receives
+ * the logits of each step, [n_new, V].  Returns 0, or -1 on bad sizes. */
+int or_opt_generate(or_opt *m, const int64_t *prompt, int n_prompt, int n_new,
+                    const int64_t *force_ids, int64_t *out_ids, float *logits_out);
+/* quantised weights as the engine sees them (for bit-exact checks) */
+const int8_t *or_opt_qweight(const or_opt *m, int layer, int which, float const **scale);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

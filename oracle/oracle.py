@@ -1,0 +1,255 @@
+"""ctypes binding of the CPU oracle (liboracle.so).
+
+TEST INFRASTRUCTURE ONLY.  Imported by tests/, `__graft_entry__.smoke()` and the
+`cpu_baseline` / `--impl reference` legs of bench.py as the checker; the product package
+never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+
+F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+I8P = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+I16P = np.ctypeslib.ndpointer(np.int16, flags="C_CONTIGUOUS")
+U16P = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+I64P = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
+
+MODE_REF_F32, MODE_DEVICE, MODE_F32 = 0, 1, 2
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(_HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = C.CDLL(path)
+        L.or_f32_to_bf16_n.argtypes = [F32P, U16P, C.c_size_t]
+        L.or_bf16_round_n.argtypes = [F32P, F32P, C.c_size_t]
+        L.or_bf16_round.argtypes = [C.c_float]
+        L.or_bf16_round.restype = C.c_float
+        L.or_quant_i8_cols.argtypes = [F32P, C.c_int, C.c_int, I8P, F32P]
+        L.or_quant_i8_rows.argtypes = [F32P, C.c_int, C.c_int, I8P, F32P]
+        L.or_lin_i8_fwd.argtypes = [F32P, I8P, F32P, C.c_void_p, C.c_int, C.c_int, F32P]
+        L.or_bfp16_blocks.argtypes = [F32P, F32P, C.c_size_t]
+        L.or_bfp16_pack.argtypes = [F32P, C.c_size_t, I16P, I8P]
+        L.or_layer_norm.argtypes = [F32P, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_float, F32P]
+        L.or_ln_normalize_f64.argtypes = [F32P, C.c_int, C.c_float, F32P]
+        L.or_rms_normalize_f64.argtypes = [F32P, C.c_int, C.c_float, F32P]
+        L.or_gemma_rmsnorm.argtypes = [F32P, F32P, C.c_int, C.c_float, F32P]
+        for fn in ("or_fast_exp_nonpos", "or_gelu_erf", "or_gelu_tanh", "or_sigmoid", "or_silu"):
+            getattr(L, fn).argtypes = [C.c_float]
+            getattr(L, fn).restype = C.c_float
+        L.or_mha.argtypes = [F32P, F32P, F32P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, F32P]
+        L.or_mha_tile_online.argtypes = [F32P, F32P, F32P, C.c_int, C.c_int, C.c_float, F32P]
+        L.or_argmax_last.argtypes = [F32P, C.c_size_t]
+        L.or_argmax_last.restype = C.c_int64
+        L.or_argmax_first.argtypes = [F32P, C.c_size_t]
+        L.or_argmax_first.restype = C.c_int64
+        L.or_kv_byte_offset.argtypes = [C.c_uint32] * 3
+        L.or_kv_byte_offset.restype = C.c_uint32
+        L.or_softmax_len.argtypes = [C.c_uint32]
+        L.or_softmax_len.restype = C.c_uint32
+        L.or_paged_kv_index.argtypes = [np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"),
+                                        C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.or_paged_kv_index.restype = C.c_size_t
+        L.or_limbs.argtypes = [F32P, C.c_int, I8P, I8P, I8P]
+        L.or_limbs.restype = C.c_int
+        L.or_gemv_i8_exact.argtypes = [F32P, I8P, F32P, C.c_void_p, C.c_int, C.c_int, F32P]
+        L.or_opt_create.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+        L.or_opt_create.restype = C.c_void_p
+        L.or_opt_free.argtypes = [C.c_void_p]
+        L.or_opt_generate.argtypes = [C.c_void_p, I64P, C.c_int, C.c_int, C.c_void_p, I64P, C.c_void_p]
+        L.or_opt_generate.restype = C.c_int
+        L.or_opt_qweight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.POINTER(C.c_float))]
+        L.or_opt_qweight.restype = C.POINTER(C.c_int8)
+        _LIB = L
+    return _LIB
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+# ---------------------------------------------------------------- scalar / vector wrappers
+def bf16_round(x):
+    x = _f32(x)
+    y = np.empty_like(x)
+    lib().or_bf16_round_n(x.ravel(), y.ravel(), x.size)
+    return y
+
+
+def f32_to_bf16_bits(x):
+    x = _f32(x)
+    y = np.empty(x.shape, np.uint16)
+    lib().or_f32_to_bf16_n(x.ravel(), y.ravel(), x.size)
+    return y
+
+
+def quant_i8_cols(w):
+    w = _f32(w)
+    K, N = w.shape
+    q = np.empty((K, N), np.int8)
+    s = np.empty(N, np.float32)
+    lib().or_quant_i8_cols(w, K, N, q, s)
+    return q, s
+
+
+def quant_i8_rows(w):
+    w = _f32(w)
+    M, K = w.shape
+    q = np.empty((M, K), np.int8)
+    s = np.empty(M, np.float32)
+    lib().or_quant_i8_rows(w, M, K, q, s)
+    return q, s
+
+
+def lin_i8_fwd(x, q, scale, bias=None):
+    x, scale = _f32(x), _f32(scale)
+    K, N = q.shape
+    y = np.empty(N, np.float32)
+    b = None if bias is None else _f32(bias)
+    lib().or_lin_i8_fwd(x, np.ascontiguousarray(q), scale, _ptr(b), K, N, y)
+    return y
+
+
+def bfp16_blocks(x):
+    x = _f32(x)
+    y = np.empty_like(x)
+    lib().or_bfp16_blocks(x.ravel(), y.ravel(), x.size)
+    return y
+
+
+def bfp16_pack(x):
+    x = _f32(x)
+    m = np.empty(x.size, np.int16)
+    e = np.empty(x.size // 8, np.int8)
+    lib().or_bfp16_pack(x.ravel(), x.size, m, e)
+    return m, e
+
+
+def layer_norm(x, g=None, b=None, eps=1e-5):
+    x = _f32(x)
+    T, D = x.shape
+    y = np.empty_like(x)
+    g = None if g is None else _f32(g)
+    b = None if b is None else _f32(b)
+    lib().or_layer_norm(x, _ptr(g), _ptr(b), T, D, eps, y)
+    return y
+
+
+def mha(q, k, v, n_heads, head_dim, round_probs, valid_len):
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    out = np.empty_like(q)
+    lib().or_mha(q, k, v, q.shape[0], n_heads, head_dim, int(round_probs), valid_len, out)
+    return out
+
+
+def limbs(x):
+    x = _f32(x)
+    K = x.size
+    a, b, c = (np.empty(K, np.int8) for _ in range(3))
+    s = lib().or_limbs(x, K, a, b, c)
+    return s, a, b, c
+
+
+def gemv_i8_exact(x, wq_nk, scale, bias=None):
+    x = _f32(x)
+    N, K = wq_nk.shape
+    y = np.empty(N, np.float32)
+    b = None if bias is None else _f32(bias)
+    lib().or_gemv_i8_exact(x, np.ascontiguousarray(wq_nk), _f32(scale), _ptr(b), K, N, y)
+    return y
+
+
+# ---------------------------------------------------------------- opt-125m decode
+class _Cfg(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("d_model", C.c_int), ("n_heads", C.c_int),
+                ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int),
+                ("max_pos", C.c_int), ("eps", C.c_float)]
+
+
+class _Layer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("ln1_w", "ln1_b", "wq", "wk", "wv", "wo", "bq", "bk",
+                                          "bv", "bo", "ln2_w", "ln2_b", "w1", "b1", "w2", "b2")]
+
+
+class _Weights(C.Structure):
+    _fields_ = [("emb_tok", C.c_void_p), ("emb_pos", C.c_void_p), ("lnf_w", C.c_void_p),
+                ("lnf_b", C.c_void_p), ("layers", C.c_void_p)]
+
+
+class OracleOpt:
+    """or_opt_* over numpy weights from xdna_engine_b200.synth.make_opt_weights."""
+
+    def __init__(self, cfg, weights, mode=MODE_DEVICE, nthreads=None):
+        self._keep = []
+
+        def p(a):
+            a = _f32(a)
+            self._keep.append(a)
+            return a.ctypes.data
+
+        self.cfg = cfg
+        c = _Cfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
+                 cfg.max_pos, cfg.eps)
+        layers = (_Layer * cfg.n_layers)()
+        for i, ly in enumerate(weights["layers"]):
+            for k in _Layer._fields_:
+                setattr(layers[i], k[0], p(ly[k[0]]))
+        w = _Weights(p(weights["emb_tok"]), p(weights["emb_pos"]), p(weights["lnf_w"]),
+                     p(weights["lnf_b"]), C.addressof(layers))
+        self._c, self._w, self._layers = c, w, layers
+        nt = nthreads or os.cpu_count() or 1
+        self._h = lib().or_opt_create(C.addressof(c), C.addressof(w), mode, nt)
+        self.mode = mode
+
+    def generate(self, prompt, n_new, want_logits=False, force=None):
+        prompt = np.ascontiguousarray(prompt, dtype=np.int64)
+        out = np.empty(n_new, np.int64)
+        lg = np.empty((n_new, self.cfg.vocab), np.float32) if want_logits else None
+        fc = None if force is None else np.ascontiguousarray(force, dtype=np.int64)
+        rc = lib().or_opt_generate(self._h, prompt, prompt.size, n_new, _ptr(fc), out, _ptr(lg))
+        if rc != 0:
+            raise RuntimeError("or_opt_generate failed")
+        return (out, lg) if want_logits else out
+
+    def qweight(self, layer, which):
+        """int8 weight + scale as the oracle quantised them (which: 0..5 q k v o fc1 fc2,
+        6 = LM head).  DEVICE mode layout: [N, K]."""
+        sp = C.POINTER(C.c_float)()
+        qp = lib().or_opt_qweight(self._h, layer, which, C.byref(sp))
+        D, F, V = self.cfg.d_model, self.cfg.ffn, self.cfg.vocab
+        shapes = [(D, D), (D, D), (D, D), (D, D), (D, F), (F, D), (D, V)]
+        K, N = shapes[which]
+        q = np.ctypeslib.as_array(qp, shape=(K * N,)).copy()
+        s = np.ctypeslib.as_array(sp, shape=(N,)).copy()
+        if self.mode == MODE_DEVICE:
+            return q.reshape(N, K), s
+        return q.reshape(K, N), s
+
+    def close(self):
+        if self._h:
+            lib().or_opt_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,137 @@
+#!/usr/bin/env python3
+"""Regenerate the committed golden fixtures under tests/golden/.
+
+Run in a container where the xdna-engine source tree is mounted (default
+/root/reference, override with XDNA_REF) and `transformers` is importable:
+
+    python tests/golden/make_golden.py
+
+It writes
+  bfp16_golden.npz  -- outputs of the reference's own numpy golden
+                       route_b_kernels/ffn_bfp16/golden_ffn_gemm.py (to_bf16, to_bfp16_blocks,
+                       gemm_bfp16), imported and run unchanged on seeded inputs;
+  opt_hf_golden.npz -- greedy tokens + per-step logits of HuggingFace OPTForCausalLM (the
+                       implementation the reference validates its opt-125m decode against,
+                       scripts/opt125m_reference.py) on a small seeded random-init OPT whose
+                       weights come from xdna_engine_b200.synth.make_opt_weights.
+The known-answer values of the reference's Rust unit tests are transcribed by hand into
+ref_kats.json (each entry cites its source file:line); this script does not touch that file.
+The GPU box never runs this script: the tests only read the .npz files.
+"""
+import importlib.util
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+REF = os.environ.get("XDNA_REF", "/root/reference")
+
+
+def bfp16_fixture():
+    path = os.path.join(REF, "route_b_kernels/ffn_bfp16/golden_ffn_gemm.py")
+    spec = importlib.util.spec_from_file_location("golden_ffn_gemm", path)
+    g = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(g)
+    rng = np.random.default_rng(20240611)
+    out = {}
+    # activations ~N(0,1) and weights ~N(0, 1/sqrt(K)) as the golden's run_case draws them,
+    # plus an N(0, 0.02) weight (the Whisper config's distribution) and edge rows.
+    a = rng.standard_normal((8, 128)).astype(np.float32)
+    b = (rng.standard_normal((128, 32)) / 11.3).astype(np.float32)
+    w02 = (rng.standard_normal((64, 128)) * 0.02).astype(np.float32)
+    edge = np.zeros((4, 64), np.float32)
+    edge[1, :8] = [1.0, -1.0, 0.5, 0.25, 127.0, -128.0, 1e-3, 3.0]
+    edge[2] = rng.standard_normal(64).astype(np.float32) * 1e-20
+    edge[3, ::8] = 2.0 ** np.arange(-4, 4, dtype=np.float32)
+    out["a"], out["b"], out["w02"], out["edge"] = a, b, w02, edge
+    out["a_bf16"] = g.to_bf16(a)
+    out["a_blocks_ax1"] = g.to_bfp16_blocks(g.to_bf16(a), axis=1)
+    out["b_blocks_ax0"] = g.to_bfp16_blocks(g.to_bf16(b), axis=0)
+    out["w02_blocks_ax0"] = g.to_bfp16_blocks(w02, axis=0)
+    out["edge_blocks_ax1"] = g.to_bfp16_blocks(edge, axis=1)
+    out["gemm_bfp16"] = g.gemm_bfp16(a, b)
+    out["gemm_fp32"] = g.gemm_fp32(a, b)
+    np.savez_compressed(os.path.join(HERE, "bfp16_golden.npz"), **out)
+    print("bfp16_golden.npz:", {k: v.shape for k, v in out.items()})
+
+
+OPT_SMALL = dict(n_layers=2, d_model=128, n_heads=2, head_dim=64, ffn=256, vocab=512,
+                 max_pos=64, eps=1e-5)
+OPT_SMALL_SEED = 7
+OPT_SMALL_STD = 0.08
+
+
+def opt_small_weights():
+    from xdna_engine_b200.synth import OptConfig, make_opt_weights
+    cfg = OptConfig(**OPT_SMALL)
+    return cfg, make_opt_weights(cfg, seed=OPT_SMALL_SEED, std=OPT_SMALL_STD, bias_std=0.05,
+                                 ln_std=0.1)
+
+
+def weights_checksum(w):
+    acc = np.float64(0.0)
+    for k in ("emb_tok", "emb_pos", "lnf_w", "lnf_b"):
+        acc += np.abs(w[k].astype(np.float64)).sum()
+    for ly in w["layers"]:
+        for v in ly.values():
+            acc += np.abs(v.astype(np.float64)).sum()
+    return acc
+
+
+def opt_hf_fixture():
+    import torch
+    from transformers import OPTConfig, OPTForCausalLM
+    cfg, w = opt_small_weights()
+    hc = OPTConfig(vocab_size=cfg.vocab, hidden_size=cfg.d_model, num_hidden_layers=cfg.n_layers,
+                   ffn_dim=cfg.ffn, num_attention_heads=cfg.n_heads,
+                   max_position_embeddings=cfg.max_pos, do_layer_norm_before=True,
+                   word_embed_proj_dim=cfg.d_model, activation_function="relu", dropout=0.0,
+                   attention_dropout=0.0, enable_bias=True, layer_norm_elementwise_affine=True,
+                   tie_word_embeddings=True, pad_token_id=1, bos_token_id=2, eos_token_id=2)
+    model = OPTForCausalLM(hc).eval().float()
+    sd = model.state_dict()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    new = {"model.decoder.embed_tokens.weight": t(w["emb_tok"]),
+           "model.decoder.embed_positions.weight": t(w["emb_pos"]),
+           "model.decoder.final_layer_norm.weight": t(w["lnf_w"]),
+           "model.decoder.final_layer_norm.bias": t(w["lnf_b"]),
+           "lm_head.weight": t(w["emb_tok"])}
+    names = {"wq": "self_attn.q_proj", "wk": "self_attn.k_proj", "wv": "self_attn.v_proj",
+             "wo": "self_attn.out_proj", "w1": "fc1", "w2": "fc2"}
+    bias = {"wq": "bq", "wk": "bk", "wv": "bv", "wo": "bo", "w1": "b1", "w2": "b2"}
+    for i, ly in enumerate(w["layers"]):
+        p = f"model.decoder.layers.{i}."
+        for k, n in names.items():
+            new[p + n + ".weight"] = t(ly[k].T)          # HF Linear is [out, in]
+            new[p + n + ".bias"] = t(ly[bias[k]])
+        new[p + "self_attn_layer_norm.weight"] = t(ly["ln1_w"])
+        new[p + "self_attn_layer_norm.bias"] = t(ly["ln1_b"])
+        new[p + "final_layer_norm.weight"] = t(ly["ln2_w"])
+        new[p + "final_layer_norm.bias"] = t(ly["ln2_b"])
+    missing = set(sd) - set(new)
+    assert not missing, missing
+    model.load_state_dict(new, strict=True)
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(2, cfg.vocab, size=10, dtype=np.int64)
+    n_new = 12
+    ids = torch.from_numpy(prompt)[None]
+    toks, logits = [], []
+    with torch.no_grad():
+        for _ in range(n_new):
+            lg = model(input_ids=ids).logits[0, -1].float().numpy()
+            nxt = int(np.argmax(lg))
+            toks.append(nxt)
+            logits.append(lg)
+            ids = torch.cat([ids, torch.tensor([[nxt]])], dim=1)
+    out = dict(prompt=prompt, tokens=np.array(toks, np.int64), logits=np.stack(logits),
+               checksum=np.float64(weights_checksum(w)))
+    np.savez_compressed(os.path.join(HERE, "opt_hf_golden.npz"), **out)
+    print("opt_hf_golden.npz: tokens", toks)
+
+
+if __name__ == "__main__":
+    bfp16_fixture()
+    opt_hf_fixture()
