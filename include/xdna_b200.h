@@ -1,0 +1,119 @@
+/*
+ * xdna_b200.h -- C ABI of the B200 backend for xdna-engine's fused transformer hot path.
+ *
+ * This library replaces the reference's device layer (rust/npu-xrt: shim/xrt_shim.h:16-113,
+ * src/lib.rs:46-158, 641-744) for the decode hot path.  Conventions follow the reference's C
+ * ABIs (rust/npu-capi/src/lib.rs:11-16, rust/npu-xrt/shim/xrt_shim.h:1-3): opaque handles,
+ * NULL / nonzero return on failure, and a thread-local message readable with
+ * xdna_last_error() until the next call on the same thread.  No entry point throws across
+ * the boundary.  Plain pointers and sizes only.
+ *
+ * Pointers documented as "device" must be CUDA device pointers; all others are host memory.
+ * `stream` arguments are cudaStream_t values passed as void* (NULL = the legacy stream).
+ */
+#ifndef XDNA_B200_H
+#define XDNA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- device (npu-xrt Device) */
+typedef struct XdnaDevice XdnaDevice;
+
+/* Number of usable sm_100 devices (0 if none).  Replaces shim_device_open's probe and
+ * npu_available (rust/npu-capi/src/lib.rs:22-25). */
+int xdna_device_count(void);
+/* Open device `ordinal`; NULL on error.  Replaces shim_device_open (xrt_shim.h:16). */
+XdnaDevice *xdna_device_open(int ordinal);
+void xdna_device_close(XdnaDevice *dev);
+/* Thread-local last error ("" if none).  Replaces shim_last_error (xrt_shim.h:113). */
+const char *xdna_last_error(void);
+
+/* ------------------------------------------------- weight quantisation (npu-weights / Lin) */
+/* Per-output-column symmetric int8 of a [K,N] row-major f32 weight, exactly Lin::load with
+ * OPT_INT8 (rust/npu-whisper/src/bin/opt125m_decode.rs:41-60): scale[n] = max_k|W[k,n]|/127
+ * (1.0 for an all-zero column), q = clamp(round_half_away(W/scale), -127, 127).  The result is
+ * written output-major, q_nk[n*K + k].  Returns 0. */
+int xdna_quant_i8_cols(const float *w, int K, int N, int8_t *q_nk, float *scale);
+
+/* ------------------------------------------------------------- op level (CtxDecode::gemv) */
+/* y[N] = dot(x, W[:,n]) * scale[n] + bias[n] on the GPU with the engine's exact int8 GEMV
+ * (activation as a 22-bit fixed-point vector split into int8 limbs, int8 tensor-core MMA,
+ * exact integer accumulation, one rounding).  Replaces CtxDecode::gemv / fused_norm_gemv's
+ * device dispatch (rust/npu-asr/src/ctx_decode.rs:325-369, 617-643).  x, q_nk, scale, bias
+ * (nullable) and y are host arrays; K must be a multiple of 256 and <= 3072, N a multiple
+ * of 8.  Returns 0, or -1 with xdna_last_error() set. */
+int xdna_gemv_i8(XdnaDevice *dev, const float *x, int K, const int8_t *q_nk, const float *scale,
+                 const float *bias, int N, float *y);
+
+/* ------------------------------------------------ opt-125m greedy decode (Opt::generate) */
+typedef struct {
+    int n_layers, d_model, n_heads, head_dim, ffn, vocab, max_pos;
+    float eps;
+} XdnaOptConfig;
+
+typedef struct {               /* f32, the reference's npy layouts: linear weights [K, N] */
+    const float *ln1_w, *ln1_b;
+    const float *wq, *wk, *wv, *wo;
+    const float *bq, *bk, *bv, *bo;
+    const float *ln2_w, *ln2_b;
+    const float *w1, *b1;      /* [D, F], [F] */
+    const float *w2, *b2;      /* [F, D], [D] */
+} XdnaOptLayer;
+
+typedef struct {
+    const float *emb_tok;      /* [V, D]; tied LM head */
+    const float *emb_pos;      /* [max_pos + 2, D]; position offset +2 */
+    const float *lnf_w, *lnf_b;
+    const XdnaOptLayer *layers;
+} XdnaOptWeights;
+
+typedef struct XdnaOptDecoder XdnaOptDecoder;
+
+/* Quantise (int8, per output channel, LM head included), pack and upload the model; the
+ * replacement of Opt::load + Lin::load (opt125m_decode.rs:41-60, 158-186).  max_ctx bounds
+ * prompt + generated tokens (<= max_pos); grid = CTAs of the persistent kernel (0 = one per
+ * SM).  Requires head_dim 64, d_model <= 1024 and a multiple of 256, ffn <= 3072 and a
+ * multiple of 256.  NULL on error. */
+XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg,
+                                const XdnaOptWeights *w, int max_ctx, int grid);
+void xdna_opt_free(XdnaOptDecoder *dec);
+
+/* Opt::generate (opt125m_decode.rs:296-315): prefill `prompt` token by token, then greedily
+ * decode n_new tokens (ties -> the last maximal logit, as max_by(partial_cmp)).  Host in,
+ * host out, synchronous.  out_logits (nullable) receives [n_new, V] f32: the logits that
+ * chose each generated token.  Returns 0, or -1 with xdna_last_error() set. */
+int xdna_opt_generate(XdnaOptDecoder *dec, const int64_t *prompt, size_t n_prompt, size_t n_new,
+                      int64_t *out_ids, float *out_logits);
+
+/* Asynchronous, device-resident form used for streaming decode and timing.
+ * The decoder owns a device token array `tokens[max_ctx + 1]` (xdna_opt_tokens_device).
+ * xdna_opt_launch runs positions start_pos .. start_pos + n_steps - 1 in ONE kernel launch:
+ * position p feeds tokens[p] when p < n_prompt or when it is the first step of the launch,
+ * otherwise the id it generated itself; every step at p >= n_prompt - 1 writes its greedy
+ * id to tokens[p + 1] and, if logits_dev is non-NULL, its logits to
+ * logits_dev[(p - max(start_pos, n_prompt - 1)) * V ...].  Positions must be launched in
+ * order: the KV cache of positions < start_pos must come from earlier launches. */
+int64_t *xdna_opt_tokens_device(XdnaOptDecoder *dec);
+/* Copy n token ids between host memory and tokens[off .. off+n) on `stream` (asynchronous
+ * when the host buffer is pinned).  Returns 0, or -1 on a bad range. */
+int xdna_opt_set_tokens(XdnaOptDecoder *dec, const int64_t *host, size_t off, size_t n,
+                        void *stream);
+int xdna_opt_get_tokens(XdnaOptDecoder *dec, int64_t *host, size_t off, size_t n, void *stream);
+int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_prompt,
+                    float *logits_dev, void *stream);
+/* Wait for the decoder's launches on `stream` and report a device-side failure (bounded
+ * waits that expired).  Returns 0, or -1 with xdna_last_error() set. */
+int xdna_opt_sync(XdnaOptDecoder *dec, void *stream);
+/* Bytes of weights one decoded token streams from HBM (int8 rows + per-row scale/bias). */
+size_t xdna_opt_stream_bytes_per_token(const XdnaOptDecoder *dec);
+int xdna_opt_grid(const XdnaOptDecoder *dec);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,67 @@
+"""CPU-side checks of the C-ABI boundary: the library loads, exports every entry point the
+public headers declare, reports errors the reference's way, and its host-side int8 quantiser
+is bit-exact with the oracle (Lin::load, opt125m_decode.rs:41-60)."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared(header):
+    src = open(os.path.join(REPO, "include", header)).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(xdna_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def xl():
+    import xdna_engine_b200 as X
+    from xdna_engine_b200 import _build
+    _build.build()
+    return X
+
+
+def test_library_exports_every_declared_symbol(xl):
+    L = xl.lib()
+    names = _declared("xdna_b200.h")
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(L, n), f"missing export {n}"
+
+
+def test_error_convention_without_device(xl):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert xl.Device.count() == 0
+    with pytest.raises(xl.XdnaError):
+        xl.Device(0)
+    assert xl.last_error() != ""
+
+
+def test_null_pointer_errors(xl):
+    L = xl.lib()
+    assert L.xdna_quant_i8_cols(None, 4, 4, None, None) == -1
+    assert "null" in xl.last_error()
+    assert L.xdna_opt_create(None, None, None, 16, 0) is None
+    assert "null" in xl.last_error()
+    assert L.xdna_opt_launch(None, 0, 1, 1, None, None) == -1
+    assert L.xdna_gemv_i8(None, None, 256, None, None, None, 8, None) == -1
+
+
+@pytest.mark.parametrize("shape", [(768, 768), (768, 3072), (3072, 768), (256, 40)])
+def test_quantiser_bit_exact_with_oracle(xl, shape):
+    K, N = shape
+    rng = np.random.default_rng(K + N)
+    w = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    w[:, 1] = 0.0
+    w[5, 2] = 1.0           # one outlier column
+    q, s = xl.quant_i8_cols(w)
+    oq, os_ = O.quant_i8_cols(w)
+    np.testing.assert_array_equal(s, os_)
+    np.testing.assert_array_equal(q, oq.T)

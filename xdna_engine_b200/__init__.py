@@ -1,0 +1,208 @@
+"""xdna_engine_b200 -- B200 (sm_100a) backend for xdna-engine's fused transformer hot path.
+
+The product is the C-ABI library libxdna_b200.so (include/xdna_b200.h), built in-tree by
+xdna_engine_b200._build.  This module is a thin ctypes binding that mirrors the reference's
+host interface for the decode path (rust/npu-whisper/src/bin/opt125m_decode.rs: Opt::load,
+Opt::generate) so Python callers and the tests drive exactly the C ABI a Rust/C host would.
+
+There is no CPU fallback: if the library or a B200 is missing, the calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from .synth import OPT_125M, OptConfig, make_opt_weights, make_prompt  # noqa: F401
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libxdna_b200.so")
+_LIB = None
+
+
+class XdnaError(RuntimeError):
+    pass
+
+
+class _OptConfig(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("d_model", C.c_int), ("n_heads", C.c_int),
+                ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int),
+                ("max_pos", C.c_int), ("eps", C.c_float)]
+
+
+_LAYER_FIELDS = ("ln1_w", "ln1_b", "wq", "wk", "wv", "wo", "bq", "bk", "bv", "bo",
+                 "ln2_w", "ln2_b", "w1", "b1", "w2", "b2")
+
+
+class _OptLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _LAYER_FIELDS]
+
+
+class _OptWeights(C.Structure):
+    _fields_ = [("emb_tok", C.c_void_p), ("emb_pos", C.c_void_p), ("lnf_w", C.c_void_p),
+                ("lnf_b", C.c_void_p), ("layers", C.c_void_p)]
+
+
+def lib():
+    """Load libxdna_b200.so (raises if it was not built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise XdnaError(f"{LIB_PATH} missing: run `python -m xdna_engine_b200._build`")
+        L = C.CDLL(LIB_PATH)
+        vp, i, sz = C.c_void_p, C.c_int, C.c_size_t
+        L.xdna_last_error.restype = C.c_char_p
+        L.xdna_device_count.restype = i
+        L.xdna_device_open.argtypes = [i]
+        L.xdna_device_open.restype = vp
+        L.xdna_device_close.argtypes = [vp]
+        L.xdna_quant_i8_cols.argtypes = [vp, i, i, vp, vp]
+        L.xdna_quant_i8_cols.restype = i
+        L.xdna_gemv_i8.argtypes = [vp, vp, i, vp, vp, vp, i, vp]
+        L.xdna_gemv_i8.restype = i
+        L.xdna_opt_create.argtypes = [vp, vp, vp, i, i]
+        L.xdna_opt_create.restype = vp
+        L.xdna_opt_free.argtypes = [vp]
+        L.xdna_opt_generate.argtypes = [vp, vp, sz, sz, vp, vp]
+        L.xdna_opt_generate.restype = i
+        L.xdna_opt_tokens_device.argtypes = [vp]
+        L.xdna_opt_tokens_device.restype = vp
+        L.xdna_opt_set_tokens.argtypes = [vp, vp, sz, sz, vp]
+        L.xdna_opt_set_tokens.restype = i
+        L.xdna_opt_get_tokens.argtypes = [vp, vp, sz, sz, vp]
+        L.xdna_opt_get_tokens.restype = i
+        L.xdna_opt_launch.argtypes = [vp, i, i, i, vp, vp]
+        L.xdna_opt_launch.restype = i
+        L.xdna_opt_sync.argtypes = [vp, vp]
+        L.xdna_opt_sync.restype = i
+        L.xdna_opt_stream_bytes_per_token.argtypes = [vp]
+        L.xdna_opt_stream_bytes_per_token.restype = sz
+        L.xdna_opt_grid.argtypes = [vp]
+        L.xdna_opt_grid.restype = i
+        _LIB = L
+    return _LIB
+
+
+def last_error() -> str:
+    return lib().xdna_last_error().decode()
+
+
+def _check(rc):
+    if rc != 0:
+        raise XdnaError(last_error())
+
+
+def _addr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def quant_i8_cols(w: np.ndarray):
+    """Lin::load int8 quantisation as the engine performs it: returns (q [N, K], scale [N])."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    K, N = w.shape
+    q = np.empty((N, K), np.int8)
+    s = np.empty(N, np.float32)
+    _check(lib().xdna_quant_i8_cols(_addr(w), K, N, _addr(q), _addr(s)))
+    return q, s
+
+
+class Device:
+    """An open sm_100 device (the npu-xrt Device replacement)."""
+
+    def __init__(self, ordinal: int = 0):
+        h = lib().xdna_device_open(ordinal)
+        if not h:
+            raise XdnaError(last_error())
+        self.handle = h
+        self.ordinal = ordinal
+
+    @staticmethod
+    def count() -> int:
+        return lib().xdna_device_count()
+
+    def gemv_i8(self, x, q_nk, scale, bias=None):
+        x = np.ascontiguousarray(x, np.float32)
+        q_nk = np.ascontiguousarray(q_nk, np.int8)
+        N, K = q_nk.shape
+        scale = np.ascontiguousarray(scale, np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        y = np.empty(N, np.float32)
+        _check(lib().xdna_gemv_i8(self.handle, _addr(x), K, _addr(q_nk), _addr(scale),
+                                  None if b is None else _addr(b), N, _addr(y)))
+        return y
+
+    def close(self):
+        if self.handle:
+            lib().xdna_device_close(self.handle)
+            self.handle = None
+
+
+class OptDecoder:
+    """opt-125m greedy decoder on one B200 (Opt::load + Opt::generate of the reference)."""
+
+    def __init__(self, device: Device, cfg: OptConfig, weights: dict, max_ctx: int | None = None,
+                 grid: int = 0):
+        self.cfg = cfg
+        self.device = device
+        keep = []
+
+        def p(a):
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            return _addr(a)
+
+        c = _OptConfig(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
+                       cfg.max_pos, cfg.eps)
+        layers = (_OptLayer * cfg.n_layers)()
+        for li, ly in enumerate(weights["layers"]):
+            for n in _LAYER_FIELDS:
+                setattr(layers[li], n, p(ly[n]))
+        w = _OptWeights(p(weights["emb_tok"]), p(weights["emb_pos"]), p(weights["lnf_w"]),
+                        p(weights["lnf_b"]), C.addressof(layers))
+        self.max_ctx = max_ctx or cfg.max_pos
+        h = lib().xdna_opt_create(device.handle, C.byref(c), C.byref(w), self.max_ctx, grid)
+        if not h:
+            raise XdnaError(last_error())
+        self.handle = h
+        self.grid = lib().xdna_opt_grid(h)
+        self.stream_bytes_per_token = lib().xdna_opt_stream_bytes_per_token(h)
+
+    def generate(self, prompt, n_new: int, want_logits: bool = False):
+        """Greedy decode (host in, host out)."""
+        prompt = np.ascontiguousarray(prompt, np.int64)
+        out = np.empty(n_new, np.int64)
+        lg = np.empty((n_new, self.cfg.vocab), np.float32) if want_logits else None
+        _check(lib().xdna_opt_generate(self.handle, _addr(prompt), prompt.size, n_new, _addr(out),
+                                       None if lg is None else _addr(lg)))
+        return (out, lg) if want_logits else out
+
+    # ---- device-resident control (streams as integer cudaStream_t handles)
+    def tokens_device_ptr(self) -> int:
+        return lib().xdna_opt_tokens_device(self.handle)
+
+    def set_tokens(self, ids, off: int = 0, stream: int = 0):
+        """Host ids -> device tokens[off:]; `ids` must stay alive until the stream passes."""
+        _check(lib().xdna_opt_set_tokens(self.handle, _addr(ids), off, ids.size, stream or None))
+
+    def get_tokens(self, out, off: int = 0, stream: int = 0):
+        _check(lib().xdna_opt_get_tokens(self.handle, _addr(out), off, out.size, stream or None))
+
+    def launch(self, start_pos: int, n_steps: int, n_prompt: int, logits_ptr: int = 0,
+               stream: int = 0):
+        _check(lib().xdna_opt_launch(self.handle, start_pos, n_steps, n_prompt,
+                                     logits_ptr or None, stream or None))
+
+    def sync(self, stream: int = 0):
+        _check(lib().xdna_opt_sync(self.handle, stream or None))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().xdna_opt_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,572 @@
+// engine.cu -- host side of the B200 backend: device handle, int8 quantiser, weight-stream
+// packer, decoder lifetime and the C ABI declared in include/xdna_b200.h.
+//
+// Replaces rust/npu-xrt (device, buffer objects, dispatch; src/lib.rs:46-158, 641-744) and
+// the weight preparation of the opt-125m decode (opt125m_decode.rs Lin::load 41-60,
+// Opt::load 155-181).  Error convention of the reference C ABIs: NULL / -1 plus a
+// thread-local message (rust/npu-capi/src/lib.rs:11-16).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/xdna_b200.h"
+#include "decode.h"
+
+namespace xdna {
+int decode_smem_bytes();
+cudaError_t launch_opt_decode(const DecodeParams &p, cudaStream_t st);
+cudaError_t launch_gemv_i8(const float *x, int K, const uint8_t *packed, const ChunkRef *chunks,
+                           int N, float *y, cudaStream_t st);
+cudaError_t max_coresident_ctas(int *out);
+}  // namespace xdna
+
+using namespace xdna;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+void set_err(const std::string &m) { g_last_error = m; }
+
+struct CudaError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+void ck(cudaError_t e, const char *what) {
+    if (e != cudaSuccess)
+        throw CudaError(std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+template <class T>
+T *dmalloc(size_t n) {
+    void *p = nullptr;
+    ck(cudaMalloc(&p, std::max<size_t>(n * sizeof(T), 16)), "cudaMalloc");
+    return static_cast<T *>(p);
+}
+
+// Lin::load (opt125m_decode.rs:41-60): per-output-column scale amax/127 (1.0 if zero),
+// q = clamp(round(w / scale), -127, 127), round = half away from zero.  Output-major.
+void quant_cols(const float *w, int K, int N, int8_t *q_nk, float *scale) {
+    for (int c = 0; c < N; c++) {
+        float amax = 0.0f;
+        for (int r = 0; r < K; r++) amax = std::fmax(amax, std::fabs(w[(size_t)r * N + c]));
+        scale[c] = amax > 0.0f ? amax / 127.0f : 1.0f;
+    }
+    for (int r = 0; r < K; r++) {
+        const float *wr = w + (size_t)r * N;
+        for (int c = 0; c < N; c++) {
+            float v = std::round(wr[c] / scale[c]);
+            v = v < -127.0f ? -127.0f : (v > 127.0f ? 127.0f : v);
+            q_nk[(size_t)c * K + r] = static_cast<int8_t>(v);
+        }
+    }
+}
+// the tied LM head: output channel v = embedding row v, same rule
+void quant_rows(const float *w, int M, int K, int8_t *q, float *scale) {
+    for (int m = 0; m < M; m++) {
+        const float *row = w + (size_t)m * K;
+        float amax = 0.0f;
+        for (int k = 0; k < K; k++) amax = std::fmax(amax, std::fabs(row[k]));
+        const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+        scale[m] = s;
+        for (int k = 0; k < K; k++) {
+            float v = std::round(row[k] / s);
+            v = v < -127.0f ? -127.0f : (v > 127.0f ? 127.0f : v);
+            q[(size_t)m * K + k] = static_cast<int8_t>(v);
+        }
+    }
+}
+
+// A GEMV operand in the engine's output-major int8 form.
+struct QMat {
+    int K = 0, N = 0;
+    std::vector<int8_t> q;      // [N][K]
+    std::vector<float> scale;   // [N]
+    std::vector<float> bias;    // [N]
+};
+
+// Append rows [r0, r0+rows) of m as chunks to `out` (see decode.h): per chunk the rows'
+// K bytes with 32-byte block kb of row r stored at block kb ^ (r & 3), then (scale, bias)
+// per row, padded to 16 bytes.
+void pack_rows(const QMat &m, int r0, int rows, std::vector<uint8_t> &out,
+               std::vector<ChunkRef> &refs, size_t base_off) {
+    const int K = m.K, rpc = rows_per_chunk(K);
+    for (int c0 = 0; c0 < rows; c0 += rpc) {
+        const int rr = std::min(rpc, rows - c0);
+        const uint32_t bytes = chunk_bytes(rr, K);
+        const size_t off = out.size();
+        out.resize(off + bytes, 0);
+        uint8_t *dst = out.data() + off;
+        for (int r = 0; r < rr; r++) {
+            const int8_t *src = m.q.data() + (size_t)(r0 + c0 + r) * K;
+            for (int kb = 0; kb < K / 32; kb++)
+                std::memcpy(dst + (size_t)r * K + ((kb ^ (r & 3)) * 32), src + kb * 32, 32);
+        }
+        float *meta = reinterpret_cast<float *>(dst + (size_t)rr * K);
+        for (int r = 0; r < rr; r++) {
+            meta[2 * r] = m.scale[r0 + c0 + r];
+            meta[2 * r + 1] = m.bias.empty() ? 0.0f : m.bias[r0 + c0 + r];
+        }
+        refs.push_back(ChunkRef{static_cast<uint32_t>(base_off + off), bytes});
+    }
+}
+
+QMat quant_linear(const float *w, const float *b, int K, int N) {
+    QMat m;
+    m.K = K;
+    m.N = N;
+    m.q.resize((size_t)K * N);
+    m.scale.resize(N);
+    quant_cols(w, K, N, m.q.data(), m.scale.data());
+    m.bias.assign(b, b + N);
+    return m;
+}
+
+// rows of several matrices stacked (q|k|v share one phase)
+QMat stack(const std::vector<const QMat *> &ms) {
+    QMat r;
+    r.K = ms[0]->K;
+    for (auto *m : ms) {
+        r.N += m->N;
+        r.q.insert(r.q.end(), m->q.begin(), m->q.end());
+        r.scale.insert(r.scale.end(), m->scale.begin(), m->scale.end());
+        r.bias.insert(r.bias.end(), m->bias.begin(), m->bias.end());
+    }
+    return r;
+}
+
+}  // namespace
+
+struct XdnaDevice {
+    int ordinal = 0;
+    int sms = 0;
+    cudaStream_t stream = nullptr;
+};
+
+struct XdnaOptDecoder {
+    XdnaDevice *dev = nullptr;
+    XdnaOptConfig cfg{};
+    int grid = 0, max_ctx = 0, n_pages = 0;
+    size_t stream_bytes = 0, token_bytes = 0;
+    uint8_t *d_stream = nullptr;
+    ChunkRef *d_chunks = nullptr;
+    int *d_nl = nullptr, *d_nlm = nullptr;
+    int chunk_stride = 0;
+    float *d_emb = nullptr, *d_pos = nullptr, *d_ln = nullptr, *d_lnf = nullptr;
+    uint16_t *d_kv = nullptr;
+    int *d_pt = nullptr;
+    uint64_t *d_ll = nullptr;
+    size_t ll_words = 0;
+    uint64_t *ll_qkv = nullptr, *ll_att = nullptr, *ll_o = nullptr, *ll_h = nullptr, *ll_f2 = nullptr,
+             *ll_lm = nullptr;
+    int64_t *d_tokens = nullptr;
+    RunState *d_state = nullptr;
+    float *d_logits = nullptr;      // scratch for xdna_opt_generate
+    size_t logits_cap = 0;
+    ~XdnaOptDecoder() {
+        void *ptrs[] = {d_stream, d_chunks, d_nl, d_nlm, d_emb, d_pos, d_ln, d_lnf, d_kv, d_pt, d_ll,
+                        d_tokens, d_state, d_logits};
+        for (void *p : ptrs)
+            if (p) cudaFree(p);
+    }
+};
+
+extern "C" {
+
+const char *xdna_last_error(void) { return g_last_error.c_str(); }
+
+int xdna_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    int usable = 0;
+    for (int i = 0; i < n; i++) {
+        cudaDeviceProp pr{};
+        if (cudaGetDeviceProperties(&pr, i) == cudaSuccess && pr.major == 10) usable++;
+    }
+    return usable;
+}
+
+XdnaDevice *xdna_device_open(int ordinal) {
+    try {
+        int n = 0;
+        ck(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+        if (ordinal < 0 || ordinal >= n) {
+            set_err("device ordinal " + std::to_string(ordinal) + " out of range (" + std::to_string(n) + " devices)");
+            return nullptr;
+        }
+        cudaDeviceProp pr{};
+        ck(cudaGetDeviceProperties(&pr, ordinal), "cudaGetDeviceProperties");
+        if (pr.major != 10) {
+            set_err(std::string("device is not sm_100 (") + pr.name + ")");
+            return nullptr;
+        }
+        ck(cudaSetDevice(ordinal), "cudaSetDevice");
+        auto *d = new XdnaDevice();
+        d->ordinal = ordinal;
+        d->sms = pr.multiProcessorCount;
+        return d;
+    } catch (const std::exception &e) {
+        set_err(e.what());
+        return nullptr;
+    }
+}
+
+void xdna_device_close(XdnaDevice *dev) { delete dev; }
+
+int xdna_quant_i8_cols(const float *w, int K, int N, int8_t *q_nk, float *scale) {
+    if (!w || !q_nk || !scale || K <= 0 || N <= 0) {
+        set_err("xdna_quant_i8_cols: null pointer or empty shape");
+        return -1;
+    }
+    quant_cols(w, K, N, q_nk, scale);
+    return 0;
+}
+
+int xdna_gemv_i8(XdnaDevice *dev, const float *x, int K, const int8_t *q_nk, const float *scale,
+                 const float *bias, int N, float *y) {
+    if (!dev || !x || !q_nk || !scale || !y) { set_err("xdna_gemv_i8: null pointer"); return -1; }
+    if (K <= 0 || K % 256 != 0 || K > kKmax || N <= 0 || N % 8 != 0) {
+        set_err("xdna_gemv_i8: K must be a multiple of 256 <= 3072 and N a multiple of 8");
+        return -1;
+    }
+    float *dx = nullptr, *dy = nullptr;
+    uint8_t *dp = nullptr;
+    ChunkRef *dc = nullptr;
+    try {
+        ck(cudaSetDevice(dev->ordinal), "cudaSetDevice");
+        QMat m;
+        m.K = K;
+        m.N = N;
+        m.q.assign(q_nk, q_nk + (size_t)K * N);
+        m.scale.assign(scale, scale + N);
+        if (bias) m.bias.assign(bias, bias + N);
+        std::vector<uint8_t> packed;
+        std::vector<ChunkRef> refs;
+        pack_rows(m, 0, N, packed, refs, 0);
+        dx = dmalloc<float>(K);
+        dy = dmalloc<float>(N);
+        dp = dmalloc<uint8_t>(packed.size());
+        dc = dmalloc<ChunkRef>(refs.size());
+        ck(cudaMemcpy(dx, x, sizeof(float) * K, cudaMemcpyHostToDevice), "copy x");
+        ck(cudaMemcpy(dp, packed.data(), packed.size(), cudaMemcpyHostToDevice), "copy weights");
+        ck(cudaMemcpy(dc, refs.data(), refs.size() * sizeof(ChunkRef), cudaMemcpyHostToDevice), "copy chunks");
+        ck(launch_gemv_i8(dx, K, dp, dc, N, dy, nullptr), "gemv_i8 launch");
+        ck(cudaMemcpy(y, dy, sizeof(float) * N, cudaMemcpyDeviceToHost), "copy y");
+        cudaFree(dx); cudaFree(dy); cudaFree(dp); cudaFree(dc);
+        return 0;
+    } catch (const std::exception &e) {
+        set_err(e.what());
+        if (dx) cudaFree(dx);
+        if (dy) cudaFree(dy);
+        if (dp) cudaFree(dp);
+        if (dc) cudaFree(dc);
+        return -1;
+    }
+}
+
+XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const XdnaOptWeights *w,
+                                int max_ctx, int grid) {
+    if (!dev || !cfg || !w || !w->layers || !w->emb_tok || !w->emb_pos || !w->lnf_w || !w->lnf_b) {
+        set_err("xdna_opt_create: null pointer");
+        return nullptr;
+    }
+    const XdnaOptConfig c = *cfg;
+    const int D = c.d_model, F = c.ffn, L = c.n_layers, V = c.vocab, H = c.n_heads;
+    if (c.head_dim != kHeadDim || H * kHeadDim != D || D % 256 || D > kDmax || F % 256 || F > kKmax ||
+        L < 1 || V < 8 || V % 8 || c.max_pos < 1) {
+        set_err("xdna_opt_create: unsupported shape (head_dim 64, d_model%256==0 <= 1024, "
+                "ffn%256==0 <= 3072, vocab%8==0)");
+        return nullptr;
+    }
+    if (max_ctx < 1 || max_ctx > c.max_pos) {
+        set_err("xdna_opt_create: max_ctx must be in [1, max_pos]");
+        return nullptr;
+    }
+    auto *dec = new (std::nothrow) XdnaOptDecoder();
+    if (!dec) { set_err("out of host memory"); return nullptr; }
+    try {
+        ck(cudaSetDevice(dev->ordinal), "cudaSetDevice");
+        dec->dev = dev;
+        dec->cfg = c;
+        dec->max_ctx = max_ctx;
+        int maxg = 0;
+        ck(max_coresident_ctas(&maxg), "occupancy query");
+        dec->grid = grid > 0 ? std::min(grid, maxg) : maxg;
+        if (dec->grid < 1) throw std::runtime_error("decode kernel cannot be resident on this device");
+        const int G = dec->grid;
+        if ((3 * D / 8 + G - 1) / G * 8 > 1024 || (F / 8 + G - 1) / G * 8 > 1024)
+            throw std::runtime_error("grid too small for the per-CTA row buffers");
+
+        // quantise every linear; the QKV phase stacks q | k | v rows
+        std::vector<QMat> qkv(L), o(L), f1(L), f2(L);
+        for (int l = 0; l < L; l++) {
+            const XdnaOptLayer &ly = w->layers[l];
+            QMat q = quant_linear(ly.wq, ly.bq, D, D), k = quant_linear(ly.wk, ly.bk, D, D),
+                 v = quant_linear(ly.wv, ly.bv, D, D);
+            qkv[l] = stack({&q, &k, &v});
+            o[l] = quant_linear(ly.wo, ly.bo, D, D);
+            f1[l] = quant_linear(ly.w1, ly.b1, D, F);
+            f2[l] = quant_linear(ly.w2, ly.b2, F, D);
+        }
+        QMat lm;
+        lm.K = D;
+        lm.N = V;
+        lm.q.resize((size_t)V * D);
+        lm.scale.resize(V);
+        quant_rows(w->emb_tok, V, D, lm.q.data(), lm.scale.data());
+
+        // per-CTA streams
+        std::vector<uint8_t> all;
+        std::vector<std::vector<ChunkRef>> refs(G);
+        std::vector<int> nl(G), nlm(G);
+        size_t per_token_max = 0;
+        for (int cta = 0; cta < G; cta++) {
+            std::vector<uint8_t> s;
+            const size_t base = all.size();
+            for (int l = 0; l < L; l++) {
+                pack_rows(qkv[l], part_row0(cta, 3 * D, G), part_rows(cta, 3 * D, G), s, refs[cta], base);
+                pack_rows(o[l], part_row0(cta, D, G), part_rows(cta, D, G), s, refs[cta], base);
+                pack_rows(f1[l], part_row0(cta, F, G), part_rows(cta, F, G), s, refs[cta], base);
+                pack_rows(f2[l], part_row0(cta, D, G), part_rows(cta, D, G), s, refs[cta], base);
+            }
+            nl[cta] = (int)refs[cta].size();
+            pack_rows(lm, part_row0(cta, V, G), part_rows(cta, V, G), s, refs[cta], base);
+            nlm[cta] = (int)refs[cta].size() - nl[cta];
+            per_token_max = std::max(per_token_max, s.size());
+            all.insert(all.end(), s.begin(), s.end());
+        }
+        dec->stream_bytes = all.size();
+        dec->token_bytes = all.size();
+        if (all.size() >= (1ull << 32)) throw std::runtime_error("weight stream exceeds 4 GiB");
+        int stride = 0;
+        for (int cta = 0; cta < G; cta++) stride = std::max(stride, (int)refs[cta].size());
+        dec->chunk_stride = stride;
+        std::vector<ChunkRef> flat((size_t)G * stride, ChunkRef{0, 0});
+        for (int cta = 0; cta < G; cta++)
+            std::copy(refs[cta].begin(), refs[cta].end(), flat.begin() + (size_t)cta * stride);
+
+        dec->d_stream = dmalloc<uint8_t>(all.size());
+        ck(cudaMemcpy(dec->d_stream, all.data(), all.size(), cudaMemcpyHostToDevice), "upload stream");
+        dec->d_chunks = dmalloc<ChunkRef>(flat.size());
+        ck(cudaMemcpy(dec->d_chunks, flat.data(), flat.size() * sizeof(ChunkRef), cudaMemcpyHostToDevice), "upload chunks");
+        dec->d_nl = dmalloc<int>(G);
+        dec->d_nlm = dmalloc<int>(G);
+        ck(cudaMemcpy(dec->d_nl, nl.data(), G * sizeof(int), cudaMemcpyHostToDevice), "upload nl");
+        ck(cudaMemcpy(dec->d_nlm, nlm.data(), G * sizeof(int), cudaMemcpyHostToDevice), "upload nlm");
+
+        // f32 parameters
+        dec->d_emb = dmalloc<float>((size_t)V * D);
+        ck(cudaMemcpy(dec->d_emb, w->emb_tok, sizeof(float) * V * D, cudaMemcpyHostToDevice), "upload emb");
+        dec->d_pos = dmalloc<float>((size_t)(c.max_pos + 2) * D);
+        ck(cudaMemcpy(dec->d_pos, w->emb_pos, sizeof(float) * (size_t)(c.max_pos + 2) * D, cudaMemcpyHostToDevice),
+           "upload pos");
+        std::vector<float> ln((size_t)L * 4 * D);
+        for (int l = 0; l < L; l++) {
+            const XdnaOptLayer &ly = w->layers[l];
+            std::copy(ly.ln1_w, ly.ln1_w + D, ln.begin() + (size_t)(l * 4 + 0) * D);
+            std::copy(ly.ln1_b, ly.ln1_b + D, ln.begin() + (size_t)(l * 4 + 1) * D);
+            std::copy(ly.ln2_w, ly.ln2_w + D, ln.begin() + (size_t)(l * 4 + 2) * D);
+            std::copy(ly.ln2_b, ly.ln2_b + D, ln.begin() + (size_t)(l * 4 + 3) * D);
+        }
+        dec->d_ln = dmalloc<float>(ln.size());
+        ck(cudaMemcpy(dec->d_ln, ln.data(), ln.size() * sizeof(float), cudaMemcpyHostToDevice), "upload ln");
+        std::vector<float> lnf(2 * D);
+        std::copy(w->lnf_w, w->lnf_w + D, lnf.begin());
+        std::copy(w->lnf_b, w->lnf_b + D, lnf.begin() + D);
+        dec->d_lnf = dmalloc<float>(2 * D);
+        ck(cudaMemcpy(dec->d_lnf, lnf.data(), 2 * D * sizeof(float), cudaMemcpyHostToDevice), "upload lnf");
+
+        // paged KV: pages in reverse physical order so the page table is exercised
+        dec->n_pages = (max_ctx + kPageTokens - 1) / kPageTokens;
+        std::vector<int> pt(dec->n_pages);
+        for (int i = 0; i < dec->n_pages; i++) pt[i] = dec->n_pages - 1 - i;
+        dec->d_pt = dmalloc<int>(pt.size());
+        ck(cudaMemcpy(dec->d_pt, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice), "upload page table");
+        const size_t kv_elems = (size_t)L * dec->n_pages * 2 * H * kPageTokens * kHeadDim;
+        dec->d_kv = dmalloc<uint16_t>(kv_elems);
+        ck(cudaMemset(dec->d_kv, 0, kv_elems * 2), "clear kv");
+
+        // flag-tagged exchange words
+        const size_t n_qkv = 3 * D / 2, n_att = (size_t)dec->n_pages * H * (2 + kHeadDim), n_o = D,
+                     n_h = F / 2, n_f2 = D, n_lm = 2 * (size_t)G;
+        dec->ll_words = n_qkv + n_att + n_o + n_h + n_f2 + n_lm;
+        dec->d_ll = dmalloc<uint64_t>(dec->ll_words);
+        ck(cudaMemset(dec->d_ll, 0, dec->ll_words * 8), "clear exchange words");
+        dec->ll_qkv = dec->d_ll;
+        dec->ll_att = dec->ll_qkv + n_qkv;
+        dec->ll_o = dec->ll_att + n_att;
+        dec->ll_h = dec->ll_o + n_o;
+        dec->ll_f2 = dec->ll_h + n_h;
+        dec->ll_lm = dec->ll_f2 + n_f2;
+
+        dec->d_tokens = dmalloc<int64_t>(max_ctx + 1);
+        ck(cudaMemset(dec->d_tokens, 0, (max_ctx + 1) * sizeof(int64_t)), "clear tokens");
+        dec->d_state = dmalloc<RunState>(1);
+        RunState rs{1u, 0u, 0u, 0u};
+        ck(cudaMemcpy(dec->d_state, &rs, sizeof(rs), cudaMemcpyHostToDevice), "init state");
+        ck(cudaDeviceSynchronize(), "create sync");
+        return dec;
+    } catch (const std::exception &e) {
+        set_err(std::string("xdna_opt_create: ") + e.what());
+        delete dec;
+        return nullptr;
+    }
+}
+
+void xdna_opt_free(XdnaOptDecoder *dec) {
+    if (!dec) return;
+    cudaSetDevice(dec->dev->ordinal);
+    cudaDeviceSynchronize();
+    delete dec;
+}
+
+int64_t *xdna_opt_tokens_device(XdnaOptDecoder *dec) { return dec ? dec->d_tokens : nullptr; }
+
+static int copy_tokens(XdnaOptDecoder *dec, void *host, size_t off, size_t n, void *stream, bool up) {
+    if (!dec || (!host && n)) { set_err("xdna_opt_*_tokens: null pointer"); return -1; }
+    if (off + n > (size_t)dec->max_ctx + 1) { set_err("xdna_opt_*_tokens: range beyond max_ctx + 1"); return -1; }
+    cudaError_t e = cudaSetDevice(dec->dev->ordinal);
+    if (e == cudaSuccess && n)
+        e = up ? cudaMemcpyAsync(dec->d_tokens + off, host, n * 8, cudaMemcpyHostToDevice, (cudaStream_t)stream)
+               : cudaMemcpyAsync(host, dec->d_tokens + off, n * 8, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    if (e != cudaSuccess) { set_err(std::string("xdna_opt_*_tokens: ") + cudaGetErrorString(e)); return -1; }
+    return 0;
+}
+int xdna_opt_set_tokens(XdnaOptDecoder *dec, const int64_t *host, size_t off, size_t n, void *stream) {
+    return copy_tokens(dec, const_cast<int64_t *>(host), off, n, stream, true);
+}
+int xdna_opt_get_tokens(XdnaOptDecoder *dec, int64_t *host, size_t off, size_t n, void *stream) {
+    return copy_tokens(dec, host, off, n, stream, false);
+}
+int xdna_opt_grid(const XdnaOptDecoder *dec) { return dec ? dec->grid : 0; }
+size_t xdna_opt_stream_bytes_per_token(const XdnaOptDecoder *dec) { return dec ? dec->token_bytes : 0; }
+
+int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_prompt, float *logits_dev,
+                    void *stream) {
+    if (!dec) { set_err("xdna_opt_launch: decoder is null"); return -1; }
+    if (start_pos < 0 || n_steps < 1 || n_prompt < 1 || start_pos + n_steps > dec->max_ctx) {
+        set_err("xdna_opt_launch: positions out of range (start_pos + n_steps must be <= max_ctx)");
+        return -1;
+    }
+    const XdnaOptConfig &c = dec->cfg;
+    DecodeParams p{};
+    p.n_layers = c.n_layers;
+    p.d_model = c.d_model;
+    p.n_heads = c.n_heads;
+    p.ffn = c.ffn;
+    p.vocab = c.vocab;
+    p.max_pos = c.max_pos;
+    p.eps = c.eps;
+    p.grid = dec->grid;
+    p.stream = dec->d_stream;
+    p.chunks = dec->d_chunks;
+    p.n_layer_chunks = dec->d_nl;
+    p.n_lm_chunks = dec->d_nlm;
+    p.chunk_stride = dec->chunk_stride;
+    p.emb_tok = dec->d_emb;
+    p.emb_pos = dec->d_pos;
+    p.ln = dec->d_ln;
+    p.lnf = dec->d_lnf;
+    p.kv = dec->d_kv;
+    p.page_table = dec->d_pt;
+    p.n_phys_pages = dec->n_pages;
+    p.ll_qkv = dec->ll_qkv;
+    p.ll_att = dec->ll_att;
+    p.ll_o = dec->ll_o;
+    p.ll_h = dec->ll_h;
+    p.ll_f2 = dec->ll_f2;
+    p.ll_lm = dec->ll_lm;
+    p.tokens = dec->d_tokens;
+    p.logits = logits_dev;
+    p.start_pos = start_pos;
+    p.n_steps = n_steps;
+    p.n_prompt = n_prompt;
+    p.state = dec->d_state;
+    p.timeout_ns = 1000000000ull;   // 1 s per wait; normal waits are microseconds
+    cudaError_t e = cudaSetDevice(dec->dev->ordinal);
+    if (e == cudaSuccess) e = launch_opt_decode(p, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        set_err(std::string("xdna_opt_launch: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+int xdna_opt_sync(XdnaOptDecoder *dec, void *stream) {
+    if (!dec) { set_err("xdna_opt_sync: decoder is null"); return -1; }
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        set_err(std::string("xdna_opt_sync: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    RunState rs{};
+    e = cudaMemcpy(&rs, dec->d_state, sizeof(rs), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) {
+        set_err(std::string("xdna_opt_sync: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    if (rs.error != ERR_NONE) {
+        static const char *names[] = {"none", "timeout waiting for a weight chunk",
+                                      "timeout waiting for a free ring stage",
+                                      "timeout waiting for an exchange word", "token id out of range",
+                                      "position out of range"};
+        char buf[256];
+        std::snprintf(buf, sizeof buf, "decode kernel error: %s (cta %u, where 0x%x)",
+                      rs.error < 6 ? names[rs.error] : "unknown", rs.error_cta, rs.error_where);
+        set_err(buf);
+        // the failed launch may have left words of its epochs behind: skip far past them
+        rs.epoch_base += 1u << 20;
+        rs.error = rs.error_cta = rs.error_where = 0;
+        cudaMemcpy(dec->d_state, &rs, sizeof(rs), cudaMemcpyHostToDevice);
+        return -1;
+    }
+    return 0;
+}
+
+int xdna_opt_generate(XdnaOptDecoder *dec, const int64_t *prompt, size_t n_prompt, size_t n_new,
+                      int64_t *out_ids, float *out_logits) {
+    if (!dec || !prompt || !out_ids) { set_err("xdna_opt_generate: null pointer"); return -1; }
+    if (n_prompt < 1 || n_new < 1 || n_prompt + n_new > (size_t)dec->max_ctx + 1) {
+        set_err("xdna_opt_generate: n_prompt + n_new - 1 must be <= max_ctx");
+        return -1;
+    }
+    const int V = dec->cfg.vocab;
+    try {
+        ck(cudaSetDevice(dec->dev->ordinal), "cudaSetDevice");
+        for (size_t i = 0; i < n_prompt; i++)
+            if (prompt[i] < 0 || prompt[i] >= V) throw std::runtime_error("prompt token id out of range");
+        if (out_logits && dec->logits_cap < n_new) {
+            if (dec->d_logits) cudaFree(dec->d_logits);
+            dec->d_logits = dmalloc<float>(n_new * (size_t)V);
+            dec->logits_cap = n_new;
+        }
+        cudaStream_t st = nullptr;
+        ck(cudaMemcpyAsync(dec->d_tokens, prompt, n_prompt * sizeof(int64_t), cudaMemcpyHostToDevice, st),
+           "copy prompt");
+        const int n_steps = (int)(n_prompt + n_new - 1);
+        if (xdna_opt_launch(dec, 0, n_steps, (int)n_prompt, out_logits ? dec->d_logits : nullptr, st) != 0)
+            return -1;
+        ck(cudaMemcpyAsync(out_ids, dec->d_tokens + n_prompt, n_new * sizeof(int64_t), cudaMemcpyDeviceToHost, st),
+           "copy ids");
+        if (out_logits)
+            ck(cudaMemcpyAsync(out_logits, dec->d_logits, n_new * (size_t)V * sizeof(float),
+                               cudaMemcpyDeviceToHost, st),
+               "copy logits");
+        return xdna_opt_sync(dec, st);
+    } catch (const std::exception &e) {
+        set_err(std::string("xdna_opt_generate: ") + e.what());
+        return -1;
+    }
+}
+
+}  // extern "C"
