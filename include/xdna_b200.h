@@ -112,6 +112,10 @@ int xdna_opt_sync(XdnaOptDecoder *dec, void *stream);
 /* Bytes of weights one decoded token streams from HBM (int8 rows + per-row scale/bias). */
 size_t xdna_opt_stream_bytes_per_token(const XdnaOptDecoder *dec);
 int xdna_opt_grid(const XdnaOptDecoder *dec);
+/* Debugging aid: when trace_dev (device, [n_steps][2*n_layers+1][d_model] f32) is non-NULL,
+ * later launches record the residual stream after each attention and each FFN residual add,
+ * then the final LayerNorm output, per step of the launch.  NULL turns it off. */
+int xdna_opt_set_trace(XdnaOptDecoder *dec, float *trace_dev);
 
 #ifdef __cplusplus
 }

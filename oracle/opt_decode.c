@@ -40,7 +40,15 @@ struct or_opt {
     float *lm_scale;       /* DEVICE: [V] */
     float *kc, *vc;        /* [L][max_ctx][D] (DEVICE: values already bf16-rounded) */
     int max_ctx;
+    float *trace;          /* optional [pos][2L+1][D] residual-stream record */
 };
+
+void or_opt_set_trace(or_opt *m, float *trace) { m->trace = trace; }
+static void trace_x(or_opt *m, int pos, int slot, const float *v) {
+    if (!m->trace) return;
+    int D = m->cfg.d_model;
+    memcpy(m->trace + ((size_t)pos * (2 * m->cfg.n_layers + 1) + slot) * D, v, sizeof(float) * D);
+}
 
 static void lin_init(lin_t *l, const float *w, const float *b, int K, int N, int mode) {
     l->K = K; l->N = N; l->bias = b; l->w = w;
@@ -227,6 +235,7 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
         }
         lin_apply(m, &lin[3], ctx, o);
         for (int d = 0; d < D; d++) xr[d] = x[d] + o[d];
+        trace_x(m, pos, 2 * l, xr);
         or_layer_norm(xr, ly->ln2_w, ly->ln2_b, 1, D, c->eps, h);
         if (dev) or_bf16_round_n(h, h, (size_t)D);
         lin_apply(m, &lin[4], h, f);
@@ -234,11 +243,13 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
         if (dev) or_bf16_round_n(f, f, (size_t)F);
         lin_apply(m, &lin[5], f, o);
         for (int d = 0; d < D; d++) x[d] = xr[d] + o[d];
+        trace_x(m, pos, 2 * l + 1, x);
     }
     if (want_logits) {
         or_layer_norm(x, m->w.lnf_w, m->w.lnf_b, 1, D, c->eps, h);
         if (dev) {
             or_bf16_round_n(h, h, (size_t)D);
+            trace_x(m, pos, 2 * c->n_layers, h);
             gemv_exact(m, m->lm_q, m->lm_scale, NULL, D, V, h, logits);
         } else {
 #pragma omp parallel for num_threads(m->nthreads) schedule(static)

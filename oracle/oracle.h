@@ -130,6 +130,9 @@ void or_opt_free(or_opt *m);
  * the logits of each step, [n_new, V].  Returns 0, or -1 on bad sizes. */
 int or_opt_generate(or_opt *m, const int64_t *prompt, int n_prompt, int n_new,
                     const int64_t *force_ids, int64_t *out_ids, float *logits_out);
+/* debugging aid: record x after each attention / FFN residual add and the final LN output
+ * (device mode) per position into trace[pos][2L+1][D]; NULL turns it off */
+void or_opt_set_trace(or_opt *m, float *trace);
 /* quantised weights as the engine sees them (for bit-exact checks) */
 const int8_t *or_opt_qweight(const or_opt *m, int layer, int which, float const **scale);
 

@@ -72,6 +72,7 @@ def lib():
         L.or_opt_free.argtypes = [C.c_void_p]
         L.or_opt_generate.argtypes = [C.c_void_p, I64P, C.c_int, C.c_int, C.c_void_p, I64P, C.c_void_p]
         L.or_opt_generate.restype = C.c_int
+        L.or_opt_set_trace.argtypes = [C.c_void_p, C.c_void_p]
         L.or_opt_qweight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.POINTER(C.c_float))]
         L.or_opt_qweight.restype = C.POINTER(C.c_int8)
         _LIB = L
@@ -228,6 +229,10 @@ class OracleOpt:
         if rc != 0:
             raise RuntimeError("or_opt_generate failed")
         return (out, lg) if want_logits else out
+
+    def set_trace(self, buf):
+        self._trace = buf
+        lib().or_opt_set_trace(self._h, None if buf is None else buf.ctypes.data)
 
     def qweight(self, layer, which):
         """int8 weight + scale as the oracle quantised them (which: 0..5 q k v o fc1 fc2,

@@ -27,7 +27,8 @@ __host__ __device__ inline int part_rows(int c, int n_rows, int grid) {
 }
 // rows per chunk for reduction length K: whole n-tiles of (K bytes + 8 bytes meta) per stage
 __host__ __device__ inline int rows_per_chunk(int K) {
-    return (kStageBytes / (K + kRowMeta)) & ~7;
+    const int r = (kStageBytes / (K + kRowMeta)) & ~7;
+    return r < 8 * kMaxTilesPerChunk ? r : 8 * kMaxTilesPerChunk;
 }
 __host__ __device__ inline int n_chunks(int rows, int K) {
     int r = rows_per_chunk(K);
@@ -96,6 +97,8 @@ struct DecodeParams {
     int start_pos, n_steps, n_prompt;
     RunState *state;
     uint64_t timeout_ns;
+    float *trace;              // optional [n_steps][2L+1][D]: residual after attention and
+                               // after the FFN of each layer, then the final LN output
 };
 
 }  // namespace xdna

@@ -506,6 +506,13 @@ __device__ void att_combine(const DecodeParams &p, Cta &S, int pos, uint32_t ep_
     cbar();
 }
 
+// optional debugging record of the residual stream (CTA 0 only)
+__device__ __forceinline__ void trace_x(const DecodeParams &p, Cta &S, int t, int slot, const float *v) {
+    if (p.trace == nullptr || blockIdx.x != 0) return;
+    float *dst = p.trace + ((size_t)t * (2 * p.n_layers + 1) + slot) * p.d_model;
+    for (int i = S.tid; i < p.d_model; i += kConsumerThreads) dst[i] = v[i];
+}
+
 // ---------------------------------------------------------------------------------- roles
 __device__ void producer(const DecodeParams &p, Cta &S) {
     if (S.lane != 0) return;
@@ -584,6 +591,7 @@ __device__ void consumer(const DecodeParams &p, Cta &S) {
                 cbar();
                 for (int i = S.tid; i < D; i += kConsumerThreads) S.xs[i] = __fadd_rn(S.xs[i], S.act[i]);
                 cbar();
+                trace_x(p, S, t, 2 * (l - 1) + 1, S.xs);
             }
             if (abort_check(p, S)) return;
             layer_norm_bf16(S, D, ln, ln + D, p.eps);
@@ -611,6 +619,7 @@ __device__ void consumer(const DecodeParams &p, Cta &S) {
             cbar();
             for (int i = S.tid; i < D; i += kConsumerThreads) S.xs[i] = __fadd_rn(S.xs[i], S.act[i]);
             cbar();
+            trace_x(p, S, t, 2 * l, S.xs);
             if (abort_check(p, S)) return;
             layer_norm_bf16(S, D, ln + 2 * D, ln + 3 * D, p.eps);
             s = make_limbs(S, D);
@@ -653,11 +662,13 @@ __device__ void consumer(const DecodeParams &p, Cta &S) {
             cbar();
             for (int i = S.tid; i < D; i += kConsumerThreads) S.xs[i] = __fadd_rn(S.xs[i], S.act[i]);
             cbar();
+            trace_x(p, S, t, 2 * L - 1, S.xs);
         }
         if (pos >= p.n_prompt - 1) {
             const uint32_t ep_lm = ep0 + (uint32_t)(L * kPhasesPerLayer);
             if (abort_check(p, S)) return;
             layer_norm_bf16(S, D, p.lnf, p.lnf + D, p.eps);
+            trace_x(p, S, t, 2 * L, S.act);
             const int s = make_limbs(S, D);
             float best = -INFINITY;
             int best_i = -1;

@@ -169,6 +169,7 @@ struct XdnaOptDecoder {
     int64_t *d_tokens = nullptr;
     RunState *d_state = nullptr;
     float *d_logits = nullptr;      // scratch for xdna_opt_generate
+    float *trace = nullptr;         // optional residual-stream record (xdna_opt_set_trace)
     size_t logits_cap = 0;
     ~XdnaOptDecoder() {
         void *ptrs[] = {d_stream, d_chunks, d_nl, d_nlm, d_emb, d_pos, d_ln, d_lnf, d_kv, d_pt, d_ll,
@@ -449,6 +450,11 @@ int xdna_opt_get_tokens(XdnaOptDecoder *dec, int64_t *host, size_t off, size_t n
     return copy_tokens(dec, host, off, n, stream, false);
 }
 int xdna_opt_grid(const XdnaOptDecoder *dec) { return dec ? dec->grid : 0; }
+int xdna_opt_set_trace(XdnaOptDecoder *dec, float *trace_dev) {
+    if (!dec) { set_err("xdna_opt_set_trace: decoder is null"); return -1; }
+    dec->trace = trace_dev;
+    return 0;
+}
 size_t xdna_opt_stream_bytes_per_token(const XdnaOptDecoder *dec) { return dec ? dec->token_bytes : 0; }
 
 int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_prompt, float *logits_dev,
@@ -493,6 +499,7 @@ int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_promp
     p.n_prompt = n_prompt;
     p.state = dec->d_state;
     p.timeout_ns = 1000000000ull;   // 1 s per wait; normal waits are microseconds
+    p.trace = dec->trace;
     cudaError_t e = cudaSetDevice(dec->dev->ordinal);
     if (e == cudaSuccess) e = launch_opt_decode(p, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {
