@@ -116,6 +116,11 @@ int xdna_opt_grid(const XdnaOptDecoder *dec);
  * later launches record the residual stream after each attention and each FFN residual add,
  * then the final LayerNorm output, per step of the launch.  NULL turns it off. */
 int xdna_opt_set_trace(XdnaOptDecoder *dec, float *trace_dev);
+/* Profiling aid: when timing_dev (device, [2][grid][128] u64) is non-NULL, the first two steps
+ * of later launches record the global nanosecond timer per CTA at each phase boundary (slot 0
+ * token start, 1 + 5*layer + {0 qkv, 1 attention, 2 out-proj, 3 fc1, 4 fc2} after the phase's
+ * outputs are published, 5*n_layers + 1 after the LM head, + 2 once the greedy id is known). */
+int xdna_opt_set_timing(XdnaOptDecoder *dec, unsigned long long *timing_dev);
 
 #ifdef __cplusplus
 }

@@ -10,7 +10,10 @@
  *                   rounded to bf16 before each GEMV, K and V stored as bf16, q scaled then
  *                   rounded to bf16, every int8 GEMV computed as the exact integer dot of the
  *                   22-bit fixed-point activation (or_limbs) rounded once to f32, int8 LM head
- *                   (same quantiser, per vocab row), residual stream f32.
+ *                   (same quantiser, per vocab row), residual stream f32.  LayerNorm sums
+ *                   and the per-page online softmax follow the engine's reduction trees and
+ *                   use the reference's fast_exp_nonpos, so this mode is bit-exact with the
+ *                   GPU (ln_dev_bf16, attn_dev_head).
  *
  * The GEMVs are parallelised over output columns with OpenMP; each output keeps the
  * reference's k-ascending summation order, so results do not depend on the thread count.
@@ -118,6 +121,93 @@ const int8_t *or_opt_qweight(const or_opt *m, int layer, int which, float const 
     return l->q;
 }
 
+/* ---- the engine's reduction trees (device numerics) --------------------------------
+ * A GPU warp reduces 32 lane partials with an xor butterfly (v = v + v[lane ^ o] for o = 16,
+ * 8, 4, 2, 1).  Float addition is commutative, so the butterfly yields one well-defined
+ * value, replayed here. */
+static float warp_tree(const float *v32) {
+    float v[32], t[32];
+    memcpy(v, v32, sizeof v);
+    for (int o = 16; o; o >>= 1) {
+        for (int l = 0; l < 32; l++) t[l] = v[l] + v[l ^ o];
+        memcpy(v, t, sizeof v);
+    }
+    return v[0];
+}
+/* LayerNorm as the engine computes it: the formula of rust/npu-asr-host/src/lib.rs:79-110 with
+ * the engine's summation tree -- thread (warp w, lane l) of 256 sums its elements
+ * 32*(w + 8j) + l in j order, each warp combines its lanes with the butterfly, and the 8
+ * warp totals are added in warp order from 0 -- output rounded to bf16. */
+static float tree256(const float *x, int D, float sub_mean, int squares) {
+    float tot = 0.0f;
+    for (int w = 0; w < 8; w++) {
+        float part[32];
+        for (int l = 0; l < 32; l++) {
+            float s = 0.0f;
+            for (int i = 32 * w + l; i < D; i += 256) {
+                if (squares) { float c = x[i] - sub_mean; s = s + c * c; }
+                else s = s + x[i];
+            }
+            part[l] = s;
+        }
+        tot = tot + warp_tree(part);
+    }
+    return tot;
+}
+static void ln_dev_bf16(const float *x, const float *g, const float *b, int D, float eps, float *y) {
+    float mean = tree256(x, D, 0.0f, 0) / (float)D;
+    float var = tree256(x, D, mean, 1) / (float)D;
+    float inv = 1.0f / sqrtf(var + eps);
+    for (int i = 0; i < D; i++) {
+        float t0 = (x[i] - mean) * inv;
+        t0 = t0 * g[i];
+        y[i] = or_bf16_round(t0 + b[i]);
+    }
+}
+/* Single-query attention of one head as the engine splits it: one partial (m, l, acc) per
+ * 64-key page (mha_tile's online softmax, route_b_kernels/mha_decode/mha_decode.cc:90-168,
+ * applied per page), pages merged in order; exp = the reference's fast_exp_nonpos. */
+static void attn_dev_head(const float *q, const float *kc, const float *vc, int stride, int tk,
+                          float *ctx) {
+    float M = -INFINITY, L = 0.0f, A[64];
+    for (int d = 0; d < 64; d++) A[d] = 0.0f;
+    for (int j0 = 0; j0 < tk; j0 += 64) {
+        int nk = tk - j0 < 64 ? tk - j0 : 64;
+        float sc[64], pr[64], m = -INFINITY;
+        for (int k = 0; k < 64; k++) {
+            if (k >= nk) { sc[k] = -INFINITY; continue; }
+            const float *kr = kc + (size_t)(j0 + k) * stride;
+            float s4[4];
+            for (int q4 = 0; q4 < 4; q4++) {
+                float sd = 0.0f;
+                for (int d = 0; d < 16; d++) sd = fmaf(q[16 * q4 + d], kr[16 * q4 + d], sd);
+                s4[q4] = sd;
+            }
+            sc[k] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+            m = fmaxf(m, sc[k]);
+        }
+        float v32[32];
+        for (int k = 0; k < 64; k++) pr[k] = k < nk ? or_fast_exp_nonpos(sc[k] - m) : 0.0f;
+        for (int l = 0; l < 32; l++) v32[l] = pr[l] + pr[l + 32];
+        float lp = warp_tree(v32);
+        float c0 = or_fast_exp_nonpos(M - fmaxf(M, m)), c1 = or_fast_exp_nonpos(m - fmaxf(M, m));
+        L = L * c0 + lp * c1;
+        for (int d = 0; d < 64; d++) {
+            float a4[4];
+            for (int q4 = 0; q4 < 4; q4++) {
+                float a = 0.0f;
+                for (int j = 16 * q4; j < 16 * q4 + 16 && j < nk; j++)
+                    a = fmaf(pr[j], vc[(size_t)(j0 + j) * stride + d], a);
+                a4[q4] = a;
+            }
+            float ap = ((a4[0] + a4[1]) + a4[2]) + a4[3];
+            A[d] = A[d] * c0 + ap * c1;
+        }
+        M = fmaxf(M, m);
+    }
+    for (int d = 0; d < 64; d++) ctx[d] = or_bf16_round(A[d] / L);
+}
+
 /* Lin::fwd (int8 branch) parallel over blocks of output columns, k-outer inside a block. */
 static void lin_fwd_ref(const or_opt *m, const lin_t *l, const float *x, float *y) {
     int K = l->K, N = l->N;
@@ -186,8 +276,8 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
     for (int l = 0; l < c->n_layers; l++) {
         const or_opt_layer *ly = &m->w.layers[l];
         lin_t *lin = m->lins + l * 6;
-        or_layer_norm(x, ly->ln1_w, ly->ln1_b, 1, D, c->eps, h);
-        if (dev) or_bf16_round_n(h, h, (size_t)D);
+        if (dev) ln_dev_bf16(x, ly->ln1_w, ly->ln1_b, D, c->eps, h);
+        else or_layer_norm(x, ly->ln1_w, ly->ln1_b, 1, D, c->eps, h);
         lin_apply(m, &lin[0], h, q);
         lin_apply(m, &lin[1], h, kn);
         lin_apply(m, &lin[2], h, vn);
@@ -216,28 +306,14 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
                     ctx[c0 + d] = s;
                 }
             } else {
-                /* device numerics: f32 scores and softmax; sums taken exactly (f64) and
-                 * rounded once, ctx rounded to bf16 for the output projection. */
-                float mx = -INFINITY;
-                for (int j = 0; j < tk; j++) {
-                    double s = 0.0;
-                    for (int d = 0; d < HD; d++) s += (double)q[c0 + d] * (double)kc[(size_t)j * D + c0 + d];
-                    sc[j] = (float)s; mx = fmaxf(mx, sc[j]);
-                }
-                double sum = 0.0;
-                for (int j = 0; j < tk; j++) { sc[j] = expf(sc[j] - mx); sum += sc[j]; }
-                for (int d = 0; d < HD; d++) {
-                    double s = 0.0;
-                    for (int j = 0; j < tk; j++) s += (double)sc[j] * (double)vc[(size_t)j * D + c0 + d];
-                    ctx[c0 + d] = or_bf16_round((float)(s / sum));
-                }
+                attn_dev_head(q + c0, kc + c0, vc + c0, D, tk, ctx + c0);
             }
         }
         lin_apply(m, &lin[3], ctx, o);
         for (int d = 0; d < D; d++) xr[d] = x[d] + o[d];
         trace_x(m, pos, 2 * l, xr);
-        or_layer_norm(xr, ly->ln2_w, ly->ln2_b, 1, D, c->eps, h);
-        if (dev) or_bf16_round_n(h, h, (size_t)D);
+        if (dev) ln_dev_bf16(xr, ly->ln2_w, ly->ln2_b, D, c->eps, h);
+        else or_layer_norm(xr, ly->ln2_w, ly->ln2_b, 1, D, c->eps, h);
         lin_apply(m, &lin[4], h, f);
         for (int i = 0; i < F; i++) f[i] = f[i] > 0.0f ? f[i] : 0.0f;
         if (dev) or_bf16_round_n(f, f, (size_t)F);
@@ -246,9 +322,9 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
         trace_x(m, pos, 2 * l + 1, x);
     }
     if (want_logits) {
-        or_layer_norm(x, m->w.lnf_w, m->w.lnf_b, 1, D, c->eps, h);
+        if (dev) ln_dev_bf16(x, m->w.lnf_w, m->w.lnf_b, D, c->eps, h);
+        else or_layer_norm(x, m->w.lnf_w, m->w.lnf_b, 1, D, c->eps, h);
         if (dev) {
-            or_bf16_round_n(h, h, (size_t)D);
             trace_x(m, pos, 2 * c->n_layers, h);
             gemv_exact(m, m->lm_q, m->lm_scale, NULL, D, V, h, logits);
         } else {
@@ -262,6 +338,16 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
         }
     }
     free(x);
+}
+
+/* One Opt::step with the LM head: feed `id` at `pos` (positions before pos must already be
+ * in the cache), return the greedy id (last max wins); logits optional. */
+int64_t or_opt_step(or_opt *m, int64_t id, int pos, float *logits_out) {
+    float *lg = logits_out ? logits_out : (float *)malloc(sizeof(float) * (size_t)m->cfg.vocab);
+    opt_step(m, id, pos, lg, 1);
+    int64_t r = or_argmax_last(lg, (size_t)m->cfg.vocab);
+    if (!logits_out) free(lg);
+    return r;
 }
 
 /* Opt::generate (opt125m_decode.rs:296-315): prefill token by token, then greedy with

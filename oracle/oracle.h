@@ -133,6 +133,8 @@ int or_opt_generate(or_opt *m, const int64_t *prompt, int n_prompt, int n_new,
 /* debugging aid: record x after each attention / FFN residual add and the final LN output
  * (device mode) per position into trace[pos][2L+1][D]; NULL turns it off */
 void or_opt_set_trace(or_opt *m, float *trace);
+/* one Opt::step (opt125m_decode.rs:252-293) with the LM head at `pos`; returns the argmax */
+int64_t or_opt_step(or_opt *m, int64_t id, int pos, float *logits_out);
 /* quantised weights as the engine sees them (for bit-exact checks) */
 const int8_t *or_opt_qweight(const or_opt *m, int layer, int which, float const **scale);
 

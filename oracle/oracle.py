@@ -73,6 +73,8 @@ def lib():
         L.or_opt_generate.argtypes = [C.c_void_p, I64P, C.c_int, C.c_int, C.c_void_p, I64P, C.c_void_p]
         L.or_opt_generate.restype = C.c_int
         L.or_opt_set_trace.argtypes = [C.c_void_p, C.c_void_p]
+        L.or_opt_step.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_void_p]
+        L.or_opt_step.restype = C.c_int64
         L.or_opt_qweight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.POINTER(C.c_float))]
         L.or_opt_qweight.restype = C.POINTER(C.c_int8)
         _LIB = L
@@ -229,6 +231,10 @@ class OracleOpt:
         if rc != 0:
             raise RuntimeError("or_opt_generate failed")
         return (out, lg) if want_logits else out
+
+    def step(self, token_id, pos):
+        """One decode step at `pos` (earlier positions already cached); returns the argmax."""
+        return int(lib().or_opt_step(self._h, int(token_id), int(pos), None))
 
     def set_trace(self, buf):
         self._trace = buf

@@ -80,6 +80,8 @@ def lib():
         L.xdna_opt_stream_bytes_per_token.restype = sz
         L.xdna_opt_grid.argtypes = [vp]
         L.xdna_opt_grid.restype = i
+        L.xdna_opt_set_timing.argtypes = [vp, vp]
+        L.xdna_opt_set_timing.restype = i
         L.xdna_opt_set_trace.argtypes = [vp, vp]
         L.xdna_opt_set_trace.restype = i
         _LIB = L
@@ -194,6 +196,9 @@ class OptDecoder:
                stream: int = 0):
         _check(lib().xdna_opt_launch(self.handle, start_pos, n_steps, n_prompt,
                                      logits_ptr or None, stream or None))
+
+    def set_timing(self, timing_ptr: int):
+        _check(lib().xdna_opt_set_timing(self.handle, timing_ptr or None))
 
     def set_trace(self, trace_ptr: int):
         _check(lib().xdna_opt_set_trace(self.handle, trace_ptr or None))

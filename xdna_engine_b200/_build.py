@@ -33,7 +33,7 @@ def build(force=False, verbose=False):
     if not force and not needs_build():
         return LIB
     cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
-           "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off", "-shared",
+           "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off", "--fmad=false", "-shared",
            "-diag-suppress", "550",
            "-o", LIB + ".tmp"] + [os.path.join(CSRC, f) for f in SOURCES]
     if verbose:

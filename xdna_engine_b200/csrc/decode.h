@@ -15,6 +15,7 @@ constexpr int kDmax = 1024;                       // largest model width
 constexpr int kHeadDim = 64;                      // the kernel's attention head size
 constexpr int kPageTokens = 64;                   // KV page = 64 positions (the reference's TKV tile)
 constexpr int kMaxTilesPerChunk = kStageBytes / (768 + 8) / 8;   // 5 for K=768
+constexpr int kMaxPages = 64;                     // KV pages per sequence (4096 positions)
 constexpr int kRowMeta = 8;                       // per-row f32 scale + f32 bias after the rows
 
 // Row partition and chunking shared by the host packer and the kernel.  Rows are assigned
@@ -99,6 +100,7 @@ struct DecodeParams {
     uint64_t timeout_ns;
     float *trace;              // optional [n_steps][2L+1][D]: residual after attention and
                                // after the FFN of each layer, then the final LN output
+    unsigned long long *timing; // optional [2][grid][128] globaltimer stamps (first 2 steps)
 };
 
 }  // namespace xdna

@@ -25,6 +25,7 @@ cudaError_t launch_opt_decode(const DecodeParams &p, cudaStream_t st);
 cudaError_t launch_gemv_i8(const float *x, int K, const uint8_t *packed, const ChunkRef *chunks,
                            int N, float *y, cudaStream_t st);
 cudaError_t max_coresident_ctas(int *out);
+bool decode_shape_supported(int d, int f);
 }  // namespace xdna
 
 using namespace xdna;
@@ -170,6 +171,7 @@ struct XdnaOptDecoder {
     RunState *d_state = nullptr;
     float *d_logits = nullptr;      // scratch for xdna_opt_generate
     float *trace = nullptr;         // optional residual-stream record (xdna_opt_set_trace)
+    unsigned long long *timing = nullptr;  // optional phase stamps (xdna_opt_set_timing)
     size_t logits_cap = 0;
     ~XdnaOptDecoder() {
         void *ptrs[] = {d_stream, d_chunks, d_nl, d_nlm, d_emb, d_pos, d_ln, d_lnf, d_kv, d_pt, d_ll,
@@ -284,13 +286,13 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
     const XdnaOptConfig c = *cfg;
     const int D = c.d_model, F = c.ffn, L = c.n_layers, V = c.vocab, H = c.n_heads;
     if (c.head_dim != kHeadDim || H * kHeadDim != D || D % 256 || D > kDmax || F % 256 || F > kKmax ||
-        L < 1 || V < 8 || V % 8 || c.max_pos < 1) {
-        set_err("xdna_opt_create: unsupported shape (head_dim 64, d_model%256==0 <= 1024, "
-                "ffn%256==0 <= 3072, vocab%8==0)");
+        L < 1 || V < 8 || V % 8 || c.max_pos < 1 || !decode_shape_supported(D, F)) {
+        set_err("xdna_opt_create: unsupported shape (head_dim 64; (d_model, ffn) one of the "
+                "compiled widths (768, 3072) or (256, 512); vocab % 8 == 0)");
         return nullptr;
     }
-    if (max_ctx < 1 || max_ctx > c.max_pos) {
-        set_err("xdna_opt_create: max_ctx must be in [1, max_pos]");
+    if (max_ctx < 1 || max_ctx > c.max_pos || max_ctx > kMaxPages * kPageTokens) {
+        set_err("xdna_opt_create: max_ctx must be in [1, min(max_pos, 4096)]");
         return nullptr;
     }
     auto *dec = new (std::nothrow) XdnaOptDecoder();
@@ -450,6 +452,11 @@ int xdna_opt_get_tokens(XdnaOptDecoder *dec, int64_t *host, size_t off, size_t n
     return copy_tokens(dec, host, off, n, stream, false);
 }
 int xdna_opt_grid(const XdnaOptDecoder *dec) { return dec ? dec->grid : 0; }
+int xdna_opt_set_timing(XdnaOptDecoder *dec, unsigned long long *timing_dev) {
+    if (!dec) { set_err("xdna_opt_set_timing: decoder is null"); return -1; }
+    dec->timing = timing_dev;
+    return 0;
+}
 int xdna_opt_set_trace(XdnaOptDecoder *dec, float *trace_dev) {
     if (!dec) { set_err("xdna_opt_set_trace: decoder is null"); return -1; }
     dec->trace = trace_dev;
@@ -500,6 +507,7 @@ int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_promp
     p.state = dec->d_state;
     p.timeout_ns = 1000000000ull;   // 1 s per wait; normal waits are microseconds
     p.trace = dec->trace;
+    p.timing = dec->timing;
     cudaError_t e = cudaSetDevice(dec->dev->ordinal);
     if (e == cudaSuccess) e = launch_opt_decode(p, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {
