@@ -1,13 +1,11 @@
 """Parity of the B200 decode path against the CPU oracle, through the C ABI.
 
-Bar: the int8 GEMV is bit-exact with the oracle's exact limbed dot; the greedy token stream
-is identical to the oracle's device-numerics run; logits agree with it to 1e-2 relative L2
-and with the reference's own f32 host path (OPT_INT8, f32 LM head) teacher-forced on the
-same tokens to 3e-2 relative L2.  The 1e-2 (the bf16 bar of the spec) is not slack: the
-GPU and the oracle reduce LayerNorm sums and softmax sums in different orders, so about
-one bf16-rounded element per few layer-steps lands one ulp (2^-8) apart; a flip in a cached
-K/V row persists into every later step and 12 layers amplify it to ~5e-3 in the logits.
-Prompt steps before the first flip are bit-exact (checked with the residual-stream trace)."""
+Bar: the int8 GEMV is bit-exact with the oracle's exact limbed dot, and the whole decode is
+bit-exact with the oracle's device-numerics mode (same quantised weights, same bf16 rounding
+points, same reduction trees, the reference's own fast_exp_nonpos): identical greedy tokens
+and identical f32 logits.  Against the reference's own f32 host path (OPT_INT8, f32 LM
+head), teacher-forced on the GPU's tokens, logits agree to 3e-2 relative L2 (int8 LM head and
+bf16 activations vs f32)."""
 import numpy as np
 import pytest
 
@@ -16,7 +14,6 @@ from xdna_engine_b200.synth import OptConfig, OPT_125M, make_opt_weights, make_p
 
 pytestmark = pytest.mark.gpu
 
-LOGIT_TOL_DEVICE = 1e-2
 LOGIT_TOL_REF = 3e-2
 
 
@@ -74,8 +71,7 @@ def test_decode_small_matches_oracle(X, dev, grid):
     ids, lg, oids, olg = _run_pair(X, dev, SMALL, w, prompt, 70, grid=grid)
     assert len(set(ids.tolist())) > 5, "degenerate stream: test would not discriminate"
     np.testing.assert_array_equal(ids, oids)
-    for t in range(len(ids)):
-        assert rel_l2(lg[t], olg[t]) < LOGIT_TOL_DEVICE, t
+    np.testing.assert_array_equal(lg, olg)
 
 
 def test_decode_prompt_of_one_and_long_context(X, dev):
@@ -83,7 +79,7 @@ def test_decode_prompt_of_one_and_long_context(X, dev):
     prompt = make_prompt(SMALL, 1, seed=4)
     ids, lg, oids, olg = _run_pair(X, dev, SMALL, w, prompt, 200, max_ctx=256)
     np.testing.assert_array_equal(ids, oids)
-    assert max(rel_l2(lg[t], olg[t]) for t in range(len(ids))) < LOGIT_TOL_DEVICE
+    np.testing.assert_array_equal(lg, olg)
 
 
 def test_launch_split_equals_single_launch(X, dev):
@@ -116,7 +112,7 @@ def test_opt125m_config_matches_oracle(X, dev):
     orc = O.OracleOpt(OPT_125M, w, O.MODE_DEVICE)
     oids, olg = orc.generate(prompt, 24, want_logits=True)   # oracle cost bounds the prefix
     np.testing.assert_array_equal(ids[:24], oids)
-    assert max(rel_l2(lg[t], olg[t]) for t in range(24)) < LOGIT_TOL_DEVICE
+    np.testing.assert_array_equal(lg[:24], olg)
     ref = O.OracleOpt(OPT_125M, w, O.MODE_REF_F32)
     _, rlg = ref.generate(prompt, 8, want_logits=True, force=ids[:8])
     assert max(rel_l2(lg[t], rlg[t]) for t in range(8)) < LOGIT_TOL_REF
