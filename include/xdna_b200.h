@@ -50,6 +50,19 @@ int xdna_quant_i8_cols(const float *w, int K, int N, int8_t *q_nk, float *scale)
 int xdna_gemv_i8(XdnaDevice *dev, const float *x, int K, const int8_t *q_nk, const float *scale,
                  const float *bias, int N, float *y);
 
+/* The same GEMV for callers that cannot allocate device memory -- a host whose device
+ * memory belongs to another allocator (a framework's caching allocator, an arena reserved at
+ * start-up) where a cudaMalloc would fail or fragment the pool.  It has no counterpart in the
+ * reference.  Arguments and result are those of xdna_gemv_i8, on device ordinal `device`;
+ * instead of cudaMalloc'd staging it uses one fixed 8 MiB __device__ array that every GPU
+ * loading this library keeps until exit, so the call allocates nothing.  Calls whose staging
+ * (about 2*N*K + 12*N + 4*K bytes) exceeds 8 MiB are rejected with an error.  The first call
+ * on a device looks up the array's address and should come before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU race and must be serialised.
+ * Synchronous; returns 0, or -1 with xdna_last_error() set. */
+int xdna_gemv_i8_noalloc(int device, const float *x, int K, const int8_t *q_nk,
+                         const float *scale, const float *bias, int N, float *y);
+
 /* ------------------------------------------------ opt-125m greedy decode (Opt::generate) */
 typedef struct {
     int n_layers, d_model, n_heads, head_dim, ffn, vocab, max_pos;

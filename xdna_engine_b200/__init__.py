@@ -61,6 +61,8 @@ def lib():
         L.xdna_quant_i8_cols.restype = i
         L.xdna_gemv_i8.argtypes = [vp, vp, i, vp, vp, vp, i, vp]
         L.xdna_gemv_i8.restype = i
+        L.xdna_gemv_i8_noalloc.argtypes = [i, vp, i, vp, vp, vp, i, vp]
+        L.xdna_gemv_i8_noalloc.restype = i
         L.xdna_opt_create.argtypes = [vp, vp, vp, i, i]
         L.xdna_opt_create.restype = vp
         L.xdna_opt_free.argtypes = [vp]

@@ -145,6 +145,10 @@ QMat stack(const std::vector<const QMat *> &ms) {
 
 }  // namespace
 
+namespace xdna {
+void set_last_error_message(const std::string &m) { set_err(m); }
+}  // namespace xdna
+
 struct XdnaDevice {
     int ordinal = 0;
     int sms = 0;
