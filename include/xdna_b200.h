@@ -63,6 +63,20 @@ int xdna_gemv_i8(XdnaDevice *dev, const float *x, int K, const int8_t *q_nk, con
 int xdna_gemv_i8_noalloc(int device, const float *x, int K, const int8_t *q_nk,
                          const float *scale, const float *bias, int N, float *y);
 
+/* ------------------------------------------- encoder GEMM (CtxAOp::forward / FfnMm2) */
+/* C[M, N] = epi(A[M, K] . B[N, K]^T) on the tcgen05 tensor cores: bf16 operands (device, row
+ * major, A rows = tokens, B = weight [out, in]), f32 accumulation, epilogue + bias[N] (f32,
+ * nullable), then the exact-erf GELU if gelu != 0 (the reference's form,
+ * npu-asr-host/src/lib.rs:464-495), then + residual[M, N] (bf16, nullable); C bf16 [M, N].
+ * Replaces the reference's resident-GEMM dispatch + host epilogue (rust/npu-asr/src/
+ * ctx2.rs:674-770, 1195-1288; npu-engine/src/bert/encoder.rs:43-57).  Needs N % 128 == 0,
+ * K % 64 == 0 and 16-byte aligned rows.  Asynchronous on `stream`; 0 or -1. */
+int xdna_gemm_bf16(const uint16_t *A, const uint16_t *B, const float *bias, const uint16_t *residual,
+                   uint16_t *C, int M, int N, int K, int gelu, void *stream);
+/* After the stream has finished: -1 (with xdna_last_error) if a GEMM's bounded wait expired
+ * since the last check, else 0. */
+int xdna_gemm_check(void);
+
 /* ------------------------------------------------ opt-125m greedy decode (Opt::generate) */
 typedef struct {
     int n_layers, d_model, n_heads, head_dim, ffn, vocab, max_pos;

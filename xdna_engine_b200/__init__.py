@@ -63,6 +63,9 @@ def lib():
         L.xdna_gemv_i8.restype = i
         L.xdna_gemv_i8_noalloc.argtypes = [i, vp, i, vp, vp, vp, i, vp]
         L.xdna_gemv_i8_noalloc.restype = i
+        L.xdna_gemm_bf16.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp]
+        L.xdna_gemm_bf16.restype = i
+        L.xdna_gemm_check.restype = i
         L.xdna_opt_create.argtypes = [vp, vp, vp, i, i]
         L.xdna_opt_create.restype = vp
         L.xdna_opt_free.argtypes = [vp]

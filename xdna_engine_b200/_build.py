@@ -9,8 +9,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libxdna_b200.so")
-SOURCES = ["decode_kernel.cu", "engine.cu", "noalloc.cu"]
-HEADERS = ["decode.h", "ptx.cuh"]
+SOURCES = ["decode_kernel.cu", "engine.cu", "noalloc.cu", "gemm_tc.cu"]
+HEADERS = ["decode.h", "ptx.cuh", "tc.cuh"]
 
 
 def nvcc():

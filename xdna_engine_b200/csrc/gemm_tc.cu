@@ -1,0 +1,265 @@
+// gemm_tc.cu -- encoder GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the reference's resident NPU GEMM engine for encoder projections,
+// CtxAOp::forward_view (rust/npu-asr/src/ctx2.rs:674-770) with its host bias / GELU epilogue
+// (bert/encoder.rs:43-57, npu-asr-host gelu lib.rs:464-495) and FfnMm2's K-split fc2
+// (ctx2.rs:1195-1288): C[M, N] = epi(A[M, K] . B[N, K]^T), bf16 operands, f32 accumulation
+// (in TMEM, so the K reduction is never split), fused epilogue: + bias, optional exact-erf
+// GELU (the reference's Abramowitz-Stegun form), optional + residual, bf16 out.
+//
+// One CTA = one 128 x 128 output tile: warp 0 issues TMA loads of A and B k-blocks (64 bf16 =
+// 128 B per row, SWIZZLE_128B) into a 3-stage ring; warp 1 allocates 128 TMEM columns and
+// issues tcgen05.mma (M 128, N 128, K 16) from one thread, releasing each stage with
+// tcgen05.commit; warps 2-5 drain the accumulator with tcgen05.ld (each warp its 32-lane TMEM
+// quarter) and write bf16 rows.  ~97 KB shared memory, so two CTAs share an SM and one
+// CTA's epilogue overlaps the other's main loop.  Every wait is bounded.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "../../include/xdna_b200.h"
+#include "ptx.cuh"
+#include "tc.cuh"
+
+namespace xdna {
+void set_last_error_message(const std::string &m);
+
+namespace gemm {
+
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+constexpr int THREADS = 192;
+constexpr uint64_t TIMEOUT_NS = 2000000000ull;
+
+static __device__ unsigned int g_gemm_error;
+
+struct Epi {
+    const float *bias;          // [N] or null
+    const uint16_t *residual;   // [M, ldr] bf16 or null
+    int ldr;
+    int gelu;
+    uint16_t *out;              // [M, ldc] bf16
+    int ldc;
+};
+
+__device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, unsigned code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > TIMEOUT_NS) {
+            atomicCAS(&g_gemm_error, 0u, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+// the reference's GELU: 0.5 x (1 + erf(x / sqrt 2)) with the Abramowitz-Stegun 7.1.26 erf
+// (rust/npu-asr-host/src/lib.rs:464-495)
+__device__ __forceinline__ float gelu_erf_as(float v) {
+    const float x = v * 0.70710678118654752440f;
+    const float sign = x < 0.0f ? -1.0f : 1.0f;
+    const float ax = fabsf(x);
+    const float t = 1.0f / (1.0f + 0.3275911f * ax);
+    const float y = 1.0f - (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
+                            0.254829592f) * t * expf(-ax * ax);
+    return 0.5f * v * (1.0f + sign * y);
+}
+
+__global__ void __launch_bounds__(THREADS, 2)
+gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                 int K, Epi epi) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *stA = smem;                            // [STAGES][BM][BK] bf16, swizzled
+    uint8_t *stB = smem + STAGES * A_BYTES;         // [STAGES][BN][BK] bf16, swizzled
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *tfull = empty + STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfull + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int nk = K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(tfull, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) { tc::tmem_alloc(tmem_slot, BN); tc::tmem_relinquish(); }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer
+        int issued = 0;
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % STAGES;
+            if (kb >= STAGES && !wait_bounded(&empty[s], ((kb / STAGES) - 1) & 1, 1u)) break;
+            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+            tc::tma_load_2d(stA + s * A_BYTES, &tmA, kb * BK, m0, &full[s]);
+            tc::tma_load_2d(stB + s * B_BYTES, &tmB, kb * BK, n0, &full[s]);
+            issued++;
+        }
+        // drain: the loads in flight must land before the CTA exits
+        for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++)
+            wait_bounded(&full[kb % STAGES], (kb / STAGES) & 1, 2u);
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer (one thread)
+        constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % STAGES;
+            if (!wait_bounded(&full[s], (kb / STAGES) & 1, 3u)) break;
+            tc::fence_after_sync();
+            const uint64_t da = tc::desc_k_sw128(smem_u32(stA + s * A_BYTES));
+            const uint64_t db = tc::desc_k_sw128(smem_u32(stB + s * B_BYTES));
+#pragma unroll
+            for (int k = 0; k < BK / 16; k++)   // K 16 per MMA = 32 bytes = +2 in the 16-byte start field
+                tc::mma_bf16(tmem, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc::commit(&empty[s]);
+        }
+        tc::commit(tfull);
+    } else if (warp >= 2) {
+        // ---------------- epilogue: TMEM quarter (warp & 3) holds rows 32*(warp & 3) + lane
+        const int q = warp & 3;
+        const int row = m0 + 32 * q + lane;
+        wait_bounded(tfull, 0, 4u);
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
+            tc::tmem_ld_wait();
+            if (row < M) {
+                const int col = n0 + c0;
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    float y = __uint_as_float(r[j]);
+                    if (epi.bias) y += epi.bias[col + j];
+                    if (epi.gelu) y = gelu_erf_as(y);
+                    v[j] = y;
+                }
+                if (epi.residual) {
+                    const uint4 *rp = reinterpret_cast<const uint4 *>(epi.residual + (size_t)row * epi.ldr + col);
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const uint4 w = rp[u];
+                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            v[8 * u + 2 * e] += bf16lo(ws[e]);
+                            v[8 * u + 2 * e + 1] += bf16hi(ws[e]);
+                        }
+                    }
+                }
+                uint4 *op = reinterpret_cast<uint4 *>(epi.out + (size_t)row * epi.ldc + col);
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    uint4 w;
+                    w.x = bf16bits(v[8 * u + 0]) | (bf16bits(v[8 * u + 1]) << 16);
+                    w.y = bf16bits(v[8 * u + 2]) | (bf16bits(v[8 * u + 3]) << 16);
+                    w.z = bf16bits(v[8 * u + 4]) | (bf16bits(v[8 * u + 5]) << 16);
+                    w.w = bf16bits(v[8 * u + 6]) | (bf16bits(v[8 * u + 7]) << 16);
+                    op[u] = w;
+                }
+            }
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) tc::tmem_dealloc(tmem, BN);
+}
+
+// ------------------------------------------------------------------------------------ host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// K-major bf16 matrix [rows, K] (row stride ld elements) as 64 x 128 boxes with 128 B swizzle
+bool make_tmap(CUtensorMap *tm, const void *base, int rows, int K, int ld) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {BK, 128};
+    cuuint32_t es[2] = {1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M, int N, int K, const Epi &epi,
+                   cudaStream_t st) {
+    CUtensorMap ta, tb;
+    if (!make_tmap(&ta, A, M, K, lda) || !make_tmap(&tb, B, N, K, ldb)) return cudaErrorInvalidValue;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    dim3 grid(N / BN, (M + BM - 1) / BM);
+    gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, M, N, K, epi);
+    return cudaGetLastError();
+}
+
+}  // namespace gemm
+
+cudaError_t gemm_bf16(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M, int N, int K,
+                      const float *bias, const uint16_t *residual, int ldr, int gelu, uint16_t *C, int ldc,
+                      cudaStream_t st) {
+    gemm::Epi e{bias, residual, ldr, gelu, C, ldc};
+    return gemm::launch(A, lda, B, ldb, M, N, K, e, st);
+}
+
+unsigned gemm_error_and_clear() {
+    unsigned v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, gemm::g_gemm_error, sizeof v);
+    cudaMemcpyToSymbol(gemm::g_gemm_error, &z, sizeof z);
+    return v;
+}
+
+}  // namespace xdna
+
+extern "C" int xdna_gemm_bf16(const uint16_t *A, const uint16_t *B, const float *bias, const uint16_t *residual,
+                              uint16_t *C, int M, int N, int K, int gelu, void *stream) {
+    using namespace xdna;
+    if (!A || !B || !C) { set_last_error_message("xdna_gemm_bf16: null pointer"); return -1; }
+    if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 64) {
+        set_last_error_message("xdna_gemm_bf16: need M > 0, N % 128 == 0, K % 64 == 0");
+        return -1;
+    }
+    cudaError_t e = gemm_bf16(A, K, B, K, M, N, K, bias, residual, N, gelu, C, N, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        set_last_error_message(std::string("xdna_gemm_bf16: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+extern "C" int xdna_gemm_check(void) {
+    const unsigned v = xdna::gemm_error_and_clear();
+    if (v) {
+        xdna::set_last_error_message("tensor-core GEMM: a bounded wait expired (code " + std::to_string(v) + ")");
+        return -1;
+    }
+    return 0;
+}
