@@ -69,7 +69,7 @@ int xdna_gemv_i8_noalloc(int device, const float *x, int K, const int8_t *q_nk,
  * nullable), then the exact-erf GELU if gelu != 0 (the reference's form,
  * npu-asr-host/src/lib.rs:464-495), then + residual[M, N] (bf16, nullable); C bf16 [M, N].
  * Replaces the reference's resident-GEMM dispatch + host epilogue (rust/npu-asr/src/
- * ctx2.rs:674-770, 1195-1288; npu-engine/src/bert/encoder.rs:43-57).  Needs N % 128 == 0,
+ * ctx2.rs:674-770, 1195-1288; npu-engine/src/bert/encoder.rs:43-57).  Needs N % 256 == 0,
  * K % 64 == 0 and 16-byte aligned rows.  Asynchronous on `stream`; 0 or -1. */
 int xdna_gemm_bf16(const uint16_t *A, const uint16_t *B, const float *bias, const uint16_t *residual,
                    uint16_t *C, int M, int N, int K, int gelu, void *stream);

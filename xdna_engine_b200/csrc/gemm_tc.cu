@@ -7,12 +7,13 @@
 // (in TMEM, so the K reduction is never split), fused epilogue: + bias, optional exact-erf
 // GELU (the reference's Abramowitz-Stegun form), optional + residual, bf16 out.
 //
-// One CTA = one 128 x 128 output tile: warp 0 issues TMA loads of A and B k-blocks (64 bf16 =
-// 128 B per row, SWIZZLE_128B) into a 3-stage ring; warp 1 allocates 128 TMEM columns and
-// issues tcgen05.mma (M 128, N 128, K 16) from one thread, releasing each stage with
-// tcgen05.commit; warps 2-5 drain the accumulator with tcgen05.ld (each warp its 32-lane TMEM
-// quarter) and write bf16 rows.  ~97 KB shared memory, so two CTAs share an SM and one
-// CTA's epilogue overlaps the other's main loop.  Every wait is bounded.
+// Persistent kernel, one CTA per SM, 128 x 256 output tiles: warp 0 issues TMA loads of A
+// and B k-blocks (64 bf16 = 128 B per row, SWIZZLE_128B, no multicast) into a 4-stage ring;
+// warp 1 allocates all 512 TMEM columns (two 256-column f32 accumulators) and issues
+// tcgen05.mma (M 128, N 256, K 16) from one thread, releasing each stage with
+// tcgen05.commit; warps 2-9 drain an accumulator with tcgen05.ld (two warps per 32-lane TMEM
+// quarter, half the columns each) while the MMAs of the next tile fill the other one.  Every wait is bounded; TMEM
+// is freed on every exit path.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -30,10 +31,11 @@ void set_last_error_message(const std::string &m);
 
 namespace gemm {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
-constexpr int THREADS = 192;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 2 * BN * 4 + 256;
+constexpr int THREADS = 320;
+constexpr int EPI_THREADS = 256;
 constexpr uint64_t TIMEOUT_NS = 2000000000ull;
 
 static __device__ unsigned int g_gemm_error;
@@ -51,6 +53,7 @@ __device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, uns
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(bar, parity)) {
+        if (*(volatile unsigned *)&g_gemm_error) return false;
         if (globaltimer_ns() - t0 > TIMEOUT_NS) {
             atomicCAS(&g_gemm_error, 0u, code);
             return false;
@@ -63,36 +66,44 @@ __device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, uns
 // (rust/npu-asr-host/src/lib.rs:464-495)
 __device__ __forceinline__ float gelu_erf_as(float v) {
     const float x = v * 0.70710678118654752440f;
-    const float sign = x < 0.0f ? -1.0f : 1.0f;
     const float ax = fabsf(x);
-    const float t = 1.0f / (1.0f + 0.3275911f * ax);
-    const float y = 1.0f - (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
-                            0.254829592f) * t * expf(-ax * ax);
-    return 0.5f * v * (1.0f + sign * y);
+    const float t = __frcp_rn(fmaf(0.3275911f, ax, 1.0f));
+    float p = fmaf(1.061405429f, t, -1.453152027f);
+    p = fmaf(p, t, 1.421413741f);
+    p = fmaf(p, t, -0.284496736f);
+    p = fmaf(p, t, 0.254829592f);
+    const float y = fmaf(-p * t, __expf(-ax * ax), 1.0f);
+    return 0.5f * v * (1.0f + copysignf(y, x));
 }
 
-__global__ void __launch_bounds__(THREADS, 2)
+// Persistent: CTA b handles tiles b, b + grid, ...; tile t -> (m = t / n_tiles, n = t % n_tiles)
+// so CTAs running together share A rows in L2.  Two TMEM accumulators of 256 columns let the
+// epilogue of tile i overlap the MMAs of tile i + 1.
+__global__ void __launch_bounds__(THREADS, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                  int K, Epi epi) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *stA = smem;                            // [STAGES][BM][BK] bf16, swizzled
     uint8_t *stB = smem + STAGES * A_BYTES;         // [STAGES][BN][BK] bf16, swizzled
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    float *sbias = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES);   // [2][BN]
+    uint64_t *full = reinterpret_cast<uint64_t *>(sbias + 2 * BN);
     uint64_t *empty = full + STAGES;
-    uint64_t *tfull = empty + STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfull + 1);
+    uint64_t *tfull = empty + STAGES;               // [2]
+    uint64_t *tempty = tfull + 2;                   // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int nk = K / BK;
+    const int n_tiles = N / BN, m_tiles = (M + BM - 1) / BM;
+    const int total = n_tiles * m_tiles;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        mbar_init(tfull, 1);
+        for (int a = 0; a < 2; a++) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], EPI_THREADS / 32); }
         mbar_fence_init();
     }
-    if (warp == 1) { tc::tmem_alloc(tmem_slot, BN); tc::tmem_relinquish(); }
+    if (warp == 1) { tc::tmem_alloc(tmem_slot, 2 * BN); tc::tmem_relinquish(); }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -100,83 +111,103 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer
-        int issued = 0;
-        for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % STAGES;
-            if (kb >= STAGES && !wait_bounded(&empty[s], ((kb / STAGES) - 1) & 1, 1u)) break;
-            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            tc::tma_load_2d(stA + s * A_BYTES, &tmA, kb * BK, m0, &full[s]);
-            tc::tma_load_2d(stB + s * B_BYTES, &tmB, kb * BK, n0, &full[s]);
-            issued++;
+        uint32_t c = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+            const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
+            for (int kb = 0; kb < nk; kb++, c++) {
+                const int s = c % STAGES;
+                if (c >= STAGES && !wait_bounded(&empty[s], ((c / STAGES) - 1) & 1, 1u)) { ok = false; break; }
+                mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                tc::tma_load_2d(stA + s * A_BYTES, &tmA, kb * BK, m0, &full[s]);
+                tc::tma_load_2d(stB + s * B_BYTES, &tmB, kb * BK, n0, &full[s]);
+            }
         }
         // drain: the loads in flight must land before the CTA exits
-        for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++)
-            wait_bounded(&full[kb % STAGES], (kb / STAGES) & 1, 2u);
+        for (uint32_t q = c > STAGES ? c - STAGES : 0; q < c; q++) wait_bounded(&full[q % STAGES], (q / STAGES) & 1, 2u);
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer (one thread)
         constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
-        for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % STAGES;
-            if (!wait_bounded(&full[s], (kb / STAGES) & 1, 3u)) break;
+        uint32_t c = 0;
+        int i = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, i++) {
+            const int acc = i & 1;
+            if (ok && i >= 2 && !wait_bounded(&tempty[acc], ((i >> 1) - 1) & 1, 3u)) ok = false;
             tc::fence_after_sync();
-            const uint64_t da = tc::desc_k_sw128(smem_u32(stA + s * A_BYTES));
-            const uint64_t db = tc::desc_k_sw128(smem_u32(stB + s * B_BYTES));
+            const uint32_t d = tmem + (uint32_t)(acc * BN);
+            for (int kb = 0; kb < nk && ok; kb++, c++) {
+                const int s = c % STAGES;
+                if (!wait_bounded(&full[s], (c / STAGES) & 1, 4u)) { ok = false; break; }
+                tc::fence_after_sync();
+                const uint64_t da = tc::desc_k_sw128(smem_u32(stA + s * A_BYTES));
+                const uint64_t db = tc::desc_k_sw128(smem_u32(stB + s * B_BYTES));
 #pragma unroll
-            for (int k = 0; k < BK / 16; k++)   // K 16 per MMA = 32 bytes = +2 in the 16-byte start field
-                tc::mma_bf16(tmem, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            tc::commit(&empty[s]);
+                for (int k = 0; k < BK / 16; k++)   // K 16 per MMA = 32 bytes = +2 in the start field
+                    tc::mma_bf16(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                tc::commit(&empty[s]);
+            }
+            tc::commit(&tfull[acc]);   // always signalled, so the epilogue never waits forever
         }
-        tc::commit(tfull);
     } else if (warp >= 2) {
-        // ---------------- epilogue: TMEM quarter (warp & 3) holds rows 32*(warp & 3) + lane
-        const int q = warp & 3;
-        const int row = m0 + 32 * q + lane;
-        wait_bounded(tfull, 0, 4u);
-        tc::fence_after_sync();
+        // ---------------- epilogue: 8 warps; TMEM lane quarter (warp & 3) holds rows
+        // 32*(warp & 3) + lane, and warp half h = (warp - 2) / 4 takes columns [128h, 128h+128)
+        const int q = warp & 3, h = (warp - 2) >> 2;
+        const int et = threadIdx.x - 64;
+        int i = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, i++) {
+            const int acc = i & 1;
+            const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
+            const int row = m0 + 32 * q + lane;
+            float *bs = sbias + acc * BN;
+            for (int j = et; j < BN; j += EPI_THREADS) bs[j] = epi.bias ? epi.bias[n0 + j] : 0.0f;
+            named_bar(2, EPI_THREADS);
+            wait_bounded(&tfull[acc], (i >> 1) & 1, 5u);
+            tc::fence_after_sync();
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-            uint32_t r[32];
-            tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
-            tc::tmem_ld_wait();
-            if (row < M) {
-                const int col = n0 + c0;
-                float v[32];
+            for (int c0 = 128 * h; c0 < 128 * h + 128; c0 += 64) {
+                uint32_t r[64];
+                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + c0);
+                tc::tmem_ld32(ta, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+                tc::tmem_ld32(ta + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+                tc::tmem_ld_wait();
+                if (row < M) {
+                    const int col = n0 + c0;
+                    const uint4 *rp = epi.residual
+                        ? reinterpret_cast<const uint4 *>(epi.residual + (size_t)row * epi.ldr + col) : nullptr;
+                    uint4 *op = reinterpret_cast<uint4 *>(epi.out + (size_t)row * epi.ldc + col);
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    float y = __uint_as_float(r[j]);
-                    if (epi.bias) y += epi.bias[col + j];
-                    if (epi.gelu) y = gelu_erf_as(y);
-                    v[j] = y;
-                }
-                if (epi.residual) {
-                    const uint4 *rp = reinterpret_cast<const uint4 *>(epi.residual + (size_t)row * epi.ldr + col);
+                    for (int u = 0; u < 8; u++) {
+                        float v[8];
 #pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const uint4 w = rp[u];
-                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            v[8 * u + 2 * e] += bf16lo(ws[e]);
-                            v[8 * u + 2 * e + 1] += bf16hi(ws[e]);
+                        for (int j = 0; j < 8; j++) {
+                            float y = __uint_as_float(r[8 * u + j]) + bs[c0 + 8 * u + j];
+                            if (epi.gelu) y = gelu_erf_as(y);
+                            v[j] = y;
                         }
+                        if (rp) {
+                            const uint4 w = rp[u];
+                            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                            for (int e = 0; e < 4; e++) { v[2 * e] += bf16lo(ws[e]); v[2 * e + 1] += bf16hi(ws[e]); }
+                        }
+                        uint4 w;
+                        w.x = bf16bits(v[0]) | (bf16bits(v[1]) << 16);
+                        w.y = bf16bits(v[2]) | (bf16bits(v[3]) << 16);
+                        w.z = bf16bits(v[4]) | (bf16bits(v[5]) << 16);
+                        w.w = bf16bits(v[6]) | (bf16bits(v[7]) << 16);
+                        op[u] = w;
                     }
                 }
-                uint4 *op = reinterpret_cast<uint4 *>(epi.out + (size_t)row * epi.ldc + col);
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    uint4 w;
-                    w.x = bf16bits(v[8 * u + 0]) | (bf16bits(v[8 * u + 1]) << 16);
-                    w.y = bf16bits(v[8 * u + 2]) | (bf16bits(v[8 * u + 3]) << 16);
-                    w.z = bf16bits(v[8 * u + 4]) | (bf16bits(v[8 * u + 5]) << 16);
-                    w.w = bf16bits(v[8 * u + 6]) | (bf16bits(v[8 * u + 7]) << 16);
-                    op[u] = w;
-                }
             }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
         }
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 1) tc::tmem_dealloc(tmem, BN);
+    if (warp == 1) tc::tmem_dealloc(tmem, 2 * BN);
 }
 
 // ------------------------------------------------------------------------------------ host
@@ -194,12 +225,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // K-major bf16 matrix [rows, K] (row stride ld elements) as 64 x 128 boxes with 128 B swizzle
-bool make_tmap(CUtensorMap *tm, const void *base, int rows, int K, int ld) {
+bool make_tmap(CUtensorMap *tm, const void *base, int rows, int K, int ld, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    cuuint32_t box[2] = {BK, 128};
+    cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
     cuuint32_t es[2] = {1, 1};
     return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -209,15 +240,21 @@ bool make_tmap(CUtensorMap *tm, const void *base, int rows, int K, int ld) {
 cudaError_t launch(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M, int N, int K, const Epi &epi,
                    cudaStream_t st) {
     CUtensorMap ta, tb;
-    if (!make_tmap(&ta, A, M, K, lda) || !make_tmap(&tb, B, N, K, ldb)) return cudaErrorInvalidValue;
+    if (!make_tmap(&ta, A, M, K, lda, BM) || !make_tmap(&tb, B, N, K, ldb, BN)) return cudaErrorInvalidValue;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    dim3 grid(N / BN, (M + BM - 1) / BM);
-    gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, M, N, K, epi);
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const int tiles = (N / BN) * ((M + BM - 1) / BM);
+    gemm_bf16_kernel<<<tiles < sms ? tiles : sms, THREADS, SMEM_BYTES, st>>>(ta, tb, M, N, K, epi);
     return cudaGetLastError();
 }
 
@@ -243,8 +280,8 @@ extern "C" int xdna_gemm_bf16(const uint16_t *A, const uint16_t *B, const float 
                               uint16_t *C, int M, int N, int K, int gelu, void *stream) {
     using namespace xdna;
     if (!A || !B || !C) { set_last_error_message("xdna_gemm_bf16: null pointer"); return -1; }
-    if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 64) {
-        set_last_error_message("xdna_gemm_bf16: need M > 0, N % 128 == 0, K % 64 == 0");
+    if (M <= 0 || N <= 0 || K <= 0 || N % 256 || K % 64) {
+        set_last_error_message("xdna_gemm_bf16: need M > 0, N % 256 == 0, K % 64 == 0");
         return -1;
     }
     cudaError_t e = gemm_bf16(A, K, B, K, M, N, K, bias, residual, N, gelu, C, N, (cudaStream_t)stream);
