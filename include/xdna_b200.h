@@ -77,6 +77,47 @@ int xdna_gemm_bf16(const uint16_t *A, const uint16_t *B, const float *bias, cons
  * since the last check, else 0. */
 int xdna_gemm_check(void);
 
+/* ------------------------------------------------ BGE / BERT embeddings (EmbedPipeline) */
+typedef struct {
+    int n_layers, d_model, n_heads, ffn, vocab, max_pos;
+    float eps;                 /* LayerNorm eps (BERT: 1e-12) */
+    int pooling;               /* 0 = CLS row, 1 = mean over valid rows (bert/head.rs:20-47) */
+} XdnaBertConfig;
+
+typedef struct {               /* f32, linear weights [K, N] = [in, out] */
+    const float *q_w, *q_b, *k_w, *k_b, *v_w, *v_b, *o_w, *o_b;
+    const float *attn_ln_w, *attn_ln_b;
+    const float *ffn1_w, *ffn1_b, *ffn2_w, *ffn2_b;
+    const float *out_ln_w, *out_ln_b;
+} XdnaBertLayer;
+
+typedef struct {
+    const float *word_emb;     /* [vocab, D] */
+    const float *pos_emb;      /* [max_pos, D] */
+    const float *type_emb;     /* [>= 1, D]; row 0 is used (single segment) */
+    const float *emb_ln_w, *emb_ln_b;
+    const XdnaBertLayer *layers;
+} XdnaBertWeights;
+
+typedef struct XdnaBert XdnaBert;
+
+/* Load a BERT-base-shaped embedder (d_model 768, 12 heads, ffn 3072): weights are rounded to
+ * bf16 and kept resident on the current device; buffers hold up to max_tokens packed tokens
+ * and max_seqs sequences.  Replaces Model::load for an embed scenario (rust/npu-engine/src/
+ * api.rs:44-100, bert/mod.rs:24-46).  NULL on error. */
+XdnaBert *xdna_bert_create(XdnaDevice *dev, const XdnaBertConfig *cfg, const XdnaBertWeights *w,
+                           int max_tokens, int max_seqs);
+void xdna_bert_free(XdnaBert *m);
+/* Embed n_seqs token-id sequences (ids concatenated, seq_lens[s] tokens each, [CLS] first):
+ * frontend (word + position + type-0, LayerNorm), the encoder blocks, then pooling + L2 --
+ * EmbedPipeline::embed without the tokenizer (bert/frontend.rs:37-61, encoder.rs:43-57,
+ * head.rs:20-47).  Host in, host out ([n_seqs, 768] f32).  Returns 0 or -1. */
+int xdna_bert_embed(XdnaBert *m, const int32_t *ids, const int32_t *seq_lens, int n_seqs, float *out);
+/* Device-resident form: ids / tok_pos [n_tokens] (position of each token in its sequence),
+ * cu [n_seqs + 1] sequence starts, out_dev [n_seqs, 768]; asynchronous on `stream`. */
+int xdna_bert_encode_device(XdnaBert *m, const int32_t *ids, const int32_t *tok_pos, const int32_t *cu,
+                            int n_tokens, int n_seqs, int max_len, float *out_dev, void *stream);
+
 /* ------------------------------------------------ opt-125m greedy decode (Opt::generate) */
 typedef struct {
     int n_layers, d_model, n_heads, head_dim, ffn, vocab, max_pos;

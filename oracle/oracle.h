@@ -138,6 +138,26 @@ int64_t or_opt_step(or_opt *m, int64_t id, int pos, float *logits_out);
 /* quantised weights as the engine sees them (for bit-exact checks) */
 const int8_t *or_opt_qweight(const or_opt *m, int layer, int which, float const **scale);
 
+/* ---- BGE / BERT embedder (rust/npu-engine/src/bert/{frontend,encoder,head}.rs) ---- */
+typedef struct {
+    int n_layers, d_model, n_heads, ffn, vocab, max_pos;
+    float eps;
+    int pooling;               /* 0 CLS, 1 mean */
+} or_bert_cfg;
+typedef struct {               /* linear weights [K, N] */
+    const float *q_w, *q_b, *k_w, *k_b, *v_w, *v_b, *o_w, *o_b;
+    const float *attn_ln_w, *attn_ln_b;
+    const float *ffn1_w, *ffn1_b, *ffn2_w, *ffn2_b;
+    const float *out_ln_w, *out_ln_b;
+} or_bert_layer;
+typedef struct {
+    const float *word_emb, *pos_emb, *type_emb, *emb_ln_w, *emb_ln_b;
+    const or_bert_layer *layers;
+} or_bert_weights;
+/* embeddings [n_seqs, D] of the token-id sequences (concatenated ids, seq_lens each) */
+int or_bert_embed(const or_bert_cfg *c, const or_bert_weights *w, const int32_t *ids,
+                  const int32_t *seq_lens, int n_seqs, float *out, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

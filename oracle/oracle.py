@@ -73,6 +73,9 @@ def lib():
         L.or_opt_generate.argtypes = [C.c_void_p, I64P, C.c_int, C.c_int, C.c_void_p, I64P, C.c_void_p]
         L.or_opt_generate.restype = C.c_int
         L.or_opt_set_trace.argtypes = [C.c_void_p, C.c_void_p]
+        L.or_bert_embed.argtypes = [C.c_void_p, C.c_void_p, np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"),
+                                    np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"), C.c_int, F32P, C.c_int]
+        L.or_bert_embed.restype = C.c_int
         L.or_opt_step.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_void_p]
         L.or_opt_step.restype = C.c_int64
         L.or_opt_qweight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.POINTER(C.c_float))]
@@ -264,3 +267,46 @@ class OracleOpt:
             self.close()
         except Exception:
             pass
+
+
+# ---------------------------------------------------------------- BGE / BERT embedder
+_BERT_LAYER = ("q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "o_w", "o_b", "attn_ln_w", "attn_ln_b",
+               "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b", "out_ln_w", "out_ln_b")
+
+
+class _BertCfg(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("d_model", C.c_int), ("n_heads", C.c_int), ("ffn", C.c_int),
+                ("vocab", C.c_int), ("max_pos", C.c_int), ("eps", C.c_float), ("pooling", C.c_int)]
+
+
+class _BertLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _BERT_LAYER]
+
+
+class _BertWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("word_emb", "pos_emb", "type_emb", "emb_ln_w", "emb_ln_b", "layers")]
+
+
+def bert_embed(cfg, w, ids, seq_lens, nthreads=None):
+    """or_bert_embed: the reference's f32 host embedder on (ids, seq_lens); [n, D] f32."""
+    keep = []
+
+    def p(a):
+        a = _f32(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    c = _BertCfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.ffn, cfg.vocab, cfg.max_pos, cfg.eps,
+                 cfg.pooling)
+    layers = (_BertLayer * cfg.n_layers)()
+    for i, ly in enumerate(w["layers"]):
+        for n in _BERT_LAYER:
+            setattr(layers[i], n, p(ly[n]))
+    ww = _BertWeights(p(w["word_emb"]), p(w["pos_emb"]), p(w["type_emb"]), p(w["emb_ln_w"]),
+                      p(w["emb_ln_b"]), C.addressof(layers))
+    ids = np.ascontiguousarray(ids, np.int32)
+    lens = np.ascontiguousarray(seq_lens, np.int32)
+    out = np.empty((lens.size, cfg.d_model), np.float32)
+    lib().or_bert_embed(C.addressof(c), C.addressof(ww), ids, lens, lens.size, out,
+                        nthreads or os.cpu_count() or 1)
+    return out

@@ -132,6 +132,61 @@ def opt_hf_fixture():
     print("opt_hf_golden.npz: tokens", toks)
 
 
+BERT_SMALL = dict(n_layers=2, d_model=64, n_heads=2, ffn=128, vocab=300, max_pos=40, eps=1e-12,
+                  pooling=0)
+BERT_SMALL_SEED = 5
+
+
+def bert_small_weights():
+    from xdna_engine_b200.synth import BertConfig, make_bert_weights
+    cfg = BertConfig(**BERT_SMALL)
+    return cfg, make_bert_weights(cfg, seed=BERT_SMALL_SEED, std=0.1, bias_std=0.05, ln_std=0.1)
+
+
+def bert_hf_fixture():
+    """HF BertModel (what the reference validates BGE against, scripts/bge_reference.py):
+    CLS row of last_hidden_state, L2-normalised, on a small seeded random BERT."""
+    import torch
+    from transformers import BertConfig as HFCfg, BertModel
+    cfg, w = bert_small_weights()
+    hc = HFCfg(vocab_size=cfg.vocab, hidden_size=cfg.d_model, num_hidden_layers=cfg.n_layers,
+               num_attention_heads=cfg.n_heads, intermediate_size=cfg.ffn, hidden_act="gelu",
+               hidden_dropout_prob=0.0, attention_probs_dropout_prob=0.0,
+               max_position_embeddings=cfg.max_pos, type_vocab_size=2, layer_norm_eps=cfg.eps)
+    model = BertModel(hc, add_pooling_layer=False).eval().float()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    sd = {"embeddings.word_embeddings.weight": t(w["word_emb"]),
+          "embeddings.position_embeddings.weight": t(w["pos_emb"]),
+          "embeddings.token_type_embeddings.weight": t(w["type_emb"]),
+          "embeddings.LayerNorm.weight": t(w["emb_ln_w"]), "embeddings.LayerNorm.bias": t(w["emb_ln_b"])}
+    m = {"q": "attention.self.query", "k": "attention.self.key", "v": "attention.self.value",
+         "o": "attention.output.dense", "ffn1": "intermediate.dense", "ffn2": "output.dense"}
+    for i, ly in enumerate(w["layers"]):
+        p = f"encoder.layer.{i}."
+        for k, n in m.items():
+            sd[p + n + ".weight"] = t(ly[k + "_w"].T)
+            sd[p + n + ".bias"] = t(ly[k + "_b"])
+        sd[p + "attention.output.LayerNorm.weight"] = t(ly["attn_ln_w"])
+        sd[p + "attention.output.LayerNorm.bias"] = t(ly["attn_ln_b"])
+        sd[p + "output.LayerNorm.weight"] = t(ly["out_ln_w"])
+        sd[p + "output.LayerNorm.bias"] = t(ly["out_ln_b"])
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    assert not unexpected and all("position_ids" in k or "token_type_ids" in k for k in missing), missing
+    rng = np.random.default_rng(21)
+    lens = np.array([1, 7, 19, 40], np.int32)
+    ids = rng.integers(3, cfg.vocab, size=int(lens.sum())).astype(np.int32)
+    embs, off = [], 0
+    with torch.no_grad():
+        for L in lens:
+            x = torch.from_numpy(ids[off:off + L].astype(np.int64))[None]
+            h = model(input_ids=x, token_type_ids=torch.zeros_like(x)).last_hidden_state[0, 0]
+            embs.append(torch.nn.functional.normalize(h, dim=0).numpy())
+            off += L
+    np.savez_compressed(os.path.join(HERE, "bert_hf_golden.npz"), ids=ids, lens=lens, emb=np.stack(embs))
+    print("bert_hf_golden.npz: ", np.stack(embs).shape)
+
+
 if __name__ == "__main__":
     bfp16_fixture()
     opt_hf_fixture()
+    bert_hf_fixture()

@@ -244,3 +244,15 @@ def test_opt_thread_count_invariant():
         outs.append(m.generate(f["prompt"], 6, True))
     np.testing.assert_array_equal(outs[0][0], outs[1][0])
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
+
+
+def test_bert_oracle_matches_hf_golden():
+    """or_bert_embed (the reference's host BERT embedder restated) vs HF BertModel, the
+    implementation the reference checks BGE against (scripts/bge_reference.py)."""
+    import sys
+    sys.path.insert(0, GOLD)
+    import make_golden as G
+    cfg, w = G.bert_small_weights()
+    f = np.load(os.path.join(GOLD, "bert_hf_golden.npz"))
+    e = O.bert_embed(cfg, w, f["ids"], f["lens"], 2)
+    np.testing.assert_allclose(e, f["emb"], atol=1e-5, rtol=0)

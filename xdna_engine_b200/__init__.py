@@ -14,7 +14,8 @@ import os
 
 import numpy as np
 
-from .synth import OPT_125M, OptConfig, make_opt_weights, make_prompt  # noqa: F401
+from .synth import (OPT_125M, OptConfig, make_opt_weights, make_prompt,  # noqa: F401
+                    BGE_BASE, BertConfig, make_bert_weights, make_bge_batch)
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libxdna_b200.so")
@@ -66,6 +67,13 @@ def lib():
         L.xdna_gemm_bf16.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp]
         L.xdna_gemm_bf16.restype = i
         L.xdna_gemm_check.restype = i
+        L.xdna_bert_create.argtypes = [vp, vp, vp, i, i]
+        L.xdna_bert_create.restype = vp
+        L.xdna_bert_free.argtypes = [vp]
+        L.xdna_bert_embed.argtypes = [vp, vp, vp, i, vp]
+        L.xdna_bert_embed.restype = i
+        L.xdna_bert_encode_device.argtypes = [vp, vp, vp, vp, i, i, i, vp, vp]
+        L.xdna_bert_encode_device.restype = i
         L.xdna_opt_create.argtypes = [vp, vp, vp, i, i]
         L.xdna_opt_create.restype = vp
         L.xdna_opt_free.argtypes = [vp]
@@ -214,6 +222,70 @@ class OptDecoder:
     def close(self):
         if getattr(self, "handle", None):
             lib().xdna_opt_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _BertCfg(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("d_model", C.c_int), ("n_heads", C.c_int), ("ffn", C.c_int),
+                ("vocab", C.c_int), ("max_pos", C.c_int), ("eps", C.c_float), ("pooling", C.c_int)]
+
+
+_BERT_LAYER = ("q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "o_w", "o_b", "attn_ln_w", "attn_ln_b",
+               "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b", "out_ln_w", "out_ln_b")
+
+
+class _BertLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _BERT_LAYER]
+
+
+class _BertWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("word_emb", "pos_emb", "type_emb", "emb_ln_w", "emb_ln_b", "layers")]
+
+
+class BertEmbedder:
+    """BGE/BERT embedder on one B200 (EmbedPipeline::embed without the tokenizer)."""
+
+    def __init__(self, device: Device, cfg, weights: dict, max_tokens: int, max_seqs: int):
+        keep = []
+
+        def p(a):
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            return _addr(a)
+
+        c = _BertCfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.ffn, cfg.vocab, cfg.max_pos, cfg.eps,
+                     cfg.pooling)
+        layers = (_BertLayer * cfg.n_layers)()
+        for li, ly in enumerate(weights["layers"]):
+            for n in _BERT_LAYER:
+                setattr(layers[li], n, p(ly[n]))
+        w = _BertWeights(p(weights["word_emb"]), p(weights["pos_emb"]), p(weights["type_emb"]),
+                         p(weights["emb_ln_w"]), p(weights["emb_ln_b"]), C.addressof(layers))
+        h = lib().xdna_bert_create(device.handle, C.byref(c), C.byref(w), max_tokens, max_seqs)
+        if not h:
+            raise XdnaError(last_error())
+        self.handle, self.cfg = h, cfg
+
+    def embed(self, ids, seq_lens):
+        ids = np.ascontiguousarray(ids, np.int32)
+        lens = np.ascontiguousarray(seq_lens, np.int32)
+        out = np.empty((lens.size, self.cfg.d_model), np.float32)
+        _check(lib().xdna_bert_embed(self.handle, _addr(ids), _addr(lens), lens.size, _addr(out)))
+        return out
+
+    def encode_device(self, ids_ptr, tokpos_ptr, cu_ptr, n_tokens, n_seqs, max_len, out_ptr, stream=0):
+        _check(lib().xdna_bert_encode_device(self.handle, ids_ptr, tokpos_ptr, cu_ptr, n_tokens, n_seqs,
+                                             max_len, out_ptr, stream or None))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().xdna_bert_free(self.handle)
             self.handle = None
 
     def __del__(self):

@@ -1,0 +1,544 @@
+// bert.cu -- the BGE-base (BERT) encoder path on B200 for batches of variable-length
+// sequences, packed without padding ([T = sum of lengths, 768] bf16 activations).
+//
+// Replaces the reference's EmbedPipeline (rust/npu-engine/src/bert/mod.rs:24-46):
+//   EmbedFrontend::run   word + position + type-0 embedding, LayerNorm eps 1e-12
+//                        (bert/frontend.rs:37-61)                  -> embed_ln_kernel
+//   BertBlock::forward   q/k/v/o, ffn1 (+GELU), ffn2 on the NPU GEMM engine, host MHA with
+//                        the key mask j >= valid_len, post-LN (bert/encoder.rs:43-57)
+//                        -> xdna_gemm_bf16 (tcgen05, fused bias/GELU/residual),
+//                           attention_kernel, ln_kernel
+//   EmbedHead::run       CLS or mean pooling over valid rows, L2 with norm clamp 1e-12
+//                        (bert/head.rs:20-47)                     -> pool_kernel
+// Packing sequences (instead of padding each to 512 and masking keys) gives the same result
+// for every valid row: a padded row can never be attended to, and only valid rows are pooled.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/xdna_b200.h"
+#include "ptx.cuh"
+
+namespace xdna {
+void set_last_error_message(const std::string &m);
+cudaError_t gemm_bf16(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M, int N, int K,
+                      const float *bias, const uint16_t *residual, int ldr, int gelu, uint16_t *C, int ldc,
+                      cudaStream_t st);
+unsigned gemm_error_and_clear();
+
+namespace bert {
+
+constexpr int D = 768, H = 12, HD = 64, F = 3072;
+
+__device__ __forceinline__ void unpack8(uint4 w, float *v) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 4; e++) { v[2 * e] = bf16lo(u[e]); v[2 * e + 1] = bf16hi(u[e]); }
+}
+__device__ __forceinline__ uint4 pack8(const float *v) {
+    uint4 w;
+    w.x = bf16bits(v[0]) | (bf16bits(v[1]) << 16);
+    w.y = bf16bits(v[2]) | (bf16bits(v[3]) << 16);
+    w.z = bf16bits(v[4]) | (bf16bits(v[5]) << 16);
+    w.w = bf16bits(v[6]) | (bf16bits(v[7]) << 16);
+    return w;
+}
+
+// LayerNorm of one 768-wide row held as 24 floats per lane (elements 8*lane + 256*j + e):
+// population variance, y = (x - mean) * inv * g + b  (rust/npu-asr-host/src/lib.rs:79-110)
+__device__ __forceinline__ void ln_row(float (&v)[24], const float *g, const float *b, float eps, int lane) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 24; i++) s += v[i];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / (float)D;
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 24; i++) { const float c = v[i] - mean; q += c * c; }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float inv = 1.0f / sqrtf(q / (float)D + eps);
+#pragma unroll
+    for (int j = 0; j < 3; j++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int c = 8 * lane + 256 * j + e;
+            v[8 * j + e] = (v[8 * j + e] - mean) * inv * g[c] + b[c];
+        }
+}
+
+// x[t] = LN(word[id] + pos[t - seq_start] + type[0]); one warp per token row
+__global__ void embed_ln_kernel(const int32_t *ids, const int32_t *tok_pos, int T, const uint16_t *word,
+                                const uint16_t *pos, const uint16_t *type0, const float *g, const float *b,
+                                float eps, uint16_t *x) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= T) return;
+    const int id = ids[row], p = tok_pos[row];
+    float v[24];
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        const int c = 8 * lane + 256 * j;
+        float a[8], bb[8], cc[8];
+        unpack8(*reinterpret_cast<const uint4 *>(word + (size_t)id * D + c), a);
+        unpack8(*reinterpret_cast<const uint4 *>(pos + (size_t)p * D + c), bb);
+        unpack8(*reinterpret_cast<const uint4 *>(type0 + c), cc);
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[8 * j + e] = a[e] + bb[e] + cc[e];
+    }
+    ln_row(v, g, b, eps, lane);
+#pragma unroll
+    for (int j = 0; j < 3; j++)
+        *reinterpret_cast<uint4 *>(x + (size_t)row * D + 8 * lane + 256 * j) = pack8(v + 8 * j);
+}
+
+// y = LN(x) row-wise, bf16 in / bf16 out; one warp per row
+__global__ void ln_kernel(const uint16_t *xin, int T, const float *g, const float *b, float eps, uint16_t *y) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= T) return;
+    float v[24];
+#pragma unroll
+    for (int j = 0; j < 3; j++)
+        unpack8(*reinterpret_cast<const uint4 *>(xin + (size_t)row * D + 8 * lane + 256 * j), v + 8 * j);
+    ln_row(v, g, b, eps, lane);
+#pragma unroll
+    for (int j = 0; j < 3; j++)
+        *reinterpret_cast<uint4 *>(y + (size_t)row * D + 8 * lane + 256 * j) = pack8(v + 8 * j);
+}
+
+// ---------------------------------------------------------------------------- attention
+// softmax(q k^T / 8) v per (sequence, head, 64-query tile) over the sequence's own keys
+// (the valid_len key mask of npu-asr-host mha, lib.rs:189-326).  Tensor cores via
+// mma.sync m16n8k16 bf16 (f32 accumulate), flash-style online softmax over 64-key tiles.
+// Shared tiles [64 rows][64 bf16] with 16-byte chunks XOR-swizzled by (row & 7).
+__device__ __forceinline__ uint32_t swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) { return bf16bits(lo) | (bf16bits(hi) << 16); }
+
+// load a 64 x 64 bf16 tile (row stride ld elements) with cp.async into a swizzled tile;
+// rows >= nrows are zero-filled
+__device__ __forceinline__ void load_tile(uint8_t *tile, const uint16_t *src, int ld, int nrows, int tid) {
+    for (int c = tid; c < 64 * 8; c += 128) {
+        const int r = c >> 3, ch = c & 7;
+        uint8_t *dst = tile + swz(r, ch);
+        if (r < nrows) cp_async16(dst, src + (size_t)r * ld + ch * 8);
+        else *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+    }
+}
+
+__global__ void __launch_bounds__(128) attention_kernel(const uint16_t *qkv, const int32_t *cu, uint16_t *ctx) {
+    __shared__ __align__(128) uint8_t sQ[64 * 128];
+    __shared__ __align__(128) uint8_t sK[2][64 * 128];
+    __shared__ __align__(128) uint8_t sV[2][64 * 128];
+    const int qt = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
+    const int s0 = cu[sq], L = cu[sq + 1] - s0;
+    const int q0 = qt * 64;
+    if (q0 >= L) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int LD = 3 * D;
+    const uint16_t *Qg = qkv + (size_t)(s0 + q0) * LD + h * HD;
+    const uint16_t *Kg = qkv + (size_t)s0 * LD + D + h * HD;
+    const uint16_t *Vg = qkv + (size_t)s0 * LD + 2 * D + h * HD;
+    const int nq = min(64, L - q0);
+    const int nkt = (L + 63) / 64;
+    load_tile(sQ, Qg, LD, nq, tid);
+    load_tile(sK[0], Kg, LD, min(64, L), tid);
+    load_tile(sV[0], Vg, LD, min(64, L), tid);
+    cp_async_commit();
+
+    const uint32_t q_base = smem_u32(sQ);
+    float o[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
+    const float scale_log2 = 0.125f * 1.4426950408889634f;
+    uint32_t qa[4][4];
+
+    for (int kt = 0; kt < nkt; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < nkt) {
+            const int r0 = (kt + 1) * 64;
+            load_tile(sK[buf ^ 1], Kg + (size_t)r0 * LD, LD, min(64, L - r0), tid);
+            load_tile(sV[buf ^ 1], Vg + (size_t)r0 * LD, LD, min(64, L - r0), tid);
+        }
+        cp_async_commit();
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();
+        if (kt == 0) {
+            // Q fragments for this warp's 16 rows, 4 k-chunks of 16 dims
+#pragma unroll
+            for (int kc = 0; kc < 4; kc++) {
+                const int r = warp * 16 + (lane & 15), ch = kc * 2 + (lane >> 4);
+                ldsm_x4(q_base + swz(r, ch), qa[kc][0], qa[kc][1], qa[kc][2], qa[kc][3]);
+            }
+        }
+        const uint32_t k_base = smem_u32(sK[buf]), v_base = smem_u32(sV[buf]);
+        float sc[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
+#pragma unroll
+        for (int kc = 0; kc < 4; kc++) {
+#pragma unroll
+            for (int np = 0; np < 4; np++) {   // two 8-key n-tiles per ldmatrix.x4
+                const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+                const int ch = kc * 2 + ((lane >> 3) & 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(k_base + swz(key, ch), b0, b1, b2, b3);
+                mma_bf16_16816(sc[2 * np], qa[kc][0], qa[kc][1], qa[kc][2], qa[kc][3], b0, b1);
+                mma_bf16_16816(sc[2 * np + 1], qa[kc][0], qa[kc][1], qa[kc][2], qa[kc][3], b2, b3);
+            }
+        }
+        // mask keys beyond the sequence, online softmax (rows g and g + 8 of the warp)
+        const int kbase = kt * 64;
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int n = 0; n < 8; n++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int key = kbase + n * 8 + 2 * (lane & 3) + (e & 1);
+                if (key >= L) sc[n][e] = -INFINITY;
+                mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
+            }
+        float corr[2], mnew[2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+            mnew[r] = fmaxf(m_r[r], mx[r]);
+            corr[r] = exp2f((m_r[r] - mnew[r]) * scale_log2);
+            m_r[r] = mnew[r];
+        }
+        float ls[2] = {0.0f, 0.0f};
+        uint32_t pa[4][4];   // P as A fragments: 4 k-chunks (16 keys each)
+#pragma unroll
+        for (int n = 0; n < 8; n++) {
+            float p[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                p[e] = exp2f((sc[n][e] - mnew[e >> 1]) * scale_log2);
+                ls[e >> 1] += p[e];
+            }
+            const int kc = n >> 1, hi = n & 1;
+            pa[kc][hi * 2 + 0] = pack_bf16x2(p[0], p[1]);
+            pa[kc][hi * 2 + 1] = pack_bf16x2(p[2], p[3]);
+        }
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
+            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
+            l_r[r] = l_r[r] * corr[r] + ls[r];
+        }
+#pragma unroll
+        for (int n = 0; n < 8; n++) {
+            o[n][0] *= corr[0]; o[n][1] *= corr[0];
+            o[n][2] *= corr[1]; o[n][3] *= corr[1];
+        }
+        // O += P V: k = keys (4 chunks of 16), n = dims (8 tiles of 8); V^T fragments by ldmatrix.trans
+#pragma unroll
+        for (int kc = 0; kc < 4; kc++) {
+            // A fragment order for m16n8k16: a0 (rows g, k 0-7), a1 (rows g+8, k 0-7),
+            // a2 (rows g, k 8-15), a3 (rows g+8, k 8-15)
+            const uint32_t a0 = pa[kc][0], a1 = pa[kc][1], a2 = pa[kc][2], a3 = pa[kc][3];
+#pragma unroll
+            for (int np = 0; np < 4; np++) {
+                const int key = kc * 16 + (lane & 15);
+                const int ch = np * 2 + (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(v_base + swz(key, ch), b0, b1, b2, b3);
+                mma_bf16_16816(o[2 * np], a0, a1, a2, a3, b0, b1);
+                mma_bf16_16816(o[2 * np + 1], a0, a1, a2, a3, b2, b3);
+            }
+        }
+        __syncthreads();
+    }
+    // write ctx rows (bf16)
+    const int g = lane >> 2, c2 = 2 * (lane & 3);
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int qi = warp * 16 + g + 8 * r;
+        if (qi < nq) {
+            const float inv = 1.0f / l_r[r];
+            uint16_t *dst = ctx + (size_t)(s0 + q0 + qi) * D + h * HD;
+#pragma unroll
+            for (int n = 0; n < 8; n++)
+                *reinterpret_cast<uint32_t *>(dst + n * 8 + c2) = pack_bf16x2(o[n][2 * r] * inv, o[n][2 * r + 1] * inv);
+        }
+    }
+}
+
+// out[b] = l2norm(pool(x rows of sequence b)); pooling 0 = CLS (row 0), 1 = mean
+__global__ void pool_kernel(const uint16_t *x, const int32_t *cu, int pooling, float *out) {
+    const int b = blockIdx.x, lane = threadIdx.x;
+    const int s0 = cu[b], L = cu[b + 1] - s0;
+    float v[24];
+#pragma unroll
+    for (int i = 0; i < 24; i++) v[i] = 0.0f;
+    const int nrows = pooling == 0 ? 1 : max(L, 1);
+    for (int t = 0; t < nrows && t < max(L, 1); t++) {
+#pragma unroll
+        for (int j = 0; j < 3; j++) {
+            float a[8];
+            unpack8(*reinterpret_cast<const uint4 *>(x + (size_t)(s0 + t) * D + 8 * lane + 256 * j), a);
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[8 * j + e] += a[e];
+        }
+    }
+    if (pooling == 1) {
+        const float inv = 1.0f / (float)max(L, 1);
+#pragma unroll
+        for (int i = 0; i < 24; i++) v[i] *= inv;
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 24; i++) s += v[i] * v[i];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float norm = fmaxf(sqrtf(s), 1e-12f);
+#pragma unroll
+    for (int j = 0; j < 3; j++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) out[(size_t)b * D + 8 * lane + 256 * j + e] = v[8 * j + e] / norm;
+}
+
+}  // namespace bert
+}  // namespace xdna
+
+// ====================================================================================== host
+namespace xdna {
+namespace {
+
+uint16_t to_bf16_bits(float f) {   // round to nearest even (rust/npu-xrt/src/lib.rs:809-818)
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+    return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+
+// [K, N] f32 (the reference's layout) -> [N, K] bf16 rows appended to out
+void append_transposed_bf16(const float *w, int K, int N, std::vector<uint16_t> &out) {
+    const size_t base = out.size();
+    out.resize(base + (size_t)N * K);
+    for (int k = 0; k < K; k++)
+        for (int n = 0; n < N; n++) out[base + (size_t)n * K + k] = to_bf16_bits(w[(size_t)k * N + n]);
+}
+
+struct CudaFail : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+void ck(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) throw CudaFail(std::string(what) + ": " + cudaGetErrorString(e));
+}
+template <class T>
+T *dalloc(size_t n) {
+    void *p = nullptr;
+    ck(cudaMalloc(&p, std::max<size_t>(n * sizeof(T), 16)), "cudaMalloc");
+    return static_cast<T *>(p);
+}
+template <class T>
+T *dupload(const std::vector<T> &v) {
+    T *p = dalloc<T>(v.size());
+    ck(cudaMemcpy(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice), "upload");
+    return p;
+}
+
+}  // namespace
+}  // namespace xdna
+
+using namespace xdna;
+
+struct XdnaBert {
+    XdnaBertConfig cfg{};
+    int ordinal = 0, max_tokens = 0, max_seqs = 0;
+    uint16_t *word = nullptr, *pos = nullptr, *type0 = nullptr;
+    float *emb_ln = nullptr;                       // [2][D]
+    struct Layer {
+        uint16_t *wqkv, *wo, *w1, *w2;             // [N, K] bf16
+        float *bqkv, *bo, *b1, *b2, *ln1, *ln2;    // ln: [2][D]
+    };
+    std::vector<Layer> layers;
+    // activations (bf16) and packing metadata
+    uint16_t *x = nullptr, *qkv = nullptr, *ctx = nullptr, *y = nullptr, *hbuf = nullptr;
+    int32_t *ids = nullptr, *tokpos = nullptr, *cu = nullptr;
+    float *out = nullptr;
+    std::vector<void *> owned;
+    ~XdnaBert() {
+        for (void *p : owned) cudaFree(p);
+    }
+};
+
+extern "C" {
+
+XdnaBert *xdna_bert_create(XdnaDevice *dev_unused, const XdnaBertConfig *cfg, const XdnaBertWeights *w,
+                           int max_tokens, int max_seqs) {
+    (void)dev_unused;
+    if (!cfg || !w || !w->layers || !w->word_emb || !w->pos_emb || !w->type_emb || !w->emb_ln_w || !w->emb_ln_b) {
+        set_last_error_message("xdna_bert_create: null pointer");
+        return nullptr;
+    }
+    const XdnaBertConfig c = *cfg;
+    if (c.d_model != bert::D || c.n_heads != bert::H || c.ffn != bert::F || c.n_layers < 1 || c.vocab < 1 ||
+        c.max_pos < 1 || max_tokens < 1 || max_seqs < 1 || (c.pooling != 0 && c.pooling != 1)) {
+        set_last_error_message("xdna_bert_create: supported shape is d_model 768, 12 heads, ffn 3072 "
+                               "(BERT-base / BGE-base); pooling 0 (CLS) or 1 (mean)");
+        return nullptr;
+    }
+    auto *m = new XdnaBert();
+    try {
+        int dev = 0;
+        ck(cudaGetDevice(&dev), "cudaGetDevice");
+        m->ordinal = dev;
+        m->cfg = c;
+        m->max_tokens = max_tokens;
+        m->max_seqs = max_seqs;
+        const int D = bert::D, F = bert::F;
+        auto keep = [&](void *p) { m->owned.push_back(p); return p; };
+        auto bf = [&](const float *src, size_t n) {
+            std::vector<uint16_t> v(n);
+            for (size_t i = 0; i < n; i++) v[i] = to_bf16_bits(src[i]);
+            return static_cast<uint16_t *>(keep(dupload(v)));
+        };
+        auto f32 = [&](std::initializer_list<std::pair<const float *, size_t>> parts) {
+            std::vector<float> v;
+            for (auto &pr : parts) v.insert(v.end(), pr.first, pr.first + pr.second);
+            return static_cast<float *>(keep(dupload(v)));
+        };
+        m->word = bf(w->word_emb, (size_t)c.vocab * D);
+        m->pos = bf(w->pos_emb, (size_t)c.max_pos * D);
+        m->type0 = bf(w->type_emb, D);
+        m->emb_ln = f32({{w->emb_ln_w, (size_t)D}, {w->emb_ln_b, (size_t)D}});
+        for (int l = 0; l < c.n_layers; l++) {
+            const XdnaBertLayer &L = w->layers[l];
+            XdnaBert::Layer o{};
+            std::vector<uint16_t> t;
+            append_transposed_bf16(L.q_w, D, D, t);
+            append_transposed_bf16(L.k_w, D, D, t);
+            append_transposed_bf16(L.v_w, D, D, t);
+            o.wqkv = static_cast<uint16_t *>(keep(dupload(t)));
+            t.clear(); append_transposed_bf16(L.o_w, D, D, t); o.wo = static_cast<uint16_t *>(keep(dupload(t)));
+            t.clear(); append_transposed_bf16(L.ffn1_w, D, F, t); o.w1 = static_cast<uint16_t *>(keep(dupload(t)));
+            t.clear(); append_transposed_bf16(L.ffn2_w, F, D, t); o.w2 = static_cast<uint16_t *>(keep(dupload(t)));
+            o.bqkv = f32({{L.q_b, (size_t)D}, {L.k_b, (size_t)D}, {L.v_b, (size_t)D}});
+            o.bo = f32({{L.o_b, (size_t)D}});
+            o.b1 = f32({{L.ffn1_b, (size_t)F}});
+            o.b2 = f32({{L.ffn2_b, (size_t)D}});
+            o.ln1 = f32({{L.attn_ln_w, (size_t)D}, {L.attn_ln_b, (size_t)D}});
+            o.ln2 = f32({{L.out_ln_w, (size_t)D}, {L.out_ln_b, (size_t)D}});
+            m->layers.push_back(o);
+        }
+        const size_t T = (size_t)max_tokens;
+        m->x = static_cast<uint16_t *>(keep(dalloc<uint16_t>(T * D)));
+        m->qkv = static_cast<uint16_t *>(keep(dalloc<uint16_t>(T * 3 * D)));
+        m->ctx = static_cast<uint16_t *>(keep(dalloc<uint16_t>(T * D)));
+        m->y = static_cast<uint16_t *>(keep(dalloc<uint16_t>(T * D)));
+        m->hbuf = static_cast<uint16_t *>(keep(dalloc<uint16_t>(T * F)));
+        m->ids = static_cast<int32_t *>(keep(dalloc<int32_t>(T)));
+        m->tokpos = static_cast<int32_t *>(keep(dalloc<int32_t>(T)));
+        m->cu = static_cast<int32_t *>(keep(dalloc<int32_t>(max_seqs + 1)));
+        m->out = static_cast<float *>(keep(dalloc<float>((size_t)max_seqs * D)));
+        ck(cudaDeviceSynchronize(), "create sync");
+        return m;
+    } catch (const std::exception &e) {
+        set_last_error_message(std::string("xdna_bert_create: ") + e.what());
+        delete m;
+        return nullptr;
+    }
+}
+
+void xdna_bert_free(XdnaBert *m) {
+    if (!m) return;
+    cudaDeviceSynchronize();
+    delete m;
+}
+
+// The encoder over device-resident packed inputs: ids/tok_pos [n_tokens], cu [n_seqs + 1]
+// (sequence starts, cu[n_seqs] = n_tokens), max_len = longest sequence; writes the pooled,
+// L2-normalised embeddings [n_seqs, 768] f32 to out_dev.  Asynchronous on `stream`.
+int xdna_bert_encode_device(XdnaBert *m, const int32_t *ids, const int32_t *tok_pos, const int32_t *cu,
+                            int n_tokens, int n_seqs, int max_len, float *out_dev, void *stream) {
+    if (!m || !ids || !tok_pos || !cu || !out_dev) { set_last_error_message("xdna_bert_encode_device: null pointer"); return -1; }
+    if (n_tokens < 1 || n_tokens > m->max_tokens || n_seqs < 1 || max_len < 1 || max_len > m->cfg.max_pos) {
+        set_last_error_message("xdna_bert_encode_device: sizes beyond the model's max_tokens / max_pos");
+        return -1;
+    }
+    using namespace bert;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int T = n_tokens;
+    const float eps = m->cfg.eps;
+    cudaError_t e;
+    embed_ln_kernel<<<(T + 7) / 8, 256, 0, st>>>(ids, tok_pos, T, m->word, m->pos, m->type0, m->emb_ln,
+                                                 m->emb_ln + D, eps, m->x);
+    for (const auto &L : m->layers) {
+        if ((e = gemm_bf16(m->x, D, L.wqkv, D, T, 3 * D, D, L.bqkv, nullptr, 0, 0, m->qkv, 3 * D, st))) break;
+        attention_kernel<<<dim3((max_len + 63) / 64, H, n_seqs), 128, 0, st>>>(m->qkv, cu, m->ctx);
+        if ((e = gemm_bf16(m->ctx, D, L.wo, D, T, D, D, L.bo, m->x, D, 0, m->y, D, st))) break;
+        ln_kernel<<<(T + 7) / 8, 256, 0, st>>>(m->y, T, L.ln1, L.ln1 + D, eps, m->x);
+        if ((e = gemm_bf16(m->x, D, L.w1, D, T, F, D, L.b1, nullptr, 0, 1, m->hbuf, F, st))) break;
+        if ((e = gemm_bf16(m->hbuf, F, L.w2, F, T, D, F, L.b2, m->x, D, 0, m->y, D, st))) break;
+        ln_kernel<<<(T + 7) / 8, 256, 0, st>>>(m->y, T, L.ln2, L.ln2 + D, eps, m->x);
+    }
+    pool_kernel<<<n_seqs, 32, 0, st>>>(m->x, cu, m->cfg.pooling, out_dev);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_last_error_message(std::string("xdna_bert_encode_device: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+int xdna_bert_embed(XdnaBert *m, const int32_t *ids, const int32_t *seq_lens, int n_seqs, float *out) {
+    if (!m || !ids || !seq_lens || !out) { set_last_error_message("xdna_bert_embed: null pointer"); return -1; }
+    if (n_seqs < 1 || n_seqs > m->max_seqs) { set_last_error_message("xdna_bert_embed: n_seqs beyond max_seqs"); return -1; }
+    std::vector<int32_t> cu(n_seqs + 1, 0), tokpos;
+    int max_len = 0;
+    for (int s = 0; s < n_seqs; s++) {
+        if (seq_lens[s] < 1 || seq_lens[s] > m->cfg.max_pos) {
+            set_last_error_message("xdna_bert_embed: sequence length outside [1, max_pos]");
+            return -1;
+        }
+        cu[s + 1] = cu[s] + seq_lens[s];
+        max_len = std::max(max_len, seq_lens[s]);
+        for (int t = 0; t < seq_lens[s]; t++) tokpos.push_back(t);
+    }
+    const int T = cu[n_seqs];
+    if (T > m->max_tokens) { set_last_error_message("xdna_bert_embed: total tokens beyond max_tokens"); return -1; }
+    for (int i = 0; i < T; i++)
+        if (ids[i] < 0 || ids[i] >= m->cfg.vocab) { set_last_error_message("xdna_bert_embed: token id out of range"); return -1; }
+    try {
+        ck(cudaMemcpy(m->ids, ids, T * 4, cudaMemcpyHostToDevice), "copy ids");
+        ck(cudaMemcpy(m->tokpos, tokpos.data(), T * 4, cudaMemcpyHostToDevice), "copy positions");
+        ck(cudaMemcpy(m->cu, cu.data(), (n_seqs + 1) * 4, cudaMemcpyHostToDevice), "copy offsets");
+        if (xdna_bert_encode_device(m, m->ids, m->tokpos, m->cu, T, n_seqs, max_len, m->out, nullptr) != 0) return -1;
+        ck(cudaMemcpy(out, m->out, (size_t)n_seqs * bert::D * 4, cudaMemcpyDeviceToHost), "copy embeddings");
+        if (gemm_error_and_clear()) {
+            set_last_error_message("xdna_bert_embed: a tensor-core GEMM wait expired");
+            return -1;
+        }
+        return 0;
+    } catch (const std::exception &ex) {
+        set_last_error_message(std::string("xdna_bert_embed: ") + ex.what());
+        return -1;
+    }
+}
+
+}  // extern "C"

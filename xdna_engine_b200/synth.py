@@ -78,3 +78,74 @@ def make_prompt(cfg: OptConfig = OPT_125M, n: int = 32, seed: int = 0) -> np.nda
     """Prompt ids uniform in [2, vocab) (the opt-125m config's synthetic prompt)."""
     rng = np.random.default_rng(seed + 1_000_003)
     return rng.integers(2, cfg.vocab, size=n, dtype=np.int64)
+
+
+# ------------------------------------------------------------------------- BGE-base / BERT
+@dataclass(frozen=True)
+class BertConfig:
+    n_layers: int = 12
+    d_model: int = 768
+    n_heads: int = 12
+    ffn: int = 3072
+    vocab: int = 30522
+    max_pos: int = 512
+    eps: float = 1e-12
+    pooling: int = 0          # 0 = CLS (BGE), 1 = mean
+
+
+BGE_BASE = BertConfig()
+BERT_LAYER_KEYS = ("q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "o_w", "o_b", "attn_ln_w", "attn_ln_b",
+                   "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b", "out_ln_w", "out_ln_b")
+
+
+def _bf16(a):
+    """Round float32 to bf16-representable float32 (nearest even), so the f32 oracle and the
+    engine's bf16 weights hold the same values."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    u = (u + np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    return u.view(np.float32)
+
+
+def make_bert_weights(cfg: BertConfig = BGE_BASE, seed: int = 0, std: float = 0.02,
+                      bias_std: float = 0.0, ln_std: float = 0.0) -> dict:
+    """Random-init BERT weights, bf16-valued float32: matrices N(0, std), biases N(0,
+    bias_std), LayerNorm gamma 1 + N(0, ln_std), beta N(0, ln_std).  Linear weights are
+    [K, N] = [in, out]."""
+    rng = np.random.default_rng(seed)
+    D, F = cfg.d_model, cfg.ffn
+
+    def normal(shape, s):
+        a = rng.standard_normal(shape, dtype=np.float32)
+        a *= np.float32(s)
+        return _bf16(a)
+
+    def vec(n, base, s):
+        if s == 0.0:
+            return np.full(n, base, np.float32)
+        return (np.float32(base) + rng.standard_normal(n, dtype=np.float32) * np.float32(s)).astype(np.float32)
+
+    w = {"word_emb": normal((cfg.vocab, D), std), "pos_emb": normal((cfg.max_pos, D), std),
+         "type_emb": normal((2, D), std), "emb_ln_w": vec(D, 1.0, ln_std), "emb_ln_b": vec(D, 0.0, ln_std)}
+    layers = []
+    for _ in range(cfg.n_layers):
+        layers.append({
+            "q_w": normal((D, D), std), "q_b": vec(D, 0.0, bias_std),
+            "k_w": normal((D, D), std), "k_b": vec(D, 0.0, bias_std),
+            "v_w": normal((D, D), std), "v_b": vec(D, 0.0, bias_std),
+            "o_w": normal((D, D), std), "o_b": vec(D, 0.0, bias_std),
+            "attn_ln_w": vec(D, 1.0, ln_std), "attn_ln_b": vec(D, 0.0, ln_std),
+            "ffn1_w": normal((D, F), std), "ffn1_b": vec(F, 0.0, bias_std),
+            "ffn2_w": normal((F, D), std), "ffn2_b": vec(D, 0.0, bias_std),
+            "out_ln_w": vec(D, 1.0, ln_std), "out_ln_b": vec(D, 0.0, ln_std),
+        })
+    w["layers"] = layers
+    return w
+
+
+def make_bge_batch(n_seqs: int = 256, seed: int = 0, lo: int = 32, hi: int = 512):
+    """The BGE config's synthetic batch: lengths uniform in [lo, hi], ids uniform in
+    [1000, 30000).  Returns (ids concatenated int32, seq_lens int32)."""
+    rng = np.random.default_rng(seed + 7_000_003)
+    lens = rng.integers(lo, hi + 1, size=n_seqs).astype(np.int32)
+    ids = rng.integers(1000, 30000, size=int(lens.sum())).astype(np.int32)
+    return ids, lens
