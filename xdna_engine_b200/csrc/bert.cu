@@ -113,7 +113,7 @@ __global__ void ln_kernel(const uint16_t *xin, int T, const float *g, const floa
 }
 
 // ---------------------------------------------------------------------------- attention
-// softmax(q k^T / 8) v per (sequence, head, 64-query tile) over the sequence's own keys
+// softmax(q k^T / 8) v per (sequence, head, 128-query tile) over the sequence's own keys
 // (the valid_len key mask of npu-asr-host mha, lib.rs:189-326).  Tensor cores via
 // mma.sync m16n8k16 bf16 (f32 accumulate), flash-style online softmax over 64-key tiles.
 // Shared tiles [64 rows][64 bf16] with 16-byte chunks XOR-swizzled by (row & 7).
@@ -138,8 +138,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) { return bf1
 
 // load a 64 x 64 bf16 tile (row stride ld elements) with cp.async into a swizzled tile;
 // rows >= nrows are zero-filled
+template <int ROWS, int NT>
 __device__ __forceinline__ void load_tile(uint8_t *tile, const uint16_t *src, int ld, int nrows, int tid) {
-    for (int c = tid; c < 64 * 8; c += 128) {
+    for (int c = tid; c < ROWS * 8; c += NT) {
         const int r = c >> 3, ch = c & 7;
         uint8_t *dst = tile + swz(r, ch);
         if (r < nrows) cp_async16(dst, src + (size_t)r * ld + ch * 8);
@@ -147,24 +148,26 @@ __device__ __forceinline__ void load_tile(uint8_t *tile, const uint16_t *src, in
     }
 }
 
-__global__ void __launch_bounds__(128) attention_kernel(const uint16_t *qkv, const int32_t *cu, uint16_t *ctx) {
-    __shared__ __align__(128) uint8_t sQ[64 * 128];
+constexpr int AQ = 128;             // queries per CTA (8 warps x 16 rows)
+constexpr int ATHREADS = 256;
+__global__ void __launch_bounds__(ATHREADS) attention_kernel(const uint16_t *qkv, const int32_t *cu, uint16_t *ctx) {
+    __shared__ __align__(128) uint8_t sQ[AQ * 128];
     __shared__ __align__(128) uint8_t sK[2][64 * 128];
     __shared__ __align__(128) uint8_t sV[2][64 * 128];
     const int qt = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
     const int s0 = cu[sq], L = cu[sq + 1] - s0;
-    const int q0 = qt * 64;
+    const int q0 = qt * AQ;
     if (q0 >= L) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr int LD = 3 * D;
     const uint16_t *Qg = qkv + (size_t)(s0 + q0) * LD + h * HD;
     const uint16_t *Kg = qkv + (size_t)s0 * LD + D + h * HD;
     const uint16_t *Vg = qkv + (size_t)s0 * LD + 2 * D + h * HD;
-    const int nq = min(64, L - q0);
+    const int nq = min(AQ, L - q0);
     const int nkt = (L + 63) / 64;
-    load_tile(sQ, Qg, LD, nq, tid);
-    load_tile(sK[0], Kg, LD, min(64, L), tid);
-    load_tile(sV[0], Vg, LD, min(64, L), tid);
+    load_tile<AQ, ATHREADS>(sQ, Qg, LD, nq, tid);
+    load_tile<64, ATHREADS>(sK[0], Kg, LD, min(64, L), tid);
+    load_tile<64, ATHREADS>(sV[0], Vg, LD, min(64, L), tid);
     cp_async_commit();
 
     const uint32_t q_base = smem_u32(sQ);
@@ -179,8 +182,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const uint16_t *qkv, con
         const int buf = kt & 1;
         if (kt + 1 < nkt) {
             const int r0 = (kt + 1) * 64;
-            load_tile(sK[buf ^ 1], Kg + (size_t)r0 * LD, LD, min(64, L - r0), tid);
-            load_tile(sV[buf ^ 1], Vg + (size_t)r0 * LD, LD, min(64, L - r0), tid);
+            load_tile<64, ATHREADS>(sK[buf ^ 1], Kg + (size_t)r0 * LD, LD, min(64, L - r0), tid);
+            load_tile<64, ATHREADS>(sV[buf ^ 1], Vg + (size_t)r0 * LD, LD, min(64, L - r0), tid);
         }
         cp_async_commit();
         asm volatile("cp.async.wait_group 1;" ::: "memory");
@@ -490,7 +493,7 @@ int xdna_bert_encode_device(XdnaBert *m, const int32_t *ids, const int32_t *tok_
                                                  m->emb_ln + D, eps, m->x);
     for (const auto &L : m->layers) {
         if ((e = gemm_bf16(m->x, D, L.wqkv, D, T, 3 * D, D, L.bqkv, nullptr, 0, 0, m->qkv, 3 * D, st))) break;
-        attention_kernel<<<dim3((max_len + 63) / 64, H, n_seqs), 128, 0, st>>>(m->qkv, cu, m->ctx);
+        attention_kernel<<<dim3((max_len + AQ - 1) / AQ, H, n_seqs), ATHREADS, 0, st>>>(m->qkv, cu, m->ctx);
         if ((e = gemm_bf16(m->ctx, D, L.wo, D, T, D, D, L.bo, m->x, D, 0, m->y, D, st))) break;
         ln_kernel<<<(T + 7) / 8, 256, 0, st>>>(m->y, T, L.ln1, L.ln1 + D, eps, m->x);
         if ((e = gemm_bf16(m->x, D, L.w1, D, T, F, D, L.b1, nullptr, 0, 1, m->hbuf, F, st))) break;
