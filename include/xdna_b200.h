@@ -118,6 +118,50 @@ int xdna_bert_embed(XdnaBert *m, const int32_t *ids, const int32_t *seq_lens, in
 int xdna_bert_encode_device(XdnaBert *m, const int32_t *ids, const int32_t *tok_pos, const int32_t *cu,
                             int n_tokens, int n_seqs, int max_len, float *out_dev, void *stream);
 
+/* ------------------------------------------------------------- bfp16 block format */
+/* to_bfp16_blocks of the reference's golden (route_b_kernels/ffn_bfp16/golden_ffn_gemm.py:
+ * 34-49) over contiguous blocks of 8: shared exponent floor(log2(max|x|)), quantum 2^(e-6),
+ * round half to even, no clamp.  n % 8 == 0.  Returns 0 or -1. */
+int xdna_bfp16_quantize(const float *x, size_t n, float *y);
+
+/* -------------------------------------------- Whisper-small encoder (WhisperEncoder) */
+typedef struct {
+    int n_layers, d_model, n_heads, ffn;
+    int n_mels, n_frames;      /* input mel [n_mels, n_frames]; output n_frames / 2 rows */
+    int max_src;               /* rows of embed_positions */
+    float eps;                 /* LayerNorm eps (Whisper: 1e-5) */
+} XdnaWhisperEncConfig;
+
+typedef struct {               /* f32; linear weights [K, N] = [in, out]; k_b may be NULL */
+    const float *ln1_w, *ln1_b;
+    const float *q_w, *q_b, *k_w, *k_b, *v_w, *v_b, *out_w, *out_b;
+    const float *ln2_w, *ln2_b;
+    const float *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+} XdnaWhisperEncLayer;
+
+typedef struct {
+    const float *conv1_w, *conv1_b;   /* [d_model, n_mels, 3], [d_model] */
+    const float *conv2_w, *conv2_b;   /* [d_model, d_model, 3] */
+    const float *embed_positions;     /* [max_src, d_model] */
+    const float *ln_post_w, *ln_post_b;
+    const XdnaWhisperEncLayer *layers;
+} XdnaWhisperEncWeights;
+
+typedef struct XdnaWhisperEnc XdnaWhisperEnc;
+
+/* Load the encoder (d_model 768, 12 heads, ffn 3072): linear weights quantised to bfp16
+ * along K, conv weights and positions bf16; up to max_batch clips per call.  Replaces
+ * WhisperEncoder's weights + conv_stem / block / forward_last (rust/npu-whisper/src/
+ * encoder.rs:183-375).  NULL on error. */
+XdnaWhisperEnc *xdna_whisper_enc_create(XdnaDevice *dev, const XdnaWhisperEncConfig *cfg,
+                                        const XdnaWhisperEncWeights *w, int max_batch);
+void xdna_whisper_enc_free(XdnaWhisperEnc *m);
+/* mel [B][n_mels][n_frames] f32 (host) -> encoder states [B][n_frames/2][768] f32 (host). */
+int xdna_whisper_encode(XdnaWhisperEnc *m, const float *mel, int B, float *out);
+/* Device-resident form: mel_dev f32, out_dev bf16 [B][n_frames/2][768]; async on `stream`. */
+int xdna_whisper_encode_device(XdnaWhisperEnc *m, const float *mel_dev, int B, uint16_t *out_dev,
+                               void *stream);
+
 /* ------------------------------------------------ opt-125m greedy decode (Opt::generate) */
 typedef struct {
     int n_layers, d_model, n_heads, head_dim, ffn, vocab, max_pos;

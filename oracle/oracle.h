@@ -158,6 +158,23 @@ typedef struct {
 int or_bert_embed(const or_bert_cfg *c, const or_bert_weights *w, const int32_t *ids,
                   const int32_t *seq_lens, int n_seqs, float *out, int nthreads);
 
+/* ---- Whisper-small encoder (rust/npu-whisper/src/encoder.rs:183-375) ---- */
+typedef struct {
+    int n_layers, d_model, n_heads, ffn, n_mels, n_frames, max_src;
+    float eps;
+} or_whisper_enc_cfg;
+typedef struct {
+    const float *ln1_w, *ln1_b, *q_w, *q_b, *k_w, *k_b, *v_w, *v_b, *out_w, *out_b;
+    const float *ln2_w, *ln2_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+} or_whisper_enc_layer;
+typedef struct {
+    const float *conv1_w, *conv1_b, *conv2_w, *conv2_b, *embed_positions, *ln_post_w, *ln_post_b;
+    const or_whisper_enc_layer *layers;
+} or_whisper_enc_weights;
+/* mel [B][n_mels][n_frames] -> out [B][n_frames/2][d_model] */
+int or_whisper_encode(const or_whisper_enc_cfg *c, const or_whisper_enc_weights *w, const float *mel,
+                      int B, float *out, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

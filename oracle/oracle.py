@@ -76,6 +76,8 @@ def lib():
         L.or_bert_embed.argtypes = [C.c_void_p, C.c_void_p, np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"),
                                     np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"), C.c_int, F32P, C.c_int]
         L.or_bert_embed.restype = C.c_int
+        L.or_whisper_encode.argtypes = [C.c_void_p, C.c_void_p, F32P, C.c_int, F32P, C.c_int]
+        L.or_whisper_encode.restype = C.c_int
         L.or_opt_step.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_void_p]
         L.or_opt_step.restype = C.c_int64
         L.or_opt_qweight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.POINTER(C.c_float))]
@@ -309,4 +311,47 @@ def bert_embed(cfg, w, ids, seq_lens, nthreads=None):
     out = np.empty((lens.size, cfg.d_model), np.float32)
     lib().or_bert_embed(C.addressof(c), C.addressof(ww), ids, lens, lens.size, out,
                         nthreads or os.cpu_count() or 1)
+    return out
+
+
+# ---------------------------------------------------------------- Whisper-small encoder
+_WENC_LAYER = ("ln1_w", "ln1_b", "q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "out_w", "out_b",
+               "ln2_w", "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b")
+
+
+class _WEncCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d_model", "n_heads", "ffn", "n_mels", "n_frames",
+                                       "max_src")] + [("eps", C.c_float)]
+
+
+class _WEncLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _WENC_LAYER]
+
+
+class _WEncWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("conv1_w", "conv1_b", "conv2_w", "conv2_b", "embed_positions",
+                                          "ln_post_w", "ln_post_b", "layers")]
+
+
+def whisper_encode(cfg, w, mel, nthreads=None):
+    """or_whisper_encode: the reference's f32 host encoder; mel [B, n_mels, n_frames]."""
+    keep = []
+
+    def p(a):
+        a = _f32(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    c = _WEncCfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.ffn, cfg.n_mels, cfg.n_frames, cfg.max_src, cfg.eps)
+    layers = (_WEncLayer * cfg.n_layers)()
+    for i, ly in enumerate(w["layers"]):
+        for n in _WENC_LAYER:
+            setattr(layers[i], n, p(ly[n]))
+    ww = _WEncWeights(*[p(w[n]) for n in ("conv1_w", "conv1_b", "conv2_w", "conv2_b", "embed_positions",
+                                          "ln_post_w", "ln_post_b")], C.addressof(layers))
+    mel = _f32(mel)
+    B = mel.shape[0]
+    out = np.empty((B, cfg.n_frames // 2, cfg.d_model), np.float32)
+    lib().or_whisper_encode(C.addressof(c), C.addressof(ww), mel.ravel(), B, out.ravel(),
+                            nthreads or os.cpu_count() or 1)
     return out

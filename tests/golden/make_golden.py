@@ -186,7 +186,59 @@ def bert_hf_fixture():
     print("bert_hf_golden.npz: ", np.stack(embs).shape)
 
 
+WHISPER_SMALL = dict(n_layers=2, d_model=64, n_heads=2, ffn=128, n_mels=8, n_frames=20, max_src=10, eps=1e-5)
+WHISPER_SMALL_SEED = 11
+
+
+def whisper_small_weights():
+    from xdna_engine_b200.synth import WhisperEncConfig, make_whisper_enc_weights, make_mel
+    cfg = WhisperEncConfig(**WHISPER_SMALL)
+    w = make_whisper_enc_weights(cfg, seed=WHISPER_SMALL_SEED, std=0.1, bias_std=0.05, ln_std=0.1)
+    return cfg, w, make_mel(cfg, batch=2, seed=WHISPER_SMALL_SEED)
+
+
+def whisper_hf_fixture():
+    """HF WhisperEncoder (the model the reference's encoder.rs restates, weights from the same
+    checkpoint layout): last_hidden_state on a small seeded random encoder, 2 clips."""
+    import torch
+    from transformers import WhisperConfig
+    from transformers.models.whisper.modeling_whisper import WhisperEncoder
+    cfg, w, mel = whisper_small_weights()
+    hc = WhisperConfig(d_model=cfg.d_model, encoder_layers=cfg.n_layers, encoder_attention_heads=cfg.n_heads,
+                       encoder_ffn_dim=cfg.ffn, num_mel_bins=cfg.n_mels, max_source_positions=cfg.max_src,
+                       activation_function="gelu", dropout=0.0, attention_dropout=0.0, activation_dropout=0.0)
+    model = WhisperEncoder(hc).eval().float()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    sd = {"conv1.weight": t(w["conv1_w"]), "conv1.bias": t(w["conv1_b"]),
+          "conv2.weight": t(w["conv2_w"]), "conv2.bias": t(w["conv2_b"]),
+          "embed_positions.weight": t(w["embed_positions"]),
+          "layer_norm.weight": t(w["ln_post_w"]), "layer_norm.bias": t(w["ln_post_b"])}
+    for i, ly in enumerate(w["layers"]):
+        p = f"layers.{i}."
+        for k, n in (("q", "self_attn.q_proj"), ("k", "self_attn.k_proj"), ("v", "self_attn.v_proj"),
+                     ("out", "self_attn.out_proj"), ("fc1", "fc1"), ("fc2", "fc2")):
+            sd[p + n + ".weight"] = t(ly[k + "_w"].T)
+            if k != "k":
+                sd[p + n + ".bias"] = t(ly[k + "_b"])
+        sd[p + "self_attn_layer_norm.weight"] = t(ly["ln1_w"])
+        sd[p + "self_attn_layer_norm.bias"] = t(ly["ln1_b"])
+        sd[p + "final_layer_norm.weight"] = t(ly["ln2_w"])
+        sd[p + "final_layer_norm.bias"] = t(ly["ln2_b"])
+    missing, unexpected = model.load_state_dict(sd, strict=True), None
+    with torch.no_grad():
+        enc = model(torch.from_numpy(mel)).last_hidden_state.numpy()
+    np.savez_compressed(os.path.join(HERE, "whisper_hf_golden.npz"), enc=enc)
+    print("whisper_hf_golden.npz:", enc.shape)
+
+
 if __name__ == "__main__":
-    bfp16_fixture()
-    opt_hf_fixture()
-    bert_hf_fixture()
+    import sys
+    only = set(sys.argv[1:])
+    if not only or "bfp16" in only:
+        bfp16_fixture()
+    if not only or "opt" in only:
+        opt_hf_fixture()
+    if not only or "bert" in only:
+        bert_hf_fixture()
+    if not only or "whisper" in only:
+        whisper_hf_fixture()

@@ -65,3 +65,19 @@ def test_quantiser_bit_exact_with_oracle(xl, shape):
     oq, os_ = O.quant_i8_cols(w)
     np.testing.assert_array_equal(s, os_)
     np.testing.assert_array_equal(q, oq.T)
+
+
+def test_bfp16_quantize_matches_oracle():
+    """xdna_bfp16_quantize (the engine's host-side weight quantiser for bfp16 linears) equals
+    or_bfp16_blocks bit for bit, zero blocks and outliers included."""
+    import xdna_engine_b200 as X
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal(8 * 4096) * np.exp(rng.uniform(-12, 12, 8 * 4096))).astype(np.float32)
+    x[:8] = 0.0
+    x[8:16] = [1e-30, 0, 0, 0, 0, 0, 0, -1e-30]
+    x[16:24] = [1.0, 2.0**-7, -2.0**-6, 3.0, 0, 0, 0, 0]
+    got = X.bfp16_quantize(x)
+    want = O.bfp16_blocks(x)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    with pytest.raises(X.XdnaError):
+        X.bfp16_quantize(x[:12])

@@ -256,3 +256,15 @@ def test_bert_oracle_matches_hf_golden():
     f = np.load(os.path.join(GOLD, "bert_hf_golden.npz"))
     e = O.bert_embed(cfg, w, f["ids"], f["lens"], 2)
     np.testing.assert_allclose(e, f["emb"], atol=1e-5, rtol=0)
+
+
+def test_whisper_encoder_oracle_matches_hf_golden():
+    """or_whisper_encode (encoder.rs conv_stem/block/forward_last restated) vs HF
+    WhisperEncoder.last_hidden_state on a small seeded encoder, 2 clips."""
+    import sys
+    sys.path.insert(0, GOLD)
+    import make_golden as G
+    cfg, w, mel = G.whisper_small_weights()
+    f = np.load(os.path.join(GOLD, "whisper_hf_golden.npz"))
+    e = O.whisper_encode(cfg, w, mel, 2)
+    np.testing.assert_allclose(e, f["enc"], atol=1e-4, rtol=0)  # A&S erf in GELU vs exact erf

@@ -15,7 +15,8 @@ import os
 import numpy as np
 
 from .synth import (OPT_125M, OptConfig, make_opt_weights, make_prompt,  # noqa: F401
-                    BGE_BASE, BertConfig, make_bert_weights, make_bge_batch)
+                    BGE_BASE, BertConfig, make_bert_weights, make_bge_batch,
+                    WHISPER_SMALL_ENC, WhisperEncConfig, make_whisper_enc_weights, make_mel)
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libxdna_b200.so")
@@ -74,6 +75,15 @@ def lib():
         L.xdna_bert_embed.restype = i
         L.xdna_bert_encode_device.argtypes = [vp, vp, vp, vp, i, i, i, vp, vp]
         L.xdna_bert_encode_device.restype = i
+        L.xdna_bfp16_quantize.argtypes = [vp, sz, vp]
+        L.xdna_bfp16_quantize.restype = i
+        L.xdna_whisper_enc_create.argtypes = [vp, vp, vp, i]
+        L.xdna_whisper_enc_create.restype = vp
+        L.xdna_whisper_enc_free.argtypes = [vp]
+        L.xdna_whisper_encode.argtypes = [vp, vp, i, vp]
+        L.xdna_whisper_encode.restype = i
+        L.xdna_whisper_encode_device.argtypes = [vp, vp, i, vp, vp]
+        L.xdna_whisper_encode_device.restype = i
         L.xdna_opt_create.argtypes = [vp, vp, vp, i, i]
         L.xdna_opt_create.restype = vp
         L.xdna_opt_free.argtypes = [vp]
@@ -286,6 +296,79 @@ class BertEmbedder:
     def close(self):
         if getattr(self, "handle", None):
             lib().xdna_bert_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def bfp16_quantize(x):
+    """The engine's bfp16 quantiser over contiguous blocks of 8 (same rule as the reference golden)."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    _check(lib().xdna_bfp16_quantize(_addr(x), x.size, _addr(y)))
+    return y
+
+
+_WENC_LAYER = ("ln1_w", "ln1_b", "q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "out_w", "out_b",
+               "ln2_w", "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b")
+
+
+class _WEncCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d_model", "n_heads", "ffn", "n_mels", "n_frames",
+                                       "max_src")] + [("eps", C.c_float)]
+
+
+class _WEncLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _WENC_LAYER]
+
+
+class _WEncWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("conv1_w", "conv1_b", "conv2_w", "conv2_b", "embed_positions",
+                                          "ln_post_w", "ln_post_b", "layers")]
+
+
+class WhisperEncoder:
+    """Whisper-small encoder on one B200 (WhisperEncoder::forward_last of the reference)."""
+
+    def __init__(self, device: Device, cfg, weights: dict, max_batch: int = 1):
+        keep = []
+
+        def p(a):
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            return _addr(a)
+
+        c = _WEncCfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.ffn, cfg.n_mels, cfg.n_frames, cfg.max_src,
+                     cfg.eps)
+        layers = (_WEncLayer * cfg.n_layers)()
+        for li, ly in enumerate(weights["layers"]):
+            for n in _WENC_LAYER:
+                setattr(layers[li], n, p(ly[n]))
+        w = _WEncWeights(*[p(weights[n]) for n in ("conv1_w", "conv1_b", "conv2_w", "conv2_b",
+                                                    "embed_positions", "ln_post_w", "ln_post_b")],
+                         C.addressof(layers))
+        h = lib().xdna_whisper_enc_create(device.handle, C.byref(c), C.byref(w), max_batch)
+        if not h:
+            raise XdnaError(last_error())
+        self.handle, self.cfg = h, cfg
+
+    def encode(self, mel):
+        mel = np.ascontiguousarray(mel, np.float32)
+        B = mel.shape[0]
+        out = np.empty((B, self.cfg.n_frames // 2, self.cfg.d_model), np.float32)
+        _check(lib().xdna_whisper_encode(self.handle, _addr(mel), B, _addr(out)))
+        return out
+
+    def encode_device(self, mel_ptr, B, out_ptr, stream=0):
+        _check(lib().xdna_whisper_encode_device(self.handle, mel_ptr, B, out_ptr, stream or None))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().xdna_whisper_enc_free(self.handle)
             self.handle = None
 
     def __del__(self):

@@ -29,7 +29,7 @@ namespace xdna {
 void set_last_error_message(const std::string &m);
 cudaError_t gemm_bf16(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M, int N, int K,
                       const float *bias, const uint16_t *residual, int ldr, int gelu, uint16_t *C, int ldc,
-                      cudaStream_t st);
+                      cudaStream_t st, int res_mod = 0);
 unsigned gemm_error_and_clear();
 
 namespace bert {
@@ -540,6 +540,265 @@ int xdna_bert_embed(XdnaBert *m, const int32_t *ids, const int32_t *seq_lens, in
         return 0;
     } catch (const std::exception &ex) {
         set_last_error_message(std::string("xdna_bert_embed: ") + ex.what());
+        return -1;
+    }
+}
+
+}  // extern "C"
+
+// =============================================================================== Whisper
+// Whisper-small encoder (rust/npu-whisper/src/encoder.rs:183-203 conv_stem, 221-227 add_pos,
+// 236-337 block, 350-375 forward_last): conv1 (k3 s1 p1) + GELU, conv2 (k3 s2 p1) + GELU,
+// + embed_positions, pre-LN blocks, ln_post.  The convolutions are tcgen05 GEMMs over an
+// im2col in tap-major order (column ki*Cin + ci; the weights are permuted to match), GELU and
+// the positional add fused into the GEMM epilogue.  Linear weights are quantised to bfp16
+// (blocks of 8 along K, route_b_kernels/ffn_bfp16/golden_ffn_gemm.py:34-49) at load; the
+// block values are exactly representable in bf16, so the bf16 tensor-core GEMM computes on
+// exactly the bfp16 weights.
+namespace xdna {
+namespace whisper {
+
+constexpr int D = 768, F = 3072;
+
+// cols[b*T + t][ki*C + ci] = mel[b][ci][t + ki - 1] (zero outside), columns C*3 .. ldc-1 zero
+__global__ void im2col_mel_kernel(const float *mel, int B, int C, int T, int ldc, uint16_t *cols) {
+    const size_t total = (size_t)B * T * ldc;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int col = (int)(i % ldc);
+        const size_t row = i / ldc;
+        const int b = (int)(row / T), t = (int)(row % T);
+        float v = 0.0f;
+        if (col < 3 * C) {
+            const int ki = col / C, ci = col % C, ts = t + ki - 1;
+            if (ts >= 0 && ts < T) v = mel[((size_t)b * C + ci) * T + ts];
+        }
+        cols[i] = (uint16_t)bf16bits(v);
+    }
+}
+
+// cols[b*To + t][ki*D + c] = h[b*Ti + 2t + ki - 1][c] (zero outside): 16-byte vectors
+__global__ void im2col_s2_kernel(const uint16_t *h, int B, int Ti, int To, uint16_t *cols) {
+    const size_t vec_per_row = 3 * D / 8;
+    const size_t total = (size_t)B * To * vec_per_row;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t row = i / vec_per_row;
+        const int v = (int)(i % vec_per_row);
+        const int b = (int)(row / To), t = (int)(row % To);
+        const int ki = v / (D / 8), c8 = v % (D / 8);
+        const int ts = 2 * t + ki - 1;
+        uint4 val = make_uint4(0, 0, 0, 0);
+        if (ts >= 0 && ts < Ti) val = reinterpret_cast<const uint4 *>(h + ((size_t)b * Ti + ts) * D)[c8];
+        reinterpret_cast<uint4 *>(cols)[i] = val;
+    }
+}
+
+// y = LN(x) with eps, x/y [rows, 768] bf16 (pre-norm: x is kept as the residual stream)
+}  // namespace whisper
+
+namespace {
+// to_bfp16_blocks along contiguous runs of 8 (golden_ffn_gemm.py:34-49): shared exponent
+// e = floor(log2(max|x|)) (max 0 -> 1.0), quantum 2^(e-6), round half to even, no clamp.
+void bfp16_blocks(const float *x, float *y, size_t n) {
+    for (size_t b0 = 0; b0 < n; b0 += 8) {
+        float m = 0.0f;
+        for (int i = 0; i < 8; i++) m = std::fmax(m, std::fabs(x[b0 + i]));
+        if (m == 0.0f) m = 1.0f;
+        int e;
+        (void)std::frexp(m, &e);
+        e -= 1;
+        const float q = std::ldexp(1.0f, e - 6);
+        for (int i = 0; i < 8; i++) y[b0 + i] = std::nearbyint(x[b0 + i] / q) * q;
+    }
+}
+// [K, N] f32 -> bfp16 along K for every output column -> [N, K] bf16 appended to out
+void append_bfp16_transposed(const float *w, int K, int N, std::vector<uint16_t> &out) {
+    const size_t base = out.size();
+    out.resize(base + (size_t)N * K);
+    std::vector<float> col(K), q(K);
+    for (int n = 0; n < N; n++) {
+        for (int k = 0; k < K; k++) col[k] = w[(size_t)k * N + n];
+        bfp16_blocks(col.data(), q.data(), K);
+        for (int k = 0; k < K; k++) out[base + (size_t)n * K + k] = to_bf16_bits(q[k]);
+    }
+}
+}  // namespace
+}  // namespace xdna
+
+struct XdnaWhisperEnc {
+    XdnaWhisperEncConfig cfg{};
+    int max_batch = 0, K1 = 0;
+    uint16_t *c1w = nullptr, *c2w = nullptr, *pos = nullptr;   // [768, K1], [768, 2304], [max_src, 768]
+    float *c1b = nullptr, *c2b = nullptr, *lnpost = nullptr;
+    struct Layer {
+        uint16_t *wqkv, *wo, *w1, *w2;
+        float *bqkv, *bo, *b1, *b2, *ln1, *ln2;
+    };
+    std::vector<Layer> layers;
+    uint16_t *cols = nullptr, *h1 = nullptr, *x = nullptr, *y = nullptr, *qkv = nullptr, *ctx = nullptr, *hb = nullptr;
+    float *mel = nullptr;
+    int32_t *cu = nullptr;
+    std::vector<void *> owned;
+    ~XdnaWhisperEnc() {
+        for (void *p : owned) cudaFree(p);
+    }
+};
+
+extern "C" {
+
+int xdna_bfp16_quantize(const float *x, size_t n, float *y) {
+    if (!x || !y || n % 8) { set_last_error_message("xdna_bfp16_quantize: null pointer or n % 8 != 0"); return -1; }
+    bfp16_blocks(x, y, n);
+    return 0;
+}
+
+XdnaWhisperEnc *xdna_whisper_enc_create(XdnaDevice *dev_unused, const XdnaWhisperEncConfig *cfg,
+                                        const XdnaWhisperEncWeights *w, int max_batch) {
+    (void)dev_unused;
+    if (!cfg || !w || !w->layers || !w->conv1_w || !w->conv1_b || !w->conv2_w || !w->conv2_b ||
+        !w->embed_positions || !w->ln_post_w || !w->ln_post_b) {
+        set_last_error_message("xdna_whisper_enc_create: null pointer");
+        return nullptr;
+    }
+    const XdnaWhisperEncConfig c = *cfg;
+    if (c.d_model != whisper::D || c.n_heads != 12 || c.ffn != whisper::F || c.n_layers < 1 || c.n_mels < 1 ||
+        c.n_frames < 2 || c.n_frames % 2 || c.n_frames / 2 > c.max_src || max_batch < 1) {
+        set_last_error_message("xdna_whisper_enc_create: supported shape is d_model 768, 12 heads, ffn 3072; "
+                               "n_frames even with n_frames / 2 <= max_src");
+        return nullptr;
+    }
+    auto *m = new XdnaWhisperEnc();
+    try {
+        const int D = whisper::D, F = whisper::F, C = c.n_mels, T = c.n_frames, To = c.n_frames / 2;
+        m->cfg = c;
+        m->max_batch = max_batch;
+        m->K1 = (3 * C + 63) / 64 * 64;
+        auto keep = [&](void *p) { m->owned.push_back(p); return p; };
+        auto f32 = [&](std::initializer_list<std::pair<const float *, size_t>> parts) {
+            std::vector<float> v;
+            for (auto &pr : parts) {
+                if (pr.first) v.insert(v.end(), pr.first, pr.first + pr.second);
+                else v.insert(v.end(), pr.second, 0.0f);
+            }
+            return static_cast<float *>(keep(dupload(v)));
+        };
+        // conv weights [Cout, Cin, 3] -> tap-major [Cout, ki*Cin + ci] bf16 (K padded)
+        std::vector<uint16_t> t1((size_t)D * m->K1, 0), t2((size_t)D * 3 * D, 0);
+        for (int co = 0; co < D; co++)
+            for (int ci = 0; ci < C; ci++)
+                for (int ki = 0; ki < 3; ki++)
+                    t1[(size_t)co * m->K1 + ki * C + ci] = to_bf16_bits(w->conv1_w[((size_t)co * C + ci) * 3 + ki]);
+        for (int co = 0; co < D; co++)
+            for (int ci = 0; ci < D; ci++)
+                for (int ki = 0; ki < 3; ki++)
+                    t2[(size_t)co * 3 * D + ki * D + ci] = to_bf16_bits(w->conv2_w[((size_t)co * D + ci) * 3 + ki]);
+        m->c1w = static_cast<uint16_t *>(keep(dupload(t1)));
+        m->c2w = static_cast<uint16_t *>(keep(dupload(t2)));
+        m->c1b = f32({{w->conv1_b, (size_t)D}});
+        m->c2b = f32({{w->conv2_b, (size_t)D}});
+        std::vector<uint16_t> pv((size_t)To * D);
+        for (size_t i = 0; i < pv.size(); i++) pv[i] = to_bf16_bits(w->embed_positions[i]);
+        m->pos = static_cast<uint16_t *>(keep(dupload(pv)));
+        m->lnpost = f32({{w->ln_post_w, (size_t)D}, {w->ln_post_b, (size_t)D}});
+        for (int l = 0; l < c.n_layers; l++) {
+            const XdnaWhisperEncLayer &L = w->layers[l];
+            XdnaWhisperEnc::Layer o{};
+            std::vector<uint16_t> t;
+            append_bfp16_transposed(L.q_w, D, D, t);
+            append_bfp16_transposed(L.k_w, D, D, t);
+            append_bfp16_transposed(L.v_w, D, D, t);
+            o.wqkv = static_cast<uint16_t *>(keep(dupload(t)));
+            t.clear(); append_bfp16_transposed(L.out_w, D, D, t); o.wo = static_cast<uint16_t *>(keep(dupload(t)));
+            t.clear(); append_bfp16_transposed(L.fc1_w, D, F, t); o.w1 = static_cast<uint16_t *>(keep(dupload(t)));
+            t.clear(); append_bfp16_transposed(L.fc2_w, F, D, t); o.w2 = static_cast<uint16_t *>(keep(dupload(t)));
+            o.bqkv = f32({{L.q_b, (size_t)D}, {L.k_b, (size_t)D}, {L.v_b, (size_t)D}});   // k_b may be null: zeros
+            o.bo = f32({{L.out_b, (size_t)D}});
+            o.b1 = f32({{L.fc1_b, (size_t)F}});
+            o.b2 = f32({{L.fc2_b, (size_t)D}});
+            o.ln1 = f32({{L.ln1_w, (size_t)D}, {L.ln1_b, (size_t)D}});
+            o.ln2 = f32({{L.ln2_w, (size_t)D}, {L.ln2_b, (size_t)D}});
+            m->layers.push_back(o);
+        }
+        const size_t B = (size_t)max_batch, R1 = B * T, R2 = B * To;
+        m->mel = static_cast<float *>(keep(dalloc<float>(B * C * T)));
+        m->cols = static_cast<uint16_t *>(keep(dalloc<uint16_t>(std::max(R1 * m->K1, R2 * 3 * D))));
+        m->h1 = static_cast<uint16_t *>(keep(dalloc<uint16_t>(R1 * D)));
+        m->x = static_cast<uint16_t *>(keep(dalloc<uint16_t>(R2 * D)));
+        m->y = static_cast<uint16_t *>(keep(dalloc<uint16_t>(R2 * D)));
+        m->qkv = static_cast<uint16_t *>(keep(dalloc<uint16_t>(R2 * 3 * D)));
+        m->ctx = static_cast<uint16_t *>(keep(dalloc<uint16_t>(R2 * D)));
+        m->hb = static_cast<uint16_t *>(keep(dalloc<uint16_t>(R2 * F)));
+        std::vector<int32_t> cu(B + 1);
+        for (size_t b = 0; b <= B; b++) cu[b] = (int32_t)(b * To);
+        m->cu = static_cast<int32_t *>(keep(dupload(cu)));
+        ck(cudaDeviceSynchronize(), "create sync");
+        return m;
+    } catch (const std::exception &ex) {
+        set_last_error_message(std::string("xdna_whisper_enc_create: ") + ex.what());
+        delete m;
+        return nullptr;
+    }
+}
+
+void xdna_whisper_enc_free(XdnaWhisperEnc *m) {
+    if (!m) return;
+    cudaDeviceSynchronize();
+    delete m;
+}
+
+// Device-resident encoder: mel_dev [B][n_mels][n_frames] f32 -> out_dev [B][n_frames/2][768] bf16
+int xdna_whisper_encode_device(XdnaWhisperEnc *m, const float *mel_dev, int B, uint16_t *out_dev, void *stream) {
+    if (!m || !mel_dev || !out_dev) { set_last_error_message("xdna_whisper_encode_device: null pointer"); return -1; }
+    if (B < 1 || B > m->max_batch) { set_last_error_message("xdna_whisper_encode_device: batch beyond max_batch"); return -1; }
+    using namespace whisper;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int C = m->cfg.n_mels, T = m->cfg.n_frames, To = T / 2, R1 = B * T, R2 = B * To;
+    const float eps = m->cfg.eps;
+    cudaError_t e = cudaSuccess;
+    im2col_mel_kernel<<<1184, 256, 0, st>>>(mel_dev, B, C, T, m->K1, m->cols);
+    if (!e) e = gemm_bf16(m->cols, m->K1, m->c1w, m->K1, R1, D, m->K1, m->c1b, nullptr, 0, 1, m->h1, D, st);
+    im2col_s2_kernel<<<1184, 256, 0, st>>>(m->h1, B, T, To, m->cols);
+    // conv2 + GELU, then + embed_positions[t] (residual row = output row mod To)
+    if (!e) e = gemm_bf16(m->cols, 3 * D, m->c2w, 3 * D, R2, D, 3 * D, m->c2b, m->pos, D, 1, m->x, D, st, To);
+    for (size_t li = 0; li < m->layers.size() && !e; li++) {
+        const auto &L = m->layers[li];
+        bert::ln_kernel<<<(R2 + 7) / 8, 256, 0, st>>>(m->x, R2, L.ln1, L.ln1 + D, eps, m->y);
+        if ((e = gemm_bf16(m->y, D, L.wqkv, D, R2, 3 * D, D, L.bqkv, nullptr, 0, 0, m->qkv, 3 * D, st))) break;
+        bert::attention_kernel<<<dim3((To + bert::AQ - 1) / bert::AQ, 12, B), bert::ATHREADS, 0, st>>>(m->qkv, m->cu, m->ctx);
+        if ((e = gemm_bf16(m->ctx, D, L.wo, D, R2, D, D, L.bo, m->x, D, 0, m->y, D, st))) break;
+        std::swap(m->x, m->y);   // x <- x + attn
+        bert::ln_kernel<<<(R2 + 7) / 8, 256, 0, st>>>(m->x, R2, L.ln2, L.ln2 + D, eps, m->y);
+        if ((e = gemm_bf16(m->y, D, L.w1, D, R2, F, D, L.b1, nullptr, 0, 1, m->hb, F, st))) break;
+        if ((e = gemm_bf16(m->hb, F, L.w2, F, R2, D, F, L.b2, m->x, D, 0, m->y, D, st))) break;
+        std::swap(m->x, m->y);   // x <- x + ffn
+    }
+    if (!e) bert::ln_kernel<<<(R2 + 7) / 8, 256, 0, st>>>(m->x, R2, m->lnpost, m->lnpost + D, eps, out_dev);
+    if (!e) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_last_error_message(std::string("xdna_whisper_encode_device: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+// Host in / host out: mel [B][n_mels][n_frames] f32 -> encoded [B][n_frames/2][768] f32
+int xdna_whisper_encode(XdnaWhisperEnc *m, const float *mel, int B, float *out) {
+    if (!m || !mel || !out) { set_last_error_message("xdna_whisper_encode: null pointer"); return -1; }
+    if (B < 1 || B > m->max_batch) { set_last_error_message("xdna_whisper_encode: batch beyond max_batch"); return -1; }
+    const int C = m->cfg.n_mels, T = m->cfg.n_frames, To = T / 2;
+    try {
+        ck(cudaMemcpy(m->mel, mel, sizeof(float) * (size_t)B * C * T, cudaMemcpyHostToDevice), "copy mel");
+        uint16_t *enc = m->hb;   // reuse the FFN buffer for the bf16 result
+        if (xdna_whisper_encode_device(m, m->mel, B, enc, nullptr) != 0) return -1;
+        std::vector<uint16_t> hbuf((size_t)B * To * whisper::D);
+        ck(cudaMemcpy(hbuf.data(), enc, hbuf.size() * 2, cudaMemcpyDeviceToHost), "copy encoded");
+        for (size_t i = 0; i < hbuf.size(); i++) {
+            const uint32_t u = (uint32_t)hbuf[i] << 16;
+            std::memcpy(out + i, &u, 4);
+        }
+        if (gemm_error_and_clear()) { set_last_error_message("xdna_whisper_encode: a GEMM wait expired"); return -1; }
+        return 0;
+    } catch (const std::exception &ex) {
+        set_last_error_message(std::string("xdna_whisper_encode: ") + ex.what());
         return -1;
     }
 }

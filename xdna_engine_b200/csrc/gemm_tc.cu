@@ -42,8 +42,9 @@ static __device__ unsigned int g_gemm_error;
 
 struct Epi {
     const float *bias;          // [N] or null
-    const uint16_t *residual;   // [M, ldr] bf16 or null
+    const uint16_t *residual;   // [M, ldr] bf16 or null; row r reads residual row r % res_mod
     int ldr;
+    int res_mod;                // 0: residual row = output row
     int gelu;
     uint16_t *out;              // [M, ldc] bf16
     int ldc;
@@ -173,8 +174,9 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 tc::tmem_ld_wait();
                 if (row < M) {
                     const int col = n0 + c0;
+                    const int rrow = epi.res_mod ? row % epi.res_mod : row;
                     const uint4 *rp = epi.residual
-                        ? reinterpret_cast<const uint4 *>(epi.residual + (size_t)row * epi.ldr + col) : nullptr;
+                        ? reinterpret_cast<const uint4 *>(epi.residual + (size_t)rrow * epi.ldr + col) : nullptr;
                     uint4 *op = reinterpret_cast<uint4 *>(epi.out + (size_t)row * epi.ldc + col);
 #pragma unroll
                     for (int u = 0; u < 8; u++) {
@@ -262,8 +264,8 @@ cudaError_t launch(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M
 
 cudaError_t gemm_bf16(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M, int N, int K,
                       const float *bias, const uint16_t *residual, int ldr, int gelu, uint16_t *C, int ldc,
-                      cudaStream_t st) {
-    gemm::Epi e{bias, residual, ldr, gelu, C, ldc};
+                      cudaStream_t st, int res_mod) {
+    gemm::Epi e{bias, residual, ldr, res_mod, gelu, C, ldc};
     return gemm::launch(A, lda, B, ldb, M, N, K, e, st);
 }
 
@@ -284,7 +286,7 @@ extern "C" int xdna_gemm_bf16(const uint16_t *A, const uint16_t *B, const float 
         set_last_error_message("xdna_gemm_bf16: need M > 0, N % 256 == 0, K % 64 == 0");
         return -1;
     }
-    cudaError_t e = gemm_bf16(A, K, B, K, M, N, K, bias, residual, N, gelu, C, N, (cudaStream_t)stream);
+    cudaError_t e = gemm_bf16(A, K, B, K, M, N, K, bias, residual, N, gelu, C, N, (cudaStream_t)stream, 0);
     if (e != cudaSuccess) {
         set_last_error_message(std::string("xdna_gemm_bf16: ") + cudaGetErrorString(e));
         return -1;

@@ -149,3 +149,64 @@ def make_bge_batch(n_seqs: int = 256, seed: int = 0, lo: int = 32, hi: int = 512
     lens = rng.integers(lo, hi + 1, size=n_seqs).astype(np.int32)
     ids = rng.integers(1000, 30000, size=int(lens.sum())).astype(np.int32)
     return ids, lens
+
+
+# --------------------------------------------------------------------- Whisper-small encoder
+@dataclass(frozen=True)
+class WhisperEncConfig:
+    n_layers: int = 12
+    d_model: int = 768
+    n_heads: int = 12
+    ffn: int = 3072
+    n_mels: int = 80
+    n_frames: int = 3000
+    max_src: int = 1500
+    eps: float = 1e-5
+
+
+WHISPER_SMALL_ENC = WhisperEncConfig()
+WHISPER_ENC_LAYER_KEYS = ("ln1_w", "ln1_b", "q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "out_w", "out_b",
+                          "ln2_w", "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b")
+
+
+def make_whisper_enc_weights(cfg: WhisperEncConfig = WHISPER_SMALL_ENC, seed: int = 0, std: float = 0.02,
+                             bias_std: float = 0.0, ln_std: float = 0.0) -> dict:
+    """Random-init Whisper encoder weights (f32; linear weights [K, N]); k has no bias (zeros),
+    as in Whisper."""
+    rng = np.random.default_rng(seed)
+    D, F = cfg.d_model, cfg.ffn
+
+    def normal(shape, s):
+        a = rng.standard_normal(shape, dtype=np.float32)
+        a *= np.float32(s)
+        return a
+
+    def vec(n, base, s):
+        if s == 0.0:
+            return np.full(n, base, np.float32)
+        return (np.float32(base) + rng.standard_normal(n, dtype=np.float32) * np.float32(s)).astype(np.float32)
+
+    w = {"conv1_w": normal((D, cfg.n_mels, 3), std), "conv1_b": vec(D, 0.0, bias_std),
+         "conv2_w": normal((D, D, 3), std), "conv2_b": vec(D, 0.0, bias_std),
+         "embed_positions": normal((cfg.max_src, D), std),
+         "ln_post_w": vec(D, 1.0, ln_std), "ln_post_b": vec(D, 0.0, ln_std)}
+    layers = []
+    for _ in range(cfg.n_layers):
+        layers.append({
+            "ln1_w": vec(D, 1.0, ln_std), "ln1_b": vec(D, 0.0, ln_std),
+            "q_w": normal((D, D), std), "q_b": vec(D, 0.0, bias_std),
+            "k_w": normal((D, D), std), "k_b": np.zeros(D, np.float32),
+            "v_w": normal((D, D), std), "v_b": vec(D, 0.0, bias_std),
+            "out_w": normal((D, D), std), "out_b": vec(D, 0.0, bias_std),
+            "ln2_w": vec(D, 1.0, ln_std), "ln2_b": vec(D, 0.0, ln_std),
+            "fc1_w": normal((D, F), std), "fc1_b": vec(F, 0.0, bias_std),
+            "fc2_w": normal((F, D), std), "fc2_b": vec(D, 0.0, bias_std),
+        })
+    w["layers"] = layers
+    return w
+
+
+def make_mel(cfg: WhisperEncConfig = WHISPER_SMALL_ENC, batch: int = 1, seed: int = 0) -> np.ndarray:
+    """Synthetic log-mel input ~N(0, 1), [batch, n_mels, n_frames]."""
+    rng = np.random.default_rng(seed + 9_000_011)
+    return rng.standard_normal((batch, cfg.n_mels, cfg.n_frames), dtype=np.float32)
