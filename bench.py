@@ -56,7 +56,7 @@ class Clocks:
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu):
-        self.gpu, self.rows, self.proc = gpu, [], None
+        self.gpu, self.rows, self.proc, self.first = gpu, [], None, 0
 
     def __enter__(self):
         try:
@@ -66,6 +66,11 @@ class Clocks:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # the sampler is live once its first row is in; only later rows are in the region
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5.0:
+                time.sleep(0.01)
+            self.first = len(self.rows)
         except Exception:
             self.proc = None
         return self
@@ -83,14 +88,15 @@ class Clocks:
                 self.proc.kill()
 
     def summary(self):
-        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        rows = self.rows[self.first:]
+        sm = [float(r[1]) for r in rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) >= 9
+        reasons = sorted({names[i] for r in rows if len(r) >= 9
                           for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+                "samples": len(rows)}
 
 
 def cpu_port_tokens_per_s(cfg, w, prompt, steps, nthreads):
@@ -563,7 +569,7 @@ def run_whisper(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--steps", type=int, default=0, help="timed steps (default: about half a second of work)")
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode", "bge", "whisper"], default="decode")
@@ -571,16 +577,20 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     if args.workload == "whisper":
-        if args.steps == 256:
-            args.steps = 10
+        if args.steps <= 0:
+            args.steps = 30
         (run_whisper_reference if args.impl == "reference" else run_whisper)(args)
     elif args.workload == "bge":
-        if args.steps == 256:
-            args.steps = 10
+        if args.steps <= 0:
+            args.steps = 30
         (run_bge_reference if args.impl == "reference" else run_bge)(args)
     elif args.impl == "reference":
+        if args.steps <= 0:
+            args.steps = 256
         run_reference(args)
     else:
+        if args.steps <= 0:
+            args.steps = 2048
         run_ours(args)
 
 

@@ -166,44 +166,56 @@ static void ln_dev_bf16(const float *x, const float *g, const float *b, int D, f
 }
 /* Single-query attention of one head as the engine splits it: one partial (m, l, acc) per
  * 64-key page (mha_tile's online softmax, route_b_kernels/mha_decode/mha_decode.cc:90-168,
- * applied per page), pages merged in order; exp = the reference's fast_exp_nonpos. */
+ * applied per page); the pages of each group of OR_GROUP_PAGES are merged in order into a
+ * group partial, and the group partials are merged in order; exp = the reference's
+ * fast_exp_nonpos.  (With one group, the second merge is the identity.) */
+#define OR_GROUP_PAGES 3
+static void fold(float *M, float *L, float *A, float m, float l, const float *a) {
+    float mn = fmaxf(*M, m);
+    float c0 = or_fast_exp_nonpos(*M - mn), c1 = or_fast_exp_nonpos(m - mn);
+    *L = *L * c0 + l * c1;
+    for (int d = 0; d < 64; d++) A[d] = A[d] * c0 + a[d] * c1;
+    *M = mn;
+}
 static void attn_dev_head(const float *q, const float *kc, const float *vc, int stride, int tk,
                           float *ctx) {
     float M = -INFINITY, L = 0.0f, A[64];
     for (int d = 0; d < 64; d++) A[d] = 0.0f;
-    for (int j0 = 0; j0 < tk; j0 += 64) {
-        int nk = tk - j0 < 64 ? tk - j0 : 64;
-        float sc[64], pr[64], m = -INFINITY;
-        for (int k = 0; k < 64; k++) {
-            if (k >= nk) { sc[k] = -INFINITY; continue; }
-            const float *kr = kc + (size_t)(j0 + k) * stride;
-            float s4[4];
-            for (int q4 = 0; q4 < 4; q4++) {
-                float sd = 0.0f;
-                for (int d = 0; d < 16; d++) sd = fmaf(q[16 * q4 + d], kr[16 * q4 + d], sd);
-                s4[q4] = sd;
+    for (int g0 = 0; g0 < tk; g0 += 64 * OR_GROUP_PAGES) {
+        float Mg = -INFINITY, Lg = 0.0f, Ag[64];
+        for (int d = 0; d < 64; d++) Ag[d] = 0.0f;
+        for (int j0 = g0; j0 < tk && j0 < g0 + 64 * OR_GROUP_PAGES; j0 += 64) {
+            int nk = tk - j0 < 64 ? tk - j0 : 64;
+            float sc[64], pr[64], m = -INFINITY, ap[64];
+            for (int k = 0; k < 64; k++) {
+                if (k >= nk) { sc[k] = -INFINITY; continue; }
+                const float *kr = kc + (size_t)(j0 + k) * stride;
+                float s4[4];
+                for (int q4 = 0; q4 < 4; q4++) {
+                    float sd = 0.0f;
+                    for (int d = 0; d < 16; d++) sd = fmaf(q[16 * q4 + d], kr[16 * q4 + d], sd);
+                    s4[q4] = sd;
+                }
+                sc[k] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+                m = fmaxf(m, sc[k]);
             }
-            sc[k] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
-            m = fmaxf(m, sc[k]);
-        }
-        float v32[32];
-        for (int k = 0; k < 64; k++) pr[k] = k < nk ? or_fast_exp_nonpos(sc[k] - m) : 0.0f;
-        for (int l = 0; l < 32; l++) v32[l] = pr[l] + pr[l + 32];
-        float lp = warp_tree(v32);
-        float c0 = or_fast_exp_nonpos(M - fmaxf(M, m)), c1 = or_fast_exp_nonpos(m - fmaxf(M, m));
-        L = L * c0 + lp * c1;
-        for (int d = 0; d < 64; d++) {
-            float a4[4];
-            for (int q4 = 0; q4 < 4; q4++) {
-                float a = 0.0f;
-                for (int j = 16 * q4; j < 16 * q4 + 16 && j < nk; j++)
-                    a = fmaf(pr[j], vc[(size_t)(j0 + j) * stride + d], a);
-                a4[q4] = a;
+            float v32[32];
+            for (int k = 0; k < 64; k++) pr[k] = k < nk ? or_fast_exp_nonpos(sc[k] - m) : 0.0f;
+            for (int l = 0; l < 32; l++) v32[l] = pr[l] + pr[l + 32];
+            float lp = warp_tree(v32);
+            for (int d = 0; d < 64; d++) {
+                float a4[4];
+                for (int q4 = 0; q4 < 4; q4++) {
+                    float a = 0.0f;
+                    for (int j = 16 * q4; j < 16 * q4 + 16 && j < nk; j++)
+                        a = fmaf(pr[j], vc[(size_t)(j0 + j) * stride + d], a);
+                    a4[q4] = a;
+                }
+                ap[d] = ((a4[0] + a4[1]) + a4[2]) + a4[3];
             }
-            float ap = ((a4[0] + a4[1]) + a4[2]) + a4[3];
-            A[d] = A[d] * c0 + ap * c1;
+            fold(&Mg, &Lg, Ag, m, lp, ap);
         }
-        M = fmaxf(M, m);
+        fold(&M, &L, A, Mg, Lg, Ag);
     }
     for (int d = 0; d < 64; d++) ctx[d] = or_bf16_round(A[d] / L);
 }

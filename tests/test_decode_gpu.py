@@ -74,10 +74,13 @@ def test_decode_small_matches_oracle(X, dev, grid):
     np.testing.assert_array_equal(lg, olg)
 
 
-def test_decode_prompt_of_one_and_long_context(X, dev):
+@pytest.mark.parametrize("n_prompt,n_new,grid", [(1, 200, 0), (200, 300, 0), (200, 300, 8)])
+def test_decode_prompt_of_one_and_long_context(X, dev, n_prompt, n_new, grid):
+    """Contexts past one attention item (3 KV pages = 192 positions): several page groups per
+    head, merged by the O-projection CTAs; grid=8 gives CTAs several groups each."""
     w = make_opt_weights(SMALL, seed=4, std=0.2)
-    prompt = make_prompt(SMALL, 1, seed=4)
-    ids, lg, oids, olg = _run_pair(X, dev, SMALL, w, prompt, 200, max_ctx=256)
+    prompt = make_prompt(SMALL, n_prompt, seed=4)
+    ids, lg, oids, olg = _run_pair(X, dev, SMALL, w, prompt, n_new, grid=grid, max_ctx=n_prompt + n_new)
     np.testing.assert_array_equal(ids, oids)
     np.testing.assert_array_equal(lg, olg)
 

@@ -9,13 +9,14 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;   // + one producer warp
 constexpr int kStageBytes = 32768;                // one weight chunk (ring stage)
-constexpr int kStages = 5;                        // ring depth: 160 KB of weights in flight
+constexpr int kStages = 4;                        // ring depth: 128 KB of weights in flight
 constexpr int kKmax = 3072;                       // largest GEMV reduction length
-constexpr int kDmax = 1024;                       // largest model width
+constexpr int kDmax = 768;                        // largest model width
 constexpr int kHeadDim = 64;                      // the kernel's attention head size
 constexpr int kPageTokens = 64;                   // KV page = 64 positions (the reference's TKV tile)
 constexpr int kMaxTilesPerChunk = kStageBytes / (768 + 8) / 8;   // 5 for K=768
 constexpr int kMaxPages = 64;                     // KV pages per sequence (4096 positions)
+constexpr int kGroupPages = 3;                    // KV pages one attention item covers (192 positions)
 constexpr int kRowMeta = 8;                       // per-row f32 scale + f32 bias after the rows
 
 // Row partition and chunking shared by the host packer and the kernel.  Rows are assigned

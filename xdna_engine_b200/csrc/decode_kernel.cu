@@ -46,11 +46,12 @@ struct SmemMap {
     static constexpr int act = limbs + 3 * kKmax;                        // kKmax bf16 / words
     static constexpr int xs = act + kKmax * 2;                           // 2 x kDmax f32
     static constexpr int lnp = xs + 2 * kDmax * 4;                       // [2][g|b][kDmax] f32
-    static constexpr int kvbuf = lnp + 4 * kDmax * 4;                    // 2 x 64 x 64 bf16
-    static constexpr int part = kvbuf + 2 * kPageTokens * kHeadDim * 2;  // 2 x partial MMA sums
+    static constexpr int kvbuf = lnp + 4 * kDmax * 4;                    // [page][K|V][64][64] bf16
+    static constexpr int kvbuf_bytes = kGroupPages * 2 * kPageTokens * kHeadDim * 2;
+    static constexpr int part = kvbuf + kvbuf_bytes;                     // 2 x partial MMA sums
     static constexpr int part_ints = kConsumerWarps * kMaxTilesPerChunk * 3 * 8;
     static constexpr int misc = part + 2 * part_ints * 4;
-    static constexpr int misc_floats = 64 + 64 + 64 + 4 * 64 + 96 + 32 + kMaxPages;
+    static constexpr int misc_floats = 64 + 64 + 64 * kGroupPages + 4 * 64 * kGroupPages + 96 + 32 + kMaxPages + 8;
     static constexpr int bars = (misc + misc_floats * 4 + 15) & ~15;
     static constexpr int total = bars + 2 * kStages * 8 + 16;
 };
@@ -62,9 +63,9 @@ struct Cta {
     uint16_t *act;              // GEMV input vector (bf16) / gather buffer (32-bit words)
     float *xs;                  // residual stream, double buffered: xs[0..kDmax), xs[kDmax..)
     float *lnp;                 // LayerNorm parameters: [buf][0 = gamma, 1 = beta][kDmax]
-    uint16_t *kvbuf;            // [2][64][64] bf16: K rows then V rows (also a gather buffer)
+    uint16_t *kvbuf;            // [kGroupPages][2][64][64] bf16: K rows then V rows per page (also a gather buffer)
     int *part;                  // [2][warps][tiles][3][8] partial limb sums
-    float *red, *qf, *sc, *accp;
+    float *red, *qf, *sc, *accp, *pst;   // pst: per-page (m, l)
     uint32_t *qkvw;             // 96 words: q, k, v of one head
     int *flag;                  // [0] abort flag, [1] greedy id
     int *pt;                    // page table copy
@@ -72,7 +73,10 @@ struct Cta {
     int tid, warp, lane;
 };
 
-__device__ __forceinline__ Cta make_cta(uint8_t *smem) {
+// the kernels' dynamic shared memory; out-of-line helpers rebuild their Cta view from it
+extern __shared__ __align__(1024) uint8_t dsmem[];
+
+__device__ __forceinline__ Cta make_cta(uint8_t *smem = dsmem) {
     Cta S;
     S.ring = smem + SmemMap::ring;
     S.limbs = reinterpret_cast<int8_t *>(smem + SmemMap::limbs);
@@ -84,11 +88,12 @@ __device__ __forceinline__ Cta make_cta(uint8_t *smem) {
     float *m = reinterpret_cast<float *>(smem + SmemMap::misc);
     S.red = m;
     S.qf = m + 64;
-    S.sc = m + 128;
-    S.accp = m + 192;
-    S.qkvw = reinterpret_cast<uint32_t *>(m + 448);
-    S.flag = reinterpret_cast<int *>(m + 544);
-    S.pt = reinterpret_cast<int *>(m + 576);
+    S.sc = m + 128;                                   // [kGroupPages][64]
+    S.accp = S.sc + 64 * kGroupPages;                 // [kGroupPages][4][64]
+    S.qkvw = reinterpret_cast<uint32_t *>(S.accp + 256 * kGroupPages);
+    S.flag = reinterpret_cast<int *>(S.qkvw + 96);
+    S.pt = S.flag + 32;
+    S.pst = reinterpret_cast<float *>(S.pt + kMaxPages);
     S.full = reinterpret_cast<uint64_t *>(smem + SmemMap::bars);
     S.empty = S.full + kStages;
     S.tid = threadIdx.x;
@@ -139,13 +144,16 @@ __device__ __forceinline__ void wait_full(const DecodeParams &p, Cta &S, int slo
 }
 
 // Poll n flag-tagged words [src, src+n) until they all carry `epoch`; store their data to
-// dst.  Only as many warps as needed poll (16 words in flight per lane), with a short sleep
-// between rounds: 148 CTAs spinning with every thread on the same few L2 lines saturate the
-// L2 slices that hold them.  The caller follows with a consumer barrier.
-__device__ __forceinline__ void ll_gather(const DecodeParams &p, Cta &S, const uint64_t *src, uint32_t *dst,
-                          int n, uint32_t epoch, uint32_t where) {
-    constexpr int B = 16;
-    const int nw = min(kConsumerWarps, (n + 32 * B - 1) / (32 * B));
+// dst.  The words are spread over the warps in units of 4 per lane (at most 8 in flight
+// per lane), and a lane re-polls only its words still missing, with a short sleep between
+// rounds: 148 CTAs spinning on the same few L2 lines would otherwise saturate the L2 slices
+// that hold them.  The caller follows with a consumer barrier.
+// (out of line: one copy of the code, called by every phase, stays in the instruction cache)
+__device__ __forceinline__ void ll_gather_impl(RunState *state, uint64_t timeout_ns, const uint64_t *src,
+                                            uint32_t *dst, int n, uint32_t epoch, uint32_t where) {
+    Cta S = make_cta();
+    constexpr int B = 8;
+    const int nw = min(kConsumerWarps, (n + 32 * 4 - 1) / (32 * 4));
     if (S.warp >= nw) return;
     const int stride = nw * 32;
     for (int base = 0; base < n; base += B * stride) {
@@ -168,7 +176,7 @@ __device__ __forceinline__ void ll_gather(const DecodeParams &p, Cta &S, const u
                 const int i = base + S.tid + j * stride;
                 if (i < n && static_cast<uint32_t>(v[j] >> 32) != epoch) v[j] = ll_load(src + i);
             }
-            if ((++it & 63) == 0 && wait_expired(p, S.flag, t0, ERR_TIMEOUT_FLAG, where)) break;
+            if ((++it & 63) == 0 && wait_expired_st(state, timeout_ns, S.flag, &t0, ERR_TIMEOUT_FLAG, where)) break;
         }
 #pragma unroll
         for (int j = 0; j < B; j++) {
@@ -177,6 +185,8 @@ __device__ __forceinline__ void ll_gather(const DecodeParams &p, Cta &S, const u
         }
     }
 }
+#define ll_gather(p, S, src, dst, n, epoch, where) \
+    ll_gather_impl((p).state, (p).timeout_ns, (src), (dst), (n), (epoch), (where))
 
 // uniform "should this CTA stop" decision among the consumer threads (shared flag only)
 __device__ __forceinline__ bool abort_check(Cta &S) {
@@ -219,10 +229,15 @@ __device__ __forceinline__ float warp_sum(float v) {
     for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+// max is order-free, so the single-instruction warp reductions give the butterfly's value
 __device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
+    float r;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    return r;
+}
+// max of non-negative floats: their bit patterns order like unsigned integers
+__device__ __forceinline__ float warp_max_nonneg(float v) {
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
 }
 
 // 22-bit fixed-point exponent for a vector whose max |x| is m: X = rint(x * 2^s), |X| < 2^22
@@ -250,8 +265,9 @@ __device__ __forceinline__ void put_limbs(int8_t *limbs, int kb, int lane, float
 // warp totals in warp order (the CPU oracle replays exactly this tree).  Three consumer
 // barriers; returns the fixed-point exponent s.  The caller ends with a consumer barrier.
 template <int D>
-__device__ __forceinline__ int resid_ln_limbs(Cta &S, const float *xo, float *xn, const uint32_t *add,
-                                              const float *g, const float *b, float eps) {
+__device__ __forceinline__ int resid_ln_limbs_impl(const float *xo, float *xn, const uint32_t *add,
+                                               const float *g, const float *b, float eps) {
+    Cta S = make_cta();
     constexpr int PER = D / kConsumerThreads;
     static_assert(D % kConsumerThreads == 0, "d_model must be a multiple of 256");
     float xv[PER];
@@ -293,7 +309,7 @@ __device__ __forceinline__ int resid_ln_limbs(Cta &S, const float *xo, float *xn
         xv[j] = bf16r(__fadd_rn(__fmul_rn(t, g[i]), b[i]));
         m = fmaxf(m, fabsf(xv[j]));
     }
-    m = warp_max(m);
+    m = warp_max_nonneg(m);
     if (S.lane == 0) S.red[16 + S.warp] = m;
     cbar();
 #pragma unroll
@@ -303,6 +319,12 @@ __device__ __forceinline__ int resid_ln_limbs(Cta &S, const float *xo, float *xn
 #pragma unroll
     for (int j = 0; j < PER; j++) put_limbs(S.limbs, S.warp + 8 * j, S.lane, xv[j], sc);
     return s;
+}
+
+template <int D>
+__device__ __forceinline__ int resid_ln_limbs(Cta &, const float *xo, float *xn, const uint32_t *add,
+                                              const float *g, const float *b, float eps) {
+    return resid_ln_limbs_impl<D>(xo, xn, add, g, b, eps);
 }
 
 // Limbs of a length-K vector already in shared memory (bf16 or f32), same ownership as
@@ -318,7 +340,7 @@ __device__ __forceinline__ int limbs_of(Cta &S, Load ld) {
         v[j] = ld(32 * (S.warp + 8 * j) + S.lane);
         m = fmaxf(m, fabsf(v[j]));
     }
-    m = warp_max(m);
+    m = warp_max_nonneg(m);
     if (S.lane == 0) S.red[24 + S.warp] = m;
     cbar();
 #pragma unroll
@@ -330,14 +352,15 @@ __device__ __forceinline__ int limbs_of(Cta &S, Load ld) {
     return s;
 }
 
-// One weight chunk: rows (multiple of 8) x K int8 (row r swizzled by r & 3) followed by
-// rows x (f32 scale, f32 bias).  Warps split K; their int32 limb partials meet in S.part
-// (double buffered by `pb`, so one barrier per chunk suffices); then each output
-// y = float(exact dot) * 2^-s * scale + bias goes to epi(row, y) -- or, with PAIR, rows
-// 2j and 2j+1 go together to epi(2j, y0, y1) from one thread.
-template <bool PAIR, class Epi>
-__device__ __forceinline__ void gemv_chunk(Cta &S, const uint8_t *stage, int rows, int K, int s, int pb,
-                                           Epi epi) {
+// limbs of the bf16 vector in S.act[0..K) (out of line)
+template <int K>
+__device__ __forceinline__ int limbs_of_act() {
+    Cta S = make_cta();
+    return limbs_of<K>(S, [&](int i) { return __uint_as_float((uint32_t)S.act[i] << 16); });
+}
+
+__device__ __forceinline__ void gemv_partials(const uint8_t *stage, int rows, int K, int pb) {
+    Cta S = make_cta();
     const int g = S.lane >> 2, tig = S.lane & 3;
     const int ntiles = rows >> 3;
     const int KS = K >> 5;
@@ -370,26 +393,40 @@ __device__ __forceinline__ void gemv_chunk(Cta &S, const uint8_t *stage, int row
             }
         }
     }
-    cbar();
+}
+
+// output row r of a chunk: float(exact dot) * 2^-s * scale + bias
+__device__ __forceinline__ float gemv_row(const uint8_t *stage, int rows, int K, int s, int pb, int r) {
+    const int *part = reinterpret_cast<const int *>(dsmem + SmemMap::part) + pb * SmemMap::part_ints;
     const float *meta = reinterpret_cast<const float *>(stage + (size_t)rows * K);
-    const float down = exp2i(-s);
-    auto row = [&](int r) {
-        const int t = r >> 3, col = r & 7;
-        long long A = 0, B = 0, C = 0;
+    const int t = r >> 3, col = r & 7;
+    long long A = 0, B = 0, C = 0;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; w++) {
-            const int *pp = part + ((w * kMaxTilesPerChunk + t) * 3) * 8 + col;
-            A += pp[0];
-            B += pp[8];
-            C += pp[16];
-        }
-        const float y = __fmul_rn(__ll2float_rn(A * 65536 + B * 256 + C), down);
-        return __fadd_rn(__fmul_rn(y, meta[2 * r]), meta[2 * r + 1]);
-    };
+    for (int w = 0; w < kConsumerWarps; w++) {
+        const int *pp = part + ((w * kMaxTilesPerChunk + t) * 3) * 8 + col;
+        A += pp[0];
+        B += pp[8];
+        C += pp[16];
+    }
+    const float y = __fmul_rn(__ll2float_rn(A * 65536 + B * 256 + C), exp2i(-s));
+    return __fadd_rn(__fmul_rn(y, meta[2 * r]), meta[2 * r + 1]);
+}
+
+// One weight chunk: rows (multiple of 8) x K int8 (row r swizzled by r & 3) followed by
+// rows x (f32 scale, f32 bias).  Warps split K; their int32 limb partials meet in S.part
+// (double buffered by `pb`, so one barrier per chunk suffices); then each output
+// y = float(exact dot) * 2^-s * scale + bias goes to epi(row, y) -- or, with PAIR, rows
+// 2j and 2j+1 go together to epi(2j, y0, y1) from one thread.
+template <bool PAIR, class Epi>
+__device__ __forceinline__ void gemv_chunk(Cta &S, const uint8_t *stage, int rows, int K, int s, int pb,
+                                           Epi epi) {
+    gemv_partials(stage, rows, K, pb);
+    cbar();
     if (PAIR) {
-        if (S.tid < (rows >> 1)) epi(2 * S.tid, row(2 * S.tid), row(2 * S.tid + 1));
+        if (S.tid < (rows >> 1))
+            epi(2 * S.tid, gemv_row(stage, rows, K, s, pb, 2 * S.tid), gemv_row(stage, rows, K, s, pb, 2 * S.tid + 1));
     } else {
-        if (S.tid < rows) epi(S.tid, row(S.tid), 0.0f);
+        if (S.tid < rows) epi(S.tid, gemv_row(stage, rows, K, s, pb, S.tid), 0.0f);
     }
 }
 
@@ -419,35 +456,41 @@ __device__ __forceinline__ size_t kv_index(const DecodeParams &p, int layer, int
            (size_t)row * kHeadDim;
 }
 
-// cp.async the cached rows [page*64, min(pos, page*64+64)) of (layer, head) into kvbuf.
+// cp.async the cached rows [j0, min(pos, j0 + 64 * kGroupPages)) of (layer, head) into
+// kvbuf, j0 = first position of the item's page group.
 __device__ __forceinline__ void kv_prefetch(const DecodeParams &p, Cta &S, int layer, int item, int pos) {
     const int H = p.n_heads;
-    const int pg = item / H, h = item % H;
-    const int j0 = pg * kPageTokens;
-    const int nrows = min(pos, j0 + kPageTokens) - j0;   // cached rows (current pos excluded)
-    if (nrows <= 0) return;
-    const int phys = S.pt[pg];
-    const uint16_t *srcK = p.kv + kv_index(p, layer, phys, 0, h, 0);
-    const uint16_t *srcV = p.kv + kv_index(p, layer, phys, 1, h, 0);
+    const int grp = item / H, h = item % H;
+    const int j0 = grp * kGroupPages * kPageTokens;
+    const int nrows = min(pos, j0 + kGroupPages * kPageTokens) - j0;   // cached rows (current pos excluded)
     for (int c = S.tid; c < nrows * 16; c += kConsumerThreads) {
         const int row = c >> 4, kv = (c >> 3) & 1, part = c & 7;
-        const uint16_t *src = (kv ? srcV : srcK) + row * kHeadDim + part * 8;
-        uint16_t *dst = S.kvbuf + kv * kPageTokens * kHeadDim + row * kHeadDim + part * 8;
+        const int pl = row / kPageTokens, r = row % kPageTokens;
+        const int phys = S.pt[grp * kGroupPages + pl];
+        const uint16_t *src = p.kv + kv_index(p, layer, phys, kv, h, r) + part * 8;
+        // K rows keep their 16-byte chunk c at c ^ (row & 7): the score loop reads one row per
+        // lane, and the swizzle spreads a quarter-warp's reads over all banks
+        const int pc = kv ? part : part ^ (r & 7);
+        uint16_t *dst = S.kvbuf + ((pl * 2 + kv) * kPageTokens + r) * kHeadDim + pc * 8;
         cp_async16(dst, src);
     }
     cp_async_commit();
 }
 
-// One (page, head) item of single-query attention (mha_tile, mha_decode.cc:90-168, in its
-// split form): scores of the page's keys against q (already * 1/sqrt(64) and bf16), the page
-// max m, l = sum exp(s - m), acc = sum exp(s - m) v.  Publishes [m, l, acc[64]].
+// One (page group, head) item of single-query attention (mha_tile, mha_decode.cc:90-168, in
+// its split form).  Per page of the group: scores of the page's keys against q (already
+// * 1/sqrt(64) and bf16), the page max m, l = sum exp(s - m), acc = sum exp(s - m) v; the
+// page partials are then merged in page order (flash-decode merge).  With one group in the
+// context (`single`) the item publishes ctx = bf16(acc / l) of its head as 32 words at
+// ll_att[h*32..]; otherwise it publishes the group partial [m, l, acc[64]] at ll_att[item*66].
 __device__ __forceinline__ void att_item(const DecodeParams &p, Cta &S, int layer, int item, int pos,
-                         bool prefetched, uint32_t ep_qkv, uint32_t ep_att) {
+                         bool prefetched, bool single, uint32_t ep_qkv, uint32_t ep_att, int t) {
     const int H = p.n_heads, D = p.d_model;
-    const int pg = item / H, h = item % H;
-    const int j0 = pg * kPageTokens;
-    const int nk = min(pos + 1, j0 + kPageTokens) - j0;
-    const bool has_cur = pos < j0 + kPageTokens;
+    const int grp = item / H, h = item % H;
+    const int j0 = grp * kGroupPages * kPageTokens;
+    const int ntok = min(pos + 1, j0 + kGroupPages * kPageTokens) - j0;   // keys, current included
+    const int np = (ntok + kPageTokens - 1) / kPageTokens;
+    const bool has_cur = pos < j0 + kGroupPages * kPageTokens;
     if (!prefetched) kv_prefetch(p, S, layer, item, pos);
     // q, k, v of head h: words [part*D/2 + h*32, +32)
     if (S.tid < 96) {
@@ -463,9 +506,10 @@ __device__ __forceinline__ void att_item(const DecodeParams &p, Cta &S, int laye
         }
         S.qkvw[S.tid] = static_cast<uint32_t>(v);
     }
+    if (layer == 1) stamp(p, S, t, 86);
     cp_async_wait_all();
     cbar();
-    if (layer == 1) stamp(p, S, 0, 80);
+    if (layer == 1) stamp(p, S, t, 80);
     if (S.tid < 32) {
         uint32_t w = S.qkvw[S.tid];
         S.qf[2 * S.tid] = bf16lo(w);
@@ -474,63 +518,132 @@ __device__ __forceinline__ void att_item(const DecodeParams &p, Cta &S, int laye
     if (has_cur && S.tid >= 32 && S.tid < 96) {
         // append this position's K (tid 32..63) or V (tid 64..95) row: kvbuf and the cache
         const int kv = (S.tid - 32) >> 5, wi = S.tid & 31, row = pos - j0;
+        const int pl = row / kPageTokens, r = row % kPageTokens;
         const uint32_t w = S.qkvw[S.tid];
-        reinterpret_cast<uint32_t *>(S.kvbuf + kv * kPageTokens * kHeadDim + row * kHeadDim)[wi] = w;
-        const int phys = S.pt[pg];
-        reinterpret_cast<uint32_t *>(p.kv + kv_index(p, layer, phys, kv, h, row))[wi] = w;
+        const int swi = kv ? wi : (wi ^ ((r & 7) << 2));    // K: chunk (wi / 4) ^ (row & 7)
+        reinterpret_cast<uint32_t *>(S.kvbuf + ((pl * 2 + kv) * kPageTokens + r) * kHeadDim)[swi] = w;
+        const int phys = S.pt[grp * kGroupPages + pl];
+        reinterpret_cast<uint32_t *>(p.kv + kv_index(p, layer, phys, kv, h, r))[wi] = w;
     }
     cbar();
-    // scores: warp w -> keys 8w..8w+7, 4 lanes per key, 16 dims per lane
-    {
-        const int key = S.warp * 8 + (S.lane >> 2), d0 = (S.lane & 3) * 16;
-        float sd = 0.0f;
+    // scores: one key per thread (thread k -> page k / 64, key k % 64), four chains of 16
+    // dims (d ascending) combined as (s0 + s1) + (s2 + s3)
+    if (S.tid < np * kPageTokens) {
+        const int pl = S.tid / kPageTokens, key = S.tid % kPageTokens;
+        const int nk = min(kPageTokens, ntok - pl * kPageTokens);
+        float sd = -INFINITY;
         if (key < nk) {
-            const uint16_t *kr = S.kvbuf + key * kHeadDim + d0;
+            const uint4 *kr = reinterpret_cast<const uint4 *>(S.kvbuf + ((pl * 2) * kPageTokens + key) * kHeadDim);
+            const float4 *q4p = reinterpret_cast<const float4 *>(S.qf);
+            float s4[4];
 #pragma unroll
-            for (int d = 0; d < 16; d++) sd = fmaf(S.qf[d0 + d], __uint_as_float((uint32_t)kr[d] << 16), sd);
+            for (int q4 = 0; q4 < 4; q4++) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int half = 0; half < 2; half++) {
+                    const int c = 2 * q4 + half;
+                    const uint4 kv8 = kr[c ^ (key & 7)];
+                    const float4 qa = q4p[2 * c], qb = q4p[2 * c + 1];
+                    acc = fmaf(qa.x, bf16lo(kv8.x), acc);
+                    acc = fmaf(qa.y, bf16hi(kv8.x), acc);
+                    acc = fmaf(qa.z, bf16lo(kv8.y), acc);
+                    acc = fmaf(qa.w, bf16hi(kv8.y), acc);
+                    acc = fmaf(qb.x, bf16lo(kv8.z), acc);
+                    acc = fmaf(qb.y, bf16hi(kv8.z), acc);
+                    acc = fmaf(qb.z, bf16lo(kv8.w), acc);
+                    acc = fmaf(qb.w, bf16hi(kv8.w), acc);
+                }
+                s4[q4] = acc;
+            }
+            sd = __fadd_rn(__fadd_rn(s4[0], s4[1]), __fadd_rn(s4[2], s4[3]));
         }
-        sd += __shfl_xor_sync(0xffffffffu, sd, 1);
-        sd += __shfl_xor_sync(0xffffffffu, sd, 2);
-        if ((S.lane & 3) == 0) S.sc[key] = key < nk ? sd : -INFINITY;
+        S.sc[pl * 64 + key] = sd;
     }
     cbar();
-    float m = warp_max(fmaxf(S.sc[S.lane], S.sc[S.lane + 32]));
-    float p0 = S.lane < nk ? fast_exp_nonpos(__fsub_rn(S.sc[S.lane], m)) : 0.0f;
-    float p1 = S.lane + 32 < nk ? fast_exp_nonpos(__fsub_rn(S.sc[S.lane + 32], m)) : 0.0f;
-    float l = warp_sum(p0 + p1);
-    cbar();                      // everyone has read the scores
-    if (S.warp == 0) { S.sc[S.lane] = p0; S.sc[S.lane + 32] = p1; }
+    if (layer == 1) stamp(p, S, t, 84);
+    // page statistics: warp pl owns page pl; probabilities replace the scores in place
+    if (S.warp < np) {
+        const int pl = S.warp;
+        const int nk = min(kPageTokens, ntok - pl * kPageTokens);
+        float *sc = S.sc + pl * 64;
+        const float s0 = sc[S.lane], s1 = sc[S.lane + 32];
+        const float m = warp_max(fmaxf(s0, s1));
+        const float p0 = S.lane < nk ? fast_exp_nonpos(__fsub_rn(s0, m)) : 0.0f;
+        const float p1 = S.lane + 32 < nk ? fast_exp_nonpos(__fsub_rn(s1, m)) : 0.0f;
+        const float l = warp_sum(p0 + p1);
+        __syncwarp();
+        sc[S.lane] = p0;
+        sc[S.lane + 32] = p1;
+        if (S.lane == 0) { S.pst[2 * pl] = m; S.pst[2 * pl + 1] = l; }
+    }
     cbar();
+    if (layer == 1) stamp(p, S, t, 85);
+    // P.V: thread (d, q4) runs the chains over keys q4*16 .. q4*16+15 of every page (j ascending)
     {
         const int d = S.tid & 63, q4 = S.tid >> 6;
-        float a = 0.0f;
-        const uint16_t *vb = S.kvbuf + kPageTokens * kHeadDim;
-        for (int j = q4 * 16; j < q4 * 16 + 16 && j < nk; j++)
-            a = fmaf(S.sc[j], __uint_as_float((uint32_t)vb[j * kHeadDim + d] << 16), a);
-        S.accp[q4 * 64 + d] = a;
+        float a[kGroupPages];
+        int nkp[kGroupPages];
+#pragma unroll
+        for (int pl = 0; pl < kGroupPages; pl++) {
+            a[pl] = 0.0f;
+            nkp[pl] = pl < np ? min(kPageTokens, ntok - pl * kPageTokens) : 0;
+        }
+#pragma unroll 4
+        for (int jj = 0; jj < 16; jj++) {
+            const int j = q4 * 16 + jj;
+#pragma unroll
+            for (int pl = 0; pl < kGroupPages; pl++) {
+                if (j < nkp[pl]) {
+                    const uint16_t v = S.kvbuf[((pl * 2 + 1) * kPageTokens + j) * kHeadDim + d];
+                    a[pl] = fmaf(S.sc[pl * 64 + j], __uint_as_float((uint32_t)v << 16), a[pl]);
+                }
+            }
+        }
+#pragma unroll
+        for (int pl = 0; pl < kGroupPages; pl++)
+            if (pl < np) S.accp[(pl * 4 + q4) * 64 + d] = a[pl];
     }
     cbar();
-    if (layer == 1) stamp(p, S, 0, 81);
-    uint64_t *dst = p.ll_att + (size_t)item * (2 + kHeadDim);
+    if (layer == 1) stamp(p, S, t, 81);
     if (S.tid < 64) {
-        float a = S.accp[S.tid] + S.accp[64 + S.tid] + S.accp[128 + S.tid] + S.accp[192 + S.tid];
-        ll_store(dst + 2 + S.tid, __float_as_uint(a), ep_att);
-    } else if (S.tid == 64) {
-        ll_store(dst, __float_as_uint(m), ep_att);
-    } else if (S.tid == 65) {
-        ll_store(dst + 1, __float_as_uint(l), ep_att);
+        float M = -INFINITY, L = 0.0f, A = 0.0f;
+        for (int pl = 0; pl < np; pl++) {
+            const float *ap = S.accp + pl * 256 + S.tid;
+            const float a = __fadd_rn(__fadd_rn(__fadd_rn(ap[0], ap[64]), ap[128]), ap[192]);
+            const float mp = S.pst[2 * pl], lp = S.pst[2 * pl + 1];
+            const float mn = fmaxf(M, mp);
+            const float c0 = fast_exp_nonpos(__fsub_rn(M, mn));
+            const float c1 = fast_exp_nonpos(__fsub_rn(mp, mn));
+            L = __fadd_rn(__fmul_rn(L, c0), __fmul_rn(lp, c1));
+            A = __fadd_rn(__fmul_rn(A, c0), __fmul_rn(a, c1));
+            M = mn;
+        }
+        if (single) {
+            const float ctx = __fdiv_rn(A, L);
+            const uint32_t mine = bf16bits(ctx);
+            const uint32_t hi = __shfl_down_sync(0xffffffffu, mine, 1);
+            if ((S.tid & 1) == 0) ll_store(p.ll_att + h * 32 + (S.tid >> 1), mine | (hi << 16), ep_att);
+        } else {
+            uint64_t *dst = p.ll_att + (size_t)item * (2 + kHeadDim);
+            ll_store(dst + 2 + S.tid, __float_as_uint(A), ep_att);
+            if (S.tid == 0) ll_store(dst, __float_as_uint(M), ep_att);
+            if (S.tid == 1) ll_store(dst + 1, __float_as_uint(L), ep_att);
+        }
     }
-    cbar();
+    // no trailing barrier: what follows writes none of sc / accp / pst before its own barrier
 }
 
-// Combine the page partials of every head (flash-decode merge, in page order) into
+// n_groups page groups cover positions [0, pos]
+__device__ __forceinline__ int att_groups(int pos) { return pos / (kGroupPages * kPageTokens) + 1; }
+
+// Combine the group partials of every head (flash-decode merge, in group order) into
 // ctx = bf16(acc / l) in S.act[0..D).  Partials are staged through kvbuf in batches of whole
 // items.  The caller ends with a consumer barrier.
 __device__ __forceinline__ void att_combine(const DecodeParams &p, Cta &S, int pos, uint32_t ep_att, int layer) {
     const int H = p.n_heads, D = p.d_model;
-    const int n_items = (pos / kPageTokens + 1) * H;
+    const int n_items = att_groups(pos) * H;
     constexpr int W = 2 + kHeadDim;
-    const int per_batch = (2 * kPageTokens * kHeadDim * 2 / 4) / W;   // items per kvbuf load
+    const int per_batch = (SmemMap::kvbuf_bytes / 4) / W;   // items per kvbuf load
     float M[4], L[4], A[4];
 #pragma unroll
     for (int k = 0; k < 4; k++) { M[k] = -INFINITY; L[k] = 0.0f; A[k] = 0.0f; }
@@ -660,15 +773,20 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
         float *xcur = S.xs;                  // x lives in xs[0..D) or xs[kDmax..kDmax+D)
         for (int i = S.tid; i < D; i += kConsumerThreads)
             xcur[i] = __fadd_rn(p.emb_tok[(size_t)id * D + i], p.emb_pos[(size_t)(pos + 2) * D + i]);
-        const int n_items = (pos / kPageTokens + 1) * H;
+        const int n_items = att_groups(pos) * H;
+        const bool single = n_items == H;
 
         for (int l = 0; l < L; l++) {
             const uint32_t ep = ep0 + (uint32_t)(l * kPhasesPerLayer);
             const float *ln = p.ln + (size_t)l * 4 * D;
+            // cp.async groups, oldest first: LN1 params (issued one phase group earlier),
+            // LN2 params, this CTA's KV pages (always committed, possibly empty)
+            ln_prefetch(S, 1, ln + 2 * D, ln + 3 * D, D);
             if (c < n_items) kv_prefetch(p, S, l, c, pos);
+            else cp_async_commit();
             // ---------------- QKV: x += fc2(prev layer); LN1; q, k, v rows
             if (l > 0) ll_gather(p, S, p.ll_f2, actw, D, ep - kPhasesPerLayer + PH_FC2, 0x10u + l);
-            cp_async_wait_all();
+            cp_async_wait_group<2>();          // LN1 params in; LN2 and KV may still be in flight
             cbar();
             if (l == 1) stamp(p, S, t, 70);
             if (*(volatile int *)S.flag) return;
@@ -678,7 +796,6 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             cbar();
             if (l == 1) stamp(p, S, t, 71);
             if (l > 0) trace_x(p, S, t, 2 * (l - 1) + 1, xcur);
-            ln_prefetch(S, 1, ln + 2 * D, ln + 3 * D, D);
             gemv_phase<true>(p, S, ctr, q_rows, D, s, 0x20u + l, [&](int r, float y0, float y1) {
                 const int n = q_row0 + r;
                 if (n < D) { y0 = __fmul_rn(y0, 0.125f); y1 = __fmul_rn(y1, 0.125f); }
@@ -688,14 +805,18 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             if (l == 1) stamp(p, S, t, 72);
             // ---------------- ATT: this CTA's (page, head) items
             for (int it = c, k = 0; it < n_items; it += G, k++)
-                att_item(p, S, l, it, pos, k == 0, ep + PH_QKV, ep + PH_ATT);
+                att_item(p, S, l, it, pos, k == 0, single, ep + PH_QKV, ep + PH_ATT, t);
             stamp(p, S, t, 1 + 5 * l + PH_ATT);
+            // LN1 of the next layer (or the final LN) into buffer 0, read by nothing until then
+            if (l + 1 < L) ln_prefetch(S, 0, ln + 4 * D, ln + 5 * D, D);
+            else ln_prefetch(S, 0, p.lnf, p.lnf + D, D);
             // ---------------- O: merge partials -> ctx; O rows
             if (o_rows > 0) {
-                att_combine(p, S, pos, ep + PH_ATT, l);
+                if (single) ll_gather(p, S, p.ll_att, actw, D / 2, ep + PH_ATT, 0x300u + l);
+                else att_combine(p, S, pos, ep + PH_ATT, l);
                 cbar();
                 if (l == 1) stamp(p, S, t, 82);
-                s = limbs_of<D>(S, [&](int i) { return __uint_as_float((uint32_t)S.act[i] << 16); });
+                s = limbs_of_act<D>();
                 cbar();
                 if (l == 1) stamp(p, S, t, 83);
                 gemv_phase<false>(p, S, ctr, o_rows, D, s, 0x30u + l, [&](int r, float y, float) {
@@ -706,7 +827,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             // ---------------- FC1: x += o; LN2; relu(fc1) -> bf16
             if (l == 1) stamp(p, S, t, 63);
             ll_gather(p, S, p.ll_o, actw, D, ep + PH_O, 0x40u + l);
-            cp_async_wait_all();
+            cp_async_wait_group<1>();          // LN2 params in; the next LN1 may still be in flight
             cbar();
             if (l == 1) stamp(p, S, t, 64);
             if (*(volatile int *)S.flag) return;
@@ -716,8 +837,6 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             cbar();
             if (l == 1) stamp(p, S, t, 65);
             trace_x(p, S, t, 2 * l, xcur);
-            if (l + 1 < L) ln_prefetch(S, 0, ln + 4 * D, ln + 5 * D, D);
-            else ln_prefetch(S, 0, p.lnf, p.lnf + D, D);
             gemv_phase<true>(p, S, ctr, f1_rows, D, s, 0x50u + l, [&](int r, float y0, float y1) {
                 y0 = fmaxf(y0, 0.0f);
                 y1 = fmaxf(y1, 0.0f);
@@ -730,7 +849,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 ll_gather(p, S, p.ll_h, actw, F / 2, ep + PH_FC1, 0x60u + l);
                 cbar();
                 if (l == 1) stamp(p, S, t, 67);
-                s = limbs_of<F>(S, [&](int i) { return __uint_as_float((uint32_t)S.act[i] << 16); });
+                s = limbs_of_act<F>();
                 cbar();
                 if (l == 1) stamp(p, S, t, 68);
                 gemv_phase<false>(p, S, ctr, f2_rows, F, s, 0x70u + l, [&](int r, float y, float) {
@@ -808,8 +927,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
 
 template <int D, int F>
 __global__ void __launch_bounds__(kThreads, 1) opt_decode_kernel(const DecodeParams p) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    Cta S = make_cta(smem);
+    Cta S = make_cta();
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; i++) {
             mbar_init(&S.full[i], 1);
@@ -830,8 +948,7 @@ __global__ void __launch_bounds__(kThreads, 1) opt_decode_kernel(const DecodePar
 // the decode kernel's limb and MMA code (for parity tests and the op-level C ABI).
 __global__ void __launch_bounds__(kThreads, 1)
 gemv_i8_kernel(const float *x, int K, const uint8_t *packed, const ChunkRef *chunks, int N, float *y) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    Cta S = make_cta(smem);
+    Cta S = make_cta();
     const int rpc = rows_per_chunk(K);
     const int row0 = blockIdx.x * rpc;
     const int rows = min(rpc, N - row0);

@@ -62,6 +62,8 @@ __device__ __forceinline__ void cp_async16(void *dst_smem, const void *src) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // ---- flag-tagged words: low 32 bits data, high 32 bits epoch; one 64-bit access -----
 __device__ __forceinline__ void ll_store(uint64_t *p, uint32_t data, uint32_t epoch) {
