@@ -175,6 +175,35 @@ typedef struct {
 int or_whisper_encode(const or_whisper_enc_cfg *c, const or_whisper_enc_weights *w, const float *mel,
                       int B, float *out, int nthreads);
 
+/* ---- Parakeet FastConformer encoder (rust/npu-parakeet/src/encoder.rs, ops.rs, pos.rs) ---- */
+typedef struct {
+    int n_layers, d_model, n_heads, ffn, n_mels, n_frames, sub_ch, kconv;
+    int int8;   /* 1: the int8 GEMM engine rule for every weight linear; 0: f32 host path */
+} or_parakeet_cfg;
+typedef struct {
+    const float *ff1_ln_w, *ff1_ln_b, *ff1_w1, *ff1_w2;             /* w1 [D, F], w2 [F, D] ([in, out]) */
+    const float *att_ln_w, *att_ln_b, *wq, *wk, *wv, *wpos, *wout;  /* [D, D] */
+    const float *pos_u, *pos_v;                                     /* [H, dk] */
+    const float *conv_ln_w, *conv_ln_b, *pw1, *dw_w, *dw_b, *pw2;   /* pw1 [D, 2D], dw_w [D, k], pw2 [D, D] */
+    const float *ff2_ln_w, *ff2_ln_b, *ff2_w1, *ff2_w2;
+    const float *out_ln_w, *out_ln_b;
+} or_parakeet_layer;
+typedef struct {
+    const float *c0_w, *c0_b, *c2_w, *c2_b, *c3_w, *c3_b, *c5_w, *c5_b, *c6_w, *c6_b;  /* conv [Co, Ci/g, kh, kw] */
+    const float *out_w, *out_b;                                     /* [C * F/8, D], [D] */
+    const or_parakeet_layer *layers;
+} or_parakeet_weights;
+/* mel [B][n_mels][n_frames] -> out [B][T'][d_model], T' = n_frames subsampled 8x */
+int or_parakeet_encode(const or_parakeet_cfg *c, const or_parakeet_weights *w, const float *mel, int B,
+                       float *out, int nthreads);
+void or_parakeet_quant_lin(const float *x, int T, int K, const float *w, const float *bias, int N, float *y,
+                           int nthreads);
+void or_conv2d(const float *x, int ci, int hin, int win, const float *w, const float *b, int co, int kh, int kw,
+               int stride, int pad, int groups, float *y, int nthreads);
+void or_dwconv1d(const float *x, int C, int T, const float *taps, const float *bias, int k, float *y);
+void or_rel_shift(const float *bd, int H, int T, float *out);
+void or_rel_pos_encoding(int T, int D, float *pe);
+
 #ifdef __cplusplus
 }
 #endif

@@ -78,6 +78,13 @@ def lib():
         L.or_bert_embed.restype = C.c_int
         L.or_whisper_encode.argtypes = [C.c_void_p, C.c_void_p, F32P, C.c_int, F32P, C.c_int]
         L.or_whisper_encode.restype = C.c_int
+        L.or_parakeet_encode.argtypes = [C.c_void_p, C.c_void_p, F32P, C.c_int, F32P, C.c_int]
+        L.or_parakeet_quant_lin.argtypes = [F32P, C.c_int, C.c_int, F32P, C.c_void_p, C.c_int, F32P, C.c_int]
+        L.or_conv2d.argtypes = [F32P, C.c_int, C.c_int, C.c_int, F32P, F32P, C.c_int, C.c_int, C.c_int,
+                                C.c_int, C.c_int, C.c_int, F32P, C.c_int]
+        L.or_dwconv1d.argtypes = [F32P, C.c_int, C.c_int, F32P, F32P, C.c_int, F32P]
+        L.or_rel_shift.argtypes = [F32P, C.c_int, C.c_int, F32P]
+        L.or_rel_pos_encoding.argtypes = [C.c_int, C.c_int, F32P]
         L.or_opt_step.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_void_p]
         L.or_opt_step.restype = C.c_int64
         L.or_opt_qweight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.POINTER(C.c_float))]
@@ -355,3 +362,91 @@ def whisper_encode(cfg, w, mel, nthreads=None):
     lib().or_whisper_encode(C.addressof(c), C.addressof(ww), mel.ravel(), B, out.ravel(),
                             nthreads or os.cpu_count() or 1)
     return out
+
+
+# ---------------------------------------------------------------- Parakeet FastConformer encoder
+_PK_LAYER = ("ff1_ln_w", "ff1_ln_b", "ff1_w1", "ff1_w2", "att_ln_w", "att_ln_b", "wq", "wk", "wv", "wpos",
+             "wout", "pos_u", "pos_v", "conv_ln_w", "conv_ln_b", "pw1", "dw_w", "dw_b", "pw2",
+             "ff2_ln_w", "ff2_ln_b", "ff2_w1", "ff2_w2", "out_ln_w", "out_ln_b")
+_PK_TOP = ("c0_w", "c0_b", "c2_w", "c2_b", "c3_w", "c3_b", "c5_w", "c5_b", "c6_w", "c6_b", "out_w", "out_b")
+
+
+class _PkCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d_model", "n_heads", "ffn", "n_mels", "n_frames", "sub_ch",
+                                       "kconv", "int8")]
+
+
+class _PkLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _PK_LAYER]
+
+
+class _PkWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _PK_TOP + ("layers",)]
+
+
+def parakeet_encode(cfg, w, mel, int8=True, nthreads=None):
+    """or_parakeet_encode: the reference's host encoder (int8 engine linears when int8)."""
+    keep = []
+
+    def p(a):
+        a = _f32(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    c = _PkCfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.ffn, cfg.n_mels, cfg.n_frames, cfg.sub_ch,
+               cfg.kconv, int(int8))
+    layers = (_PkLayer * cfg.n_layers)()
+    for i, ly in enumerate(w["layers"][:cfg.n_layers]):
+        for n in _PK_LAYER:
+            setattr(layers[i], n, p(ly[n]))
+    ww = _PkWeights(*[p(w[n]) for n in _PK_TOP], C.addressof(layers))
+    mel = _f32(mel)
+    B = mel.shape[0]
+    out = np.empty((B, cfg.frames_out, cfg.d_model), np.float32)
+    lib().or_parakeet_encode(C.addressof(c), C.addressof(ww), mel.ravel(), B, out.ravel(),
+                             nthreads or os.cpu_count() or 1)
+    return out
+
+
+def quant_lin(x, w, bias=None, nthreads=None):
+    """The int8 GEMM engine rule (ctx2.rs): y = (acc * s_a) * ws[n] (+ bias)."""
+    x, w = _f32(x), _f32(w)
+    T, K = x.shape
+    N = w.shape[1]
+    y = np.empty((T, N), np.float32)
+    b = _f32(bias) if bias is not None else None
+    lib().or_parakeet_quant_lin(x.ravel(), T, K, w.ravel(), b.ctypes.data if b is not None else None, N,
+                                y.ravel(), nthreads or os.cpu_count() or 1)
+    return y
+
+
+def conv2d(x, w, b, stride, pad, groups):
+    x, w, b = _f32(x), _f32(w), _f32(b)
+    ci, hin, win = x.shape
+    co, _, kh, kw = w.shape
+    ho, wo = (hin + 2 * pad - kh) // stride + 1, (win + 2 * pad - kw) // stride + 1
+    y = np.empty((co, ho, wo), np.float32)
+    lib().or_conv2d(x.ravel(), ci, hin, win, w.ravel(), b.ravel(), co, kh, kw, stride, pad, groups, y.ravel(), 1)
+    return y
+
+
+def dwconv1d(x, taps, bias):
+    x, taps, bias = _f32(x), _f32(taps), _f32(bias)
+    C_, T = x.shape
+    y = np.empty_like(x)
+    lib().or_dwconv1d(x.ravel(), C_, T, taps.ravel(), bias.ravel(), taps.shape[1], y.ravel())
+    return y
+
+
+def rel_shift(bd):
+    bd = _f32(bd)
+    H, T, _ = bd.shape
+    y = np.empty((H, T, T), np.float32)
+    lib().or_rel_shift(bd.ravel(), H, T, y.ravel())
+    return y
+
+
+def rel_pos_encoding(T, D):
+    pe = np.empty((2 * T - 1, D), np.float32)
+    lib().or_rel_pos_encoding(T, D, pe.ravel())
+    return pe

@@ -231,9 +231,57 @@ def whisper_hf_fixture():
     print("whisper_hf_golden.npz:", enc.shape)
 
 
+def _load_ref_module(rel, name):
+    spec = importlib.util.spec_from_file_location(name, os.path.join(REF, rel))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+PK_DW_CHANNELS = np.array([0, 1, 2, 3, 100, 255, 256, 511, 512, 700, 777, 900, 1000, 1021, 1022, 1023])
+
+
+def parakeet_fixture():
+    """Outputs of the reference's own Parakeet numpy goldens on seeded synthetic inputs:
+    rel_shift_host / rel_shift_strided (scripts/parakeet_relpos_mha_golden.py:59-75), the fp32
+    depthwise conv 'same' host_reference (route_b_kernels/dwconv1d/golden_dwconv1d_k9.py:40-48;
+    its module fixes C = 1024, T = 400, k = 9: 16 channels are stored, plus the f64 sum of all)
+    and conv2d_ref (route_b_kernels/subsample_conv2d/golden_subsample.py:58-79, f64)."""
+    rs = _load_ref_module("scripts/parakeet_relpos_mha_golden.py", "pk_relpos")
+    dwm = _load_ref_module("route_b_kernels/dwconv1d/golden_dwconv1d_k9.py", "pk_dw")
+    ssm = _load_ref_module("route_b_kernels/subsample_conv2d/golden_subsample.py", "pk_sub")
+    rng = np.random.default_rng(77)
+    out = {}
+    for T in (1, 2, 9, 31):
+        bd = rng.standard_normal((3, T, 2 * T - 1)).astype(np.float32)
+        out[f"bd_{T}"] = bd
+        out[f"shift_{T}"] = rs.rel_shift_host(bd)
+        assert np.array_equal(out[f"shift_{T}"], rs.rel_shift_strided(bd))
+    x = np.random.default_rng(78).standard_normal((dwm.C, dwm.T)).astype(np.float32)
+    dw = (np.random.default_rng(79).standard_normal((dwm.C, dwm.K)) / 3).astype(np.float32)
+    db = (np.random.default_rng(80).standard_normal(dwm.C) * 0.02).astype(np.float32)
+    y = dwm.host_reference(x, dw, db)
+    out["dw_out"] = y[PK_DW_CHANNELS]
+    out["dw_sum"] = np.array(np.sum(y.astype(np.float64)))
+    cases = [((2, 9, 10), (4, 2, 3, 3), 2, 1, 1), ((4, 9, 10), (4, 1, 3, 3), 2, 1, 4),
+             ((4, 5, 6), (3, 4, 1, 1), 1, 0, 1), ((1, 12, 8), (5, 1, 3, 3), 2, 1, 1)]
+    for i, (xs, ws, st, pd, g) in enumerate(cases):
+        xi = rng.standard_normal(xs).astype(np.float32)
+        wi = (rng.standard_normal(ws) * 0.3).astype(np.float32)
+        bi = (rng.standard_normal(ws[0]) * 0.1).astype(np.float32)
+        out[f"c2d_x{i}"], out[f"c2d_w{i}"], out[f"c2d_b{i}"] = xi, wi, bi
+        out[f"c2d_y{i}"] = ssm.conv2d_ref(xi.astype(np.float64), wi.astype(np.float64), bi.astype(np.float64),
+                                          st, pd, g)
+        out[f"c2d_meta{i}"] = np.array([st, pd, g])
+    np.savez_compressed(os.path.join(HERE, "parakeet_golden.npz"), **out)
+    print("parakeet_golden.npz:", len(out), "arrays")
+
+
 if __name__ == "__main__":
     import sys
     only = set(sys.argv[1:])
+    if not only or "parakeet" in only:
+        parakeet_fixture()
     if not only or "bfp16" in only:
         bfp16_fixture()
     if not only or "opt" in only:

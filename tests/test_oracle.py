@@ -268,3 +268,89 @@ def test_whisper_encoder_oracle_matches_hf_golden():
     f = np.load(os.path.join(GOLD, "whisper_hf_golden.npz"))
     e = O.whisper_encode(cfg, w, mel, 2)
     np.testing.assert_allclose(e, f["enc"], atol=1e-4, rtol=0)  # A&S erf in GELU vs exact erf
+
+
+# ------------------------------------------------------------------ Parakeet primitives
+def _pk_gold():
+    return np.load(os.path.join(GOLD, "parakeet_golden.npz"))
+
+
+def test_parakeet_rel_shift_matches_reference_golden():
+    """or_rel_shift (ops.rs:113-133) vs the reference's numpy rel_shift_host, bit-exact,
+    including T = 1 and 2."""
+    f = _pk_gold()
+    for T in (1, 2, 9, 31):
+        np.testing.assert_array_equal(O.rel_shift(f[f"bd_{T}"]), f[f"shift_{T}"])
+
+
+def test_parakeet_dwconv_matches_reference_golden():
+    """or_dwconv1d (ops.rs:92-110) vs golden_dwconv1d_k9.host_reference (fp32, C=1024, T=400)."""
+    f = _pk_gold()
+    x = np.random.default_rng(78).standard_normal((1024, 400)).astype(np.float32)
+    dw = (np.random.default_rng(79).standard_normal((1024, 9)) / 3).astype(np.float32)
+    db = (np.random.default_rng(80).standard_normal(1024) * 0.02).astype(np.float32)
+    y = O.dwconv1d(x, dw, db)
+    import sys
+    sys.path.insert(0, GOLD)
+    import make_golden as G
+    np.testing.assert_allclose(y[G.PK_DW_CHANNELS], f["dw_out"], rtol=0, atol=2e-6)
+    assert abs(np.sum(y.astype(np.float64)) - float(f["dw_sum"])) < 1e-3
+
+
+def test_parakeet_conv2d_matches_reference_golden():
+    """or_conv2d (ops.rs:38-89: strided, depthwise, pointwise) vs golden_subsample.conv2d_ref."""
+    f = _pk_gold()
+    for i in range(4):
+        st, pd, g = (int(v) for v in f[f"c2d_meta{i}"])
+        y = O.conv2d(f[f"c2d_x{i}"], f[f"c2d_w{i}"], f[f"c2d_b{i}"], st, pd, g)
+        np.testing.assert_allclose(y, f[f"c2d_y{i}"], rtol=1e-5, atol=1e-5)
+
+
+def test_parakeet_rel_pos_encoding_rows():
+    """pos.rs:7-47: 2T-1 rows, positions T-1 .. 0 .. -(T-1); row T-1 is position 0
+    (sin 0 = 0, cos 0 = 1) and rows T-1-p and T-1+p are mirror images (sin odd, cos even)."""
+    for T in (1, 2, 5, 125):
+        pe = O.rel_pos_encoding(T, 16)
+        assert pe.shape == (2 * T - 1, 16)
+        np.testing.assert_array_equal(pe[T - 1, 0::2], 0.0)
+        np.testing.assert_array_equal(pe[T - 1, 1::2], 1.0)
+        for p in range(1, T):
+            np.testing.assert_array_equal(pe[T - 1 - p, 0::2], -pe[T - 1 + p, 0::2])
+            np.testing.assert_array_equal(pe[T - 1 - p, 1::2], pe[T - 1 + p, 1::2])
+    pe = O.rel_pos_encoding(3, 4)
+    div1 = np.exp(-np.log(10000.0) * 2 / 4)
+    np.testing.assert_allclose(pe[0], np.array([np.sin(2.0), np.cos(2.0), np.sin(2 * div1), np.cos(2 * div1)],
+                                               np.float32), rtol=1e-7)
+
+
+def test_parakeet_int8_linear_rule():
+    """or_parakeet_quant_lin follows ctx2.rs: per-column weight scale, dynamic per-tensor
+    activation scale, round-half-away quantisation, exact i32 dot, (acc * s_a) * ws + b."""
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((7, 64)).astype(np.float32)
+    x[3, 5] = 4.0                                     # the tensor max -> +127 exactly
+    w = (rng.standard_normal((64, 24)) * 0.02).astype(np.float32)
+    w[:, 3] = 0.0                                     # zero column -> scale 1.0
+    b = rng.standard_normal(24).astype(np.float32)
+    y = O.quant_lin(x, w, b)
+    sa = np.float32(np.abs(x).max()) / np.float32(127)
+    xq = np.clip(np.trunc(x / sa + np.copysign(np.float32(0.5), x / sa)), -127, 127).astype(np.int64)
+    amax = np.abs(w).max(0)
+    ws = np.where(amax > 0, amax / np.float32(127), np.float32(1)).astype(np.float32)
+    wq = np.clip(np.trunc(w / ws + np.copysign(np.float32(0.5), w / ws)), -127, 127).astype(np.int64)
+    acc = xq @ wq
+    want = ((acc.astype(np.float32) * sa).astype(np.float32) * ws).astype(np.float32) + b
+    np.testing.assert_array_equal(y, want)
+    assert xq[3, 5] == 127
+
+
+def test_parakeet_oracle_int8_tracks_f32():
+    """The int8-engine encoder stays close to the reference's f32 host encoder."""
+    from xdna_engine_b200.synth import ParakeetConfig, make_parakeet_weights, make_parakeet_mel
+    cfg = ParakeetConfig(n_layers=2, n_frames=120)
+    w = make_parakeet_weights(cfg, seed=2)
+    mel = make_parakeet_mel(cfg, 1, 2)
+    a = O.parakeet_encode(cfg, w, mel, int8=True)
+    b = O.parakeet_encode(cfg, w, mel, int8=False)
+    cos = (a * b).sum(-1) / np.linalg.norm(a, axis=-1) / np.linalg.norm(b, axis=-1)
+    assert a.shape == (1, 15, 1024) and cos.min() > 0.999

@@ -210,3 +210,85 @@ def make_mel(cfg: WhisperEncConfig = WHISPER_SMALL_ENC, batch: int = 1, seed: in
     """Synthetic log-mel input ~N(0, 1), [batch, n_mels, n_frames]."""
     rng = np.random.default_rng(seed + 9_000_011)
     return rng.standard_normal((batch, cfg.n_mels, cfg.n_frames), dtype=np.float32)
+
+
+# --------------------------------------------------------------- Parakeet FastConformer encoder
+@dataclass(frozen=True)
+class ParakeetConfig:
+    n_layers: int = 24
+    d_model: int = 1024
+    n_heads: int = 8
+    ffn: int = 4096
+    n_mels: int = 128
+    n_frames: int = 1000
+    sub_ch: int = 256
+    kconv: int = 9
+
+    @property
+    def frames_out(self) -> int:
+        t = self.n_frames
+        for _ in range(3):
+            t = (t - 1) // 2 + 1
+        return t
+
+    @property
+    def freq_out(self) -> int:
+        f = self.n_mels
+        for _ in range(3):
+            f = (f - 1) // 2 + 1
+        return f
+
+
+PARAKEET_V3 = ParakeetConfig()
+
+
+def make_parakeet_weights(cfg: ParakeetConfig = PARAKEET_V3, seed: int = 0, std: float = 0.02,
+                          ln_std: float = 0.0, n_layers: int | None = None) -> dict:
+    """Random-init FastConformer weights (f32).  Linear weights N(0, std) in [in, out] layout
+    (no linear biases, as in the checkpoint the reference bakes); the subsample convolutions
+    use N(0, 1/sqrt(fan_in)) so the stem's activations stay O(1); depthwise taps and bias are
+    the BatchNorm-folded values the reference loads."""
+    rng = np.random.default_rng(seed)
+    D, F, C, H = cfg.d_model, cfg.ffn, cfg.sub_ch, cfg.n_heads
+    dk = D // H
+
+    def normal(shape, s):
+        a = rng.standard_normal(shape, dtype=np.float32)
+        a *= np.float32(s)
+        return a
+
+    def vec(n, base, s):
+        if s == 0.0:
+            return np.full(n, base, np.float32)
+        return (np.float32(base) + rng.standard_normal(n, dtype=np.float32) * np.float32(s)).astype(np.float32)
+
+    fo = cfg.freq_out
+    w = {"c0_w": normal((C, 1, 3, 3), 1 / 3), "c0_b": normal((C,), 0.1),
+         "c2_w": normal((C, 1, 3, 3), 1 / 3), "c2_b": normal((C,), 0.1),
+         "c3_w": normal((C, C, 1, 1), 1 / 16), "c3_b": normal((C,), 0.1),
+         "c5_w": normal((C, 1, 3, 3), 1 / 3), "c5_b": normal((C,), 0.1),
+         "c6_w": normal((C, C, 1, 1), 1 / 16), "c6_b": normal((C,), 0.1),
+         "out_w": normal((C * fo, D), 1 / np.sqrt(C * fo)), "out_b": normal((D,), 0.02)}
+    layers = []
+    for _ in range(cfg.n_layers if n_layers is None else n_layers):
+        ly = {}
+        for p in ("ff1", "ff2"):
+            ly[p + "_ln_w"], ly[p + "_ln_b"] = vec(D, 1.0, ln_std), vec(D, 0.0, ln_std)
+            ly[p + "_w1"], ly[p + "_w2"] = normal((D, F), std), normal((F, D), std)
+        ly["att_ln_w"], ly["att_ln_b"] = vec(D, 1.0, ln_std), vec(D, 0.0, ln_std)
+        for n in ("wq", "wk", "wv", "wpos", "wout"):
+            ly[n] = normal((D, D), std)
+        ly["pos_u"], ly["pos_v"] = normal((H, dk), 0.02), normal((H, dk), 0.02)
+        ly["conv_ln_w"], ly["conv_ln_b"] = vec(D, 1.0, ln_std), vec(D, 0.0, ln_std)
+        ly["pw1"], ly["pw2"] = normal((D, 2 * D), std), normal((D, D), std)
+        ly["dw_w"], ly["dw_b"] = normal((D, cfg.kconv), 1 / 3), normal((D,), 0.02)
+        ly["out_ln_w"], ly["out_ln_b"] = vec(D, 1.0, ln_std), vec(D, 0.0, ln_std)
+        layers.append(ly)
+    w["layers"] = layers
+    return w
+
+
+def make_parakeet_mel(cfg: ParakeetConfig = PARAKEET_V3, batch: int = 1, seed: int = 0) -> np.ndarray:
+    """Synthetic log-mel input ~N(0, 1), [batch, n_mels, n_frames]."""
+    rng = np.random.default_rng(seed + 7_000_003)
+    return rng.standard_normal((batch, cfg.n_mels, cfg.n_frames), dtype=np.float32)
