@@ -73,6 +73,19 @@ int xdna_gemv_i8_noalloc(int device, const float *x, int K, const int8_t *q_nk,
  * K % 64 == 0 and 16-byte aligned rows.  Asynchronous on `stream`; 0 or -1. */
 int xdna_gemm_bf16(const uint16_t *A, const uint16_t *B, const float *bias, const uint16_t *residual,
                    uint16_t *C, int M, int N, int K, int gelu, void *stream);
+/* The int8 encoder GEMM on the tcgen05 tensor cores (kind::i8, exact s32 accumulation in
+ * TMEM) with the reference's dequant epilogue (rust/npu-asr/src/ctx2.rs forward_view_int8
+ * 771-829, dequant_epi 1386-1411): A int8 [M, K] quantised per clip with scale sa[clip]
+ * (clip = row / rows_per_clip), B int8 weight [N, K] with per-output-channel scales ws[N];
+ * y = (float(acc) * sa) * ws[n] (+ bias[n], nullable); act 0 none, 1 SiLU
+ * (v * (1 / (1 + e^-v))), 3 GLU over interleaved column pairs (2c value, 2c + 1 gate) ->
+ * y[2c] * sigmoid(y[2c + 1]) at column c; then C = residual + alpha * y (residual f32,
+ * nullable, may equal C); C f32 [M, N] (N / 2 columns for GLU).  amax (nullable, [clips]
+ * uint32): atomically raised to the bit pattern of each clip's max |C|, the next layer's
+ * activation scale.  Needs N % 256 == 0, K % 128 == 0.  Asynchronous on `stream`; 0 or -1. */
+int xdna_gemm_i8(const int8_t *A, const int8_t *B, const float *sa, int rows_per_clip, const float *ws,
+                 const float *bias, int act, const float *residual, float alpha, float *C,
+                 unsigned *amax, int M, int N, int K, void *stream);
 /* After the stream has finished: -1 (with xdna_last_error) if a GEMM's bounded wait expired
  * since the last check, else 0. */
 int xdna_gemm_check(void);

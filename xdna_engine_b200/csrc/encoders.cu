@@ -28,8 +28,8 @@
 namespace xdna {
 void set_last_error_message(const std::string &m);
 cudaError_t gemm_bf16(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M, int N, int K,
-                      const float *bias, const uint16_t *residual, int ldr, int gelu, uint16_t *C, int ldc,
-                      cudaStream_t st, int res_mod = 0);
+                      const float *bias, const uint16_t *residual, int ldr, int act, uint16_t *C, int ldc,
+                      cudaStream_t st, int res_mod = 0, float *C_f32 = nullptr);
 unsigned gemm_error_and_clear();
 
 namespace bert {

@@ -33,22 +33,12 @@ namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 2 * BN * 4 + 256;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 4 * BN * 4 + 256;
 constexpr int THREADS = 320;
 constexpr int EPI_THREADS = 256;
 constexpr uint64_t TIMEOUT_NS = 2000000000ull;
 
 static __device__ unsigned int g_gemm_error;
-
-struct Epi {
-    const float *bias;          // [N] or null
-    const uint16_t *residual;   // [M, ldr] bf16 or null; row r reads residual row r % res_mod
-    int ldr;
-    int res_mod;                // 0: residual row = output row
-    int gelu;
-    uint16_t *out;              // [M, ldc] bf16
-    int ldc;
-};
 
 __device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, unsigned code) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -77,25 +67,145 @@ __device__ __forceinline__ float gelu_erf_as(float v) {
     return 0.5f * v * (1.0f + copysignf(y, x));
 }
 
+// bf16 operands, f32 accumulators: C = act(acc + bias) (+ residual), bf16 or f32 out
+struct EpiBf16 {
+    const float *bias;          // [N] or null
+    const uint16_t *residual;   // [M, ldr] bf16 or null; row r reads residual row r % res_mod
+    int ldr;
+    int res_mod;                // 0: residual row = output row
+    int act;                    // 0 none, 1 exact-erf GELU, 2 ReLU
+    uint16_t *out;              // [M, ldc] bf16 (or null when out_f32 is set)
+    float *out_f32;             // [M, ldc] f32 or null
+    int ldc;
+
+    __device__ __forceinline__ void load_cols(float *s, int n0, int j) const {
+        s[j] = bias ? bias[n0 + j] : 0.0f;
+    }
+    // 64 accumulator columns [col, col + 64) of output row `row`; s = this tile's column params
+    __device__ __forceinline__ void apply(int row, int col, const uint32_t *r, const float *s) const {
+        const int rrow = res_mod ? row % res_mod : row;
+        const uint4 *rp = residual ? reinterpret_cast<const uint4 *>(residual + (size_t)rrow * ldr + col) : nullptr;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                float y = __uint_as_float(r[8 * u + j]) + s[8 * u + j];
+                if (act == 1) y = gelu_erf_as(y);
+                else if (act == 2) y = fmaxf(y, 0.0f);
+                v[j] = y;
+            }
+            if (rp) {
+                const uint4 w = rp[u];
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 4; e++) { v[2 * e] += bf16lo(ws[e]); v[2 * e + 1] += bf16hi(ws[e]); }
+            }
+            if (out_f32) {
+                float4 *op = reinterpret_cast<float4 *>(out_f32 + (size_t)row * ldc + col + 8 * u);
+                op[0] = make_float4(v[0], v[1], v[2], v[3]);
+                op[1] = make_float4(v[4], v[5], v[6], v[7]);
+            } else {
+                uint4 w;
+                w.x = bf16bits(v[0]) | (bf16bits(v[1]) << 16);
+                w.y = bf16bits(v[2]) | (bf16bits(v[3]) << 16);
+                w.z = bf16bits(v[4]) | (bf16bits(v[5]) << 16);
+                w.w = bf16bits(v[6]) | (bf16bits(v[7]) << 16);
+                reinterpret_cast<uint4 *>(out + (size_t)row * ldc + col)[u] = w;
+            }
+        }
+    }
+};
+
+// int8 operands, s32 accumulators, the reference's dequant epilogue (rust/npu-asr/src/ctx2.rs
+// dequant_epi 1386-1411): y = (float(acc) * s_a[clip(row)]) * ws[n] (+ bias[n]), then
+// act (SiLU v * (1 / (1 + e^-v)), or GLU over interleaved column pairs (value, gate) ->
+// value * sigmoid(gate), written at column n / 2), then out = residual + alpha * y; f32 out.
+// Optionally the per-clip max |out| (the next quantisation's scale) is folded into amax[clip]
+// (atomicMax on the bit pattern: order-free and exact for non-negative floats).
+struct EpiI8 {
+    const float *sa;            // [clips] activation scales
+    int rows_per_clip;
+    const float *ws;            // [N] weight scales
+    const float *bias;          // [N] or null
+    int act;                    // 0 none, 1 SiLU, 3 GLU pairs
+    const float *residual;      // [M, ldr] f32 or null (may alias out)
+    int ldr;
+    float alpha;
+    float *out;                 // [M, ldc] f32
+    int ldc;
+    unsigned *amax;             // [clips] or null
+
+    __device__ __forceinline__ void load_cols(float *s, int n0, int j) const {
+        s[j] = ws[n0 + j];
+        s[BN + j] = bias ? bias[n0 + j] : 0.0f;
+    }
+    __device__ __forceinline__ void apply(int row, int col, const uint32_t *r, const float *s) const {
+        const float a = sa[row / rows_per_clip];
+        float v[64];
+#pragma unroll
+        for (int j = 0; j < 64; j++) {
+            float y = __fmul_rn(__fmul_rn((float)(int)r[j], a), s[j]);
+            if (bias) y = __fadd_rn(y, s[BN + j]);
+            if (act == 1) y = __fmul_rn(y, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-y))));
+            v[j] = y;
+        }
+        float m = 0.0f;
+        if (act == 3) {
+            const int oc = col >> 1;
+            const float *rp = residual ? residual + (size_t)row * ldr + oc : nullptr;
+            float *op = out + (size_t)row * ldc + oc;
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                float y = __fmul_rn(v[2 * j], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[2 * j + 1]))));
+                if (rp) y = __fadd_rn(rp[j], __fmul_rn(alpha, y));
+                op[j] = y;
+                m = fmaxf(m, fabsf(y));
+            }
+        } else {
+            const float *rp = residual ? residual + (size_t)row * ldr + col : nullptr;
+            float *op = out + (size_t)row * ldc + col;
+#pragma unroll
+            for (int j = 0; j < 64; j += 4) {
+                float4 y = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                if (rp) {
+                    const float4 q = *reinterpret_cast<const float4 *>(rp + j);
+                    y.x = __fadd_rn(q.x, __fmul_rn(alpha, y.x));
+                    y.y = __fadd_rn(q.y, __fmul_rn(alpha, y.y));
+                    y.z = __fadd_rn(q.z, __fmul_rn(alpha, y.z));
+                    y.w = __fadd_rn(q.w, __fmul_rn(alpha, y.w));
+                }
+                *reinterpret_cast<float4 *>(op + j) = y;
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+            }
+        }
+        if (amax) atomicMax(amax + row / rows_per_clip, __float_as_uint(m));
+    }
+};
+
 // Persistent: CTA b handles tiles b, b + grid, ...; tile t -> (m = t / n_tiles, n = t % n_tiles)
 // so CTAs running together share A rows in L2.  Two TMEM accumulators of 256 columns let the
-// epilogue of tile i overlap the MMAs of tile i + 1.
+// epilogue of tile i overlap the MMAs of tile i + 1.  I8 selects kind::i8 (int8 operands, 128
+// K-elements per 128-byte stage row, s32 accumulators) over kind::f16 (bf16, 64 per row).
+template <bool I8, class E>
 __global__ void __launch_bounds__(THREADS, 1)
-gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                 int K, Epi epi) {
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+            E epi) {
+    constexpr int KE = I8 ? 128 : 64;            // K elements per stage (128 bytes per row)
+    constexpr int KI = I8 ? 32 : 16;             // K elements per MMA instruction (32 bytes)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t *stA = smem;                            // [STAGES][BM][BK] bf16, swizzled
-    uint8_t *stB = smem + STAGES * A_BYTES;         // [STAGES][BN][BK] bf16, swizzled
-    float *sbias = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES);   // [2][BN]
-    uint64_t *full = reinterpret_cast<uint64_t *>(sbias + 2 * BN);
+    uint8_t *stA = smem;                            // [STAGES][BM][128 B], swizzled
+    uint8_t *stB = smem + STAGES * A_BYTES;         // [STAGES][BN][128 B], swizzled
+    float *scol = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES);   // [2][2][BN] column params
+    uint64_t *full = reinterpret_cast<uint64_t *>(scol + 4 * BN);
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;               // [2]
     uint64_t *tempty = tfull + 2;                   // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nk = K / BK;
+    const int nk = K / KE;
     const int n_tiles = N / BN, m_tiles = (M + BM - 1) / BM;
     const int total = n_tiles * m_tiles;
 
@@ -120,15 +230,15 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 const int s = c % STAGES;
                 if (c >= STAGES && !wait_bounded(&empty[s], ((c / STAGES) - 1) & 1, 1u)) { ok = false; break; }
                 mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                tc::tma_load_2d(stA + s * A_BYTES, &tmA, kb * BK, m0, &full[s]);
-                tc::tma_load_2d(stB + s * B_BYTES, &tmB, kb * BK, n0, &full[s]);
+                tc::tma_load_2d(stA + s * A_BYTES, &tmA, kb * KE, m0, &full[s]);
+                tc::tma_load_2d(stB + s * B_BYTES, &tmB, kb * KE, n0, &full[s]);
             }
         }
         // drain: the loads in flight must land before the CTA exits
         for (uint32_t q = c > STAGES ? c - STAGES : 0; q < c; q++) wait_bounded(&full[q % STAGES], (q / STAGES) & 1, 2u);
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer (one thread)
-        constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
+        constexpr uint32_t idesc = I8 ? tc::idesc_s8_s32(BM, BN) : tc::idesc_bf16_f32(BM, BN);
         uint32_t c = 0;
         int i = 0;
         bool ok = true;
@@ -144,8 +254,10 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 const uint64_t da = tc::desc_k_sw128(smem_u32(stA + s * A_BYTES));
                 const uint64_t db = tc::desc_k_sw128(smem_u32(stB + s * B_BYTES));
 #pragma unroll
-                for (int k = 0; k < BK / 16; k++)   // K 16 per MMA = 32 bytes = +2 in the start field
-                    tc::mma_bf16(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                for (int k = 0; k < KE / KI; k++) {   // 32 bytes per MMA = +2 in the start field
+                    if (I8) tc::mma_s8(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    else tc::mma_bf16(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                }
                 tc::commit(&empty[s]);
             }
             tc::commit(&tfull[acc]);   // always signalled, so the epilogue never waits forever
@@ -160,8 +272,8 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const int acc = i & 1;
             const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
             const int row = m0 + 32 * q + lane;
-            float *bs = sbias + acc * BN;
-            for (int j = et; j < BN; j += EPI_THREADS) bs[j] = epi.bias ? epi.bias[n0 + j] : 0.0f;
+            float *cs = scol + acc * 2 * BN;
+            for (int j = et; j < BN; j += EPI_THREADS) epi.load_cols(cs, n0, j);
             named_bar(2, EPI_THREADS);
             wait_bounded(&tfull[acc], (i >> 1) & 1, 5u);
             tc::fence_after_sync();
@@ -172,35 +284,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 tc::tmem_ld32(ta, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
                 tc::tmem_ld32(ta + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
                 tc::tmem_ld_wait();
-                if (row < M) {
-                    const int col = n0 + c0;
-                    const int rrow = epi.res_mod ? row % epi.res_mod : row;
-                    const uint4 *rp = epi.residual
-                        ? reinterpret_cast<const uint4 *>(epi.residual + (size_t)rrow * epi.ldr + col) : nullptr;
-                    uint4 *op = reinterpret_cast<uint4 *>(epi.out + (size_t)row * epi.ldc + col);
-#pragma unroll
-                    for (int u = 0; u < 8; u++) {
-                        float v[8];
-#pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            float y = __uint_as_float(r[8 * u + j]) + bs[c0 + 8 * u + j];
-                            if (epi.gelu) y = gelu_erf_as(y);
-                            v[j] = y;
-                        }
-                        if (rp) {
-                            const uint4 w = rp[u];
-                            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                            for (int e = 0; e < 4; e++) { v[2 * e] += bf16lo(ws[e]); v[2 * e + 1] += bf16hi(ws[e]); }
-                        }
-                        uint4 w;
-                        w.x = bf16bits(v[0]) | (bf16bits(v[1]) << 16);
-                        w.y = bf16bits(v[2]) | (bf16bits(v[3]) << 16);
-                        w.z = bf16bits(v[4]) | (bf16bits(v[5]) << 16);
-                        w.w = bf16bits(v[6]) | (bf16bits(v[7]) << 16);
-                        op[u] = w;
-                    }
-                }
+                if (row < M) epi.apply(row, n0 + c0, r, cs + c0);
             }
             tc::fence_before_sync();
             __syncwarp();
@@ -226,47 +310,62 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// K-major bf16 matrix [rows, K] (row stride ld elements) as 64 x 128 boxes with 128 B swizzle
-bool make_tmap(CUtensorMap *tm, const void *base, int rows, int K, int ld, int box_rows) {
+// K-major matrix [rows, K] (row stride ld elements) as 128-byte x box_rows boxes with 128 B
+// swizzle: bf16 (64 elements per box row) or int8 (128)
+bool make_tmap(CUtensorMap *tm, const void *base, int rows, int K, int ld, int box_rows, bool i8) {
     auto fn = encode_fn();
     if (!fn) return false;
+    const int es = i8 ? 1 : 2;
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
-    cuuint32_t es[2] = {1, 1};
-    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    cuuint64_t strides[1] = {(cuuint64_t)ld * es};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(tm, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base),
+              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-cudaError_t launch(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M, int N, int K, const Epi &epi,
-                   cudaStream_t st) {
-    CUtensorMap ta, tb;
-    if (!make_tmap(&ta, A, M, K, lda, BM) || !make_tmap(&tb, B, N, K, ldb, BN)) return cudaErrorInvalidValue;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+static int sm_count() {
     static int sms = 0;
     if (!sms) {
         int dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     }
+    return sms;
+}
+
+template <bool I8, class E>
+cudaError_t launch_t(const void *A, int lda, const void *B, int ldb, int M, int N, int K, const E &epi,
+                     cudaStream_t st) {
+    CUtensorMap ta, tb;
+    if (!make_tmap(&ta, A, M, K, lda, BM, I8) || !make_tmap(&tb, B, N, K, ldb, BN, I8)) return cudaErrorInvalidValue;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<I8, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
     const int tiles = (N / BN) * ((M + BM - 1) / BM);
-    gemm_bf16_kernel<<<tiles < sms ? tiles : sms, THREADS, SMEM_BYTES, st>>>(ta, tb, M, N, K, epi);
+    const int sms = sm_count();
+    gemm_kernel<I8, E><<<tiles < sms ? tiles : sms, THREADS, SMEM_BYTES, st>>>(ta, tb, M, N, K, epi);
     return cudaGetLastError();
 }
 
 }  // namespace gemm
 
 cudaError_t gemm_bf16(const uint16_t *A, int lda, const uint16_t *B, int ldb, int M, int N, int K,
-                      const float *bias, const uint16_t *residual, int ldr, int gelu, uint16_t *C, int ldc,
-                      cudaStream_t st, int res_mod) {
-    gemm::Epi e{bias, residual, ldr, res_mod, gelu, C, ldc};
-    return gemm::launch(A, lda, B, ldb, M, N, K, e, st);
+                      const float *bias, const uint16_t *residual, int ldr, int act, uint16_t *C, int ldc,
+                      cudaStream_t st, int res_mod, float *C_f32) {
+    gemm::EpiBf16 e{bias, residual, ldr, res_mod, act, C, C_f32, ldc};
+    return gemm::launch_t<false>(A, lda, B, ldb, M, N, K, e, st);
+}
+
+cudaError_t gemm_i8(const int8_t *A, int lda, const int8_t *B, int ldb, int M, int N, int K, const float *sa,
+                    int rows_per_clip, const float *ws, const float *bias, int act, const float *residual, int ldr,
+                    float alpha, float *C, int ldc, unsigned *amax, cudaStream_t st) {
+    gemm::EpiI8 e{sa, rows_per_clip, ws, bias, act, residual, ldr, alpha, C, ldc, amax};
+    return gemm::launch_t<true>(A, lda, B, ldb, M, N, K, e, st);
 }
 
 unsigned gemm_error_and_clear() {
@@ -286,9 +385,28 @@ extern "C" int xdna_gemm_bf16(const uint16_t *A, const uint16_t *B, const float 
         set_last_error_message("xdna_gemm_bf16: need M > 0, N % 256 == 0, K % 64 == 0");
         return -1;
     }
-    cudaError_t e = gemm_bf16(A, K, B, K, M, N, K, bias, residual, N, gelu, C, N, (cudaStream_t)stream, 0);
+    cudaError_t e = gemm_bf16(A, K, B, K, M, N, K, bias, residual, N, gelu, C, N, (cudaStream_t)stream, 0, nullptr);
     if (e != cudaSuccess) {
         set_last_error_message(std::string("xdna_gemm_bf16: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+extern "C" int xdna_gemm_i8(const int8_t *A, const int8_t *B, const float *sa, int rows_per_clip, const float *ws,
+                            const float *bias, int act, const float *residual, float alpha, float *C,
+                            unsigned *amax, int M, int N, int K, void *stream) {
+    using namespace xdna;
+    if (!A || !B || !sa || !ws || !C) { set_last_error_message("xdna_gemm_i8: null pointer"); return -1; }
+    if (M <= 0 || N <= 0 || K <= 0 || N % 256 || K % 128 || rows_per_clip <= 0 || (act != 0 && act != 1 && act != 3)) {
+        set_last_error_message("xdna_gemm_i8: need M > 0, N % 256 == 0, K % 128 == 0, rows_per_clip > 0, act 0/1/3");
+        return -1;
+    }
+    const int ldc = act == 3 ? N / 2 : N;
+    cudaError_t e = gemm_i8(A, K, B, K, M, N, K, sa, rows_per_clip, ws, bias, act, residual, ldc, alpha, C, ldc, amax,
+                            (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        set_last_error_message(std::string("xdna_gemm_i8: ") + cudaGetErrorString(e));
         return -1;
     }
     return 0;
