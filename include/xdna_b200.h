@@ -247,6 +247,39 @@ int xdna_opt_set_trace(XdnaOptDecoder *dec, float *trace_dev);
  * outputs are published, 5*n_layers + 1 after the LM head, + 2 once the greedy id is known). */
 int xdna_opt_set_timing(XdnaOptDecoder *dec, unsigned long long *timing_dev);
 
+/* ------------------------------------ Parakeet FastConformer encoder (FastConformerEncoder) */
+/* Replaces rust/npu-parakeet/src/encoder.rs FastConformerEncoder::subsample (200-237) +
+ * forward_last (657-665) with every weight linear on the int8 GEMM engine (the reference's
+ * NPU_PRECISION=int8 rule, rust/npu-asr/src/ctx2.rs).  Shapes: d_model 1024, 8 heads x 128,
+ * ffn 4096, 256 subsample channels, conv kernel 9, at most 128 frames after the 8x
+ * subsampling (n_frames <= 1017). */
+typedef struct {
+    int n_layers, d_model, n_heads, ffn, n_mels, n_frames, sub_ch, kconv;
+} XdnaParakeetConfig;
+typedef struct {               /* f32; linear weights [K, N] = [in, out], no biases */
+    const float *ff1_ln_w, *ff1_ln_b, *ff1_w1, *ff1_w2;
+    const float *att_ln_w, *att_ln_b, *wq, *wk, *wv, *wpos, *wout;
+    const float *pos_u, *pos_v;                       /* [heads, 128] */
+    const float *conv_ln_w, *conv_ln_b, *pw1, *dw_w, *dw_b, *pw2;   /* pw1 [D, 2D] (value | gate), dw_w [D, 9] */
+    const float *ff2_ln_w, *ff2_ln_b, *ff2_w1, *ff2_w2;
+    const float *out_ln_w, *out_ln_b;
+} XdnaParakeetLayer;
+typedef struct {
+    const float *c0_w, *c0_b, *c2_w, *c2_b, *c3_w, *c3_b, *c5_w, *c5_b, *c6_w, *c6_b;  /* conv [Co, Ci/g, kh, kw] */
+    const float *out_w, *out_b;                       /* [256 * F/8, D] ([in, out]), [D] */
+    const XdnaParakeetLayer *layers;
+} XdnaParakeetWeights;
+typedef struct XdnaParakeet XdnaParakeet;
+XdnaParakeet *xdna_parakeet_create(XdnaDevice *dev, const XdnaParakeetConfig *cfg, const XdnaParakeetWeights *w,
+                                   int max_batch);
+void xdna_parakeet_free(XdnaParakeet *m);
+/* frames per clip after subsampling (T') */
+int xdna_parakeet_frames_out(const XdnaParakeet *m);
+/* host mel [B][n_mels][n_frames] f32 -> host encodings [B][T'][1024] f32.  Synchronous. */
+int xdna_parakeet_encode(XdnaParakeet *m, const float *mel, int B, float *out);
+/* device-resident form: asynchronous on `stream` */
+int xdna_parakeet_encode_device(XdnaParakeet *m, const float *mel_dev, int B, float *out_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,3 +73,54 @@ def test_gemm_i8_silu_and_glu(X):
     C, _ = _gemm_i8(X, A, B, sa, 125, ws, act=3)
     want = y[:, 0::2] / (1 + np.exp(-y[:, 1::2]))
     np.testing.assert_allclose(C, want, rtol=2e-6, atol=1e-6)
+
+
+def _compare(got, want, cos_min=0.998, rel_max=0.1):
+    g = got.reshape(-1, got.shape[-1]).astype(np.float64)
+    r = want.reshape(-1, want.shape[-1]).astype(np.float64)
+    cos = (g * r).sum(1) / np.linalg.norm(g, axis=1) / np.linalg.norm(r, axis=1)
+    rel = np.abs(g - r).max(1) / np.sqrt((r * r).mean(1))
+    assert cos.min() >= cos_min, (cos.min(), rel.max())
+    assert rel.max() <= rel_max, (cos.min(), rel.max())
+    return cos.min(), rel.max()
+
+
+def test_parakeet_encoder_small_vs_oracle(X):
+    """2 blocks on 200-frame clips (25 frames after subsampling), 3 clips, against the oracle's
+    int8-engine encoder; each clip alone gives the same bits as inside the batch."""
+    from oracle import oracle as O
+    cfg = X.ParakeetConfig(n_layers=2, n_frames=200)
+    w = X.make_parakeet_weights(cfg, seed=3, ln_std=0.05)
+    mel = X.make_parakeet_mel(cfg, 3, seed=3)
+    enc = X.ParakeetEncoder(X.Device(0), cfg, w, max_batch=4)
+    assert enc.frames_out == 25
+    got = enc.encode(mel)
+    want = O.parakeet_encode(cfg, w, mel, int8=True)
+    print("small", _compare(got, want))
+    for b in range(3):
+        assert np.array_equal(enc.encode(mel[b:b + 1])[0], got[b])
+    enc.close()
+
+
+def test_parakeet_encoder_full_clip_vs_oracle(X):
+    """A 10 s clip (1000 frames -> 125), two blocks: attention over all 125 positions and the
+    249-row rel-pos table; a batch of 2 clips."""
+    from oracle import oracle as O
+    cfg = X.ParakeetConfig(n_layers=2)
+    w = X.make_parakeet_weights(cfg, seed=4)
+    mel = X.make_parakeet_mel(cfg, 2, seed=4)
+    enc = X.ParakeetEncoder(X.Device(0), cfg, w, max_batch=2)
+    got = enc.encode(mel)
+    print("full", _compare(got, O.parakeet_encode(cfg, w, mel, int8=True)))
+    enc.close()
+
+
+def test_parakeet_rejects_bad_shapes(X):
+    bad = X.ParakeetConfig(n_layers=1, n_frames=2000)          # 250 frames after subsampling
+    with pytest.raises(X.XdnaError):
+        X.ParakeetEncoder(X.Device(0), bad, X.make_parakeet_weights(bad, n_layers=1))
+    cfg = X.ParakeetConfig(n_layers=1, n_frames=64)
+    enc = X.ParakeetEncoder(X.Device(0), cfg, X.make_parakeet_weights(cfg), max_batch=1)
+    with pytest.raises(X.XdnaError):
+        enc.encode(X.make_parakeet_mel(cfg, 2))
+    enc.close()

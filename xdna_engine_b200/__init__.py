@@ -16,7 +16,8 @@ import numpy as np
 
 from .synth import (OPT_125M, OptConfig, make_opt_weights, make_prompt,  # noqa: F401
                     BGE_BASE, BertConfig, make_bert_weights, make_bge_batch,
-                    WHISPER_SMALL_ENC, WhisperEncConfig, make_whisper_enc_weights, make_mel)
+                    WHISPER_SMALL_ENC, WhisperEncConfig, make_whisper_enc_weights, make_mel,
+                    PARAKEET_V3, ParakeetConfig, make_parakeet_weights, make_parakeet_mel)
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libxdna_b200.so")
@@ -86,6 +87,15 @@ def lib():
         L.xdna_whisper_encode.restype = i
         L.xdna_whisper_encode_device.argtypes = [vp, vp, i, vp, vp]
         L.xdna_whisper_encode_device.restype = i
+        L.xdna_parakeet_create.argtypes = [vp, vp, vp, i]
+        L.xdna_parakeet_create.restype = vp
+        L.xdna_parakeet_free.argtypes = [vp]
+        L.xdna_parakeet_frames_out.argtypes = [vp]
+        L.xdna_parakeet_frames_out.restype = i
+        L.xdna_parakeet_encode.argtypes = [vp, vp, i, vp]
+        L.xdna_parakeet_encode.restype = i
+        L.xdna_parakeet_encode_device.argtypes = [vp, vp, i, vp, vp]
+        L.xdna_parakeet_encode_device.restype = i
         L.xdna_opt_create.argtypes = [vp, vp, vp, i, i]
         L.xdna_opt_create.restype = vp
         L.xdna_opt_free.argtypes = [vp]
@@ -371,6 +381,71 @@ class WhisperEncoder:
     def close(self):
         if getattr(self, "handle", None):
             lib().xdna_whisper_enc_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_PK_LAYER = ("ff1_ln_w", "ff1_ln_b", "ff1_w1", "ff1_w2", "att_ln_w", "att_ln_b", "wq", "wk", "wv", "wpos",
+             "wout", "pos_u", "pos_v", "conv_ln_w", "conv_ln_b", "pw1", "dw_w", "dw_b", "pw2",
+             "ff2_ln_w", "ff2_ln_b", "ff2_w1", "ff2_w2", "out_ln_w", "out_ln_b")
+_PK_TOP = ("c0_w", "c0_b", "c2_w", "c2_b", "c3_w", "c3_b", "c5_w", "c5_b", "c6_w", "c6_b", "out_w", "out_b")
+
+
+class _PkCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d_model", "n_heads", "ffn", "n_mels", "n_frames", "sub_ch",
+                                       "kconv")]
+
+
+class _PkLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _PK_LAYER]
+
+
+class _PkWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _PK_TOP + ("layers",)]
+
+
+class ParakeetEncoder:
+    """Parakeet FastConformer encoder on one B200 (FastConformerEncoder::subsample +
+    forward_last of the reference, int8 GEMM engine)."""
+
+    def __init__(self, device: Device, cfg, weights: dict, max_batch: int = 1):
+        keep = []
+
+        def p(a):
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            return _addr(a)
+
+        c = _PkCfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.ffn, cfg.n_mels, cfg.n_frames, cfg.sub_ch, cfg.kconv)
+        layers = (_PkLayer * cfg.n_layers)()
+        for li, ly in enumerate(weights["layers"][:cfg.n_layers]):
+            for n in _PK_LAYER:
+                setattr(layers[li], n, p(ly[n]))
+        w = _PkWeights(*[p(weights[n]) for n in _PK_TOP], C.addressof(layers))
+        h = lib().xdna_parakeet_create(device.handle, C.byref(c), C.byref(w), max_batch)
+        if not h:
+            raise XdnaError(last_error())
+        self.handle, self.cfg = h, cfg
+        self.frames_out = lib().xdna_parakeet_frames_out(h)
+
+    def encode(self, mel):
+        mel = np.ascontiguousarray(mel, np.float32)
+        B = mel.shape[0]
+        out = np.empty((B, self.frames_out, self.cfg.d_model), np.float32)
+        _check(lib().xdna_parakeet_encode(self.handle, _addr(mel), B, _addr(out)))
+        return out
+
+    def encode_device(self, mel_ptr, B, out_ptr, stream=0):
+        _check(lib().xdna_parakeet_encode_device(self.handle, mel_ptr, B, out_ptr, stream or None))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().xdna_parakeet_free(self.handle)
             self.handle = None
 
     def __del__(self):
