@@ -566,17 +566,189 @@ def run_whisper(args):
         torch.distributed.destroy_process_group()
 
 
+# ------------------------------------------------------------ Parakeet FastConformer encoder
+PARAKEET_METRIC = "Parakeet FastConformer encoder throughput (10 s clips: mel 128x1000 -> 125x1024, batch 64)"
+PARAKEET_BATCH = 64
+
+
+def parakeet_clip_ops(n_layers=24, T=125):
+    """Operations of one clip: the subsample stem (conv.0 147.5 M, conv.2 36.9 M, conv.3 1049 M,
+    conv.5 9.2 M, conv.6 262 M, out linear 1049 M) plus per block the int8 linears
+    (2 x 2 FFN, qkv, out, pw1, pw2 = 2 T x 1024 x 11264) and attention (AC, rel-pos BD over 2T-1
+    positions, PV: 2 x 8 x 128 x (T^2 + T(2T-1) + T^2)).  The rel-pos projection pos_enc . W_pos
+    does not depend on the input and is computed once per model, so it is not counted."""
+    stem = 147_456_000 + 36_864_000 + 1_048_576_000 + 9_216_000 + 262_144_000 + 1_048_576_000
+    layer = 2.0 * T * 1024 * 11264 + 2.0 * 8 * 128 * (T * T + T * (2 * T - 1) + T * T)
+    return stem + n_layers * layer
+
+
+def parakeet_cpu_sample(cores):
+    """The oracle on one clip with one block, scaled to the 24-block encoder by operations."""
+    from oracle import oracle as O
+    from xdna_engine_b200.synth import ParakeetConfig, make_parakeet_weights, make_parakeet_mel
+    cfg = ParakeetConfig(n_layers=1)
+    w = make_parakeet_weights(cfg, seed=0)
+    mel = make_parakeet_mel(cfg, 1, seed=0)
+    t0 = time.perf_counter()
+    O.parakeet_encode(cfg, w, mel, int8=True, nthreads=cores)
+    dt = time.perf_counter() - t0
+    return 1.0 / (dt * parakeet_clip_ops(24) / parakeet_clip_ops(1)), dt
+
+
+def run_parakeet_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    clips_s, dt = parakeet_cpu_sample(cores)
+    line = {"impl": "reference", "metric": PARAKEET_METRIC, "value": clips_s, "unit": "clips/s",
+            "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": {"workload": "Parakeet FastConformer encoder, 10 s clips"},
+            "cpu_baseline": {"value": clips_s, "unit": "clips/s", "cores": cores, "kind": "port",
+                             "sample": "1 clip through the subsample stem and 1 of 24 blocks, scaled by operations"},
+            "e2e": {"value": clips_s, "unit": "clips/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def int8_peak_tops():
+    """Dense int8 throughput of cuBLASLt (torch._int_mm) on 8192^3: the measured denominator
+    for the int8 GEMM (the driver's peaks file has no int8 figure)."""
+    import torch
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(10):
+        torch._int_mm(a, b)
+    e1.record()
+    torch.cuda.synchronize()
+    return 2.0 * n ** 3 * 10 / (e0.elapsed_time(e1) * 1e-3) / 1e12
+
+
+def run_parakeet(args):
+    import torch
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    import xdna_engine_b200 as X
+    from xdna_engine_b200.synth import PARAKEET_V3 as cfg, make_parakeet_weights, make_parakeet_mel
+    B = PARAKEET_BATCH
+    w = make_parakeet_weights(cfg, seed=0)
+    mel = make_parakeet_mel(cfg, B, seed=rank)            # 64 clips per GPU (weak scaling)
+    enc = X.ParakeetEncoder(X.Device(local), cfg, w, max_batch=B)
+    T = enc.frames_out
+    d_mel = torch.from_numpy(mel).cuda()
+    out = torch.empty(B, T, 1024, device="cuda")
+    st = torch.cuda.current_stream()
+    sp = st.cuda_stream
+
+    def step():
+        enc.encode_device(d_mel.data_ptr(), B, out.data_ptr(), sp)
+
+    for _ in range(args.warmup):
+        step()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    with Clocks(local) as clk:
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    assert X.lib().xdna_gemm_check() == 0, X.last_error()
+    # dominant kernel: the int8 tcgen05 GEMM, timed alone on one block's eight linears at M = B*T
+    M = B * T
+    A = torch.randint(-127, 128, (M, 4096), dtype=torch.int8, device="cuda")
+    Wt = torch.randint(-127, 128, (4096, 4096), dtype=torch.int8, device="cuda")
+    sa = torch.full((B,), 0.01, device="cuda")
+    ws = torch.full((4096,), 0.001, device="cuda")
+    Cf = torch.empty(M, 4096, device="cuda")
+    shapes = [(4096, 1024, 1), (1024, 4096, 0), (3072, 1024, 0), (1024, 1024, 0), (2048, 1024, 3),
+              (1024, 1024, 0), (4096, 1024, 1), (1024, 4096, 0)]
+    g0, g1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    for rep in range(2):
+        g0.record(st)
+        for (N, K, act) in shapes:
+            X.lib().xdna_gemm_i8(A.data_ptr(), Wt.data_ptr(), sa.data_ptr(), T, ws.data_ptr(), None, act, None,
+                                 1.0, Cf.data_ptr(), None, M, N, K, sp)
+        g1.record(st)
+        torch.cuda.synchronize()
+    gemm_tops = (2.0 * M * 1024 * 11264) / (g0.elapsed_time(g1) * 1e-3) / 1e12
+    peak = int8_peak_tops()
+    del A, Wt, Cf
+    # end to end through xdna_parakeet_encode: host mel in, host encodings out
+    host_out = np.empty((B, T, 1024), np.float32)
+    e2e = []
+    for _ in range(3):
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        torch.cuda.synchronize()
+        a.record(torch.cuda.default_stream())
+        rc = X.lib().xdna_parakeet_encode(enc.handle, mel.ctypes.data, B, host_out.ctypes.data)
+        b.record(torch.cuda.default_stream())
+        torch.cuda.synchronize()
+        assert rc == 0, X.last_error()
+        e2e.append(a.elapsed_time(b))
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    cores = os.cpu_count() or 1
+    cpu_clips, _ = parakeet_cpu_sample(cores)
+    line = {
+        "metric": PARAKEET_METRIC, "value": world * B / (ms * 1e-3), "unit": "clips/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (random-init N(0,0.02) linears, fan-in scaled convs, mel ~ N(0,1))",
+        "config": {"workload": "Parakeet FastConformer encoder (24 blocks, int8 linears), 64 clips of 10 s per GPU",
+                   "model": "parakeet-tdt-0.6b-v3 encoder shapes (random init)", "global_batch": world * B,
+                   "parallelism": f"dp{world} (independent batches, no collective)",
+                   "l2": "activations (131 MB FFN hidden) larger than L2"},
+        "tops": B * parakeet_clip_ops() / (ms * 1e-3) / 1e12,
+        "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": peak, "unit": "TOP/s",
+                     "frac": gemm_tops / peak, "traffic": None,
+                     "peak_kind": "measured: cuBLASLt int8 (torch._int_mm) 8192^3 on this GPU",
+                     "kernel": "gemm_kernel<I8> (one block's eight int8 linears at M = 8000)"},
+        "cpu_baseline": {"value": cpu_clips, "unit": "clips/s", "cores": cores, "kind": "port",
+                         "sample": "1 clip through the subsample stem and 1 of 24 blocks, scaled by operations"},
+        "e2e": {"value": world * B / (min(e2e) * 1e-3), "unit": "clips/s",
+                "h2d_bytes_per_step": int(mel.nbytes), "d2h_bytes_per_step": int(host_out.nbytes),
+                "step": "one xdna_parakeet_encode call (host mel in, host f32 encodings out)"},
+        "gpu_launches": args.steps * (6 + 24 * 21),
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=0, help="timed steps (default: about half a second of work)")
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "bge", "whisper"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "bge", "whisper", "parakeet"], default="decode")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload == "whisper":
+    if args.workload == "parakeet":
+        if args.steps <= 0:
+            args.steps = 10
+        (run_parakeet_reference if args.impl == "reference" else run_parakeet)(args)
+    elif args.workload == "whisper":
         if args.steps <= 0:
             args.steps = 30
         (run_whisper_reference if args.impl == "reference" else run_whisper)(args)
