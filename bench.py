@@ -573,12 +573,12 @@ PARAKEET_BATCH = 64
 
 def parakeet_clip_ops(n_layers=24, T=125):
     """Operations of one clip: the subsample stem (conv.0 147.5 M, conv.2 36.9 M, conv.3 1049 M,
-    conv.5 9.2 M, conv.6 262 M, out linear 1049 M) plus per block the int8 linears
-    (2 x 2 FFN, qkv, out, pw1, pw2 = 2 T x 1024 x 11264) and attention (AC, rel-pos BD over 2T-1
-    positions, PV: 2 x 8 x 128 x (T^2 + T(2T-1) + T^2)).  The rel-pos projection pos_enc . W_pos
+    conv.5 9.2 M, conv.6 262 M, out linear 1049 M) plus per block the int8 linears (2 T x 1024
+    x 23552: two FFNs 4 x 4096, qkv 3072, out 1024, pw1 2048, pw2 1024) and attention (AC,
+    rel-pos BD over 2T-1 positions, PV: 2 x 8 x 128 x (T^2 + T(2T-1) + T^2)).  The rel-pos projection pos_enc . W_pos
     does not depend on the input and is computed once per model, so it is not counted."""
     stem = 147_456_000 + 36_864_000 + 1_048_576_000 + 9_216_000 + 262_144_000 + 1_048_576_000
-    layer = 2.0 * T * 1024 * 11264 + 2.0 * 8 * 128 * (T * T + T * (2 * T - 1) + T * T)
+    layer = 2.0 * T * 1024 * 23552 + 2.0 * 8 * 128 * (T * T + T * (2 * T - 1) + T * T)
     return stem + n_layers * layer
 
 
@@ -686,7 +686,7 @@ def run_parakeet(args):
                                  1.0, Cf.data_ptr(), None, M, N, K, sp)
         g1.record(st)
         torch.cuda.synchronize()
-    gemm_tops = (2.0 * M * 1024 * 11264) / (g0.elapsed_time(g1) * 1e-3) / 1e12
+    gemm_tops = (2.0 * M * 1024 * 23552) / (g0.elapsed_time(g1) * 1e-3) / 1e12
     peak = int8_peak_tops()
     del A, Wt, Cf
     # end to end through xdna_parakeet_encode: host mel in, host encodings out

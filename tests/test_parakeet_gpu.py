@@ -61,6 +61,9 @@ def test_gemm_i8_dequant_bit_exact(X, M, N, K, rpc):
 
 
 def test_gemm_i8_silu_and_glu(X):
+    """SiLU / GLU epilogues: the sigmoid comes from the hardware tanh (sigmoid(g) =
+    (1 + tanh(g/2)) / 2), whose absolute error is below 2^-10, so each output is within
+    1e-3 * |value input| (+1e-6) of the exact form."""
     rng = np.random.default_rng(9)
     M, N, K = 250, 512, 256
     A = rng.integers(-127, 128, (M, K), dtype=np.int8)
@@ -69,10 +72,10 @@ def test_gemm_i8_silu_and_glu(X):
     ws = np.full(N, 0.002, np.float32)
     y = (A.astype(np.int64) @ B.astype(np.int64).T).astype(np.float32) * sa[np.arange(M) // 125][:, None] * ws
     C, _ = _gemm_i8(X, A, B, sa, 125, ws, act=1)
-    np.testing.assert_allclose(C, y / (1 + np.exp(-y)), rtol=2e-6, atol=1e-6)
+    assert np.all(np.abs(C - y / (1 + np.exp(-y))) <= 1e-3 * np.abs(y) + 1e-6)
     C, _ = _gemm_i8(X, A, B, sa, 125, ws, act=3)
     want = y[:, 0::2] / (1 + np.exp(-y[:, 1::2]))
-    np.testing.assert_allclose(C, want, rtol=2e-6, atol=1e-6)
+    assert np.all(np.abs(C - want) <= 1e-3 * np.abs(y[:, 0::2]) + 1e-6)
 
 
 def _compare(got, want, cos_min=0.998, rel_max=0.1):

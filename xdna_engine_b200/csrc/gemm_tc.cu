@@ -31,9 +31,12 @@ void set_last_error_message(const std::string &m);
 
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 4 * BN * 4 + 256;
+// the int8 kernel gives one ring stage to the epilogue's output staging (8 warps x 8 KB)
+__host__ __device__ constexpr int stages_of(bool i8) { return i8 ? 3 : 4; }
+constexpr int STG_BYTES = 8 * 8192;
+__host__ __device__ constexpr int smem_of(bool i8) { return 1024 + stages_of(i8) * STAGE_BYTES + (i8 ? STG_BYTES : 0) + 4 * BN * 4 + 256; }
 constexpr int THREADS = 320;
 constexpr int EPI_THREADS = 256;
 constexpr uint64_t TIMEOUT_NS = 2000000000ull;
@@ -119,10 +122,12 @@ struct EpiBf16 {
 
 // int8 operands, s32 accumulators, the reference's dequant epilogue (rust/npu-asr/src/ctx2.rs
 // dequant_epi 1386-1411): y = (float(acc) * s_a[clip(row)]) * ws[n] (+ bias[n]), then
-// act (SiLU v * (1 / (1 + e^-v)), or GLU over interleaved column pairs (value, gate) ->
+// act (SiLU v * sigmoid(v), or GLU over interleaved column pairs (value, gate) ->
 // value * sigmoid(gate), written at column n / 2), then out = residual + alpha * y; f32 out.
 // Optionally the per-clip max |out| (the next quantisation's scale) is folded into amax[clip]
-// (atomicMax on the bit pattern: order-free and exact for non-negative floats).
+// (atomicMax on the bit pattern: order-free and exact for non-negative floats).  The kernel
+// stages each warp's 32-row output slices in shared memory and writes them with TMA stores
+// (the residual slice comes in by TMA the same way).
 struct EpiI8 {
     const float *sa;            // [clips] activation scales
     int rows_per_clip;
@@ -140,46 +145,31 @@ struct EpiI8 {
         s[j] = ws[n0 + j];
         s[BN + j] = bias ? bias[n0 + j] : 0.0f;
     }
-    __device__ __forceinline__ void apply(int row, int col, const uint32_t *r, const float *s) const {
+    // sigmoid(g) = (1 + tanh(g / 2)) / 2 with the hardware tanh (one special-function op)
+    __device__ __forceinline__ static float sigmoid(float g) {
+        float t;
+        asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
+        return fmaf(0.5f, t, 0.5f);
+    }
+    // values of row `row` for the 64 accumulator columns in r; returns how many (64, or 32 for GLU)
+    __device__ __forceinline__ int compute(int row, const uint32_t *r, const float *s, float *v) const {
         const float a = sa[row / rows_per_clip];
-        float v[64];
 #pragma unroll
         for (int j = 0; j < 64; j++) {
-            float y = __fmul_rn(__fmul_rn((float)(int)r[j], a), s[j]);
-            if (bias) y = __fadd_rn(y, s[BN + j]);
-            if (act == 1) y = __fmul_rn(y, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-y))));
-            v[j] = y;
+            float t = __fmul_rn(__fmul_rn((float)(int)r[j], a), s[j]);
+            if (bias) t = __fadd_rn(t, s[BN + j]);
+            v[j] = t;
         }
-        float m = 0.0f;
         if (act == 3) {
-            const int oc = col >> 1;
-            const float *rp = residual ? residual + (size_t)row * ldr + oc : nullptr;
-            float *op = out + (size_t)row * ldc + oc;
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                float y = __fmul_rn(v[2 * j], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[2 * j + 1]))));
-                if (rp) y = __fadd_rn(rp[j], __fmul_rn(alpha, y));
-                op[j] = y;
-                m = fmaxf(m, fabsf(y));
-            }
-        } else {
-            const float *rp = residual ? residual + (size_t)row * ldr + col : nullptr;
-            float *op = out + (size_t)row * ldc + col;
-#pragma unroll
-            for (int j = 0; j < 64; j += 4) {
-                float4 y = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                if (rp) {
-                    const float4 q = *reinterpret_cast<const float4 *>(rp + j);
-                    y.x = __fadd_rn(q.x, __fmul_rn(alpha, y.x));
-                    y.y = __fadd_rn(q.y, __fmul_rn(alpha, y.y));
-                    y.z = __fadd_rn(q.z, __fmul_rn(alpha, y.z));
-                    y.w = __fadd_rn(q.w, __fmul_rn(alpha, y.w));
-                }
-                *reinterpret_cast<float4 *>(op + j) = y;
-                m = fmaxf(m, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
-            }
+            for (int j = 0; j < 32; j++) v[j] = __fmul_rn(v[2 * j], sigmoid(v[2 * j + 1]));
+            return 32;
         }
-        if (amax) atomicMax(amax + row / rows_per_clip, __float_as_uint(m));
+        if (act == 1) {
+#pragma unroll
+            for (int j = 0; j < 64; j++) v[j] = __fmul_rn(v[j], sigmoid(v[j]));
+        }
+        return 64;
     }
 };
 
@@ -189,20 +179,24 @@ struct EpiI8 {
 // K-elements per 128-byte stage row, s32 accumulators) over kind::f16 (bf16, 64 per row).
 template <bool I8, class E>
 __global__ void __launch_bounds__(THREADS, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, int M, int N, int K,
             E epi) {
+    constexpr int STAGES = stages_of(I8);
     constexpr int KE = I8 ? 128 : 64;            // K elements per stage (128 bytes per row)
     constexpr int KI = I8 ? 32 : 16;             // K elements per MMA instruction (32 bytes)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *stA = smem;                            // [STAGES][BM][128 B], swizzled
     uint8_t *stB = smem + STAGES * A_BYTES;         // [STAGES][BN][128 B], swizzled
-    float *scol = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES);   // [2][2][BN] column params
+    uint8_t *stg = smem + STAGES * STAGE_BYTES;     // I8: [8 warps][2 boxes][32 rows][128 B], swizzled
+    float *scol = reinterpret_cast<float *>(stg + (I8 ? STG_BYTES : 0));   // [2][2][BN] column params
     uint64_t *full = reinterpret_cast<uint64_t *>(scol + 4 * BN);
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;               // [2]
     uint64_t *tempty = tfull + 2;                   // [2]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    uint64_t *rbar = tempty + 2;                    // [8] residual loads, one per epilogue warp
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(rbar + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = K / KE;
@@ -212,6 +206,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int a = 0; a < 2; a++) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], EPI_THREADS / 32); }
+        for (int a = 0; a < 8; a++) mbar_init(&rbar[a], 1);
         mbar_fence_init();
     }
     if (warp == 1) { tc::tmem_alloc(tmem_slot, 2 * BN); tc::tmem_relinquish(); }
@@ -267,6 +262,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         // 32*(warp & 3) + lane, and warp half h = (warp - 2) / 4 takes columns [128h, 128h+128)
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int et = threadIdx.x - 64;
+        float rmax = 0.0f;
+        uint32_t rph = 0;
         int i = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, i++) {
             const int acc = i & 1;
@@ -284,12 +281,61 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 tc::tmem_ld32(ta, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
                 tc::tmem_ld32(ta + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
                 tc::tmem_ld_wait();
-                if (row < M) epi.apply(row, n0 + c0, r, cs + c0);
+                if constexpr (I8) {
+                    float v[64];
+                    const int nc = epi.compute(row < M ? row : m0, r, cs + c0, v);
+                    const int oc = epi.act == 3 ? (n0 + c0) >> 1 : n0 + c0;
+                    const int r0 = m0 + 32 * q;
+                    uint8_t *sb = stg + (warp - 2) * 8192;
+                    if (lane == 0) tc::bulk_wait_read0();   // the previous slice's stores have read sb
+                    __syncwarp();
+                    if (epi.residual) {
+                        if (lane == 0) {
+                            mbar_arrive_expect_tx(&rbar[warp - 2], (uint32_t)nc * 128);
+                            for (int b = 0; b < nc / 32; b++) tc::tma_load_2d(sb + b * 4096, &tmR, oc + 32 * b, r0, &rbar[warp - 2]);
+                        }
+                        wait_bounded(&rbar[warp - 2], rph, 6u);
+                        rph ^= 1u;
+                    }
+#pragma unroll
+                    for (int b = 0; b < 2; b++) {
+                        if (b * 32 < nc) {
+#pragma unroll
+                            for (int j = 0; j < 8; j++) {
+                                float4 *p = reinterpret_cast<float4 *>(sb + b * 4096 + lane * 128 + ((j ^ (lane & 7)) << 4));
+                                float4 y = make_float4(v[32 * b + 4 * j], v[32 * b + 4 * j + 1], v[32 * b + 4 * j + 2],
+                                                       v[32 * b + 4 * j + 3]);
+                                if (epi.residual) {
+                                    const float4 rq = *p;
+                                    y.x = __fadd_rn(rq.x, __fmul_rn(epi.alpha, y.x));
+                                    y.y = __fadd_rn(rq.y, __fmul_rn(epi.alpha, y.y));
+                                    y.z = __fadd_rn(rq.z, __fmul_rn(epi.alpha, y.z));
+                                    y.w = __fadd_rn(rq.w, __fmul_rn(epi.alpha, y.w));
+                                }
+                                *p = y;
+                                rmax = fmaxf(rmax, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+                            }
+                        }
+                    }
+                    tc::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        for (int b = 0; b < nc / 32; b++) tc::tma_store_2d(&tmO, sb + b * 4096, oc + 32 * b, r0);
+                        tc::bulk_commit();
+                    }
+                } else {
+                    if (row < M) epi.apply(row, n0 + c0, r, cs + c0);
+                }
+            }
+            if constexpr (I8) {
+                if (epi.amax && row < M) atomicMax(epi.amax + row / epi.rows_per_clip, __float_as_uint(rmax));
+                rmax = 0.0f;
             }
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
         }
+        if (I8 && lane == 0) tc::bulk_wait0();   // every output store has landed before the CTA exits
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -335,20 +381,35 @@ static int sm_count() {
     return sms;
 }
 
+// f32 matrix [rows, cols] (row stride ld) as 32 x 32 boxes (128-byte rows) with 128 B swizzle:
+// the int8 epilogue's output and residual slices
+bool make_tmap_f32(CUtensorMap *tm, const void *base, int rows, int cols, int ld) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <bool I8, class E>
 cudaError_t launch_t(const void *A, int lda, const void *B, int ldb, int M, int N, int K, const E &epi,
-                     cudaStream_t st) {
+                     cudaStream_t st, const CUtensorMap &to, const CUtensorMap &tr) {
     CUtensorMap ta, tb;
     if (!make_tmap(&ta, A, M, K, lda, BM, I8) || !make_tmap(&tb, B, N, K, ldb, BN, I8)) return cudaErrorInvalidValue;
+    constexpr int smem = smem_of(I8);
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<I8, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<I8, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         attr = true;
     }
     const int tiles = (N / BN) * ((M + BM - 1) / BM);
     const int sms = sm_count();
-    gemm_kernel<I8, E><<<tiles < sms ? tiles : sms, THREADS, SMEM_BYTES, st>>>(ta, tb, M, N, K, epi);
+    gemm_kernel<I8, E><<<tiles < sms ? tiles : sms, THREADS, smem, st>>>(ta, tb, to, tr, M, N, K, epi);
     return cudaGetLastError();
 }
 
@@ -358,14 +419,20 @@ cudaError_t gemm_bf16(const uint16_t *A, int lda, const uint16_t *B, int ldb, in
                       const float *bias, const uint16_t *residual, int ldr, int act, uint16_t *C, int ldc,
                       cudaStream_t st, int res_mod, float *C_f32) {
     gemm::EpiBf16 e{bias, residual, ldr, res_mod, act, C, C_f32, ldc};
-    return gemm::launch_t<false>(A, lda, B, ldb, M, N, K, e, st);
+    CUtensorMap unused{};
+    return gemm::launch_t<false>(A, lda, B, ldb, M, N, K, e, st, unused, unused);
 }
 
 cudaError_t gemm_i8(const int8_t *A, int lda, const int8_t *B, int ldb, int M, int N, int K, const float *sa,
                     int rows_per_clip, const float *ws, const float *bias, int act, const float *residual, int ldr,
                     float alpha, float *C, int ldc, unsigned *amax, cudaStream_t st) {
     gemm::EpiI8 e{sa, rows_per_clip, ws, bias, act, residual, ldr, alpha, C, ldc, amax};
-    return gemm::launch_t<true>(A, lda, B, ldb, M, N, K, e, st);
+    const int ncols = act == 3 ? N / 2 : N;
+    CUtensorMap to, tr;
+    if (!gemm::make_tmap_f32(&to, C, M, ncols, ldc) ||
+        !gemm::make_tmap_f32(&tr, residual ? residual : C, M, ncols, residual ? ldr : ldc))
+        return cudaErrorInvalidValue;
+    return gemm::launch_t<true>(A, lda, B, ldb, M, N, K, e, st, to, tr);
 }
 
 unsigned gemm_error_and_clear() {
