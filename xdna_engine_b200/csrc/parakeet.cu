@@ -133,18 +133,19 @@ __global__ void __launch_bounds__(C) dw_s2_kernel(const uint16_t *in, int Hin, i
 // ------------------------------------------------------------ per-clip rows, cluster of 8
 // Row layout inside a warp: lane holds columns 128 j + 4 lane + e (j < 8, e < 4).
 __device__ __forceinline__ float cluster_max(float m, float *slot, cg::cluster_group &cl) {
+    // slot: 33 floats of shared memory (one per warp, [32] = this CTA's maximum)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
     if (lane == 0) slot[warp] = m;
     __syncthreads();
     if (threadIdx.x == 0) {
         float cm = 0.0f;
-        for (int w = 0; w < 8; w++) cm = fmaxf(cm, slot[w]);
-        slot[8] = cm;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) cm = fmaxf(cm, slot[w]);
+        slot[32] = cm;
     }
     cl.sync();
     float tot = 0.0f;
-    for (unsigned r = 0; r < cl.num_blocks(); r++) tot = fmaxf(tot, *cl.map_shared_rank(slot + 8, r));
+    for (unsigned r = 0; r < cl.num_blocks(); r++) tot = fmaxf(tot, *cl.map_shared_rank(slot + 32, r));
     cl.sync();   // every CTA has read every other CTA's slot before any of them moves on
     return tot;
 }
@@ -152,25 +153,30 @@ __device__ __forceinline__ float cluster_max(float m, float *slot, cg::cluster_g
 // y = LN(x) per row (ops.rs:17-35: mean, population variance, (x - mu) * inv * g + b, eps
 // 1e-5); quantise: q int8 with the clip's dynamic scale (sa[clip]), or (q == null) y f32 to
 // yf (may alias x).  Cluster of 8 CTAs per clip, each 16 rows (2 per warp).
-__global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(256)
+__global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(256, 2)
     ln_quant_kernel(const float *x, int T, const float *g, const float *bt, int8_t *q, float *sa, float *yf) {
-    __shared__ float slot[16];
+    __shared__ float slot[33];
     cg::cluster_group cl = cg::this_cluster();
     const int clip = blockIdx.x / CLUSTER, rank = blockIdx.x % CLUSTER;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float v[2][32];
     float m = 0.0f;
+    // both rows are requested before any arithmetic (one round trip)
 #pragma unroll
     for (int rr = 0; rr < 2; rr++) {
         const int t = rank * ROWS_PER_CTA + warp * 2 + rr;
-        if (t >= T) continue;
-        const float *xr = x + ((size_t)clip * T + t) * D;
-        float s = 0.0f;
+        const float *xr = x + ((size_t)clip * T + min(t, T - 1)) * D;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             const float4 a = *reinterpret_cast<const float4 *>(xr + 128 * j + 4 * lane);
             v[rr][4 * j] = a.x; v[rr][4 * j + 1] = a.y; v[rr][4 * j + 2] = a.z; v[rr][4 * j + 3] = a.w;
         }
+    }
+#pragma unroll
+    for (int rr = 0; rr < 2; rr++) {
+        const int t = rank * ROWS_PER_CTA + warp * 2 + rr;
+        if (t >= T) continue;
+        float s = 0.0f;
 #pragma unroll
         for (int i = 0; i < 32; i++) s += v[rr][i];
 #pragma unroll
@@ -183,14 +189,17 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(256)
         for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(var, (float)D), 1e-5f)));
 #pragma unroll
-        for (int j = 0; j < 8; j++)
+        for (int j = 0; j < 8; j++) {
+            const float4 g4 = *reinterpret_cast<const float4 *>(g + 128 * j + 4 * lane);
+            const float4 b4 = *reinterpret_cast<const float4 *>(bt + 128 * j + 4 * lane);
+            const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                const int col = 128 * j + 4 * lane + e;
-                const float y = (v[rr][4 * j + e] - mu) * inv * g[col] + bt[col];
+                const float y = (v[rr][4 * j + e] - mu) * inv * gv[e] + bv[e];
                 v[rr][4 * j + e] = y;
                 m = fmaxf(m, fabsf(y));
             }
+        }
         if (!q) {
             float *yr = yf + ((size_t)clip * T + t) * D;
 #pragma unroll
@@ -217,42 +226,48 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(256)
 
 // conv_module's depthwise conv (ops.rs:92-110: k 9 'same', acc = bias then + taps[j] * x
 // for valid j in order) + SiLU, then quantised with the clip's dynamic scale.  x = GLU output
-// f32 [clip*T + t][D]; thread owns channels 4 tid .. 4 tid + 3 for the CTA's 16 rows.
-__global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(256)
+// f32 [clip*T + t][D]; thread owns channels 2 tid, 2 tid + 1 for the CTA's 16 rows.
+__global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(512)
     dwconv_silu_quant_kernel(const float *x, int T, const float *taps, const float *bias, int8_t *q, float *sa) {
-    __shared__ float slot[16];
+    __shared__ float slot[33];
     cg::cluster_group cl = cg::this_cluster();
     const int clip = blockIdx.x / CLUSTER, rank = blockIdx.x % CLUSTER;
-    const int c0 = 4 * threadIdx.x;
-    float tp[4][KC];
+    const int c0 = 2 * threadIdx.x;
+    float tp[2][KC];
 #pragma unroll
-    for (int e = 0; e < 4; e++)
+    for (int e = 0; e < 2; e++)
 #pragma unroll
         for (int j = 0; j < KC; j++) tp[e][j] = taps[(c0 + e) * KC + j];
-    const float4 bb = *reinterpret_cast<const float4 *>(bias + c0);
-    float o[ROWS_PER_CTA][4];
+    const float2 bb = *reinterpret_cast<const float2 *>(bias + c0);
+    float o[ROWS_PER_CTA][2];
     float m = 0.0f;
     const float *xc = x + (size_t)clip * T * D + c0;
+    constexpr int HALO = (KC - 1) / 2, NIN = ROWS_PER_CTA + KC - 1;
+    const int t0 = rank * ROWS_PER_CTA;
+    float2 xin[NIN];      // input rows t0 - 4 .. t0 + 19, all requested up front
+#pragma unroll
+    for (int u = 0; u < NIN; u++) {
+        const int s = t0 - HALO + u;
+        xin[u] = (s >= 0 && s < T) ? *reinterpret_cast<const float2 *>(xc + (size_t)s * D) : make_float2(0.f, 0.f);
+    }
 #pragma unroll
     for (int r = 0; r < ROWS_PER_CTA; r++) {
-        const int t = rank * ROWS_PER_CTA + r;
-        float a[4] = {bb.x, bb.y, bb.z, bb.w};
+        const int t = t0 + r;
+        float a[2] = {bb.x, bb.y};
         if (t < T) {
 #pragma unroll
             for (int j = 0; j < KC; j++) {
-                const int s = t + j - (KC - 1) / 2;
+                const int s = t + j - HALO;
                 if (s < 0 || s >= T) continue;
-                const float4 xv = *reinterpret_cast<const float4 *>(xc + (size_t)s * D);
-                a[0] = __fadd_rn(a[0], __fmul_rn(tp[0][j], xv.x));
-                a[1] = __fadd_rn(a[1], __fmul_rn(tp[1][j], xv.y));
-                a[2] = __fadd_rn(a[2], __fmul_rn(tp[2][j], xv.z));
-                a[3] = __fadd_rn(a[3], __fmul_rn(tp[3][j], xv.w));
+                a[0] = __fadd_rn(a[0], __fmul_rn(tp[0][j], xin[r + j].x));
+                a[1] = __fadd_rn(a[1], __fmul_rn(tp[1][j], xin[r + j].y));
             }
-#pragma unroll
-            for (int e = 0; e < 4; e++) { a[e] = silu(a[e]); m = fmaxf(m, fabsf(a[e])); }
+            a[0] = silu(a[0]);
+            a[1] = silu(a[1]);
+            m = fmaxf(m, fmaxf(fabsf(a[0]), fabsf(a[1])));
         }
-#pragma unroll
-        for (int e = 0; e < 4; e++) o[r][e] = a[e];
+        o[r][0] = a[0];
+        o[r][1] = a[1];
     }
     const float s = quant_scale(cluster_max(m, slot, cl));
     if (rank == 0 && threadIdx.x == 0) sa[clip] = s;
@@ -260,22 +275,23 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(256)
     for (int r = 0; r < ROWS_PER_CTA; r++) {
         const int t = rank * ROWS_PER_CTA + r;
         if (t >= T) continue;
-        *reinterpret_cast<uint32_t *>(q + ((size_t)clip * T + t) * D + c0) =
-            pack_i8x4(quant_i8(o[r][0], s), quant_i8(o[r][1], s), quant_i8(o[r][2], s), quant_i8(o[r][3], s));
+        *reinterpret_cast<uint16_t *>(q + ((size_t)clip * T + t) * D + c0) =
+            (uint16_t)((quant_i8(o[r][0], s) & 255) | ((quant_i8(o[r][1], s) & 255) << 8));
     }
 }
 
 // q = quant_i8(x, s[clip]) for a GEMM-produced f32 tensor whose per-clip max |x| is in amax;
 // also records s[clip].  x [clips * T, K], K % 4 == 0.
 __global__ void quant_kernel(const float *x, int T, int K, int clips, const unsigned *amax, int8_t *q, float *sa) {
-    const size_t n4 = (size_t)clips * T * K / 4;
-    const size_t per_clip4 = (size_t)T * K / 4;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-        const int clip = (int)(i / per_clip4);
-        const float s = quant_scale(__uint_as_float(amax[clip]));
-        if (i % per_clip4 == 0) sa[clip] = s;
-        const float4 v = reinterpret_cast<const float4 *>(x)[i];
-        reinterpret_cast<uint32_t *>(q)[i] = pack_i8x4(quant_i8(v.x, s), quant_i8(v.y, s), quant_i8(v.z, s), quant_i8(v.w, s));
+    const int clip = blockIdx.y;
+    const float s = quant_scale(__uint_as_float(amax[clip]));
+    if (blockIdx.x == 0 && threadIdx.x == 0) sa[clip] = s;
+    const int n4 = T * K / 4;
+    const float4 *xs = reinterpret_cast<const float4 *>(x) + (size_t)clip * n4;
+    uint32_t *qs = reinterpret_cast<uint32_t *>(q) + (size_t)clip * n4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        const float4 v = xs[i];
+        qs[i] = pack_i8x4(quant_i8(v.x, s), quant_i8(v.y, s), quant_i8(v.z, s), quant_i8(v.w, s));
     }
 }
 
@@ -315,15 +331,26 @@ __device__ __forceinline__ uint32_t pk(float lo, float hi) { return bf16bits(lo)
 // dst_row0 + r; other rows of [dst_row0 + r_lo, dst_row0 + r_hi) zero
 __device__ __forceinline__ void load_rows_bf16(uint8_t *tile, const float *src, int ld, int r_lo, int r_hi,
                                                int nrows, int dst_row0) {
-    for (int c = threadIdx.x; c < (r_hi - r_lo) * 16; c += ATT_THREADS) {
-        const int r = r_lo + c / 16, ch = c % 16;
-        uint4 w = make_uint4(0, 0, 0, 0);
-        if (r >= 0 && r < nrows) {
-            const float4 a = *reinterpret_cast<const float4 *>(src + (size_t)r * ld + ch * 8);
-            const float4 b = *reinterpret_cast<const float4 *>(src + (size_t)r * ld + ch * 8 + 4);
-            w = make_uint4(pk(a.x, a.y), pk(a.z, a.w), pk(b.x, b.y), pk(b.z, b.w));
+    // 8 pieces (16 floats each) per thread in flight before any is converted
+    const int n = (r_hi - r_lo) * 16;
+    for (int c0 = threadIdx.x; c0 < n; c0 += 8 * ATT_THREADS) {
+        float4 a[8], b[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int c = c0 + u * ATT_THREADS, r = r_lo + c / 16, ch = c % 16;
+            a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (c < n && r >= 0 && r < nrows) {
+                a[u] = *reinterpret_cast<const float4 *>(src + (size_t)r * ld + ch * 8);
+                b[u] = *reinterpret_cast<const float4 *>(src + (size_t)r * ld + ch * 8 + 4);
+            }
         }
-        *reinterpret_cast<uint4 *>(tile + swz256(dst_row0 + r, ch)) = w;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int c = c0 + u * ATT_THREADS, r = r_lo + c / 16, ch = c % 16;
+            if (c < n)
+                *reinterpret_cast<uint4 *>(tile + swz256(dst_row0 + r, ch)) =
+                    make_uint4(pk(a[u].x, a[u].y), pk(a[u].z, a[u].w), pk(b[u].x, b[u].y), pk(b[u].z, b[u].w));
+        }
     }
 }
 
@@ -576,7 +603,7 @@ cudaError_t lin(XdnaParakeet *m, const XdnaParakeet::Lin &L, int M, int N, int K
     return gemm_i8(m->q8, K, L.q, K, M, N, K, m->sa, m->T, L.s, nullptr, act, res, ldc, alpha, out, ldc, amax, st);
 }
 cudaError_t quant(XdnaParakeet *m, const float *src, int K, int B, cudaStream_t st) {
-    parakeet::quant_kernel<<<148 * 8, 256, 0, st>>>(src, m->T, K, B, m->amax, m->q8, m->sa);
+    parakeet::quant_kernel<<<dim3(std::max(1, 148 * 8 / B), B), 256, 0, st>>>(src, m->T, K, B, m->amax, m->q8, m->sa);
     return cudaGetLastError();
 }
 cudaError_t ffn(XdnaParakeet *m, const float *ln, const XdnaParakeet::Lin &a, const XdnaParakeet::Lin &b, int B,
@@ -773,7 +800,7 @@ int xdna_parakeet_encode_device(XdnaParakeet *m, const float *mel_dev, int B, fl
         // conv module
         run_ln(m, L.ln_conv, B, true, st);
         if ((e = lin(m, L.pw1, M, 2 * kD, kD, 3, nullptr, 1.0f, m->ctx, nullptr, st))) break;
-        parakeet::dwconv_silu_quant_kernel<<<B * parakeet::CLUSTER, 256, 0, st>>>(m->ctx, T, L.dw_w, L.dw_b, m->q8,
+        parakeet::dwconv_silu_quant_kernel<<<B * parakeet::CLUSTER, 512, 0, st>>>(m->ctx, T, L.dw_w, L.dw_b, m->q8,
                                                                                  m->sa);
         if ((e = lin(m, L.pw2, M, kD, kD, 0, m->x, 1.0f, m->x, nullptr, st))) break;
         if ((e = ffn(m, L.ln_ff2, L.ff2a, L.ff2b, B, st))) break;
