@@ -66,50 +66,67 @@ __device__ __forceinline__ uint32_t pack_i8x4(int a, int b, int c, int d) {
 }
 
 // ------------------------------------------------------------------------------ subsample
-// out2[b][h2][w2][c] (bf16, channels last) = conv.2(relu(conv.0(mel^T)))[c][h2][w2]: conv.0 is
-// recomputed for the 3 x 3 window each conv.2 output reads (its input is one channel).  The
-// accumulations follow conv2d of ops.rs: bias first, taps in (i, j) order, zero taps skipped.
-// One CTA per (b, h2, w2 block of 4), one thread per channel.
+// out2[b][h2][w2][c] (bf16, channels last) = conv.2(relu(conv.0(mel^T)))[c][h2][w2].  One CTA
+// per (b, 2 rows of h2, 8 columns of w2), one thread per channel: the thread first computes
+// the 5 x 17 conv.0 outputs its 16 conv.2 outputs read (conv.0 has one input channel, so this
+// is cheap), keeps them in registers, then applies conv.2.  The accumulations follow conv2d of
+// ops.rs: bias first, then + w * x tap by tap in (i, j) order; conv.0's zero padding of the
+// input is in the staged patch (adding w * 0 leaves a finite sum unchanged, the same as the
+// reference's skipped taps), conv.2 skips conv.0 positions outside the image.
+constexpr int SH = 2, SW = 8;                                  // conv.2 outputs per CTA
+constexpr int PH = 4 * SH + 3, PW = 4 * SW + 3;                // mel patch (time x freq)
+constexpr int C0H = 2 * SH + 1, C0W = 2 * SW + 1;              // conv.0 outputs per thread
 __global__ void __launch_bounds__(C) sub_conv02_kernel(const float *mel, int NM, int T0, int H1, int W1, int H2,
                                                        int W2, const float *w0, const float *b0, const float *w2,
                                                        const float *b2, uint16_t *out) {
-    __shared__ float patch[7][4 * 4 + 3];   // mel[t = 4h2-3 .. 4h2+3][f = 4*w2_0-3 .. ]
-    const int wb = blockIdx.x, h2 = blockIdx.y, b = blockIdx.z, c = threadIdx.x;
-    const int w2_0 = wb * 4;
+    __shared__ float patch[PH][PW];
+    const int h2_0 = blockIdx.y * SH, w2_0 = blockIdx.x * SW, b = blockIdx.z, c = threadIdx.x;
+    const int t_0 = 4 * h2_0 - 3, f_0 = 4 * w2_0 - 3;           // patch origin
     const float *m = mel + (size_t)b * NM * T0;
-    for (int i = threadIdx.x; i < 7 * 19; i += C) {
-        const int pt = i / 19, pf = i % 19;
-        const int t = 4 * h2 - 3 + pt, f = 4 * w2_0 - 3 + pf;
-        patch[pt][pf] = (t >= 0 && t < T0 && f >= 0 && f < NM) ? m[(size_t)f * T0 + t] : 0.0f;
+    for (int i = threadIdx.x; i < PH * PW; i += C) {
+        const int t = t_0 + i / PW, f = f_0 + i % PW;
+        patch[i / PW][i % PW] = (t >= 0 && t < T0 && f >= 0 && f < NM) ? m[(size_t)f * T0 + t] : 0.0f;
     }
     __syncthreads();
-    float k0[9], k2[9];
+    float k0[9];
 #pragma unroll
-    for (int i = 0; i < 9; i++) { k0[i] = w0[c * 9 + i]; k2[i] = w2[c * 9 + i]; }
-    const float bias0 = b0[c], bias2 = b2[c];
-    for (int wi = 0; wi < 4; wi++) {
-        const int ow = w2_0 + wi;
-        if (ow >= W2) break;
-        float acc2 = bias2;
+    for (int i = 0; i < 9; i++) k0[i] = w0[c * 9 + i];
+    const float bias0 = b0[c];
+    // conv.0 output (h1, w1) = (2 h2_0 - 1 + u, 2 w2_0 - 1 + v); its taps read patch rows 2u + i
+    // and columns 2v + j
+    float a0[C0H][C0W];
 #pragma unroll
-        for (int i = 0; i < 3; i++)
+    for (int u = 0; u < C0H; u++)
 #pragma unroll
-            for (int j = 0; j < 3; j++) {
-                const int h1 = 2 * h2 + i - 1, w1 = 2 * ow + j - 1;
-                if (h1 < 0 || h1 >= H1 || w1 < 0 || w1 >= W1 || k2[3 * i + j] == 0.0f) continue;
-                float acc0 = bias0;
+        for (int v = 0; v < C0W; v++) {
+            float acc = bias0;
 #pragma unroll
-                for (int u = 0; u < 3; u++)
+            for (int i = 0; i < 3; i++)
 #pragma unroll
-                    for (int v = 0; v < 3; v++) {
-                        const int t = 2 * h1 + u - 1, f = 2 * w1 + v - 1;
-                        if (t < 0 || t >= T0 || f < 0 || f >= NM || k0[3 * u + v] == 0.0f) continue;
-                        acc0 = __fadd_rn(acc0, __fmul_rn(k0[3 * u + v], patch[t - (4 * h2 - 3)][f - (4 * w2_0 - 3)]));
-                    }
-                acc2 = __fadd_rn(acc2, __fmul_rn(k2[3 * i + j], fmaxf(acc0, 0.0f)));
-            }
-        out[(((size_t)b * H2 + h2) * W2 + ow) * C + c] = (uint16_t)bf16bits(acc2);
-    }
+                for (int j = 0; j < 3; j++) acc = __fadd_rn(acc, __fmul_rn(k0[3 * i + j], patch[2 * u + i][2 * v + j]));
+            const int h1 = 2 * h2_0 - 1 + u, w1 = 2 * w2_0 - 1 + v;
+            a0[u][v] = (h1 >= 0 && h1 < H1 && w1 >= 0 && w1 < W1) ? fmaxf(acc, 0.0f) : 0.0f;
+        }
+    float k2[9];
+#pragma unroll
+    for (int i = 0; i < 9; i++) k2[i] = w2[c * 9 + i];
+    const float bias2 = b2[c];
+#pragma unroll
+    for (int oh = 0; oh < SH; oh++)
+#pragma unroll
+        for (int ow = 0; ow < SW; ow++) {
+            const int h2 = h2_0 + oh, w2o = w2_0 + ow;
+            float acc = bias2;
+#pragma unroll
+            for (int i = 0; i < 3; i++)
+#pragma unroll
+                for (int j = 0; j < 3; j++) {
+                    const int h1 = 2 * h2 + i - 1, w1 = 2 * w2o + j - 1;
+                    if (h1 < 0 || h1 >= H1 || w1 < 0 || w1 >= W1) continue;
+                    acc = __fadd_rn(acc, __fmul_rn(k2[3 * i + j], a0[2 * oh + i][2 * ow + j]));
+                }
+            if (h2 < H2 && w2o < W2) out[(((size_t)b * H2 + h2) * W2 + w2o) * C + c] = (uint16_t)bf16bits(acc);
+        }
 }
 
 // depthwise k3 s2 p1 over channels-last bf16 [b][hin][win][C] -> [b][hout][wout][C]
@@ -585,7 +602,20 @@ struct XdnaParakeet {
     unsigned *amax = nullptr;
     uint16_t *a2 = nullptr, *a3 = nullptr, *a5 = nullptr, *a6 = nullptr;
     std::vector<void *> owned;
+    // replay graphs of the whole forward, one per (batch, input, output) seen twice
+    struct Graph {
+        int B;
+        const float *mel;
+        float *out;
+        int calls;
+        cudaGraphExec_t exec;
+    };
+    std::vector<Graph> graphs;
+    cudaStream_t cap = nullptr;
     ~XdnaParakeet() {
+        for (auto &g : graphs)
+            if (g.exec) cudaGraphExecDestroy(g.exec);
+        if (cap) cudaStreamDestroy(cap);
         for (void *p : owned) cudaFree(p);
     }
 };
@@ -765,17 +795,14 @@ void xdna_parakeet_free(XdnaParakeet *m) {
 
 int xdna_parakeet_frames_out(const XdnaParakeet *m) { return m ? m->T : -1; }
 
-int xdna_parakeet_encode_device(XdnaParakeet *m, const float *mel_dev, int B, float *out_dev, void *stream) {
-    if (!m || !mel_dev || !out_dev) { set_last_error_message("xdna_parakeet_encode_device: null pointer"); return -1; }
-    if (B < 1 || B > m->max_batch) {
-        set_last_error_message("xdna_parakeet_encode_device: batch beyond max_batch");
-        return -1;
-    }
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+}  // extern "C"
+
+// the forward's ~500 launches, in stream order on st
+static int parakeet_enqueue(XdnaParakeet *m, const float *mel_dev, int B, float *out_dev, cudaStream_t st) {
     const int T = m->T, M = B * T, NM = m->cfg.n_mels, T0 = m->cfg.n_frames;
     cudaError_t e = cudaSuccess;
     // ---- subsample
-    parakeet::sub_conv02_kernel<<<dim3((m->W2 + 3) / 4, m->H2, B), kC, 0, st>>>(
+    parakeet::sub_conv02_kernel<<<dim3((m->W2 + parakeet::SW - 1) / parakeet::SW, (m->H2 + parakeet::SH - 1) / parakeet::SH, B), kC, 0, st>>>(
         mel_dev, NM, T0, m->H1, m->W1, m->H2, m->W2, m->c0w, m->c0b, m->c2w, m->c2b, m->a2);
     const int R2 = B * m->H2 * m->W2, R3 = B * T * m->W3;
     e = gemm_bf16(m->a2, kC, m->c3w, kC, R2, kC, kC, m->c3b, nullptr, 0, 2, m->a3, kC, st);
@@ -809,6 +836,53 @@ int xdna_parakeet_encode_device(XdnaParakeet *m, const float *mel_dev, int B, fl
     if (!e) e = cudaMemcpyAsync(out_dev, m->x, sizeof(float) * (size_t)M * kD, cudaMemcpyDeviceToDevice, st);
     if (!e) e = cudaGetLastError();
     if (e != cudaSuccess) {
+        set_last_error_message(std::string("xdna_parakeet_encode_device: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+extern "C" {
+
+// The second call with the same (batch, input, output) captures the forward into a CUDA graph
+// on a private stream; that call and later ones replay it on `stream` (one launch instead of
+// ~500).  The first call runs eagerly, so every kernel attribute is set before any capture.
+int xdna_parakeet_encode_device(XdnaParakeet *m, const float *mel_dev, int B, float *out_dev, void *stream) {
+    if (!m || !mel_dev || !out_dev) { set_last_error_message("xdna_parakeet_encode_device: null pointer"); return -1; }
+    if (B < 1 || B > m->max_batch) {
+        set_last_error_message("xdna_parakeet_encode_device: batch beyond max_batch");
+        return -1;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    XdnaParakeet::Graph *g = nullptr;
+    for (auto &x : m->graphs)
+        if (x.B == B && x.mel == mel_dev && x.out == out_dev) g = &x;
+    if (!g) {
+        m->graphs.push_back({B, mel_dev, out_dev, 0, nullptr});
+        g = &m->graphs.back();
+    }
+    if (g->calls++ == 0) return parakeet_enqueue(m, mel_dev, B, out_dev, st);
+    if (!g->exec) {
+        cudaError_t e = m->cap ? cudaSuccess : cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking);
+        cudaGraph_t graph = nullptr;
+        if (!e) e = cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal);
+        if (e) {
+            set_last_error_message(std::string("xdna_parakeet_encode_device: capture: ") + cudaGetErrorString(e));
+            return -1;
+        }
+        const int rc = parakeet_enqueue(m, mel_dev, B, out_dev, m->cap);
+        e = cudaStreamEndCapture(m->cap, &graph);
+        if (rc != 0) { if (graph) cudaGraphDestroy(graph); return -1; }
+        if (!e) e = cudaGraphInstantiate(&g->exec, graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+        if (e) {
+            g->exec = nullptr;
+            set_last_error_message(std::string("xdna_parakeet_encode_device: graph: ") + cudaGetErrorString(e));
+            return -1;
+        }
+    }
+    const cudaError_t e = cudaGraphLaunch(g->exec, st);
+    if (e) {
         set_last_error_message(std::string("xdna_parakeet_encode_device: ") + cudaGetErrorString(e));
         return -1;
     }
