@@ -204,6 +204,26 @@ void or_dwconv1d(const float *x, int C, int T, const float *taps, const float *b
 void or_rel_shift(const float *bd, int H, int T, float *out);
 void or_rel_pos_encoding(int T, int D, float *pe);
 
+/* ---- Whisper-small greedy decoder (rust/npu-engine/src/asr/whisper_decoder.rs:388-560) ---- */
+typedef struct {
+    int n_layers, d_model, n_heads, ffn, vocab, max_tgt, n_enc;
+} or_whisper_dec_cfg;
+typedef struct {               /* linear weights [K, N] = [in, out] */
+    const float *ln_self_w, *ln_self_b, *q_w, *q_b, *k_w, *k_b, *v_w, *v_b, *out_w, *out_b;
+    const float *ln_cross_w, *ln_cross_b, *cross_q_w, *cross_q_b, *cross_k_w, *cross_k_b;
+    const float *cross_v_w, *cross_v_b, *cross_out_w, *cross_out_b;
+    const float *ln_final_w, *ln_final_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+} or_whisper_dec_layer;
+typedef struct {
+    const float *embed_tokens, *embed_positions, *proj_out, *ln_post_w, *ln_post_b;  /* proj_out [D, V] */
+    const or_whisper_dec_layer *layers;
+} or_whisper_dec_weights;
+/* enc [B][n_enc][d_model]; the same prompt for every stream; out_tokens [B][n_new],
+ * logits (nullable) [B][n_new][vocab] */
+int or_whisper_decode(const or_whisper_dec_cfg *c, const or_whisper_dec_weights *w, const float *enc, int B,
+                      const int64_t *prompt, int n_prompt, int n_new, int64_t *out_tokens, float *logits,
+                      int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,6 +85,9 @@ def lib():
         L.or_dwconv1d.argtypes = [F32P, C.c_int, C.c_int, F32P, F32P, C.c_int, F32P]
         L.or_rel_shift.argtypes = [F32P, C.c_int, C.c_int, F32P]
         L.or_rel_pos_encoding.argtypes = [C.c_int, C.c_int, F32P]
+        L.or_whisper_decode.argtypes = [C.c_void_p, C.c_void_p, F32P, C.c_int, C.c_void_p, C.c_int, C.c_int,
+                                        C.c_void_p, C.c_void_p, C.c_int]
+        L.or_whisper_decode.restype = C.c_int
         L.or_opt_step.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_void_p]
         L.or_opt_step.restype = C.c_int64
         L.or_opt_qweight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.POINTER(C.c_float))]
@@ -450,3 +453,51 @@ def rel_pos_encoding(T, D):
     pe = np.empty((2 * T - 1, D), np.float32)
     lib().or_rel_pos_encoding(T, D, pe.ravel())
     return pe
+
+
+# ---------------------------------------------------------------- Whisper-small decoder
+_WDEC_LAYER = ("ln_self_w", "ln_self_b", "q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "out_w", "out_b",
+               "ln_cross_w", "ln_cross_b", "cross_q_w", "cross_q_b", "cross_k_w", "cross_k_b",
+               "cross_v_w", "cross_v_b", "cross_out_w", "cross_out_b",
+               "ln_final_w", "ln_final_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b")
+_WDEC_TOP = ("embed_tokens", "embed_positions", "proj_out", "ln_post_w", "ln_post_b")
+
+
+class _WDecCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d_model", "n_heads", "ffn", "vocab", "max_tgt", "n_enc")]
+
+
+class _WDecLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _WDEC_LAYER]
+
+
+class _WDecWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _WDEC_TOP + ("layers",)]
+
+
+def whisper_decode(cfg, w, enc, prompt, n_new, want_logits=False, nthreads=None):
+    """or_whisper_decode: greedy decode of B streams (enc [B, n_enc, D]) after a shared prompt."""
+    keep = []
+
+    def p(a):
+        a = _f32(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    c = _WDecCfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.ffn, cfg.vocab, cfg.max_tgt, cfg.n_enc)
+    layers = (_WDecLayer * cfg.n_layers)()
+    for i, ly in enumerate(w["layers"][:cfg.n_layers]):
+        for n in _WDEC_LAYER:
+            setattr(layers[i], n, p(ly[n]))
+    ww = _WDecWeights(*[p(w[n]) for n in _WDEC_TOP], C.addressof(layers))
+    enc = _f32(enc)
+    B = enc.shape[0]
+    pr = np.ascontiguousarray(prompt, np.int64)
+    toks = np.empty((B, n_new), np.int64)
+    lg = np.empty((B, n_new, cfg.vocab), np.float32) if want_logits else None
+    rc = lib().or_whisper_decode(C.addressof(c), C.addressof(ww), enc.ravel(), B, pr.ctypes.data, len(pr), n_new,
+                                 toks.ctypes.data, lg.ctypes.data if lg is not None else None,
+                                 nthreads or os.cpu_count() or 1)
+    if rc != 0:
+        raise ValueError("or_whisper_decode: prompt + new tokens beyond max_tgt")
+    return (toks, lg) if want_logits else toks

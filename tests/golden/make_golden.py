@@ -231,6 +231,64 @@ def whisper_hf_fixture():
     print("whisper_hf_golden.npz:", enc.shape)
 
 
+WHISPER_DEC_SMALL = dict(n_layers=2, d_model=64, n_heads=2, ffn=128, vocab=300, max_tgt=40, n_enc=24)
+WHISPER_DEC_SEED = 13
+WHISPER_DEC_PROMPT = [1, 5, 7]
+
+
+def whisper_dec_small():
+    from xdna_engine_b200.synth import WhisperDecConfig, make_whisper_dec_weights, make_encoder_states
+    cfg = WhisperDecConfig(**WHISPER_DEC_SMALL)
+    w = make_whisper_dec_weights(cfg, seed=WHISPER_DEC_SEED, std=0.2, bias_std=0.05, ln_std=0.1)
+    return cfg, w, make_encoder_states(cfg, 2, WHISPER_DEC_SEED)
+
+
+def whisper_dec_hf_fixture():
+    """HF WhisperDecoder + the tied proj_out (the model whisper_decoder.rs restates) on a small
+    seeded decoder: greedy tokens and per-step logits for 2 streams after a 3-token prompt,
+    recomputing the whole sequence each step (no cache)."""
+    import torch
+    from transformers import WhisperConfig
+    from transformers.models.whisper.modeling_whisper import WhisperDecoder
+    cfg, w, enc = whisper_dec_small()
+    hc = WhisperConfig(d_model=cfg.d_model, decoder_layers=cfg.n_layers, decoder_attention_heads=cfg.n_heads,
+                       decoder_ffn_dim=cfg.ffn, vocab_size=cfg.vocab, max_target_positions=cfg.max_tgt,
+                       max_source_positions=cfg.n_enc, activation_function="gelu", dropout=0.0,
+                       attention_dropout=0.0, activation_dropout=0.0, pad_token_id=0)
+    model = WhisperDecoder(hc).eval().float()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    sd = {"embed_tokens.weight": t(w["embed_tokens"]), "embed_positions.weight": t(w["embed_positions"]),
+          "layer_norm.weight": t(w["ln_post_w"]), "layer_norm.bias": t(w["ln_post_b"])}
+    names = {"q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj", "out": "self_attn.out_proj",
+             "cross_q": "encoder_attn.q_proj", "cross_k": "encoder_attn.k_proj", "cross_v": "encoder_attn.v_proj",
+             "cross_out": "encoder_attn.out_proj", "fc1": "fc1", "fc2": "fc2"}
+    for i, ly in enumerate(w["layers"]):
+        p = f"layers.{i}."
+        for k, n in names.items():
+            sd[p + n + ".weight"] = t(ly[k + "_w"].T)
+            if k not in ("k", "cross_k"):
+                sd[p + n + ".bias"] = t(ly[k + "_b"])
+        for a, b in (("ln_self", "self_attn_layer_norm"), ("ln_cross", "encoder_attn_layer_norm"),
+                     ("ln_final", "final_layer_norm")):
+            sd[p + b + ".weight"] = t(ly[a + "_w"])
+            sd[p + b + ".bias"] = t(ly[a + "_b"])
+    model.load_state_dict(sd, strict=True)
+    n_new = 12
+    toks = np.zeros((2, n_new), np.int64)
+    lgs = np.zeros((2, n_new, cfg.vocab), np.float32)
+    with torch.no_grad():
+        for b in range(2):
+            seq = list(WHISPER_DEC_PROMPT)
+            for s in range(n_new):
+                h = model(input_ids=torch.tensor([seq]), encoder_hidden_states=t(enc[b:b + 1])).last_hidden_state
+                lg = (h[0, -1] @ t(w["embed_tokens"]).T).numpy()
+                lgs[b, s] = lg
+                toks[b, s] = int(np.argmax(lg))
+                seq.append(int(toks[b, s]))
+    np.savez_compressed(os.path.join(HERE, "whisper_dec_hf_golden.npz"), tokens=toks, logits=lgs)
+    print("whisper_dec_hf_golden.npz:", toks.tolist())
+
+
 def _load_ref_module(rel, name):
     spec = importlib.util.spec_from_file_location(name, os.path.join(REF, rel))
     mod = importlib.util.module_from_spec(spec)
@@ -280,6 +338,8 @@ def parakeet_fixture():
 if __name__ == "__main__":
     import sys
     only = set(sys.argv[1:])
+    if not only or "whisper_dec" in only:
+        whisper_dec_hf_fixture()
     if not only or "parakeet" in only:
         parakeet_fixture()
     if not only or "bfp16" in only:

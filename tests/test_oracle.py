@@ -354,3 +354,16 @@ def test_parakeet_oracle_int8_tracks_f32():
     b = O.parakeet_encode(cfg, w, mel, int8=False)
     cos = (a * b).sum(-1) / np.linalg.norm(a, axis=-1) / np.linalg.norm(b, axis=-1)
     assert a.shape == (1, 15, 1024) and cos.min() > 0.999
+
+
+def test_whisper_decoder_oracle_matches_hf_golden():
+    """or_whisper_decode (HostDecoder::step restated) vs HF WhisperDecoder + tied proj_out:
+    the same greedy tokens, logits to 1e-4 (A&S erf in GELU vs the exact erf)."""
+    import sys
+    sys.path.insert(0, GOLD)
+    import make_golden as G
+    cfg, w, enc = G.whisper_dec_small()
+    f = np.load(os.path.join(GOLD, "whisper_dec_hf_golden.npz"))
+    toks, lg = O.whisper_decode(cfg, w, enc, G.WHISPER_DEC_PROMPT, 12, want_logits=True, nthreads=2)
+    np.testing.assert_array_equal(toks, f["tokens"])
+    np.testing.assert_allclose(lg, f["logits"], atol=1e-4, rtol=0)

@@ -292,3 +292,61 @@ def make_parakeet_mel(cfg: ParakeetConfig = PARAKEET_V3, batch: int = 1, seed: i
     """Synthetic log-mel input ~N(0, 1), [batch, n_mels, n_frames]."""
     rng = np.random.default_rng(seed + 7_000_003)
     return rng.standard_normal((batch, cfg.n_mels, cfg.n_frames), dtype=np.float32)
+
+
+# ------------------------------------------------------------------- Whisper-small decoder
+@dataclass(frozen=True)
+class WhisperDecConfig:
+    n_layers: int = 12
+    d_model: int = 768
+    n_heads: int = 12
+    ffn: int = 3072
+    vocab: int = 51865
+    max_tgt: int = 448
+    n_enc: int = 1500
+
+
+WHISPER_SMALL_DEC = WhisperDecConfig()
+# start-of-transcript, language (en), transcribe, no-timestamps: the greedy decode's forced prefix
+WHISPER_PROMPT = (50258, 50259, 50359, 50363)
+
+
+def make_whisper_dec_weights(cfg: WhisperDecConfig = WHISPER_SMALL_DEC, seed: int = 0, std: float = 0.02,
+                             bias_std: float = 0.0, ln_std: float = 0.0) -> dict:
+    """Random-init Whisper decoder weights (f32; linear weights [K, N] = [in, out]; k biases 0;
+    proj_out tied to embed_tokens as in the checkpoint)."""
+    rng = np.random.default_rng(seed)
+    D, F, V = cfg.d_model, cfg.ffn, cfg.vocab
+
+    def normal(shape, s):
+        a = rng.standard_normal(shape, dtype=np.float32)
+        a *= np.float32(s)
+        return a
+
+    def vec(n, base, s):
+        if s == 0.0:
+            return np.full(n, base, np.float32)
+        return (np.float32(base) + rng.standard_normal(n, dtype=np.float32) * np.float32(s)).astype(np.float32)
+
+    emb = normal((V, D), std)
+    w = {"embed_tokens": emb, "embed_positions": normal((cfg.max_tgt, D), std),
+         "proj_out": np.ascontiguousarray(emb.T), "ln_post_w": vec(D, 1.0, ln_std), "ln_post_b": vec(D, 0.0, ln_std)}
+    layers = []
+    for _ in range(cfg.n_layers):
+        ly = {}
+        for p in ("ln_self", "ln_cross", "ln_final"):
+            ly[p + "_w"], ly[p + "_b"] = vec(D, 1.0, ln_std), vec(D, 0.0, ln_std)
+        for n in ("q", "k", "v", "out", "cross_q", "cross_k", "cross_v", "cross_out"):
+            ly[n + "_w"] = normal((D, D), std)
+            ly[n + "_b"] = np.zeros(D, np.float32) if n in ("k", "cross_k") else vec(D, 0.0, bias_std)
+        ly["fc1_w"], ly["fc1_b"] = normal((D, F), std), vec(F, 0.0, bias_std)
+        ly["fc2_w"], ly["fc2_b"] = normal((F, D), std), vec(D, 0.0, bias_std)
+        layers.append(ly)
+    w["layers"] = layers
+    return w
+
+
+def make_encoder_states(cfg: WhisperDecConfig = WHISPER_SMALL_DEC, batch: int = 1, seed: int = 0) -> np.ndarray:
+    """Synthetic encoder output (the decoder's cross-attention input) ~N(0, 1), [batch, n_enc, D]."""
+    rng = np.random.default_rng(seed + 5_000_017)
+    return rng.standard_normal((batch, cfg.n_enc, cfg.d_model), dtype=np.float32)
