@@ -247,6 +247,45 @@ int xdna_opt_set_trace(XdnaOptDecoder *dec, float *trace_dev);
  * outputs are published, 5*n_layers + 1 after the LM head, + 2 once the greedy id is known). */
 int xdna_opt_set_timing(XdnaOptDecoder *dec, unsigned long long *timing_dev);
 
+/* ------------------------------------------- Whisper-small greedy decoder (HostDecoder) */
+/* Replaces rust/npu-engine/src/asr/whisper_decoder.rs HostDecoder (precompute_cross 388-399,
+ * step 401-560) and the fused per-token decode ELF (route_b_kernels/decode_fused/gen_decode.py)
+ * with the device lm-head + argmax (gen_projout.py, argmax_slice.cc; whisper.rs:749-757 first
+ * maximum).  Linear weights and proj_out are quantised to the reference's bfp16 blocks
+ * (golden_ffn_gemm.py:34-49) along K.  1..32 streams decode in lockstep after one shared
+ * prompt.  Shapes: d_model 768, 12 heads, ffn 3072, max_tgt <= 448. */
+typedef struct {
+    int n_layers, d_model, n_heads, ffn, vocab, max_tgt, n_enc;
+} XdnaWhisperDecConfig;
+typedef struct {               /* f32; linear weights [K, N] = [in, out]; k biases may be NULL */
+    const float *ln_self_w, *ln_self_b, *q_w, *q_b, *k_w, *k_b, *v_w, *v_b, *out_w, *out_b;
+    const float *ln_cross_w, *ln_cross_b, *cross_q_w, *cross_q_b, *cross_k_w, *cross_k_b;
+    const float *cross_v_w, *cross_v_b, *cross_out_w, *cross_out_b;
+    const float *ln_final_w, *ln_final_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+} XdnaWhisperDecLayer;
+typedef struct {
+    const float *embed_tokens, *embed_positions, *proj_out, *ln_post_w, *ln_post_b;  /* proj_out [D, vocab] */
+    const XdnaWhisperDecLayer *layers;
+} XdnaWhisperDecWeights;
+typedef struct XdnaWhisperDec XdnaWhisperDec;
+XdnaWhisperDec *xdna_whisper_dec_create(XdnaDevice *dev, const XdnaWhisperDecConfig *cfg,
+                                        const XdnaWhisperDecWeights *w, int max_batch);
+void xdna_whisper_dec_free(XdnaWhisperDec *m);
+/* bfp16 blocks that held both mantissa +128 and -128 (stored with +128 as 127; 0 in practice) */
+long long xdna_whisper_dec_clamped_blocks(const XdnaWhisperDec *m);
+/* cross K/V of every layer from encoder states enc_dev [B][n_enc][768] f32 (device); async */
+int xdna_whisper_dec_set_encoder(XdnaWhisperDec *m, const float *enc_dev, int B, void *stream);
+/* greedy decode of n_new tokens per stream after the prompt (host array); tokens_dev [B][n_new],
+ * logits_dev [B][n_new][vocab] (nullable), both device; async on `stream` after a short
+ * synchronous staging of the prompt.  The first run of a shape records a CUDA graph of one
+ * token, later runs replay it per token. */
+int xdna_whisper_dec_run(XdnaWhisperDec *m, int B, const int64_t *prompt_host, int n_prompt, int n_new,
+                         int64_t *tokens_dev, float *logits_dev, void *stream);
+/* host in / host out: encoder states enc [B][n_enc][768] f32 -> tokens [B][n_new] (+ logits,
+ * nullable, [B][n_new][vocab]).  Synchronous. */
+int xdna_whisper_dec_generate(XdnaWhisperDec *m, const float *enc_host, int B, const int64_t *prompt, int n_prompt,
+                              int n_new, int64_t *tokens_host, float *logits_host);
+
 /* ------------------------------------ Parakeet FastConformer encoder (FastConformerEncoder) */
 /* Replaces rust/npu-parakeet/src/encoder.rs FastConformerEncoder::subsample (200-237) +
  * forward_last (657-665) with every weight linear on the int8 GEMM engine (the reference's

@@ -17,7 +17,9 @@ import numpy as np
 from .synth import (OPT_125M, OptConfig, make_opt_weights, make_prompt,  # noqa: F401
                     BGE_BASE, BertConfig, make_bert_weights, make_bge_batch,
                     WHISPER_SMALL_ENC, WhisperEncConfig, make_whisper_enc_weights, make_mel,
-                    PARAKEET_V3, ParakeetConfig, make_parakeet_weights, make_parakeet_mel)
+                    PARAKEET_V3, ParakeetConfig, make_parakeet_weights, make_parakeet_mel,
+                    WHISPER_SMALL_DEC, WhisperDecConfig, make_whisper_dec_weights, make_encoder_states,
+                    WHISPER_PROMPT)
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libxdna_b200.so")
@@ -96,6 +98,17 @@ def lib():
         L.xdna_parakeet_encode.restype = i
         L.xdna_parakeet_encode_device.argtypes = [vp, vp, i, vp, vp]
         L.xdna_parakeet_encode_device.restype = i
+        L.xdna_whisper_dec_create.argtypes = [vp, vp, vp, i]
+        L.xdna_whisper_dec_create.restype = vp
+        L.xdna_whisper_dec_free.argtypes = [vp]
+        L.xdna_whisper_dec_clamped_blocks.argtypes = [vp]
+        L.xdna_whisper_dec_clamped_blocks.restype = C.c_longlong
+        L.xdna_whisper_dec_set_encoder.argtypes = [vp, vp, i, vp]
+        L.xdna_whisper_dec_set_encoder.restype = i
+        L.xdna_whisper_dec_run.argtypes = [vp, i, vp, i, i, vp, vp, vp]
+        L.xdna_whisper_dec_run.restype = i
+        L.xdna_whisper_dec_generate.argtypes = [vp, vp, i, vp, i, i, vp, vp]
+        L.xdna_whisper_dec_generate.restype = i
         L.xdna_opt_create.argtypes = [vp, vp, vp, i, i]
         L.xdna_opt_create.restype = vp
         L.xdna_opt_free.argtypes = [vp]
@@ -446,6 +459,74 @@ class ParakeetEncoder:
     def close(self):
         if getattr(self, "handle", None):
             lib().xdna_parakeet_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_WDEC_LAYER = ("ln_self_w", "ln_self_b", "q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "out_w", "out_b",
+               "ln_cross_w", "ln_cross_b", "cross_q_w", "cross_q_b", "cross_k_w", "cross_k_b",
+               "cross_v_w", "cross_v_b", "cross_out_w", "cross_out_b",
+               "ln_final_w", "ln_final_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b")
+_WDEC_TOP = ("embed_tokens", "embed_positions", "proj_out", "ln_post_w", "ln_post_b")
+
+
+class _WDecCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d_model", "n_heads", "ffn", "vocab", "max_tgt", "n_enc")]
+
+
+class _WDecLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _WDEC_LAYER]
+
+
+class _WDecWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _WDEC_TOP + ("layers",)]
+
+
+class WhisperDecoder:
+    """Whisper-small greedy decoder on one B200 (HostDecoder::precompute_cross + step loop of
+    the reference, bfp16 weights), 1..32 streams in lockstep."""
+
+    def __init__(self, device: Device, cfg, weights: dict, max_batch: int = 1):
+        keep = []
+
+        def p(a):
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            return _addr(a)
+
+        c = _WDecCfg(cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.ffn, cfg.vocab, cfg.max_tgt, cfg.n_enc)
+        layers = (_WDecLayer * cfg.n_layers)()
+        for li, ly in enumerate(weights["layers"][:cfg.n_layers]):
+            for n in _WDEC_LAYER:
+                setattr(layers[li], n, p(ly[n]))
+        w = _WDecWeights(*[p(weights[n]) for n in _WDEC_TOP], C.addressof(layers))
+        h = lib().xdna_whisper_dec_create(device.handle, C.byref(c), C.byref(w), max_batch)
+        if not h:
+            raise XdnaError(last_error())
+        self.handle, self.cfg = h, cfg
+
+    @property
+    def clamped_blocks(self) -> int:
+        return lib().xdna_whisper_dec_clamped_blocks(self.handle)
+
+    def generate(self, enc, prompt, n_new, want_logits=False):
+        enc = np.ascontiguousarray(enc, np.float32)
+        B = enc.shape[0]
+        pr = np.ascontiguousarray(prompt, np.int64)
+        toks = np.empty((B, n_new), np.int64)
+        lg = np.empty((B, n_new, self.cfg.vocab), np.float32) if want_logits else None
+        _check(lib().xdna_whisper_dec_generate(self.handle, _addr(enc), B, _addr(pr), len(pr), n_new, _addr(toks),
+                                               _addr(lg) if lg is not None else None))
+        return (toks, lg) if want_logits else toks
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().xdna_whisper_dec_free(self.handle)
             self.handle = None
 
     def __del__(self):
