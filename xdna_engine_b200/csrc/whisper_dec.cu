@@ -39,7 +39,6 @@ namespace wdec {
 constexpr int D = 768, H = 12, HD = 64, F = 3072;
 constexpr int MAXB = 32;              // streams per decoder
 constexpr int KC = 128;               // K per split of the GEMV (8 mma k-steps)
-constexpr int XLD = KC + 8;           // padded bf16 row of the staged input chunk (bank-conflict free)
 constexpr int GEMV_WARPS = 4;
 
 enum { OUT_F32 = 0, OUT_RESID = 1, OUT_GELU_BF16 = 2 };
@@ -75,7 +74,7 @@ struct GemvArgs {
     const uint8_t *ecode;       // [row groups][K/16][8 quads][4]
     const float *bias;          // [N] or null
     const uint16_t *x;          // bf16 [B][K]
-    int B, N, K, nsplit;
+    int B, N, K, nsplit, kchunk;
     float *part;                // [nsplit][Np][MAXB] split-K partials
     unsigned *count;            // [row groups] arrival counters (left at zero)
     int mode;
@@ -85,50 +84,59 @@ struct GemvArgs {
 };
 
 // Y[b][n] = X[b] . W[n] for b < B: warp w of the CTA owns 16 output rows (row group) and one K
-// split of KC; the weight fragments come straight from HBM in mma order (8 bytes of mantissas
-// + a quad-shared 4-byte exponent word per lane and k-step), X from a padded shared chunk.
-// With several splits, partials go to `part` and the last warp to finish a row group sums
-// them in split order and applies the epilogue (deterministic; the counter is reset to 0).
+// range of kchunk (a multiple of 128); the weight fragments come straight from HBM in mma order
+// (8 bytes of mantissas + a quad-shared 4-byte exponent word per lane and k-step), 8 k-steps
+// at a time with the next 8 already in flight; X comes from a padded shared copy of the range.
+// With several ranges, partials go to `part` and the last warp to finish a row group sums
+// them in range order and applies the epilogue (deterministic; the counter is reset to 0).
 template <int NT>
 __global__ void __launch_bounds__(GEMV_WARPS * 32) bfp_gemv_kernel(GemvArgs a) {
-    __shared__ __align__(16) uint16_t xs[NT * 8][XLD];
+    extern __shared__ __align__(16) uint16_t xs[];           // [NT*8][kchunk + 8]
     __shared__ int last_flag[GEMV_WARPS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int split = blockIdx.y;
     const int rg = blockIdx.x * GEMV_WARPS + warp;
     const int n_rg = (a.N + 15) / 16;
-    const int k0 = split * KC;
-    // stage X[:, k0 : k0 + KC] (rows >= B are zero)
-    for (int i = threadIdx.x; i < NT * 8 * (KC / 8); i += blockDim.x) {
-        const int b = i / (KC / 8), c = i % (KC / 8);
+    const int k0 = split * a.kchunk, xld = a.kchunk + 8;
+    for (int i = threadIdx.x; i < NT * 8 * (a.kchunk / 8); i += blockDim.x) {
+        const int b = i / (a.kchunk / 8), c = i % (a.kchunk / 8);
         uint4 v = make_uint4(0, 0, 0, 0);
         if (b < a.B) v = *reinterpret_cast<const uint4 *>(a.x + (size_t)b * a.K + k0 + c * 8);
-        *reinterpret_cast<uint4 *>(&xs[b][c * 8]) = v;
+        *reinterpret_cast<uint4 *>(&xs[b * xld + c * 8]) = v;
     }
     __syncthreads();
     if (rg >= n_rg) return;
     float acc[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-    const int ks0 = k0 / 16, nks = a.K / 16;
+    const int ks0 = k0 / 16, nks = a.K / 16, ngrp = a.kchunk / 128;
     const uint2 *mp = reinterpret_cast<const uint2 *>(a.mant) + ((size_t)rg * nks + ks0) * 32 + lane;
     const uint32_t *ep = reinterpret_cast<const uint32_t *>(a.ecode) + ((size_t)rg * nks + ks0) * 8 + g;
-    uint2 mv[KC / 16];
-    uint32_t ev[KC / 16];
+    uint2 mv[8], mn[8];
+    uint32_t ev[8], en[8];
 #pragma unroll
-    for (int s = 0; s < KC / 16; s++) { mv[s] = mp[s * 32]; ev[s] = ep[s * 8]; }
+    for (int s = 0; s < 8; s++) { mv[s] = __ldcs(mp + s * 32); ev[s] = __ldcs(ep + s * 8); }
+    for (int gi = 0; gi < ngrp; gi++) {
+        if (gi + 1 < ngrp) {
 #pragma unroll
-    for (int s = 0; s < KC / 16; s++) {
-        // a0 (row g, k 2t..) a1 (row g+8, k 2t..) block 0; a2, a3 (k 2t+8..) block 1
-        const uint32_t e = ev[s];
-        const uint32_t a0 = deq2(mv[s].x & 0xffffu, e & 255u), a1 = deq2(mv[s].x >> 16, (e >> 8) & 255u);
-        const uint32_t a2 = deq2(mv[s].y & 0xffffu, (e >> 16) & 255u), a3 = deq2(mv[s].y >> 16, e >> 24);
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-            const uint32_t b0 = *reinterpret_cast<const uint32_t *>(&xs[n * 8 + g][s * 16 + 2 * t]);
-            const uint32_t b1 = *reinterpret_cast<const uint32_t *>(&xs[n * 8 + g][s * 16 + 8 + 2 * t]);
-            mma16816(acc[n], a0, a1, a2, a3, b0, b1);
+            for (int s = 0; s < 8; s++) { mn[s] = __ldcs(mp + ((gi + 1) * 8 + s) * 32); en[s] = __ldcs(ep + ((gi + 1) * 8 + s) * 8); }
         }
+#pragma unroll
+        for (int s = 0; s < 8; s++) {
+            // a0 (row g, k 2t..) a1 (row g+8, k 2t..) block 0; a2, a3 (k 2t+8..) block 1
+            const uint32_t e = ev[s];
+            const uint32_t a0 = deq2(mv[s].x & 0xffffu, e & 255u), a1 = deq2(mv[s].x >> 16, (e >> 8) & 255u);
+            const uint32_t a2 = deq2(mv[s].y & 0xffffu, (e >> 16) & 255u), a3 = deq2(mv[s].y >> 16, e >> 24);
+            const int kk = (gi * 8 + s) * 16;
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(&xs[(n * 8 + g) * xld + kk + 2 * t]);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(&xs[(n * 8 + g) * xld + kk + 8 + 2 * t]);
+                mma16816(acc[n], a0, a1, a2, a3, b0, b1);
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < 8; s++) { mv[s] = mn[s]; ev[s] = en[s]; }
     }
     // acc[n][e]: row (n0 + g + 8 (e >> 1)), stream (n*8 + 2t + (e & 1))
     const int n0 = rg * 16;
@@ -145,17 +153,29 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) bfp_gemv_kernel(GemvArgs a) {
         __syncwarp();
         if (!last_flag[warp]) return;
         __threadfence();
+#pragma unroll
         for (int n = 0; n < NT; n++)
-            for (int e = 0; e < 4; e++) acc[n][e] = 0.0f;
-        for (int s = 0; s < a.nsplit; s++) {
-            const float *ps = a.part + (size_t)s * Np * MAXB;
 #pragma unroll
-            for (int n = 0; n < NT; n++)
+            for (int e = 0; e < 4; e++) {
+                // every split's value requested before the ordered sum
+                const size_t off = (size_t)(n0 + g + 8 * (e >> 1)) * MAXB + n * 8 + 2 * t + (e & 1);
+                float pv[8];
+                float sum = 0.0f;
+                for (int s0 = 0; s0 < a.nsplit; s0 += 8) {
 #pragma unroll
-                for (int e = 0; e < 4; e++)
-                    acc[n][e] += __ldcg(ps + (size_t)(n0 + g + 8 * (e >> 1)) * MAXB + n * 8 + 2 * t + (e & 1));
-        }
+                    for (int u = 0; u < 8; u++) pv[u] = s0 + u < a.nsplit ? __ldcg(a.part + (size_t)(s0 + u) * Np * MAXB + off) : 0.0f;
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (s0 + u < a.nsplit) sum += pv[u];
+                }
+                acc[n][e] = sum;
+            }
         if (lane == 0) a.count[rg] = 0;
+    }
+    float bv[2] = {0.0f, 0.0f};
+    if (a.bias) {
+        if (n0 + g < a.N) bv[0] = a.bias[n0 + g];
+        if (n0 + g + 8 < a.N) bv[1] = a.bias[n0 + g + 8];
     }
 #pragma unroll
     for (int n = 0; n < NT; n++)
@@ -163,7 +183,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) bfp_gemv_kernel(GemvArgs a) {
         for (int e = 0; e < 4; e++) {
             const int row = n0 + g + 8 * (e >> 1), b = n * 8 + 2 * t + (e & 1);
             if (row >= a.N || b >= a.B) continue;
-            const float y = acc[n][e] + (a.bias ? a.bias[row] : 0.0f);
+            const float y = acc[n][e] + bv[e >> 1];
             if (a.mode == OUT_F32) a.out[(size_t)b * a.ldo + row] = y;
             else if (a.mode == OUT_RESID) a.out[(size_t)b * a.ldo + row] += y;
             else a.out_bf16[(size_t)b * a.ldo + row] = (uint16_t)bf16bits(gelu_erf_as(y));
@@ -178,13 +198,20 @@ __global__ void embed_kernel(const int64_t *tok, const int *pos, const float *et
 }
 
 // y = bf16(LN(x)) per stream row (ln_row: population variance, eps 1e-5); one warp per row
-__global__ void ln_kernel(const float *x, int B, const float *gm, const float *bt, uint16_t *y) {
+__global__ void ln_kernel(const float *__restrict__ x, int B, const float *__restrict__ gm,
+                          const float *__restrict__ bt, uint16_t *__restrict__ y) {
     const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (b >= B) return;
-    float v[24];
+    float v[24], gv[24], bv[24];
+#pragma unroll
+    for (int i = 0; i < 24; i++) {
+        v[i] = x[(size_t)b * D + lane + 32 * i];
+        gv[i] = gm[lane + 32 * i];
+        bv[i] = bt[lane + 32 * i];
+    }
     float s = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 24; i++) { v[i] = x[(size_t)b * D + lane + 32 * i]; s += v[i]; }
+    for (int i = 0; i < 24; i++) s += v[i];
 #pragma unroll
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float mu = s / (float)D;
@@ -196,8 +223,7 @@ __global__ void ln_kernel(const float *x, int B, const float *gm, const float *b
     const float inv = 1.0f / sqrtf(q / (float)D + 1e-5f);
 #pragma unroll
     for (int i = 0; i < 24; i++) {
-        const int c = lane + 32 * i;
-        y[(size_t)b * D + c] = (uint16_t)bf16bits((v[i] - mu) * inv * gm[c] + bt[c]);
+        y[(size_t)b * D + lane + 32 * i] = (uint16_t)bf16bits((v[i] - mu) * inv * gv[i] + bv[i]);
     }
 }
 
@@ -321,16 +347,22 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const u
     if (tid < HD) pp[2 + tid] = pacc[0][tid] + pacc[1][tid];
     if (tid == 0) { pp[0] = mx; pp[1] = red[0] + red[1] + red[2] + red[3]; }
 }
-__global__ void cross_merge_kernel(const float *part, int nsplit, uint16_t *ctx) {
+__global__ void cross_merge_kernel(const float *__restrict__ part, int nsplit, uint16_t *__restrict__ ctx) {
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const float *pp = part + ((size_t)b * H + h) * nsplit * (HD + 2);
+    constexpr int MAXS = 16;                           // encoder positions <= 16 x 128
+    float m[MAXS], l[MAXS], a[MAXS];
+#pragma unroll
+    for (int s = 0; s < MAXS; s++)
+        if (s < nsplit) { m[s] = pp[s * (HD + 2)]; l[s] = pp[s * (HD + 2) + 1]; a[s] = pp[s * (HD + 2) + 2 + d]; }
     float M = -INFINITY, L = 0.0f, A = 0.0f;
-    for (int s = 0; s < nsplit; s++) {
-        const float m = pp[s * (HD + 2)], l = pp[s * (HD + 2) + 1], a = pp[s * (HD + 2) + 2 + d];
-        const float mn = fmaxf(M, m);
-        const float c0 = M == -INFINITY ? 0.0f : expf(M - mn), c1 = expf(m - mn);
-        L = L * c0 + l * c1;
-        A = A * c0 + a * c1;
+#pragma unroll
+    for (int s = 0; s < MAXS; s++) {
+        if (s >= nsplit) break;
+        const float mn = fmaxf(M, m[s]);
+        const float c0 = M == -INFINITY ? 0.0f : expf(M - mn), c1 = expf(m[s] - mn);
+        L = L * c0 + l[s] * c1;
+        A = A * c0 + a[s] * c1;
         M = mn;
     }
     ctx[(size_t)b * D + h * HD + d] = (uint16_t)bf16bits(A / L);
@@ -543,12 +575,18 @@ BfpMat pack_bfp(XdnaWhisperDec *m, const float *w, const float *bias, int K, int
 
 cudaError_t gemv(XdnaWhisperDec *m, const BfpMat &w, const uint16_t *x, int B, int mode, float *out, uint16_t *ob,
                  int ldo, cudaStream_t st) {
-    wdec::GemvArgs a{w.mant, w.ecode, w.bias, x, B, w.N, w.K, w.K / wdec::KC, m->part, m->count, mode, out, ob, ldo};
-    const int nrg = (w.N + 15) / 16;
-    dim3 grid((nrg + wdec::GEMV_WARPS - 1) / wdec::GEMV_WARPS, a.nsplit);
-    if (B <= 8) wdec::bfp_gemv_kernel<1><<<grid, wdec::GEMV_WARPS * 32, 0, st>>>(a);
-    else if (B <= 16) wdec::bfp_gemv_kernel<2><<<grid, wdec::GEMV_WARPS * 32, 0, st>>>(a);
-    else wdec::bfp_gemv_kernel<4><<<grid, wdec::GEMV_WARPS * 32, 0, st>>>(a);
+    // K ranges: as few as give about two warps per SM (fewer ranges = shorter reduction)
+    const int nrg = (w.N + 15) / 16, kb = w.K / wdec::KC;
+    int nsplit = std::min(kb, std::max(1, (2 * 148 + nrg - 1) / nrg));
+    while (kb % nsplit) nsplit--;
+    const int kchunk = w.K / nsplit;
+    wdec::GemvArgs a{w.mant, w.ecode, w.bias, x, B, w.N, w.K, nsplit, kchunk, m->part, m->count, mode, out, ob, ldo};
+    dim3 grid((nrg + wdec::GEMV_WARPS - 1) / wdec::GEMV_WARPS, nsplit);
+    const int nt = B <= 8 ? 1 : (B <= 16 ? 2 : 4);
+    const size_t smem = (size_t)nt * 8 * (kchunk + 8) * 2;
+    if (nt == 1) wdec::bfp_gemv_kernel<1><<<grid, wdec::GEMV_WARPS * 32, smem, st>>>(a);
+    else if (nt == 2) wdec::bfp_gemv_kernel<2><<<grid, wdec::GEMV_WARPS * 32, smem, st>>>(a);
+    else wdec::bfp_gemv_kernel<4><<<grid, wdec::GEMV_WARPS * 32, smem, st>>>(a);
     return cudaGetLastError();
 }
 
@@ -695,6 +733,11 @@ XdnaWhisperDec *xdna_whisper_dec_create(XdnaDevice *dev_unused, const XdnaWhispe
         ck(cudaMemset(m->count, 0, sizeof(unsigned) * n_rg_max), "memset");
         ck(cudaMemset(m->done, 0, sizeof(unsigned)), "memset");
         ck(cudaFuncSetAttribute(self_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SA_SMEM), "smem");
+        // the GEMV's staged input: up to 32 streams x (3072 + 8) bf16
+        const int gsm = 4 * 8 * (F + 8) * 2;
+        ck(cudaFuncSetAttribute(bfp_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
+        ck(cudaFuncSetAttribute(bfp_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
+        ck(cudaFuncSetAttribute(bfp_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
         ck(cudaDeviceSynchronize(), "create sync");
         return m;
     } catch (const std::exception &ex) {
