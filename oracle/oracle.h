@@ -224,6 +224,24 @@ int or_whisper_decode(const or_whisper_dec_cfg *c, const or_whisper_dec_weights 
                       const int64_t *prompt, int n_prompt, int n_new, int64_t *out_tokens, float *logits,
                       int nthreads);
 
+/* ---- Gemma-3 text decoder (npu-gemma pieces + the HF Gemma-3 model they port) ---- */
+typedef struct {
+    int n_layers, d_model, n_q_heads, head_dim, ffn, vocab, window, pattern;
+    float theta_local, theta_global, query_pre_attn_scalar, eps;
+    int int8;            /* 1: int8 per-channel linears + LM head (Lin rule) */
+} or_gemma_cfg;
+typedef struct {         /* [K, N] = [in, out]; one KV head */
+    const float *in_norm, *wq, *wk, *wv, *q_norm, *k_norm, *wo, *post_attn_norm;
+    const float *pre_ffn_norm, *wg, *wu, *wd, *post_ffn_norm;
+} or_gemma_layer;
+typedef struct {
+    const float *embed, *final_norm;      /* embed [V, D], tied LM head */
+    const or_gemma_layer *layers;
+} or_gemma_weights;
+int or_gemma_decode(const or_gemma_cfg *c, const or_gemma_weights *w, const int64_t *prompt, int n_prompt,
+                    int n_new, int64_t *out_tokens, float *logits, int nthreads);
+float or_gelu_tanh_gemma(float x);
+
 #ifdef __cplusplus
 }
 #endif

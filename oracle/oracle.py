@@ -88,6 +88,9 @@ def lib():
         L.or_whisper_decode.argtypes = [C.c_void_p, C.c_void_p, F32P, C.c_int, C.c_void_p, C.c_int, C.c_int,
                                         C.c_void_p, C.c_void_p, C.c_int]
         L.or_whisper_decode.restype = C.c_int
+        L.or_gemma_decode.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                      C.c_void_p, C.c_int]
+        L.or_gemma_decode.restype = C.c_int
         L.or_opt_step.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_void_p]
         L.or_opt_step.restype = C.c_int64
         L.or_opt_qweight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.POINTER(C.c_float))]
@@ -500,4 +503,48 @@ def whisper_decode(cfg, w, enc, prompt, n_new, want_logits=False, nthreads=None)
                                  nthreads or os.cpu_count() or 1)
     if rc != 0:
         raise ValueError("or_whisper_decode: prompt + new tokens beyond max_tgt")
+    return (toks, lg) if want_logits else toks
+
+
+# ---------------------------------------------------------------- Gemma-3 text decoder
+_GM_LAYER = ("in_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo", "post_attn_norm", "pre_ffn_norm", "wg", "wu",
+             "wd", "post_ffn_norm")
+
+
+class _GmCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d_model", "n_q_heads", "head_dim", "ffn", "vocab", "window",
+                                       "pattern")] + \
+               [(n, C.c_float) for n in ("theta_local", "theta_global", "query_pre_attn_scalar", "eps")] + \
+               [("int8", C.c_int)]
+
+
+class _GmLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _GM_LAYER]
+
+
+class _GmWeights(C.Structure):
+    _fields_ = [("embed", C.c_void_p), ("final_norm", C.c_void_p), ("layers", C.c_void_p)]
+
+
+def gemma_decode(cfg, w, prompt, n_new, int8=True, want_logits=False, nthreads=None):
+    """or_gemma_decode: greedy decode of one stream after the prompt."""
+    keep = []
+
+    def p(a):
+        a = _f32(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    c = _GmCfg(cfg.n_layers, cfg.d_model, cfg.n_q_heads, cfg.head_dim, cfg.ffn, cfg.vocab, cfg.window, cfg.pattern,
+               cfg.theta_local, cfg.theta_global, cfg.query_pre_attn_scalar, cfg.eps, int(int8))
+    layers = (_GmLayer * cfg.n_layers)()
+    for i, ly in enumerate(w["layers"][:cfg.n_layers]):
+        for n in _GM_LAYER:
+            setattr(layers[i], n, p(ly[n]))
+    ww = _GmWeights(p(w["embed"]), p(w["final_norm"]), C.addressof(layers))
+    pr = np.ascontiguousarray(prompt, np.int64)
+    toks = np.empty(n_new, np.int64)
+    lg = np.empty((n_new, cfg.vocab), np.float32) if want_logits else None
+    lib().or_gemma_decode(C.addressof(c), C.addressof(ww), pr.ctypes.data, len(pr), n_new, toks.ctypes.data,
+                          lg.ctypes.data if lg is not None else None, nthreads or os.cpu_count() or 1)
     return (toks, lg) if want_logits else toks

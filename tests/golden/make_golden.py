@@ -289,6 +289,60 @@ def whisper_dec_hf_fixture():
     print("whisper_dec_hf_golden.npz:", toks.tolist())
 
 
+GEMMA_SMALL = dict(n_layers=7, d_model=256, n_q_heads=4, head_dim=64, ffn=512, vocab=500, window=8)
+GEMMA_SEED = 1
+GEMMA_PROMPT = [2, 3, 4, 5, 6, 7, 8, 9, 10, 11]
+
+
+def gemma_small():
+    from xdna_engine_b200.synth import GemmaConfig, make_gemma_weights
+    cfg = GemmaConfig(**GEMMA_SMALL)
+    return cfg, make_gemma_weights(cfg, seed=GEMMA_SEED, std=0.2, norm_std=0.1, embed_std=0.01)
+
+
+def gemma_hf_fixture():
+    """HF Gemma3ForCausalLM (the model rust/npu-gemma ports) on a small seeded config with a
+    sliding window of 8 and the 5:1 local:global pattern: greedy tokens and logits."""
+    import torch
+    from transformers import Gemma3TextConfig, Gemma3ForCausalLM
+    cfg, w = gemma_small()
+    types = ["full_attention" if (i + 1) % cfg.pattern == 0 else "sliding_attention" for i in range(cfg.n_layers)]
+    hc = Gemma3TextConfig(vocab_size=cfg.vocab, hidden_size=cfg.d_model, intermediate_size=cfg.ffn,
+                          num_hidden_layers=cfg.n_layers, num_attention_heads=cfg.n_q_heads, num_key_value_heads=1,
+                          head_dim=cfg.head_dim, sliding_window=cfg.window, layer_types=types,
+                          query_pre_attn_scalar=int(cfg.query_pre_attn_scalar), rms_norm_eps=cfg.eps,
+                          rope_parameters={"sliding_attention": {"rope_type": "default", "rope_theta": cfg.theta_local},
+                                           "full_attention": {"rope_type": "default", "rope_theta": cfg.theta_global}},
+                          max_position_embeddings=64, attn_implementation="eager", tie_word_embeddings=True)
+    model = Gemma3ForCausalLM(hc).eval().float()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    sd = {"model.embed_tokens.weight": t(w["embed"]), "model.norm.weight": t(w["final_norm"]),
+          "lm_head.weight": t(w["embed"])}
+    names = {"wq": "self_attn.q_proj", "wk": "self_attn.k_proj", "wv": "self_attn.v_proj", "wo": "self_attn.o_proj",
+             "wg": "mlp.gate_proj", "wu": "mlp.up_proj", "wd": "mlp.down_proj"}
+    norms = {"in_norm": "input_layernorm", "q_norm": "self_attn.q_norm", "k_norm": "self_attn.k_norm",
+             "post_attn_norm": "post_attention_layernorm", "pre_ffn_norm": "pre_feedforward_layernorm",
+             "post_ffn_norm": "post_feedforward_layernorm"}
+    for i, ly in enumerate(w["layers"]):
+        p = f"model.layers.{i}."
+        for k, n in names.items():
+            sd[p + n + ".weight"] = t(ly[k].T)
+        for k, n in norms.items():
+            sd[p + n + ".weight"] = t(ly[k])
+    model.load_state_dict(sd, strict=True)
+    seq = list(GEMMA_PROMPT)
+    n_new = 12
+    toks, lgs = [], []
+    with torch.no_grad():
+        for _ in range(n_new):
+            lg = model(input_ids=torch.tensor([seq])).logits[0, -1].numpy()
+            lgs.append(lg)
+            toks.append(int(np.argmax(lg)))
+            seq.append(toks[-1])
+    np.savez_compressed(os.path.join(HERE, "gemma_hf_golden.npz"), tokens=np.array(toks), logits=np.stack(lgs))
+    print("gemma_hf_golden.npz:", toks)
+
+
 def _load_ref_module(rel, name):
     spec = importlib.util.spec_from_file_location(name, os.path.join(REF, rel))
     mod = importlib.util.module_from_spec(spec)
@@ -338,6 +392,8 @@ def parakeet_fixture():
 if __name__ == "__main__":
     import sys
     only = set(sys.argv[1:])
+    if not only or "gemma" in only:
+        gemma_hf_fixture()
     if not only or "whisper_dec" in only:
         whisper_dec_hf_fixture()
     if not only or "parakeet" in only:

@@ -350,3 +350,52 @@ def make_encoder_states(cfg: WhisperDecConfig = WHISPER_SMALL_DEC, batch: int = 
     """Synthetic encoder output (the decoder's cross-attention input) ~N(0, 1), [batch, n_enc, D]."""
     rng = np.random.default_rng(seed + 5_000_017)
     return rng.standard_normal((batch, cfg.n_enc, cfg.d_model), dtype=np.float32)
+
+
+# --------------------------------------------------------------------- Gemma-3 text decoder
+@dataclass(frozen=True)
+class GemmaConfig:
+    """rust/npu-gemma/src/config.rs GEMMA3_1B (one KV head; every 6th layer global)."""
+    n_layers: int = 26
+    d_model: int = 1152
+    n_q_heads: int = 4
+    head_dim: int = 256
+    ffn: int = 6912
+    vocab: int = 262144
+    window: int = 512
+    pattern: int = 6
+    theta_local: float = 10_000.0
+    theta_global: float = 1_000_000.0
+    query_pre_attn_scalar: float = 256.0
+    eps: float = 1e-6
+
+
+GEMMA3_1B = GemmaConfig()
+
+
+def make_gemma_weights(cfg: GemmaConfig = GEMMA3_1B, seed: int = 0, std: float = 0.02, norm_std: float = 0.0,
+                       n_layers: int | None = None, embed_std: float | None = None) -> dict:
+    """Random-init Gemma-3 weights (f32, linear weights [K, N] = [in, out]); norm weights are
+    the (1 + w) offsets, 0 by default.  The embedding (tied LM head) uses embed_std (default
+    std)."""
+    rng = np.random.default_rng(seed)
+    D, F, HQ, HD = cfg.d_model, cfg.ffn, cfg.n_q_heads, cfg.head_dim
+
+    def normal(shape, s):
+        a = rng.standard_normal(shape, dtype=np.float32)
+        a *= np.float32(s)
+        return a
+
+    def nrm(n):
+        return normal((n,), norm_std) if norm_std else np.zeros(n, np.float32)
+
+    w = {"embed": normal((cfg.vocab, D), std if embed_std is None else embed_std), "final_norm": nrm(D)}
+    layers = []
+    for _ in range(cfg.n_layers if n_layers is None else n_layers):
+        layers.append({"in_norm": nrm(D), "wq": normal((D, HQ * HD), std), "wk": normal((D, HD), std),
+                       "wv": normal((D, HD), std), "q_norm": nrm(HD), "k_norm": nrm(HD),
+                       "wo": normal((HQ * HD, D), std), "post_attn_norm": nrm(D), "pre_ffn_norm": nrm(D),
+                       "wg": normal((D, F), std), "wu": normal((D, F), std), "wd": normal((F, D), std),
+                       "post_ffn_norm": nrm(D)})
+    w["layers"] = layers
+    return w
