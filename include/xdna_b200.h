@@ -286,6 +286,39 @@ int xdna_whisper_dec_run(XdnaWhisperDec *m, int B, const int64_t *prompt_host, i
 int xdna_whisper_dec_generate(XdnaWhisperDec *m, const float *enc_host, int B, const int64_t *prompt, int n_prompt,
                               int n_new, int64_t *tokens_host, float *logits_host);
 
+/* ------------------------------------------------------------ Gemma-3 text decoder */
+/* The reference has no Gemma decode step (rust/npu-gemma/src/lib.rs:30-43 maps what to reuse:
+ * rmsnorm_ref 55-64, geglu_ref 68-77, config.rs GEMMA3_1B, is_global_layer 131-133); this is
+ * the HF Gemma-3 text model on those pieces, with the reference's int8 Lin rule
+ * (opt125m_decode.rs:41-60) for every linear and the tied LM head.  1..64 streams decode in
+ * lockstep; tensor parallel over tp_size GPUs (one process per GPU, same calls on every
+ * rank): q heads, FFN columns and LM-head vocabulary rows are split, partial sums are
+ * all-reduced in rank order over peer memory (xdna_gemma_ipc_handle / xdna_gemma_connect). */
+typedef struct {
+    int n_layers, d_model, n_q_heads, head_dim, ffn, vocab, window, pattern;
+    float theta_local, theta_global, query_pre_attn_scalar, eps;
+} XdnaGemmaConfig;
+typedef struct {               /* f32, [K, N] = [in, out]; norm weights are the (1 + w) offsets */
+    const float *in_norm, *wq, *wk, *wv, *q_norm, *k_norm, *wo, *post_attn_norm;
+    const float *pre_ffn_norm, *wg, *wu, *wd, *post_ffn_norm;
+} XdnaGemmaLayer;
+typedef struct {
+    const float *embed, *final_norm;           /* embed [vocab, d_model], tied LM head */
+    const XdnaGemmaLayer *layers;
+} XdnaGemmaWeights;
+typedef struct XdnaGemma XdnaGemma;
+XdnaGemma *xdna_gemma_create(XdnaDevice *dev, const XdnaGemmaConfig *cfg, const XdnaGemmaWeights *w, int max_batch,
+                             int max_ctx, int tp_rank, int tp_size);
+void xdna_gemma_free(XdnaGemma *m);
+/* tensor parallel set-up: this rank's 64-byte IPC handle; then every rank passes all handles
+ * (tp_size x 64 bytes, rank order) to xdna_gemma_connect */
+int xdna_gemma_ipc_handle(XdnaGemma *m, void *handle64);
+int xdna_gemma_connect(XdnaGemma *m, const void *handles);
+/* greedy decode: prompts [B][n_prompt] (host) -> tokens [B][n_new] (host); the prompt is run
+ * through the decode step (prefill); synchronous; -1 also when a peer exchange timed out */
+int xdna_gemma_generate(XdnaGemma *m, int B, const int64_t *prompts, int n_prompt, int n_new, int64_t *tokens_host,
+                        void *stream);
+
 /* ------------------------------------ Parakeet FastConformer encoder (FastConformerEncoder) */
 /* Replaces rust/npu-parakeet/src/encoder.rs FastConformerEncoder::subsample (200-237) +
  * forward_last (657-665) with every weight linear on the int8 GEMM engine (the reference's

@@ -1,0 +1,110 @@
+"""Gemma-3 decoder (xdna_gemma_*) against the oracle (npu-gemma pieces + the HF Gemma-3 model,
+int8 Lin rule), single GPU and tensor parallel over 2 GPUs when the box has them.
+
+The engine feeds bf16 activations to its int8 GEMVs (the oracle: f32) and keeps the KV cache
+in bf16, so the greedy stream is compared token by token only while the oracle's top-2 logit
+margin exceeds the engine's expected error (the small test model's logits are ~0.08 rms;
+tolerance 0.01)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CFG_KW = dict(n_layers=7, ffn=512, vocab=500, window=8)
+PROMPT = list(range(2, 12))
+
+
+@pytest.fixture(scope="module")
+def X():
+    import xdna_engine_b200 as X
+    from xdna_engine_b200 import _build
+    _build.build()
+    return X
+
+
+def model(X):
+    cfg = X.GemmaConfig(**CFG_KW)
+    return cfg, X.make_gemma_weights(cfg, seed=1, std=0.3, norm_std=0.5, embed_std=0.002)
+
+
+def agree_until_close(got, want_t, want_l, tol=0.01):
+    srt = np.sort(want_l, axis=1)
+    for s in range(len(want_t)):
+        if got[s] != want_t[s]:
+            assert srt[s, -1] - srt[s, -2] < tol, (s, "token differs with a clear margin")
+            return s
+    return len(want_t)
+
+
+def test_gemma_single_gpu_vs_oracle(X):
+    from oracle import oracle as O
+    cfg, w = model(X)
+    dec = X.GemmaDecoder(X.Device(0), cfg, w, max_batch=4, max_ctx=64)
+    wt, wl = O.gemma_decode(cfg, w, PROMPT, 12, int8=True, want_logits=True)
+    got = dec.generate(np.array([PROMPT]), 12)[0]
+    n = agree_until_close(got, wt, wl)
+    assert n >= 4, (got, wt)
+    # three streams with different prompts: each equals its own single-stream run
+    prompts = np.array([PROMPT, list(range(20, 30)), list(range(40, 50))])
+    batch = dec.generate(prompts, 12)
+    for b in range(3):
+        assert np.array_equal(batch[b], dec.generate(prompts[b:b + 1], 12)[0])
+    dec.close()
+
+
+def test_gemma_rejects_bad_input(X):
+    cfg, w = model(X)
+    with pytest.raises(X.XdnaError):
+        X.GemmaDecoder(X.Device(0), X.GemmaConfig(**{**CFG_KW, "d_model": 1024}), w)
+    dec = X.GemmaDecoder(X.Device(0), cfg, w, max_batch=1, max_ctx=16)
+    with pytest.raises(X.XdnaError):
+        dec.generate(np.array([PROMPT]), 12)          # beyond max_ctx
+    with pytest.raises(X.XdnaError):
+        dec.generate(np.array([[1, 999]]), 2)         # token outside the vocabulary
+    dec.close()
+
+
+def _tp_worker(rank, world, port, q):
+    import os
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.cuda.set_device(rank)
+    import xdna_engine_b200 as X
+    cfg, w = model(X)
+    dec = X.GemmaDecoder(X.Device(rank), cfg, w, max_batch=2, max_ctx=64, tp_rank=rank, tp_size=world)
+    hs = [None] * world
+    dist.all_gather_object(hs, dec.ipc_handle())
+    dec.connect(hs)
+    dist.barrier()
+    toks = dec.generate(np.array([PROMPT, list(range(20, 30))]), 12)
+    dist.barrier()
+    q.put((rank, toks))
+    dec.close()
+    dist.destroy_process_group()
+
+
+def test_gemma_tensor_parallel_2gpu(X):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+    assert np.array_equal(res[0], res[1]), "ranks disagree"
+    cfg, w = model(X)
+    single = X.GemmaDecoder(X.Device(0), cfg, w, max_batch=2, max_ctx=64)
+    ref = single.generate(np.array([PROMPT, list(range(20, 30))]), 12)
+    assert (res[0][:, :4] == ref[:, :4]).all(), (res[0], ref)
+    single.close()

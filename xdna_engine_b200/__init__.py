@@ -19,7 +19,7 @@ from .synth import (OPT_125M, OptConfig, make_opt_weights, make_prompt,  # noqa:
                     WHISPER_SMALL_ENC, WhisperEncConfig, make_whisper_enc_weights, make_mel,
                     PARAKEET_V3, ParakeetConfig, make_parakeet_weights, make_parakeet_mel,
                     WHISPER_SMALL_DEC, WhisperDecConfig, make_whisper_dec_weights, make_encoder_states,
-                    WHISPER_PROMPT)
+                    WHISPER_PROMPT, GEMMA3_1B, GemmaConfig, make_gemma_weights)
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libxdna_b200.so")
@@ -109,6 +109,15 @@ def lib():
         L.xdna_whisper_dec_run.restype = i
         L.xdna_whisper_dec_generate.argtypes = [vp, vp, i, vp, i, i, vp, vp]
         L.xdna_whisper_dec_generate.restype = i
+        L.xdna_gemma_create.argtypes = [vp, vp, vp, i, i, i, i]
+        L.xdna_gemma_create.restype = vp
+        L.xdna_gemma_free.argtypes = [vp]
+        L.xdna_gemma_ipc_handle.argtypes = [vp, vp]
+        L.xdna_gemma_ipc_handle.restype = i
+        L.xdna_gemma_connect.argtypes = [vp, vp]
+        L.xdna_gemma_connect.restype = i
+        L.xdna_gemma_generate.argtypes = [vp, i, vp, i, i, vp, vp]
+        L.xdna_gemma_generate.restype = i
         L.xdna_opt_create.argtypes = [vp, vp, vp, i, i]
         L.xdna_opt_create.restype = vp
         L.xdna_opt_free.argtypes = [vp]
@@ -527,6 +536,77 @@ class WhisperDecoder:
     def close(self):
         if getattr(self, "handle", None):
             lib().xdna_whisper_dec_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_GM_LAYER = ("in_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo", "post_attn_norm", "pre_ffn_norm", "wg", "wu",
+             "wd", "post_ffn_norm")
+
+
+class _GmCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d_model", "n_q_heads", "head_dim", "ffn", "vocab", "window",
+                                       "pattern")] + \
+               [(n, C.c_float) for n in ("theta_local", "theta_global", "query_pre_attn_scalar", "eps")]
+
+
+class _GmLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _GM_LAYER]
+
+
+class _GmWeights(C.Structure):
+    _fields_ = [("embed", C.c_void_p), ("final_norm", C.c_void_p), ("layers", C.c_void_p)]
+
+
+class GemmaDecoder:
+    """Gemma-3 greedy decoder on one B200, or one tensor-parallel rank (tp_size > 1: call
+    ipc_handle() on every rank, exchange the handles, then connect(all_handles))."""
+
+    def __init__(self, device: Device, cfg, weights: dict, max_batch=1, max_ctx=4352, tp_rank=0, tp_size=1):
+        keep = []
+
+        def p(a):
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            return _addr(a)
+
+        c = _GmCfg(cfg.n_layers, cfg.d_model, cfg.n_q_heads, cfg.head_dim, cfg.ffn, cfg.vocab, cfg.window,
+                   cfg.pattern, cfg.theta_local, cfg.theta_global, cfg.query_pre_attn_scalar, cfg.eps)
+        layers = (_GmLayer * cfg.n_layers)()
+        for li, ly in enumerate(weights["layers"][:cfg.n_layers]):
+            for n in _GM_LAYER:
+                setattr(layers[li], n, p(ly[n]))
+        w = _GmWeights(p(weights["embed"]), p(weights["final_norm"]), C.addressof(layers))
+        h = lib().xdna_gemma_create(device.handle, C.byref(c), C.byref(w), max_batch, max_ctx, tp_rank, tp_size)
+        if not h:
+            raise XdnaError(last_error())
+        self.handle, self.cfg = h, cfg
+
+    def ipc_handle(self) -> bytes:
+        buf = (C.c_uint8 * 64)()
+        _check(lib().xdna_gemma_ipc_handle(self.handle, buf))
+        return bytes(buf)
+
+    def connect(self, handles: list):
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        _check(lib().xdna_gemma_connect(self.handle, buf))
+
+    def generate(self, prompts, n_new, stream=0):
+        pr = np.ascontiguousarray(np.atleast_2d(prompts), np.int64)
+        B, n_prompt = pr.shape
+        out = np.empty((B, n_new), np.int64)
+        _check(lib().xdna_gemma_generate(self.handle, B, _addr(pr), n_prompt, n_new, _addr(out), stream or None))
+        return out
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().xdna_gemma_free(self.handle)
             self.handle = None
 
     def __del__(self):
