@@ -318,6 +318,11 @@ int xdna_gemma_connect(XdnaGemma *m, const void *handles);
  * through the decode step (prefill); synchronous; -1 also when a peer exchange timed out */
 int xdna_gemma_generate(XdnaGemma *m, int B, const int64_t *prompts, int n_prompt, int n_new, int64_t *tokens_host,
                         void *stream);
+/* the same in parts: stage (synchronous), enqueue steps (asynchronous on `stream`; the first
+ * n_prompt - 1 of the n_prompt + n_new - 1 steps are the prefill), collect the tokens */
+int xdna_gemma_begin(XdnaGemma *m, int B, const int64_t *prompts, int n_prompt, int n_new);
+int xdna_gemma_steps(XdnaGemma *m, int n_steps, void *stream);
+int xdna_gemma_tokens(XdnaGemma *m, int64_t *tokens_host, void *stream);
 
 /* ------------------------------------ Parakeet FastConformer encoder (FastConformerEncoder) */
 /* Replaces rust/npu-parakeet/src/encoder.rs FastConformerEncoder::subsample (200-237) +

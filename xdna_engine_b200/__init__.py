@@ -118,6 +118,12 @@ def lib():
         L.xdna_gemma_connect.restype = i
         L.xdna_gemma_generate.argtypes = [vp, i, vp, i, i, vp, vp]
         L.xdna_gemma_generate.restype = i
+        L.xdna_gemma_begin.argtypes = [vp, i, vp, i, i]
+        L.xdna_gemma_begin.restype = i
+        L.xdna_gemma_steps.argtypes = [vp, i, vp]
+        L.xdna_gemma_steps.restype = i
+        L.xdna_gemma_tokens.argtypes = [vp, vp, vp]
+        L.xdna_gemma_tokens.restype = i
         L.xdna_opt_create.argtypes = [vp, vp, vp, i, i]
         L.xdna_opt_create.restype = vp
         L.xdna_opt_free.argtypes = [vp]

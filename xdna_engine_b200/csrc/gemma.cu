@@ -536,6 +536,7 @@ struct XdnaGemma {
     int *pos = nullptr;
     int64_t *tok = nullptr, *prompt = nullptr, *out = nullptr;
     int n_prompt_cap = 0;
+    int run_B = 0, run_prompt = 0, run_new = 0, run_done = 0;   // the staged decode
     // tensor parallel exchange: bufs[r] = rank r's exchange buffer (own or IPC-mapped)
     uint64_t *xbuf = nullptr;
     uint64_t **dbufs = nullptr;
@@ -591,10 +592,16 @@ GmMat pack_i8(XdnaGemma *m, const float *w, int K, int N, const std::vector<int>
 }
 
 // K ranges of a GEMV: as few as give about two warps per SM, each a multiple of 16 of K
+// (and short enough that 64 streams of the range fit the GEMV's shared staging)
+constexpr int kMaxChunk = 1792;
 int splits_of(int N, int K) {
     const int nrg = (N + 15) / 16, ks = K / 16;
     int nsplit = std::min(ks, std::max(1, (2 * 148 + nrg - 1) / nrg));
     while (ks % nsplit) nsplit--;
+    while (K / nsplit > kMaxChunk) {
+        nsplit++;
+        while (ks % nsplit) nsplit++;
+    }
     return nsplit;
 }
 
@@ -815,8 +822,7 @@ XdnaGemma *xdna_gemma_create(XdnaDevice *dev_unused, const XdnaGemmaConfig *cfg,
         ck(cudaMemset(m->bestv, 0, sizeof(float) * MAXTP * MAXB), "memset");
         ck(cudaMemset(m->besti, 0, sizeof(int) * MAXTP * MAXB), "memset");
         ck(cudaFuncSetAttribute(gqa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * AK * HD * 2), "smem");
-        const int gsm = 8 * 8 * (std::max(c.ffn / tp_size, kD) + 8) * 2;
-        if (gsm > 227 * 1024) throw CudaFail("ffn slice too wide for the GEMV staging");
+        const int gsm = 8 * 8 * (kMaxChunk + 8) * 2;      // the widest K range of 64 streams
         ck(cudaFuncSetAttribute(i8_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
         ck(cudaFuncSetAttribute(i8_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
         ck(cudaFuncSetAttribute(i8_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
@@ -872,22 +878,20 @@ int xdna_gemma_connect(XdnaGemma *m, const void *handles) {
     return 0;
 }
 
-// Greedy decode of B streams: prompts [B][n_prompt] (host), n_new tokens each -> tokens_host
-// [B][n_new] (host).  Steps run eagerly on `stream`; every rank of a tensor-parallel group
-// makes the same call.  Synchronous.
-int xdna_gemma_generate(XdnaGemma *m, int B, const int64_t *prompts, int n_prompt, int n_new, int64_t *tokens_host,
-                        void *stream) {
-    if (!m || !prompts || !tokens_host) { set_last_error_message("xdna_gemma_generate: null pointer"); return -1; }
+// Stage a greedy decode of B streams: prompts [B][n_prompt] (host), n_new tokens each.  The
+// n_prompt - 1 + n_new steps then run through xdna_gemma_steps (the first n_prompt - 1 are the
+// prefill).  Synchronous.
+int xdna_gemma_begin(XdnaGemma *m, int B, const int64_t *prompts, int n_prompt, int n_new) {
+    if (!m || !prompts) { set_last_error_message("xdna_gemma_begin: null pointer"); return -1; }
     if (B < 1 || B > m->max_batch || n_prompt < 1 || n_new < 1 || n_prompt + n_new > m->max_ctx) {
-        set_last_error_message("xdna_gemma_generate: bad batch or prompt + new tokens beyond max_ctx");
+        set_last_error_message("xdna_gemma_begin: bad batch or prompt + new tokens beyond max_ctx");
         return -1;
     }
     for (size_t i = 0; i < (size_t)B * n_prompt; i++)
         if (prompts[i] < 0 || prompts[i] >= m->cfg.vocab) {
-            set_last_error_message("xdna_gemma_generate: prompt token out of range");
+            set_last_error_message("xdna_gemma_begin: prompt token out of range");
             return -1;
         }
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     try {
         if (n_prompt * B > m->n_prompt_cap) {
             if (m->prompt) cudaFree(m->prompt);
@@ -897,20 +901,64 @@ int xdna_gemma_generate(XdnaGemma *m, int B, const int64_t *prompts, int n_promp
         std::vector<int64_t> t0(B);
         for (int b = 0; b < B; b++) t0[b] = prompts[(size_t)b * n_prompt];
         const int zero = 0;
+        ck(cudaDeviceSynchronize(), "sync");
         ck(cudaMemcpy(m->prompt, prompts, sizeof(int64_t) * B * n_prompt, cudaMemcpyHostToDevice), "prompt");
         ck(cudaMemcpy(m->tok, t0.data(), sizeof(int64_t) * B, cudaMemcpyHostToDevice), "tokens");
         ck(cudaMemcpy(m->pos, &zero, sizeof(int), cudaMemcpyHostToDevice), "pos");
-        for (int s = 0; s < n_prompt + n_new - 1; s++) ck(step(m, B, n_prompt, n_new, st), "step");
-        ck(cudaMemcpyAsync(tokens_host, m->out, sizeof(int64_t) * B * n_new, cudaMemcpyDeviceToHost, st), "tokens out");
+        m->run_B = B;
+        m->run_prompt = n_prompt;
+        m->run_new = n_new;
+        m->run_done = 0;
+        return 0;
+    } catch (const std::exception &ex) {
+        set_last_error_message(std::string("xdna_gemma_begin: ") + ex.what());
+        return -1;
+    }
+}
+
+// Enqueue the next n_steps steps of the staged decode on `stream` (asynchronous; every rank of a
+// tensor-parallel group makes the same calls).
+int xdna_gemma_steps(XdnaGemma *m, int n_steps, void *stream) {
+    if (!m || m->run_B == 0) { set_last_error_message("xdna_gemma_steps: nothing staged"); return -1; }
+    if (n_steps < 0 || m->run_done + n_steps > m->run_prompt + m->run_new - 1) {
+        set_last_error_message("xdna_gemma_steps: beyond the staged decode");
+        return -1;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int s = 0; s < n_steps; s++) {
+        const cudaError_t e = step(m, m->run_B, m->run_prompt, m->run_new, st);
+        if (e) { set_last_error_message(std::string("xdna_gemma_steps: ") + cudaGetErrorString(e)); return -1; }
+        m->run_done++;
+    }
+    return 0;
+}
+
+// Wait for the staged decode and copy its tokens [B][n_new] to the host; -1 also when a peer
+// exchange timed out.
+int xdna_gemma_tokens(XdnaGemma *m, int64_t *tokens_host, void *stream) {
+    if (!m || !tokens_host || m->run_B == 0) { set_last_error_message("xdna_gemma_tokens: nothing staged"); return -1; }
+    try {
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        ck(cudaMemcpyAsync(tokens_host, m->out, sizeof(int64_t) * m->run_B * m->run_new, cudaMemcpyDeviceToHost, st),
+           "tokens out");
         ck(cudaStreamSynchronize(st), "sync");
         unsigned err = 0;
         ck(cudaMemcpy(&err, m->err, 4, cudaMemcpyDeviceToHost), "err");
-        if (err) { set_last_error_message("xdna_gemma_generate: a tensor-parallel exchange wait expired"); return -1; }
+        if (err) { set_last_error_message("xdna_gemma_tokens: a tensor-parallel exchange wait expired"); return -1; }
         return 0;
     } catch (const std::exception &ex) {
-        set_last_error_message(std::string("xdna_gemma_generate: ") + ex.what());
+        set_last_error_message(std::string("xdna_gemma_tokens: ") + ex.what());
         return -1;
     }
+}
+
+// begin + every step + tokens.  Synchronous.
+int xdna_gemma_generate(XdnaGemma *m, int B, const int64_t *prompts, int n_prompt, int n_new, int64_t *tokens_host,
+                        void *stream) {
+    if (!tokens_host) { set_last_error_message("xdna_gemma_generate: null pointer"); return -1; }
+    if (xdna_gemma_begin(m, B, prompts, n_prompt, n_new) != 0) return -1;
+    if (xdna_gemma_steps(m, n_prompt + n_new - 1, stream) != 0) return -1;
+    return xdna_gemma_tokens(m, tokens_host, stream);
 }
 
 }  // extern "C"
