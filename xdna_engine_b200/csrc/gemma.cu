@@ -35,7 +35,7 @@ namespace gm {
 
 constexpr int HD = 256;              // head dim
 constexpr int MAXB = 64;             // streams
-constexpr int GW = 4;                // warps per GEMV CTA
+constexpr int GW = 16;               // warps per GEMV CTA (one staged input range, 16 row groups)
 constexpr int AK = 64;               // keys per attention split
 constexpr int MAXTP = 8;
 
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(GW * 32) i8_gemv_kernel(GemvArgs a) {
     extern __shared__ __align__(16) uint16_t xs[];
     __shared__ int last_flag[GW];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int split = blockIdx.y, rg = blockIdx.x * GW + warp, n_rg = (a.N + 15) / 16;
+    const int split = blockIdx.y, n_rg = (a.N + 15) / 16;
     const int k0 = split * a.kchunk, xld = a.kchunk + 8;
     for (int i = threadIdx.x; i < NT * 8 * (a.kchunk / 8); i += blockDim.x) {
         const int b = i / (a.kchunk / 8), c = i % (a.kchunk / 8);
@@ -88,7 +88,8 @@ __global__ void __launch_bounds__(GW * 32) i8_gemv_kernel(GemvArgs a) {
         *reinterpret_cast<uint4 *>(&xs[b * xld + c * 8]) = v;
     }
     __syncthreads();
-    if (rg >= n_rg) return;
+    // the staged input range serves every row group this warp owns (grid-strided)
+    for (int rg = blockIdx.x * GW + warp; rg < n_rg; rg += gridDim.x * GW) {
     float acc[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
@@ -130,23 +131,23 @@ __global__ void __launch_bounds__(GW * 32) i8_gemv_kernel(GemvArgs a) {
         __syncwarp();
         if (lane == 0) last_flag[warp] = atomicAdd(&a.count[rg], 1u) == (unsigned)a.nsplit - 1;
         __syncwarp();
-        if (!last_flag[warp]) return;
+        if (!last_flag[warp]) continue;
         __threadfence();
+        // ordered sum over the ranges: per range, all of this lane's values are requested at once
 #pragma unroll
-        for (int n = 0; n < NT; n++)
+        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+        for (int sp = 0; sp < a.nsplit; sp++) {
+            const float *ps = a.part + (size_t)sp * Np * MAXB;
+            float pv[NT][4];
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const size_t off = (size_t)(n0 + g + 8 * (e >> 1)) * MAXB + n * 8 + 2 * t + (e & 1);
-                float pv[8], sum = 0.0f;
-                for (int s0 = 0; s0 < a.nsplit; s0 += 8) {
+            for (int n = 0; n < NT; n++)
 #pragma unroll
-                    for (int u = 0; u < 8; u++) pv[u] = s0 + u < a.nsplit ? __ldcg(a.part + (size_t)(s0 + u) * Np * MAXB + off) : 0.0f;
+                for (int e = 0; e < 4; e++) pv[n][e] = __ldcg(ps + (size_t)(n0 + g + 8 * (e >> 1)) * MAXB + n * 8 + 2 * t + (e & 1));
 #pragma unroll
-                    for (int u = 0; u < 8; u++)
-                        if (s0 + u < a.nsplit) sum += pv[u];
-                }
-                acc[n][e] = sum;
-            }
+            for (int n = 0; n < NT; n++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) acc[n][e] += pv[n][e];
+        }
         if (lane == 0) a.count[rg] = 0;
     }
     const float s0v = a.scale[n0 + g], s1v = a.scale[n0 + g + 8];
@@ -164,6 +165,7 @@ __global__ void __launch_bounds__(GW * 32) i8_gemv_kernel(GemvArgs a) {
                 a.out_bf16[(size_t)b * a.ldo + rg * 8 + g] = (uint16_t)bf16bits(gelu_tanh(y0) * y1);
             }
         }
+    }
     }
 }
 
@@ -591,12 +593,12 @@ GmMat pack_i8(XdnaGemma *m, const float *w, int K, int N, const std::vector<int>
     return o;
 }
 
-// K ranges of a GEMV: as few as give about two warps per SM, each a multiple of 16 of K
+// K ranges of a GEMV: as few as give every SM a CTA of warps, each a multiple of 16 of K
 // (and short enough that 64 streams of the range fit the GEMV's shared staging)
 constexpr int kMaxChunk = 1792;
 int splits_of(int N, int K) {
     const int nrg = (N + 15) / 16, ks = K / 16;
-    int nsplit = std::min(ks, std::max(1, (2 * 148 + nrg - 1) / nrg));
+    int nsplit = std::min({ks, 8, std::max(1, (148 * gm::GW + nrg - 1) / nrg)});   // ~ a CTA of warps per SM
     while (ks % nsplit) nsplit--;
     while (K / nsplit > kMaxChunk) {
         nsplit++;
@@ -611,7 +613,8 @@ cudaError_t gemv(XdnaGemma *m, const GmMat &w, const uint16_t *x, int B, int mod
     const int nsplit = splits_of(w.N, w.K);
     const int kchunk = w.K / nsplit;
     gm::GemvArgs a{w.w, w.scale, x, B, w.N, w.K, nsplit, kchunk, m->part, m->count, mode, out, ob, ldo};
-    dim3 grid((nrg + gm::GW - 1) / gm::GW, nsplit);
+    // about one CTA per SM over all K ranges; each stages its range of X once
+    dim3 grid(std::max(1, std::min((nrg + gm::GW - 1) / gm::GW, 148 / nsplit)), nsplit);
     const int nt = (B + 7) / 8;
     const size_t smem = (size_t)nt * 8 * (kchunk + 8) * 2;
     switch (nt) {
