@@ -1,7 +1,7 @@
 """Gemma-3 decoder (xdna_gemma_*) against the oracle (npu-gemma pieces + the HF Gemma-3 model,
 int8 Lin rule), single GPU and tensor parallel over 2 GPUs when the box has them.
 
-The engine feeds bf16 activations to its int8 GEMVs (the oracle: f32) and keeps the KV cache
+The engine feeds f16 activations to its int8 GEMVs (the oracle: f32) and keeps the KV cache
 in bf16, so the greedy stream is compared token by token only while the oracle's top-2 logit
 margin exceeds the engine's expected error (the small test model's logits are ~0.08 rms;
 tolerance 0.01)."""

@@ -4,7 +4,7 @@
 // The reference has no Gemma decode step (rust/npu-gemma/src/lib.rs:30-43 lists what to
 // reuse); this is the HF Gemma-3 text model with npu-gemma's pieces (rmsnorm_ref lib.rs:55-64,
 // geglu_ref 68-77, is_global_layer config.rs:131-133).  Per token and layer:
-//   in-norm (bf16 out) -> int8 GEMV q | k | v (tensor cores, row scales in the epilogue)
+//   in-norm (f16 out) -> int8 GEMV q | k | v (tensor cores, row scales in the epilogue)
 //   -> q/k RMS norms + RoPE + cache append -> split GQA attention (the 4 q heads share the one
 //   K/V head; local layers over the last 512 positions of a ring buffer, global layers over
 //   all) + ordered merge -> GEMV o -> [all-reduce] -> post-attention norm + residual + pre-FFN
@@ -15,6 +15,8 @@
 // LM head's vocabulary rows are split; the single K/V head is replicated.  The all-reduce sums
 // the P partial vectors in rank order from every peer's buffer (CUDA IPC peer pointers,
 // flag-tagged words with bounded waits), so every rank gets the same bits.
+#include <cooperative_groups.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -32,14 +34,18 @@ namespace xdna {
 void set_last_error_message(const std::string &m);
 
 namespace gm {
+namespace cg = cooperative_groups;
 
 constexpr int HD = 256;              // head dim
 constexpr int MAXB = 64;             // streams
-constexpr int GW = 16;               // warps per GEMV CTA (one staged input range, 16 row groups)
+constexpr int GWARPS = 8;           // warps per GEMV CTA
 constexpr int AK = 64;               // keys per attention split
 constexpr int MAXTP = 8;
 
-enum { OUT_F32 = 0, OUT_GEGLU_BF16 = 1 };
+enum { OUT_F32 = 0, OUT_GEGLU_F16 = 1, OUT_ARGMAX = 2 };
+// the GeGLU output (the down projection's input) is stored divided by this power of two, so
+// that large activations stay inside the f16 range; the down GEMV multiplies it back
+constexpr float kHScale = 64.0f;
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -48,125 +54,202 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-// two int8 weights -> bf16x2 (exact: |q| <= 127)
-__device__ __forceinline__ uint32_t i8x2_bf16(uint32_t m2) {
-    return bf16bits((float)(int8_t)(m2 & 255u)) | (bf16bits((float)(int8_t)(m2 >> 8)) << 16);
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
 }
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma16816h(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// two stored weight bytes u = q + 128 -> f16x2 of q (exact): the byte becomes the low mantissa
+// of 1024 + u (exponent byte 0x64), then 1152 is subtracted.  sel picks bytes 0,1 (0x5140) or
+// 2,3 (0x7362) of the word.
+__device__ __forceinline__ uint32_t u8x2_f16(uint32_t w, uint32_t sel) {
+    const uint32_t h = __byte_perm(w, 0x64646464u, sel);
+    uint32_t r;
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
+    return r;
+}
+__device__ __forceinline__ uint16_t f16bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
 __device__ __forceinline__ float gelu_tanh(float x) {   // npu-gemma lib.rs:74-77
     const float C = 0.79788456f;
     return 0.5f * x * (1.0f + tanhf(C * (x + 0.044715f * x * x * x)));
 }
 
 struct GemvArgs {
-    const uint8_t *w;           // [row groups][K/16][32 lanes][8] int8 in mma fragment order
+    const uint8_t *w;           // [row groups][K/16][32 lanes][8] bytes q + 128 in mma fragment order
     const float *scale;         // [Np] per output row
-    const uint16_t *x;          // bf16 [B][K]
-    int B, N, K, nsplit, kchunk;
-    float *part;                // [nsplit][Np][MAXB]
-    unsigned *count;            // [row groups]
+    const uint16_t *x;          // f16 [B][K]
+    int B, N, K;
+    int R, Wk, nsplit;          // row groups per CTA, warps per row group (along K), K ranges = cluster size
+    int red_off;                // float offset of the partial-sum area in shared memory (0: aliases X)
     int mode;
+    float oscale;               // output multiplier (kHScale for the down projection, else 1)
     float *out;                 // OUT_F32: [B][ldo]
-    uint16_t *out_bf16;         // OUT_GEGLU_BF16: [B][ldo], column = row group * 8 + g
+    uint16_t *out_h;            // OUT_GEGLU_F16: [B][ldo] f16, column = row group * 8 + g, divided by kHScale
     int ldo;
+    unsigned long long *best;   // OUT_ARGMAX: [B] max of amax_key(y, base + row) (no logits are stored)
+    int base;
 };
 
-// Y[b][n] = (X[b] . Wq[n]) * scale[n]: the bfp16 GEMV design of whisper_dec.cu with per-row
-// int8 scales (warp = 16 rows x one K range, the next 8 k-steps in flight, deterministic
-// split-K reduction by the last warp).  OUT_GEGLU_BF16: row group = 8 gate rows then the 8
-// matching up rows; the epilogue writes gelu_tanh(gate) * up.
+// (value, index) -> a 64-bit key whose unsigned maximum is the largest value, and among equal
+// values the smallest index (the first maximum); 0 is below every key
+__device__ __forceinline__ unsigned long long amax_key(float v, int idx) {
+    const uint32_t b = __float_as_uint(v), o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)o << 32) | (0xffffffffu - (uint32_t)idx);
+}
+__device__ __forceinline__ void amax_unkey(unsigned long long k, float &v, int &idx) {
+    const uint32_t o = (uint32_t)(k >> 32);
+    v = __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+    idx = (int)(0xffffffffu - (uint32_t)k);
+}
+
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Y[b][n] = (X[b] . Wq[n]) * scale[n] on the f16 tensor cores (int8 weights widen exactly; f16 activations).
+// Grid (row-group blocks, K ranges); the K ranges of one row-group block form a thread-block
+// cluster.  CTA = GWARPS warps = R row groups x Wk warps along the CTA's K range.  The CTA
+// first requests its warps' first 8 k-steps of weights (they do not depend on the previous
+// kernel, which may still be running: programmatic dependent launch), then waits for the
+// previous grid and stages its X range [B][kc] with cp.async in one round trip.  Partial sums
+// go to shared memory, are added over the Wk warps and then over the cluster's K ranges through
+// distributed shared memory, in a fixed order (results do not depend on timing).
+// OUT_GEGLU_F16: row group = 8 gate rows then the 8 matching up rows; the epilogue writes
+// gelu_tanh(gate) * up.
 template <int NT>
-__global__ void __launch_bounds__(GW * 32) i8_gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(GWARPS * 32, 2) i8_gemv_kernel(GemvArgs a) {
     extern __shared__ __align__(16) uint16_t xs[];
-    __shared__ int last_flag[GW];
+    float *red = reinterpret_cast<float *>(xs) + a.red_off;
+    const uint32_t xs_a = smem_u32(xs);
+    __shared__ unsigned long long sbest[MAXB];
+    if (a.mode == OUT_ARGMAX && threadIdx.x < MAXB) sbest[threadIdx.x] = 0ull;
+    griddep_launch();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int split = blockIdx.y, n_rg = (a.N + 15) / 16;
-    const int k0 = split * a.kchunk, xld = a.kchunk + 8;
-    for (int i = threadIdx.x; i < NT * 8 * (a.kchunk / 8); i += blockDim.x) {
-        const int b = i / (a.kchunk / 8), c = i % (a.kchunk / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (b < a.B) v = *reinterpret_cast<const uint4 *>(a.x + (size_t)b * a.K + k0 + c * 8);
-        *reinterpret_cast<uint4 *>(&xs[b * xld + c * 8]) = v;
+    const int n_rg = (a.N + 15) / 16, nks = a.K / 16, split = blockIdx.y;
+    const int ks0 = split * nks / a.nsplit, nkc = (split + 1) * nks / a.nsplit - ks0, xld = nkc * 16 + 8;
+    const int r = warp / a.Wk, wk = warp % a.Wk;
+    const int w0 = wk * nkc / a.Wk, nst = (wk + 1) * nkc / a.Wk - w0, ngrp = (nst + 7) / 8;
+    const int rstride = gridDim.x * a.R;
+    uint2 mv[8], mn[8];
+    auto fetch = [&](uint2 (&dst)[8], int rg, int s0) {
+        const uint2 *mp = reinterpret_cast<const uint2 *>(a.w) + ((size_t)rg * nks + ks0 + w0 + s0) * 32 + lane;
+        const bool live = rg < n_rg;
+#pragma unroll
+        for (int s = 0; s < 8; s++) dst[s] = live && s0 + s < nst ? __ldcs(mp + s * 32) : make_uint2(0, 0);
+    };
+    fetch(mv, blockIdx.x * a.R + r, 0);
+    griddep_wait();
+    {
+        const int cpr = nkc * 2;                        // 16-byte pieces per row
+        for (int i = threadIdx.x; i < NT * 8 * cpr; i += blockDim.x) {
+            const int b = i / cpr, c = i - b * cpr;
+            uint16_t *d = &xs[b * xld + c * 8];
+            if (b < a.B) cp_async16(d, a.x + (size_t)b * a.K + ks0 * 16 + c * 8);
+            else *reinterpret_cast<uint4 *>(d) = make_uint4(0, 0, 0, 0);
+        }
+        cp_async_commit();
+        cp_async_wait_all();
     }
     __syncthreads();
-    // the staged input range serves every row group this warp owns (grid-strided)
-    for (int rg = blockIdx.x * GW + warp; rg < n_rg; rg += gridDim.x * GW) {
-    float acc[NT][4];
+    for (int rg0 = blockIdx.x * a.R; rg0 < n_rg; rg0 += rstride) {
+        const int rg = rg0 + r;
+        if (rg0 != (int)blockIdx.x * a.R) fetch(mv, rg, 0);
+        float acc[NT][4];
 #pragma unroll
-    for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-    const int nks = a.K / 16, nst = a.kchunk / 16, ngrp = (nst + 7) / 8;
-    const uint2 *mp = reinterpret_cast<const uint2 *>(a.w) + ((size_t)rg * nks + k0 / 16) * 32 + lane;
-    uint2 mv[8], mn[8];
+        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+        for (int gi = 0; gi < ngrp; gi++) {
+            if (gi + 1 < ngrp) fetch(mn, rg, (gi + 1) * 8);
 #pragma unroll
-    for (int s = 0; s < 8; s++) mv[s] = s < nst ? __ldcs(mp + s * 32) : make_uint2(0, 0);
-    for (int gi = 0; gi < ngrp; gi++) {
-        if (gi + 1 < ngrp) {
+            for (int s = 0; s < 8; s++) {
+                if (gi * 8 + s >= nst) break;
+                const uint32_t a0 = u8x2_f16(mv[s].x, 0x5140u), a1 = u8x2_f16(mv[s].x, 0x7362u);
+                const uint32_t a2 = u8x2_f16(mv[s].y, 0x5140u), a3 = u8x2_f16(mv[s].y, 0x7362u);
+                const int kk = (w0 + gi * 8 + s) * 16;
+                if constexpr (NT == 1) {
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t *>(&xs[g * xld + kk + 2 * t]);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t *>(&xs[g * xld + kk + 8 + 2 * t]);
+                    mma16816h(acc[0], a0, a1, a2, a3, b0, b1);
+                } else {
 #pragma unroll
-            for (int s = 0; s < 8; s++)
-                mn[s] = (gi + 1) * 8 + s < nst ? __ldcs(mp + ((gi + 1) * 8 + s) * 32) : make_uint2(0, 0);
-        }
-#pragma unroll
-        for (int s = 0; s < 8; s++) {
-            if (gi * 8 + s >= nst) break;
-            const uint32_t a0 = i8x2_bf16(mv[s].x & 0xffffu), a1 = i8x2_bf16(mv[s].x >> 16);
-            const uint32_t a2 = i8x2_bf16(mv[s].y & 0xffffu), a3 = i8x2_bf16(mv[s].y >> 16);
-            const int kk = (gi * 8 + s) * 16;
-#pragma unroll
-            for (int n = 0; n < NT; n++) {
-                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(&xs[(n * 8 + g) * xld + kk + 2 * t]);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(&xs[(n * 8 + g) * xld + kk + 8 + 2 * t]);
-                mma16816(acc[n], a0, a1, a2, a3, b0, b1);
+                    for (int n = 0; n < NT; n += 2) {
+                        uint32_t r0, r1, r2, r3;
+                        ldsm_x4(xs_a + 2u * ((n * 8 + ((lane >> 4) << 3) + (lane & 7)) * xld + kk + (((lane >> 3) & 1) << 3)),
+                                r0, r1, r2, r3);
+                        mma16816h(acc[n], a0, a1, a2, a3, r0, r1);
+                        mma16816h(acc[n + 1], a0, a1, a2, a3, r2, r3);
+                    }
+                }
             }
-        }
 #pragma unroll
-        for (int s = 0; s < 8; s++) mv[s] = mn[s];
-    }
-    const int n0 = rg * 16, Np = n_rg * 16;
-    if (a.nsplit > 1) {
-        float *pp = a.part + (size_t)split * Np * MAXB;
+            for (int s = 0; s < 8; s++) mv[s] = mn[s];
+        }
+        if (a.red_off == 0) __syncthreads();            // the partials overwrite the staged X
+        float *rw = red + warp * NT * 128;
 #pragma unroll
         for (int n = 0; n < NT; n++)
 #pragma unroll
-            for (int e = 0; e < 4; e++) pp[(size_t)(n0 + g + 8 * (e >> 1)) * MAXB + n * 8 + 2 * t + (e & 1)] = acc[n][e];
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) last_flag[warp] = atomicAdd(&a.count[rg], 1u) == (unsigned)a.nsplit - 1;
-        __syncwarp();
-        if (!last_flag[warp]) continue;
-        __threadfence();
-        // ordered sum over the ranges: per range, all of this lane's values are requested at once
+            for (int e = 0; e < 4; e++) rw[(n * 4 + e) * 32 + lane] = acc[n][e];
+        __syncthreads();
+        // add over the Wk warps of each row group (in place, into the wk = 0 slot)
+        if (a.Wk > 1)
+            for (int i = threadIdx.x; i < a.R * NT * 128; i += blockDim.x) {
+                const int rr = i / (NT * 128), e = i - rr * (NT * 128);
+                float sum = red[rr * a.Wk * NT * 128 + e];
+                for (int k = 1; k < a.Wk; k++) sum += red[(rr * a.Wk + k) * NT * 128 + e];
+                red[rr * a.Wk * NT * 128 + e] = sum;
+            }
+        cg::cluster_group cl = cg::this_cluster();
+        if (a.nsplit > 1) cl.sync(); else __syncthreads();
+        // outputs: item = (row group, n tile, column c, lane) -> rows g and g + 8, stream n*8 + 2t + c;
+        // this CTA takes its share of the items and adds the K ranges in rank order
+        const int items = a.R * NT * 64, i0 = split * items / a.nsplit, i1 = (split + 1) * items / a.nsplit;
+        for (int it = i0 + threadIdx.x; it < i1; it += blockDim.x) {
+            const int rr = it / (NT * 64), rem = it - rr * (NT * 64), n = rem >> 6, c = (rem >> 5) & 1, ln = rem & 31;
+            const int off = rr * a.Wk * NT * 128 + (n * 4 + c) * 32 + ln;
+            float v0 = 0.0f, v1 = 0.0f;
+            if (a.nsplit > 1) {
+                float p0[8], p1[8];
 #pragma unroll
-        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-        for (int sp = 0; sp < a.nsplit; sp++) {
-            const float *ps = a.part + (size_t)sp * Np * MAXB;
-            float pv[NT][4];
+                for (int q = 0; q < 8; q++)
+                    if (q < a.nsplit) {
+                        const float *rp = cl.map_shared_rank(red, q);
+                        p0[q] = rp[off];
+                        p1[q] = rp[off + 64];
+                    }
 #pragma unroll
-            for (int n = 0; n < NT; n++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) pv[n][e] = __ldcg(ps + (size_t)(n0 + g + 8 * (e >> 1)) * MAXB + n * 8 + 2 * t + (e & 1));
-#pragma unroll
-            for (int n = 0; n < NT; n++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) acc[n][e] += pv[n][e];
-        }
-        if (lane == 0) a.count[rg] = 0;
-    }
-    const float s0v = a.scale[n0 + g], s1v = a.scale[n0 + g + 8];
-#pragma unroll
-    for (int n = 0; n < NT; n++) {
-#pragma unroll
-        for (int c = 0; c < 2; c++) {
-            const int b = n * 8 + 2 * t + c;
-            if (b >= a.B) continue;
-            const float y0 = acc[n][c] * s0v, y1 = acc[n][2 + c] * s1v;
-            if (a.mode == OUT_F32) {
-                if (n0 + g < a.N) a.out[(size_t)b * a.ldo + n0 + g] = y0;
-                if (n0 + g + 8 < a.N) a.out[(size_t)b * a.ldo + n0 + g + 8] = y1;
+                for (int q = 0; q < 8; q++)
+                    if (q < a.nsplit) { v0 += p0[q]; v1 += p1[q]; }
             } else {
-                a.out_bf16[(size_t)b * a.ldo + rg * 8 + g] = (uint16_t)bf16bits(gelu_tanh(y0) * y1);
+                v0 = red[off];
+                v1 = red[off + 64];
+            }
+            const int orow = rg0 + rr, b = n * 8 + 2 * (ln & 3) + c, gg = ln >> 2, n0 = orow * 16;
+            if (orow >= n_rg || b >= a.B) continue;
+            const float y0 = v0 * a.scale[n0 + gg] * a.oscale, y1 = v1 * a.scale[n0 + gg + 8] * a.oscale;
+            if (a.mode == OUT_F32) {
+                if (n0 + gg < a.N) a.out[(size_t)b * a.ldo + n0 + gg] = y0;
+                if (n0 + gg + 8 < a.N) a.out[(size_t)b * a.ldo + n0 + gg + 8] = y1;
+            } else if (a.mode == OUT_ARGMAX) {
+                unsigned long long k = n0 + gg < a.N ? amax_key(y0, a.base + n0 + gg) : 0ull;
+                if (n0 + gg + 8 < a.N) k = max(k, amax_key(y1, a.base + n0 + gg + 8));
+                atomicMax(&sbest[b], k);
+            } else {
+                a.out_h[(size_t)b * a.ldo + orow * 8 + gg] = f16bits(gelu_tanh(y0) * y1 * (1.0f / kHScale));
             }
         }
+        if (a.nsplit > 1) cl.sync(); else __syncthreads();   // partials stay until every CTA has read them
     }
-    }
+    if (a.mode == OUT_ARGMAX && threadIdx.x < a.B && sbest[threadIdx.x]) atomicMax(&a.best[threadIdx.x], sbest[threadIdx.x]);
 }
 
 // RMS norm of a row held by one warp: v[i] = x[lane + 32 i], D = 32 * NPL
@@ -180,11 +263,12 @@ __device__ __forceinline__ float rms_inv(const float (&v)[NPL], int D, float eps
     return 1.0f / sqrtf(s / (float)D + eps);
 }
 
-// x[b] = embed[tok[b]] * sqrt(D); xn = bf16(rms(x) * (1 + w)); one warp per stream
+// x[b] = embed[tok[b]] * sqrt(D); xn = f16(rms(x) * (1 + w)); one warp per stream
 template <int NPL>
 __global__ void embed_norm_kernel(const int64_t *__restrict__ tok, const float *__restrict__ emb, float es, int B,
                                   const float *__restrict__ w, float eps, float *__restrict__ x,
                                   uint16_t *__restrict__ xn) {
+    griddep_launch();                                 // the next GEMV may start its weight fetch
     const int b = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (b >= B) return;
     constexpr int D = 32 * NPL;
@@ -196,15 +280,16 @@ __global__ void embed_norm_kernel(const int64_t *__restrict__ tok, const float *
 #pragma unroll
     for (int i = 0; i < NPL; i++) {
         x[(size_t)b * D + lane + 32 * i] = v[i];
-        xn[(size_t)b * D + lane + 32 * i] = (uint16_t)bf16bits(v[i] * inv * (1.0f + wv[i]));
+        xn[(size_t)b * D + lane + 32 * i] = f16bits(v[i] * inv * (1.0f + wv[i]));
     }
 }
 
-// x += rms(y) * (1 + w_post); xn = bf16(rms(x) * (1 + w_next)); one warp per stream
+// x += rms(y) * (1 + w_post); xn = f16(rms(x) * (1 + w_next)); one warp per stream
 template <int NPL>
 __global__ void post_add_norm_kernel(const float *__restrict__ y, int B, const float *__restrict__ wpost,
                                      const float *__restrict__ wnext, float eps, float *__restrict__ x,
                                      uint16_t *__restrict__ xn) {
+    griddep_launch();
     const int b = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (b >= B) return;
     constexpr int D = 32 * NPL;
@@ -223,7 +308,7 @@ __global__ void post_add_norm_kernel(const float *__restrict__ y, int B, const f
 #pragma unroll
     for (int i = 0; i < NPL; i++) {
         x[(size_t)b * D + lane + 32 * i] = xv[i];
-        xn[(size_t)b * D + lane + 32 * i] = (uint16_t)bf16bits(xv[i] * inv2 * (1.0f + wn[i]));
+        xn[(size_t)b * D + lane + 32 * i] = f16bits(xv[i] * inv2 * (1.0f + wn[i]));
     }
 }
 
@@ -265,58 +350,83 @@ __global__ void __launch_bounds__(HD) qk_prep_kernel(const float *__restrict__ q
     vc[slot * HD + d] = (uint16_t)bf16bits(r[(hq + 1) * HD + d]);
 }
 
-// split attention: block (split s, stream b) takes AK cache slots; every local q head against
-// the shared K/V head; writes per head (max, sum, acc[256]).  Keys visible: positions
-// [lo, pos] with lo = max(0, pos - window + 1) for local layers (ring of cache_len slots).
-__global__ void __launch_bounds__(256) gqa_attn_kernel(const float *__restrict__ q, int hq, const int *posp,
+// One K range (AK keys) of one stream's attention for the hq query heads that share the K/V
+// head, on the tensor cores: the range's K and V rows are staged with cp.async (16-byte chunks
+// XOR-swizzled by key so ldmatrix is conflict-free; K and V in separate groups, so the scores
+// start while V still arrives); warp w scores keys [16w, 16w + 16) for all heads
+// (mma m16n8k16, query rows padded to 16 with zeros, Q from f32 rounded to bf16); softmax
+// statistics per head; then warp w accumulates P.V for dims [64w, 64w + 64) with P in bf16.
+// Writes the range's (max, sum, unnormalised output) per head for the ordered merge.  Keys
+// visible: positions [lo, pos] with lo = max(0, pos - window + 1) for local layers (ring of
+// cache_len slots), lo = 0 for global ones.
+__device__ __forceinline__ uint32_t kv_off(int key, int chunk) {      // byte offset in a K or V tile
+    return (uint32_t)(key * (HD * 2) + ((chunk ^ (key & 7)) << 4));
+}
+__global__ void __launch_bounds__(128) gqa_attn_kernel(const float *__restrict__ q, int hq, const int *posp,
                                                        int window, int cache_len, const uint16_t *__restrict__ kc,
                                                        const uint16_t *__restrict__ vc, float scaling,
                                                        float *__restrict__ part, int nsplit) {
-    extern __shared__ __align__(16) uint16_t kv[];           // K [AK][HD] then V [AK][HD]
-    __shared__ float qs[4][HD], sc[4][AK], stat[4][2];
+    extern __shared__ __align__(128) uint8_t kvs[];          // K [AK][HD] then V [AK][HD], swizzled
+    __shared__ float sc[4][AK], stat[4][2];
+    __shared__ __align__(16) uint16_t ps[4][AK + 8];
     const int s = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, pos = *posp;
+    const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     const int lo = window > 0 ? max(0, pos - window + 1) : 0;
     const int p0 = lo + s * AK;
     const int nk = max(0, min(AK, pos + 1 - p0));
     float *pp = part + ((size_t)b * nsplit + s) * 4 * (HD + 2);
     if (nk == 0) {
         if (tid < hq) { pp[tid * (HD + 2)] = -INFINITY; pp[tid * (HD + 2) + 1] = 0.0f; }
-        for (int i = tid; i < hq * HD; i += 256) pp[(i / HD) * (HD + 2) + 2 + i % HD] = 0.0f;
+        for (int i = tid; i < hq * HD; i += 128) pp[(i / HD) * (HD + 2) + 2 + i % HD] = 0.0f;
         return;
     }
-    uint16_t *ks = kv, *vs = kv + AK * HD;
-    for (int i = tid; i < nk * (HD / 8); i += 256) {
-        const int j = i / (HD / 8), c = i % (HD / 8);
-        const size_t slot = (size_t)b * cache_len + (p0 + j) % cache_len;
-        reinterpret_cast<uint4 *>(ks)[i] = reinterpret_cast<const uint4 *>(kc + slot * HD)[c];
-        reinterpret_cast<uint4 *>(vs)[i] = reinterpret_cast<const uint4 *>(vc + slot * HD)[c];
+    uint8_t *ks = kvs, *vs = kvs + AK * HD * 2;
+    const uint32_t ks_a = smem_u32(ks), vs_a = smem_u32(vs);
+    for (int i = tid; i < AK * (HD / 8); i += 128) {
+        const int j = i >> 5, c = i & 31;
+        if (j < nk) cp_async16(ks + kv_off(j, c), kc + ((size_t)b * cache_len + (p0 + j) % cache_len) * HD + c * 8);
     }
-    for (int i = tid; i < hq * HD; i += 256) qs[i / HD][i % HD] = q[(size_t)b * hq * HD + i];
-    __syncthreads();
-    // scores: thread = (head, key)
+    cp_async_commit();
+    for (int i = tid; i < AK * (HD / 8); i += 128) {
+        const int j = i >> 5, c = i & 31;
+        if (j < nk) cp_async16(vs + kv_off(j, c), vc + ((size_t)b * cache_len + (p0 + j) % cache_len) * HD + c * 8);
+        else *reinterpret_cast<uint4 *>(vs + kv_off(j, c)) = make_uint4(0, 0, 0, 0);   // P = 0 there, V must be finite
+    }
+    cp_async_commit();
+    // query fragments (rows g < hq; rows g + 8 are padding): a0 = Q[g][16k + 2t..], a2 = Q[g][16k + 8 + 2t..]
+    uint32_t qa[16][2];
     {
-        const int hh = tid / AK, j = tid % AK;
-        if (hh < hq) {
-            float dot = -INFINITY;
-            if (j < nk) {
-                dot = 0.0f;
-                const uint4 *kr = reinterpret_cast<const uint4 *>(ks + j * HD);
-#pragma unroll 4
-                for (int c0 = 0; c0 < HD / 8; c0++) {
-                    const int c = (c0 + j) & (HD / 8 - 1);
-                    const uint4 w = kr[c];
-                    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+        const float *qr = q + ((size_t)b * hq + (g < hq ? g : 0)) * HD;
 #pragma unroll
-                    for (int e = 0; e < 4; e++) dot += qs[hh][8 * c + 2 * e] * bf16lo(u[e]) + qs[hh][8 * c + 2 * e + 1] * bf16hi(u[e]);
-                }
-                dot *= scaling;
-            }
-            sc[hh][j] = dot;
+        for (int k = 0; k < 16; k++) {
+            const float2 x0 = *reinterpret_cast<const float2 *>(qr + 16 * k + 2 * t);
+            const float2 x1 = *reinterpret_cast<const float2 *>(qr + 16 * k + 8 + 2 * t);
+            qa[k][0] = g < hq ? bf16bits(x0.x) | (bf16bits(x0.y) << 16) : 0u;
+            qa[k][1] = g < hq ? bf16bits(x1.x) | (bf16bits(x1.y) << 16) : 0u;
         }
     }
+    cp_async_wait_group<1>();
     __syncthreads();
-    // per head max / exp / sum: warp w < hq (two keys per lane)
-    const int warp = tid >> 5, lane = tid & 31;
+    {
+        float acc[2][4] = {};
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            uint32_t r0, r1, r2, r3;
+            const int key = 16 * warp + ((lane >> 4) << 3) + (lane & 7), ch = 2 * k + ((lane >> 3) & 1);
+            ldsm_x4(ks_a + kv_off(key, ch), r0, r1, r2, r3);
+            mma16816(acc[0], qa[k][0], 0u, qa[k][1], 0u, r0, r1);
+            mma16816(acc[1], qa[k][0], 0u, qa[k][1], 0u, r2, r3);
+        }
+        if (g < hq)
+#pragma unroll
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    const int j = 16 * warp + 8 * n + 2 * t + c;
+                    sc[g][j] = j < nk ? acc[n][c] * scaling : -INFINITY;
+                }
+    }
+    __syncthreads();
     if (warp < hq) {
         const float a0 = sc[warp][lane], a1 = sc[warp][lane + 32];
         float m = fmaxf(a0, a1);
@@ -326,22 +436,39 @@ __global__ void __launch_bounds__(256) gqa_attn_kernel(const float *__restrict__
         float l = e0 + e1;
 #pragma unroll
         for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        sc[warp][lane] = e0;
-        sc[warp][lane + 32] = e1;
+        ps[warp][lane] = (uint16_t)bf16bits(e0);
+        ps[warp][lane + 32] = (uint16_t)bf16bits(e1);
         if (lane == 0) { stat[warp][0] = m; stat[warp][1] = l; }
     }
+    cp_async_wait_group<0>();
     __syncthreads();
-    // acc[head][d]: thread = d, loop heads
-    for (int hh = 0; hh < hq; hh++) {
-        float a = 0.0f;
-        for (int j = 0; j < nk; j++) a += sc[hh][j] * bf16lo(vs[j * HD + tid]);
-        pp[hh * (HD + 2) + 2 + tid] = a;
+    {
+        float acc[8][4] = {};
+#pragma unroll
+        for (int k = 0; k < AK / 16; k++) {
+            const uint32_t a0 = g < hq ? *reinterpret_cast<const uint32_t *>(&ps[g][16 * k + 2 * t]) : 0u;
+            const uint32_t a2 = g < hq ? *reinterpret_cast<const uint32_t *>(&ps[g][16 * k + 8 + 2 * t]) : 0u;
+#pragma unroll
+            for (int n = 0; n < 8; n += 2) {
+                uint32_t r0, r1, r2, r3;
+                const int key = 16 * k + (((lane >> 3) & 1) << 3) + (lane & 7), ch = 8 * warp + n + (lane >> 4);
+                ldsm_x4_t(vs_a + kv_off(key, ch), r0, r1, r2, r3);
+                mma16816(acc[n], a0, 0u, a2, 0u, r0, r1);
+                mma16816(acc[n + 1], a0, 0u, a2, 0u, r2, r3);
+            }
+        }
+        if (g < hq)
+#pragma unroll
+            for (int n = 0; n < 8; n++)
+                *reinterpret_cast<float2 *>(&pp[g * (HD + 2) + 2 + 64 * warp + 8 * n + 2 * t]) =
+                    make_float2(acc[n][0], acc[n][1]);
     }
     if (tid < hq) { pp[tid * (HD + 2)] = stat[tid][0]; pp[tid * (HD + 2) + 1] = stat[tid][1]; }
 }
 
-// fold the splits in order -> ctx bf16 [B][hq * 256]; block = (head, stream), thread = dim
+// fold the splits in order -> ctx f16 [B][hq * 256]; block = (head, stream), thread = dim
 __global__ void gqa_merge_kernel(const float *__restrict__ part, int hq, int nsplit, uint16_t *__restrict__ ctx) {
+    griddep_launch();
     const int hh = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     float M = -INFINITY, L = 0.0f, A = 0.0f;
     for (int s0 = 0; s0 < nsplit; s0 += 8) {
@@ -363,42 +490,22 @@ __global__ void gqa_merge_kernel(const float *__restrict__ part, int hq, int nsp
             M = mn;
         }
     }
-    ctx[((size_t)b * hq + hh) * HD + d] = (uint16_t)bf16bits(A / L);
+    ctx[((size_t)b * hq + hh) * HD + d] = f16bits(A / L);
 }
 
-// per stream: the first maximum of this rank's logit slice -> (value, global index)
-__global__ void __launch_bounds__(1024) argmax_local_kernel(const float *__restrict__ logits, int n, int ldl,
-                                                            int base, float *__restrict__ bestv, int *__restrict__ besti) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    const int b = blockIdx.x, tid = threadIdx.x;
-    const float *lr = logits + (size_t)b * ldl;
-    float best = -INFINITY;
-    int idx = 0x7fffffff;
-    for (int i = tid; i < n; i += blockDim.x) {
-        const float v = lr[i];
-        if (v > best) { best = v; idx = i; }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
-    }
-    if ((tid & 31) == 0) { bv[tid >> 5] = best; bi[tid >> 5] = idx; }
-    __syncthreads();
-    if (tid == 0) {
-        for (int w = 1; w < 32; w++)
-            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
-        bestv[b] = best;
-        besti[b] = base + idx;
-    }
+// this rank's (value, index) per stream from the LM head's keys; clears the keys for the next step
+__global__ void unpack_best_kernel(unsigned long long *keys, int B, float *bestv, int *besti) {
+    const int b = threadIdx.x;
+    if (b >= B) return;
+    amax_unkey(keys[b], bestv[b], besti[b]);
+    keys[b] = 0ull;
 }
 
 // next token per stream from the P ranks' (value, index) pairs (first maximum overall), or the
 // prompt while it lasts; records generated tokens; the last block advances *pos
 __global__ void pick_kernel(const float *bestv, const int *besti, int P, int B, const int64_t *prompt, int n_prompt,
-                            int *posp, int64_t *tok, int64_t *out, int n_new, unsigned *done) {
+                            int *posp, int64_t *tok, int64_t *out, int n_new, unsigned *done, uint32_t *ebase,
+                            uint32_t ex_step) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     const int pos = *posp;
     if (b < B) {
@@ -421,7 +528,11 @@ __global__ void pick_kernel(const float *bestv, const int *besti, int P, int B, 
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        if (atomicAdd(done, 1u) == gridDim.x - 1) { *done = 0; *posp = pos + 1; }
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            *done = 0;
+            *posp = pos + 1;
+            *ebase += ex_step;                     // the next step's exchanges use fresh epochs
+        }
     }
 }
 
@@ -434,8 +545,9 @@ __global__ void pick_kernel(const float *bestv, const int *besti, int P, int B, 
 // any peer (it cannot finish exchange e+1 before every peer has finished exchange e), so the
 // slot it overwrites at e+2 has been read.  Slot layout: bufs[r][parity][n].
 __global__ void tp_allreduce_kernel(const float *__restrict__ y, int n, uint64_t *const *bufs, int P, int rank,
-                                    uint32_t epoch, float *__restrict__ out, unsigned *err) {
+                                    const uint32_t *ebase, uint32_t off, float *__restrict__ out, unsigned *err) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t epoch = *ebase + off;
     const size_t slot = (size_t)(epoch & 1u) * n;
     if (i < n) {
         const uint64_t wv = ((uint64_t)epoch << 32) | __float_as_uint(y[i]);
@@ -458,9 +570,10 @@ __global__ void tp_allreduce_kernel(const float *__restrict__ y, int n, uint64_t
 }
 
 // gather every rank's per-stream (value, index) pairs through the same exchange slots
-__global__ void tp_gather_best_kernel(int B, uint64_t *const *bufs, int P, int rank, uint32_t epoch, float *bestv,
-                                      int *besti, unsigned *err) {
+__global__ void tp_gather_best_kernel(int B, uint64_t *const *bufs, int P, int rank, const uint32_t *ebase,
+                                      uint32_t off, float *bestv, int *besti, unsigned *err) {
     const int i = threadIdx.x;                     // 2 * MAXB words: values then indices
+    const uint32_t epoch = *ebase + off;
     const int n = 2 * MAXB;
     const size_t slot = (size_t)(epoch & 1u) * n;
     if (i < n) {
@@ -514,6 +627,7 @@ struct GmMat {
     uint8_t *w = nullptr;
     float *scale = nullptr;
     int N = 0, K = 0;
+    float oscale = 1.0f;                  // output multiplier undoing an input prescale
 };
 
 struct XdnaGemma {
@@ -530,11 +644,11 @@ struct XdnaGemma {
     GmMat lm;
     float *emb = nullptr, *final_norm = nullptr;
     // state
-    float *x = nullptr, *qkv = nullptr, *q = nullptr, *y = nullptr, *yr = nullptr, *logits = nullptr, *part = nullptr,
-          *apart = nullptr, *bestv = nullptr;
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *y = nullptr, *yr = nullptr, *apart = nullptr, *bestv = nullptr;
     int *besti = nullptr;
+    unsigned long long *lmbest = nullptr;  // LM head: per stream max key of (logit, vocabulary index)
     uint16_t *xn = nullptr, *ctx = nullptr, *h = nullptr;
-    unsigned *count = nullptr, *done = nullptr, *err = nullptr;
+    unsigned *done = nullptr, *err = nullptr;
     int *pos = nullptr;
     int64_t *tok = nullptr, *prompt = nullptr, *out = nullptr;
     int n_prompt_cap = 0;
@@ -543,9 +657,18 @@ struct XdnaGemma {
     uint64_t *xbuf = nullptr;
     uint64_t **dbufs = nullptr;
     std::vector<void *> peer_maps;
-    uint32_t epoch = 0;
+    uint32_t *ebase = nullptr;             // device: epoch base of this step's exchanges
+    struct Graph {
+        int B, n_prompt, n_new;
+        cudaGraphExec_t exec;
+    };
+    std::vector<Graph> graphs;            // one decode step per staged shape
+    cudaStream_t cap = nullptr;
     std::vector<void *> owned;
     ~XdnaGemma() {
+        for (auto &g : graphs)
+            if (g.exec) cudaGraphExecDestroy(g.exec);
+        if (cap) cudaStreamDestroy(cap);
         for (void *p : peer_maps) cudaIpcCloseMemHandle(p);
         for (void *p : owned) cudaFree(p);
     }
@@ -581,7 +704,9 @@ GmMat pack_i8(XdnaGemma *m, const float *w, int K, int N, const std::vector<int>
                 const int8_t v[8] = {q[(size_t)r0 * K + k], q[(size_t)r0 * K + k + 1], q[(size_t)r1 * K + k],
                                      q[(size_t)r1 * K + k + 1], q[(size_t)r0 * K + k + 8], q[(size_t)r0 * K + k + 9],
                                      q[(size_t)r1 * K + k + 8], q[(size_t)r1 * K + k + 9]};
-                std::memcpy(&packed[(((size_t)rg * nks + ks) * 32 + lane) * 8], v, 8);
+                uint8_t u[8];                  // stored as q + 128 (the kernel's f16 widening)
+                for (int i = 0; i < 8; i++) u[i] = (uint8_t)(v[i] + 128);
+                std::memcpy(&packed[(((size_t)rg * nks + ks) * 32 + lane) * 8], u, 8);
             }
     GmMat o;
     o.N = R;
@@ -593,45 +718,71 @@ GmMat pack_i8(XdnaGemma *m, const float *w, int K, int N, const std::vector<int>
     return o;
 }
 
-// K ranges of a GEMV: as few as give every SM a CTA of warps, each a multiple of 16 of K
-// (and short enough that 64 streams of the range fit the GEMV's shared staging)
-constexpr int kMaxChunk = 1792;
-int splits_of(int N, int K) {
+// GEMV launch shape: the largest row-group block per CTA (more reuse of the staged X) and the
+// fewest K ranges that still give about 1.3 CTAs per SM, within the shared memory that lets two
+// CTAs share an SM.  One pass when the grid covers every row group, else CTAs loop over row-group
+// blocks with the staged X kept (then the partial sums get their own area).
+struct GemvPlan {
+    int R, nsplit, gx, red_off;
+    size_t smem;
+};
+constexpr size_t kGemvSmemCap = 113 * 1024;
+GemvPlan plan_of(int N, int K, int nt) {
     const int nrg = (N + 15) / 16, ks = K / 16;
-    int nsplit = std::min({ks, 8, std::max(1, (148 * gm::GW + nrg - 1) / nrg)});   // ~ a CTA of warps per SM
-    while (ks % nsplit) nsplit--;
-    while (K / nsplit > kMaxChunk) {
-        nsplit++;
-        while (ks % nsplit) nsplit++;
-    }
-    return nsplit;
+    GemvPlan best{1, 1, 1, 0, 0};
+    long best_ctas = -1;
+    for (int R : {8, 4, 2, 1})
+        for (int ns : {1, 2, 4, 8}) {
+            if (ns > ks) continue;
+            const int kc = (ks + ns - 1) / ns * 16, blocks = (nrg + R - 1) / R;
+            const size_t xsb = (size_t)nt * 8 * (kc + 8) * 2, redb = (size_t)gm::GWARPS * nt * 128 * 4;
+            const int gx = std::min(blocks, std::max(1, 296 / ns));
+            const bool loop = gx < blocks;
+            const size_t smem = loop ? xsb + redb : std::max(xsb, redb);
+            if (smem > kGemvSmemCap) continue;
+            const long ctas = (long)blocks * ns;
+            const GemvPlan p{R, ns, gx, loop ? (int)(xsb / 4) : 0, smem};
+            if (ctas >= 190) return p;
+            if (ctas > best_ctas) { best = p; best_ctas = ctas; }
+        }
+    if (best_ctas < 0) throw std::runtime_error("GEMV shape does not fit shared memory");
+    return best;
 }
 
 cudaError_t gemv(XdnaGemma *m, const GmMat &w, const uint16_t *x, int B, int mode, float *out, uint16_t *ob, int ldo,
                  cudaStream_t st) {
-    const int nrg = (w.N + 15) / 16;
-    const int nsplit = splits_of(w.N, w.K);
-    const int kchunk = w.K / nsplit;
-    gm::GemvArgs a{w.w, w.scale, x, B, w.N, w.K, nsplit, kchunk, m->part, m->count, mode, out, ob, ldo};
-    // about one CTA per SM over all K ranges; each stages its range of X once
-    dim3 grid(std::max(1, std::min((nrg + gm::GW - 1) / gm::GW, 148 / nsplit)), nsplit);
-    const int nt = (B + 7) / 8;
-    const size_t smem = (size_t)nt * 8 * (kchunk + 8) * 2;
+    const int nt = B <= 8 ? 1 : B <= 16 ? 2 : B <= 32 ? 4 : 8;
+    GemvPlan p;
+    try { p = plan_of(w.N, w.K, nt); } catch (...) { return cudaErrorInvalidValue; }
+    gm::GemvArgs a{w.w, w.scale, x, B, w.N, w.K, p.R, gm::GWARPS / p.R, p.nsplit, p.red_off, mode, w.oscale, out, ob, ldo,
+                   m->lmbest, m->v_base};
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(p.gx, p.nsplit);
+    lc.blockDim = dim3(gm::GWARPS * 32);
+    lc.dynamicSmemBytes = p.smem;
+    lc.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = p.nsplit;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 2;
     switch (nt) {
-    case 1: gm::i8_gemv_kernel<1><<<grid, gm::GW * 32, smem, st>>>(a); break;
-    case 2: gm::i8_gemv_kernel<2><<<grid, gm::GW * 32, smem, st>>>(a); break;
-    case 3: case 4: gm::i8_gemv_kernel<4><<<grid, gm::GW * 32, smem, st>>>(a); break;
-    default: gm::i8_gemv_kernel<8><<<grid, gm::GW * 32, smem, st>>>(a); break;
+    case 1: return cudaLaunchKernelEx(&lc, gm::i8_gemv_kernel<1>, a);
+    case 2: return cudaLaunchKernelEx(&lc, gm::i8_gemv_kernel<2>, a);
+    case 4: return cudaLaunchKernelEx(&lc, gm::i8_gemv_kernel<4>, a);
+    default: return cudaLaunchKernelEx(&lc, gm::i8_gemv_kernel<8>, a);
     }
-    return cudaGetLastError();
 }
 
-// sum partial vectors y [B][D] over the ranks into out (or copy when tp == 1)
-cudaError_t allreduce(XdnaGemma *m, const float *y, int B, float *out, cudaStream_t st) {
+// sum partial vectors y [B][D] over the ranks into out (nothing to do when tp == 1)
+cudaError_t allreduce(XdnaGemma *m, const float *y, int B, float *out, uint32_t off, cudaStream_t st) {
     const int n = B * kD;
-    if (m->tp == 1) return cudaMemcpyAsync(out, y, sizeof(float) * n, cudaMemcpyDeviceToDevice, st);
-    m->epoch++;
-    gm::tp_allreduce_kernel<<<(n + 255) / 256, 256, 0, st>>>(y, n, m->dbufs, m->tp, m->rank, m->epoch, out, m->err);
+    if (m->tp == 1) return cudaSuccess;             // the caller reads y itself
+    gm::tp_allreduce_kernel<<<(n + 255) / 256, 256, 0, st>>>(y, n, m->dbufs, m->tp, m->rank, m->ebase, off, out, m->err);
     return cudaGetLastError();
 }
 
@@ -640,6 +791,8 @@ cudaError_t step(XdnaGemma *m, int B, int n_prompt, int n_new, cudaStream_t st) 
     const auto &c = m->cfg;
     const float eps = c.eps;
     cudaError_t e = cudaSuccess;
+    uint32_t ex = 0;                               // exchanges so far in this step (epoch offsets)
+    const float *yin = m->tp == 1 ? m->y : m->yr;  // the (all-reduced) output of o and down
     embed_norm_kernel<kNPL><<<(B + 3) / 4, 128, 0, st>>>(m->tok, m->emb, sqrtf((float)kD), B, m->layers[0].norms, eps,
                                                          m->x, m->xn);
     const int hq = m->hq;
@@ -651,31 +804,29 @@ cudaError_t step(XdnaGemma *m, int B, int n_prompt, int n_new, cudaStream_t st) 
                                          nrm + kD, nrm + kD + HD, eps, L.cache_len, L.kc, L.vc, m->q);
         const int span = L.global ? m->max_ctx : c.window;
         const int nsplit = (span + AK - 1) / AK;
-        gqa_attn_kernel<<<dim3(nsplit, B), 256, 2 * AK * HD * 2, st>>>(m->q, hq, m->pos, L.global ? 0 : c.window,
+        gqa_attn_kernel<<<dim3(nsplit, B), 128, 2 * AK * HD * 2, st>>>(m->q, hq, m->pos, L.global ? 0 : c.window,
                                                                     L.cache_len, L.kc, L.vc,
                                                                     1.0f / sqrtf(c.query_pre_attn_scalar), m->apart, nsplit);
         gqa_merge_kernel<<<dim3(hq, B), HD, 0, st>>>(m->apart, hq, nsplit, m->ctx);
         if ((e = gemv(m, L.o, m->ctx, B, OUT_F32, m->y, nullptr, kD, st))) break;
-        if ((e = allreduce(m, m->y, B, m->yr, st))) break;
-        post_add_norm_kernel<kNPL><<<(B + 3) / 4, 128, 0, st>>>(m->yr, B, nrm + kD + 2 * HD, nrm + 2 * kD + 2 * HD, eps,
+        if ((e = allreduce(m, m->y, B, m->yr, ++ex, st))) break;
+        post_add_norm_kernel<kNPL><<<(B + 3) / 4, 128, 0, st>>>(yin, B, nrm + kD + 2 * HD, nrm + 2 * kD + 2 * HD, eps,
                                                                 m->x, m->xn);
-        if ((e = gemv(m, L.gu, m->xn, B, OUT_GEGLU_BF16, nullptr, m->h, m->f_loc, st))) break;
+        if ((e = gemv(m, L.gu, m->xn, B, OUT_GEGLU_F16, nullptr, m->h, m->f_loc, st))) break;
         if ((e = gemv(m, L.down, m->h, B, OUT_F32, m->y, nullptr, kD, st))) break;
-        if ((e = allreduce(m, m->y, B, m->yr, st))) break;
+        if ((e = allreduce(m, m->y, B, m->yr, ++ex, st))) break;
         const float *wnext = l + 1 < c.n_layers ? m->layers[l + 1].norms : m->final_norm;
-        post_add_norm_kernel<kNPL><<<(B + 3) / 4, 128, 0, st>>>(m->yr, B, nrm + 3 * kD + 2 * HD, wnext, eps, m->x, m->xn);
+        post_add_norm_kernel<kNPL><<<(B + 3) / 4, 128, 0, st>>>(yin, B, nrm + 3 * kD + 2 * HD, wnext, eps, m->x, m->xn);
     }
     if (e) return e;
-    const int ldl = (m->v_loc + 15) / 16 * 16;
-    if ((e = gemv(m, m->lm, m->xn, B, OUT_F32, m->logits, nullptr, ldl, st))) return e;
-    argmax_local_kernel<<<B, 1024, 0, st>>>(m->logits, m->v_loc, ldl, m->v_base, m->bestv + m->rank * MAXB,
+    if ((e = gemv(m, m->lm, m->xn, B, OUT_ARGMAX, nullptr, nullptr, 0, st))) return e;
+    unpack_best_kernel<<<1, MAXB, 0, st>>>(m->lmbest, B, m->bestv + m->rank * MAXB,
                                             m->besti + m->rank * MAXB);
-    if (m->tp > 1) {
-        m->epoch++;
-        tp_gather_best_kernel<<<1, 2 * MAXB, 0, st>>>(B, m->dbufs, m->tp, m->rank, m->epoch, m->bestv, m->besti, m->err);
-    }
+    if (m->tp > 1)
+        tp_gather_best_kernel<<<1, 2 * MAXB, 0, st>>>(B, m->dbufs, m->tp, m->rank, m->ebase, ++ex, m->bestv, m->besti,
+                                                     m->err);
     pick_kernel<<<1, MAXB, 0, st>>>(m->bestv, m->besti, m->tp == 1 ? 1 : m->tp, B, m->prompt, n_prompt, m->pos, m->tok,
-                                    m->out, n_new, m->done);
+                                    m->out, n_new, m->done, m->ebase, ex);
     return cudaGetLastError();
 }
 }  // namespace
@@ -770,6 +921,7 @@ XdnaGemma *xdna_gemma_create(XdnaDevice *dev_unused, const XdnaGemmaConfig *cfg,
                 std::vector<int> cols(kD);
                 for (int n = 0; n < kD; n++) cols[n] = n;
                 o.down = pack_i8(m, L.wd + (size_t)f0 * kD, m->f_loc, kD, cols);
+                o.down.oscale = gm::kHScale;   // its input is the GeGLU output divided by kHScale
             }
             o.norms = f32({{L.in_norm, (size_t)kD}, {L.q_norm, (size_t)HD}, {L.k_norm, (size_t)HD},
                            {L.post_attn_norm, (size_t)kD}, {L.pre_ffn_norm, (size_t)kD}, {L.post_ffn_norm, (size_t)kD}});
@@ -788,23 +940,19 @@ XdnaGemma *xdna_gemma_create(XdnaDevice *dev_unused, const XdnaGemmaConfig *cfg,
         }
         m->emb = f32({{w->embed, (size_t)c.vocab * kD}});
         m->final_norm = f32({{w->final_norm, (size_t)kD}});
-        const int hqmax = 4, ldl = (m->v_loc + 15) / 16 * 16;
+        const int hqmax = 4;
         m->x = static_cast<float *>(keep(dalloc<float>(B * kD)));
         m->qkv = static_cast<float *>(keep(dalloc<float>(B * (hqmax + 2) * HD)));
         m->q = static_cast<float *>(keep(dalloc<float>(B * hqmax * HD)));
         m->y = static_cast<float *>(keep(dalloc<float>(B * kD)));
         m->yr = static_cast<float *>(keep(dalloc<float>(B * kD)));
-        m->logits = static_cast<float *>(keep(dalloc<float>(B * ldl)));
-        size_t part = 0, rows_max = 0;
-        auto acct = [&](const GmMat &g) {
-            const size_t np = (size_t)(g.N + 15) / 16 * 16;
-            rows_max = std::max(rows_max, np);
-            const int ns = splits_of(g.N, g.K);
-            if (ns > 1) part = std::max(part, (size_t)ns * np);
-        };
-        for (auto &L : m->layers) { acct(L.qkv); acct(L.o); acct(L.gu); acct(L.down); }
-        acct(m->lm);
-        m->part = static_cast<float *>(keep(dalloc<float>(std::max<size_t>(part, 1) * MAXB)));
+        m->lmbest = static_cast<unsigned long long *>(keep(dalloc<unsigned long long>(MAXB)));
+        ck(cudaMemset(m->lmbest, 0, sizeof(unsigned long long) * MAXB), "memset");
+        for (int nt : {1, 2, 4, 8}) {              // every GEMV shape has a launch plan
+            for (auto &L : m->layers) { plan_of(L.qkv.N, L.qkv.K, nt); plan_of(L.o.N, L.o.K, nt);
+                                        plan_of(L.gu.N, L.gu.K, nt); plan_of(L.down.N, L.down.K, nt); }
+            plan_of(m->lm.N, m->lm.K, nt);
+        }
         const int nsplit_max = (std::max(max_ctx, c.window) + AK - 1) / AK;
         m->apart = static_cast<float *>(keep(dalloc<float>(B * nsplit_max * 4 * (HD + 2))));
         m->bestv = static_cast<float *>(keep(dalloc<float>(MAXTP * MAXB)));
@@ -812,20 +960,19 @@ XdnaGemma *xdna_gemma_create(XdnaDevice *dev_unused, const XdnaGemmaConfig *cfg,
         m->xn = static_cast<uint16_t *>(keep(dalloc<uint16_t>(B * kD)));
         m->ctx = static_cast<uint16_t *>(keep(dalloc<uint16_t>(B * hqmax * HD)));
         m->h = static_cast<uint16_t *>(keep(dalloc<uint16_t>(B * m->f_loc)));
-        const size_t rg_max = rows_max / 16 + 1;
-        m->count = static_cast<unsigned *>(keep(dalloc<unsigned>(rg_max)));
         m->done = static_cast<unsigned *>(keep(dalloc<unsigned>(1)));
         m->err = static_cast<unsigned *>(keep(dalloc<unsigned>(1)));
+        m->ebase = static_cast<uint32_t *>(keep(dalloc<uint32_t>(1)));
+        ck(cudaMemset(m->ebase, 0, 4), "memset");
         m->pos = static_cast<int *>(keep(dalloc<int>(1)));
         m->tok = static_cast<int64_t *>(keep(dalloc<int64_t>(B)));
         m->out = static_cast<int64_t *>(keep(dalloc<int64_t>(B * max_ctx)));
-        ck(cudaMemset(m->count, 0, sizeof(unsigned) * rg_max), "memset");
         ck(cudaMemset(m->done, 0, 4), "memset");
         ck(cudaMemset(m->err, 0, 4), "memset");
         ck(cudaMemset(m->bestv, 0, sizeof(float) * MAXTP * MAXB), "memset");
         ck(cudaMemset(m->besti, 0, sizeof(int) * MAXTP * MAXB), "memset");
         ck(cudaFuncSetAttribute(gqa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * AK * HD * 2), "smem");
-        const int gsm = 8 * 8 * (kMaxChunk + 8) * 2;      // the widest K range of 64 streams
+        const int gsm = (int)kGemvSmemCap;
         ck(cudaFuncSetAttribute(i8_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
         ck(cudaFuncSetAttribute(i8_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
         ck(cudaFuncSetAttribute(i8_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
@@ -928,8 +1075,33 @@ int xdna_gemma_steps(XdnaGemma *m, int n_steps, void *stream) {
         return -1;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the first step of a staged shape runs eagerly and is then recorded as a graph (positions,
+    // tokens and exchange epochs live on the device); later steps replay the graph
+    XdnaGemma::Graph *g = nullptr;
+    for (auto &x : m->graphs)
+        if (x.B == m->run_B && x.n_prompt == m->run_prompt && x.n_new == m->run_new) g = &x;
     for (int s = 0; s < n_steps; s++) {
-        const cudaError_t e = step(m, m->run_B, m->run_prompt, m->run_new, st);
+        cudaError_t e;
+        if (g) {
+            e = cudaGraphLaunch(g->exec, st);
+        } else {
+            e = step(m, m->run_B, m->run_prompt, m->run_new, st);
+            if (!e) {
+                m->graphs.push_back({m->run_B, m->run_prompt, m->run_new, nullptr});
+                g = &m->graphs.back();
+                if (!m->cap) e = cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking);
+                cudaGraph_t graph = nullptr;
+                if (!e) e = cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal);
+                if (!e) {
+                    const cudaError_t e2 = step(m, m->run_B, m->run_prompt, m->run_new, m->cap);
+                    e = cudaStreamEndCapture(m->cap, &graph);
+                    if (!e) e = e2;
+                }
+                if (!e) e = cudaGraphInstantiate(&g->exec, graph, 0);
+                if (graph) cudaGraphDestroy(graph);
+                if (e) { m->graphs.pop_back(); g = nullptr; }
+            }
+        }
         if (e) { set_last_error_message(std::string("xdna_gemma_steps: ") + cudaGetErrorString(e)); return -1; }
         m->run_done++;
     }
