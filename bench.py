@@ -1002,7 +1002,7 @@ def run_gemma(args):
     line = {
         "metric": GEMMA_METRIC, "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "int8 weights, bf16 activations",
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8 weights, f16 activations",
         "data": "synthetic (random-init N(0,0.02) weights, uniform prompt ids)",
         "config": {"workload": "Gemma-3-1B, 64 streams, 4096-token prompts (prefill untimed), 256 greedy tokens",
                    "model": "gemma-3-1b text decoder shapes (random init)", "global_batch": B,
@@ -1017,7 +1017,9 @@ def run_gemma(args):
         "e2e": {"value": B * 64 / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(pe.nbytes),
                 "d2h_bytes_per_step": int(oute.nbytes),
                 "step": "one xdna_gemma_generate call: 64 streams, 128-token prompts (prefill included) + 64 tokens"},
-        "gpu_launches": steps * (2 + 26 * 11 + 3),
+        # per step: embed, 26 x (qkv, q/k prep, attention, merge, o, norm, gate|up, down, norm),
+        # LM head + argmax, unpack, pick; with TP also 2 all-reduces per layer and the gather
+        "gpu_launches": steps * (1 + 26 * 9 + 3 + (26 * 2 + 1 if world > 1 else 0)),
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
