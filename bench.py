@@ -925,6 +925,17 @@ def run_gemma_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_gemma_case(args):
+    """One xdna_gemma generate of B streams x ctx-token prompts + 4 tokens (ncu captures of the
+    step at a chosen context; nothing timed)."""
+    import xdna_engine_b200 as X
+    from xdna_engine_b200.synth import GEMMA3_1B as cfg, make_gemma_weights
+    B, ctx = (int(v) for v in args.case.split(","))
+    dec = X.GemmaDecoder(X.Device(0), cfg, make_gemma_weights(cfg, seed=0), max_batch=B, max_ctx=ctx + 8)
+    prompts = np.random.default_rng(0).integers(2, cfg.vocab, (B, ctx)).astype(np.int64)
+    print(dec.generate(prompts, 4)[0], flush=True)
+
+
 def run_gemma(args):
     import torch
     world, rank, local = dist_env()
@@ -1034,7 +1045,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode", "bge", "whisper", "parakeet", "whisper_dec", "gemma"], default="decode")
+    ap.add_argument("--case", default="", help="gemma only: 'B,ctx' runs one small generate (B streams, ctx-token "
+                    "prompts, ctx - 1 prefill steps + 4 tokens) and prints its tokens: the profiling case")
     args = ap.parse_args()
+    if args.case:
+        run_gemma_case(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.workload == "gemma":
