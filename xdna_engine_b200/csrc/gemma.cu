@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstdint>
 #include <cstring>
 #include <stdexcept>
@@ -29,6 +30,7 @@
 
 #include "../../include/xdna_b200.h"
 #include "ptx.cuh"
+#include "tc.cuh"
 
 namespace xdna {
 void set_last_error_message(const std::string &m);
@@ -234,15 +236,22 @@ __global__ void __launch_bounds__(GWARPS * 32, 2) i8_gemv_kernel(GemvArgs a) {
                 v1 = red[off + 64];
             }
             const int orow = rg0 + rr, b = n * 8 + 2 * (ln & 3) + c, gg = ln >> 2, n0 = orow * 16;
-            if (orow >= n_rg || b >= a.B) continue;
+            const bool valid = orow < n_rg && b < a.B;
+            if (a.mode == OUT_ARGMAX) {
+                unsigned long long k = 0ull;
+                if (valid) {
+                    const float y0 = v0 * a.scale[n0 + gg] * a.oscale, y1 = v1 * a.scale[n0 + gg + 8] * a.oscale;
+                    if (n0 + gg < a.N) k = amax_key(y0, a.base + n0 + gg);
+                    if (n0 + gg + 8 < a.N) k = max(k, amax_key(y1, a.base + n0 + gg + 8));
+                }
+                atomicMax(&sbest[b], k);
+                continue;
+            }
+            if (!valid) continue;
             const float y0 = v0 * a.scale[n0 + gg] * a.oscale, y1 = v1 * a.scale[n0 + gg + 8] * a.oscale;
             if (a.mode == OUT_F32) {
                 if (n0 + gg < a.N) a.out[(size_t)b * a.ldo + n0 + gg] = y0;
                 if (n0 + gg + 8 < a.N) a.out[(size_t)b * a.ldo + n0 + gg + 8] = y1;
-            } else if (a.mode == OUT_ARGMAX) {
-                unsigned long long k = n0 + gg < a.N ? amax_key(y0, a.base + n0 + gg) : 0ull;
-                if (n0 + gg + 8 < a.N) k = max(k, amax_key(y1, a.base + n0 + gg + 8));
-                atomicMax(&sbest[b], k);
             } else {
                 a.out_h[(size_t)b * a.ldo + orow * 8 + gg] = f16bits(gelu_tanh(y0) * y1 * (1.0f / kHScale));
             }
@@ -597,6 +606,245 @@ __global__ void tp_gather_best_kernel(int B, uint64_t *const *bufs, int P, int r
     }
 }
 
+
+// ---- tcgen05 GEMV for 17..64 streams ---------------------------------------------------------
+// At 64 streams every weight byte carries 128 FLOP, which the mma.sync pipe cannot sustain at
+// HBM rate; this kernel runs the same Y = (X . Wq^T) * scale on tcgen05.  CTA = 128 weight rows
+// (one TMEM lane each) x one K range; warps 0-3 (thread r = row r) fetch the rows' int8 tiles
+// (64 K: bytes q + 128, laid out so each 16-byte chunk index is one coalesced warp load) up to 4
+// tiles ahead in registers, widen them to f16 exactly (byte-permute + sub.f16x2) and store them
+// into a 4-slot ring of A operands in TMEM (tcgen05.st, 32 columns per tile); warp 4 issues
+// tcgen05.mma (A from TMEM, B = the staged X range in shared memory, SW128 K-major; D = 128 x NB
+// f32 in TMEM) and frees ring slots with tcgen05.commit.  The X range [NB streams][K range] is
+// staged with cp.async once per CTA.  Partials leave TMEM by tcgen05.ld and are stored straight
+// into the shared memory of the cluster CTA that owns their rows; owners add the K ranges in
+// rank order; epilogues as i8_gemv_kernel.  Every mbarrier wait is bounded (1 s): on expiry the
+// kernel sets *err and runs to its end without waiting (results invalid, reported by the host).
+constexpr int TCK = 64;           // K per tile
+constexpr int TC_SLOTS = 4;       // TMEM ring of A tiles (32 columns each)
+constexpr int TC_PF = 4;          // tiles in flight per converter thread (registers)
+constexpr int TC_THREADS = 160;
+
+struct TcArgs {
+    const uint8_t *w;           // [row blocks][K tiles][4 chunks][128 rows][16 B]
+    const float *scale;         // [row blocks * 128]
+    const uint16_t *x;          // f16 [B][K]
+    int B, N, K, nkt;           // nkt = K tiles (K padded to 64 with zero weights)
+    int nsplit, red_off;        // K ranges (= cluster size); float offset of the partials (0: alias X)
+    int mode;
+    float oscale;
+    float *out;
+    uint16_t *out_h;
+    int ldo;
+    unsigned long long *best;
+    int base;
+    unsigned *err;
+};
+
+__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, bool &ok, unsigned *err) {
+    if (!ok) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > 1000000000ull) {
+            atomicCAS(err, 0u, 2u);
+            ok = false;
+            return false;
+        }
+    }
+    return true;
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// D[tmem] (+)= A[tmem] . B[smem]^T, kind::f16
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// kind::f16 with f16 A and B, f32 accumulate, both K-major
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+template <int NB>
+__global__ void __launch_bounds__(TC_THREADS) tc_gemv_kernel(TcArgs a) {
+    extern __shared__ __align__(1024) uint8_t tsm[];
+    uint8_t *xs = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tsm) + 1023) & ~uintptr_t(1023));
+    float *red = reinterpret_cast<float *>(xs) + a.red_off;
+    __shared__ __align__(8) uint64_t full[TC_SLOTS], empty[TC_SLOTS], done;
+    __shared__ uint32_t tbase_s;
+    __shared__ unsigned long long sbest[MAXB];
+    griddep_launch();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int split = blockIdx.y, nrb = (a.N + 127) / 128;
+    const int kt0 = split * a.nkt / a.nsplit, nkc = (split + 1) * a.nkt / a.nsplit - kt0;
+    bool ok = true;
+    if (tid == 0) {
+        for (int i = 0; i < TC_SLOTS; i++) { mbar_init(&full[i], 128); mbar_init(&empty[i], 1); }
+        mbar_init(&done, 1);
+        mbar_fence_init();
+    }
+    if (a.mode == OUT_ARGMAX && tid < MAXB) sbest[tid] = 0ull;
+    if (warp == 4) { tc::tmem_alloc(&tbase_s, 256); tc::tmem_relinquish(); }
+    // converters: first TC_PF tiles of the first row block (weights only: before the grid dependency)
+    uint4 pf[TC_PF][4];
+    auto fetch = [&](uint4 (&d)[4], int rb, int kt) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.w) + ((size_t)rb * a.nkt + kt) * 512 + tid;
+#pragma unroll
+        for (int c = 0; c < 4; c++) d[c] = __ldcs(src + c * 128);
+    };
+    if (warp < 4) {
+#pragma unroll
+        for (int j = 0; j < TC_PF; j++)
+            if (j < nkc && (int)blockIdx.x < nrb) fetch(pf[j], blockIdx.x, kt0 + j);
+    }
+    griddep_wait();
+    {   // X range -> [tile][NB rows][128 B], 16-byte chunk c of row b at chunk c ^ (b & 7)
+        const int pieces = nkc * NB * 8;
+        for (int i = tid; i < pieces; i += TC_THREADS) {
+            const int j = i / (NB * 8), rem = i - j * (NB * 8), b = rem >> 3, c = rem & 7;
+            uint8_t *dst = xs + j * (NB * 128) + b * 128 + ((c ^ (b & 7)) << 4);
+            const int k = (kt0 + j) * TCK + c * 8;
+            if (b < a.B && k < a.K) cp_async16(dst, a.x + (size_t)b * a.K + k);
+            else *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+        }
+        cp_async_commit();
+        cp_async_wait_all();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    tc::fence_before_sync();
+    cg::cluster_group cl = cg::this_cluster();
+    if (a.nsplit > 1) cl.sync(); else __syncthreads();   // (peers store into this CTA only once it runs)
+    tc::fence_after_sync();
+    const uint32_t tbase = tbase_s, tD = tbase, tA = tbase + 64;
+    constexpr uint32_t IDESC = idesc_f16_f32(128, NB);
+    const uint32_t xs_a = smem_u32(xs);
+    int it = 0;                               // ring position (continues over row blocks)
+    int rbi = 0;
+    for (int rb = blockIdx.x; rb < nrb; rb += gridDim.x, rbi++) {
+        if (warp < 4) {
+            for (int t0 = 0; t0 < nkc; t0 += TC_PF) {
+#pragma unroll
+                for (int j = 0; j < TC_PF; j++) {
+                    const int t = t0 + j;
+                    if (t >= nkc) break;
+                    const int slot = (it + t) % TC_SLOTS;
+                    const uint32_t ph = (uint32_t)(((it + t) / TC_SLOTS) & 1);
+                    uint32_t h[32];
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const uint32_t wv[4] = {pf[j][c].x, pf[j][c].y, pf[j][c].z, pf[j][c].w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            h[c * 8 + 2 * e] = u8x2_f16(wv[e], 0x5140u);
+                            h[c * 8 + 2 * e + 1] = u8x2_f16(wv[e], 0x7362u);
+                        }
+                    }
+                    if (t + TC_PF < nkc) fetch(pf[j], rb, kt0 + t + TC_PF);
+                    tc_wait(&empty[slot], ph ^ 1u, ok, a.err);
+                    tmem_st32(tA + ((uint32_t)(warp * 32) << 16) + slot * 32, h);
+                    tmem_st_wait();
+                    tc::fence_before_sync();
+                    mbar_arrive(&full[slot]);
+                }
+            }
+            // the next row block's first tiles, in flight during this block's epilogue
+            const int rn = rb + gridDim.x;
+#pragma unroll
+            for (int j = 0; j < TC_PF; j++)
+                if (j < nkc && rn < nrb) fetch(pf[j], rn, kt0 + j);
+        } else if (lane == 0) {
+            for (int t = 0; t < nkc; t++) {
+                const int slot = (it + t) % TC_SLOTS;
+                const uint32_t ph = (uint32_t)(((it + t) / TC_SLOTS) & 1);
+                tc_wait(&full[slot], ph, ok, a.err);
+                tc::fence_after_sync();
+                if (ok) {
+#pragma unroll
+                    for (int k4 = 0; k4 < 4; k4++)
+                        mma_f16_ta(tD, tA + slot * 32 + k4 * 8,
+                                   tc::desc_k_sw128(xs_a + t * (NB * 128) + k4 * 32), IDESC, (t | k4) != 0);
+                }
+                tc::commit(&empty[slot]);
+            }
+            tc::commit(&done);
+        }
+        it += nkc;
+        // partials: thread r takes row r of D from TMEM and stores it into the shared memory of the
+        // CTA that owns rows [q*rpo, (q+1)*rpo) of the block (rpo = 128 / nsplit), as
+        // red[src rank][stream][row - q*rpo]: remote stores, no round trips.  Each owner then adds
+        // the K ranges in rank order from its own shared memory.
+        const int rpo = 128 / a.nsplit;
+        if (warp < 4) {
+            tc_wait(&done, (uint32_t)(rbi & 1), ok, a.err);
+            tc::fence_after_sync();
+            const int q = tid / rpo, lr = tid - q * rpo;
+            float *dst = a.nsplit > 1 ? cl.map_shared_rank(red, q) : red;
+            dst += (size_t)split * NB * rpo + lr;
+#pragma unroll
+            for (int c0 = 0; c0 < NB; c0 += 32) {
+                uint32_t r[32];
+                tc::tmem_ld32(tD + ((uint32_t)(warp * 32) << 16) + c0, r);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < 32; c++) dst[(c0 + c) * rpo] = __uint_as_float(r[c]);
+            }
+            tc::fence_before_sync();
+        }
+        if (a.nsplit > 1) cl.sync(); else __syncthreads();
+        tc::fence_after_sync();
+        // this CTA's rows: item = (row pair p: local rows (p/8)*16 + p%8 and +8, stream b)
+        const int npair = rpo / 2, items = npair * NB;
+        for (int i = tid; i < items; i += TC_THREADS) {
+            const int b = i / npair, p = i - b * npair, lrow = (p >> 3) * 16 + (p & 7);
+            float v0 = 0.0f, v1 = 0.0f;
+            for (int q = 0; q < a.nsplit; q++) {
+                const float *rp = red + ((size_t)q * NB + b) * rpo + lrow;
+                v0 += rp[0];
+                v1 += rp[8];
+            }
+            const int n0 = rb * 128 + split * rpo + lrow;
+            if (a.mode == OUT_ARGMAX) {
+                unsigned long long k = 0ull;
+                if (b < a.B) {
+                    const float y0 = v0 * a.scale[n0] * a.oscale, y1 = v1 * a.scale[n0 + 8] * a.oscale;
+                    if (n0 < a.N) k = amax_key(y0, a.base + n0);
+                    if (n0 + 8 < a.N) k = max(k, amax_key(y1, a.base + n0 + 8));
+                }
+                atomicMax(&sbest[b], k);
+                continue;
+            }
+            if (b >= a.B) continue;
+            const float y0 = v0 * a.scale[n0] * a.oscale, y1 = v1 * a.scale[n0 + 8] * a.oscale;
+            if (a.mode == OUT_F32) {
+                if (n0 < a.N) a.out[(size_t)b * a.ldo + n0] = y0;
+                if (n0 + 8 < a.N) a.out[(size_t)b * a.ldo + n0 + 8] = y1;
+            } else {
+                a.out_h[(size_t)b * a.ldo + (n0 >> 4) * 8 + (n0 & 7)] = f16bits(gelu_tanh(y0) * y1 * (1.0f / kHScale));
+            }
+        }
+        tc::fence_before_sync();
+        if (a.nsplit > 1) cl.sync(); else __syncthreads();
+        tc::fence_after_sync();
+    }
+    if (a.mode == OUT_ARGMAX && tid < a.B && sbest[tid]) atomicMax(&a.best[tid], sbest[tid]);
+    __syncthreads();
+    if (warp == 4) tc::tmem_dealloc(tbase, 256);
+}
+
 }  // namespace gm
 
 namespace {
@@ -628,11 +876,14 @@ struct GmMat {
     float *scale = nullptr;
     int N = 0, K = 0;
     float oscale = 1.0f;                  // output multiplier undoing an input prescale
+    uint8_t *wt = nullptr;                // tcgen05 layout (engines created for more than 16 streams)
+    int nkt = 0;
 };
 
 struct XdnaGemma {
     XdnaGemmaConfig cfg{};
     int max_batch = 0, max_ctx = 0, rank = 0, tp = 1, hq = 0, f_loc = 0, v_loc = 0, v_base = 0, k_loc = 0, k_base = 0;
+    bool use_tc = false;
     struct Layer {
         GmMat qkv, o, gu, down;
         float *norms;                      // in, q, k, post_attn, pre_ffn, post_ffn (q, k: 256)
@@ -680,9 +931,9 @@ constexpr int kD = 1152, kNPL = kD / 32;
 // rows = outputs; W given [K, N] with the output columns listed in `cols` (in this order);
 // pack in mma fragment order with a per-row scale (Lin::load rule, opt125m_decode.rs:41-60)
 GmMat pack_i8(XdnaGemma *m, const float *w, int K, int N, const std::vector<int> &cols) {
-    const int R = (int)cols.size(), nrg = (R + 15) / 16, nks = K / 16;
-    std::vector<int8_t> q((size_t)nrg * 16 * K, 0);
-    std::vector<float> sc((size_t)nrg * 16, 1.0f);
+    const int R = (int)cols.size(), nrg = (R + 15) / 16, nks = K / 16, nrb = (R + 127) / 128;
+    std::vector<int8_t> q((size_t)nrb * 128 * K, 0);
+    std::vector<float> sc((size_t)nrb * 128, 1.0f);
     for (int r = 0; r < R; r++) {
         const int n = cols[r];
         if (n < 0) continue;                       // padding row
@@ -715,6 +966,25 @@ GmMat pack_i8(XdnaGemma *m, const float *w, int K, int N, const std::vector<int>
     o.scale = dupload(sc);
     m->owned.push_back(o.w);
     m->owned.push_back(o.scale);
+    if (m->use_tc) {
+        // tcgen05 layout: [row block of 128][K tile of 64][chunk c of 16 K][row][16 B], K padded
+        // with zero weights (bytes 128)
+        const int nkt = (K + gm::TCK - 1) / gm::TCK;
+        std::vector<uint8_t> t((size_t)nrb * nkt * 8192, 128);
+        for (int rb = 0; rb < nrb; rb++)
+            for (int kt = 0; kt < nkt; kt++)
+                for (int c = 0; c < 4; c++)
+                    for (int r = 0; r < 128; r++)
+                        for (int e = 0; e < 16; e++) {
+                            const int k = kt * 64 + c * 16 + e, row = rb * 128 + r;
+                            if (k < K)
+                                t[((((size_t)rb * nkt + kt) * 4 + c) * 128 + r) * 16 + e] =
+                                    (uint8_t)(q[(size_t)row * K + k] + 128);
+                        }
+        o.wt = dupload(t);
+        o.nkt = nkt;
+        m->owned.push_back(o.wt);
+    }
     return o;
 }
 
@@ -749,8 +1019,68 @@ GemvPlan plan_of(int N, int K, int nt) {
     return best;
 }
 
+// tcgen05 GEMV launch shape: the fewest K ranges (cluster size 1..8) giving about one CTA per
+// SM with two CTAs per SM, else the most CTAs whose staged X range fits one per SM; at least
+// 80 KB of shared memory per CTA so that at most two CTAs share an SM (two x 256 TMEM columns).
+struct TcPlan {
+    int nsplit, gx, red_off;
+    size_t smem;
+};
+constexpr size_t kTcSmemMax = 220 * 1024;
+TcPlan tc_plan_of(int N, int nkt, int nb) {
+    const int nrb = (N + 127) / 128;
+    TcPlan best{0, 0, 0, 0};
+    long best_ctas = -1;
+    for (int ns : {1, 2, 4, 8}) {
+        if (ns > nkt) break;
+        const int nkc = (nkt + ns - 1) / ns;
+        const size_t xsb = (size_t)nkc * nb * 128, redb = (size_t)nb * 128 * 4;
+        const size_t xsa = (xsb + 1023) / 1024 * 1024;
+        for (int per : {2, 1}) {                 // CTAs per SM
+            const int gx = std::min(nrb, std::max(1, 148 * per / ns));
+            // the partials may alias the staged X only when no other CTA writes them and the
+            // CTA does not loop (peers store into a CTA's partials while its MMAs may still read X)
+            const bool alias = ns == 1 && gx == nrb;
+            const size_t smem = std::max<size_t>(80 * 1024, 1024 + (alias ? std::max(xsb, redb) : xsa + redb));
+            if (smem > (per == 2 ? kGemvSmemCap : kTcSmemMax)) continue;
+            const TcPlan p{ns, gx, alias ? 0 : (int)(xsa / 4), smem};
+            const long ctas = (long)nrb * ns;
+            if (per == 2 && ctas >= 140) return p;
+            if (ctas > best_ctas) { best = p; best_ctas = ctas; }
+            break;
+        }
+    }
+    if (best.nsplit == 0) throw std::runtime_error("tcgen05 GEMV shape does not fit shared memory");
+    return best;
+}
+
+cudaError_t gemv_tc(XdnaGemma *m, const GmMat &w, const uint16_t *x, int B, int mode, float *out, uint16_t *ob,
+                    int ldo, cudaStream_t st) {
+    const int nb = B <= 32 ? 32 : 64;
+    TcPlan p;
+    try { p = tc_plan_of(w.N, w.nkt, nb); } catch (...) { return cudaErrorInvalidValue; }
+    gm::TcArgs a{w.wt, w.scale, x, B, w.N, w.K, w.nkt, p.nsplit, p.red_off, mode, w.oscale, out, ob, ldo,
+                 m->lmbest, m->v_base, m->err};
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(p.gx, p.nsplit);
+    lc.blockDim = dim3(gm::TC_THREADS);
+    lc.dynamicSmemBytes = p.smem;
+    lc.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = p.nsplit;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 2;
+    return nb == 32 ? cudaLaunchKernelEx(&lc, gm::tc_gemv_kernel<32>, a) : cudaLaunchKernelEx(&lc, gm::tc_gemv_kernel<64>, a);
+}
+
 cudaError_t gemv(XdnaGemma *m, const GmMat &w, const uint16_t *x, int B, int mode, float *out, uint16_t *ob, int ldo,
                  cudaStream_t st) {
+    if (B > 16 && w.wt) return gemv_tc(m, w, x, B, mode, out, ob, ldo, st);
     const int nt = B <= 8 ? 1 : B <= 16 ? 2 : B <= 32 ? 4 : 8;
     GemvPlan p;
     try { p = plan_of(w.N, w.K, nt); } catch (...) { return cudaErrorInvalidValue; }
@@ -854,6 +1184,9 @@ XdnaGemma *xdna_gemma_create(XdnaDevice *dev_unused, const XdnaGemmaConfig *cfg,
     try {
         m->cfg = c;
         m->max_batch = max_batch;
+        // GEMVs of more than 16 streams on tcgen05 (XDNA_GEMMA_TC=0 keeps them on mma.sync)
+        const char *tcv = std::getenv("XDNA_GEMMA_TC");
+        m->use_tc = max_batch > 16 && !(tcv && tcv[0] == '0');
         m->max_ctx = max_ctx;
         m->rank = tp_rank;
         m->tp = tp_size;
@@ -953,6 +1286,12 @@ XdnaGemma *xdna_gemma_create(XdnaDevice *dev_unused, const XdnaGemmaConfig *cfg,
                                         plan_of(L.gu.N, L.gu.K, nt); plan_of(L.down.N, L.down.K, nt); }
             plan_of(m->lm.N, m->lm.K, nt);
         }
+        if (m->use_tc)
+            for (int nb : {32, 64}) {
+                for (auto &L : m->layers) { tc_plan_of(L.qkv.N, L.qkv.nkt, nb); tc_plan_of(L.o.N, L.o.nkt, nb);
+                                            tc_plan_of(L.gu.N, L.gu.nkt, nb); tc_plan_of(L.down.N, L.down.nkt, nb); }
+                tc_plan_of(m->lm.N, m->lm.nkt, nb);
+            }
         const int nsplit_max = (std::max(max_ctx, c.window) + AK - 1) / AK;
         m->apart = static_cast<float *>(keep(dalloc<float>(B * nsplit_max * 4 * (HD + 2))));
         m->bestv = static_cast<float *>(keep(dalloc<float>(MAXTP * MAXB)));
@@ -977,6 +1316,8 @@ XdnaGemma *xdna_gemma_create(XdnaDevice *dev_unused, const XdnaGemmaConfig *cfg,
         ck(cudaFuncSetAttribute(i8_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
         ck(cudaFuncSetAttribute(i8_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
         ck(cudaFuncSetAttribute(i8_gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
+        ck(cudaFuncSetAttribute(tc_gemv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemMax), "smem");
+        ck(cudaFuncSetAttribute(tc_gemv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemMax), "smem");
         if (tp_size > 1) {
             // exchange buffer [2 parities][MAXB * D] of 64-bit words; zero = epoch 0 (never used)
             const size_t words = (size_t)2 * MAXB * kD;
