@@ -276,7 +276,7 @@ BGE_METRIC = "BGE-base embeddings throughput (batch 256, lengths U[32,512], CLS 
 
 
 def bge_batch_flops(lens):
-    """Valid-token FLOPs of one batch (SURVEY 8d): 12 layers x (14,155,776 L + 3,072 L^2) per
+    """Valid-token FLOPs of one batch: 12 layers x (14,155,776 L + 3,072 L^2) per
     sequence -- the four projections/FFN GEMMs plus QK^T and PV."""
     L = np.asarray(lens, np.float64)
     return 12.0 * (14155776.0 * L.sum() + 3072.0 * (L * L).sum())

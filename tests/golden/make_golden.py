@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
 """Regenerate the committed golden fixtures under tests/golden/.
 
-Run in a container where the xdna-engine source tree is mounted (default
-/root/reference, override with XDNA_REF) and `transformers` is importable:
+Run where the xdna-engine source tree is checked out (its path in XDNA_REF) and
+`transformers` is importable:
 
-    python tests/golden/make_golden.py
+    XDNA_REF=<path of the xdna-engine checkout> python tests/golden/make_golden.py
 
 It writes
   bfp16_golden.npz  -- outputs of the reference's own numpy golden
@@ -27,7 +27,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
-REF = os.environ.get("XDNA_REF", "/root/reference")
+REF = os.environ.get("XDNA_REF", "")      # the xdna-engine checkout (needed only to regenerate)
 
 
 def bfp16_fixture():
@@ -390,6 +390,8 @@ def parakeet_fixture():
 
 
 if __name__ == "__main__":
+    if not REF or not os.path.isdir(REF):
+        sys.exit("make_golden.py: set XDNA_REF to the xdna-engine source checkout")
     import sys
     only = set(sys.argv[1:])
     if not only or "gemma" in only:
