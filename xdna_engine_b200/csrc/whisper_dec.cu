@@ -14,6 +14,7 @@
 // x / 2^(e-6)), stored as int8 mantissas + one byte per block (1.125 bytes per weight) in the
 // order the tensor-core GEMV consumes them, and dequantised in registers (exactly: every bfp16
 // value is a bf16 value).
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -35,11 +36,11 @@ cudaError_t gemm_bf16(const uint16_t *A, int lda, const uint16_t *B, int ldb, in
 unsigned gemm_error_and_clear();
 
 namespace wdec {
+namespace cg = cooperative_groups;
 
 constexpr int D = 768, H = 12, HD = 64, F = 3072;
 constexpr int MAXB = 32;              // streams per decoder
-constexpr int KC = 128;               // K per split of the GEMV (8 mma k-steps)
-constexpr int GEMV_WARPS = 4;
+constexpr int GEMV_WARPS = 8;
 
 enum { OUT_F32 = 0, OUT_RESID = 1, OUT_GELU_BF16 = 2 };
 
@@ -74,123 +75,161 @@ struct GemvArgs {
     const uint8_t *ecode;       // [row groups][K/16][8 quads][4]
     const float *bias;          // [N] or null
     const uint16_t *x;          // bf16 [B][K]
-    int B, N, K, nsplit, kchunk;
-    float *part;                // [nsplit][Np][MAXB] split-K partials
-    unsigned *count;            // [row groups] arrival counters (left at zero)
+    int B, N, K;
+    int R, Wk, nsplit;          // row groups per CTA, warps per row group (along K), K ranges = cluster size
+    int red_off;                // float offset of the partial-sum area in shared memory (0: aliases X)
     int mode;
     float *out;                 // OUT_F32: [B][ldo]; OUT_RESID: x f32 [B][ldo] (+=)
     uint16_t *out_bf16;         // OUT_GELU_BF16: [B][ldo]
     int ldo;
 };
 
-// Y[b][n] = X[b] . W[n] for b < B: warp w of the CTA owns 16 output rows (row group) and one K
-// range of kchunk (a multiple of 128); the weight fragments come straight from HBM in mma order
-// (8 bytes of mantissas + a quad-shared 4-byte exponent word per lane and k-step), 8 k-steps
-// at a time with the next 8 already in flight; X comes from a padded shared copy of the range.
-// With several ranges, partials go to `part` and the last warp to finish a row group sums
-// them in range order and applies the epilogue (deterministic; the counter is reset to 0).
-template <int NT>
-__global__ void __launch_bounds__(GEMV_WARPS * 32) bfp_gemv_kernel(GemvArgs a) {
-    extern __shared__ __align__(16) uint16_t xs[];           // [NT*8][kchunk + 8]
-    __shared__ int last_flag[GEMV_WARPS];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int split = blockIdx.y;
-    const int rg = blockIdx.x * GEMV_WARPS + warp;
-    const int n_rg = (a.N + 15) / 16;
-    const int k0 = split * a.kchunk, xld = a.kchunk + 8;
-    for (int i = threadIdx.x; i < NT * 8 * (a.kchunk / 8); i += blockDim.x) {
-        const int b = i / (a.kchunk / 8), c = i % (a.kchunk / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (b < a.B) v = *reinterpret_cast<const uint4 *>(a.x + (size_t)b * a.K + k0 + c * 8);
-        *reinterpret_cast<uint4 *>(&xs[b * xld + c * 8]) = v;
-    }
-    __syncthreads();
-    if (rg >= n_rg) return;
-    float acc[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-    const int ks0 = k0 / 16, nks = a.K / 16, ngrp = a.kchunk / 128;
-    const uint2 *mp = reinterpret_cast<const uint2 *>(a.mant) + ((size_t)rg * nks + ks0) * 32 + lane;
-    const uint32_t *ep = reinterpret_cast<const uint32_t *>(a.ecode) + ((size_t)rg * nks + ks0) * 8 + g;
-    uint2 mv[8], mn[8];
-    uint32_t ev[8], en[8];
-#pragma unroll
-    for (int s = 0; s < 8; s++) { mv[s] = __ldcs(mp + s * 32); ev[s] = __ldcs(ep + s * 8); }
-    for (int gi = 0; gi < ngrp; gi++) {
-        if (gi + 1 < ngrp) {
-#pragma unroll
-            for (int s = 0; s < 8; s++) { mn[s] = __ldcs(mp + ((gi + 1) * 8 + s) * 32); en[s] = __ldcs(ep + ((gi + 1) * 8 + s) * 8); }
-        }
-#pragma unroll
-        for (int s = 0; s < 8; s++) {
-            // a0 (row g, k 2t..) a1 (row g+8, k 2t..) block 0; a2, a3 (k 2t+8..) block 1
-            const uint32_t e = ev[s];
-            const uint32_t a0 = deq2(mv[s].x & 0xffffu, e & 255u), a1 = deq2(mv[s].x >> 16, (e >> 8) & 255u);
-            const uint32_t a2 = deq2(mv[s].y & 0xffffu, (e >> 16) & 255u), a3 = deq2(mv[s].y >> 16, e >> 24);
-            const int kk = (gi * 8 + s) * 16;
-#pragma unroll
-            for (int n = 0; n < NT; n++) {
-                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(&xs[(n * 8 + g) * xld + kk + 2 * t]);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(&xs[(n * 8 + g) * xld + kk + 8 + 2 * t]);
-                mma16816(acc[n], a0, a1, a2, a3, b0, b1);
-            }
-        }
-#pragma unroll
-        for (int s = 0; s < 8; s++) { mv[s] = mn[s]; ev[s] = en[s]; }
-    }
-    // acc[n][e]: row (n0 + g + 8 (e >> 1)), stream (n*8 + 2t + (e & 1))
-    const int n0 = rg * 16;
-    const int Np = n_rg * 16;
-    if (a.nsplit > 1) {
-        float *pp = a.part + (size_t)split * Np * MAXB;
-#pragma unroll
-        for (int n = 0; n < NT; n++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) pp[(size_t)(n0 + g + 8 * (e >> 1)) * MAXB + n * 8 + 2 * t + (e & 1)] = acc[n][e];
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) last_flag[warp] = atomicAdd(&a.count[rg], 1u) == (unsigned)a.nsplit - 1;
-        __syncwarp();
-        if (!last_flag[warp]) return;
-        __threadfence();
-#pragma unroll
-        for (int n = 0; n < NT; n++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                // every split's value requested before the ordered sum
-                const size_t off = (size_t)(n0 + g + 8 * (e >> 1)) * MAXB + n * 8 + 2 * t + (e & 1);
-                float pv[8];
-                float sum = 0.0f;
-                for (int s0 = 0; s0 < a.nsplit; s0 += 8) {
-#pragma unroll
-                    for (int u = 0; u < 8; u++) pv[u] = s0 + u < a.nsplit ? __ldcg(a.part + (size_t)(s0 + u) * Np * MAXB + off) : 0.0f;
-#pragma unroll
-                    for (int u = 0; u < 8; u++)
-                        if (s0 + u < a.nsplit) sum += pv[u];
-                }
-                acc[n][e] = sum;
-            }
-        if (lane == 0) a.count[rg] = 0;
-    }
-    float bv[2] = {0.0f, 0.0f};
-    if (a.bias) {
-        if (n0 + g < a.N) bv[0] = a.bias[n0 + g];
-        if (n0 + g + 8 < a.N) bv[1] = a.bias[n0 + g + 8];
-    }
-#pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int row = n0 + g + 8 * (e >> 1), b = n * 8 + 2 * t + (e & 1);
-            if (row >= a.N || b >= a.B) continue;
-            const float y = acc[n][e] + bv[e >> 1];
-            if (a.mode == OUT_F32) a.out[(size_t)b * a.ldo + row] = y;
-            else if (a.mode == OUT_RESID) a.out[(size_t)b * a.ldo + row] += y;
-            else a.out_bf16[(size_t)b * a.ldo + row] = (uint16_t)bf16bits(gelu_erf_as(y));
-        }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
 }
 
-// x[b] = embed_tokens[tok[b]] + embed_positions[pos]  (f32)
+// Y[b][n] = X[b] . W[n] + bias for b < B on the bf16 tensor cores (bfp16 values are exact in
+// bf16).  Grid (row-group blocks, K ranges); the K ranges of one row-group block form a
+// thread-block cluster.  CTA = GEMV_WARPS warps = R row groups x Wk warps along the CTA's K
+// range; warp = 16 output rows whose weight fragments come straight from HBM in mma order
+// (8 bytes of mantissas + a quad-shared 4-byte exponent word per lane and k-step), 8 k-steps at
+// a time with the next 8 in flight.  The first 8 are requested before the wait for the previous
+// grid (programmatic dependent launch); the X range is staged with cp.async in one round trip
+// and read with ldmatrix.  Partial sums meet in shared memory, are added over the Wk warps and
+// then over the cluster's CTAs through DSMEM in rank order (deterministic).
+template <int NT>
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 2) bfp_gemv_kernel(GemvArgs a) {
+    extern __shared__ __align__(16) uint16_t xs[];
+    float *red = reinterpret_cast<float *>(xs) + a.red_off;
+    const uint32_t xs_a = smem_u32(xs);
+    griddep_launch();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int n_rg = (a.N + 15) / 16, nks = a.K / 16, split = blockIdx.y;
+    const int ks0 = split * nks / a.nsplit, nkc = (split + 1) * nks / a.nsplit - ks0, xld = nkc * 16 + 8;
+    const int r = warp / a.Wk, wk = warp % a.Wk;
+    const int w0 = wk * nkc / a.Wk, nst = (wk + 1) * nkc / a.Wk - w0, ngrp = (nst + 7) / 8;
+    const int rstride = gridDim.x * a.R;
+    uint2 mv[8], mn[8];
+    uint32_t ev[8], en[8];
+    auto fetch = [&](uint2 (&dm)[8], uint32_t (&de)[8], int rg, int s0) {
+        const bool live = rg < n_rg;
+        const size_t base = (size_t)(live ? rg : 0) * nks + ks0 + w0 + s0;
+        const uint2 *mp = reinterpret_cast<const uint2 *>(a.mant) + base * 32 + lane;
+        const uint32_t *ep = reinterpret_cast<const uint32_t *>(a.ecode) + base * 8 + g;
+#pragma unroll
+        for (int s = 0; s < 8; s++) {
+            const bool ok = live && s0 + s < nst;
+            dm[s] = ok ? __ldcs(mp + s * 32) : make_uint2(0, 0);
+            de[s] = ok ? __ldcs(ep + s * 8) : 0u;
+        }
+    };
+    fetch(mv, ev, blockIdx.x * a.R + r, 0);
+    griddep_wait();
+    {
+        const int cpr = nkc * 2;                        // 16-byte pieces per row
+        for (int b = warp; b < NT * 8; b += GEMV_WARPS)
+            for (int c = lane; c < cpr; c += 32) {
+                uint16_t *d = &xs[b * xld + c * 8];
+                if (b < a.B) cp_async16(d, a.x + (size_t)b * a.K + ks0 * 16 + c * 8);
+                else *reinterpret_cast<uint4 *>(d) = make_uint4(0, 0, 0, 0);
+            }
+        cp_async_commit();
+        cp_async_wait_all();
+    }
+    __syncthreads();
+    cg::cluster_group cl = cg::this_cluster();
+    for (int rg0 = blockIdx.x * a.R; rg0 < n_rg; rg0 += rstride) {
+        const int rg = rg0 + r;
+        if (rg0 != (int)blockIdx.x * a.R) fetch(mv, ev, rg, 0);
+        float acc[NT][4];
+#pragma unroll
+        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+        for (int gi = 0; gi < ngrp; gi++) {
+            if (gi + 1 < ngrp) fetch(mn, en, rg, (gi + 1) * 8);
+#pragma unroll
+            for (int s = 0; s < 8; s++) {
+                if (gi * 8 + s >= nst) break;
+                // a0 (row g, k 2t..) a1 (row g+8, k 2t..) block 0; a2, a3 (k 2t+8..) block 1
+                const uint32_t e = ev[s];
+                const uint32_t a0 = deq2(mv[s].x & 0xffffu, e & 255u), a1 = deq2(mv[s].x >> 16, (e >> 8) & 255u);
+                const uint32_t a2 = deq2(mv[s].y & 0xffffu, (e >> 16) & 255u), a3 = deq2(mv[s].y >> 16, e >> 24);
+                const int kk = (w0 + gi * 8 + s) * 16;
+                if constexpr (NT == 1) {
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t *>(&xs[g * xld + kk + 2 * t]);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t *>(&xs[g * xld + kk + 8 + 2 * t]);
+                    mma16816(acc[0], a0, a1, a2, a3, b0, b1);
+                } else {
+#pragma unroll
+                    for (int n = 0; n < NT; n += 2) {
+                        uint32_t r0, r1, r2, r3;
+                        ldsm_x4(xs_a + 2u * ((n * 8 + ((lane >> 4) << 3) + (lane & 7)) * xld + kk + (((lane >> 3) & 1) << 3)),
+                                r0, r1, r2, r3);
+                        mma16816(acc[n], a0, a1, a2, a3, r0, r1);
+                        mma16816(acc[n + 1], a0, a1, a2, a3, r2, r3);
+                    }
+                }
+            }
+#pragma unroll
+            for (int s = 0; s < 8; s++) { mv[s] = mn[s]; ev[s] = en[s]; }
+        }
+        if (a.red_off == 0) __syncthreads();            // the partials overwrite the staged X
+        float *rw = red + warp * NT * 128;
+#pragma unroll
+        for (int n = 0; n < NT; n++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) rw[(n * 4 + e) * 32 + lane] = acc[n][e];
+        __syncthreads();
+        if (a.Wk > 1)
+            for (int i = threadIdx.x; i < a.R * NT * 128; i += blockDim.x) {
+                const int rr = i / (NT * 128), e = i - rr * (NT * 128);
+                float sum = red[rr * a.Wk * NT * 128 + e];
+                for (int k = 1; k < a.Wk; k++) sum += red[(rr * a.Wk + k) * NT * 128 + e];
+                red[rr * a.Wk * NT * 128 + e] = sum;
+            }
+        if (a.nsplit > 1) cl.sync(); else __syncthreads();
+        // outputs: item = (row group, n tile, column c, lane) -> rows g and g + 8, stream n*8 + 2t + c;
+        // this CTA takes its share of the items and adds the K ranges in rank order
+        const int items = a.R * NT * 64, i0 = split * items / a.nsplit, i1 = (split + 1) * items / a.nsplit;
+        for (int it = i0 + threadIdx.x; it < i1; it += blockDim.x) {
+            const int rr = it / (NT * 64), rem = it - rr * (NT * 64), n = rem >> 6, c = (rem >> 5) & 1, ln = rem & 31;
+            const int off = rr * a.Wk * NT * 128 + (n * 4 + c) * 32 + ln;
+            float v0 = 0.0f, v1 = 0.0f;
+            if (a.nsplit > 1) {
+                float p0[8], p1[8];
+#pragma unroll
+                for (int q = 0; q < 8; q++)
+                    if (q < a.nsplit) {
+                        const float *rp = cl.map_shared_rank(red, q);
+                        p0[q] = rp[off];
+                        p1[q] = rp[off + 64];
+                    }
+#pragma unroll
+                for (int q = 0; q < 8; q++)
+                    if (q < a.nsplit) { v0 += p0[q]; v1 += p1[q]; }
+            } else {
+                v0 = red[off];
+                v1 = red[off + 64];
+            }
+            const int orow = rg0 + rr, b = n * 8 + 2 * (ln & 3) + c, n0 = orow * 16 + (ln >> 2);
+            if (orow >= n_rg || b >= a.B) continue;
+            const float vv[2] = {v0, v1};
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int row = n0 + 8 * h;
+                if (row >= a.N) continue;
+                const float y = vv[h] + (a.bias ? a.bias[row] : 0.0f);
+                if (a.mode == OUT_F32) a.out[(size_t)b * a.ldo + row] = y;
+                else if (a.mode == OUT_RESID) a.out[(size_t)b * a.ldo + row] += y;
+                else a.out_bf16[(size_t)b * a.ldo + row] = (uint16_t)bf16bits(gelu_erf_as(y));
+            }
+        }
+        if (a.nsplit > 1) cl.sync(); else __syncthreads();   // partials stay until every CTA has read them
+    }
+}
+
 __global__ void embed_kernel(const int64_t *tok, const int *pos, const float *et, const float *ep, float *x) {
     const int b = blockIdx.x, p = *pos;
     const int64_t id = tok[b];
@@ -200,6 +239,7 @@ __global__ void embed_kernel(const int64_t *tok, const int *pos, const float *et
 // y = bf16(LN(x)) per stream row (ln_row: population variance, eps 1e-5); one warp per row
 __global__ void ln_kernel(const float *__restrict__ x, int B, const float *__restrict__ gm,
                           const float *__restrict__ bt, uint16_t *__restrict__ y) {
+    griddep_launch();                                 // the next GEMV may start its weight fetch
     const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (b >= B) return;
     float v[24], gv[24], bv[24];
@@ -235,6 +275,7 @@ constexpr int SA_MAX = 448;
 constexpr int SA_SMEM = 2 * SA_MAX * HD * 2;
 __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const int *posp, int max_tgt,
                                                         uint16_t *kc, uint16_t *vc, uint16_t *ctx) {
+    griddep_launch();                                 // the next GEMV may start its weight fetch
     extern __shared__ __align__(16) uint16_t kvs[];        // K rows then V rows
     __shared__ float q[HD], sc[SA_MAX], red[8], part[2][HD];
     const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, pos = *posp;
@@ -348,6 +389,7 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const u
     if (tid == 0) { pp[0] = mx; pp[1] = red[0] + red[1] + red[2] + red[3]; }
 }
 __global__ void cross_merge_kernel(const float *__restrict__ part, int nsplit, uint16_t *__restrict__ ctx) {
+    griddep_launch();                                 // the next GEMV may start its weight fetch
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const float *pp = part + ((size_t)b * H + h) * nsplit * (HD + 2);
     constexpr int MAXS = 16;                           // encoder positions <= 16 x 128
@@ -482,11 +524,11 @@ struct XdnaWhisperDec {
     uint16_t *ckv_w = nullptr;              // [L * 2 * D][D] bf16 cross k|v weights (rows = outputs)
     float *ckv_b = nullptr;                 // [L * 2 * D]
     // state
-    float *x = nullptr, *qkv = nullptr, *q = nullptr, *logits = nullptr, *part = nullptr, *xpart = nullptr;
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *logits = nullptr, *xpart = nullptr;
     uint16_t *xn = nullptr, *ctx = nullptr, *h = nullptr, *kcache = nullptr, *vcache = nullptr, *ckv = nullptr,
              *enc_bf = nullptr;
     float *enc_f = nullptr;
-    unsigned *count = nullptr, *done = nullptr;
+    unsigned *done = nullptr;
     int *pos = nullptr;
     int64_t *tok = nullptr, *prompt = nullptr, *out_tok = nullptr, *tok_out = nullptr;
     float *lrec = nullptr;                  // logits record of xdna_whisper_dec_generate
@@ -573,21 +615,62 @@ BfpMat pack_bfp(XdnaWhisperDec *m, const float *w, const float *bias, int K, int
     return o;
 }
 
+// GEMV launch shape: the largest row-group block per CTA (more reuse of the staged X) and the
+// fewest K ranges that still give about 1.3 CTAs per SM, within the shared memory that lets two
+// CTAs share an SM.  One pass when the grid covers every row group, else CTAs loop over row-group
+// blocks with the staged X kept (then the partial sums get their own area).
+struct GemvPlan {
+    int R, nsplit, gx, red_off;
+    size_t smem;
+};
+constexpr size_t kGemvSmemCap = 113 * 1024;
+GemvPlan plan_of(int N, int K, int nt) {
+    const int nrg = (N + 15) / 16, ks = K / 16;
+    GemvPlan best{1, 1, 1, 0, 0};
+    long best_ctas = -1;
+    for (int R : {8, 4, 2, 1})
+        for (int ns : {1, 2, 4, 8}) {
+            if (ns > ks) continue;
+            const int kc = (ks + ns - 1) / ns * 16, blocks = (nrg + R - 1) / R;
+            const size_t xsb = (size_t)nt * 8 * (kc + 8) * 2, redb = (size_t)wdec::GEMV_WARPS * nt * 128 * 4;
+            const int gx = std::min(blocks, std::max(1, 296 / ns));
+            const bool loop = gx < blocks;
+            const size_t smem = loop ? xsb + redb : std::max(xsb, redb);
+            if (smem > kGemvSmemCap) continue;
+            const long ctas = (long)blocks * ns;
+            const GemvPlan p{R, ns, gx, loop ? (int)(xsb / 4) : 0, smem};
+            if (ctas >= 190) return p;
+            if (ctas > best_ctas) { best = p; best_ctas = ctas; }
+        }
+    if (best_ctas < 0) throw std::runtime_error("GEMV shape does not fit shared memory");
+    return best;
+}
+
 cudaError_t gemv(XdnaWhisperDec *m, const BfpMat &w, const uint16_t *x, int B, int mode, float *out, uint16_t *ob,
                  int ldo, cudaStream_t st) {
-    // K ranges: as few as give about two warps per SM (fewer ranges = shorter reduction)
-    const int nrg = (w.N + 15) / 16, kb = w.K / wdec::KC;
-    int nsplit = std::min(kb, std::max(1, (2 * 148 + nrg - 1) / nrg));
-    while (kb % nsplit) nsplit--;
-    const int kchunk = w.K / nsplit;
-    wdec::GemvArgs a{w.mant, w.ecode, w.bias, x, B, w.N, w.K, nsplit, kchunk, m->part, m->count, mode, out, ob, ldo};
-    dim3 grid((nrg + wdec::GEMV_WARPS - 1) / wdec::GEMV_WARPS, nsplit);
+    (void)m;
     const int nt = B <= 8 ? 1 : (B <= 16 ? 2 : 4);
-    const size_t smem = (size_t)nt * 8 * (kchunk + 8) * 2;
-    if (nt == 1) wdec::bfp_gemv_kernel<1><<<grid, wdec::GEMV_WARPS * 32, smem, st>>>(a);
-    else if (nt == 2) wdec::bfp_gemv_kernel<2><<<grid, wdec::GEMV_WARPS * 32, smem, st>>>(a);
-    else wdec::bfp_gemv_kernel<4><<<grid, wdec::GEMV_WARPS * 32, smem, st>>>(a);
-    return cudaGetLastError();
+    GemvPlan p;
+    try { p = plan_of(w.N, w.K, nt); } catch (...) { return cudaErrorInvalidValue; }
+    wdec::GemvArgs a{w.mant, w.ecode, w.bias, x, B, w.N, w.K, p.R, wdec::GEMV_WARPS / p.R, p.nsplit, p.red_off,
+                     mode, out, ob, ldo};
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(p.gx, p.nsplit);
+    lc.blockDim = dim3(wdec::GEMV_WARPS * 32);
+    lc.dynamicSmemBytes = p.smem;
+    lc.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = p.nsplit;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 2;
+    if (nt == 1) return cudaLaunchKernelEx(&lc, wdec::bfp_gemv_kernel<1>, a);
+    if (nt == 2) return cudaLaunchKernelEx(&lc, wdec::bfp_gemv_kernel<2>, a);
+    return cudaLaunchKernelEx(&lc, wdec::bfp_gemv_kernel<4>, a);
 }
 
 // one token for B streams (reads *pos and tok on the device, advances both)
@@ -709,9 +792,10 @@ XdnaWhisperDec *xdna_whisper_dec_create(XdnaDevice *dev_unused, const XdnaWhispe
         m->qkv = static_cast<float *>(keep(dalloc<float>(B * 3 * D)));
         m->q = static_cast<float *>(keep(dalloc<float>(B * D)));
         m->logits = static_cast<float *>(keep(dalloc<float>(B * ldl)));
-        // split-K partials: largest (splits x padded rows) over the GEMVs, MAXB streams each
-        const size_t part = std::max({(size_t)(F / KC) * D, (size_t)(D / KC) * 3 * D, (size_t)(D / KC) * ldl});
-        m->part = static_cast<float *>(keep(dalloc<float>(part * MAXB)));
+        for (int nt : {1, 2, 4}) {                 // every GEMV shape has a launch plan
+            plan_of(3 * D, D, nt); plan_of(D, D, nt); plan_of(F, D, nt); plan_of(D, F, nt);
+            plan_of(c.vocab, D, nt);
+        }
         const int nsplit = (c.n_enc + XCH - 1) / XCH;
         m->xpart = static_cast<float *>(keep(dalloc<float>(B * H * nsplit * (HD + 2))));
         m->xn = static_cast<uint16_t *>(keep(dalloc<uint16_t>(B * D)));
@@ -722,19 +806,15 @@ XdnaWhisperDec *xdna_whisper_dec_create(XdnaDevice *dev_unused, const XdnaWhispe
         m->ckv = static_cast<uint16_t *>(keep(dalloc<uint16_t>(B * c.n_enc * L * 2 * D)));
         m->enc_bf = static_cast<uint16_t *>(keep(dalloc<uint16_t>(B * c.n_enc * D)));
         m->enc_f = static_cast<float *>(keep(dalloc<float>(B * c.n_enc * D)));
-        const size_t n_rg_max = std::max({ldl / 16, (size_t)3 * D / 16, (size_t)F / 16});   // row groups of any GEMV
-        m->count = static_cast<unsigned *>(keep(dalloc<unsigned>(n_rg_max)));
         m->done = static_cast<unsigned *>(keep(dalloc<unsigned>(1)));
         m->pos = static_cast<int *>(keep(dalloc<int>(1)));
         m->tok = static_cast<int64_t *>(keep(dalloc<int64_t>(B)));
         m->prompt = static_cast<int64_t *>(keep(dalloc<int64_t>(c.max_tgt)));
         m->out_tok = static_cast<int64_t *>(keep(dalloc<int64_t>(B * c.max_tgt)));
         m->tok_out = static_cast<int64_t *>(keep(dalloc<int64_t>(B * c.max_tgt)));
-        ck(cudaMemset(m->count, 0, sizeof(unsigned) * n_rg_max), "memset");
         ck(cudaMemset(m->done, 0, sizeof(unsigned)), "memset");
         ck(cudaFuncSetAttribute(self_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SA_SMEM), "smem");
-        // the GEMV's staged input: up to 32 streams x (3072 + 8) bf16
-        const int gsm = 4 * 8 * (F + 8) * 2;
+        const int gsm = (int)kGemvSmemCap;
         ck(cudaFuncSetAttribute(bfp_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
         ck(cudaFuncSetAttribute(bfp_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
         ck(cudaFuncSetAttribute(bfp_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm), "smem");
