@@ -39,6 +39,10 @@ const char *xdna_last_error(void);
  * (1.0 for an all-zero column), q = clamp(round_half_away(W/scale), -127, 127).  The result is
  * written output-major, q_nk[n*K + k].  Returns 0. */
 int xdna_quant_i8_cols(const float *w, int K, int N, int8_t *q_nk, float *scale);
+/* qrow, the fused decode ELF's per-output-row int8 rule (route_b_kernels/decode_fused/
+ * gen_decode.py:158-165): w [M, K] -> q [M, K], scale [M]; max|row|/127 (1.0 if zero), round
+ * half to even, clip +-127.  q and scale feed xdna_gemv_i8 as q_nk / scale.  Host only. */
+int xdna_quant_i8_rows(const float *w, int M, int K, int8_t *q, float *scale);
 
 /* ------------------------------------------------------------- op level (CtxDecode::gemv) */
 /* y[N] = dot(x, W[:,n]) * scale[n] + bias[n] on the GPU with the engine's exact int8 GEMV

@@ -67,6 +67,21 @@ def test_quantiser_bit_exact_with_oracle(xl, shape):
     np.testing.assert_array_equal(q, oq.T)
 
 
+def test_quant_i8_rows_matches_oracle(xl):
+    """xdna_quant_i8_rows (qrow, the fused ELF's per-row rule) equals or_quant_i8_rows bit for
+    bit; ties round half to even (a row with max 127 has scale exactly 1.0)."""
+    rng = np.random.default_rng(11)
+    w = (rng.standard_normal((40, 96)) * 0.02).astype(np.float32)
+    w[3] = 0.0
+    w[7, :6] = [127.0, 2.5, -3.5, 0.5, -0.5, 126.5]
+    q, s = xl.quant_i8_rows(w)
+    oq, os_ = O.quant_i8_rows(w)
+    np.testing.assert_array_equal(s, os_)
+    np.testing.assert_array_equal(q, oq)
+    assert s[3] == 1.0 and s[7] == 1.0
+    assert list(q[7, :6]) == [127, 2, -4, 0, 0, 126]
+
+
 def test_bfp16_quantize_matches_oracle():
     """xdna_bfp16_quantize (the engine's host-side weight quantiser for bfp16 linears) equals
     or_bfp16_blocks bit for bit, zero blocks and outliers included."""

@@ -49,6 +49,19 @@ def test_gemv_i8_bit_exact(dev, K, N):
     np.testing.assert_array_equal(y0, np.zeros(N, np.float32))
 
 
+def test_gemv_i8_qrow_weights(dev):
+    """The fused ELF's qrow weights (per-row scale, applied before the bias) through the GPU
+    GEMV, bit-exact against the oracle's exact GEMV."""
+    import xdna_engine_b200 as X
+    rng = np.random.default_rng(5)
+    K, N = 768, 2304
+    x = O.bf16_round(rng.standard_normal(K).astype(np.float32))
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    q, s = X.quant_i8_rows(w)
+    b = rng.standard_normal(N).astype(np.float32)
+    np.testing.assert_array_equal(dev.gemv_i8(x, q, s, b), O.gemv_i8_exact(x, q, s, b))
+
+
 SMALL = OptConfig(n_layers=2, d_model=256, n_heads=4, head_dim=64, ffn=512, vocab=1000,
                   max_pos=512)
 

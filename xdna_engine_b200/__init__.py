@@ -64,6 +64,8 @@ def lib():
         L.xdna_device_close.argtypes = [vp]
         L.xdna_quant_i8_cols.argtypes = [vp, i, i, vp, vp]
         L.xdna_quant_i8_cols.restype = i
+        L.xdna_quant_i8_rows.argtypes = [vp, i, i, vp, vp]
+        L.xdna_quant_i8_rows.restype = i
         L.xdna_gemv_i8.argtypes = [vp, vp, i, vp, vp, vp, i, vp]
         L.xdna_gemv_i8.restype = i
         L.xdna_gemv_i8_noalloc.argtypes = [i, vp, i, vp, vp, vp, i, vp]
@@ -162,6 +164,17 @@ def _check(rc):
 
 def _addr(a: np.ndarray) -> int:
     return a.ctypes.data
+
+
+def quant_i8_rows(w: np.ndarray):
+    """qrow (the fused decode ELF's per-row int8 rule, round half to even) of an [M, K] weight:
+    returns (q [M, K], scale [M]), ready for Device.gemv_i8."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    M, K = w.shape
+    q = np.empty((M, K), np.int8)
+    s = np.empty(M, np.float32)
+    _check(lib().xdna_quant_i8_rows(_addr(w), M, K, _addr(q), _addr(s)))
+    return q, s
 
 
 def quant_i8_cols(w: np.ndarray):

@@ -239,6 +239,29 @@ int xdna_quant_i8_cols(const float *w, int K, int N, int8_t *q_nk, float *scale)
     return 0;
 }
 
+// qrow of the fused decode ELF (route_b_kernels/decode_fused/gen_decode.py:158-165): per output
+// row m of an [M, K] weight, scale = max_k |W[m][k]| / 127 (1.0 for an all-zero row),
+// q = clip(round half to even(W / scale), -127, 127).  The result feeds xdna_gemv_i8 directly
+// (q_nk = q, y = (x . q) * scale + bias: the ELF's op_mulw scale before the bias add).
+int xdna_quant_i8_rows(const float *w, int M, int K, int8_t *q, float *scale) {
+    if (!w || !q || !scale || M <= 0 || K <= 0) {
+        set_err("xdna_quant_i8_rows: null pointer or empty shape");
+        return -1;
+    }
+    for (int m = 0; m < M; m++) {
+        const float *row = w + (size_t)m * K;
+        float amax = 0.0f;
+        for (int k = 0; k < K; k++) amax = std::max(amax, std::fabs(row[k]));
+        const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+        scale[m] = s;
+        for (int k = 0; k < K; k++) {
+            const float v = std::nearbyint(row[k] / s);      // round-to-nearest-even mode
+            q[(size_t)m * K + k] = (int8_t)std::min(127.0f, std::max(-127.0f, v));
+        }
+    }
+    return 0;
+}
+
 int xdna_gemv_i8(XdnaDevice *dev, const float *x, int K, const int8_t *q_nk, const float *scale,
                  const float *bias, int N, float *y) {
     if (!dev || !x || !q_nk || !scale || !y) { set_err("xdna_gemv_i8: null pointer"); return -1; }
