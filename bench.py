@@ -117,6 +117,17 @@ def cpu_port_tokens_per_s(cfg, w, prompt, steps, nthreads):
     return steps / dt, dt * 1e3 / steps
 
 
+def max_over_ranks(value, world, device="cuda"):
+    """The largest `value` over the ranks of the process group (the slowest rank's time);
+    `value` itself when world == 1."""
+    if world <= 1:
+        return value
+    import torch
+    t = torch.tensor([float(value)], device=device, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -197,10 +208,7 @@ def run_ours(args):
         torch.distributed.barrier()
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = float(sum(per))
-    if world > 1:
-        t = torch.tensor([total_ms], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        total_ms = float(t.item())
+    total_ms = max_over_ranks(total_ms, world)
     ms_tok = total_ms / args.steps
 
     # L2-warm in-loop figure: one launch decoding the 127 remaining positions
@@ -353,10 +361,7 @@ def run_bge(args):
         e1.record(st)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, world)
     assert X.lib().xdna_gemm_check() == 0, X.last_error()
     # dominant kernel: the tcgen05 GEMM, timed alone on this batch's four GEMM shapes
     A = torch.randn(T, 3072, device="cuda").to(torch.bfloat16)
@@ -499,10 +504,7 @@ def run_whisper(args):
         e1.record(st)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, world)
     assert X.lib().xdna_gemm_check() == 0, X.last_error()
     # dominant kernel: the tcgen05 GEMM, timed alone on one block's four GEMM shapes at M = B*1500
     M = B * 1500
@@ -664,10 +666,7 @@ def run_parakeet(args):
         e1.record(st)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, world)
     assert X.lib().xdna_gemm_check() == 0, X.last_error()
     # dominant kernel: the int8 tcgen05 GEMM, timed alone on one block's eight linears at M = B*T
     M = B * T
@@ -816,10 +815,7 @@ def run_wdec(args):
         e1.record(st)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, world)
     ms_token = ms / steps
     # batch 1 (one stream) per-token latency, same graph machinery
     assert L.xdna_whisper_dec_set_encoder(dec.handle, d_enc.data_ptr(), 1, sp) == 0
@@ -975,10 +971,7 @@ def run_gemma(args):
     ms = e0.elapsed_time(e1) / steps
     toks = np.empty((B, n_new), np.int64)
     assert L.xdna_gemma_tokens(dec.handle, toks.ctypes.data, sp) == 0, X.last_error()
-    if world > 1:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, world)
     # batch 1 per-token latency at a short context, and the end-to-end call (host prompt in)
     p1 = prompts[:1, :64]
     assert L.xdna_gemma_begin(dec.handle, 1, p1.ctypes.data, 64, 64) == 0
