@@ -57,3 +57,35 @@ def test_noalloc_rejects_oversized_call(X):
     x, q, s, b = _case(3, 3072, 2048, True)          # 2 x 6.3 MB of staging > 8 MiB
     with pytest.raises(X.XdnaError, match="8 MiB"):
         _call_noalloc(X, x, q, s, b)
+
+
+def _call_noalloc_on(X, device, x, q_nk, scale, bias):
+    N, K = q_nk.shape
+    y = np.empty(N, np.float32)
+    rc = X.lib().xdna_gemv_i8_noalloc(device, x.ctypes.data, K, q_nk.ctypes.data, scale.ctypes.data,
+                                      None if bias is None else bias.ctypes.data, N, y.ctypes.data)
+    if rc != 0:
+        raise X.XdnaError(X.last_error())
+    return y
+
+
+def test_noalloc_restores_current_device(X):
+    import torch
+    before = torch.cuda.current_device()
+    x, q, s, b = _case(4, 768, 768, True)
+    _call_noalloc_on(X, 0, x, q, s, b)
+    assert torch.cuda.current_device() == before
+
+
+def test_noalloc_per_device_scratch():
+    """device 0, then device 1, then device 0 again: each GPU has its own copy of the array
+    and its own launch attributes, so every call equals that device's allocating GEMV."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import xdna_engine_b200 as X
+    devs = [X.Device(0), X.Device(1)]
+    x, q, s, b = _case(5, 768, 1536, True)
+    for d in (0, 1, 0):
+        got = _call_noalloc_on(X, d, x, q, s, b)
+        np.testing.assert_array_equal(got, devs[d].gemv_i8(x, q, s, b))

@@ -1004,13 +1004,10 @@ cudaError_t launch_opt_decode(const DecodeParams &p, cudaStream_t st) {
 
 cudaError_t launch_gemv_i8(const float *x, int K, const uint8_t *packed, const ChunkRef *chunks,
                            int N, float *y, cudaStream_t st) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SmemMap::total);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    // per-device attribute: set on every launch (cheap), so a second device is covered too
+    cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SmemMap::total);
+    if (e != cudaSuccess) return e;
     const int nch = (N + rows_per_chunk(K) - 1) / rows_per_chunk(K);
     gemv_i8_kernel<<<nch, kThreads, SmemMap::total, st>>>(x, K, packed, chunks, N, y);
     return cudaGetLastError();

@@ -401,12 +401,10 @@ cudaError_t launch_t(const void *A, int lda, const void *B, int ldb, int M, int 
     CUtensorMap ta, tb;
     if (!make_tmap(&ta, A, M, K, lda, BM, I8) || !make_tmap(&tb, B, N, K, ldb, BN, I8)) return cudaErrorInvalidValue;
     constexpr int smem = smem_of(I8);
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<I8, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    // the attribute is per device and cheap to set, so it is set on every launch (a
+    // process-wide "done" flag would skip it on a second device)
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<I8, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
     const int tiles = (N / BN) * ((M + BM - 1) / BM);
     const int sms = sm_count();
     gemm_kernel<I8, E><<<tiles < sms ? tiles : sms, THREADS, smem, st>>>(ta, tb, to, tr, M, N, K, epi);

@@ -13,6 +13,8 @@
 //  * the array is kNoAllocScratchBytes (8 MiB) and every GPU that loads this library keeps it
 //    until the process exits; a call whose staged bytes (N*K int8 + packed copy + vectors)
 //    exceed it is rejected with an error and nothing runs;
+//  * the call makes `device` current for its duration and restores the calling thread's
+//    previous current device before returning;
 //  * the first call on a device looks up the array's device address (cudaGetSymbolAddress)
 //    with that device current; make that first call before any stream capture;
 //  * all calls share the array, which keeps the previous call's contents: every byte the
@@ -115,7 +117,15 @@ extern "C" int xdna_gemv_i8_noalloc(int device, const float *x, int K, const int
                                "(use xdna_gemv_i8 for larger matrices)");
         return -1;
     }
-    cudaError_t e = cudaSetDevice(device);
+    // the call runs with `device` current and gives the calling thread its previous current
+    // device back before it returns, on every path
+    int prev_device = -1;
+    cudaError_t e = cudaGetDevice(&prev_device);
+    if (e == cudaSuccess) e = cudaSetDevice(device);
+    struct RestoreDevice {
+        int dev;
+        ~RestoreDevice() { if (dev >= 0) cudaSetDevice(dev); }
+    } restore{e == cudaSuccess ? prev_device : -1};
     uint8_t *s = e == cudaSuccess ? scratch_for(device, &e) : nullptr;
     if (!s) {
         set_last_error_message(std::string("xdna_gemv_i8_noalloc: scratch set-up failed: ") + cudaGetErrorString(e));
