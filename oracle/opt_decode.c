@@ -9,11 +9,13 @@
  *  OR_MODE_DEVICE   the B200 engine's numerics: LN outputs / attention context / FFN hidden
  *                   rounded to bf16 before each GEMV, K and V stored as bf16, q scaled then
  *                   rounded to bf16, every int8 GEMV computed as the exact integer dot of the
- *                   22-bit fixed-point activation (or_limbs) rounded once to f32, int8 LM head
- *                   (same quantiser, per vocab row), residual stream f32.  LayerNorm sums
- *                   and the per-page online softmax follow the engine's reduction trees and
- *                   use the reference's fast_exp_nonpos, so this mode is bit-exact with the
- *                   GPU (ln_dev_bf16, attn_dev_head).
+ *                   activation in 29-bit fixed point (exponent from the vector's max for the
+ *                   LayerNorm outputs; a weight-derived bound per layer for the attention
+ *                   context and the fc1 output, whose GEMVs the engine splits over K), rounded
+ *                   once to f32, int8 LM head (same quantiser, per vocab row), residual stream
+ *                   f32.  LayerNorm sums and the softmax follow the engine's reduction trees
+ *                   and use the reference's fast_exp_nonpos, so this mode is bit-exact with
+ *                   the GPU (ln_dev_bf16, attn_dev_head, gemv_fix).
  *
  * The GEMVs are parallelised over output columns with OpenMP; each output keeps the
  * reference's k-ascending summation order, so results do not depend on the thread count.
@@ -44,6 +46,7 @@ struct or_opt {
     float *kc, *vc;        /* [L][max_ctx][D] (DEVICE: values already bf16-rounded) */
     int max_ctx;
     float *trace;          /* optional [pos][2L+1][D] residual-stream record */
+    int *fix_ctx, *fix_h;  /* DEVICE: [L] fixed-point exponents of the K-split GEMV inputs */
 };
 
 void or_opt_set_trace(or_opt *m, float *trace) { m->trace = trace; }
@@ -52,6 +55,8 @@ static void trace_x(or_opt *m, int pos, int slot, const float *v) {
     int D = m->cfg.d_model;
     memcpy(m->trace + ((size_t)pos * (2 * m->cfg.n_layers + 1) + slot) * D, v, sizeof(float) * D);
 }
+
+static int fix_of_bound(const lin_t *l, int n0, int n1, const float *g, const float *b, int D);
 
 static void lin_init(lin_t *l, const float *w, const float *b, int K, int N, int mode) {
     l->K = K; l->N = N; l->bias = b; l->w = w;
@@ -102,6 +107,15 @@ or_opt *or_opt_create(const or_opt_cfg *cfg, const or_opt_weights *w, int mode, 
             }
         }
     }
+    if (mode == OR_MODE_DEVICE) {
+        m->fix_ctx = (int *)malloc(sizeof(int) * (size_t)L);
+        m->fix_h = (int *)malloc(sizeof(int) * (size_t)L);
+        for (int l = 0; l < L; l++) {
+            const or_opt_layer *ly = &w->layers[l];
+            m->fix_ctx[l] = fix_of_bound(&m->lins[l * 6 + 2], 0, D, ly->ln1_w, ly->ln1_b, D);
+            m->fix_h[l] = fix_of_bound(&m->lins[l * 6 + 4], 0, F, ly->ln2_w, ly->ln2_b, D);
+        }
+    }
     m->max_ctx = cfg->max_pos;
     m->kc = (float *)malloc(sizeof(float) * (size_t)L * m->max_ctx * D);
     m->vc = (float *)malloc(sizeof(float) * (size_t)L * m->max_ctx * D);
@@ -111,7 +125,8 @@ or_opt *or_opt_create(const or_opt_cfg *cfg, const or_opt_weights *w, int mode, 
 void or_opt_free(or_opt *m) {
     if (!m) return;
     for (int i = 0; i < m->cfg.n_layers * 6; i++) { free(m->lins[i].q); free(m->lins[i].scale); }
-    free(m->lins); free(m->lm_q); free(m->lm_scale); free(m->kc); free(m->vc); free(m);
+    free(m->lins); free(m->lm_q); free(m->lm_scale); free(m->kc); free(m->vc);
+    free(m->fix_ctx); free(m->fix_h); free(m);
 }
 
 const int8_t *or_opt_qweight(const or_opt *m, int layer, int which, float const **scale) {
@@ -134,29 +149,24 @@ static float warp_tree(const float *v32) {
     }
     return v[0];
 }
-/* LayerNorm as the engine computes it: the formula of rust/npu-asr-host/src/lib.rs:79-110 with
- * the engine's summation tree -- thread (warp w, lane l) of 256 sums its elements
- * 32*(w + 8j) + l in j order, each warp combines its lanes with the butterfly, and the 8
- * warp totals are added in warp order from 0 -- output rounded to bf16. */
-static float tree256(const float *x, int D, float sub_mean, int squares) {
-    float tot = 0.0f;
-    for (int w = 0; w < 8; w++) {
-        float part[32];
-        for (int l = 0; l < 32; l++) {
-            float s = 0.0f;
-            for (int i = 32 * w + l; i < D; i += 256) {
-                if (squares) { float c = x[i] - sub_mean; s = s + c * c; }
-                else s = s + x[i];
-            }
-            part[l] = s;
+/* LayerNorm as one engine warp computes it: the formula of rust/npu-asr-host/src/lib.rs:79-110
+ * with lane l summing elements l + 32j in j order, then the butterfly; output rounded to
+ * bf16. */
+static float lane_tree(const float *x, int D, float sub_mean, int squares) {
+    float part[32];
+    for (int l = 0; l < 32; l++) {
+        float s = 0.0f;
+        for (int i = l; i < D; i += 32) {
+            if (squares) { float c = x[i] - sub_mean; s = s + c * c; }
+            else s = s + x[i];
         }
-        tot = tot + warp_tree(part);
+        part[l] = s;
     }
-    return tot;
+    return warp_tree(part);
 }
 static void ln_dev_bf16(const float *x, const float *g, const float *b, int D, float eps, float *y) {
-    float mean = tree256(x, D, 0.0f, 0) / (float)D;
-    float var = tree256(x, D, mean, 1) / (float)D;
+    float mean = lane_tree(x, D, 0.0f, 0) / (float)D;
+    float var = lane_tree(x, D, mean, 1) / (float)D;
     float inv = 1.0f / sqrtf(var + eps);
     for (int i = 0; i < D; i++) {
         float t0 = (x[i] - mean) * inv;
@@ -164,60 +174,112 @@ static void ln_dev_bf16(const float *x, const float *g, const float *b, int D, f
         y[i] = or_bf16_round(t0 + b[i]);
     }
 }
-/* Single-query attention of one head as the engine splits it: one partial (m, l, acc) per
- * 64-key page (mha_tile's online softmax, route_b_kernels/mha_decode/mha_decode.cc:90-168,
- * applied per page); the pages of each group of OR_GROUP_PAGES are merged in order into a
- * group partial, and the group partials are merged in order; exp = the reference's
- * fast_exp_nonpos.  (With one group, the second merge is the identity.) */
-#define OR_GROUP_PAGES 3
-static void fold(float *M, float *L, float *A, float m, float l, const float *a) {
-    float mn = fmaxf(*M, m);
-    float c0 = or_fast_exp_nonpos(*M - mn), c1 = or_fast_exp_nonpos(m - mn);
-    *L = *L * c0 + l * c1;
-    for (int d = 0; d < 64; d++) A[d] = A[d] * c0 + a[d] * c1;
-    *M = mn;
+
+/* ---- 29-bit fixed point (the engine's GEMV input) ---------------------------------- */
+#define FIX_BITS 29
+/* exponent s with max|x| * 2^s < 2^29 (29 when max|x| < 2^-96) */
+static int fix_of_max(float m) {
+    uint32_t u;
+    memcpy(&u, &m, 4);
+    int E = m >= 0x1p-96f ? (int)((u >> 23) & 0xff) - 126 : 0;
+    return FIX_BITS - E;
 }
-static void attn_dev_head(const float *q, const float *kc, const float *vc, int stride, int tk,
-                          float *ctx) {
-    float M = -INFINITY, L = 0.0f, A[64];
-    for (int d = 0; d < 64; d++) A[d] = 0.0f;
-    for (int g0 = 0; g0 < tk; g0 += 64 * OR_GROUP_PAGES) {
-        float Mg = -INFINITY, Lg = 0.0f, Ag[64];
-        for (int d = 0; d < 64; d++) Ag[d] = 0.0f;
-        for (int j0 = g0; j0 < tk && j0 < g0 + 64 * OR_GROUP_PAGES; j0 += 64) {
-            int nk = tk - j0 < 64 ? tk - j0 : 64;
-            float sc[64], pr[64], m = -INFINITY, ap[64];
-            for (int k = 0; k < 64; k++) {
-                if (k >= nk) { sc[k] = -INFINITY; continue; }
-                const float *kr = kc + (size_t)(j0 + k) * stride;
-                float s4[4];
-                for (int q4 = 0; q4 < 4; q4++) {
-                    float sd = 0.0f;
-                    for (int d = 0; d < 16; d++) sd = fmaf(q[16 * q4 + d], kr[16 * q4 + d], sd);
-                    s4[q4] = sd;
-                }
-                sc[k] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
-                m = fmaxf(m, sc[k]);
-            }
-            float v32[32];
-            for (int k = 0; k < 64; k++) pr[k] = k < nk ? or_fast_exp_nonpos(sc[k] - m) : 0.0f;
-            for (int l = 0; l < 32; l++) v32[l] = pr[l] + pr[l + 32];
-            float lp = warp_tree(v32);
-            for (int d = 0; d < 64; d++) {
-                float a4[4];
-                for (int q4 = 0; q4 < 4; q4++) {
-                    float a = 0.0f;
-                    for (int j = 16 * q4; j < 16 * q4 + 16 && j < nk; j++)
-                        a = fmaf(pr[j], vc[(size_t)(j0 + j) * stride + d], a);
-                    a4[q4] = a;
-                }
-                ap[d] = ((a4[0] + a4[1]) + a4[2]) + a4[3];
-            }
-            fold(&Mg, &Lg, Ag, m, lp, ap);
-        }
-        fold(&M, &L, A, Mg, Lg, Ag);
+static int fix_of_vec(const float *x, int n) {
+    float m = 0.0f;
+    for (int i = 0; i < n; i++) m = fmaxf(m, fabsf(x[i]));
+    return fix_of_max(m);
+}
+/* X = rint(x * 2^s), clamped to +-(2^30 - 64) */
+static int32_t to_fix(float x, int s) {
+    float v = x * ldexpf(1.0f, s);
+    v = fminf(fmaxf(v, -1073741760.0f), 1073741760.0f);
+    return (int32_t)nearbyintf(v);
+}
+/* Data-independent exponent for a linear's output rows [n0, n1) fed by a LayerNorm with
+ * parameters (g, b): |y_n| <= sum_k |q[n][k]| scale[n] (sqrt(D)|g_k| + |b_k|) + |bias_n|;
+ * 1% margins cover the bf16 / f32 roundings.  The same double arithmetic as the engine. */
+static int fix_of_bound(const lin_t *l, int n0, int n1, const float *g, const float *b, int D) {
+    double *lnmax = (double *)malloc(sizeof(double) * (size_t)D);
+    for (int k = 0; k < D; k++) lnmax[k] = (sqrt((double)D) * fabs((double)g[k]) + fabs((double)b[k])) * 1.01;
+    double B = 0.0;
+    for (int n = n0; n < n1; n++) {
+        const int8_t *q = l->q + (size_t)n * l->K;
+        double s = 0.0;
+        for (int k = 0; k < l->K; k++) s += fabs((double)q[k]) * lnmax[k];
+        s = s * (double)l->scale[n] + fabs((double)(l->bias ? l->bias[n] : 0.0f));
+        if (s > B) B = s;
     }
-    for (int d = 0; d < 64; d++) ctx[d] = or_bf16_round(A[d] / L);
+    free(lnmax);
+    B *= 1.01;
+    if (!(B > 0.0)) return FIX_BITS;
+    int E = 0;
+    frexp(B, &E);
+    return FIX_BITS - E;
+}
+/* exact int8 GEMV on an output-major [N,K] weight with the activation in fixed point 2^s:
+ * y = ((float)sum X_k q_nk * 2^-s) * scale + bias */
+static void gemv_fix(const or_opt *m, const int8_t *wq, const float *scale, const float *bias, int K, int N,
+                     const float *x, int s, float *y) {
+    int32_t *X = (int32_t *)malloc(sizeof(int32_t) * (size_t)K);
+    for (int k = 0; k < K; k++) X[k] = to_fix(x[k], s);
+    float inv = ldexpf(1.0f, -s);
+#pragma omp parallel for num_threads(m->nthreads) schedule(static)
+    for (int n = 0; n < N; n++) {
+        const int8_t *w = wq + (size_t)n * K;
+        int64_t S = 0;
+        for (int k = 0; k < K; k++) S += (int64_t)X[k] * w[k];
+        float t = (float)S * inv;
+        t = t * scale[n];
+        y[n] = t + (bias ? bias[n] : 0.0f);
+    }
+    free(X);
+}
+
+/* Single-query attention of one head as an engine head pair computes it: CTA r owns dims
+ * [32r, 32r+32); its partial score of key j is 4 fma chains of 8 dims, (c0 + c1) + (c2 + c3);
+ * s_j = part_0 + part_1; M = max s; p_j = fast_exp_nonpos(s_j - M) (rust/npu-asr-host/src/
+ * lib.rs:38-58); l = sum over 256 lanes of keys j = t mod 256 in order, butterfly per warp of
+ * 32, the 8 warp sums in order; ctx_d = (sum over groups g = 0..7, in order, of the fma chain
+ * over keys j = g mod 8) / l, rounded to bf16.  mha_tile (route_b_kernels/mha_decode/
+ * mha_decode.cc:90-168) with one softmax over the whole context. */
+static void attn_dev_head(const float *q, const float *kc, const float *vc, int stride, int tk,
+                          float *sc, float *ctx) {
+    float M = -INFINITY;
+    for (int j = 0; j < tk; j++) {
+        const float *kr = kc + (size_t)j * stride;
+        float part[2];
+        for (int r = 0; r < 2; r++) {
+            float c4[4];
+            for (int i = 0; i < 4; i++) {
+                float a = 0.0f;
+                for (int d = 0; d < 8; d++) a = fmaf(q[32 * r + 8 * i + d], kr[32 * r + 8 * i + d], a);
+                c4[i] = a;
+            }
+            part[r] = (c4[0] + c4[1]) + (c4[2] + c4[3]);
+        }
+        sc[j] = part[0] + part[1];
+        M = fmaxf(M, sc[j]);
+    }
+    for (int j = 0; j < tk; j++) sc[j] = or_fast_exp_nonpos(sc[j] - M);
+    float L = 0.0f;
+    for (int w = 0; w < 8; w++) {
+        float v32[32];
+        for (int l = 0; l < 32; l++) {
+            float a = 0.0f;
+            for (int j = 32 * w + l; j < tk; j += 256) a = a + sc[j];
+            v32[l] = a;
+        }
+        L = L + warp_tree(v32);
+    }
+    for (int d = 0; d < 64; d++) {
+        float tot = 0.0f;
+        for (int g = 0; g < 8; g++) {
+            float a = 0.0f;
+            for (int j = g; j < tk; j += 8) a = fmaf(sc[j], vc[(size_t)j * stride + d], a);
+            tot = tot + a;
+        }
+        ctx[d] = or_bf16_round(tot / L);
+    }
 }
 
 /* Lin::fwd (int8 branch) parallel over blocks of output columns, k-outer inside a block. */
@@ -238,25 +300,6 @@ static void lin_fwd_ref(const or_opt *m, const lin_t *l, const float *x, float *
     }
 }
 
-/* exact limbed int8 GEMV on an output-major [N,K] weight (device numerics) */
-static void gemv_exact(const or_opt *m, const int8_t *wq, const float *scale, const float *bias,
-                       int K, int N, const float *x, float *y) {
-    int8_t *a = (int8_t *)malloc((size_t)K * 3);
-    int8_t *b = a + K, *c = b + K;
-    int s = or_limbs(x, K, a, b, c);
-#pragma omp parallel for num_threads(m->nthreads) schedule(static)
-    for (int n = 0; n < N; n++) {
-        const int8_t *w = wq + (size_t)n * K;
-        int64_t A = 0, B = 0, C = 0;
-        for (int k = 0; k < K; k++) { A += a[k] * w[k]; B += b[k] * w[k]; C += c[k] * w[k]; }
-        int64_t S = A * 65536 + B * 256 + C;
-        float t = ldexpf((float)S, -s);
-        t = t * scale[n];
-        y[n] = t + (bias ? bias[n] : 0.0f);
-    }
-    free(a);
-}
-
 /* Lin::fwd f32 branch (opt125m_decode.rs:125-128): y = x.W + b, k ascending. */
 static void lin_fwd_f32(const or_opt *m, const lin_t *l, const float *x, float *y) {
     int K = l->K, N = l->N;
@@ -268,9 +311,10 @@ static void lin_fwd_f32(const or_opt *m, const lin_t *l, const float *x, float *
     }
 }
 
-static void lin_apply(const or_opt *m, const lin_t *l, const float *x, float *y) {
+/* s_fix: the device mode's fixed-point exponent (ignored by the other modes) */
+static void lin_apply(const or_opt *m, const lin_t *l, const float *x, int s_fix, float *y) {
     if (m->mode == OR_MODE_F32) lin_fwd_f32(m, l, x, y);
-    else if (m->mode == OR_MODE_DEVICE) gemv_exact(m, l->q, l->scale, l->bias, l->K, l->N, x, y);
+    else if (m->mode == OR_MODE_DEVICE) gemv_fix(m, l->q, l->scale, l->bias, l->K, l->N, x, s_fix, y);
     else lin_fwd_ref(m, l, x, y);
 }
 
@@ -290,9 +334,10 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
         lin_t *lin = m->lins + l * 6;
         if (dev) ln_dev_bf16(x, ly->ln1_w, ly->ln1_b, D, c->eps, h);
         else or_layer_norm(x, ly->ln1_w, ly->ln1_b, 1, D, c->eps, h);
-        lin_apply(m, &lin[0], h, q);
-        lin_apply(m, &lin[1], h, kn);
-        lin_apply(m, &lin[2], h, vn);
+        int sx = dev ? fix_of_vec(h, D) : 0;
+        lin_apply(m, &lin[0], h, sx, q);
+        lin_apply(m, &lin[1], h, sx, kn);
+        lin_apply(m, &lin[2], h, sx, vn);
         for (int d = 0; d < D; d++) q[d] = q[d] * scale;
         if (dev) { or_bf16_round_n(q, q, D); or_bf16_round_n(kn, kn, D); or_bf16_round_n(vn, vn, D); }
         float *kc = m->kc + (size_t)l * m->max_ctx * D, *vc = m->vc + (size_t)l * m->max_ctx * D;
@@ -318,18 +363,18 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
                     ctx[c0 + d] = s;
                 }
             } else {
-                attn_dev_head(q + c0, kc + c0, vc + c0, D, tk, ctx + c0);
+                attn_dev_head(q + c0, kc + c0, vc + c0, D, tk, sc, ctx + c0);
             }
         }
-        lin_apply(m, &lin[3], ctx, o);
+        lin_apply(m, &lin[3], ctx, dev ? m->fix_ctx[l] : 0, o);
         for (int d = 0; d < D; d++) xr[d] = x[d] + o[d];
         trace_x(m, pos, 2 * l, xr);
         if (dev) ln_dev_bf16(xr, ly->ln2_w, ly->ln2_b, D, c->eps, h);
         else or_layer_norm(xr, ly->ln2_w, ly->ln2_b, 1, D, c->eps, h);
-        lin_apply(m, &lin[4], h, f);
+        lin_apply(m, &lin[4], h, dev ? fix_of_vec(h, D) : 0, f);
         for (int i = 0; i < F; i++) f[i] = f[i] > 0.0f ? f[i] : 0.0f;
         if (dev) or_bf16_round_n(f, f, (size_t)F);
-        lin_apply(m, &lin[5], f, o);
+        lin_apply(m, &lin[5], f, dev ? m->fix_h[l] : 0, o);
         for (int d = 0; d < D; d++) x[d] = xr[d] + o[d];
         trace_x(m, pos, 2 * l + 1, x);
     }
@@ -338,7 +383,7 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
         else or_layer_norm(x, m->w.lnf_w, m->w.lnf_b, 1, D, c->eps, h);
         if (dev) {
             trace_x(m, pos, 2 * c->n_layers, h);
-            gemv_exact(m, m->lm_q, m->lm_scale, NULL, D, V, h, logits);
+            gemv_fix(m, m->lm_q, m->lm_scale, NULL, D, V, h, fix_of_vec(h, D), logits);
         } else {
 #pragma omp parallel for num_threads(m->nthreads) schedule(static)
             for (int v = 0; v < V; v++) {

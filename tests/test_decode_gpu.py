@@ -75,10 +75,11 @@ def _run_pair(X, dev, cfg, w, prompt, n_new, grid=0, max_ctx=None):
     return ids, lg, oids, olg
 
 
-@pytest.mark.parametrize("grid", [0, 8])
+@pytest.mark.parametrize("grid", [0, 10])
 def test_decode_small_matches_oracle(X, dev, grid):
     """2-layer model, std 0.2 weights so the greedy stream varies; 70 new tokens cross the
-    64-token KV page boundary; grid=8 makes every CTA own several attention items."""
+    64-token KV page boundary; grid=10 leaves two FC CTAs, each owning 8 blocks of fc1 rows
+    (several row-tile groups and k-blocks per CTA)."""
     w = make_opt_weights(SMALL, seed=3, std=0.2, bias_std=0.05, ln_std=0.1)
     prompt = make_prompt(SMALL, 9, seed=3)
     ids, lg, oids, olg = _run_pair(X, dev, SMALL, w, prompt, 70, grid=grid)
@@ -87,10 +88,10 @@ def test_decode_small_matches_oracle(X, dev, grid):
     np.testing.assert_array_equal(lg, olg)
 
 
-@pytest.mark.parametrize("n_prompt,n_new,grid", [(1, 200, 0), (200, 300, 0), (200, 300, 8)])
+@pytest.mark.parametrize("n_prompt,n_new,grid", [(1, 200, 0), (200, 300, 0), (200, 300, 10)])
 def test_decode_prompt_of_one_and_long_context(X, dev, n_prompt, n_new, grid):
-    """Contexts past one attention item (3 KV pages = 192 positions): several page groups per
-    head, merged by the O-projection CTAs; grid=8 gives CTAs several groups each."""
+    """Contexts past the 256 keys staged once per layer: keys and values are then streamed in
+    chunks of 512; the prompt of one token starts with an LM-head step."""
     w = make_opt_weights(SMALL, seed=4, std=0.2)
     prompt = make_prompt(SMALL, n_prompt, seed=4)
     ids, lg, oids, olg = _run_pair(X, dev, SMALL, w, prompt, n_new, grid=grid, max_ctx=n_prompt + n_new)

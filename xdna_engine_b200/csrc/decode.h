@@ -1,5 +1,18 @@
-// decode.h -- device-side parameter block and layout constants of the persistent opt decode
-// kernel, shared by the kernel (decode_kernel.cu) and the host packer (engine.cpp).
+// decode.h -- parameter block, layout constants and work partition of the persistent opt
+// decode kernel, shared by the kernel (decode_kernel.cu) and the host packer (engine.cu).
+//
+// CTA roles (grid G, clusters of 2 CTAs):
+//   head pair h (CTAs 2h, 2h+1; cluster rank r): q|k|v rows of dims [32r, 32r+32) of head h,
+//     single-query attention over those dims (partial scores swapped with the pair's other
+//     CTA through distributed shared memory), then its K-split slice of the out projection;
+//   FC CTA i (CTAs 2H + i, i < n_fc): 32-row blocks [kb0_i, kb1_i) of fc1, then the K-split
+//     slice of fc2 over exactly those hidden rows;
+//   spare CTAs: neither; like every CTA they keep the residual stream and take a share of the
+//     LM head.
+// The out projection and fc2 are summed over their K slices in exact integer arithmetic:
+// every contributor adds (partial + 2^bias_shift + 2^56) into one 64-bit accumulator word per
+// output with red.add.u64; the top 8 bits count contributions, so a reader knows the word is
+// complete when the count reaches the number of contributors (no flags, no fences).
 #pragma once
 #include <cstdint>
 
@@ -8,54 +21,57 @@ namespace xdna {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;   // + one producer warp
-constexpr int kStageBytes = 32768;                // one weight chunk (ring stage)
-constexpr int kStages = 4;                        // ring depth: 128 KB of weights in flight
-constexpr int kKmax = 3072;                       // largest GEMV reduction length
+constexpr int kSlotBytes = 16384;                 // one ring slot
+constexpr int kSlots = 8;                         // ring depth: 128 KB of weights in flight
 constexpr int kDmax = 768;                        // largest model width
+constexpr int kFmax = 3072;                       // largest FFN width
 constexpr int kHeadDim = 64;                      // the kernel's attention head size
+constexpr int kHalfDim = 32;                      // head dims owned by one CTA of a pair
 constexpr int kPageTokens = 64;                   // KV page = 64 positions (the reference's TKV tile)
-constexpr int kMaxTilesPerChunk = kStageBytes / (768 + 8) / 8;   // 5 for K=768
-constexpr int kMaxPages = 64;                     // KV pages per sequence (4096 positions)
-constexpr int kGroupPages = 3;                    // KV pages one attention item covers (192 positions)
-constexpr int kRowMeta = 8;                       // per-row f32 scale + f32 bias after the rows
+constexpr int kMaxCtx = 2048;                     // positions per sequence
+constexpr int kMaxPages = kMaxCtx / kPageTokens;
+constexpr int kStageKeys = 256;                   // cached keys staged once per layer (fast path)
+constexpr int kChunkKeys = 512;                   // keys per staged chunk beyond that
+constexpr int kAccSlots = 4;                      // token ring of the accumulator words
+constexpr int kLimbs = 4;                         // X = a*2^24 + b*2^16 + c*2^8 + d
+constexpr int kLimbStride = kFmax + 16;           // bytes per limb row (bank offset 4 words)
+constexpr int kTile = 16;                         // output rows of one MMA m-tile
+constexpr int kFragBytes = 512;                   // one m-tile x one 32-wide k-block
+constexpr int kSliceTilesPerChunk = 24;           // m-tiles of a K-split chunk (12 KB)
+constexpr int kFcRows = 32;                       // fc1 rows per k-block of fc2
+constexpr int kFixBits = 29;                      // |X| < 2^29
+constexpr int kCountShift = 56;                   // accumulator word: count in bits 56..63
+constexpr int kMaxVocabTilesPerCta = 64;
 
-// Row partition and chunking shared by the host packer and the kernel.  Rows are assigned
-// in units of 8 (one MMA n-tile); CTA c of `grid` owns units [c*U/grid, (c+1)*U/grid).
-__host__ __device__ inline int part_row0(int c, int n_rows, int grid) {
-    return 8 * (int)((long long)c * (n_rows / 8) / grid);
-}
-__host__ __device__ inline int part_rows(int c, int n_rows, int grid) {
-    return part_row0(c + 1, n_rows, grid) - part_row0(c, n_rows, grid);
-}
-// rows per chunk for reduction length K: whole n-tiles of (K bytes + 8 bytes meta) per stage
-__host__ __device__ inline int rows_per_chunk(int K) {
-    const int r = (kStageBytes / (K + kRowMeta)) & ~7;
-    return r < 8 * kMaxTilesPerChunk ? r : 8 * kMaxTilesPerChunk;
-}
-__host__ __device__ inline int n_chunks(int rows, int K) {
-    int r = rows_per_chunk(K);
-    return (rows + r - 1) / r;
-}
-__host__ __device__ inline uint32_t chunk_bytes(int rows, int K) {
-    return (uint32_t)(((size_t)rows * (K + kRowMeta) + 15) & ~(size_t)15);
-}
+// 32-row blocks of fc1 / k-blocks of fc2 owned by FC CTA i of n
+__host__ __device__ inline int fc_kb0(int i, int n_kb, int n_fc) { return (int)((long long)i * n_kb / n_fc); }
+// LM-head m-tiles owned by CTA c of G
+__host__ __device__ inline int lm_tile0(int c, int n_tiles, int G) { return (int)((long long)c * n_tiles / G); }
 
-// GEMV phases of one token, in weight-stream order per layer, then the LM head.
-enum Phase { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_FC1 = 3, PH_FC2 = 4 };
-constexpr int kPhasesPerLayer = 5;
+// bytes of a row-tile chunk (16 output rows x K, fragment order, then 16 x (scale, bias))
+__host__ __device__ inline uint32_t row_chunk_bytes(int K) { return (uint32_t)(kTile * K + kTile * 8); }
+// K-split chunks of an N-output slice (one 32-wide k-block)
+__host__ __device__ inline int slice_chunks(int N) {
+    return (N / kTile + kSliceTilesPerChunk - 1) / kSliceTilesPerChunk;
+}
+__host__ __device__ inline int slice_chunk_tiles(int N, int c) {
+    const int t = N / kTile - c * kSliceTilesPerChunk;
+    return t < kSliceTilesPerChunk ? t : kSliceTilesPerChunk;
+}
 
 // error codes written to RunState::error
 enum : uint32_t {
     ERR_NONE = 0,
     ERR_TIMEOUT_FULL = 1,      // consumer waited too long for a weight chunk
-    ERR_TIMEOUT_EMPTY = 2,     // producer waited too long for a free stage
-    ERR_TIMEOUT_FLAG = 3,      // a flag-tagged word never reached its epoch
+    ERR_TIMEOUT_EMPTY = 2,     // producer waited too long for a free slot
+    ERR_TIMEOUT_FLAG = 3,      // an exchange word never completed
     ERR_BAD_TOKEN = 4,         // token id out of range
     ERR_BAD_POS = 5,           // position beyond the KV capacity
+    ERR_TIMEOUT_PEER = 6,      // the pair CTA's partial scores never arrived
 };
 
 struct RunState {
-    uint32_t epoch_base;       // first epoch of the next launch (advanced by CTA 0 at exit)
+    uint32_t tok_base;         // tokens decoded by earlier launches (advanced by CTA 0 at exit)
     uint32_t error;            // first error code (0 = none)
     uint32_t error_cta;        // CTA that reported it
     uint32_t error_where;      // phase / detail
@@ -63,15 +79,16 @@ struct RunState {
 
 struct ChunkRef {              // one weight chunk of a CTA's stream
     uint32_t off;              // byte offset from DecodeParams::stream
-    uint32_t bytes;            // multiple of 16
+    uint32_t bytes;            // multiple of 16, <= kSlotBytes
 };
 
 struct DecodeParams {
     // model
     int n_layers, d_model, n_heads, ffn, vocab, max_pos;
     float eps;
-    // grid / stream
-    int grid;                  // number of CTAs (all co-resident)
+    // grid / roles
+    int grid, n_fc;            // G CTAs (even, clusters of 2); FC CTAs
+    int vocab_tiles;           // ceil(vocab / 16)
     const uint8_t *stream;     // packed int8 weight stream of all CTAs
     const ChunkRef *chunks;    // [grid][chunk_stride]: layer chunks, then LM chunks
     const int *n_layer_chunks; // [grid]
@@ -82,26 +99,27 @@ struct DecodeParams {
     const float *emb_pos;      // [max_pos + 2, D]
     const float *ln;           // [L][4][D]: ln1_w ln1_b ln2_w ln2_b
     const float *lnf;          // [2][D]
-    // paged KV cache: [L][n_phys_pages][2][H][page][hd] bf16
+    const float *osb;          // [L][2][D]: out-proj scale, bias
+    const float *f2sb;         // [L][2][D]: fc2 scale, bias
+    const int *fix_ctx;        // [L] fixed-point exponent of the attention context (out-proj input)
+    const int *fix_h;          // [L] fixed-point exponent of the fc1 output (fc2 input)
+    int o_bias_shift, f2_bias_shift;
+    // paged KV cache: [L][phys_page][H][2 halves][K|V][64 positions][32 dims] bf16
     uint16_t *kv;
     const int *page_table;     // logical page -> physical page
     int n_phys_pages;
-    // flag-tagged exchange words
-    uint64_t *ll_qkv;          // [3D/2]   bf16 pairs
-    uint64_t *ll_att;          // [max_pages*H][2+hd]  m, l, acc[hd]
-    uint64_t *ll_o;            // [D]      f32
-    uint64_t *ll_h;            // [F/2]    bf16 pairs
-    uint64_t *ll_f2;           // [D]      f32
-    uint64_t *ll_lm;           // [grid][2] (best value, index)
+    // exchange
+    unsigned long long *acc;   // [kAccSlots][L][2: out-proj, fc2][D] accumulator words
+    uint64_t *ll_lm;           // [grid][2] flag-tagged LM-head best keys
     // run
-    int64_t *tokens;           // [max_pos + 1]: prompt in, generated ids out at pos+1
+    int64_t *tokens;           // [max_ctx + 1]: prompt in, generated ids out at pos+1
     float *logits;             // optional [n_steps][V] (only steps with an LM head)
     int start_pos, n_steps, n_prompt;
     RunState *state;
     uint64_t timeout_ns;
     float *trace;              // optional [n_steps][2L+1][D]: residual after attention and
                                // after the FFN of each layer, then the final LN output
-    unsigned long long *timing; // optional [2][grid][128] globaltimer stamps (first 2 steps)
+    unsigned long long *timing; // optional [2][grid][64] globaltimer stamps (first 2 steps)
 };
 
 }  // namespace xdna

@@ -4,31 +4,32 @@
 // Opt::step (252-293) / Opt::generate (296-315) on the host, and the fused NPU decode ELF
 // route_b_kernels/decode_fused/gen_decode.py (runlist 391-425).
 //
-// Design (B200-first):
-//  * one CTA per SM, all co-resident (cooperative launch); each CTA = 8 consumer warps + 1
-//    producer warp.
-//  * every weight byte of a token is pre-packed on the host into ONE contiguous stream per
-//    CTA, in the order the CTA consumes it (QKV, O, FC1, FC2 rows of each layer, then its
-//    slice of the LM head).  The producer warp streams it with 1-D bulk async copies
-//    (cp.async.bulk + mbarrier complete_tx) through a 5 x 32 KB shared-memory ring.  Weights
-//    do not depend on activations, so HBM streaming never waits for the layer chain: it only
-//    stalls when the ring is full.
-//  * GEMV = int8 tensor-core MMA (m16n8k32): the bf16 activation vector is turned into a
-//    22-bit fixed-point integer (per-vector power-of-two scale) split into three int8 limbs,
-//    the limbs are the A operand rows, the int8 weight rows straight from the ring are the B
-//    operand.  The int32 limb sums are combined exactly (int64) and rounded once to f32:
-//    the dot product is exact, so the kernel reproduces the CPU oracle bit for bit.
-//  * consecutive phases exchange their small output vectors through flag-tagged 64-bit
-//    words (data | epoch) in global memory: a consumer polls the words it needs until their
-//    epoch matches; no grid barrier, no fence on the critical path.
-//  * attention: item (page p, head h) -> CTA (p*H + h) mod grid, statically, so the CTA
-//    that appends a position's K/V to a page is the one that later reads that page: the KV
-//    cache never crosses CTAs within a launch.  The page's cached rows are prefetched with
-//    cp.async at the start of the layer.  Partial (max, sum, acc) per page are combined
-//    flash-decode style by the O-projection CTAs.
+// A batch-1 decode token is latency-bound (about 128 MB of weights, but dozens of dependent
+// steps), so the design minimises the dependent global exchanges per layer -- two -- and
+// keeps every step between them short:
+//  * one CTA per SM, clusters of 2, each CTA = 8 consumer warps + 1 producer warp.  The roles
+//    (head pair / FC / spare) and the exact-integer accumulator words are described in
+//    decode.h.
+//  * every weight byte a CTA needs for a token is pre-packed on the host into ONE contiguous
+//    stream in consumption order and in mma.sync fragment order; the producer warp streams it
+//    with 1-D bulk async copies (cp.async.bulk + mbarrier complete_tx, no multicast) through
+//    an 8 x 16 KB ring.  Weights do not depend on activations, so HBM streaming runs ahead of
+//    the layer chain and only stalls when the ring is full.
+//  * GEMV = int8 tensor-core MMA (m16n8k32, weights = A, 16 output rows per MMA): the bf16
+//    activation vector becomes a 29-bit fixed-point integer X split into four int8 limbs,
+//    which are the four live columns of B.  Limb sums are combined exactly in int64 and
+//    rounded once to f32: every dot product is exact, so the result does not depend on how K
+//    is split and the CPU oracle reproduces it bit for bit.
+//  * layer chain: [all CTAs: residual += fc2 of the previous layer (accumulator words)] ->
+//    head pairs: LayerNorm (each warp redundantly, no block barrier), q|k|v of their 32 dims,
+//    partial scores swapped with the other CTA of the pair by st.async into its shared memory,
+//    softmax, P.V of their dims, K-split out projection added into the accumulator words ->
+//    [all CTAs: residual += out projection] -> FC CTAs: LayerNorm, fc1 rows, ReLU, K-split fc2
+//    added into the accumulator words.
 //  * every wait is bounded (globaltimer deadline); a timeout records an error code in
-//    RunState, makes all CTAs leave at their next phase boundary, and the producer drains
-//    its in-flight copies before exiting.
+//    RunState, the CTA's threads agree on leaving through a barrier reduction, the producer
+//    drains its in-flight copies, and both CTAs of a cluster meet at a final cluster barrier
+//    (so neither exits while the other may still write into its shared memory).
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cstdint>
@@ -42,67 +43,127 @@ namespace xdna {
 // ------------------------------------------------------------------------------ smem map
 struct SmemMap {
     static constexpr int ring = 0;
-    static constexpr int limbs = ring + kStages * kStageBytes;           // 3 x kKmax int8
-    static constexpr int act = limbs + 3 * kKmax;                        // kKmax bf16 / words
-    static constexpr int xs = act + kKmax * 2;                           // 2 x kDmax f32
-    static constexpr int lnp = xs + 2 * kDmax * 4;                       // [2][g|b][kDmax] f32
-    static constexpr int kvbuf = lnp + 4 * kDmax * 4;                    // [page][K|V][64][64] bf16
-    static constexpr int kvbuf_bytes = kGroupPages * 2 * kPageTokens * kHeadDim * 2;
-    static constexpr int part = kvbuf + kvbuf_bytes;                     // 2 x partial MMA sums
-    static constexpr int part_ints = kConsumerWarps * kMaxTilesPerChunk * 3 * 8;
-    static constexpr int misc = part + 2 * part_ints * 4;
-    static constexpr int misc_floats = 64 + 64 + 64 * kGroupPages + 4 * 64 * kGroupPages + 96 + 32 + kMaxPages + 8;
-    static constexpr int bars = (misc + misc_floats * 4 + 15) & ~15;
-    static constexpr int total = bars + 2 * kStages * 8 + 16;
+    static constexpr int kvst = ring + kSlots * kSlotBytes;              // staged K | V (32 KB)
+    static constexpr int kvst_bytes = 2 * kStageKeys * kHalfDim * 2;
+    static constexpr int ps = kvst + kvst_bytes;                         // [2][kMaxCtx] f32
+    static constexpr int lnp = ps + 2 * kMaxCtx * 4;                     // [2][g|b][kDmax] f32
+    static constexpr int part = lnp + 4 * kDmax * 4;                     // [8][96][4] int32
+    static constexpr int part_rows = 96;
+    static constexpr int xs = part + kConsumerWarps * part_rows * 4 * 4; // [kDmax] f32 residual
+    static constexpr int limbs = xs + kDmax * 4;                         // [4][kLimbStride] int8
+    static constexpr int misc = limbs + kLimbs * kLimbStride;
+    static constexpr int misc_bytes = 2048;
+    static constexpr int bars = misc + misc_bytes;
+    static constexpr int total = bars + (2 * kSlots + 2) * 8;
 };
 static_assert(SmemMap::total <= 227 * 1024, "shared memory budget");
+static_assert(kChunkKeys * kHalfDim * 2 <= SmemMap::kvst_bytes, "key chunk fits the staging area");
+static_assert(kSliceTilesPerChunk * kFragBytes <= kSlotBytes, "slice chunk fits a slot");
+static_assert(kTile * kDmax + kTile * 8 <= kSlotBytes, "row chunk fits a slot");
+
+// limb column of the K-split GEMV inputs (attention context dims / fc1 rows)
+constexpr int kSlimbOff = 1024;
+
+extern __shared__ __align__(1024) uint8_t dsmem[];
 
 struct Cta {
     uint8_t *ring;
-    int8_t *limbs;
-    uint16_t *act;              // GEMV input vector (bf16) / gather buffer (32-bit words)
-    float *xs;                  // residual stream, double buffered: xs[0..kDmax), xs[kDmax..)
-    float *lnp;                 // LayerNorm parameters: [buf][0 = gamma, 1 = beta][kDmax]
-    uint16_t *kvbuf;            // [kGroupPages][2][64][64] bf16: K rows then V rows per page (also a gather buffer)
-    int *part;                  // [2][warps][tiles][3][8] partial limb sums
-    float *red, *qf, *sc, *accp, *pst;   // pst: per-page (m, l)
-    uint32_t *qkvw;             // 96 words: q, k, v of one head
-    int *flag;                  // [0] abort flag, [1] greedy id
-    int *pt;                    // page table copy
-    uint64_t *full, *empty;
+    uint16_t *kst, *vst;        // staged K rows (64 B, 16-byte chunks swizzled by row & 3), V rows
+    float *ps;                  // [2][kMaxCtx]: the pair's partial scores, then probabilities
+    float *lnp;                 // [2 buffers][gamma | beta][kDmax]
+    int *part;                  // [warp][row][limb] partial limb sums
+    float *x;                   // residual stream
+    int8_t *limbs;              // [limb][kLimbStride]
+    float *qf;                  // [32] q of the own dims (bf16 values)
+    uint16_t *kcur, *vcur;      // [32] k, v of the current position (kcur swizzled like kst)
+    float *red;                 // [64] reductions
+    float *accg;                // [8][32] P.V group partials
+    unsigned long long *keys;   // [8] argmax keys
+    int *pt;                    // [kMaxPages] page table
+    int *flag;                  // [0] abort, [1] next token id
+    uint64_t *full, *empty, *xchg;
     int tid, warp, lane;
 };
 
-// the kernels' dynamic shared memory; out-of-line helpers rebuild their Cta view from it
-extern __shared__ __align__(1024) uint8_t dsmem[];
-
-__device__ __forceinline__ Cta make_cta(uint8_t *smem = dsmem) {
+__device__ __forceinline__ Cta make_cta() {
+    uint8_t *s = dsmem;
     Cta S;
-    S.ring = smem + SmemMap::ring;
-    S.limbs = reinterpret_cast<int8_t *>(smem + SmemMap::limbs);
-    S.act = reinterpret_cast<uint16_t *>(smem + SmemMap::act);
-    S.xs = reinterpret_cast<float *>(smem + SmemMap::xs);
-    S.lnp = reinterpret_cast<float *>(smem + SmemMap::lnp);
-    S.kvbuf = reinterpret_cast<uint16_t *>(smem + SmemMap::kvbuf);
-    S.part = reinterpret_cast<int *>(smem + SmemMap::part);
-    float *m = reinterpret_cast<float *>(smem + SmemMap::misc);
-    S.red = m;
-    S.qf = m + 64;
-    S.sc = m + 128;                                   // [kGroupPages][64]
-    S.accp = S.sc + 64 * kGroupPages;                 // [kGroupPages][4][64]
-    S.qkvw = reinterpret_cast<uint32_t *>(S.accp + 256 * kGroupPages);
-    S.flag = reinterpret_cast<int *>(S.qkvw + 96);
-    S.pt = S.flag + 32;
-    S.pst = reinterpret_cast<float *>(S.pt + kMaxPages);
-    S.full = reinterpret_cast<uint64_t *>(smem + SmemMap::bars);
-    S.empty = S.full + kStages;
+    S.ring = s + SmemMap::ring;
+    S.kst = reinterpret_cast<uint16_t *>(s + SmemMap::kvst);
+    S.vst = S.kst + kStageKeys * kHalfDim;
+    S.ps = reinterpret_cast<float *>(s + SmemMap::ps);
+    S.lnp = reinterpret_cast<float *>(s + SmemMap::lnp);
+    S.part = reinterpret_cast<int *>(s + SmemMap::part);
+    S.x = reinterpret_cast<float *>(s + SmemMap::xs);
+    S.limbs = reinterpret_cast<int8_t *>(s + SmemMap::limbs);
+    uint8_t *m = s + SmemMap::misc;
+    S.qf = reinterpret_cast<float *>(m);                          // 128 B
+    S.kcur = reinterpret_cast<uint16_t *>(m + 128);               // 64 B
+    S.vcur = reinterpret_cast<uint16_t *>(m + 192);               // 64 B
+    S.red = reinterpret_cast<float *>(m + 256);                   // 256 B
+    S.accg = reinterpret_cast<float *>(m + 512);                  // 1024 B
+    S.keys = reinterpret_cast<unsigned long long *>(m + 1536);    // 64 B
+    S.pt = reinterpret_cast<int *>(m + 1600);                     // 128 B
+    S.flag = reinterpret_cast<int *>(m + 1728);                   // 32 B
+    S.full = reinterpret_cast<uint64_t *>(s + SmemMap::bars);
+    S.empty = S.full + kSlots;
+    S.xchg = S.empty + kSlots;
     S.tid = threadIdx.x;
     S.warp = threadIdx.x >> 5;
     S.lane = threadIdx.x & 31;
     return S;
 }
 
+// ------------------------------------------------------------------ small PTX helpers
 __device__ __forceinline__ void cbar() { named_bar(1, kConsumerThreads); }
+// consumer barrier that also ORs a predicate over the 256 consumer threads (uniform result)
+__device__ __forceinline__ bool cbar_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ uint32_t mapa_peer(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_async_b32(uint32_t raddr, uint32_t v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+                 "r"(v), "r"(rbar)
+                 : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t *bar, uint32_t cnt) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(cnt) : "memory");
+}
+__device__ __forceinline__ void red_add_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 // ------------------------------------------------------------------------- error handling
 __device__ __forceinline__ uint32_t read_error(const RunState *st) {
@@ -114,15 +175,12 @@ __device__ __noinline__ void set_error_st(RunState *st, uint32_t code, uint32_t 
         st->error_where = where;
     }
 }
-#define set_error(p, code, where) set_error_st((p).state, (code), (where))
-// Slow path of every bounded wait, called every few dozen polls: returns true when the
-// waiter must give up -- another CTA already failed, or the deadline (counted from the
-// first call, *t0) passed, in which case this CTA records the timeout.  Either way the
-// CTA's shared abort flag is raised, so every consumer thread leaves at the next phase
-// boundary without another global read.
-__device__ __noinline__ bool wait_expired_st(RunState *st, uint64_t timeout_ns, int *sflag,
-                                             uint64_t *t0, uint32_t code, uint32_t where) {
-    if (read_error(st) != 0) { *(volatile int *)sflag = 1; return true; }
+// Slow path of every bounded wait, called every few dozen polls: true when the waiter must
+// give up -- the CTA's abort flag is up, another CTA already failed, or the deadline (counted
+// from the first call, *t0) passed, in which case this CTA records the timeout.
+__device__ __noinline__ bool wait_expired(RunState *st, uint64_t timeout_ns, int *sflag, uint64_t *t0,
+                                          uint32_t code, uint32_t where) {
+    if (*(volatile int *)sflag != 0 || read_error(st) != 0) { *(volatile int *)sflag = 1; return true; }
     const uint64_t now = globaltimer_ns();
     if (*t0 == 0) { *t0 = now; return false; }
     if (now - *t0 > timeout_ns) {
@@ -132,77 +190,40 @@ __device__ __noinline__ bool wait_expired_st(RunState *st, uint64_t timeout_ns, 
     }
     return false;
 }
-#define wait_expired(p, sflag, t0, code, where) \
-    wait_expired_st((p).state, (p).timeout_ns, (sflag), &(t0), (code), (where))
 
-__device__ __forceinline__ void wait_full(const DecodeParams &p, Cta &S, int slot, uint32_t parity,
-                                          uint32_t where) {
-    if (mbar_try_wait(&S.full[slot], parity)) return;
-    uint64_t t0 = 0;
-    while (!mbar_try_wait(&S.full[slot], parity))
-        if (wait_expired(p, S.flag, t0, ERR_TIMEOUT_FULL, where)) return;
-}
-
-// Poll n flag-tagged words [src, src+n) until they all carry `epoch`; store their data to
-// dst.  The words are spread over the warps in units of 4 per lane (at most 8 in flight
-// per lane), and a lane re-polls only its words still missing, with a short sleep between
-// rounds: 148 CTAs spinning on the same few L2 lines would otherwise saturate the L2 slices
-// that hold them.  The caller follows with a consumer barrier.
-// (out of line: one copy of the code, called by every phase, stays in the instruction cache)
-__device__ __forceinline__ void ll_gather_impl(RunState *state, uint64_t timeout_ns, const uint64_t *src,
-                                            uint32_t *dst, int n, uint32_t epoch, uint32_t where) {
-    Cta S = make_cta();
-    constexpr int B = 8;
-    const int nw = min(kConsumerWarps, (n + 32 * 4 - 1) / (32 * 4));
-    if (S.warp >= nw) return;
-    const int stride = nw * 32;
-    for (int base = 0; base < n; base += B * stride) {
-        uint64_t v[B];
-#pragma unroll
-        for (int j = 0; j < B; j++) {
-            const int i = base + S.tid + j * stride;
-            v[j] = i < n ? ll_load(src + i) : (static_cast<uint64_t>(epoch) << 32);
-        }
+// Wait for the chunk with stream index `ctr` to be in its ring slot; false on timeout /
+// abort.  Warp-collective (all 32 lanes call it and get the same answer): lane 0 polls, and
+// after success every lane observes the completed phase itself (acquire of the copy's data).
+__device__ __forceinline__ bool wait_full(const DecodeParams &p, Cta &S, uint32_t ctr, uint32_t where) {
+    const int slot = ctr % kSlots;
+    const uint32_t parity = (ctr / kSlots) & 1u;
+    bool ok = true;
+    if (S.lane == 0 && !mbar_try_wait(&S.full[slot], parity)) {
         uint64_t t0 = 0;
         uint32_t it = 0;
-        while (true) {
-            bool all = true;
-#pragma unroll
-            for (int j = 0; j < B; j++) all &= static_cast<uint32_t>(v[j] >> 32) == epoch;
-            if (all) break;
-            __nanosleep(32);
-#pragma unroll
-            for (int j = 0; j < B; j++) {
-                const int i = base + S.tid + j * stride;
-                if (i < n && static_cast<uint32_t>(v[j] >> 32) != epoch) v[j] = ll_load(src + i);
+        while (!mbar_try_wait(&S.full[slot], parity))
+            if ((++it & 15) == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FULL, where)) {
+                ok = false;
+                break;
             }
-            if ((++it & 63) == 0 && wait_expired_st(state, timeout_ns, S.flag, &t0, ERR_TIMEOUT_FLAG, where)) break;
-        }
-#pragma unroll
-        for (int j = 0; j < B; j++) {
-            const int i = base + S.tid + j * stride;
-            if (i < n) dst[i] = static_cast<uint32_t>(v[j]);
-        }
     }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok) (void)mbar_try_wait(&S.full[slot], parity);
+    return ok;
 }
-#define ll_gather(p, S, src, dst, n, epoch, where) \
-    ll_gather_impl((p).state, (p).timeout_ns, (src), (dst), (n), (epoch), (where))
-
-// uniform "should this CTA stop" decision among the consumer threads (shared flag only)
-__device__ __forceinline__ bool abort_check(Cta &S) {
-    cbar();
-    const bool stop = *(volatile int *)S.flag != 0;
-    cbar();
-    return stop;
+__device__ __forceinline__ const uint8_t *slot_ptr(const Cta &S, uint32_t ctr) {
+    return S.ring + (ctr % kSlots) * kSlotBytes;
+}
+// the consumer warps release a slot: one arrival per warp
+__device__ __forceinline__ void release_slot(Cta &S, uint32_t ctr) {
+    __syncwarp();
+    if (S.lane == 0) mbar_arrive(&S.empty[ctr % kSlots]);
 }
 
-// optional phase timestamps: slot 0 token start, 1 + 5l + phase after each phase's publish,
-// 5L + 1 after the LM head, 5L + 2 after the greedy id is known
+// optional phase timestamps (first two steps of a launch)
 __device__ __forceinline__ void stamp(const DecodeParams &p, const Cta &S, int t, int slot) {
     if (p.timing == nullptr || t >= 2 || S.tid != 0) return;
-    p.timing[((size_t)t * p.grid + blockIdx.x) * 128 + slot] = globaltimer_ns();
-    if (slot == 0 || slot == 5 * p.n_layers + 2)
-        p.timing[((size_t)t * p.grid + blockIdx.x) * 128 + 120 + (slot != 0)] = clock64();
+    p.timing[((size_t)t * p.grid + blockIdx.x) * 64 + slot] = globaltimer_ns();
 }
 
 // e^x for x <= 0 with the reference's own 2^floor x degree-5 polynomial
@@ -229,7 +250,6 @@ __device__ __forceinline__ float warp_sum(float v) {
     for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
-// max is order-free, so the single-instruction warp reductions give the butterfly's value
 __device__ __forceinline__ float warp_max(float v) {
     float r;
     asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
@@ -239,445 +259,419 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ float warp_max_nonneg(float v) {
     return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
 }
-
-// 22-bit fixed-point exponent for a vector whose max |x| is m: X = rint(x * 2^s), |X| < 2^22
-__device__ __forceinline__ int limb_exponent(float m) {
-    const int E = m >= 0x1p-100f ? (int)((__float_as_uint(m) >> 23) & 0xff) - 126 : 0;   // m < 2^E
-    return 22 - E;
-}
-// write the three int8 limbs of element i = lane + 32*kb: logical byte i of each limb row,
-// 32-byte block kb of row j stored at block kb ^ j (bank-conflict-free MMA fragment loads)
-__device__ __forceinline__ void put_limbs(int8_t *limbs, int kb, int lane, float x, float sc) {
-    const int X = __float2int_rn(x * sc);
-    const int c = ((X + 128) & 255) - 128;
-    const int X1 = (X - c) >> 8;
-    const int b = ((X1 + 128) & 255) - 128;
-    const int a = (X1 - b) >> 8;
-    limbs[0 * kKmax + ((kb ^ 0) << 5) + lane] = (int8_t)a;
-    limbs[1 * kKmax + ((kb ^ 1) << 5) + lane] = (int8_t)b;
-    limbs[2 * kKmax + ((kb ^ 2) << 5) + lane] = (int8_t)c;
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = w > v ? w : v;
+    }
+    return v;
 }
 
-// Residual add + LayerNorm + limbs, fused: x_new = x_old (+ add), h = bf16(LN(x_new))
-// (rust/npu-asr-host/src/lib.rs:79-110: population variance, (x - mean) * inv * g + b, each
-// op rounded), then the limbs of h.  Thread (warp w, lane l) owns elements 32*(w + 8j) + l;
-// sums run over the thread's elements in j order, then the warp's xor butterfly, then the 8
-// warp totals in warp order (the CPU oracle replays exactly this tree).  Three consumer
-// barriers; returns the fixed-point exponent s.  The caller ends with a consumer barrier.
+// ---------------------------------------------------------------- fixed point and limbs
+// exponent s so that |x| * 2^s < 2^29 for max |x| = m (s = 29 when m < 2^-96)
+__device__ __forceinline__ int fix_exponent(float m) {
+    const int E = m >= 0x1p-96f ? (int)((__float_as_uint(m) >> 23) & 0xff) - 126 : 0;   // m < 2^E
+    return kFixBits - E;
+}
+// X = rint(x * 2^s) clamped to +-(2^30 - 64), split into four int8 limbs at column k
+__device__ __forceinline__ void put_limbs4(int8_t *L, int k, float x, float sc) {
+    float v = __fmul_rn(x, sc);
+    v = fminf(fmaxf(v, -1073741760.0f), 1073741760.0f);
+    const int X = __float2int_rn(v);
+    const int d = ((X + 128) & 255) - 128;
+    const int X1 = (X - d) >> 8;
+    const int c = ((X1 + 128) & 255) - 128;
+    const int X2 = (X1 - c) >> 8;
+    const int b = ((X2 + 128) & 255) - 128;
+    const int a = (X2 - b) >> 8;
+    L[0 * kLimbStride + k] = (int8_t)a;
+    L[1 * kLimbStride + k] = (int8_t)b;
+    L[2 * kLimbStride + k] = (int8_t)c;
+    L[3 * kLimbStride + k] = (int8_t)d;
+}
+// B fragment (32 k x 8 columns; columns 0..3 = limbs) of k-block kb at limb column base
+__device__ __forceinline__ void load_bfrag(const int8_t *L, int base, int kb, int lane, uint32_t &b0, uint32_t &b1) {
+    const int g = lane >> 2, tig = lane & 3;
+    if (g < kLimbs) {
+        const int8_t *r = L + g * kLimbStride + base + kb * 32 + tig * 4;
+        b0 = *reinterpret_cast<const uint32_t *>(r);
+        b1 = *reinterpret_cast<const uint32_t *>(r + 16);
+    } else {
+        b0 = b1 = 0u;
+    }
+}
+// exact dot of the four limb columns: ((a * 256 + b) * 256 + c) * 256 + d
+__device__ __forceinline__ long long limb_dot(int a, int b, int c, int d) {
+    return (((long long)a * 256 + b) * 256 + c) * 256 + d;
+}
+
+// LayerNorm of the full D-vector x by ONE warp (every warp computes it; no block barrier),
+// the formula of rust/npu-asr-host/src/lib.rs:79-110 (population variance, each op rounded)
+// with this tree: lane l sums elements l + 32j in j order, then the xor butterfly.  Output
+// rounded to bf16; the warp writes the limbs of its 32-wide blocks [kb0, kb1) (fixed point
+// from the max over the whole output) and, if `out` is given, those outputs; returns the
+// exponent.
 template <int D>
-__device__ __forceinline__ int resid_ln_limbs_impl(const float *xo, float *xn, const uint32_t *add,
-                                               const float *g, const float *b, float eps) {
-    Cta S = make_cta();
-    constexpr int PER = D / kConsumerThreads;
-    static_assert(D % kConsumerThreads == 0, "d_model must be a multiple of 256");
-    float xv[PER];
-    float sum = 0.0f;
+__device__ __forceinline__ int ln_limbs(const float *x, const float *g, const float *b, float eps, int8_t *L,
+                                        int lane, int kb0, int kb1, float *out = nullptr) {
+    constexpr int J = D / 32;
+    float v[J];
+    float s = 0.0f;
 #pragma unroll
-    for (int j = 0; j < PER; j++) {
-        const int i = 32 * (S.warp + 8 * j) + S.lane;
-        float x = xo[i];
-        if (add) { x = __fadd_rn(x, __uint_as_float(add[i])); xn[i] = x; }
-        xv[j] = x;
-        sum = __fadd_rn(sum, x);
+    for (int j = 0; j < J; j++) {
+        v[j] = x[lane + 32 * j];
+        s = __fadd_rn(s, v[j]);
     }
-    sum = warp_sum(sum);
-    if (S.lane == 0) S.red[S.warp] = sum;
-    cbar();
-    sum = 0.0f;
+    const float mean = __fdiv_rn(warp_sum(s), (float)D);
+    float q = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) sum = __fadd_rn(sum, S.red[w]);
-    const float mean = __fdiv_rn(sum, (float)D);
-    float var = 0.0f;
-#pragma unroll
-    for (int j = 0; j < PER; j++) {
-        const float c = __fsub_rn(xv[j], mean);
-        var = __fadd_rn(var, __fmul_rn(c, c));
+    for (int j = 0; j < J; j++) {
+        const float c = __fsub_rn(v[j], mean);
+        q = __fadd_rn(q, __fmul_rn(c, c));
     }
-    var = warp_sum(var);
-    if (S.lane == 0) S.red[8 + S.warp] = var;
-    cbar();
-    var = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) var = __fadd_rn(var, S.red[8 + w]);
-    var = __fdiv_rn(var, (float)D);
+    const float var = __fdiv_rn(warp_sum(q), (float)D);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
     float m = 0.0f;
 #pragma unroll
-    for (int j = 0; j < PER; j++) {
-        const int i = 32 * (S.warp + 8 * j) + S.lane;
-        const float t = __fmul_rn(__fsub_rn(xv[j], mean), inv);
-        xv[j] = bf16r(__fadd_rn(__fmul_rn(t, g[i]), b[i]));
-        m = fmaxf(m, fabsf(xv[j]));
-    }
-    m = warp_max_nonneg(m);
-    if (S.lane == 0) S.red[16 + S.warp] = m;
-    cbar();
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) m = fmaxf(m, S.red[16 + w]);
-    const int s = limb_exponent(m);
-    const float sc = exp2i(s);
-#pragma unroll
-    for (int j = 0; j < PER; j++) put_limbs(S.limbs, S.warp + 8 * j, S.lane, xv[j], sc);
-    return s;
-}
-
-template <int D>
-__device__ __forceinline__ int resid_ln_limbs(Cta &, const float *xo, float *xn, const uint32_t *add,
-                                              const float *g, const float *b, float eps) {
-    return resid_ln_limbs_impl<D>(xo, xn, add, g, b, eps);
-}
-
-// Limbs of a length-K vector already in shared memory (bf16 or f32), same ownership as
-// resid_ln_limbs.  One consumer barrier; the caller ends with another.
-template <int K, class Load>
-__device__ __forceinline__ int limbs_of(Cta &S, Load ld) {
-    constexpr int PER = K / kConsumerThreads;
-    static_assert(K % kConsumerThreads == 0, "length must be a multiple of 256");
-    float v[PER];
-    float m = 0.0f;
-#pragma unroll
-    for (int j = 0; j < PER; j++) {
-        v[j] = ld(32 * (S.warp + 8 * j) + S.lane);
+    for (int j = 0; j < J; j++) {
+        const int i = lane + 32 * j;
+        const float t = __fmul_rn(__fsub_rn(v[j], mean), inv);
+        v[j] = bf16r(__fadd_rn(__fmul_rn(t, g[i]), b[i]));
         m = fmaxf(m, fabsf(v[j]));
     }
-    m = warp_max_nonneg(m);
-    if (S.lane == 0) S.red[24 + S.warp] = m;
-    cbar();
+    const int e = fix_exponent(warp_max_nonneg(m));
+    const float sc = exp2i(e);
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) m = fmaxf(m, S.red[24 + w]);
-    const int s = limb_exponent(m);
-    const float sc = exp2i(s);
-#pragma unroll
-    for (int j = 0; j < PER; j++) put_limbs(S.limbs, S.warp + 8 * j, S.lane, v[j], sc);
-    return s;
+    for (int j = 0; j < J; j++) {
+        if (j >= kb0 && j < kb1) {
+            put_limbs4(L, lane + 32 * j, v[j], sc);
+            if (out) out[lane + 32 * j] = v[j];
+        }
+    }
+    __syncwarp();
+    return e;
 }
 
-// limbs of the bf16 vector in S.act[0..K) (out of line)
-template <int K>
-__device__ __forceinline__ int limbs_of_act() {
-    Cta S = make_cta();
-    return limbs_of<K>(S, [&](int i) { return __uint_as_float((uint32_t)S.act[i] << 16); });
-}
-
-__device__ __forceinline__ void gemv_partials(const uint8_t *stage, int rows, int K, int pb) {
-    Cta S = make_cta();
+// ------------------------------------------------------------------------------ GEMVs
+// K-split row-tile GEMV: nt m-tiles (chunks ctr .. ctr+nt-1, one 16-row tile each, K = 32 *
+// 8 * KBW) against the limbs at column 0; warp w covers k-blocks [w*KBW, (w+1)*KBW).  Partial
+// limb sums go to S.part[warp][row][limb]; the caller combines them after a consumer
+// barrier.  The slots stay owned (their meta is read by the combine) until release_tiles.
+template <int KBW>
+__device__ __forceinline__ bool rowtile_mma(const DecodeParams &p, Cta &S, uint32_t ctr, int nt, uint32_t where) {
     const int g = S.lane >> 2, tig = S.lane & 3;
-    const int ntiles = rows >> 3;
-    const int KS = K >> 5;
-    const int kb0 = S.warp * KS / kConsumerWarps, kb1 = (S.warp + 1) * KS / kConsumerWarps;
-    int acc[kMaxTilesPerChunk][4];
+    uint32_t bf[KBW][2];
 #pragma unroll
-    for (int t = 0; t < kMaxTilesPerChunk; t++) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
-    const int8_t *arow = S.limbs + (g < 3 ? g : 0) * kKmax;
-#pragma unroll 4
-    for (int kb = kb0; kb < kb1; kb++) {
-        uint2 av = make_uint2(0u, 0u);
-        if (g < 3) av = *reinterpret_cast<const uint2 *>(arow + ((kb ^ g) << 5) + tig * 8);
+    for (int kk = 0; kk < KBW; kk++) load_bfrag(S.limbs, 0, S.warp * KBW + kk, S.lane, bf[kk][0], bf[kk][1]);
+    for (int t = 0; t < nt; t++) {
+        if (!wait_full(p, S, ctr + t, where)) return false;
+        const uint8_t *ch = slot_ptr(S, ctr + t);
+        int acc[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int t = 0; t < kMaxTilesPerChunk; t++) {
-            if (t < ntiles) {
-                const uint8_t *br = stage + (size_t)(t * 8 + g) * K;
-                uint2 bv = *reinterpret_cast<const uint2 *>(br + ((kb ^ (g & 3)) << 5) + tig * 8);
-                mma_s8_16832(acc[t], av.x, 0u, av.y, 0u, bv.x, bv.y);
-            }
+        for (int kk = 0; kk < KBW; kk++) {
+            const uint4 a = *reinterpret_cast<const uint4 *>(ch + (S.warp * KBW + kk) * kFragBytes + S.lane * 16);
+            mma_s8_16832(acc, a.x, a.y, a.z, a.w, bf[kk][0], bf[kk][1]);
+        }
+        if (tig < 2) {
+            int *pp = S.part + ((S.warp * SmemMap::part_rows + t * kTile + g) * 4 + tig * 2);
+            *reinterpret_cast<int2 *>(pp) = make_int2(acc[0], acc[1]);
+            *reinterpret_cast<int2 *>(pp + 8 * 4) = make_int2(acc[2], acc[3]);
         }
     }
-    int *part = S.part + pb * SmemMap::part_ints;
-    if (g < 3) {
-#pragma unroll
-        for (int t = 0; t < kMaxTilesPerChunk; t++) {
-            if (t < ntiles) {
-                int *pp = part + ((S.warp * kMaxTilesPerChunk + t) * 3 + g) * 8 + 2 * tig;
-                pp[0] = acc[t][0];
-                pp[1] = acc[t][1];
-            }
-        }
-    }
+    return true;
 }
-
-// output row r of a chunk: float(exact dot) * 2^-s * scale + bias
-__device__ __forceinline__ float gemv_row(const uint8_t *stage, int rows, int K, int s, int pb, int r) {
-    const int *part = reinterpret_cast<const int *>(dsmem + SmemMap::part) + pb * SmemMap::part_ints;
-    const float *meta = reinterpret_cast<const float *>(stage + (size_t)rows * K);
-    const int t = r >> 3, col = r & 7;
-    long long A = 0, B = 0, C = 0;
+// exact output row r of the K-split row-tile GEMV: float(sum) * 2^-s * scale + bias
+__device__ __forceinline__ float rowtile_out(const Cta &S, uint32_t ctr, int r, int K, int s) {
+    int a = 0, b = 0, c = 0, d = 0;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; w++) {
-        const int *pp = part + ((w * kMaxTilesPerChunk + t) * 3) * 8 + col;
-        A += pp[0];
-        B += pp[8];
-        C += pp[16];
+        const int4 v = *reinterpret_cast<const int4 *>(S.part + (w * SmemMap::part_rows + r) * 4);
+        a += v.x; b += v.y; c += v.z; d += v.w;
     }
-    const float y = __fmul_rn(__ll2float_rn(A * 65536 + B * 256 + C), exp2i(-s));
-    return __fadd_rn(__fmul_rn(y, meta[2 * r]), meta[2 * r + 1]);
+    const float *meta = reinterpret_cast<const float *>(slot_ptr(S, ctr + r / kTile) + kTile * K);
+    const float y = __fmul_rn(__ll2float_rn(limb_dot(a, b, c, d)), exp2i(-s));
+    return __fadd_rn(__fmul_rn(y, meta[2 * (r % kTile)]), meta[2 * (r % kTile) + 1]);
+}
+__device__ __forceinline__ void release_tiles(Cta &S, uint32_t ctr, int nt) {
+    __syncwarp();
+    if (S.lane == 0)
+        for (int t = 0; t < nt; t++) mbar_arrive(&S.empty[(ctr + t) % kSlots]);
 }
 
-// One weight chunk: rows (multiple of 8) x K int8 (row r swizzled by r & 3) followed by
-// rows x (f32 scale, f32 bias).  Warps split K; their int32 limb partials meet in S.part
-// (double buffered by `pb`, so one barrier per chunk suffices); then each output
-// y = float(exact dot) * 2^-s * scale + bias goes to epi(row, y) -- or, with PAIR, rows
-// 2j and 2j+1 go together to epi(2j, y0, y1) from one thread.
-template <bool PAIR, class Epi>
-__device__ __forceinline__ void gemv_chunk(Cta &S, const uint8_t *stage, int rows, int K, int s, int pb,
-                                           Epi epi) {
-    gemv_partials(stage, rows, K, pb);
-    cbar();
-    if (PAIR) {
-        if (S.tid < (rows >> 1))
-            epi(2 * S.tid, gemv_row(stage, rows, K, s, pb, 2 * S.tid), gemv_row(stage, rows, K, s, pb, 2 * S.tid + 1));
-    } else {
-        if (S.tid < rows) epi(S.tid, gemv_row(stage, rows, K, s, pb, S.tid), 0.0f);
+// K-split slice GEMV with integer accumulation across CTAs: for each of nkb k-blocks (limb
+// columns kSlimbOff + 32 kb), the slice chunks of D outputs; warp w owns the m-tiles w, w+8, ...
+// Each output's exact partial is added as (partial + 2^bshift + 2^56) into words[n].
+template <int D>
+__device__ __forceinline__ bool slice_mma_red(const DecodeParams &p, Cta &S, uint32_t &ctr, int nkb,
+                                              unsigned long long *words, int bshift, uint32_t where) {
+    constexpr int NT = D / kTile / kConsumerWarps;       // m-tiles per warp
+    const int nch = slice_chunks(D);
+    int acc[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0;
+    for (int kb = 0; kb < nkb; kb++) {
+        uint32_t b0, b1;
+        load_bfrag(S.limbs, kSlimbOff, kb, S.lane, b0, b1);
+        for (int c = 0; c < nch; c++) {
+            if (!wait_full(p, S, ctr, where)) return false;
+            const uint8_t *ch = slot_ptr(S, ctr);
+#pragma unroll
+            for (int i = 0; i < NT; i++) {
+                const int tile = S.warp + kConsumerWarps * i;
+                if (tile / kSliceTilesPerChunk == c) {
+                    const uint4 a = *reinterpret_cast<const uint4 *>(
+                        ch + (tile % kSliceTilesPerChunk) * kFragBytes + S.lane * 16);
+                    mma_s8_16832(acc[i], a.x, a.y, a.z, a.w, b0, b1);
+                }
+            }
+            release_slot(S, ctr);
+            ctr++;
+        }
     }
+    const int g = S.lane >> 2, tig = S.lane & 3;
+    const unsigned long long add = (1ull << bshift) + (1ull << kCountShift);
+#pragma unroll
+    for (int i = 0; i < NT; i++) {
+        const int tile = S.warp + kConsumerWarps * i;
+        const int x0 = __shfl_down_sync(0xffffffffu, acc[i][0], 1);
+        const int x1 = __shfl_down_sync(0xffffffffu, acc[i][1], 1);
+        const int x2 = __shfl_down_sync(0xffffffffu, acc[i][2], 1);
+        const int x3 = __shfl_down_sync(0xffffffffu, acc[i][3], 1);
+        if (tig == 0) {
+            const int n = tile * kTile + g;
+            red_add_u64(words + n, (unsigned long long)limb_dot(acc[i][0], acc[i][1], x0, x1) + add);
+            red_add_u64(words + n + 8, (unsigned long long)limb_dot(acc[i][2], acc[i][3], x2, x3) + add);
+        }
+    }
+    return true;
 }
 
-// Consume one phase's chunks from the ring (rows of reduction length K).
-template <bool PAIR, class Epi>
-__device__ __forceinline__ void gemv_phase(const DecodeParams &p, Cta &S, uint32_t &ctr, int rows, int K, int s,
-                           uint32_t where, Epi epi) {
-    const int rpc = rows_per_chunk(K);
-    for (int r0 = 0; r0 < rows; r0 += rpc) {
-        const int rr = min(rpc, rows - r0);
-        const int slot = ctr % kStages;
-        const uint32_t parity = (ctr / kStages) & 1u;
-        wait_full(p, S, slot, parity, where);
-        gemv_chunk<PAIR>(S, S.ring + slot * kStageBytes, rr, K, s, (int)(ctr & 1u),
-                         [&](int r, float y0, float y1) { epi(r0 + r, y0, y1); });
-        __syncwarp();
-        if (S.lane == 0) mbar_arrive(&S.empty[slot]);
-        ctr++;
+// Read the D accumulator words of one exchange (complete when their count is `cnt`) and add
+// the decoded values into the residual: x[n] += float(Y) * 2^-fix * scale[n] + bias[n].
+// Thread t owns n = t + 256 i.  Returns false on timeout / abort.  The caller follows with a
+// barrier.
+template <int D>
+__device__ __forceinline__ bool gather_acc(const DecodeParams &p, Cta &S, const unsigned long long *words, int cnt,
+                                           int bshift, int fix, const float *sb, uint32_t where) {
+    constexpr int PER = D / kConsumerThreads;
+    float sc[PER], bi[PER];
+    unsigned long long v[PER];
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int n = S.tid + kConsumerThreads * i;
+        sc[i] = sb[n];
+        bi[i] = sb[D + n];
+        v[i] = ld_relaxed_u64(words + n);
     }
+    const unsigned want = (unsigned)cnt;
+    uint64_t t0 = 0;
+    uint32_t it = 0;
+    bool ok = true;
+    while (true) {
+        bool all = true;
+#pragma unroll
+        for (int i = 0; i < PER; i++) all &= (unsigned)(v[i] >> kCountShift) == want;
+        if (all) break;
+        __nanosleep(20);
+#pragma unroll
+        for (int i = 0; i < PER; i++)
+            if ((unsigned)(v[i] >> kCountShift) != want) v[i] = ld_relaxed_u64(words + S.tid + kConsumerThreads * i);
+        if ((++it & 31) == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FLAG, where)) {
+            ok = false;
+            break;
+        }
+    }
+    const long long off = (long long)cnt << bshift;
+    const float inv = exp2i(-fix);
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int n = S.tid + kConsumerThreads * i;
+        const long long Y = (long long)(v[i] & ((1ull << kCountShift) - 1)) - off;
+        const float val = __fadd_rn(__fmul_rn(__fmul_rn(__ll2float_rn(Y), inv), sc[i]), bi[i]);
+        S.x[n] = __fadd_rn(S.x[n], val);
+    }
+    return ok;
 }
 
 // ------------------------------------------------------------------------------ attention
-__device__ __forceinline__ size_t kv_index(const DecodeParams &p, int layer, int phys, int kv,
-                                           int head, int row) {
-    return ((((size_t)layer * p.n_phys_pages + phys) * 2 + kv) * p.n_heads + head) *
-               (size_t)(kPageTokens * kHeadDim) +
-           (size_t)row * kHeadDim;
+__device__ __forceinline__ size_t kv_index(const DecodeParams &p, int layer, int phys, int head, int half,
+                                           int kv, int row) {
+    return (((((size_t)layer * p.n_phys_pages + phys) * p.n_heads + head) * 2 + half) * 2 + kv) *
+               (size_t)(kPageTokens * kHalfDim) +
+           (size_t)row * kHalfDim;
 }
-
-// cp.async the cached rows [j0, min(pos, j0 + 64 * kGroupPages)) of (layer, head) into
-// kvbuf, j0 = first position of the item's page group.
-__device__ __forceinline__ void kv_prefetch(const DecodeParams &p, Cta &S, int layer, int item, int pos) {
-    const int H = p.n_heads;
-    const int grp = item / H, h = item % H;
-    const int j0 = grp * kGroupPages * kPageTokens;
-    const int nrows = min(pos, j0 + kGroupPages * kPageTokens) - j0;   // cached rows (current pos excluded)
-    for (int c = S.tid; c < nrows * 16; c += kConsumerThreads) {
-        const int row = c >> 4, kv = (c >> 3) & 1, part = c & 7;
-        const int pl = row / kPageTokens, r = row % kPageTokens;
-        const int phys = S.pt[grp * kGroupPages + pl];
-        const uint16_t *src = p.kv + kv_index(p, layer, phys, kv, h, r) + part * 8;
-        // K rows keep their 16-byte chunk c at c ^ (row & 7): the score loop reads one row per
-        // lane, and the swizzle spreads a quarter-warp's reads over all banks
-        const int pc = kv ? part : part ^ (r & 7);
-        uint16_t *dst = S.kvbuf + ((pl * 2 + kv) * kPageTokens + r) * kHeadDim + pc * 8;
-        cp_async16(dst, src);
+// cp.async rows [j0, j1) of this CTA's K (kv = 0) or V (kv = 1) dims to dst (row j at
+// j - j0; K rows keep 16-byte chunk c at c ^ (j & 3) so the one-key-per-thread score loop is
+// bank-conflict free); no commit
+__device__ __forceinline__ void kv_stage(const DecodeParams &p, Cta &S, int layer, int head, int half, int kv,
+                                         int j0, int j1, uint16_t *dst) {
+    for (int c = S.tid; c < (j1 - j0) * 4; c += kConsumerThreads) {
+        const int j = j0 + (c >> 2), part = c & 3;
+        const uint16_t *src =
+            p.kv + kv_index(p, layer, S.pt[j / kPageTokens], head, half, kv, j % kPageTokens) + part * 8;
+        const int pc = kv ? part : part ^ (j & 3);
+        cp_async16(dst + (size_t)(j - j0) * kHalfDim + pc * 8, src);
     }
-    cp_async_commit();
+}
+// partial score of key j over the own 32 dims: 4 chains of 8 dims (fma, d ascending),
+// combined as (c0 + c1) + (c2 + c3); krow = the key's 64-byte row (chunks swizzled by j & 3)
+__device__ __forceinline__ float part_score(const float *qf, const uint16_t *krow, int j) {
+    const uint4 *kr = reinterpret_cast<const uint4 *>(krow);
+    const float4 *q4 = reinterpret_cast<const float4 *>(qf);
+    float c[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint4 w = kr[i ^ (j & 3)];
+        const float4 qa = q4[2 * i], qb = q4[2 * i + 1];
+        float a = 0.0f;
+        a = fmaf(qa.x, bf16lo(w.x), a);
+        a = fmaf(qa.y, bf16hi(w.x), a);
+        a = fmaf(qa.z, bf16lo(w.y), a);
+        a = fmaf(qa.w, bf16hi(w.y), a);
+        a = fmaf(qb.x, bf16lo(w.z), a);
+        a = fmaf(qb.y, bf16hi(w.z), a);
+        a = fmaf(qb.z, bf16lo(w.w), a);
+        a = fmaf(qb.w, bf16hi(w.w), a);
+        c[i] = a;
+    }
+    return __fadd_rn(__fadd_rn(c[0], c[1]), __fadd_rn(c[2], c[3]));
 }
 
-// One (page group, head) item of single-query attention (mha_tile, mha_decode.cc:90-168, in
-// its split form).  Per page of the group: scores of the page's keys against q (already
-// * 1/sqrt(64) and bf16), the page max m, l = sum exp(s - m), acc = sum exp(s - m) v; the
-// page partials are then merged in page order (flash-decode merge).  With one group in the
-// context (`single`) the item publishes ctx = bf16(acc / l) of its head as 32 words at
-// ll_att[h*32..]; otherwise it publishes the group partial [m, l, acc[64]] at ll_att[item*66].
-__device__ __forceinline__ void att_item(const DecodeParams &p, Cta &S, int layer, int item, int pos,
-                         bool prefetched, bool single, uint32_t ep_qkv, uint32_t ep_att, int t) {
-    const int H = p.n_heads, D = p.d_model;
-    const int grp = item / H, h = item % H;
-    const int j0 = grp * kGroupPages * kPageTokens;
-    const int ntok = min(pos + 1, j0 + kGroupPages * kPageTokens) - j0;   // keys, current included
-    const int np = (ntok + kPageTokens - 1) / kPageTokens;
-    const bool has_cur = pos < j0 + kGroupPages * kPageTokens;
-    if (!prefetched) kv_prefetch(p, S, layer, item, pos);
-    // q, k, v of head h: words [part*D/2 + h*32, +32)
-    if (S.tid < 96) {
-        const int part = S.tid >> 5, wi = S.tid & 31;
-        const uint64_t *src = p.ll_qkv + part * (D / 2) + h * 32 + wi;
-        uint64_t v = ll_load(src);
+// One head pair's single-query attention over keys [0, pos] (mha_tile, mha_decode.cc:90-168,
+// with one softmax over the whole context): this CTA's partial scores go to the other CTA by
+// st.async; s_j = part_rank0 + part_rank1; M = max s; p_j = fast_exp(s_j - M); l = sum p
+// (thread t sums keys j = t mod 256 in order, then the butterfly, then the warps in order);
+// ctx_d = (sum over 8 key groups j = g mod 8, in group order, of fma chains) / l, bf16.  The
+// ctx limbs (fixed point 2^fix) land at limb column kSlimbOff + d.  `xu` counts the pair
+// exchanges of this launch (mbarrier buffer and parity).  Returns false on timeout / abort;
+// the caller follows with a barrier.
+__device__ __forceinline__ bool attention(const DecodeParams &p, Cta &S, int layer, int head, int half, int pos,
+                                       bool staged, uint32_t xu, int fix, int t) {
+    const int tk = pos + 1;
+    const int buf = xu & 1;
+    const uint32_t par = (xu >> 1) & 1u;
+    float *pbuf = S.ps + buf * kMaxCtx;
+    const uint32_t peer = (uint32_t)half ^ 1u;
+    const uint32_t rbuf = mapa_peer(pbuf, peer);
+    const uint32_t rbar = mapa_peer(&S.xchg[buf], peer);
+    constexpr int KPT = kMaxCtx / kConsumerThreads;       // keys per thread (8)
+    float own[KPT];
+    // ---- partial scores of the own dims, sent to the peer as they are made
+    if (staged) {
+#pragma unroll
+        for (int i = 0; i < KPT; i++) {
+            const int j = S.tid + kConsumerThreads * i;
+            own[i] = 0.0f;
+            if (j < tk) {
+                own[i] = part_score(S.qf, j < pos ? S.kst + j * kHalfDim : S.kcur, j);
+                st_async_b32(rbuf + 4u * j, __float_as_uint(own[i]), rbar);
+            }
+        }
+    } else {
+        uint16_t *kchunk = S.kst;                         // the whole staging area holds K rows
+#pragma unroll
+        for (int i = 0; i < KPT; i++) own[i] = 0.0f;
+        for (int j0 = 0; j0 < pos; j0 += kChunkKeys) {
+            const int j1 = min(pos, j0 + kChunkKeys);
+            cbar();                                       // previous chunk fully read
+            kv_stage(p, S, layer, head, half, 0, j0, j1, kchunk);
+            cp_async_commit();
+            cp_async_wait_all();
+            cbar();
+#pragma unroll
+            for (int i = 0; i < KPT; i++) {
+                const int j = S.tid + kConsumerThreads * i;
+                if (j >= j0 && j < j1) own[i] = part_score(S.qf, kchunk + (j - j0) * kHalfDim, j);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < KPT; i++) {
+            const int j = S.tid + kConsumerThreads * i;
+            if (j == pos) own[i] = part_score(S.qf, S.kcur, j);
+            if (j < tk) st_async_b32(rbuf + 4u * j, __float_as_uint(own[i]), rbar);
+        }
+    }
+    if (layer == 1) stamp(p, S, t, 53);
+    // ---- the peer's partials
+    bool ok = true;
+    if (!mbar_try_wait_cluster(&S.xchg[buf], par)) {
         uint64_t t0 = 0;
         uint32_t it = 0;
-        while (static_cast<uint32_t>(v >> 32) != ep_qkv) {
-            v = ll_load(src);
-            if ((++it & 63) == 0 && wait_expired(p, S.flag, t0, ERR_TIMEOUT_FLAG, 0x200u + layer)) break;
-            __nanosleep(32);
-        }
-        S.qkvw[S.tid] = static_cast<uint32_t>(v);
-    }
-    if (layer == 1) stamp(p, S, t, 86);
-    cp_async_wait_all();
-    cbar();
-    if (layer == 1) stamp(p, S, t, 80);
-    if (S.tid < 32) {
-        uint32_t w = S.qkvw[S.tid];
-        S.qf[2 * S.tid] = bf16lo(w);
-        S.qf[2 * S.tid + 1] = bf16hi(w);
-    }
-    if (has_cur && S.tid >= 32 && S.tid < 96) {
-        // append this position's K (tid 32..63) or V (tid 64..95) row: kvbuf and the cache
-        const int kv = (S.tid - 32) >> 5, wi = S.tid & 31, row = pos - j0;
-        const int pl = row / kPageTokens, r = row % kPageTokens;
-        const uint32_t w = S.qkvw[S.tid];
-        const int swi = kv ? wi : (wi ^ ((r & 7) << 2));    // K: chunk (wi / 4) ^ (row & 7)
-        reinterpret_cast<uint32_t *>(S.kvbuf + ((pl * 2 + kv) * kPageTokens + r) * kHeadDim)[swi] = w;
-        const int phys = S.pt[grp * kGroupPages + pl];
-        reinterpret_cast<uint32_t *>(p.kv + kv_index(p, layer, phys, kv, h, r))[wi] = w;
-    }
-    cbar();
-    // scores: one key per thread (thread k -> page k / 64, key k % 64), four chains of 16
-    // dims (d ascending) combined as (s0 + s1) + (s2 + s3)
-    if (S.tid < np * kPageTokens) {
-        const int pl = S.tid / kPageTokens, key = S.tid % kPageTokens;
-        const int nk = min(kPageTokens, ntok - pl * kPageTokens);
-        float sd = -INFINITY;
-        if (key < nk) {
-            const uint4 *kr = reinterpret_cast<const uint4 *>(S.kvbuf + ((pl * 2) * kPageTokens + key) * kHeadDim);
-            const float4 *q4p = reinterpret_cast<const float4 *>(S.qf);
-            float s4[4];
-#pragma unroll
-            for (int q4 = 0; q4 < 4; q4++) {
-                float acc = 0.0f;
-#pragma unroll
-                for (int half = 0; half < 2; half++) {
-                    const int c = 2 * q4 + half;
-                    const uint4 kv8 = kr[c ^ (key & 7)];
-                    const float4 qa = q4p[2 * c], qb = q4p[2 * c + 1];
-                    acc = fmaf(qa.x, bf16lo(kv8.x), acc);
-                    acc = fmaf(qa.y, bf16hi(kv8.x), acc);
-                    acc = fmaf(qa.z, bf16lo(kv8.y), acc);
-                    acc = fmaf(qa.w, bf16hi(kv8.y), acc);
-                    acc = fmaf(qb.x, bf16lo(kv8.z), acc);
-                    acc = fmaf(qb.y, bf16hi(kv8.z), acc);
-                    acc = fmaf(qb.z, bf16lo(kv8.w), acc);
-                    acc = fmaf(qb.w, bf16hi(kv8.w), acc);
-                }
-                s4[q4] = acc;
+        while (!mbar_try_wait_cluster(&S.xchg[buf], par))
+            if ((++it & 15) == 0 &&
+                wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_PEER, 0x500u + layer)) {
+                ok = false;
+                break;
             }
-            sd = __fadd_rn(__fadd_rn(s4[0], s4[1]), __fadd_rn(s4[2], s4[3]));
-        }
-        S.sc[pl * 64 + key] = sd;
     }
+    if (layer == 1) stamp(p, S, t, 54);
+    float s[KPT];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < KPT; i++) {
+        const int j = S.tid + kConsumerThreads * i;
+        s[i] = -INFINITY;
+        if (j < tk) {
+            const float pr = pbuf[j];
+            s[i] = half == 0 ? __fadd_rn(own[i], pr) : __fadd_rn(pr, own[i]);
+            m = fmaxf(m, s[i]);
+        }
+    }
+    m = warp_max(m);
+    if (S.lane == 0) S.red[S.warp] = m;
+    if (cbar_or(!ok)) return false;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) m = fmaxf(m, S.red[w]);
+    float l = 0.0f;
+#pragma unroll
+    for (int i = 0; i < KPT; i++) {
+        const int j = S.tid + kConsumerThreads * i;
+        if (j < tk) {
+            const float pj = fast_exp_nonpos(__fsub_rn(s[i], m));
+            pbuf[j] = pj;
+            l = __fadd_rn(l, pj);
+        }
+    }
+    l = warp_sum(l);
+    if (S.lane == 0) S.red[8 + S.warp] = l;
     cbar();
-    if (layer == 1) stamp(p, S, t, 84);
-    // page statistics: warp pl owns page pl; probabilities replace the scores in place
-    if (S.warp < np) {
-        const int pl = S.warp;
-        const int nk = min(kPageTokens, ntok - pl * kPageTokens);
-        float *sc = S.sc + pl * 64;
-        const float s0 = sc[S.lane], s1 = sc[S.lane + 32];
-        const float m = warp_max(fmaxf(s0, s1));
-        const float p0 = S.lane < nk ? fast_exp_nonpos(__fsub_rn(s0, m)) : 0.0f;
-        const float p1 = S.lane + 32 < nk ? fast_exp_nonpos(__fsub_rn(s1, m)) : 0.0f;
-        const float l = warp_sum(p0 + p1);
-        __syncwarp();
-        sc[S.lane] = p0;
-        sc[S.lane + 32] = p1;
-        if (S.lane == 0) { S.pst[2 * pl] = m; S.pst[2 * pl + 1] = l; }
+    l = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) l = __fadd_rn(l, S.red[8 + w]);
+    if (layer == 1) stamp(p, S, t, 55);
+    // ---- P.V over the own dims: thread (d, g) chains keys j = g mod 8
+    const int d = S.tid & 31, g = S.tid >> 5;
+    float a = 0.0f;
+    if (staged) {
+        for (int j = g; j < tk; j += 8) {
+            const uint16_t vv = j < pos ? S.vst[j * kHalfDim + d] : S.vcur[d];
+            a = fmaf(pbuf[j], __uint_as_float((uint32_t)vv << 16), a);
+        }
+    } else {
+        uint16_t *vchunk = S.kst;
+        for (int j0 = 0; j0 < pos; j0 += kChunkKeys) {
+            const int j1 = min(pos, j0 + kChunkKeys);
+            cbar();
+            kv_stage(p, S, layer, head, half, 1, j0, j1, vchunk);
+            cp_async_commit();
+            cp_async_wait_all();
+            cbar();
+            for (int j = j0 + ((g - j0 % 8) + 8) % 8; j < j1; j += 8)
+                a = fmaf(pbuf[j], __uint_as_float((uint32_t)vchunk[(j - j0) * kHalfDim + d] << 16), a);
+        }
+        if (pos % 8 == g) a = fmaf(pbuf[pos], __uint_as_float((uint32_t)S.vcur[d] << 16), a);
     }
+    S.accg[g * 32 + d] = a;
     cbar();
-    if (layer == 1) stamp(p, S, t, 85);
-    // P.V: thread (d, q4) runs the chains over keys q4*16 .. q4*16+15 of every page (j ascending)
-    {
-        const int d = S.tid & 63, q4 = S.tid >> 6;
-        float a[kGroupPages];
-        int nkp[kGroupPages];
+    if (S.tid < kHalfDim) {
+        float tot = 0.0f;
 #pragma unroll
-        for (int pl = 0; pl < kGroupPages; pl++) {
-            a[pl] = 0.0f;
-            nkp[pl] = pl < np ? min(kPageTokens, ntok - pl * kPageTokens) : 0;
-        }
-#pragma unroll 4
-        for (int jj = 0; jj < 16; jj++) {
-            const int j = q4 * 16 + jj;
-#pragma unroll
-            for (int pl = 0; pl < kGroupPages; pl++) {
-                if (j < nkp[pl]) {
-                    const uint16_t v = S.kvbuf[((pl * 2 + 1) * kPageTokens + j) * kHeadDim + d];
-                    a[pl] = fmaf(S.sc[pl * 64 + j], __uint_as_float((uint32_t)v << 16), a[pl]);
-                }
-            }
-        }
-#pragma unroll
-        for (int pl = 0; pl < kGroupPages; pl++)
-            if (pl < np) S.accp[(pl * 4 + q4) * 64 + d] = a[pl];
+        for (int gg = 0; gg < 8; gg++) tot = __fadd_rn(tot, S.accg[gg * 32 + S.tid]);
+        put_limbs4(S.limbs, kSlimbOff + S.tid, bf16r(__fdiv_rn(tot, l)), exp2i(fix));
     }
-    cbar();
-    if (layer == 1) stamp(p, S, t, 81);
-    if (S.tid < 64) {
-        float M = -INFINITY, L = 0.0f, A = 0.0f;
-        for (int pl = 0; pl < np; pl++) {
-            const float *ap = S.accp + pl * 256 + S.tid;
-            const float a = __fadd_rn(__fadd_rn(__fadd_rn(ap[0], ap[64]), ap[128]), ap[192]);
-            const float mp = S.pst[2 * pl], lp = S.pst[2 * pl + 1];
-            const float mn = fmaxf(M, mp);
-            const float c0 = fast_exp_nonpos(__fsub_rn(M, mn));
-            const float c1 = fast_exp_nonpos(__fsub_rn(mp, mn));
-            L = __fadd_rn(__fmul_rn(L, c0), __fmul_rn(lp, c1));
-            A = __fadd_rn(__fmul_rn(A, c0), __fmul_rn(a, c1));
-            M = mn;
-        }
-        if (single) {
-            const float ctx = __fdiv_rn(A, L);
-            const uint32_t mine = bf16bits(ctx);
-            const uint32_t hi = __shfl_down_sync(0xffffffffu, mine, 1);
-            if ((S.tid & 1) == 0) ll_store(p.ll_att + h * 32 + (S.tid >> 1), mine | (hi << 16), ep_att);
-        } else {
-            uint64_t *dst = p.ll_att + (size_t)item * (2 + kHeadDim);
-            ll_store(dst + 2 + S.tid, __float_as_uint(A), ep_att);
-            if (S.tid == 0) ll_store(dst, __float_as_uint(M), ep_att);
-            if (S.tid == 1) ll_store(dst + 1, __float_as_uint(L), ep_att);
-        }
-    }
-    // no trailing barrier: what follows writes none of sc / accp / pst before its own barrier
-}
-
-// n_groups page groups cover positions [0, pos]
-__device__ __forceinline__ int att_groups(int pos) { return pos / (kGroupPages * kPageTokens) + 1; }
-
-// Combine the group partials of every head (flash-decode merge, in group order) into
-// ctx = bf16(acc / l) in S.act[0..D).  Partials are staged through kvbuf in batches of whole
-// items.  The caller ends with a consumer barrier.
-__device__ __forceinline__ void att_combine(const DecodeParams &p, Cta &S, int pos, uint32_t ep_att, int layer) {
-    const int H = p.n_heads, D = p.d_model;
-    const int n_items = att_groups(pos) * H;
-    constexpr int W = 2 + kHeadDim;
-    const int per_batch = (SmemMap::kvbuf_bytes / 4) / W;   // items per kvbuf load
-    float M[4], L[4], A[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++) { M[k] = -INFINITY; L[k] = 0.0f; A[k] = 0.0f; }
-    uint32_t *buf = reinterpret_cast<uint32_t *>(S.kvbuf);
-    for (int b0 = 0; b0 < n_items; b0 += per_batch) {
-        const int b1 = min(n_items, b0 + per_batch);
-        if (b0 > 0) cbar();                       // previous batch fully read
-        ll_gather(p, S, p.ll_att + (size_t)b0 * W, buf, (b1 - b0) * W, ep_att, 0x300u + layer);
-        cbar();
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const int i = S.tid + k * kConsumerThreads;
-            if (i < D) {
-                const int h = i / kHeadDim, d = i % kHeadDim;
-                int it = b0 + ((h - b0 % H) + H) % H;       // first item of head h in batch
-                for (; it < b1; it += H) {
-                    const uint32_t *w = buf + (size_t)(it - b0) * W;
-                    const float mp = __uint_as_float(w[0]), lp = __uint_as_float(w[1]);
-                    const float ap = __uint_as_float(w[2 + d]);
-                    const float mn = fmaxf(M[k], mp);
-                    const float c0 = fast_exp_nonpos(__fsub_rn(M[k], mn));
-                    const float c1 = fast_exp_nonpos(__fsub_rn(mp, mn));
-                    L[k] = __fadd_rn(__fmul_rn(L[k], c0), __fmul_rn(lp, c1));
-                    A[k] = __fadd_rn(__fmul_rn(A[k], c0), __fmul_rn(ap, c1));
-                    M[k] = mn;
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        const int i = S.tid + k * kConsumerThreads;
-        if (i < D) S.act[i] = (uint16_t)bf16bits(__fdiv_rn(A[k], L[k]));
-    }
+    if (layer == 1) stamp(p, S, t, 56);
+    return true;
 }
 
 // optional debugging record of the residual stream (CTA 0 only); after a consumer barrier
@@ -686,7 +680,7 @@ __device__ __forceinline__ void trace_x(const DecodeParams &p, Cta &S, int t, in
     float *dst = p.trace + ((size_t)t * (2 * p.n_layers + 1) + slot) * p.d_model;
     for (int i = S.tid; i < p.d_model; i += kConsumerThreads) dst[i] = v[i];
 }
-// prefetch a LayerNorm's gamma and beta into S.lnp[buf] (cp.async, generic proxy)
+// prefetch a LayerNorm's gamma and beta into S.lnp[buf] (cp.async, one commit group)
 __device__ __forceinline__ void ln_prefetch(Cta &S, int buf, const float *g, const float *b, int D) {
     float *dst = S.lnp + buf * 2 * kDmax;
     for (int c = S.tid; c < D / 2; c += kConsumerThreads) {   // D/4 16-byte pieces per vector
@@ -696,8 +690,8 @@ __device__ __forceinline__ void ln_prefetch(Cta &S, int buf, const float *g, con
     cp_async_commit();
 }
 
+// ------------------------------------------------------------------------------ producer
 __device__ __forceinline__ void producer(const DecodeParams &p, Cta &S) {
-    if (S.lane != 0) return;
     const int c = blockIdx.x;
     const ChunkRef *tab = p.chunks + (size_t)c * p.chunk_stride;
     const int nl = p.n_layer_chunks[c], nlm = p.n_lm_chunks[c];
@@ -707,279 +701,345 @@ __device__ __forceinline__ void producer(const DecodeParams &p, Cta &S) {
         const int pos = p.start_pos + t;
         const int n = nl + (pos >= p.n_prompt - 1 ? nlm : 0);
         for (int i = 0; i < n; i++) {
-            const int slot = ctr % kStages;
-            const uint32_t k = ctr / kStages;
+            const int slot = ctr % kSlots;
+            const uint32_t k = ctr / kSlots;
             if (k > 0 && !mbar_try_wait(&S.empty[slot], (k - 1) & 1u)) {
                 uint64_t t0 = 0;
+                uint32_t it = 0;
                 while (!mbar_try_wait(&S.empty[slot], (k - 1) & 1u))
-                    if (wait_expired(p, S.flag, t0, ERR_TIMEOUT_EMPTY, 0x400u)) { failed = true; break; }
+                    if ((++it & 15) == 0 &&
+                        wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_EMPTY, 0x400u)) {
+                        failed = true;
+                        break;
+                    }
                 if (failed) break;
             }
             const ChunkRef ch = tab[i];
             mbar_arrive_expect_tx(&S.full[slot], ch.bytes);
-            bulk_g2s(S.ring + slot * kStageBytes, p.stream + ch.off, ch.bytes, &S.full[slot]);
+            bulk_g2s(S.ring + slot * kSlotBytes, p.stream + ch.off, ch.bytes, &S.full[slot]);
             ctr++;
         }
     }
     // drain: every issued copy must land before the CTA's shared memory is released
-    const uint32_t first = ctr > (uint32_t)kStages ? ctr - kStages : 0u;
+    const uint32_t first = ctr > (uint32_t)kSlots ? ctr - kSlots : 0u;
     for (uint32_t q = first; q < ctr; q++) {
-        const int slot = q % kStages;
-        const uint32_t par = (q / kStages) & 1u;
-        uint64_t t0 = 0;
         const uint64_t start = globaltimer_ns();
-        while (!mbar_try_wait(&S.full[slot], par)) {
-            (void)t0;
+        while (!mbar_try_wait(&S.full[q % kSlots], (q / kSlots) & 1u))
             if (globaltimer_ns() - start > p.timeout_ns) break;
-        }
     }
 }
 
+// ------------------------------------------------------------------------------ consumer
 template <int D, int F>
 __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
     const int c = blockIdx.x, G = p.grid;
     const int L = p.n_layers, V = p.vocab, H = p.n_heads;
-    const uint32_t base = p.state->epoch_base;
-    const int PHT = kPhasesPerLayer * L + 1;
-    const int q_row0 = part_row0(c, 3 * D, G), q_rows = part_rows(c, 3 * D, G);
-    const int o_row0 = part_row0(c, D, G), o_rows = part_rows(c, D, G);
-    const int f1_row0 = part_row0(c, F, G), f1_rows = part_rows(c, F, G);
-    const int f2_row0 = part_row0(c, D, G), f2_rows = part_rows(c, D, G);
-    const int lm_row0 = part_row0(c, V, G), lm_rows = part_rows(c, V, G);
-    uint32_t ctr = 0;
+    const bool is_head = c < 2 * H;
+    const int head = c >> 1, half = c & 1;
+    const int fci = c - 2 * H;
+    const bool is_fc = !is_head && fci < p.n_fc;
+    constexpr int NKB_D = D / 32;
+    constexpr int KBW = NKB_D / kConsumerWarps;          // k-blocks per warp for K = D
+    const int fc_kb_begin = is_fc ? fc_kb0(fci, F / 32, p.n_fc) : 0;
+    const int fc_nkb = is_fc ? fc_kb0(fci + 1, F / 32, p.n_fc) - fc_kb_begin : 0;
+    const uint32_t tok0 = p.state->tok_base;
+    const int lm_t0 = lm_tile0(c, p.vocab_tiles, G);
+    const int lm_nt = lm_tile0(c + 1, p.vocab_tiles, G) - lm_t0;
+    uint32_t ctr = 0, xu = 0;
     int64_t next_id = 0;
-    uint32_t *actw = reinterpret_cast<uint32_t *>(S.act);
-    const float *lng = S.lnp, *lnb = S.lnp + kDmax;                     // buffer 0: LN1 / LNf
-    const float *ln2g = S.lnp + 2 * kDmax, *ln2b = S.lnp + 3 * kDmax;  // buffer 1: LN2
-    for (int i = S.tid; i < kMaxPages; i += kConsumerThreads)
-        S.pt[i] = i < p.n_phys_pages ? p.page_table[i] : 0;
+    for (int i = S.tid; i < kMaxPages; i += kConsumerThreads) S.pt[i] = i < p.n_phys_pages ? p.page_table[i] : 0;
     if (S.tid == 0) { S.flag[0] = 0; S.flag[1] = 0; }
     cbar();
 
     for (int t = 0; t < p.n_steps; t++) {
         const int pos = p.start_pos + t;
-        const uint32_t ep0 = base + (uint32_t)(t * PHT) + 1u;
+        const uint32_t tau = tok0 + (uint32_t)t;
+        unsigned long long *acc_tok = p.acc + (size_t)(tau % kAccSlots) * L * 2 * D;
         const int64_t id = (t == 0 || pos < p.n_prompt) ? p.tokens[pos] : next_id;
-        if (id < 0 || id >= V || pos + 2 > p.max_pos + 1) {
-            if (S.tid == 0) {
-                set_error(p, id < 0 || id >= V ? ERR_BAD_TOKEN : ERR_BAD_POS, pos);
-                S.flag[0] = 1;
-            }
+        bool bad = false;
+        if (id < 0 || id >= V || pos + 2 > p.max_pos + 1 || pos >= kMaxCtx) {
+            bad = true;
+            if (S.tid == 0) set_error_st(p.state, id < 0 || id >= V ? ERR_BAD_TOKEN : ERR_BAD_POS, pos);
         }
-        cp_async_wait_all();                 // no stale LN prefetch may land after the next
-        if (abort_check(S)) return;
+        cp_async_wait_all();                 // no stale prefetch may land after the next
+        if (cbar_or(bad || *(volatile int *)S.flag != 0)) return;
+        const bool lm_token = pos >= p.n_prompt - 1;
+        if (!is_head && !is_fc && !lm_token) {
+            // a spare CTA has nothing to do in a token without an LM head; it must not read
+            // the accumulator words then, because nothing would keep it from falling behind
+            // the CTAs that clear them
+            next_id = p.tokens[pos + 1];
+            continue;
+        }
         stamp(p, S, t, 0);
-        ln_prefetch(S, 0, p.ln, p.ln + D, D);
-        float *xcur = S.xs;                  // x lives in xs[0..D) or xs[kDmax..kDmax+D)
         for (int i = S.tid; i < D; i += kConsumerThreads)
-            xcur[i] = __fadd_rn(p.emb_tok[(size_t)id * D + i], p.emb_pos[(size_t)(pos + 2) * D + i]);
-        const int n_items = att_groups(pos) * H;
-        const bool single = n_items == H;
+            S.x[i] = __fadd_rn(p.emb_tok[(size_t)id * D + i], p.emb_pos[(size_t)(pos + 2) * D + i]);
+        // the accumulator words of token tau + 2 (last used by token tau - 2, which every CTA
+        // has finished: an FC CTA starts token tau only after all fc2 contributions of token
+        // tau - 1, which needed every head pair's and FC CTA's work of that token) are cleared
+        // by the FC CTAs and made visible before anything this CTA publishes later
+        if (is_fc) {
+            const int nz = p.n_fc, zi = fci;
+            const size_t W = (size_t)L * 2 * D;
+            unsigned long long *z = p.acc + (size_t)((tau + 2) % kAccSlots) * W;
+            const size_t z0 = W * zi / nz, z1 = W * (zi + 1) / nz;
+            for (size_t i = z0 + S.tid; i < z1; i += kConsumerThreads) z[i] = 0ull;
+            __threadfence();
+        }
+        const float *ln_first = is_head ? p.ln : p.ln + 2 * D;
+        ln_prefetch(S, 0, ln_first, ln_first + D, D);
+        const bool staged = pos <= kStageKeys;
 
         for (int l = 0; l < L; l++) {
-            const uint32_t ep = ep0 + (uint32_t)(l * kPhasesPerLayer);
-            const float *ln = p.ln + (size_t)l * 4 * D;
-            // cp.async groups, oldest first: LN1 params (issued one phase group earlier),
-            // LN2 params, this CTA's KV pages (always committed, possibly empty)
-            ln_prefetch(S, 1, ln + 2 * D, ln + 3 * D, D);
-            if (c < n_items) kv_prefetch(p, S, l, c, pos);
-            else cp_async_commit();
-            // ---------------- QKV: x += fc2(prev layer); LN1; q, k, v rows
-            if (l > 0) ll_gather(p, S, p.ll_f2, actw, D, ep - kPhasesPerLayer + PH_FC2, 0x10u + l);
-            cp_async_wait_group<2>();          // LN1 params in; LN2 and KV may still be in flight
-            cbar();
-            if (l == 1) stamp(p, S, t, 70);
-            if (*(volatile int *)S.flag) return;
-            float *xnext = xcur == S.xs ? S.xs + kDmax : S.xs;
-            int s = resid_ln_limbs<D>(S, xcur, xnext, l > 0 ? actw : nullptr, lng, lnb, p.eps);
-            if (l > 0) xcur = xnext;
-            cbar();
-            if (l == 1) stamp(p, S, t, 71);
-            if (l > 0) trace_x(p, S, t, 2 * (l - 1) + 1, xcur);
-            gemv_phase<true>(p, S, ctr, q_rows, D, s, 0x20u + l, [&](int r, float y0, float y1) {
-                const int n = q_row0 + r;
-                if (n < D) { y0 = __fmul_rn(y0, 0.125f); y1 = __fmul_rn(y1, 0.125f); }
-                ll_store(p.ll_qkv + n / 2, bf16bits(y0) | (bf16bits(y1) << 16), ep + PH_QKV);
-            });
-            stamp(p, S, t, 1 + 5 * l + PH_QKV);
-            if (l == 1) stamp(p, S, t, 72);
-            // ---------------- ATT: this CTA's (page, head) items
-            for (int it = c, k = 0; it < n_items; it += G, k++)
-                att_item(p, S, l, it, pos, k == 0, single, ep + PH_QKV, ep + PH_ATT, t);
-            stamp(p, S, t, 1 + 5 * l + PH_ATT);
-            // LN1 of the next layer (or the final LN) into buffer 0, read by nothing until then
-            if (l + 1 < L) ln_prefetch(S, 0, ln + 4 * D, ln + 5 * D, D);
-            else ln_prefetch(S, 0, p.lnf, p.lnf + D, D);
-            // ---------------- O: merge partials -> ctx; O rows
-            if (o_rows > 0) {
-                if (single) ll_gather(p, S, p.ll_att, actw, D / 2, ep + PH_ATT, 0x300u + l);
-                else att_combine(p, S, pos, ep + PH_ATT, l);
-                cbar();
-                if (l == 1) stamp(p, S, t, 82);
-                s = limbs_of_act<D>();
-                cbar();
-                if (l == 1) stamp(p, S, t, 83);
-                gemv_phase<false>(p, S, ctr, o_rows, D, s, 0x30u + l, [&](int r, float y, float) {
-                    ll_store(p.ll_o + o_row0 + r, __float_as_uint(y), ep + PH_O);
-                });
+            unsigned long long *acc_o = acc_tok + (size_t)(l * 2 + 0) * D;
+            unsigned long long *acc_f = acc_tok + (size_t)(l * 2 + 1) * D;
+            // LayerNorm parameters of the next layer (or the final LN) into the other buffer
+            {
+                const float *nx = l + 1 < L ? p.ln + (size_t)(l + 1) * 4 * D + (is_head ? 0 : 2 * D) : p.lnf;
+                ln_prefetch(S, (l + 1) & 1, nx, nx + D, D);
             }
-            stamp(p, S, t, 1 + 5 * l + PH_O);
-            // ---------------- FC1: x += o; LN2; relu(fc1) -> bf16
-            if (l == 1) stamp(p, S, t, 63);
-            ll_gather(p, S, p.ll_o, actw, D, ep + PH_O, 0x40u + l);
-            cp_async_wait_group<1>();          // LN2 params in; the next LN1 may still be in flight
-            cbar();
-            if (l == 1) stamp(p, S, t, 64);
-            if (*(volatile int *)S.flag) return;
-            xnext = xcur == S.xs ? S.xs + kDmax : S.xs;
-            s = resid_ln_limbs<D>(S, xcur, xnext, actw, ln2g, ln2b, p.eps);
-            xcur = xnext;
-            cbar();
-            if (l == 1) stamp(p, S, t, 65);
-            trace_x(p, S, t, 2 * l, xcur);
-            gemv_phase<true>(p, S, ctr, f1_rows, D, s, 0x50u + l, [&](int r, float y0, float y1) {
-                y0 = fmaxf(y0, 0.0f);
-                y1 = fmaxf(y1, 0.0f);
-                ll_store(p.ll_h + (f1_row0 + r) / 2, bf16bits(y0) | (bf16bits(y1) << 16), ep + PH_FC1);
-            });
-            stamp(p, S, t, 1 + 5 * l + PH_FC1);
-            // ---------------- FC2
-            if (f2_rows > 0) {
-                if (l == 1) stamp(p, S, t, 66);
-                ll_gather(p, S, p.ll_h, actw, F / 2, ep + PH_FC1, 0x60u + l);
+            if (is_head) {
+                // ---------------- head pair: x += fc2(l-1); LN1; q|k|v of the own dims
+                if (staged) {
+                    kv_stage(p, S, l, head, half, 0, 0, pos, S.kst);
+                    kv_stage(p, S, l, head, half, 1, 0, pos, S.vst);
+                }
+                cp_async_commit();
+                bool ok = true;
+                if (l > 0)
+                    ok = gather_acc<D>(p, S, acc_tok + (size_t)((l - 1) * 2 + 1) * D, p.n_fc, p.f2_bias_shift,
+                                       p.fix_h[l - 1], p.f2sb + (size_t)(l - 1) * 2 * D, 0x10u + l);
+                cp_async_wait_group<2>();          // this layer's LN parameters
+                if (cbar_or(!ok)) return;
+                if (l > 0) trace_x(p, S, t, 2 * (l - 1) + 1, S.x);
+                stamp(p, S, t, 1 + 4 * l);
+                const float *lg = S.lnp + (l & 1) * 2 * kDmax;
+                const int s = ln_limbs<D>(S.x, lg, lg + kDmax, p.eps, S.limbs, S.lane, S.warp * KBW,
+                                          (S.warp + 1) * KBW);
+                ok = rowtile_mma<KBW>(p, S, ctr, 6, 0x20u + l);
+                if (cbar_or(!ok)) return;
+                if (S.tid < 96) {
+                    const int r = S.tid, part = r >> 5, i = r & 31;
+                    const float y = rowtile_out(S, ctr, r, D, s);
+                    if (part == 0) {
+                        S.qf[i] = bf16r(__fmul_rn(y, 0.125f));
+                    } else {
+                        const uint16_t bits = (uint16_t)bf16bits(y);
+                        p.kv[kv_index(p, l, S.pt[pos / kPageTokens], head, half, part - 1, pos % kPageTokens) + i] = bits;
+                        if (part == 1) S.kcur[(((i >> 3) ^ (pos & 3)) << 3) + (i & 7)] = bits;
+                        else S.vcur[i] = bits;
+                    }
+                }
+                if (S.tid == 0) mbar_arrive_expect_tx(&S.xchg[xu & 1], 4u * (pos + 1));
+                cp_async_wait_all();               // staged K / V rows
                 cbar();
-                if (l == 1) stamp(p, S, t, 67);
-                s = limbs_of_act<F>();
-                cbar();
-                if (l == 1) stamp(p, S, t, 68);
-                gemv_phase<false>(p, S, ctr, f2_rows, F, s, 0x70u + l, [&](int r, float y, float) {
-                    ll_store(p.ll_f2 + f2_row0 + r, __float_as_uint(y), ep + PH_FC2);
-                });
+                release_tiles(S, ctr, 6);
+                ctr += 6;
+                stamp(p, S, t, 2 + 4 * l);
+                // ---------------- attention over the own dims, then the K-split out projection
+                ok = attention(p, S, l, head, half, pos, staged, xu, p.fix_ctx[l], t);
+                xu++;
+                if (cbar_or(!ok)) return;
+                ok = slice_mma_red<D>(p, S, ctr, 1, acc_o, p.o_bias_shift, 0x30u + l);
+                stamp(p, S, t, 3 + 4 * l);
+                // ---------------- x += out projection
+                ok = ok && gather_acc<D>(p, S, acc_o, 2 * H, p.o_bias_shift, p.fix_ctx[l],
+                                         p.osb + (size_t)l * 2 * D, 0x40u + l);
+                if (cbar_or(!ok)) return;
+                trace_x(p, S, t, 2 * l, S.x);
+                stamp(p, S, t, 4 + 4 * l);
+            } else {
+                // ---------------- x += out projection; LN2; fc1 rows; ReLU; K-split fc2
+                cp_async_commit();                 // (keeps the group count of the head path)
+                bool ok = gather_acc<D>(p, S, acc_o, 2 * H, p.o_bias_shift, p.fix_ctx[l],
+                                        p.osb + (size_t)l * 2 * D, 0x40u + l);
+                cp_async_wait_group<2>();
+                if (cbar_or(!ok)) return;
+                trace_x(p, S, t, 2 * l, S.x);
+                stamp(p, S, t, 1 + 4 * l);
+                if (is_fc) {
+                    const float *lg = S.lnp + (l & 1) * 2 * kDmax;
+                    const int s = ln_limbs<D>(S.x, lg, lg + kDmax, p.eps, S.limbs, S.lane, S.warp * KBW,
+                                              (S.warp + 1) * KBW);
+                    const float hsc = exp2i(p.fix_h[l]);
+                    const int ntile = 2 * fc_nkb;
+                    for (int t0 = 0; t0 < ntile; t0 += 6) {
+                        const int nt = min(6, ntile - t0);
+                        ok = rowtile_mma<KBW>(p, S, ctr, nt, 0x50u + l);
+                        if (cbar_or(!ok)) return;
+                        if (S.tid < nt * kTile) {
+                            const float y = fmaxf(rowtile_out(S, ctr, S.tid, D, s), 0.0f);
+                            put_limbs4(S.limbs, kSlimbOff + t0 * kTile + S.tid, bf16r(y), hsc);
+                        }
+                        cbar();
+                        release_tiles(S, ctr, nt);
+                        ctr += nt;
+                    }
+                    stamp(p, S, t, 2 + 4 * l);
+                    ok = slice_mma_red<D>(p, S, ctr, fc_nkb, acc_f, p.f2_bias_shift, 0x60u + l);
+                    stamp(p, S, t, 3 + 4 * l);
+                }
+                // ---------------- x += fc2
+                ok = ok && gather_acc<D>(p, S, acc_f, p.n_fc, p.f2_bias_shift, p.fix_h[l],
+                                         p.f2sb + (size_t)l * 2 * D, 0x70u + l);
+                if (cbar_or(!ok)) return;
+                trace_x(p, S, t, 2 * l + 1, S.x);
+                stamp(p, S, t, 4 + 4 * l);
             }
-            stamp(p, S, t, 1 + 5 * l + PH_FC2);
+            // the LM-head rows of this CTA go to L2 a few layers before they are needed
+            if (l == max(0, L - 4) && lm_token && S.tid < lm_nt) {
+                const ChunkRef ch = p.chunks[(size_t)c * p.chunk_stride + p.n_layer_chunks[c] + S.tid];
+                prefetch_l2(p.stream + ch.off, ch.bytes);
+            }
         }
-        // ---------------- final residual, LN, LM head + greedy argmax
-        const uint32_t ep_last = ep0 + (uint32_t)((L - 1) * kPhasesPerLayer) + PH_FC2;
-        if (pos >= p.n_prompt - 1) {
-            const uint32_t ep_lm = ep0 + (uint32_t)(L * kPhasesPerLayer);
-            ll_gather(p, S, p.ll_f2, actw, D, ep_last, 0x80u);
+        if (is_head) {
+            const bool ok = gather_acc<D>(p, S, acc_tok + (size_t)((L - 1) * 2 + 1) * D, p.n_fc, p.f2_bias_shift,
+                                          p.fix_h[L - 1], p.f2sb + (size_t)(L - 1) * 2 * D, 0x80u);
+            if (cbar_or(!ok)) return;
+            trace_x(p, S, t, 2 * L - 1, S.x);
+        }
+        // ---------------- final LN, LM head + greedy argmax
+        if (lm_token) {
+            const uint32_t ep_lm = tau + 1u;
             cp_async_wait_all();
             cbar();
-            if (*(volatile int *)S.flag) return;
-            float *xnext = xcur == S.xs ? S.xs + kDmax : S.xs;
-            const int s = resid_ln_limbs<D>(S, xcur, xnext, actw, lng, lnb, p.eps);
+            const float *lg = S.lnp + (L & 1) * 2 * kDmax;
+            float *tr = (p.trace && c == 0) ? p.trace + ((size_t)t * (2 * L + 1) + 2 * L) * D : nullptr;
+            const int s = ln_limbs<D>(S.x, lg, lg + kDmax, p.eps, S.limbs, S.lane, S.warp * KBW,
+                                      (S.warp + 1) * KBW, tr);
             cbar();
-            trace_x(p, S, t, 2 * L - 1, xnext);
-            float best = -INFINITY;
-            int best_i = -1;
             const int lm_step = pos - max(p.start_pos, p.n_prompt - 1);
             float *lrow = p.logits ? p.logits + (size_t)lm_step * V : nullptr;
-            gemv_phase<false>(p, S, ctr, lm_rows, D, s, 0x100u, [&](int r, float y, float) {
-                const int idx = lm_row0 + r;
-                if (lrow) lrow[idx] = y;
-                if (y > best || (y == best && idx > best_i)) { best = y; best_i = idx; }
-            });
-            // CTA-level argmax (ties -> larger index: Iterator::max_by, opt125m_decode.rs:303)
+            unsigned long long best = 0ull;
+            bool ok = true;
+            const float inv = exp2i(-s);
+            const int g = S.lane >> 2, tig = S.lane & 3;
+            for (int i = S.warp; i < lm_nt; i += kConsumerWarps) {
+                if (!wait_full(p, S, ctr + i, 0x100u)) { ok = false; break; }
+                const uint8_t *ch = slot_ptr(S, ctr + i);
+                int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+#pragma unroll 4
+                for (int kb = 0; kb < NKB_D; kb += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    load_bfrag(S.limbs, 0, kb, S.lane, b0, b1);
+                    load_bfrag(S.limbs, 0, kb + 1, S.lane, b2, b3);
+                    const uint4 x0 = *reinterpret_cast<const uint4 *>(ch + kb * kFragBytes + S.lane * 16);
+                    const uint4 x1 = *reinterpret_cast<const uint4 *>(ch + (kb + 1) * kFragBytes + S.lane * 16);
+                    mma_s8_16832(a0, x0.x, x0.y, x0.z, x0.w, b0, b1);
+                    mma_s8_16832(a1, x1.x, x1.y, x1.z, x1.w, b2, b3);
+                }
+                const float *meta = reinterpret_cast<const float *>(ch + kTile * D);
+                const float2 m0 = *reinterpret_cast<const float2 *>(meta + 2 * g);
+                const float2 m1 = *reinterpret_cast<const float2 *>(meta + 2 * (g + 8));
+                __syncwarp();
+                if (S.lane == 0) mbar_arrive_cnt(&S.empty[(ctr + i) % kSlots], kConsumerWarps);
+                int v[4];
 #pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-                if (ob > best || (ob == best && oi > best_i)) { best = ob; best_i = oi; }
-            }
-            if (S.lane == 0) { S.red[S.warp] = best; S.red[32 + S.warp] = __int_as_float(best_i); }
-            cbar();
-            if (S.tid == 0) {
-                float b = S.red[0];
-                int bi = __float_as_int(S.red[32]);
-                for (int w = 1; w < kConsumerWarps; w++) {
-                    const float ob = S.red[w];
-                    const int oi = __float_as_int(S.red[32 + w]);
-                    if (ob > b || (ob == b && oi > bi)) { b = ob; bi = oi; }
+                for (int k = 0; k < 4; k++) v[k] = a0[k] + a1[k];
+                const int x0 = __shfl_down_sync(0xffffffffu, v[0], 1);
+                const int x1 = __shfl_down_sync(0xffffffffu, v[1], 1);
+                const int x2 = __shfl_down_sync(0xffffffffu, v[2], 1);
+                const int x3 = __shfl_down_sync(0xffffffffu, v[3], 1);
+                if (tig == 0) {
+                    const int r0 = (lm_t0 + i) * kTile + g, r1 = r0 + 8;
+                    const float y0 = __fadd_rn(
+                        __fmul_rn(__fmul_rn(__ll2float_rn(limb_dot(v[0], v[1], x0, x1)), inv), m0.x), m0.y);
+                    const float y1 = __fadd_rn(
+                        __fmul_rn(__fmul_rn(__ll2float_rn(limb_dot(v[2], v[3], x2, x3)), inv), m1.x), m1.y);
+                    // key: value order (sign-flipped bits), then the larger index (ties -> last
+                    // max, Iterator::max_by in opt125m_decode.rs:303)
+                    if (r0 < V) {
+                        if (lrow) lrow[r0] = y0;
+                        const uint32_t u = __float_as_uint(y0);
+                        const unsigned long long k =
+                            ((unsigned long long)(u & 0x80000000u ? ~u : u | 0x80000000u) << 32) | (uint32_t)r0;
+                        best = k > best ? k : best;
+                    }
+                    if (r1 < V) {
+                        if (lrow) lrow[r1] = y1;
+                        const uint32_t u = __float_as_uint(y1);
+                        const unsigned long long k =
+                            ((unsigned long long)(u & 0x80000000u ? ~u : u | 0x80000000u) << 32) | (uint32_t)r1;
+                        best = k > best ? k : best;
+                    }
                 }
-                ll_store(p.ll_lm + 2 * c, __float_as_uint(b), ep_lm);
-                ll_store(p.ll_lm + 2 * c + 1, (uint32_t)bi, ep_lm);
             }
-            stamp(p, S, t, 5 * L + 1);
-            // global argmax over all CTAs (every CTA computes it in the same order)
-            ll_gather(p, S, p.ll_lm, actw, 2 * G, ep_lm, 0x90u);
-            cbar();
+            ctr += lm_nt;
+            best = warp_max_u64(best);
+            if (S.lane == 0) S.keys[S.warp] = best;
+            if (cbar_or(!ok)) return;
             if (S.tid == 0) {
-                float b = -INFINITY;
-                int bi = -1;
-                for (int q = 0; q < G; q++) {
-                    const float ob = __uint_as_float(actw[2 * q]);
-                    const int oi = (int)actw[2 * q + 1];
-                    if (oi < 0) continue;
-                    if (bi < 0 || ob > b || (ob == b && oi > bi)) { b = ob; bi = oi; }
+                unsigned long long b = 0ull;
+                for (int w = 0; w < kConsumerWarps; w++) b = S.keys[w] > b ? S.keys[w] : b;
+                ll_store(p.ll_lm + 2 * c, (uint32_t)(b >> 32), ep_lm);
+                ll_store(p.ll_lm + 2 * c + 1, (uint32_t)b, ep_lm);
+            }
+            stamp(p, S, t, 50);
+            // global argmax over all CTAs: thread q reads CTA q's key
+            unsigned long long kq = 0ull;
+            if (S.tid < G) {
+                uint64_t hi = ll_load(p.ll_lm + 2 * S.tid), lo = ll_load(p.ll_lm + 2 * S.tid + 1);
+                uint64_t t0 = 0;
+                uint32_t it = 0;
+                while ((uint32_t)(hi >> 32) != ep_lm || (uint32_t)(lo >> 32) != ep_lm) {
+                    __nanosleep(20);
+                    if ((uint32_t)(hi >> 32) != ep_lm) hi = ll_load(p.ll_lm + 2 * S.tid);
+                    if ((uint32_t)(lo >> 32) != ep_lm) lo = ll_load(p.ll_lm + 2 * S.tid + 1);
+                    if ((++it & 31) == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FLAG, 0x90u)) {
+                        ok = false;
+                        break;
+                    }
                 }
+                kq = ((unsigned long long)(uint32_t)hi << 32) | (uint32_t)lo;
+            }
+            kq = warp_max_u64(kq);
+            if (S.lane == 0) S.keys[S.warp] = kq;
+            if (cbar_or(!ok)) return;
+            if (S.tid == 0) {
+                unsigned long long b = 0ull;
+                for (int w = 0; w < kConsumerWarps; w++) b = S.keys[w] > b ? S.keys[w] : b;
+                const int bi = (int)(uint32_t)b;
                 S.flag[1] = bi;
                 if (c == 0) p.tokens[pos + 1] = bi;
             }
             cbar();
             next_id = S.flag[1];
-            stamp(p, S, t, 5 * L + 2);
+            stamp(p, S, t, 51);
         } else {
             next_id = p.tokens[pos + 1];
         }
     }
-    if (c == 0 && S.tid == 0) p.state->epoch_base = base + (uint32_t)(p.n_steps * PHT);
+    if (c == 0 && S.tid == 0) p.state->tok_base = tok0 + (uint32_t)p.n_steps;
 }
 
 template <int D, int F>
-__global__ void __launch_bounds__(kThreads, 1) opt_decode_kernel(const DecodeParams p) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) opt_decode_kernel(const DecodeParams p) {
     Cta S = make_cta();
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kStages; i++) {
+        for (int i = 0; i < kSlots; i++) {
             mbar_init(&S.full[i], 1);
             mbar_init(&S.empty[i], kConsumerWarps);
         }
+        mbar_init(&S.xchg[0], 1);
+        mbar_init(&S.xchg[1], 1);
         mbar_fence_init();
     }
     __syncthreads();
-    if (S.warp == kConsumerWarps) producer(p, S);
-    else consumer<D, F>(p, S);
+    cluster_sync_all();                      // the pair's mbarriers exist before any st.async
+    if (S.warp == kConsumerWarps) {
+        if (S.lane == 0) producer(p, S);
+        __syncwarp();
+    } else {
+        consumer<D, F>(p, S);
+        // after the last token, or after an agreed early exit: a producer still waiting for a
+        // free slot sees the flag at its next poll and stops
+        if (S.tid == 0) *(volatile int *)S.flag = 1;
+    }
+    cluster_sync_all();                      // neither CTA leaves while its pair may write into it
 }
 
 // model widths the decode kernel is compiled for (d_model, ffn)
 #define XDNA_DECODE_SHAPES(X) X(768, 3072) X(256, 512)
-
-// ------------------------------------------------------------------ standalone GEMV (op API)
-// y[N] = exact-int8-GEMV(x[K]) * scale + bias over a packed chunk list: one CTA per chunk,
-// the decode kernel's limb and MMA code (for parity tests and the op-level C ABI).
-__global__ void __launch_bounds__(kThreads, 1)
-gemv_i8_kernel(const float *x, int K, const uint8_t *packed, const ChunkRef *chunks, int N, float *y) {
-    Cta S = make_cta();
-    const int rpc = rows_per_chunk(K);
-    const int row0 = blockIdx.x * rpc;
-    const int rows = min(rpc, N - row0);
-    if (threadIdx.x == 0) {
-        mbar_init(&S.full[0], 1);
-        mbar_fence_init();
-    }
-    __syncthreads();
-    if (threadIdx.x == kConsumerThreads) {
-        const ChunkRef ch = chunks[blockIdx.x];
-        mbar_arrive_expect_tx(&S.full[0], ch.bytes);
-        bulk_g2s(S.ring, packed + ch.off, ch.bytes, &S.full[0]);
-    }
-    if (S.warp == kConsumerWarps) return;
-    float *xf = reinterpret_cast<float *>(S.kvbuf);
-    for (int i = S.tid; i < K; i += kConsumerThreads) xf[i] = x[i];
-    cbar();
-    int s = 0;
-    switch (K) {
-#define XDNA_GEMV_K(KK) case KK: s = limbs_of<KK>(S, [&](int i) { return xf[i]; }); break;
-        XDNA_GEMV_K(256) XDNA_GEMV_K(512) XDNA_GEMV_K(768) XDNA_GEMV_K(1024) XDNA_GEMV_K(1536)
-        XDNA_GEMV_K(2048) XDNA_GEMV_K(2560) XDNA_GEMV_K(3072)
-#undef XDNA_GEMV_K
-        default: return;
-    }
-    cbar();
-    const uint64_t start = globaltimer_ns();
-    while (!mbar_try_wait(&S.full[0], 0u))
-        if (globaltimer_ns() - start > 1000000000ull) return;   // bounded (1 s)
-    gemv_chunk<false>(S, S.ring, rows, K, s, 0, [&](int r, float v, float) { y[row0 + r] = v; });
-}
 
 int decode_smem_bytes() { return SmemMap::total; }
 
@@ -999,30 +1059,26 @@ cudaError_t launch_opt_decode(const DecodeParams &p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     DecodeParams pp = p;
     void *args[] = {&pp};
-    return cudaLaunchCooperativeKernel(fn, dim3(p.grid), dim3(kThreads), args, SmemMap::total, st);
+    return cudaLaunchKernel(fn, dim3(p.grid), dim3(kThreads), args, SmemMap::total, st);
 }
 
-cudaError_t launch_gemv_i8(const float *x, int K, const uint8_t *packed, const ChunkRef *chunks,
-                           int N, float *y, cudaStream_t st) {
-    // per-device attribute: set on every launch (cheap), so a second device is covered too
-    cudaError_t e = cudaFuncSetAttribute(gemv_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SmemMap::total);
-    if (e != cudaSuccess) return e;
-    const int nch = (N + rows_per_chunk(K) - 1) / rows_per_chunk(K);
-    gemv_i8_kernel<<<nch, kThreads, SmemMap::total, st>>>(x, K, packed, chunks, N, y);
-    return cudaGetLastError();
-}
-
-cudaError_t max_coresident_ctas(int *out) {
-    const void *fn = decode_kernel_for(768, 3072);
+// largest even grid whose clusters of 2 are all co-resident (one CTA per SM)
+cudaError_t max_coresident_ctas(int d, int f, int *out) {
+    const void *fn = decode_kernel_for(d, f);
+    if (!fn) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemMap::total);
     if (e != cudaSuccess) return e;
-    int dev = 0, sms = 0, per = 0;
+    int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, fn, kThreads, SmemMap::total);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms & ~1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = SmemMap::total;
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg);
     if (e != cudaSuccess) return e;
-    *out = sms * per;
+    *out = 2 * clusters;
     return cudaSuccess;
 }
 

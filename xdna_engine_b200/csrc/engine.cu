@@ -18,13 +18,12 @@
 
 #include "../../include/xdna_b200.h"
 #include "decode.h"
+#include "gemv_op.h"
 
 namespace xdna {
 int decode_smem_bytes();
 cudaError_t launch_opt_decode(const DecodeParams &p, cudaStream_t st);
-cudaError_t launch_gemv_i8(const float *x, int K, const uint8_t *packed, const ChunkRef *chunks,
-                           int N, float *y, cudaStream_t st);
-cudaError_t max_coresident_ctas(int *out);
+cudaError_t max_coresident_ctas(int d, int f, int *out);
 bool decode_shape_supported(int d, int f);
 }  // namespace xdna
 
@@ -93,11 +92,12 @@ struct QMat {
     std::vector<float> bias;    // [N]
 };
 
-// Append rows [r0, r0+rows) of m as chunks to `out` (see decode.h): per chunk the rows'
-// K bytes with 32-byte block kb of row r stored at block kb ^ (r & 3), then (scale, bias)
-// per row, padded to 16 bytes.
+// Append rows [r0, r0+rows) of m as chunks of the op-level GEMV (gemv_op.h): per chunk the
+// rows' K bytes with 32-byte block kb of row r stored at block kb ^ (r & 3), then (scale,
+// bias) per row, padded to 16 bytes.
 void pack_rows(const QMat &m, int r0, int rows, std::vector<uint8_t> &out,
-               std::vector<ChunkRef> &refs, size_t base_off) {
+               std::vector<gemvop::ChunkRef> &refs, size_t base_off) {
+    using namespace gemvop;
     const int K = m.K, rpc = rows_per_chunk(K);
     for (int c0 = 0; c0 < rows; c0 += rpc) {
         const int rr = std::min(rpc, rows - c0);
@@ -115,8 +115,102 @@ void pack_rows(const QMat &m, int r0, int rows, std::vector<uint8_t> &out,
             meta[2 * r] = m.scale[r0 + c0 + r];
             meta[2 * r + 1] = m.bias.empty() ? 0.0f : m.bias[r0 + c0 + r];
         }
-        refs.push_back(ChunkRef{static_cast<uint32_t>(base_off + off), bytes});
+        refs.push_back(gemvop::ChunkRef{static_cast<uint32_t>(base_off + off), bytes});
     }
+}
+
+// ---- the decode kernel's stream (decode.h): chunks in mma.sync m16n8k32 A-fragment order.
+// Lane (g, tig) of an m-tile x 32-wide k-block holds 16 bytes: A[g][4tig..+3],
+// A[g+8][4tig..+3], A[g][16+4tig..+3], A[g+8][16+4tig..+3].
+template <class At>
+void put_frag(uint8_t *dst, At A) {
+    for (int lane = 0; lane < 32; lane++) {
+        const int g = lane >> 2, tig = lane & 3;
+        const int rows[4] = {g, g + 8, g, g + 8}, ks[4] = {4 * tig, 4 * tig, 16 + 4 * tig, 16 + 4 * tig};
+        for (int w = 0; w < 4; w++)
+            for (int i = 0; i < 4; i++) dst[lane * 16 + w * 4 + i] = (uint8_t)A(rows[w], ks[w] + i);
+    }
+}
+
+struct StreamBuilder {
+    std::vector<uint8_t> bytes;
+    std::vector<ChunkRef> refs;
+    size_t base = 0;                       // offset of this CTA's stream in the whole stream
+    uint8_t *chunk(size_t n) {
+        const size_t off = bytes.size();
+        bytes.resize(off + ((n + 15) & ~(size_t)15), 0);
+        refs.push_back(ChunkRef{static_cast<uint32_t>(base + off), static_cast<uint32_t>((n + 15) & ~(size_t)15)});
+        return bytes.data() + off;
+    }
+};
+
+// one 16-row tile of a GEMV whose output row r (r < 16) is row(r) of an output-major int8
+// matrix with K columns (nullptr = zero row), followed by 16 x (scale, bias)
+template <class RowFn>
+void pack_row_tile(StreamBuilder &sb, int K, RowFn row) {
+    uint8_t *dst = sb.chunk(row_chunk_bytes(K));
+    for (int kb = 0; kb < K / 32; kb++)
+        put_frag(dst + kb * kFragBytes, [&](int r, int k) -> int8_t {
+            const int8_t *q = row(r).q;
+            return q ? q[kb * 32 + k] : (int8_t)0;
+        });
+    float *meta = reinterpret_cast<float *>(dst + (size_t)kTile * K);
+    for (int r = 0; r < kTile; r++) {
+        meta[2 * r] = row(r).scale;
+        meta[2 * r + 1] = row(r).bias;
+    }
+}
+struct RowRef {
+    const int8_t *q;
+    float scale, bias;
+};
+RowRef row_of(const QMat &m, int n) {
+    if (n < 0 || n >= m.N) return RowRef{nullptr, 1.0f, 0.0f};
+    return RowRef{m.q.data() + (size_t)n * m.K, m.scale[n], m.bias.empty() ? 0.0f : m.bias[n]};
+}
+// the K-split slice of m over input columns [k0, k0 + 32) for all N outputs, as
+// slice_chunks(N) chunks of up to 24 m-tiles
+void pack_slice(StreamBuilder &sb, const QMat &m, int k0) {
+    const int N = m.N;
+    for (int c = 0; c < slice_chunks(N); c++) {
+        const int nt = slice_chunk_tiles(N, c);
+        uint8_t *dst = sb.chunk((size_t)nt * kFragBytes);
+        for (int t = 0; t < nt; t++) {
+            const int n0 = (c * kSliceTilesPerChunk + t) * kTile;
+            put_frag(dst + t * kFragBytes,
+                     [&](int r, int k) -> int8_t { return m.q[(size_t)(n0 + r) * m.K + k0 + k]; });
+        }
+    }
+}
+
+// Fixed-point exponent for values bounded by B: |x| * 2^s < 2^29.  The bounds are data
+// independent (weights and LayerNorm parameters only): a LayerNorm output satisfies
+// |y_k| <= sqrt(D) |gamma_k| + |beta_k|, so a linear output row n is bounded by
+// sum_k |W[n][k]| * scale[n] * lnmax_k + |bias[n]|; 1% covers the bf16 and f32 roundings.
+int fix_from_bound(double B) {
+    if (!(B > 0.0)) return kFixBits;
+    int E = 0;
+    std::frexp(B, &E);                     // B < 2^E
+    return kFixBits - E;
+}
+double rows_bound(const QMat &m, int n0, int n1, const float *g, const float *b, int D) {
+    std::vector<double> lnmax(D);
+    for (int k = 0; k < D; k++)
+        lnmax[k] = (std::sqrt((double)D) * std::fabs((double)g[k]) + std::fabs((double)b[k])) * 1.01;
+    double B = 0.0;
+    for (int n = n0; n < n1; n++) {
+        const int8_t *q = m.q.data() + (size_t)n * m.K;
+        double s = 0.0;
+        for (int k = 0; k < m.K; k++) s += std::fabs((double)q[k]) * lnmax[k];
+        s = s * (double)m.scale[n] + std::fabs((double)(m.bias.empty() ? 0.0f : m.bias[n]));
+        B = std::max(B, s);
+    }
+    return B * 1.01;
+}
+int ceil_log2(int v) {
+    int e = 0;
+    while ((1 << e) < v) e++;
+    return e;
 }
 
 QMat quant_linear(const float *w, const float *b, int K, int N) {
@@ -128,19 +222,6 @@ QMat quant_linear(const float *w, const float *b, int K, int N) {
     quant_cols(w, K, N, m.q.data(), m.scale.data());
     m.bias.assign(b, b + N);
     return m;
-}
-
-// rows of several matrices stacked (q|k|v share one phase)
-QMat stack(const std::vector<const QMat *> &ms) {
-    QMat r;
-    r.K = ms[0]->K;
-    for (auto *m : ms) {
-        r.N += m->N;
-        r.q.insert(r.q.end(), m->q.begin(), m->q.end());
-        r.scale.insert(r.scale.end(), m->scale.begin(), m->scale.end());
-        r.bias.insert(r.bias.end(), m->bias.begin(), m->bias.end());
-    }
-    return r;
 }
 
 }  // namespace
@@ -158,19 +239,21 @@ struct XdnaDevice {
 struct XdnaOptDecoder {
     XdnaDevice *dev = nullptr;
     XdnaOptConfig cfg{};
-    int grid = 0, max_ctx = 0, n_pages = 0;
+    int grid = 0, n_fc = 0, max_ctx = 0, n_pages = 0, vocab_tiles = 0;
+    int o_bias_shift = 0, f2_bias_shift = 0;
     size_t stream_bytes = 0, token_bytes = 0;
     uint8_t *d_stream = nullptr;
     ChunkRef *d_chunks = nullptr;
     int *d_nl = nullptr, *d_nlm = nullptr;
     int chunk_stride = 0;
-    float *d_emb = nullptr, *d_pos = nullptr, *d_ln = nullptr, *d_lnf = nullptr;
+    float *d_emb = nullptr, *d_pos = nullptr, *d_ln = nullptr, *d_lnf = nullptr, *d_osb = nullptr,
+          *d_f2sb = nullptr;
+    int *d_fix = nullptr;                  // [2][L]: context, fc1-output exponents
     uint16_t *d_kv = nullptr;
     int *d_pt = nullptr;
+    unsigned long long *d_acc = nullptr;
+    size_t acc_words = 0;
     uint64_t *d_ll = nullptr;
-    size_t ll_words = 0;
-    uint64_t *ll_qkv = nullptr, *ll_att = nullptr, *ll_o = nullptr, *ll_h = nullptr, *ll_f2 = nullptr,
-             *ll_lm = nullptr;
     int64_t *d_tokens = nullptr;
     RunState *d_state = nullptr;
     float *d_logits = nullptr;      // scratch for xdna_opt_generate
@@ -178,8 +261,8 @@ struct XdnaOptDecoder {
     unsigned long long *timing = nullptr;  // optional phase stamps (xdna_opt_set_timing)
     size_t logits_cap = 0;
     ~XdnaOptDecoder() {
-        void *ptrs[] = {d_stream, d_chunks, d_nl, d_nlm, d_emb, d_pos, d_ln, d_lnf, d_kv, d_pt, d_ll,
-                        d_tokens, d_state, d_logits};
+        void *ptrs[] = {d_stream, d_chunks, d_nl, d_nlm, d_emb, d_pos, d_ln, d_lnf, d_osb, d_f2sb, d_fix,
+                        d_kv, d_pt, d_acc, d_ll, d_tokens, d_state, d_logits};
         for (void *p : ptrs)
             if (p) cudaFree(p);
     }
@@ -265,13 +348,13 @@ int xdna_quant_i8_rows(const float *w, int M, int K, int8_t *q, float *scale) {
 int xdna_gemv_i8(XdnaDevice *dev, const float *x, int K, const int8_t *q_nk, const float *scale,
                  const float *bias, int N, float *y) {
     if (!dev || !x || !q_nk || !scale || !y) { set_err("xdna_gemv_i8: null pointer"); return -1; }
-    if (K <= 0 || K % 256 != 0 || K > kKmax || N <= 0 || N % 8 != 0) {
+    if (K <= 0 || K % 256 != 0 || K > gemvop::kKmax || N <= 0 || N % 8 != 0) {
         set_err("xdna_gemv_i8: K must be a multiple of 256 <= 3072 and N a multiple of 8");
         return -1;
     }
     float *dx = nullptr, *dy = nullptr;
     uint8_t *dp = nullptr;
-    ChunkRef *dc = nullptr;
+    gemvop::ChunkRef *dc = nullptr;
     try {
         ck(cudaSetDevice(dev->ordinal), "cudaSetDevice");
         QMat m;
@@ -281,16 +364,16 @@ int xdna_gemv_i8(XdnaDevice *dev, const float *x, int K, const int8_t *q_nk, con
         m.scale.assign(scale, scale + N);
         if (bias) m.bias.assign(bias, bias + N);
         std::vector<uint8_t> packed;
-        std::vector<ChunkRef> refs;
+        std::vector<gemvop::ChunkRef> refs;
         pack_rows(m, 0, N, packed, refs, 0);
         dx = dmalloc<float>(K);
         dy = dmalloc<float>(N);
         dp = dmalloc<uint8_t>(packed.size());
-        dc = dmalloc<ChunkRef>(refs.size());
+        dc = dmalloc<gemvop::ChunkRef>(refs.size());
         ck(cudaMemcpy(dx, x, sizeof(float) * K, cudaMemcpyHostToDevice), "copy x");
         ck(cudaMemcpy(dp, packed.data(), packed.size(), cudaMemcpyHostToDevice), "copy weights");
-        ck(cudaMemcpy(dc, refs.data(), refs.size() * sizeof(ChunkRef), cudaMemcpyHostToDevice), "copy chunks");
-        ck(launch_gemv_i8(dx, K, dp, dc, N, dy, nullptr), "gemv_i8 launch");
+        ck(cudaMemcpy(dc, refs.data(), refs.size() * sizeof(gemvop::ChunkRef), cudaMemcpyHostToDevice), "copy chunks");
+        ck(gemvop::launch_gemv_i8(dx, K, dp, dc, N, dy, nullptr), "gemv_i8 launch");
         ck(cudaMemcpy(y, dy, sizeof(float) * N, cudaMemcpyDeviceToHost), "copy y");
         cudaFree(dx); cudaFree(dy); cudaFree(dp); cudaFree(dc);
         return 0;
@@ -312,14 +395,14 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
     }
     const XdnaOptConfig c = *cfg;
     const int D = c.d_model, F = c.ffn, L = c.n_layers, V = c.vocab, H = c.n_heads;
-    if (c.head_dim != kHeadDim || H * kHeadDim != D || D % 256 || D > kDmax || F % 256 || F > kKmax ||
-        L < 1 || V < 8 || V % 8 || c.max_pos < 1 || !decode_shape_supported(D, F)) {
+    if (c.head_dim != kHeadDim || H * kHeadDim != D || D % 256 || D > kDmax || F % 256 || F > kFmax ||
+        L < 1 || V < 8 || c.max_pos < 1 || !decode_shape_supported(D, F)) {
         set_err("xdna_opt_create: unsupported shape (head_dim 64; (d_model, ffn) one of the "
-                "compiled widths (768, 3072) or (256, 512); vocab % 8 == 0)");
+                "compiled widths (768, 3072) or (256, 512))");
         return nullptr;
     }
-    if (max_ctx < 1 || max_ctx > c.max_pos || max_ctx > kMaxPages * kPageTokens) {
-        set_err("xdna_opt_create: max_ctx must be in [1, min(max_pos, 4096)]");
+    if (max_ctx < 1 || max_ctx > c.max_pos || max_ctx > kMaxCtx) {
+        set_err("xdna_opt_create: max_ctx must be in [1, min(max_pos, 2048)]");
         return nullptr;
     }
     auto *dec = new (std::nothrow) XdnaOptDecoder();
@@ -330,23 +413,35 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         dec->cfg = c;
         dec->max_ctx = max_ctx;
         int maxg = 0;
-        ck(max_coresident_ctas(&maxg), "occupancy query");
-        dec->grid = grid > 0 ? std::min(grid, maxg) : maxg;
-        if (dec->grid < 1) throw std::runtime_error("decode kernel cannot be resident on this device");
-        const int G = dec->grid;
-        if ((3 * D / 8 + G - 1) / G * 8 > 1024 || (F / 8 + G - 1) / G * 8 > 1024)
-            throw std::runtime_error("grid too small for the per-CTA row buffers");
+        ck(max_coresident_ctas(D, F, &maxg), "occupancy query");
+        maxg = std::min(maxg, 256);
+        int G = grid > 0 ? std::min(grid, maxg) : maxg;
+        G &= ~1;
+        const int KB = F / 32;
+        if (G < 2 * H + 1) throw std::runtime_error("grid too small: needs 2 * n_heads CTAs plus FC CTAs");
+        const int n_fc = std::min(G - 2 * H, KB);
+        int max_nkb = 0;
+        for (int i = 0; i < n_fc; i++) max_nkb = std::max(max_nkb, fc_kb0(i + 1, KB, n_fc) - fc_kb0(i, KB, n_fc));
+        if (max_nkb > 64) throw std::runtime_error("grid too small: an FC CTA would own more than 2048 fc1 rows");
+        dec->grid = G;
+        dec->n_fc = n_fc;
+        dec->o_bias_shift = 43;
+        dec->f2_bias_shift = 43 + ceil_log2(max_nkb);
+        dec->vocab_tiles = (V + kTile - 1) / kTile;
 
-        // quantise every linear; the QKV phase stacks q | k | v rows
-        std::vector<QMat> qkv(L), o(L), f1(L), f2(L);
+        // quantise every linear (Lin::load rule)
+        std::vector<QMat> q(L), k(L), v(L), o(L), f1(L), f2(L);
+        std::vector<int> fix(2 * L);
         for (int l = 0; l < L; l++) {
             const XdnaOptLayer &ly = w->layers[l];
-            QMat q = quant_linear(ly.wq, ly.bq, D, D), k = quant_linear(ly.wk, ly.bk, D, D),
-                 v = quant_linear(ly.wv, ly.bv, D, D);
-            qkv[l] = stack({&q, &k, &v});
+            q[l] = quant_linear(ly.wq, ly.bq, D, D);
+            k[l] = quant_linear(ly.wk, ly.bk, D, D);
+            v[l] = quant_linear(ly.wv, ly.bv, D, D);
             o[l] = quant_linear(ly.wo, ly.bo, D, D);
             f1[l] = quant_linear(ly.w1, ly.b1, D, F);
             f2[l] = quant_linear(ly.w2, ly.b2, F, D);
+            fix[l] = fix_from_bound(rows_bound(v[l], 0, D, ly.ln1_w, ly.ln1_b, D));
+            fix[L + l] = fix_from_bound(rows_bound(f1[l], 0, F, ly.ln2_w, ly.ln2_b, D));
         }
         QMat lm;
         lm.K = D;
@@ -355,25 +450,38 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         lm.scale.resize(V);
         quant_rows(w->emb_tok, V, D, lm.q.data(), lm.scale.data());
 
-        // per-CTA streams
+        // per-CTA streams in consumption order
         std::vector<uint8_t> all;
         std::vector<std::vector<ChunkRef>> refs(G);
         std::vector<int> nl(G), nlm(G);
-        size_t per_token_max = 0;
         for (int cta = 0; cta < G; cta++) {
-            std::vector<uint8_t> s;
-            const size_t base = all.size();
+            StreamBuilder sb;
+            sb.base = all.size();
             for (int l = 0; l < L; l++) {
-                pack_rows(qkv[l], part_row0(cta, 3 * D, G), part_rows(cta, 3 * D, G), s, refs[cta], base);
-                pack_rows(o[l], part_row0(cta, D, G), part_rows(cta, D, G), s, refs[cta], base);
-                pack_rows(f1[l], part_row0(cta, F, G), part_rows(cta, F, G), s, refs[cta], base);
-                pack_rows(f2[l], part_row0(cta, D, G), part_rows(cta, D, G), s, refs[cta], base);
+                if (cta < 2 * H) {
+                    const int h = cta / 2, r = cta % 2;
+                    const QMat *qkv[3] = {&q[l], &k[l], &v[l]};
+                    for (int tile = 0; tile < 6; tile++) {
+                        const QMat &m = *qkv[tile / 2];
+                        const int n0 = h * kHeadDim + r * kHalfDim + (tile % 2) * kTile;
+                        pack_row_tile(sb, D, [&](int rr) { return row_of(m, n0 + rr); });
+                    }
+                    pack_slice(sb, o[l], h * kHeadDim + r * kHalfDim);
+                } else if (cta - 2 * H < n_fc) {
+                    const int i = cta - 2 * H;
+                    const int kb0 = fc_kb0(i, KB, n_fc), kb1 = fc_kb0(i + 1, KB, n_fc);
+                    for (int tile = 2 * kb0; tile < 2 * kb1; tile++)
+                        pack_row_tile(sb, D, [&](int rr) { return row_of(f1[l], tile * kTile + rr); });
+                    for (int kb = kb0; kb < kb1; kb++) pack_slice(sb, f2[l], kb * 32);
+                }
             }
-            nl[cta] = (int)refs[cta].size();
-            pack_rows(lm, part_row0(cta, V, G), part_rows(cta, V, G), s, refs[cta], base);
-            nlm[cta] = (int)refs[cta].size() - nl[cta];
-            per_token_max = std::max(per_token_max, s.size());
-            all.insert(all.end(), s.begin(), s.end());
+            nl[cta] = (int)sb.refs.size();
+            const int t0 = lm_tile0(cta, dec->vocab_tiles, G), t1 = lm_tile0(cta + 1, dec->vocab_tiles, G);
+            if (t1 - t0 > kMaxVocabTilesPerCta) throw std::runtime_error("vocabulary too large for the grid");
+            for (int t = t0; t < t1; t++) pack_row_tile(sb, D, [&](int rr) { return row_of(lm, t * kTile + rr); });
+            nlm[cta] = (int)sb.refs.size() - nl[cta];
+            refs[cta] = sb.refs;
+            all.insert(all.end(), sb.bytes.begin(), sb.bytes.end());
         }
         dec->stream_bytes = all.size();
         dec->token_bytes = all.size();
@@ -394,27 +502,37 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         ck(cudaMemcpy(dec->d_nl, nl.data(), G * sizeof(int), cudaMemcpyHostToDevice), "upload nl");
         ck(cudaMemcpy(dec->d_nlm, nlm.data(), G * sizeof(int), cudaMemcpyHostToDevice), "upload nlm");
 
-        // f32 parameters
+        // f32 parameters that are not streamed
         dec->d_emb = dmalloc<float>((size_t)V * D);
         ck(cudaMemcpy(dec->d_emb, w->emb_tok, sizeof(float) * V * D, cudaMemcpyHostToDevice), "upload emb");
         dec->d_pos = dmalloc<float>((size_t)(c.max_pos + 2) * D);
         ck(cudaMemcpy(dec->d_pos, w->emb_pos, sizeof(float) * (size_t)(c.max_pos + 2) * D, cudaMemcpyHostToDevice),
            "upload pos");
-        std::vector<float> ln((size_t)L * 4 * D);
+        std::vector<float> ln((size_t)L * 4 * D), osb((size_t)L * 2 * D), f2sb((size_t)L * 2 * D);
         for (int l = 0; l < L; l++) {
             const XdnaOptLayer &ly = w->layers[l];
             std::copy(ly.ln1_w, ly.ln1_w + D, ln.begin() + (size_t)(l * 4 + 0) * D);
             std::copy(ly.ln1_b, ly.ln1_b + D, ln.begin() + (size_t)(l * 4 + 1) * D);
             std::copy(ly.ln2_w, ly.ln2_w + D, ln.begin() + (size_t)(l * 4 + 2) * D);
             std::copy(ly.ln2_b, ly.ln2_b + D, ln.begin() + (size_t)(l * 4 + 3) * D);
+            std::copy(o[l].scale.begin(), o[l].scale.end(), osb.begin() + (size_t)(l * 2 + 0) * D);
+            std::copy(o[l].bias.begin(), o[l].bias.end(), osb.begin() + (size_t)(l * 2 + 1) * D);
+            std::copy(f2[l].scale.begin(), f2[l].scale.end(), f2sb.begin() + (size_t)(l * 2 + 0) * D);
+            std::copy(f2[l].bias.begin(), f2[l].bias.end(), f2sb.begin() + (size_t)(l * 2 + 1) * D);
         }
-        dec->d_ln = dmalloc<float>(ln.size());
-        ck(cudaMemcpy(dec->d_ln, ln.data(), ln.size() * sizeof(float), cudaMemcpyHostToDevice), "upload ln");
+        auto upload = [](const std::vector<float> &h, float **d, const char *what) {
+            *d = dmalloc<float>(h.size());
+            ck(cudaMemcpy(*d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice), what);
+        };
+        upload(ln, &dec->d_ln, "upload ln");
+        upload(osb, &dec->d_osb, "upload out-proj scales");
+        upload(f2sb, &dec->d_f2sb, "upload fc2 scales");
         std::vector<float> lnf(2 * D);
         std::copy(w->lnf_w, w->lnf_w + D, lnf.begin());
         std::copy(w->lnf_b, w->lnf_b + D, lnf.begin() + D);
-        dec->d_lnf = dmalloc<float>(2 * D);
-        ck(cudaMemcpy(dec->d_lnf, lnf.data(), 2 * D * sizeof(float), cudaMemcpyHostToDevice), "upload lnf");
+        upload(lnf, &dec->d_lnf, "upload lnf");
+        dec->d_fix = dmalloc<int>(2 * L);
+        ck(cudaMemcpy(dec->d_fix, fix.data(), 2 * L * sizeof(int), cudaMemcpyHostToDevice), "upload exponents");
 
         // paged KV: pages in reverse physical order so the page table is exercised
         dec->n_pages = (max_ctx + kPageTokens - 1) / kPageTokens;
@@ -422,27 +540,21 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         for (int i = 0; i < dec->n_pages; i++) pt[i] = dec->n_pages - 1 - i;
         dec->d_pt = dmalloc<int>(pt.size());
         ck(cudaMemcpy(dec->d_pt, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice), "upload page table");
-        const size_t kv_elems = (size_t)L * dec->n_pages * 2 * H * kPageTokens * kHeadDim;
+        const size_t kv_elems = (size_t)L * dec->n_pages * H * 2 * 2 * kPageTokens * kHalfDim;
         dec->d_kv = dmalloc<uint16_t>(kv_elems);
         ck(cudaMemset(dec->d_kv, 0, kv_elems * 2), "clear kv");
 
-        // flag-tagged exchange words
-        const size_t n_qkv = 3 * D / 2, n_att = (size_t)dec->n_pages * H * (2 + kHeadDim), n_o = D,
-                     n_h = F / 2, n_f2 = D, n_lm = 2 * (size_t)G;
-        dec->ll_words = n_qkv + n_att + n_o + n_h + n_f2 + n_lm;
-        dec->d_ll = dmalloc<uint64_t>(dec->ll_words);
-        ck(cudaMemset(dec->d_ll, 0, dec->ll_words * 8), "clear exchange words");
-        dec->ll_qkv = dec->d_ll;
-        dec->ll_att = dec->ll_qkv + n_qkv;
-        dec->ll_o = dec->ll_att + n_att;
-        dec->ll_h = dec->ll_o + n_o;
-        dec->ll_f2 = dec->ll_h + n_h;
-        dec->ll_lm = dec->ll_f2 + n_f2;
+        // exchange: accumulator words (zero) and the LM-head key words (epoch 0)
+        dec->acc_words = (size_t)kAccSlots * L * 2 * D;
+        dec->d_acc = dmalloc<unsigned long long>(dec->acc_words);
+        ck(cudaMemset(dec->d_acc, 0, dec->acc_words * 8), "clear accumulators");
+        dec->d_ll = dmalloc<uint64_t>(2 * (size_t)G);
+        ck(cudaMemset(dec->d_ll, 0, 2 * (size_t)G * 8), "clear exchange words");
 
         dec->d_tokens = dmalloc<int64_t>(max_ctx + 1);
         ck(cudaMemset(dec->d_tokens, 0, (max_ctx + 1) * sizeof(int64_t)), "clear tokens");
         dec->d_state = dmalloc<RunState>(1);
-        RunState rs{1u, 0u, 0u, 0u};
+        RunState rs{0u, 0u, 0u, 0u};
         ck(cudaMemcpy(dec->d_state, &rs, sizeof(rs), cudaMemcpyHostToDevice), "init state");
         ck(cudaDeviceSynchronize(), "create sync");
         return dec;
@@ -508,6 +620,8 @@ int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_promp
     p.max_pos = c.max_pos;
     p.eps = c.eps;
     p.grid = dec->grid;
+    p.n_fc = dec->n_fc;
+    p.vocab_tiles = dec->vocab_tiles;
     p.stream = dec->d_stream;
     p.chunks = dec->d_chunks;
     p.n_layer_chunks = dec->d_nl;
@@ -517,15 +631,17 @@ int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_promp
     p.emb_pos = dec->d_pos;
     p.ln = dec->d_ln;
     p.lnf = dec->d_lnf;
+    p.osb = dec->d_osb;
+    p.f2sb = dec->d_f2sb;
+    p.fix_ctx = dec->d_fix;
+    p.fix_h = dec->d_fix + c.n_layers;
+    p.o_bias_shift = dec->o_bias_shift;
+    p.f2_bias_shift = dec->f2_bias_shift;
     p.kv = dec->d_kv;
     p.page_table = dec->d_pt;
     p.n_phys_pages = dec->n_pages;
-    p.ll_qkv = dec->ll_qkv;
-    p.ll_att = dec->ll_att;
-    p.ll_o = dec->ll_o;
-    p.ll_h = dec->ll_h;
-    p.ll_f2 = dec->ll_f2;
-    p.ll_lm = dec->ll_lm;
+    p.acc = dec->d_acc;
+    p.ll_lm = dec->d_ll;
     p.tokens = dec->d_tokens;
     p.logits = logits_dev;
     p.start_pos = start_pos;
@@ -559,16 +675,18 @@ int xdna_opt_sync(XdnaOptDecoder *dec, void *stream) {
     }
     if (rs.error != ERR_NONE) {
         static const char *names[] = {"none", "timeout waiting for a weight chunk",
-                                      "timeout waiting for a free ring stage",
+                                      "timeout waiting for a free ring slot",
                                       "timeout waiting for an exchange word", "token id out of range",
-                                      "position out of range"};
+                                      "position out of range", "timeout waiting for the pair CTA"};
         char buf[256];
         std::snprintf(buf, sizeof buf, "decode kernel error: %s (cta %u, where 0x%x)",
-                      rs.error < 6 ? names[rs.error] : "unknown", rs.error_cta, rs.error_where);
+                      rs.error < 7 ? names[rs.error] : "unknown", rs.error_cta, rs.error_where);
         set_err(buf);
-        // the failed launch may have left words of its epochs behind: skip far past them
-        rs.epoch_base += 1u << 20;
+        // the failed launch may have left partial sums and key words behind: clear the
+        // accumulators and skip the LM-key epochs far past the failed ones
+        rs.tok_base += 1u << 20;
         rs.error = rs.error_cta = rs.error_where = 0;
+        cudaMemset(dec->d_acc, 0, dec->acc_words * 8);
         cudaMemcpy(dec->d_state, &rs, sizeof(rs), cudaMemcpyHostToDevice);
         return -1;
     }

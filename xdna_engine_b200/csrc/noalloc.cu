@@ -29,15 +29,14 @@
 #include <string>
 
 #include "../../include/xdna_b200.h"
-#include "decode.h"
+#include "gemv_op.h"
 
 namespace xdna {
-cudaError_t launch_gemv_i8(const float *x, int K, const uint8_t *packed, const ChunkRef *chunks,
-                           int N, float *y, cudaStream_t st);
 void set_last_error_message(const std::string &m);
 }  // namespace xdna
 
 using namespace xdna;
+using namespace xdna::gemvop;
 
 namespace {
 
