@@ -284,6 +284,48 @@ class OracleOpt:
             pass
 
 
+def _top2_margin(row):
+    """top value minus the best other value (the greedy choice's margin)"""
+    i = int(np.argmax(row[::-1]))
+    i = row.size - 1 - i                      # last maximum (Iterator::max_by tie rule)
+    rest = np.delete(row, i)
+    return float(row[i] - rest.max())
+
+
+def opt_parity_report(cfg, weights, prompt, ids, logits, nthreads=None):
+    """Compare a decoded stream (ids [n], logits [n, V], e.g. the GPU's) with the reference's
+    own host path (MODE_REF_F32: rust/npu-whisper/src/bin/opt125m_decode.rs:252-315 with
+    OPT_INT8).  Returns
+      tf_rel_l2      per step, relative L2 of logits against the reference teacher-forced on
+                     `ids` (so both see the same history);
+      tf_flips       steps where the teacher-forced argmaxes differ, each with the reference's
+                     top-2 margin there and the step's max |logit difference|;
+      free_first_div first step where the free-running reference stream differs (None if
+                     never), with the reference's margin at that step;
+      free_match     fraction of positions where the free-running streams agree."""
+    n = len(ids)
+    ref = OracleOpt(cfg, weights, MODE_REF_F32, nthreads)
+    tf_ids, tf_lg = ref.generate(prompt, n, want_logits=True, force=ids)
+    ref.close()
+    ref = OracleOpt(cfg, weights, MODE_REF_F32, nthreads)
+    fr_ids, fr_lg = ref.generate(prompt, n, want_logits=True)
+    ref.close()
+    rel = [float(np.linalg.norm(logits[t] - tf_lg[t]) / max(np.linalg.norm(tf_lg[t]), 1e-30))
+           for t in range(n)]
+    flips = []
+    for t in range(n):
+        if int(tf_ids[t]) != int(ids[t]):
+            flips.append({"step": t, "ref_margin": _top2_margin(tf_lg[t]),
+                          "max_abs_diff": float(np.abs(logits[t] - tf_lg[t]).max())})
+    diff = np.nonzero(np.asarray(fr_ids) != np.asarray(ids))[0]
+    first = int(diff[0]) if diff.size else None
+    return {"tf_rel_l2": rel, "tf_flips": flips,
+            "free_first_div": first,
+            "free_div_margin": None if first is None else _top2_margin(fr_lg[first]),
+            "free_match": float(np.mean(np.asarray(fr_ids) == np.asarray(ids))),
+            "ref_ids": fr_ids}
+
+
 # ---------------------------------------------------------------- BGE / BERT embedder
 _BERT_LAYER = ("q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "o_w", "o_b", "attn_ln_w", "attn_ln_b",
                "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b", "out_ln_w", "out_ln_b")

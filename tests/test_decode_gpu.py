@@ -4,8 +4,8 @@ Bar: the int8 GEMV is bit-exact with the oracle's exact limbed dot, and the whol
 bit-exact with the oracle's device-numerics mode (same quantised weights, same bf16 rounding
 points, same reduction trees, the reference's own fast_exp_nonpos): identical greedy tokens
 and identical f32 logits.  Against the reference's own f32 host path (OPT_INT8, f32 LM
-head), teacher-forced on the GPU's tokens, logits agree to 3e-2 relative L2 (int8 LM head and
-bf16 activations vs f32)."""
+head), teacher-forced on the GPU's tokens, logits agree to 1e-2 relative L2 at every step (int8
+LM head and bf16 activations vs f32), and every argmax that differs is a near tie."""
 import numpy as np
 import pytest
 
@@ -14,7 +14,7 @@ from xdna_engine_b200.synth import OptConfig, OPT_125M, make_opt_weights, make_p
 
 pytestmark = pytest.mark.gpu
 
-LOGIT_TOL_REF = 3e-2
+LOGIT_TOL_REF = 1e-2
 
 
 @pytest.fixture(scope="module")
@@ -119,7 +119,15 @@ def test_launch_split_equals_single_launch(X, dev):
 
 
 def test_opt125m_config_matches_oracle(X, dev):
-    """The BASELINE config: opt-125m, N(0,0.02) weights, 32-token prompt, 128 new tokens."""
+    """The BASELINE config: opt-125m, N(0,0.02) weights, 32-token prompt, 128 new tokens.
+
+    (a) every one of the 128 greedy tokens and logits rows equals the oracle's device-numerics
+        mode bit for bit;
+    (b) against the reference's own host path (OPT_INT8 Lin layers, f32 activations, f32 LM
+        head), teacher-forced on the GPU's tokens, every step's logits agree within 1e-2
+        relative L2;
+    (c) every step where the teacher-forced argmaxes differ is a near tie: the reference's
+        top-2 margin there is below the step's largest |logit difference|."""
     w = make_opt_weights(OPT_125M, seed=0)
     prompt = make_prompt(OPT_125M, 32, seed=0)
     n_new = 128
@@ -127,12 +135,15 @@ def test_opt125m_config_matches_oracle(X, dev):
     ids, lg = dec.generate(prompt, n_new, want_logits=True)
     dec.close()
     orc = O.OracleOpt(OPT_125M, w, O.MODE_DEVICE)
-    oids, olg = orc.generate(prompt, 24, want_logits=True)   # oracle cost bounds the prefix
-    np.testing.assert_array_equal(ids[:24], oids)
-    np.testing.assert_array_equal(lg[:24], olg)
-    ref = O.OracleOpt(OPT_125M, w, O.MODE_REF_F32)
-    _, rlg = ref.generate(prompt, 8, want_logits=True, force=ids[:8])
-    assert max(rel_l2(lg[t], rlg[t]) for t in range(8)) < LOGIT_TOL_REF
+    oids, olg = orc.generate(prompt, n_new, want_logits=True)
+    np.testing.assert_array_equal(ids, oids)
+    np.testing.assert_array_equal(lg, olg)
+    rep = O.opt_parity_report(OPT_125M, w, prompt, ids, lg)
+    assert max(rep["tf_rel_l2"]) <= LOGIT_TOL_REF, max(rep["tf_rel_l2"])
+    for f in rep["tf_flips"]:
+        assert f["ref_margin"] < f["max_abs_diff"], f
+    print("parity:", {k: v for k, v in rep.items() if k not in ("tf_rel_l2", "ref_ids")},
+          "max tf rel-L2", max(rep["tf_rel_l2"]))
 
 
 def test_bad_token_reports_error(X, dev):

@@ -396,3 +396,21 @@ def test_gemma_geglu_and_layer_pattern():
     assert abs(O.lib().or_gelu_tanh_gemma(1.0) - 0.8411920) < 1e-6
     glob = [(i + 1) % 6 == 0 for i in range(18)]
     assert glob[5] and glob[17] and not glob[0]
+
+
+def test_opt_device_numerics_track_reference_host_path():
+    """The engine's device numerics (bf16 activations, 29-bit fixed-point exact int8 GEMVs,
+    int8 LM head), restated by the oracle, against the reference's own host path
+    (opt125m_decode.rs:252-315 with OPT_INT8) at the BASELINE config over all 128 tokens:
+    teacher-forced logits within 1e-2 relative L2 at every step, and every argmax that differs
+    is a near tie (reference top-2 margin below the step's largest |logit difference|)."""
+    from xdna_engine_b200.synth import OPT_125M, make_opt_weights, make_prompt
+    w = make_opt_weights(OPT_125M, seed=0)
+    prompt = make_prompt(OPT_125M, 32, seed=0)
+    ids, lg = O.OracleOpt(OPT_125M, w, O.MODE_DEVICE).generate(prompt, 128, want_logits=True)
+    rep = O.opt_parity_report(OPT_125M, w, prompt, ids, lg)
+    assert max(rep["tf_rel_l2"]) <= 1e-2
+    for f in rep["tf_flips"]:
+        assert f["ref_margin"] < f["max_abs_diff"], f
+    if rep["free_first_div"] is not None:
+        assert rep["free_div_margin"] < max(f["max_abs_diff"] for f in rep["tf_flips"] or [{"max_abs_diff": 1.0}])

@@ -109,7 +109,9 @@ struct DecodeParams {
     const int *page_table;     // logical page -> physical page
     int n_phys_pages;
     // exchange
-    unsigned long long *acc;   // [kAccSlots][L][2: out-proj, fc2][D] accumulator words
+    unsigned long long *acc;   // [kAccSlots][L][2: out-proj, fc2][D * acc_stride] accumulator words
+    int acc_stride;            // words between consecutive outputs' accumulators (spreads atomics)
+    int poll_ns;               // sleep between polls of incomplete words
     uint64_t *ll_lm;           // [grid][2] flag-tagged LM-head best keys
     // run
     int64_t *tokens;           // [max_ctx + 1]: prompt in, generated ids out at pos+1

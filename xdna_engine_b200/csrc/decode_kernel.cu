@@ -51,7 +51,8 @@ struct SmemMap {
     static constexpr int part_rows = 96;
     static constexpr int xs = part + kConsumerWarps * part_rows * 4 * 4; // [kDmax] f32 residual
     static constexpr int limbs = xs + kDmax * 4;                         // [4][kLimbStride] int8
-    static constexpr int misc = limbs + kLimbs * kLimbStride;
+    static constexpr int own = limbs + kLimbs * kLimbStride;            // [kMaxCtx] f32
+    static constexpr int misc = own + kMaxCtx * 4;
     static constexpr int misc_bytes = 2048;
     static constexpr int bars = misc + misc_bytes;
     static constexpr int total = bars + (2 * kSlots + 2) * 8;
@@ -70,6 +71,7 @@ struct Cta {
     uint8_t *ring;
     uint16_t *kst, *vst;        // staged K rows (64 B, 16-byte chunks swizzled by row & 3), V rows
     float *ps;                  // [2][kMaxCtx]: the pair's partial scores, then probabilities
+    float *own;                 // [kMaxCtx]: this CTA's partial scores, then the full scores
     float *lnp;                 // [2 buffers][gamma | beta][kDmax]
     int *part;                  // [warp][row][limb] partial limb sums
     float *x;                   // residual stream
@@ -96,6 +98,7 @@ __device__ __forceinline__ Cta make_cta() {
     S.part = reinterpret_cast<int *>(s + SmemMap::part);
     S.x = reinterpret_cast<float *>(s + SmemMap::xs);
     S.limbs = reinterpret_cast<int8_t *>(s + SmemMap::limbs);
+    S.own = reinterpret_cast<float *>(s + SmemMap::own);
     uint8_t *m = s + SmemMap::misc;
     S.qf = reinterpret_cast<float *>(m);                          // 128 B
     S.kcur = reinterpret_cast<uint16_t *>(m + 128);               // 64 B
@@ -194,7 +197,7 @@ __device__ __noinline__ bool wait_expired(RunState *st, uint64_t timeout_ns, int
 // Wait for the chunk with stream index `ctr` to be in its ring slot; false on timeout /
 // abort.  Warp-collective (all 32 lanes call it and get the same answer): lane 0 polls, and
 // after success every lane observes the completed phase itself (acquire of the copy's data).
-__device__ __forceinline__ bool wait_full(const DecodeParams &p, Cta &S, uint32_t ctr, uint32_t where) {
+__device__ __forceinline__ bool wait_full(const DecodeParams &p, const Cta &S, uint32_t ctr, uint32_t where) {
     const int slot = ctr % kSlots;
     const uint32_t parity = (ctr / kSlots) & 1u;
     bool ok = true;
@@ -215,7 +218,7 @@ __device__ __forceinline__ const uint8_t *slot_ptr(const Cta &S, uint32_t ctr) {
     return S.ring + (ctr % kSlots) * kSlotBytes;
 }
 // the consumer warps release a slot: one arrival per warp
-__device__ __forceinline__ void release_slot(Cta &S, uint32_t ctr) {
+__device__ __forceinline__ void release_slot(const Cta &S, uint32_t ctr) {
     __syncwarp();
     if (S.lane == 0) mbar_arrive(&S.empty[ctr % kSlots]);
 }
@@ -313,9 +316,13 @@ __device__ __forceinline__ long long limb_dot(int a, int b, int c, int d) {
 // from the max over the whole output) and, if `out` is given, those outputs; returns the
 // exponent.
 template <int D>
-__device__ __forceinline__ int ln_limbs(const float *x, const float *g, const float *b, float eps, int8_t *L,
-                                        int lane, int kb0, int kb1, float *out = nullptr) {
+__device__ __noinline__ int ln_limbs(const float *g, const float *b, float eps, float *out) {
     constexpr int J = D / 32;
+    constexpr int KBW = J / kConsumerWarps;
+    const Cta S = make_cta();
+    const float *x = S.x;
+    int8_t *L = S.limbs;
+    const int lane = S.lane, kb0 = S.warp * KBW;
     float v[J];
     float s = 0.0f;
 #pragma unroll
@@ -342,12 +349,14 @@ __device__ __forceinline__ int ln_limbs(const float *x, const float *g, const fl
     }
     const int e = fix_exponent(warp_max_nonneg(m));
     const float sc = exp2i(e);
+    float mine[KBW];
 #pragma unroll
-    for (int j = 0; j < J; j++) {
-        if (j >= kb0 && j < kb1) {
-            put_limbs4(L, lane + 32 * j, v[j], sc);
-            if (out) out[lane + 32 * j] = v[j];
-        }
+    for (int j = 0; j < J; j++)
+        if (j / KBW == S.warp) mine[j % KBW] = v[j];
+#pragma unroll
+    for (int kk = 0; kk < KBW; kk++) {
+        put_limbs4(L, lane + 32 * (kb0 + kk), mine[kk], sc);
+        if (out) out[lane + 32 * (kb0 + kk)] = mine[kk];
     }
     __syncwarp();
     return e;
@@ -359,7 +368,8 @@ __device__ __forceinline__ int ln_limbs(const float *x, const float *g, const fl
 // limb sums go to S.part[warp][row][limb]; the caller combines them after a consumer
 // barrier.  The slots stay owned (their meta is read by the combine) until release_tiles.
 template <int KBW>
-__device__ __forceinline__ bool rowtile_mma(const DecodeParams &p, Cta &S, uint32_t ctr, int nt, uint32_t where) {
+__device__ __noinline__ bool rowtile_mma(const DecodeParams &p, uint32_t ctr, int nt, uint32_t where) {
+    const Cta S = make_cta();
     const int g = S.lane >> 2, tig = S.lane & 3;
     uint32_t bf[KBW][2];
 #pragma unroll
@@ -393,7 +403,7 @@ __device__ __forceinline__ float rowtile_out(const Cta &S, uint32_t ctr, int r, 
     const float y = __fmul_rn(__ll2float_rn(limb_dot(a, b, c, d)), exp2i(-s));
     return __fadd_rn(__fmul_rn(y, meta[2 * (r % kTile)]), meta[2 * (r % kTile) + 1]);
 }
-__device__ __forceinline__ void release_tiles(Cta &S, uint32_t ctr, int nt) {
+__device__ __forceinline__ void release_tiles(const Cta &S, uint32_t ctr, int nt) {
     __syncwarp();
     if (S.lane == 0)
         for (int t = 0; t < nt; t++) mbar_arrive(&S.empty[(ctr + t) % kSlots]);
@@ -403,8 +413,9 @@ __device__ __forceinline__ void release_tiles(Cta &S, uint32_t ctr, int nt) {
 // columns kSlimbOff + 32 kb), the slice chunks of D outputs; warp w owns the m-tiles w, w+8, ...
 // Each output's exact partial is added as (partial + 2^bshift + 2^56) into words[n].
 template <int D>
-__device__ __forceinline__ bool slice_mma_red(const DecodeParams &p, Cta &S, uint32_t &ctr, int nkb,
-                                              unsigned long long *words, int bshift, uint32_t where) {
+__device__ __noinline__ bool slice_mma_red(const DecodeParams &p, uint32_t ctr, int nkb,
+                                           unsigned long long *words, int bshift, uint32_t where) {
+    const Cta S = make_cta();
     constexpr int NT = D / kTile / kConsumerWarps;       // m-tiles per warp
     const int nch = slice_chunks(D);
     int acc[NT][4];
@@ -440,8 +451,9 @@ __device__ __forceinline__ bool slice_mma_red(const DecodeParams &p, Cta &S, uin
         const int x3 = __shfl_down_sync(0xffffffffu, acc[i][3], 1);
         if (tig == 0) {
             const int n = tile * kTile + g;
-            red_add_u64(words + n, (unsigned long long)limb_dot(acc[i][0], acc[i][1], x0, x1) + add);
-            red_add_u64(words + n + 8, (unsigned long long)limb_dot(acc[i][2], acc[i][3], x2, x3) + add);
+            red_add_u64(words + (size_t)n * p.acc_stride, (unsigned long long)limb_dot(acc[i][0], acc[i][1], x0, x1) + add);
+            red_add_u64(words + (size_t)(n + 8) * p.acc_stride,
+                        (unsigned long long)limb_dot(acc[i][2], acc[i][3], x2, x3) + add);
         }
     }
     return true;
@@ -452,8 +464,9 @@ __device__ __forceinline__ bool slice_mma_red(const DecodeParams &p, Cta &S, uin
 // Thread t owns n = t + 256 i.  Returns false on timeout / abort.  The caller follows with a
 // barrier.
 template <int D>
-__device__ __forceinline__ bool gather_acc(const DecodeParams &p, Cta &S, const unsigned long long *words, int cnt,
-                                           int bshift, int fix, const float *sb, uint32_t where) {
+__device__ __noinline__ bool gather_acc(const DecodeParams &p, const unsigned long long *words, int cnt, int bshift,
+                                        int fix, const float *sb, uint32_t where) {
+    const Cta S = make_cta();
     constexpr int PER = D / kConsumerThreads;
     float sc[PER], bi[PER];
     unsigned long long v[PER];
@@ -462,7 +475,7 @@ __device__ __forceinline__ bool gather_acc(const DecodeParams &p, Cta &S, const 
         const int n = S.tid + kConsumerThreads * i;
         sc[i] = sb[n];
         bi[i] = sb[D + n];
-        v[i] = ld_relaxed_u64(words + n);
+        v[i] = ld_relaxed_u64(words + (size_t)n * p.acc_stride);
     }
     const unsigned want = (unsigned)cnt;
     uint64_t t0 = 0;
@@ -473,10 +486,11 @@ __device__ __forceinline__ bool gather_acc(const DecodeParams &p, Cta &S, const 
 #pragma unroll
         for (int i = 0; i < PER; i++) all &= (unsigned)(v[i] >> kCountShift) == want;
         if (all) break;
-        __nanosleep(20);
+        __nanosleep(p.poll_ns);
 #pragma unroll
         for (int i = 0; i < PER; i++)
-            if ((unsigned)(v[i] >> kCountShift) != want) v[i] = ld_relaxed_u64(words + S.tid + kConsumerThreads * i);
+            if ((unsigned)(v[i] >> kCountShift) != want)
+                v[i] = ld_relaxed_u64(words + (size_t)(S.tid + kConsumerThreads * i) * p.acc_stride);
         if ((++it & 31) == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FLAG, where)) {
             ok = false;
             break;
@@ -504,7 +518,7 @@ __device__ __forceinline__ size_t kv_index(const DecodeParams &p, int layer, int
 // cp.async rows [j0, j1) of this CTA's K (kv = 0) or V (kv = 1) dims to dst (row j at
 // j - j0; K rows keep 16-byte chunk c at c ^ (j & 3) so the one-key-per-thread score loop is
 // bank-conflict free); no commit
-__device__ __forceinline__ void kv_stage(const DecodeParams &p, Cta &S, int layer, int head, int half, int kv,
+__device__ __forceinline__ void kv_stage(const DecodeParams &p, const Cta &S, int layer, int head, int half, int kv,
                                          int j0, int j1, uint16_t *dst) {
     for (int c = S.tid; c < (j1 - j0) * 4; c += kConsumerThreads) {
         const int j = j0 + (c >> 2), part = c & 3;
@@ -546,8 +560,9 @@ __device__ __forceinline__ float part_score(const float *qf, const uint16_t *kro
 // ctx limbs (fixed point 2^fix) land at limb column kSlimbOff + d.  `xu` counts the pair
 // exchanges of this launch (mbarrier buffer and parity).  Returns false on timeout / abort;
 // the caller follows with a barrier.
-__device__ __forceinline__ bool attention(const DecodeParams &p, Cta &S, int layer, int head, int half, int pos,
-                                       bool staged, uint32_t xu, int fix, int t) {
+__device__ __noinline__ bool attention(const DecodeParams &p, int layer, int head, int half, int pos, bool staged,
+                                       uint32_t xu, int fix, int t) {
+    const Cta S = make_cta();
     const int tk = pos + 1;
     const int buf = xu & 1;
     const uint32_t par = (xu >> 1) & 1u;
@@ -555,23 +570,18 @@ __device__ __forceinline__ bool attention(const DecodeParams &p, Cta &S, int lay
     const uint32_t peer = (uint32_t)half ^ 1u;
     const uint32_t rbuf = mapa_peer(pbuf, peer);
     const uint32_t rbar = mapa_peer(&S.xchg[buf], peer);
-    constexpr int KPT = kMaxCtx / kConsumerThreads;       // keys per thread (8)
-    float own[KPT];
+    float *own = S.own;
     // ---- partial scores of the own dims, sent to the peer as they are made
     if (staged) {
-#pragma unroll
-        for (int i = 0; i < KPT; i++) {
-            const int j = S.tid + kConsumerThreads * i;
-            own[i] = 0.0f;
-            if (j < tk) {
-                own[i] = part_score(S.qf, j < pos ? S.kst + j * kHalfDim : S.kcur, j);
-                st_async_b32(rbuf + 4u * j, __float_as_uint(own[i]), rbar);
-            }
+#pragma unroll 1
+        for (int j = S.tid; j < tk; j += kConsumerThreads) {
+            const float v = part_score(S.qf, j < pos ? S.kst + j * kHalfDim : S.kcur, j);
+            own[j] = v;
+            st_async_b32(rbuf + 4u * j, __float_as_uint(v), rbar);
         }
     } else {
         uint16_t *kchunk = S.kst;                         // the whole staging area holds K rows
-#pragma unroll
-        for (int i = 0; i < KPT; i++) own[i] = 0.0f;
+#pragma unroll 1
         for (int j0 = 0; j0 < pos; j0 += kChunkKeys) {
             const int j1 = min(pos, j0 + kChunkKeys);
             cbar();                                       // previous chunk fully read
@@ -579,18 +589,13 @@ __device__ __forceinline__ bool attention(const DecodeParams &p, Cta &S, int lay
             cp_async_commit();
             cp_async_wait_all();
             cbar();
-#pragma unroll
-            for (int i = 0; i < KPT; i++) {
-                const int j = S.tid + kConsumerThreads * i;
-                if (j >= j0 && j < j1) own[i] = part_score(S.qf, kchunk + (j - j0) * kHalfDim, j);
-            }
+#pragma unroll 1
+            for (int j = j0 + S.tid; j < j1; j += kConsumerThreads)
+                own[j] = part_score(S.qf, kchunk + (j - j0) * kHalfDim, j);
         }
-#pragma unroll
-        for (int i = 0; i < KPT; i++) {
-            const int j = S.tid + kConsumerThreads * i;
-            if (j == pos) own[i] = part_score(S.qf, S.kcur, j);
-            if (j < tk) st_async_b32(rbuf + 4u * j, __float_as_uint(own[i]), rbar);
-        }
+        if (S.tid == pos % kConsumerThreads) own[pos] = part_score(S.qf, S.kcur, pos);
+#pragma unroll 1
+        for (int j = S.tid; j < tk; j += kConsumerThreads) st_async_b32(rbuf + 4u * j, __float_as_uint(own[j]), rbar);
     }
     if (layer == 1) stamp(p, S, t, 53);
     // ---- the peer's partials
@@ -606,17 +611,15 @@ __device__ __forceinline__ bool attention(const DecodeParams &p, Cta &S, int lay
             }
     }
     if (layer == 1) stamp(p, S, t, 54);
-    float s[KPT];
+    // every thread touches only its own keys j = tid mod 256 in own[] and pbuf[] until the
+    // barrier before P.V
     float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < KPT; i++) {
-        const int j = S.tid + kConsumerThreads * i;
-        s[i] = -INFINITY;
-        if (j < tk) {
-            const float pr = pbuf[j];
-            s[i] = half == 0 ? __fadd_rn(own[i], pr) : __fadd_rn(pr, own[i]);
-            m = fmaxf(m, s[i]);
-        }
+#pragma unroll 1
+    for (int j = S.tid; j < tk; j += kConsumerThreads) {
+        const float pr = pbuf[j];
+        const float sj = half == 0 ? __fadd_rn(own[j], pr) : __fadd_rn(pr, own[j]);
+        own[j] = sj;
+        m = fmaxf(m, sj);
     }
     m = warp_max(m);
     if (S.lane == 0) S.red[S.warp] = m;
@@ -624,14 +627,11 @@ __device__ __forceinline__ bool attention(const DecodeParams &p, Cta &S, int lay
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; w++) m = fmaxf(m, S.red[w]);
     float l = 0.0f;
-#pragma unroll
-    for (int i = 0; i < KPT; i++) {
-        const int j = S.tid + kConsumerThreads * i;
-        if (j < tk) {
-            const float pj = fast_exp_nonpos(__fsub_rn(s[i], m));
-            pbuf[j] = pj;
-            l = __fadd_rn(l, pj);
-        }
+#pragma unroll 1
+    for (int j = S.tid; j < tk; j += kConsumerThreads) {
+        const float pj = fast_exp_nonpos(__fsub_rn(own[j], m));
+        pbuf[j] = pj;
+        l = __fadd_rn(l, pj);
     }
     l = warp_sum(l);
     if (S.lane == 0) S.red[8 + S.warp] = l;
@@ -644,6 +644,7 @@ __device__ __forceinline__ bool attention(const DecodeParams &p, Cta &S, int lay
     const int d = S.tid & 31, g = S.tid >> 5;
     float a = 0.0f;
     if (staged) {
+#pragma unroll 4
         for (int j = g; j < tk; j += 8) {
             const uint16_t vv = j < pos ? S.vst[j * kHalfDim + d] : S.vcur[d];
             a = fmaf(pbuf[j], __uint_as_float((uint32_t)vv << 16), a);
@@ -675,19 +676,127 @@ __device__ __forceinline__ bool attention(const DecodeParams &p, Cta &S, int lay
 }
 
 // optional debugging record of the residual stream (CTA 0 only); after a consumer barrier
-__device__ __forceinline__ void trace_x(const DecodeParams &p, Cta &S, int t, int slot, const float *v) {
+__device__ __forceinline__ void trace_x(const DecodeParams &p, const Cta &S, int t, int slot, const float *v) {
     if (p.trace == nullptr || blockIdx.x != 0) return;
     float *dst = p.trace + ((size_t)t * (2 * p.n_layers + 1) + slot) * p.d_model;
     for (int i = S.tid; i < p.d_model; i += kConsumerThreads) dst[i] = v[i];
 }
 // prefetch a LayerNorm's gamma and beta into S.lnp[buf] (cp.async, one commit group)
-__device__ __forceinline__ void ln_prefetch(Cta &S, int buf, const float *g, const float *b, int D) {
+__device__ __forceinline__ void ln_prefetch(const Cta &S, int buf, const float *g, const float *b, int D) {
     float *dst = S.lnp + buf * 2 * kDmax;
     for (int c = S.tid; c < D / 2; c += kConsumerThreads) {   // D/4 16-byte pieces per vector
         const int v = c / (D / 4), q = c % (D / 4);
         cp_async16(dst + v * kDmax + 4 * q, (v ? b : g) + 4 * q);
     }
     cp_async_commit();
+}
+
+// LM head (the tied embedding as int8 rows) + greedy argmax for one token: warp w takes this
+// CTA's row tiles w, w+8, ... (chunks ctr + i), all 24 k-blocks each; per CTA the best key
+// (value order, then the larger index) is published as two flag-tagged words; then every CTA
+// reads all CTAs' keys and leaves the winning id in S.flag[1] (CTA 0 also stores it in the
+// token array).  Returns false on timeout / abort (uniform over the CTA).
+template <int D>
+__device__ __noinline__ bool lm_head(const DecodeParams &p, uint32_t ctr, int t, int pos, uint32_t tau, int lm_t0,
+                                     int lm_nt, int s) {
+    const Cta S = make_cta();
+    constexpr int NKB_D = D / 32;
+    const int c = blockIdx.x, G = p.grid, V = p.vocab;
+    const uint32_t ep_lm = tau + 1u;
+    const int lm_step = pos - max(p.start_pos, p.n_prompt - 1);
+    float *lrow = p.logits ? p.logits + (size_t)lm_step * V : nullptr;
+    unsigned long long best = 0ull;
+    bool ok = true;
+    const float inv = exp2i(-s);
+    const int g = S.lane >> 2, tig = S.lane & 3;
+    for (int i = S.warp; i < lm_nt; i += kConsumerWarps) {
+        if (!wait_full(p, S, ctr + i, 0x100u)) { ok = false; break; }
+        const uint8_t *ch = slot_ptr(S, ctr + i);
+        int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+#pragma unroll 4
+        for (int kb = 0; kb < NKB_D; kb += 2) {
+            uint32_t b0, b1, b2, b3;
+            load_bfrag(S.limbs, 0, kb, S.lane, b0, b1);
+            load_bfrag(S.limbs, 0, kb + 1, S.lane, b2, b3);
+            const uint4 x0 = *reinterpret_cast<const uint4 *>(ch + kb * kFragBytes + S.lane * 16);
+            const uint4 x1 = *reinterpret_cast<const uint4 *>(ch + (kb + 1) * kFragBytes + S.lane * 16);
+            mma_s8_16832(a0, x0.x, x0.y, x0.z, x0.w, b0, b1);
+            mma_s8_16832(a1, x1.x, x1.y, x1.z, x1.w, b2, b3);
+        }
+        const float *meta = reinterpret_cast<const float *>(ch + kTile * D);
+        const float2 m0 = *reinterpret_cast<const float2 *>(meta + 2 * g);
+        const float2 m1 = *reinterpret_cast<const float2 *>(meta + 2 * (g + 8));
+        __syncwarp();
+        if (S.lane == 0) mbar_arrive_cnt(&S.empty[(ctr + i) % kSlots], kConsumerWarps);
+        int v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = a0[k] + a1[k];
+        const int x0 = __shfl_down_sync(0xffffffffu, v[0], 1);
+        const int x1 = __shfl_down_sync(0xffffffffu, v[1], 1);
+        const int x2 = __shfl_down_sync(0xffffffffu, v[2], 1);
+        const int x3 = __shfl_down_sync(0xffffffffu, v[3], 1);
+        if (tig == 0) {
+            const int r0 = (lm_t0 + i) * kTile + g, r1 = r0 + 8;
+            const float y0 = __fadd_rn(
+                __fmul_rn(__fmul_rn(__ll2float_rn(limb_dot(v[0], v[1], x0, x1)), inv), m0.x), m0.y);
+            const float y1 = __fadd_rn(
+                __fmul_rn(__fmul_rn(__ll2float_rn(limb_dot(v[2], v[3], x2, x3)), inv), m1.x), m1.y);
+            // key: value order (sign-flipped bits), then the larger index (ties -> last
+            // max, Iterator::max_by in opt125m_decode.rs:303)
+            if (r0 < V) {
+                if (lrow) lrow[r0] = y0;
+                const uint32_t u = __float_as_uint(y0);
+                const unsigned long long k =
+                    ((unsigned long long)(u & 0x80000000u ? ~u : u | 0x80000000u) << 32) | (uint32_t)r0;
+                best = k > best ? k : best;
+            }
+            if (r1 < V) {
+                if (lrow) lrow[r1] = y1;
+                const uint32_t u = __float_as_uint(y1);
+                const unsigned long long k =
+                    ((unsigned long long)(u & 0x80000000u ? ~u : u | 0x80000000u) << 32) | (uint32_t)r1;
+                best = k > best ? k : best;
+            }
+        }
+    }
+    best = warp_max_u64(best);
+    if (S.lane == 0) S.keys[S.warp] = best;
+    if (cbar_or(!ok)) return false;
+    if (S.tid == 0) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < kConsumerWarps; w++) b = S.keys[w] > b ? S.keys[w] : b;
+        ll_store(p.ll_lm + 2 * c, (uint32_t)(b >> 32), ep_lm);
+        ll_store(p.ll_lm + 2 * c + 1, (uint32_t)b, ep_lm);
+    }
+    stamp(p, S, t, 50);
+    // global argmax over all CTAs: thread q reads CTA q's key
+    unsigned long long kq = 0ull;
+    if (S.tid < G) {
+        uint64_t hi = ll_load(p.ll_lm + 2 * S.tid), lo = ll_load(p.ll_lm + 2 * S.tid + 1);
+        uint64_t t0 = 0;
+        uint32_t it = 0;
+        while ((uint32_t)(hi >> 32) != ep_lm || (uint32_t)(lo >> 32) != ep_lm) {
+            __nanosleep(20);
+            if ((uint32_t)(hi >> 32) != ep_lm) hi = ll_load(p.ll_lm + 2 * S.tid);
+            if ((uint32_t)(lo >> 32) != ep_lm) lo = ll_load(p.ll_lm + 2 * S.tid + 1);
+            if ((++it & 31) == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FLAG, 0x90u)) {
+                ok = false;
+                break;
+            }
+        }
+        kq = ((unsigned long long)(uint32_t)hi << 32) | (uint32_t)lo;
+    }
+    kq = warp_max_u64(kq);
+    if (S.lane == 0) S.keys[S.warp] = kq;
+    if (cbar_or(!ok)) return false;
+    if (S.tid == 0) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < kConsumerWarps; w++) b = S.keys[w] > b ? S.keys[w] : b;
+        const int bi = (int)(uint32_t)b;
+        S.flag[1] = bi;
+        if (c == 0) p.tokens[pos + 1] = bi;
+    }
+    return true;
 }
 
 // ------------------------------------------------------------------------------ producer
@@ -754,7 +863,8 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
     for (int t = 0; t < p.n_steps; t++) {
         const int pos = p.start_pos + t;
         const uint32_t tau = tok0 + (uint32_t)t;
-        unsigned long long *acc_tok = p.acc + (size_t)(tau % kAccSlots) * L * 2 * D;
+        const size_t XW = (size_t)D * p.acc_stride;        // words of one exchange
+        unsigned long long *acc_tok = p.acc + (size_t)(tau % kAccSlots) * L * 2 * XW;
         const int64_t id = (t == 0 || pos < p.n_prompt) ? p.tokens[pos] : next_id;
         bool bad = false;
         if (id < 0 || id >= V || pos + 2 > p.max_pos + 1 || pos >= kMaxCtx) {
@@ -765,9 +875,12 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
         if (cbar_or(bad || *(volatile int *)S.flag != 0)) return;
         const bool lm_token = pos >= p.n_prompt - 1;
         if (!is_head && !is_fc && !lm_token) {
-            // a spare CTA has nothing to do in a token without an LM head; it must not read
-            // the accumulator words then, because nothing would keep it from falling behind
-            // the CTAs that clear them
+            // A spare CTA has no work in a token without an LM head, but it still waits for
+            // the token's last fc2 words: that keeps it from running ahead into the slot of a
+            // later token while the words there still hold an older token's complete sums.
+            const bool ok = gather_acc<D>(p, acc_tok + (size_t)((L - 1) * 2 + 1) * XW, p.n_fc, p.f2_bias_shift,
+                                          p.fix_h[L - 1], p.f2sb + (size_t)(L - 1) * 2 * D, 0x88u);
+            if (cbar_or(!ok)) return;
             next_id = p.tokens[pos + 1];
             continue;
         }
@@ -780,7 +893,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
         // by the FC CTAs and made visible before anything this CTA publishes later
         if (is_fc) {
             const int nz = p.n_fc, zi = fci;
-            const size_t W = (size_t)L * 2 * D;
+            const size_t W = (size_t)L * 2 * XW;
             unsigned long long *z = p.acc + (size_t)((tau + 2) % kAccSlots) * W;
             const size_t z0 = W * zi / nz, z1 = W * (zi + 1) / nz;
             for (size_t i = z0 + S.tid; i < z1; i += kConsumerThreads) z[i] = 0ull;
@@ -791,8 +904,8 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
         const bool staged = pos <= kStageKeys;
 
         for (int l = 0; l < L; l++) {
-            unsigned long long *acc_o = acc_tok + (size_t)(l * 2 + 0) * D;
-            unsigned long long *acc_f = acc_tok + (size_t)(l * 2 + 1) * D;
+            unsigned long long *acc_o = acc_tok + (size_t)(l * 2 + 0) * XW;
+            unsigned long long *acc_f = acc_tok + (size_t)(l * 2 + 1) * XW;
             // LayerNorm parameters of the next layer (or the final LN) into the other buffer
             {
                 const float *nx = l + 1 < L ? p.ln + (size_t)(l + 1) * 4 * D + (is_head ? 0 : 2 * D) : p.lnf;
@@ -807,17 +920,19 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 cp_async_commit();
                 bool ok = true;
                 if (l > 0)
-                    ok = gather_acc<D>(p, S, acc_tok + (size_t)((l - 1) * 2 + 1) * D, p.n_fc, p.f2_bias_shift,
+                    ok = gather_acc<D>(p, acc_tok + (size_t)((l - 1) * 2 + 1) * XW, p.n_fc, p.f2_bias_shift,
                                        p.fix_h[l - 1], p.f2sb + (size_t)(l - 1) * 2 * D, 0x10u + l);
                 cp_async_wait_group<2>();          // this layer's LN parameters
                 if (cbar_or(!ok)) return;
                 if (l > 0) trace_x(p, S, t, 2 * (l - 1) + 1, S.x);
                 stamp(p, S, t, 1 + 4 * l);
                 const float *lg = S.lnp + (l & 1) * 2 * kDmax;
-                const int s = ln_limbs<D>(S.x, lg, lg + kDmax, p.eps, S.limbs, S.lane, S.warp * KBW,
-                                          (S.warp + 1) * KBW);
-                ok = rowtile_mma<KBW>(p, S, ctr, 6, 0x20u + l);
+                const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                if (l == 1) stamp(p, S, t, 57);
+                ok = rowtile_mma<KBW>(p, ctr, 6, 0x20u + l);
+                if (l == 1) stamp(p, S, t, 58);
                 if (cbar_or(!ok)) return;
+                if (l == 1) stamp(p, S, t, 59);
                 if (S.tid < 96) {
                     const int r = S.tid, part = r >> 5, i = r & 31;
                     const float y = rowtile_out(S, ctr, r, D, s);
@@ -837,13 +952,15 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 ctr += 6;
                 stamp(p, S, t, 2 + 4 * l);
                 // ---------------- attention over the own dims, then the K-split out projection
-                ok = attention(p, S, l, head, half, pos, staged, xu, p.fix_ctx[l], t);
+                ok = attention(p, l, head, half, pos, staged, xu, p.fix_ctx[l], t);
                 xu++;
                 if (cbar_or(!ok)) return;
-                ok = slice_mma_red<D>(p, S, ctr, 1, acc_o, p.o_bias_shift, 0x30u + l);
+                if (l == 1) stamp(p, S, t, 60);
+                ok = slice_mma_red<D>(p, ctr, 1, acc_o, p.o_bias_shift, 0x30u + l);
+                ctr += slice_chunks(D);
                 stamp(p, S, t, 3 + 4 * l);
                 // ---------------- x += out projection
-                ok = ok && gather_acc<D>(p, S, acc_o, 2 * H, p.o_bias_shift, p.fix_ctx[l],
+                ok = ok && gather_acc<D>(p, acc_o, 2 * H, p.o_bias_shift, p.fix_ctx[l],
                                          p.osb + (size_t)l * 2 * D, 0x40u + l);
                 if (cbar_or(!ok)) return;
                 trace_x(p, S, t, 2 * l, S.x);
@@ -851,7 +968,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             } else {
                 // ---------------- x += out projection; LN2; fc1 rows; ReLU; K-split fc2
                 cp_async_commit();                 // (keeps the group count of the head path)
-                bool ok = gather_acc<D>(p, S, acc_o, 2 * H, p.o_bias_shift, p.fix_ctx[l],
+                bool ok = gather_acc<D>(p, acc_o, 2 * H, p.o_bias_shift, p.fix_ctx[l],
                                         p.osb + (size_t)l * 2 * D, 0x40u + l);
                 cp_async_wait_group<2>();
                 if (cbar_or(!ok)) return;
@@ -859,14 +976,16 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 stamp(p, S, t, 1 + 4 * l);
                 if (is_fc) {
                     const float *lg = S.lnp + (l & 1) * 2 * kDmax;
-                    const int s = ln_limbs<D>(S.x, lg, lg + kDmax, p.eps, S.limbs, S.lane, S.warp * KBW,
-                                              (S.warp + 1) * KBW);
+                    const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                    if (l == 1) stamp(p, S, t, 57);
                     const float hsc = exp2i(p.fix_h[l]);
                     const int ntile = 2 * fc_nkb;
                     for (int t0 = 0; t0 < ntile; t0 += 6) {
                         const int nt = min(6, ntile - t0);
-                        ok = rowtile_mma<KBW>(p, S, ctr, nt, 0x50u + l);
+                        ok = rowtile_mma<KBW>(p, ctr, nt, 0x50u + l);
+                        if (l == 1) stamp(p, S, t, 58);
                         if (cbar_or(!ok)) return;
+                        if (l == 1) stamp(p, S, t, 59);
                         if (S.tid < nt * kTile) {
                             const float y = fmaxf(rowtile_out(S, ctr, S.tid, D, s), 0.0f);
                             put_limbs4(S.limbs, kSlimbOff + t0 * kTile + S.tid, bf16r(y), hsc);
@@ -876,11 +995,13 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                         ctr += nt;
                     }
                     stamp(p, S, t, 2 + 4 * l);
-                    ok = slice_mma_red<D>(p, S, ctr, fc_nkb, acc_f, p.f2_bias_shift, 0x60u + l);
+                    if (l == 1) stamp(p, S, t, 60);
+                    ok = slice_mma_red<D>(p, ctr, fc_nkb, acc_f, p.f2_bias_shift, 0x60u + l);
+                    ctr += fc_nkb * slice_chunks(D);
                     stamp(p, S, t, 3 + 4 * l);
                 }
                 // ---------------- x += fc2
-                ok = ok && gather_acc<D>(p, S, acc_f, p.n_fc, p.f2_bias_shift, p.fix_h[l],
+                ok = ok && gather_acc<D>(p, acc_f, p.n_fc, p.f2_bias_shift, p.fix_h[l],
                                          p.f2sb + (size_t)l * 2 * D, 0x70u + l);
                 if (cbar_or(!ok)) return;
                 trace_x(p, S, t, 2 * l + 1, S.x);
@@ -893,115 +1014,21 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             }
         }
         if (is_head) {
-            const bool ok = gather_acc<D>(p, S, acc_tok + (size_t)((L - 1) * 2 + 1) * D, p.n_fc, p.f2_bias_shift,
+            const bool ok = gather_acc<D>(p, acc_tok + (size_t)((L - 1) * 2 + 1) * XW, p.n_fc, p.f2_bias_shift,
                                           p.fix_h[L - 1], p.f2sb + (size_t)(L - 1) * 2 * D, 0x80u);
             if (cbar_or(!ok)) return;
             trace_x(p, S, t, 2 * L - 1, S.x);
         }
         // ---------------- final LN, LM head + greedy argmax
         if (lm_token) {
-            const uint32_t ep_lm = tau + 1u;
             cp_async_wait_all();
             cbar();
             const float *lg = S.lnp + (L & 1) * 2 * kDmax;
             float *tr = (p.trace && c == 0) ? p.trace + ((size_t)t * (2 * L + 1) + 2 * L) * D : nullptr;
-            const int s = ln_limbs<D>(S.x, lg, lg + kDmax, p.eps, S.limbs, S.lane, S.warp * KBW,
-                                      (S.warp + 1) * KBW, tr);
+            const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, tr);
             cbar();
-            const int lm_step = pos - max(p.start_pos, p.n_prompt - 1);
-            float *lrow = p.logits ? p.logits + (size_t)lm_step * V : nullptr;
-            unsigned long long best = 0ull;
-            bool ok = true;
-            const float inv = exp2i(-s);
-            const int g = S.lane >> 2, tig = S.lane & 3;
-            for (int i = S.warp; i < lm_nt; i += kConsumerWarps) {
-                if (!wait_full(p, S, ctr + i, 0x100u)) { ok = false; break; }
-                const uint8_t *ch = slot_ptr(S, ctr + i);
-                int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
-#pragma unroll 4
-                for (int kb = 0; kb < NKB_D; kb += 2) {
-                    uint32_t b0, b1, b2, b3;
-                    load_bfrag(S.limbs, 0, kb, S.lane, b0, b1);
-                    load_bfrag(S.limbs, 0, kb + 1, S.lane, b2, b3);
-                    const uint4 x0 = *reinterpret_cast<const uint4 *>(ch + kb * kFragBytes + S.lane * 16);
-                    const uint4 x1 = *reinterpret_cast<const uint4 *>(ch + (kb + 1) * kFragBytes + S.lane * 16);
-                    mma_s8_16832(a0, x0.x, x0.y, x0.z, x0.w, b0, b1);
-                    mma_s8_16832(a1, x1.x, x1.y, x1.z, x1.w, b2, b3);
-                }
-                const float *meta = reinterpret_cast<const float *>(ch + kTile * D);
-                const float2 m0 = *reinterpret_cast<const float2 *>(meta + 2 * g);
-                const float2 m1 = *reinterpret_cast<const float2 *>(meta + 2 * (g + 8));
-                __syncwarp();
-                if (S.lane == 0) mbar_arrive_cnt(&S.empty[(ctr + i) % kSlots], kConsumerWarps);
-                int v[4];
-#pragma unroll
-                for (int k = 0; k < 4; k++) v[k] = a0[k] + a1[k];
-                const int x0 = __shfl_down_sync(0xffffffffu, v[0], 1);
-                const int x1 = __shfl_down_sync(0xffffffffu, v[1], 1);
-                const int x2 = __shfl_down_sync(0xffffffffu, v[2], 1);
-                const int x3 = __shfl_down_sync(0xffffffffu, v[3], 1);
-                if (tig == 0) {
-                    const int r0 = (lm_t0 + i) * kTile + g, r1 = r0 + 8;
-                    const float y0 = __fadd_rn(
-                        __fmul_rn(__fmul_rn(__ll2float_rn(limb_dot(v[0], v[1], x0, x1)), inv), m0.x), m0.y);
-                    const float y1 = __fadd_rn(
-                        __fmul_rn(__fmul_rn(__ll2float_rn(limb_dot(v[2], v[3], x2, x3)), inv), m1.x), m1.y);
-                    // key: value order (sign-flipped bits), then the larger index (ties -> last
-                    // max, Iterator::max_by in opt125m_decode.rs:303)
-                    if (r0 < V) {
-                        if (lrow) lrow[r0] = y0;
-                        const uint32_t u = __float_as_uint(y0);
-                        const unsigned long long k =
-                            ((unsigned long long)(u & 0x80000000u ? ~u : u | 0x80000000u) << 32) | (uint32_t)r0;
-                        best = k > best ? k : best;
-                    }
-                    if (r1 < V) {
-                        if (lrow) lrow[r1] = y1;
-                        const uint32_t u = __float_as_uint(y1);
-                        const unsigned long long k =
-                            ((unsigned long long)(u & 0x80000000u ? ~u : u | 0x80000000u) << 32) | (uint32_t)r1;
-                        best = k > best ? k : best;
-                    }
-                }
-            }
+            if (!lm_head<D>(p, ctr, t, pos, tau, lm_t0, lm_nt, s)) return;
             ctr += lm_nt;
-            best = warp_max_u64(best);
-            if (S.lane == 0) S.keys[S.warp] = best;
-            if (cbar_or(!ok)) return;
-            if (S.tid == 0) {
-                unsigned long long b = 0ull;
-                for (int w = 0; w < kConsumerWarps; w++) b = S.keys[w] > b ? S.keys[w] : b;
-                ll_store(p.ll_lm + 2 * c, (uint32_t)(b >> 32), ep_lm);
-                ll_store(p.ll_lm + 2 * c + 1, (uint32_t)b, ep_lm);
-            }
-            stamp(p, S, t, 50);
-            // global argmax over all CTAs: thread q reads CTA q's key
-            unsigned long long kq = 0ull;
-            if (S.tid < G) {
-                uint64_t hi = ll_load(p.ll_lm + 2 * S.tid), lo = ll_load(p.ll_lm + 2 * S.tid + 1);
-                uint64_t t0 = 0;
-                uint32_t it = 0;
-                while ((uint32_t)(hi >> 32) != ep_lm || (uint32_t)(lo >> 32) != ep_lm) {
-                    __nanosleep(20);
-                    if ((uint32_t)(hi >> 32) != ep_lm) hi = ll_load(p.ll_lm + 2 * S.tid);
-                    if ((uint32_t)(lo >> 32) != ep_lm) lo = ll_load(p.ll_lm + 2 * S.tid + 1);
-                    if ((++it & 31) == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FLAG, 0x90u)) {
-                        ok = false;
-                        break;
-                    }
-                }
-                kq = ((unsigned long long)(uint32_t)hi << 32) | (uint32_t)lo;
-            }
-            kq = warp_max_u64(kq);
-            if (S.lane == 0) S.keys[S.warp] = kq;
-            if (cbar_or(!ok)) return;
-            if (S.tid == 0) {
-                unsigned long long b = 0ull;
-                for (int w = 0; w < kConsumerWarps; w++) b = S.keys[w] > b ? S.keys[w] : b;
-                const int bi = (int)(uint32_t)b;
-                S.flag[1] = bi;
-                if (c == 0) p.tokens[pos + 1] = bi;
-            }
             cbar();
             next_id = S.flag[1];
             stamp(p, S, t, 51);
@@ -1013,7 +1040,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
 }
 
 template <int D, int F>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) opt_decode_kernel(const DecodeParams p) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) opt_decode_kernel(const __grid_constant__ DecodeParams p) {
     Cta S = make_cta();
     if (threadIdx.x == 0) {
         for (int i = 0; i < kSlots; i++) {

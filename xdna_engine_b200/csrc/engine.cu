@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <stdexcept>
@@ -207,6 +208,14 @@ double rows_bound(const QMat &m, int n0, int n1, const float *g, const float *b,
     }
     return B * 1.01;
 }
+// integer tuning knob from the environment (default when unset or not a number)
+int env_int(const char *name, int dflt) {
+    const char *v = std::getenv(name);
+    if (!v || !*v) return dflt;
+    char *end = nullptr;
+    const long r = std::strtol(v, &end, 10);
+    return (end && *end == 0 && r > 0 && r < 1000000) ? (int)r : dflt;
+}
 int ceil_log2(int v) {
     int e = 0;
     while ((1 << e) < v) e++;
@@ -240,7 +249,7 @@ struct XdnaOptDecoder {
     XdnaDevice *dev = nullptr;
     XdnaOptConfig cfg{};
     int grid = 0, n_fc = 0, max_ctx = 0, n_pages = 0, vocab_tiles = 0;
-    int o_bias_shift = 0, f2_bias_shift = 0;
+    int o_bias_shift = 0, f2_bias_shift = 0, acc_stride = 1, poll_ns = 20;
     size_t stream_bytes = 0, token_bytes = 0;
     uint8_t *d_stream = nullptr;
     ChunkRef *d_chunks = nullptr;
@@ -545,7 +554,9 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         ck(cudaMemset(dec->d_kv, 0, kv_elems * 2), "clear kv");
 
         // exchange: accumulator words (zero) and the LM-head key words (epoch 0)
-        dec->acc_words = (size_t)kAccSlots * L * 2 * D;
+        dec->acc_stride = env_int("XDNA_OPT_ACC_STRIDE", 4);
+        dec->poll_ns = env_int("XDNA_OPT_POLL_NS", 20);
+        dec->acc_words = (size_t)kAccSlots * L * 2 * D * dec->acc_stride;
         dec->d_acc = dmalloc<unsigned long long>(dec->acc_words);
         ck(cudaMemset(dec->d_acc, 0, dec->acc_words * 8), "clear accumulators");
         dec->d_ll = dmalloc<uint64_t>(2 * (size_t)G);
@@ -641,6 +652,8 @@ int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_promp
     p.page_table = dec->d_pt;
     p.n_phys_pages = dec->n_pages;
     p.acc = dec->d_acc;
+    p.acc_stride = dec->acc_stride;
+    p.poll_ns = dec->poll_ns;
     p.ll_lm = dec->d_ll;
     p.tokens = dec->d_tokens;
     p.logits = logits_dev;
