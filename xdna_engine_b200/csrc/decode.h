@@ -121,7 +121,7 @@ struct DecodeParams {
     uint64_t timeout_ns;
     float *trace;              // optional [n_steps][2L+1][D]: residual after attention and
                                // after the FFN of each layer, then the final LN output
-    unsigned long long *timing; // optional [2][grid][64] globaltimer stamps (first 2 steps)
+    unsigned long long *timing; // optional [2][grid][128] globaltimer / clock stamps (first 2 steps)
 };
 
 }  // namespace xdna

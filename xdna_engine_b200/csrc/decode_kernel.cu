@@ -226,7 +226,12 @@ __device__ __forceinline__ void release_slot(const Cta &S, uint32_t ctr) {
 // optional phase timestamps (first two steps of a launch)
 __device__ __forceinline__ void stamp(const DecodeParams &p, const Cta &S, int t, int slot) {
     if (p.timing == nullptr || t >= 2 || S.tid != 0) return;
-    p.timing[((size_t)t * p.grid + blockIdx.x) * 64 + slot] = globaltimer_ns();
+    p.timing[((size_t)t * p.grid + blockIdx.x) * 128 + slot] = globaltimer_ns();
+}
+// SM cycle counter into slot 64 + k (same record)
+__device__ __forceinline__ void stamp_clk(const DecodeParams &p, const Cta &S, int t, int k) {
+    if (p.timing == nullptr || t >= 2 || S.tid != 0) return;
+    p.timing[((size_t)t * p.grid + blockIdx.x) * 128 + 64 + k] = clock64();
 }
 
 // e^x for x <= 0 with the reference's own 2^floor x degree-5 polynomial
@@ -885,6 +890,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             continue;
         }
         stamp(p, S, t, 0);
+        stamp_clk(p, S, t, 0);
         for (int i = S.tid; i < D; i += kConsumerThreads)
             S.x[i] = __fadd_rn(p.emb_tok[(size_t)id * D + i], p.emb_pos[(size_t)(pos + 2) * D + i]);
         // the accumulator words of token tau + 2 (last used by token tau - 2, which every CTA
@@ -927,9 +933,12 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 if (l > 0) trace_x(p, S, t, 2 * (l - 1) + 1, S.x);
                 stamp(p, S, t, 1 + 4 * l);
                 const float *lg = S.lnp + (l & 1) * 2 * kDmax;
+                if (l == 1) stamp_clk(p, S, t, 1);
                 const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                if (l == 1) stamp_clk(p, S, t, 2);
                 if (l == 1) stamp(p, S, t, 57);
                 ok = rowtile_mma<KBW>(p, ctr, 6, 0x20u + l);
+                if (l == 1) stamp_clk(p, S, t, 3);
                 if (l == 1) stamp(p, S, t, 58);
                 if (cbar_or(!ok)) return;
                 if (l == 1) stamp(p, S, t, 59);
@@ -1032,6 +1041,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             cbar();
             next_id = S.flag[1];
             stamp(p, S, t, 51);
+            stamp_clk(p, S, t, 4);
         } else {
             next_id = p.tokens[pos + 1];
         }
