@@ -98,7 +98,8 @@ int xdna_gemm_check(void);
 typedef struct {
     int n_layers, d_model, n_heads, ffn, vocab, max_pos;
     float eps;                 /* LayerNorm eps (BERT: 1e-12) */
-    int pooling;               /* 0 = CLS row, 1 = mean over valid rows (bert/head.rs:20-47) */
+    int pooling;               /* 0 = CLS row, 1 = mean over valid rows (bert/head.rs:20-47);
+                                  + 2: skip the L2 normalisation (EmbedHead normalize = false) */
 } XdnaBertConfig;
 
 typedef struct {               /* f32, linear weights [K, N] = [in, out] */
@@ -134,6 +135,13 @@ int xdna_bert_embed(XdnaBert *m, const int32_t *ids, const int32_t *seq_lens, in
  * cu [n_seqs + 1] sequence starts, out_dev [n_seqs, 768]; asynchronous on `stream`. */
 int xdna_bert_encode_device(XdnaBert *m, const int32_t *ids, const int32_t *tok_pos, const int32_t *cu,
                             int n_tokens, int n_seqs, int max_len, float *out_dev, void *stream);
+
+/* The embedding front end on its own, host only: the token ids npu_embed (include/npu_engine.h)
+ * feeds the encoder for `text` -- BERT uncased WordPiece over the vocabulary of tokenizer_path
+ * (HuggingFace tokenizer.json with a WordPiece model, or vocab.txt), [CLS] ... [SEP], truncated
+ * to max_len (rust/npu-engine/src/bert/frontend.rs:29-35).  Writes min(count, cap) ids and
+ * returns the count, or -1 with npu_last_error() set. */
+int xdna_wordpiece_encode(const char *tokenizer_path, const char *text, int max_len, int32_t *ids, int cap);
 
 /* ------------------------------------------------------------- bfp16 block format */
 /* to_bfp16_blocks of the reference's golden (route_b_kernels/ffn_bfp16/golden_ffn_gemm.py:

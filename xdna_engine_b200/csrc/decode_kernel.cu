@@ -934,8 +934,12 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 stamp(p, S, t, 1 + 4 * l);
                 const float *lg = S.lnp + (l & 1) * 2 * kDmax;
                 if (l == 1) stamp_clk(p, S, t, 1);
-                const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
                 if (l == 1) stamp_clk(p, S, t, 2);
+                if (p.timing && l == 1) {
+                    s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                    stamp_clk(p, S, t, 5);
+                }
                 if (l == 1) stamp(p, S, t, 57);
                 ok = rowtile_mma<KBW>(p, ctr, 6, 0x20u + l);
                 if (l == 1) stamp_clk(p, S, t, 3);

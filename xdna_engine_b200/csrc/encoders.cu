@@ -290,8 +290,11 @@ __global__ void __launch_bounds__(ATHREADS) attention_kernel(const uint16_t *qkv
     }
 }
 
-// out[b] = l2norm(pool(x rows of sequence b)); pooling 0 = CLS (row 0), 1 = mean
-__global__ void pool_kernel(const uint16_t *x, const int32_t *cu, int pooling, float *out) {
+// out[b] = l2norm(pool(x rows of sequence b)); pooling bit 0: 0 = CLS (row 0), 1 = mean;
+// bit 1 set: no L2 normalisation (EmbedHead with normalize = false, bert/head.rs:20-47)
+__global__ void pool_kernel(const uint16_t *x, const int32_t *cu, int pooling_flags, float *out) {
+    const int pooling = pooling_flags & 1;
+    const bool l2 = (pooling_flags & 2) == 0;
     const int b = blockIdx.x, lane = threadIdx.x;
     const int s0 = cu[b], L = cu[b + 1] - s0;
     float v[24];
@@ -317,7 +320,7 @@ __global__ void pool_kernel(const uint16_t *x, const int32_t *cu, int pooling, f
     for (int i = 0; i < 24; i++) s += v[i] * v[i];
 #pragma unroll
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const float norm = fmaxf(sqrtf(s), 1e-12f);
+    const float norm = l2 ? fmaxf(sqrtf(s), 1e-12f) : 1.0f;
 #pragma unroll
     for (int j = 0; j < 3; j++)
 #pragma unroll
@@ -401,9 +404,9 @@ XdnaBert *xdna_bert_create(XdnaDevice *dev_unused, const XdnaBertConfig *cfg, co
     }
     const XdnaBertConfig c = *cfg;
     if (c.d_model != bert::D || c.n_heads != bert::H || c.ffn != bert::F || c.n_layers < 1 || c.vocab < 1 ||
-        c.max_pos < 1 || max_tokens < 1 || max_seqs < 1 || (c.pooling != 0 && c.pooling != 1)) {
+        c.max_pos < 1 || max_tokens < 1 || max_seqs < 1 || c.pooling < 0 || c.pooling > 3) {
         set_last_error_message("xdna_bert_create: supported shape is d_model 768, 12 heads, ffn 3072 "
-                               "(BERT-base / BGE-base); pooling 0 (CLS) or 1 (mean)");
+                               "(BERT-base / BGE-base); pooling 0 (CLS) or 1 (mean), + 2 for no L2 normalisation");
         return nullptr;
     }
     auto *m = new XdnaBert();
