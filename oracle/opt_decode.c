@@ -149,20 +149,29 @@ static float warp_tree(const float *v32) {
     }
     return v[0];
 }
-/* LayerNorm as one engine warp computes it: the formula of rust/npu-asr-host/src/lib.rs:79-110
- * with lane l summing elements l + 32j in j order, then the butterfly; output rounded to
- * bf16. */
+/* LayerNorm as the engine's 8 consumer warps compute it: the formula of
+ * rust/npu-asr-host/src/lib.rs:79-110; warp w owns the 32-wide blocks [w*D/256, (w+1)*D/256),
+ * lane l sums its elements 32*kb + l in kb order, each warp adds its lanes with the butterfly,
+ * and the 8 warp sums are added in warp order; output rounded to bf16. */
 static float lane_tree(const float *x, int D, float sub_mean, int squares) {
-    float part[32];
-    for (int l = 0; l < 32; l++) {
-        float s = 0.0f;
-        for (int i = l; i < D; i += 32) {
-            if (squares) { float c = x[i] - sub_mean; s = s + c * c; }
-            else s = s + x[i];
+    /* warp w owns blocks [w*nkb/8, (w+1)*nkb/8): the engine's split for D = 256 and 768, and
+     * a defined tree for the narrower models the HuggingFace goldens use */
+    int nkb = D / 32;
+    float tot = 0.0f;
+    for (int w = 0; w < 8; w++) {
+        float part[32];
+        for (int l = 0; l < 32; l++) {
+            float s = 0.0f;
+            for (int kb = w * nkb / 8; kb < (w + 1) * nkb / 8; kb++) {
+                float v = x[32 * kb + l];
+                if (squares) { float c = v - sub_mean; s = s + c * c; }
+                else s = s + v;
+            }
+            part[l] = s;
         }
-        part[l] = s;
+        tot = tot + warp_tree(part);
     }
-    return warp_tree(part);
+    return tot;
 }
 static void ln_dev_bf16(const float *x, const float *g, const float *b, int D, float eps, float *y) {
     float mean = lane_tree(x, D, 0.0f, 0) / (float)D;

@@ -112,7 +112,8 @@ struct DecodeParams {
     unsigned long long *acc;   // [kAccSlots][L][2: out-proj, fc2][D * acc_stride] accumulator words
     int acc_stride;            // words between consecutive outputs' accumulators (spreads atomics)
     int poll_ns;               // sleep between polls of incomplete words
-    uint64_t *ll_lm;           // [grid][2] flag-tagged LM-head best keys
+    unsigned long long *lm_words; // [kAccSlots][2]: per token the max LM-head key, the CTAs counted in
+    int lm_prefetch_layer;     // layer during which the LM-head rows go to L2 (< 0: never)
     // run
     int64_t *tokens;           // [max_ctx + 1]: prompt in, generated ids out at pos+1
     float *logits;             // optional [n_steps][V] (only steps with an LM head)

@@ -61,6 +61,7 @@ static_assert(SmemMap::total <= 227 * 1024, "shared memory budget");
 static_assert(kChunkKeys * kHalfDim * 2 <= SmemMap::kvst_bytes, "key chunk fits the staging area");
 static_assert(kSliceTilesPerChunk * kFragBytes <= kSlotBytes, "slice chunk fits a slot");
 static_assert(kTile * kDmax + kTile * 8 <= kSlotBytes, "row chunk fits a slot");
+static_assert(kDmax / kTile * kFragBytes <= SmemMap::kvst_bytes, "slice epilogue scratch fits the staging area");
 
 // limb column of the K-split GEMV inputs (attention context dims / fc1 rows)
 constexpr int kSlimbOff = 1024;
@@ -194,25 +195,27 @@ __device__ __noinline__ bool wait_expired(RunState *st, uint64_t timeout_ns, int
     return false;
 }
 
-// Wait for the chunk with stream index `ctr` to be in its ring slot; false on timeout /
-// abort.  Warp-collective (all 32 lanes call it and get the same answer): lane 0 polls, and
-// after success every lane observes the completed phase itself (acquire of the copy's data).
-__device__ __forceinline__ bool wait_full(const DecodeParams &p, const Cta &S, uint32_t ctr, uint32_t where) {
-    const int slot = ctr % kSlots;
-    const uint32_t parity = (ctr / kSlots) & 1u;
-    bool ok = true;
-    if (S.lane == 0 && !mbar_try_wait(&S.full[slot], parity)) {
-        uint64_t t0 = 0;
-        uint32_t it = 0;
-        while (!mbar_try_wait(&S.full[slot], parity))
-            if ((++it & 15) == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FULL, where)) {
-                ok = false;
-                break;
-            }
+// Wait for the chunks with stream indices ctr .. ctr+n-1 (n <= kSlots) to be in their ring
+// slots; false on timeout / abort.  Warp-collective: lane i watches chunk ctr + i itself (so
+// every lane that reads a chunk has the completed phase ordered before its reads through the
+// warp-wide vote), and all lanes get the same answer.
+__device__ __forceinline__ bool wait_chunks(const DecodeParams &p, const Cta &S, uint32_t ctr, int n, uint32_t where) {
+    const uint32_t q = ctr + (uint32_t)S.lane;
+    bool mine = S.lane >= n || mbar_try_wait(&S.full[q % kSlots], (q / kSlots) & 1u);
+    if (__all_sync(0xffffffffu, mine)) return true;
+    uint64_t t0 = 0;
+    uint32_t it = 0;
+    while (true) {
+        if (!mine) mine = mbar_try_wait(&S.full[q % kSlots], (q / kSlots) & 1u);
+        if (__all_sync(0xffffffffu, mine)) return true;
+        if ((++it & 15) == 0) {
+            const bool gone = S.lane == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FULL, where);
+            if (__shfl_sync(0xffffffffu, gone, 0)) return false;
+        }
     }
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (ok) (void)mbar_try_wait(&S.full[slot], parity);
-    return ok;
+}
+__device__ __forceinline__ bool wait_full(const DecodeParams &p, const Cta &S, uint32_t ctr, uint32_t where) {
+    return wait_chunks(p, S, ctr, 1, where);
 }
 __device__ __forceinline__ const uint8_t *slot_ptr(const Cta &S, uint32_t ctr) {
     return S.ring + (ctr % kSlots) * kSlotBytes;
@@ -309,105 +312,133 @@ __device__ __forceinline__ void load_bfrag(const int8_t *L, int base, int kb, in
         b0 = b1 = 0u;
     }
 }
-// exact dot of the four limb columns: ((a * 256 + b) * 256 + c) * 256 + d
+// exact dot of the four limb columns: ((a * 256 + b) * 256 + c) * 256 + d, as two wide
+// multiply-adds.  Every dot here has K <= 768 (the host limits an FC CTA's fc2 slice to 24
+// k-blocks), so |a| <= 64 * 127 * 768 < 2^23 and |b| < 2^24: a * 256 + b fits in 32 bits.
 __device__ __forceinline__ long long limb_dot(int a, int b, int c, int d) {
-    return (((long long)a * 256 + b) * 256 + c) * 256 + d;
+    const int hi = a * 256 + b;
+    const long long lo = (long long)c * 256 + d;
+    return (long long)hi * 65536 + lo;
 }
 
-// LayerNorm of the full D-vector x by ONE warp (every warp computes it; no block barrier),
-// the formula of rust/npu-asr-host/src/lib.rs:79-110 (population variance, each op rounded)
-// with this tree: lane l sums elements l + 32j in j order, then the xor butterfly.  Output
-// rounded to bf16; the warp writes the limbs of its 32-wide blocks [kb0, kb1) (fixed point
-// from the max over the whole output) and, if `out` is given, those outputs; returns the
-// exponent.
+// LayerNorm of the D-vector x by the 8 consumer warps together, the formula of
+// rust/npu-asr-host/src/lib.rs:79-110 (population variance, each op rounded), with this tree:
+// warp w owns the 32-wide blocks [w*D/256, (w+1)*D/256) (the K range of its GEMV share), lane l
+// sums its elements 32*kb + l in kb order, the warp adds its lanes with the xor butterfly, and
+// the 8 warp sums are added in warp order.  Output rounded to bf16; the fixed-point exponent
+// comes from the max over the whole output; each warp writes the limbs of its own blocks and,
+// if `out` is given, those outputs.  Three consumer barriers; every consumer thread calls it.
 template <int D>
 __device__ __noinline__ int ln_limbs(const float *g, const float *b, float eps, float *out) {
-    constexpr int J = D / 32;
-    constexpr int KBW = J / kConsumerWarps;
+    constexpr int KBW = D / 32 / kConsumerWarps;
     const Cta S = make_cta();
-    const float *x = S.x;
-    int8_t *L = S.limbs;
     const int lane = S.lane, kb0 = S.warp * KBW;
-    float v[J];
+    float *red = S.red + 32;                      // [3][8]
+    float v[KBW];
     float s = 0.0f;
 #pragma unroll
-    for (int j = 0; j < J; j++) {
-        v[j] = x[lane + 32 * j];
-        s = __fadd_rn(s, v[j]);
+    for (int kk = 0; kk < KBW; kk++) {
+        v[kk] = S.x[32 * (kb0 + kk) + lane];
+        s = __fadd_rn(s, v[kk]);
     }
-    const float mean = __fdiv_rn(warp_sum(s), (float)D);
+    s = warp_sum(s);
+    if (lane == 0) red[S.warp] = s;
+    cbar();
+    s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) s = __fadd_rn(s, red[w]);
+    const float mean = __fdiv_rn(s, (float)D);
     float q = 0.0f;
 #pragma unroll
-    for (int j = 0; j < J; j++) {
-        const float c = __fsub_rn(v[j], mean);
+    for (int kk = 0; kk < KBW; kk++) {
+        const float c = __fsub_rn(v[kk], mean);
         q = __fadd_rn(q, __fmul_rn(c, c));
     }
-    const float var = __fdiv_rn(warp_sum(q), (float)D);
+    q = warp_sum(q);
+    if (lane == 0) red[8 + S.warp] = q;
+    cbar();
+    q = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) q = __fadd_rn(q, red[8 + w]);
+    const float var = __fdiv_rn(q, (float)D);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
     float m = 0.0f;
 #pragma unroll
-    for (int j = 0; j < J; j++) {
-        const int i = lane + 32 * j;
-        const float t = __fmul_rn(__fsub_rn(v[j], mean), inv);
-        v[j] = bf16r(__fadd_rn(__fmul_rn(t, g[i]), b[i]));
-        m = fmaxf(m, fabsf(v[j]));
+    for (int kk = 0; kk < KBW; kk++) {
+        const int i = 32 * (kb0 + kk) + lane;
+        const float t = __fmul_rn(__fsub_rn(v[kk], mean), inv);
+        v[kk] = bf16r(__fadd_rn(__fmul_rn(t, g[i]), b[i]));
+        m = fmaxf(m, fabsf(v[kk]));
     }
-    const int e = fix_exponent(warp_max_nonneg(m));
-    const float sc = exp2i(e);
-    float mine[KBW];
+    m = warp_max_nonneg(m);
+    if (lane == 0) red[16 + S.warp] = m;
+    cbar();
 #pragma unroll
-    for (int j = 0; j < J; j++)
-        if (j / KBW == S.warp) mine[j % KBW] = v[j];
+    for (int w = 0; w < kConsumerWarps; w++) m = fmaxf(m, red[16 + w]);
+    const int e = fix_exponent(m);
+    const float sc = exp2i(e);
 #pragma unroll
     for (int kk = 0; kk < KBW; kk++) {
-        put_limbs4(L, lane + 32 * (kb0 + kk), mine[kk], sc);
-        if (out) out[lane + 32 * (kb0 + kk)] = mine[kk];
+        put_limbs4(S.limbs, 32 * (kb0 + kk) + lane, v[kk], sc);
+        if (out) out[32 * (kb0 + kk) + lane] = v[kk];
     }
     __syncwarp();
     return e;
 }
 
 // ------------------------------------------------------------------------------ GEMVs
-// K-split row-tile GEMV: nt m-tiles (chunks ctr .. ctr+nt-1, one 16-row tile each, K = 32 *
-// 8 * KBW) against the limbs at column 0; warp w covers k-blocks [w*KBW, (w+1)*KBW).  Partial
-// limb sums go to S.part[warp][row][limb]; the caller combines them after a consumer
-// barrier.  The slots stay owned (their meta is read by the combine) until release_tiles.
-template <int KBW>
-__device__ __noinline__ bool rowtile_mma(const DecodeParams &p, uint32_t ctr, int nt, uint32_t where) {
-    const Cta S = make_cta();
-    const int g = S.lane >> 2, tig = S.lane & 3;
-    uint32_t bf[KBW][2];
-#pragma unroll
-    for (int kk = 0; kk < KBW; kk++) load_bfrag(S.limbs, 0, S.warp * KBW + kk, S.lane, bf[kk][0], bf[kk][1]);
-    for (int t = 0; t < nt; t++) {
-        if (!wait_full(p, S, ctr + t, where)) return false;
-        const uint8_t *ch = slot_ptr(S, ctr + t);
-        int acc[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int kk = 0; kk < KBW; kk++) {
-            const uint4 a = *reinterpret_cast<const uint4 *>(ch + (S.warp * KBW + kk) * kFragBytes + S.lane * 16);
-            mma_s8_16832(acc, a.x, a.y, a.z, a.w, bf[kk][0], bf[kk][1]);
-        }
-        if (tig < 2) {
-            int *pp = S.part + ((S.warp * SmemMap::part_rows + t * kTile + g) * 4 + tig * 2);
-            *reinterpret_cast<int2 *>(pp) = make_int2(acc[0], acc[1]);
-            *reinterpret_cast<int2 *>(pp + 8 * 4) = make_int2(acc[2], acc[3]);
-        }
+// Exact dot of one 16-row tile (chunk `ch`, K = 32 * NKB, fragment order) with the limbs at
+// column 0, by one warp over the whole K (two accumulation chains).  Lanes with tig == 0 get
+// the exact sums of rows g and g + 8 in P0, P1.
+template <int NKB>
+__device__ __forceinline__ void tile_dot(const Cta &S, const uint8_t *ch, long long &P0, long long &P1) {
+    int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+#pragma unroll 4
+    for (int kb = 0; kb < NKB; kb += 2) {
+        uint32_t b0, b1, b2, b3;
+        load_bfrag(S.limbs, 0, kb, S.lane, b0, b1);
+        load_bfrag(S.limbs, 0, kb + 1, S.lane, b2, b3);
+        const uint4 x0 = *reinterpret_cast<const uint4 *>(ch + kb * kFragBytes + S.lane * 16);
+        const uint4 x1 = *reinterpret_cast<const uint4 *>(ch + (kb + 1) * kFragBytes + S.lane * 16);
+        mma_s8_16832(a0, x0.x, x0.y, x0.z, x0.w, b0, b1);
+        mma_s8_16832(a1, x1.x, x1.y, x1.z, x1.w, b2, b3);
     }
+    int v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) v[k] = a0[k] + a1[k];
+    const int x0 = __shfl_down_sync(0xffffffffu, v[0], 1);
+    const int x1 = __shfl_down_sync(0xffffffffu, v[1], 1);
+    const int x2 = __shfl_down_sync(0xffffffffu, v[2], 1);
+    const int x3 = __shfl_down_sync(0xffffffffu, v[3], 1);
+    P0 = limb_dot(v[0], v[1], x0, x1);
+    P1 = limb_dot(v[2], v[3], x2, x3);
+}
+
+// Row-tile GEMV with one warp per tile: warp w < nt takes chunk ctr + w (16 output rows, K =
+// 32 * NKB) against the limbs at column 0 (all of them: the caller puts a consumer barrier
+// after the LayerNorm).  Lanes with tig == 0 of warp w get y0 / y1 for rows 16w + g and
+// 16w + g + 8: float(exact dot) * 2^-s * scale + bias.  No cross-warp partial sums.  The
+// slots stay owned until release_tiles.
+template <int NKB>
+__device__ __noinline__ bool rowtile_warp(const DecodeParams &p, uint32_t ctr, int nt, int s, uint32_t where,
+                                          float *y) {
+    const Cta S = make_cta();
+    if (S.warp >= nt) return true;
+    if (!wait_chunks(p, S, ctr + S.warp, 1, where)) return false;
+    const uint8_t *ch = slot_ptr(S, ctr + S.warp);
+    long long P0, P1;
+    tile_dot<NKB>(S, ch, P0, P1);
+    const int g = S.lane >> 2;
+    const float *meta = reinterpret_cast<const float *>(ch + kTile * NKB * 32);
+    const float2 m0 = *reinterpret_cast<const float2 *>(meta + 2 * g);
+    const float2 m1 = *reinterpret_cast<const float2 *>(meta + 2 * (g + 8));
+    const float inv = exp2i(-s);
+    y[0] = __fadd_rn(__fmul_rn(__fmul_rn(__ll2float_rn(P0), inv), m0.x), m0.y);
+    y[1] = __fadd_rn(__fmul_rn(__fmul_rn(__ll2float_rn(P1), inv), m1.x), m1.y);
     return true;
 }
-// exact output row r of the K-split row-tile GEMV: float(sum) * 2^-s * scale + bias
-__device__ __forceinline__ float rowtile_out(const Cta &S, uint32_t ctr, int r, int K, int s) {
-    int a = 0, b = 0, c = 0, d = 0;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) {
-        const int4 v = *reinterpret_cast<const int4 *>(S.part + (w * SmemMap::part_rows + r) * 4);
-        a += v.x; b += v.y; c += v.z; d += v.w;
-    }
-    const float *meta = reinterpret_cast<const float *>(slot_ptr(S, ctr + r / kTile) + kTile * K);
-    const float y = __fmul_rn(__ll2float_rn(limb_dot(a, b, c, d)), exp2i(-s));
-    return __fadd_rn(__fmul_rn(y, meta[2 * (r % kTile)]), meta[2 * (r % kTile) + 1]);
-}
+
+// release the nt row-tile slots from ctr: one arrival per warp on each
 __device__ __forceinline__ void release_tiles(const Cta &S, uint32_t ctr, int nt) {
     __syncwarp();
     if (S.lane == 0)
@@ -419,7 +450,8 @@ __device__ __forceinline__ void release_tiles(const Cta &S, uint32_t ctr, int nt
 // Each output's exact partial is added as (partial + 2^bshift + 2^56) into words[n].
 template <int D>
 __device__ __noinline__ bool slice_mma_red(const DecodeParams &p, uint32_t ctr, int nkb,
-                                           unsigned long long *words, int bshift, uint32_t where) {
+                                           unsigned long long *words, int bshift, uint32_t where,
+                                           unsigned long long *clk = nullptr) {
     const Cta S = make_cta();
     constexpr int NT = D / kTile / kConsumerWarps;       // m-tiles per warp
     const int nch = slice_chunks(D);
@@ -429,8 +461,9 @@ __device__ __noinline__ bool slice_mma_red(const DecodeParams &p, uint32_t ctr, 
     for (int kb = 0; kb < nkb; kb++) {
         uint32_t b0, b1;
         load_bfrag(S.limbs, kSlimbOff, kb, S.lane, b0, b1);
+        if (!wait_chunks(p, S, ctr, nch, where)) return false;
+        if (clk && S.tid == 0 && kb == 0) clk[0] = clock64();
         for (int c = 0; c < nch; c++) {
-            if (!wait_full(p, S, ctr, where)) return false;
             const uint8_t *ch = slot_ptr(S, ctr);
 #pragma unroll
             for (int i = 0; i < NT; i++) {
@@ -445,22 +478,25 @@ __device__ __noinline__ bool slice_mma_red(const DecodeParams &p, uint32_t ctr, 
             ctr++;
         }
     }
-    const int g = S.lane >> 2, tig = S.lane & 3;
-    const unsigned long long add = (1ull << bshift) + (1ull << kCountShift);
+    if (clk && S.tid == 0) clk[1] = clock64();
+    // Each lane parks its fragments (rows g / g + 8, limb pairs by tig) in the warp's scratch
+    // with full-width stores; then lane L of round q owns output row L % 16 of tile 2q + L / 16
+    // and gathers its four limb sums, so every red below is a full, coalesced warp operation.
+    int4 *scr = reinterpret_cast<int4 *>(S.kst) + S.warp * NT * 32;
 #pragma unroll
-    for (int i = 0; i < NT; i++) {
-        const int tile = S.warp + kConsumerWarps * i;
-        const int x0 = __shfl_down_sync(0xffffffffu, acc[i][0], 1);
-        const int x1 = __shfl_down_sync(0xffffffffu, acc[i][1], 1);
-        const int x2 = __shfl_down_sync(0xffffffffu, acc[i][2], 1);
-        const int x3 = __shfl_down_sync(0xffffffffu, acc[i][3], 1);
-        if (tig == 0) {
-            const int n = tile * kTile + g;
-            red_add_u64(words + (size_t)n * p.acc_stride, (unsigned long long)limb_dot(acc[i][0], acc[i][1], x0, x1) + add);
-            red_add_u64(words + (size_t)(n + 8) * p.acc_stride,
-                        (unsigned long long)limb_dot(acc[i][2], acc[i][3], x2, x3) + add);
-        }
+    for (int i = 0; i < NT; i++) scr[i * 32 + S.lane] = make_int4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    __syncwarp();
+    const unsigned long long add = (1ull << bshift) + (1ull << kCountShift);
+    const int r = S.lane & 15, gg = r & 7, hi = r >> 3;
+#pragma unroll
+    for (int q = 0; q < NT / 2; q++) {
+        const int i = 2 * q + (S.lane >> 4);
+        const int2 lo2 = reinterpret_cast<const int2 *>(scr + i * 32 + 4 * gg)[hi];       // limbs 0, 1
+        const int2 hi2 = reinterpret_cast<const int2 *>(scr + i * 32 + 4 * gg + 1)[hi];   // limbs 2, 3
+        const int n = (S.warp + kConsumerWarps * i) * kTile + r;
+        red_add_u64(words + (size_t)n * p.acc_stride, (unsigned long long)limb_dot(lo2.x, lo2.y, hi2.x, hi2.y) + add);
     }
+    __syncwarp();
     return true;
 }
 
@@ -707,7 +743,6 @@ __device__ __noinline__ bool lm_head(const DecodeParams &p, uint32_t ctr, int t,
     const Cta S = make_cta();
     constexpr int NKB_D = D / 32;
     const int c = blockIdx.x, G = p.grid, V = p.vocab;
-    const uint32_t ep_lm = tau + 1u;
     const int lm_step = pos - max(p.start_pos, p.n_prompt - 1);
     float *lrow = p.logits ? p.logits + (size_t)lm_step * V : nullptr;
     unsigned long long best = 0ull;
@@ -767,40 +802,35 @@ __device__ __noinline__ bool lm_head(const DecodeParams &p, uint32_t ctr, int t,
     best = warp_max_u64(best);
     if (S.lane == 0) S.keys[S.warp] = best;
     if (cbar_or(!ok)) return false;
+    // global argmax: every CTA folds its best key into the token's max word, then counts
+    // itself in with release order; one thread per CTA waits for the count to reach G
+    unsigned long long *lmw = p.lm_words + 2 * (tau % kAccSlots);
     if (S.tid == 0) {
         unsigned long long b = 0ull;
         for (int w = 0; w < kConsumerWarps; w++) b = S.keys[w] > b ? S.keys[w] : b;
-        ll_store(p.ll_lm + 2 * c, (uint32_t)(b >> 32), ep_lm);
-        ll_store(p.ll_lm + 2 * c + 1, (uint32_t)b, ep_lm);
+        atomicMax(lmw, b);
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(lmw + 1) : "memory");
     }
     stamp(p, S, t, 50);
-    // global argmax over all CTAs: thread q reads CTA q's key
-    unsigned long long kq = 0ull;
-    if (S.tid < G) {
-        uint64_t hi = ll_load(p.ll_lm + 2 * S.tid), lo = ll_load(p.ll_lm + 2 * S.tid + 1);
+    if (S.tid == 0) {
         uint64_t t0 = 0;
         uint32_t it = 0;
-        while ((uint32_t)(hi >> 32) != ep_lm || (uint32_t)(lo >> 32) != ep_lm) {
-            __nanosleep(20);
-            if ((uint32_t)(hi >> 32) != ep_lm) hi = ll_load(p.ll_lm + 2 * S.tid);
-            if ((uint32_t)(lo >> 32) != ep_lm) lo = ll_load(p.ll_lm + 2 * S.tid + 1);
+        unsigned long long n;
+        while (true) {
+            asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(n) : "l"(lmw + 1) : "memory");
+            if (n >= (unsigned long long)G) break;
+            __nanosleep(32);
             if ((++it & 31) == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FLAG, 0x90u)) {
                 ok = false;
                 break;
             }
         }
-        kq = ((unsigned long long)(uint32_t)hi << 32) | (uint32_t)lo;
-    }
-    kq = warp_max_u64(kq);
-    if (S.lane == 0) S.keys[S.warp] = kq;
-    if (cbar_or(!ok)) return false;
-    if (S.tid == 0) {
-        unsigned long long b = 0ull;
-        for (int w = 0; w < kConsumerWarps; w++) b = S.keys[w] > b ? S.keys[w] : b;
+        const unsigned long long b = ld_relaxed_u64(lmw);
         const int bi = (int)(uint32_t)b;
         S.flag[1] = bi;
-        if (c == 0) p.tokens[pos + 1] = bi;
+        if (ok && c == 0) p.tokens[pos + 1] = bi;
     }
+    if (cbar_or(!ok)) return false;
     return true;
 }
 
@@ -820,12 +850,16 @@ __device__ __forceinline__ void producer(const DecodeParams &p, Cta &S) {
             if (k > 0 && !mbar_try_wait(&S.empty[slot], (k - 1) & 1u)) {
                 uint64_t t0 = 0;
                 uint32_t it = 0;
-                while (!mbar_try_wait(&S.empty[slot], (k - 1) & 1u))
+                // the producer runs a layer or more ahead of its consumers, so it can back off
+                // between polls and leave the issue slots to them
+                while (!mbar_try_wait(&S.empty[slot], (k - 1) & 1u)) {
+                    __nanosleep(200);
                     if ((++it & 15) == 0 &&
                         wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_EMPTY, 0x400u)) {
                         failed = true;
                         break;
                     }
+                }
                 if (failed) break;
             }
             const ChunkRef ch = tab[i];
@@ -853,7 +887,6 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
     const int fci = c - 2 * H;
     const bool is_fc = !is_head && fci < p.n_fc;
     constexpr int NKB_D = D / 32;
-    constexpr int KBW = NKB_D / kConsumerWarps;          // k-blocks per warp for K = D
     const int fc_kb_begin = is_fc ? fc_kb0(fci, F / 32, p.n_fc) : 0;
     const int fc_nkb = is_fc ? fc_kb0(fci + 1, F / 32, p.n_fc) - fc_kb_begin : 0;
     const uint32_t tok0 = p.state->tok_base;
@@ -903,6 +936,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             unsigned long long *z = p.acc + (size_t)((tau + 2) % kAccSlots) * W;
             const size_t z0 = W * zi / nz, z1 = W * (zi + 1) / nz;
             for (size_t i = z0 + S.tid; i < z1; i += kConsumerThreads) z[i] = 0ull;
+            if (zi == 0 && S.tid < 2) p.lm_words[2 * ((tau + 2) % kAccSlots) + S.tid] = 0ull;
             __threadfence();
         }
         const float *ln_first = is_head ? p.ln : p.ln + 2 * D;
@@ -934,30 +968,31 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 stamp(p, S, t, 1 + 4 * l);
                 const float *lg = S.lnp + (l & 1) * 2 * kDmax;
                 if (l == 1) stamp_clk(p, S, t, 1);
-                int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                cbar();                            // every warp's GEMV reads all limbs
                 if (l == 1) stamp_clk(p, S, t, 2);
-                if (p.timing && l == 1) {
-                    s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
-                    stamp_clk(p, S, t, 5);
-                }
                 if (l == 1) stamp(p, S, t, 57);
-                ok = rowtile_mma<KBW>(p, ctr, 6, 0x20u + l);
+                float y[2];
+                ok = rowtile_warp<D / 32>(p, ctr, 6, s, 0x20u + l, y);
                 if (l == 1) stamp_clk(p, S, t, 3);
                 if (l == 1) stamp(p, S, t, 58);
-                if (cbar_or(!ok)) return;
-                if (l == 1) stamp(p, S, t, 59);
-                if (S.tid < 96) {
-                    const int r = S.tid, part = r >> 5, i = r & 31;
-                    const float y = rowtile_out(S, ctr, r, D, s);
-                    if (part == 0) {
-                        S.qf[i] = bf16r(__fmul_rn(y, 0.125f));
-                    } else {
-                        const uint16_t bits = (uint16_t)bf16bits(y);
-                        p.kv[kv_index(p, l, S.pt[pos / kPageTokens], head, half, part - 1, pos % kPageTokens) + i] = bits;
-                        if (part == 1) S.kcur[(((i >> 3) ^ (pos & 3)) << 3) + (i & 7)] = bits;
-                        else S.vcur[i] = bits;
+                // rows 16w + g and 16w + g + 8 of q | k | v (32 own dims each)
+                if (ok && S.warp < 6 && (S.lane & 3) == 0) {
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        const int r = S.warp * kTile + (S.lane >> 2) + 8 * h2, part = r >> 5, i = r & 31;
+                        if (part == 0) {
+                            S.qf[i] = bf16r(__fmul_rn(y[h2], 0.125f));
+                        } else {
+                            const uint16_t bits = (uint16_t)bf16bits(y[h2]);
+                            p.kv[kv_index(p, l, S.pt[pos / kPageTokens], head, half, part - 1, pos % kPageTokens) + i] = bits;
+                            if (part == 1) S.kcur[(((i >> 3) ^ (pos & 3)) << 3) + (i & 7)] = bits;
+                            else S.vcur[i] = bits;
+                        }
                     }
                 }
+                if (cbar_or(!ok)) return;
+                if (l == 1) stamp(p, S, t, 59);
                 if (S.tid == 0) mbar_arrive_expect_tx(&S.xchg[xu & 1], 4u * (pos + 1));
                 cp_async_wait_all();               // staged K / V rows
                 cbar();
@@ -969,7 +1004,10 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 xu++;
                 if (cbar_or(!ok)) return;
                 if (l == 1) stamp(p, S, t, 60);
-                ok = slice_mma_red<D>(p, ctr, 1, acc_o, p.o_bias_shift, 0x30u + l);
+                if (l == 1) stamp_clk(p, S, t, 10);
+                ok = slice_mma_red<D>(p, ctr, 1, acc_o, p.o_bias_shift, 0x30u + l,
+                                      (p.timing && l == 1 && t < 2) ? p.timing + ((size_t)t * p.grid + blockIdx.x) * 128 + 75 : nullptr);
+                if (l == 1) stamp_clk(p, S, t, 13);
                 ctr += slice_chunks(D);
                 stamp(p, S, t, 3 + 4 * l);
                 // ---------------- x += out projection
@@ -990,20 +1028,22 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 if (is_fc) {
                     const float *lg = S.lnp + (l & 1) * 2 * kDmax;
                     const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                    cbar();                        // every warp's GEMV reads all limbs
                     if (l == 1) stamp(p, S, t, 57);
                     const float hsc = exp2i(p.fix_h[l]);
                     const int ntile = 2 * fc_nkb;
-                    for (int t0 = 0; t0 < ntile; t0 += 6) {
-                        const int nt = min(6, ntile - t0);
-                        ok = rowtile_mma<KBW>(p, ctr, nt, 0x50u + l);
+                    for (int t0 = 0; t0 < ntile; t0 += kConsumerWarps) {
+                        const int nt = min(kConsumerWarps, ntile - t0);
+                        float y[2];
+                        ok = rowtile_warp<D / 32>(p, ctr, nt, s, 0x50u + l, y);
+                        if (ok && S.warp < nt && (S.lane & 3) == 0) {
+                            const int r = (t0 + S.warp) * kTile + (S.lane >> 2);
+                            put_limbs4(S.limbs, kSlimbOff + r, bf16r(fmaxf(y[0], 0.0f)), hsc);
+                            put_limbs4(S.limbs, kSlimbOff + r + 8, bf16r(fmaxf(y[1], 0.0f)), hsc);
+                        }
                         if (l == 1) stamp(p, S, t, 58);
                         if (cbar_or(!ok)) return;
                         if (l == 1) stamp(p, S, t, 59);
-                        if (S.tid < nt * kTile) {
-                            const float y = fmaxf(rowtile_out(S, ctr, S.tid, D, s), 0.0f);
-                            put_limbs4(S.limbs, kSlimbOff + t0 * kTile + S.tid, bf16r(y), hsc);
-                        }
-                        cbar();
                         release_tiles(S, ctr, nt);
                         ctr += nt;
                     }
@@ -1021,7 +1061,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 stamp(p, S, t, 4 + 4 * l);
             }
             // the LM-head rows of this CTA go to L2 a few layers before they are needed
-            if (l == max(0, L - 4) && lm_token && S.tid < lm_nt) {
+            if (l == p.lm_prefetch_layer && lm_token && S.tid < lm_nt) {
                 const ChunkRef ch = p.chunks[(size_t)c * p.chunk_stride + p.n_layer_chunks[c] + S.tid];
                 prefetch_l2(p.stream + ch.off, ch.bytes);
             }
@@ -1031,6 +1071,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                                           p.fix_h[L - 1], p.f2sb + (size_t)(L - 1) * 2 * D, 0x80u);
             if (cbar_or(!ok)) return;
             trace_x(p, S, t, 2 * L - 1, S.x);
+            stamp(p, S, t, 49);
         }
         // ---------------- final LN, LM head + greedy argmax
         if (lm_token) {

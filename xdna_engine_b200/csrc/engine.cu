@@ -249,7 +249,7 @@ struct XdnaOptDecoder {
     XdnaDevice *dev = nullptr;
     XdnaOptConfig cfg{};
     int grid = 0, n_fc = 0, max_ctx = 0, n_pages = 0, vocab_tiles = 0;
-    int o_bias_shift = 0, f2_bias_shift = 0, acc_stride = 1, poll_ns = 20;
+    int o_bias_shift = 0, f2_bias_shift = 0, acc_stride = 1, poll_ns = 20, lm_prefetch_layer = 0;
     size_t stream_bytes = 0, token_bytes = 0;
     uint8_t *d_stream = nullptr;
     ChunkRef *d_chunks = nullptr;
@@ -262,7 +262,7 @@ struct XdnaOptDecoder {
     int *d_pt = nullptr;
     unsigned long long *d_acc = nullptr;
     size_t acc_words = 0;
-    uint64_t *d_ll = nullptr;
+    unsigned long long *d_ll = nullptr;
     int64_t *d_tokens = nullptr;
     RunState *d_state = nullptr;
     float *d_logits = nullptr;      // scratch for xdna_opt_generate
@@ -428,10 +428,13 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         G &= ~1;
         const int KB = F / 32;
         if (G < 2 * H + 1) throw std::runtime_error("grid too small: needs 2 * n_heads CTAs plus FC CTAs");
-        const int n_fc = std::min(G - 2 * H, KB);
+        // FC CTAs: at most one per 32-row block of fc1; fewer CTAs each own more blocks and add
+        // fewer partial sums into each fc2 accumulator word
+        const int n_fc = std::min(std::min(G - 2 * H, KB), env_int("XDNA_OPT_FC_CTAS", KB));
         int max_nkb = 0;
         for (int i = 0; i < n_fc; i++) max_nkb = std::max(max_nkb, fc_kb0(i + 1, KB, n_fc) - fc_kb0(i, KB, n_fc));
-        if (max_nkb > 64) throw std::runtime_error("grid too small: an FC CTA would own more than 2048 fc1 rows");
+        // the exact limb combination keeps a * 256 + b in 32 bits for reduction lengths up to 768
+        if (max_nkb > 24) throw std::runtime_error("grid too small: an FC CTA would own more than 768 fc1 rows");
         dec->grid = G;
         dec->n_fc = n_fc;
         dec->o_bias_shift = 43;
@@ -554,13 +557,15 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         ck(cudaMemset(dec->d_kv, 0, kv_elems * 2), "clear kv");
 
         // exchange: accumulator words (zero) and the LM-head key words (epoch 0)
-        dec->acc_stride = env_int("XDNA_OPT_ACC_STRIDE", 4);
+        dec->acc_stride = env_int("XDNA_OPT_ACC_STRIDE", 1);
         dec->poll_ns = env_int("XDNA_OPT_POLL_NS", 20);
+        dec->lm_prefetch_layer = std::max(0, L - 4);
+        if (const char *e = std::getenv("XDNA_OPT_LM_PREFETCH_LAYER")) dec->lm_prefetch_layer = std::atoi(e);
         dec->acc_words = (size_t)kAccSlots * L * 2 * D * dec->acc_stride;
         dec->d_acc = dmalloc<unsigned long long>(dec->acc_words);
         ck(cudaMemset(dec->d_acc, 0, dec->acc_words * 8), "clear accumulators");
-        dec->d_ll = dmalloc<uint64_t>(2 * (size_t)G);
-        ck(cudaMemset(dec->d_ll, 0, 2 * (size_t)G * 8), "clear exchange words");
+        dec->d_ll = dmalloc<unsigned long long>(2 * kAccSlots);
+        ck(cudaMemset(dec->d_ll, 0, 2 * kAccSlots * 8), "clear LM-head words");
 
         dec->d_tokens = dmalloc<int64_t>(max_ctx + 1);
         ck(cudaMemset(dec->d_tokens, 0, (max_ctx + 1) * sizeof(int64_t)), "clear tokens");
@@ -654,7 +659,8 @@ int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_promp
     p.acc = dec->d_acc;
     p.acc_stride = dec->acc_stride;
     p.poll_ns = dec->poll_ns;
-    p.ll_lm = dec->d_ll;
+    p.lm_words = dec->d_ll;
+    p.lm_prefetch_layer = dec->lm_prefetch_layer;
     p.tokens = dec->d_tokens;
     p.logits = logits_dev;
     p.start_pos = start_pos;
@@ -700,6 +706,7 @@ int xdna_opt_sync(XdnaOptDecoder *dec, void *stream) {
         rs.tok_base += 1u << 20;
         rs.error = rs.error_cta = rs.error_where = 0;
         cudaMemset(dec->d_acc, 0, dec->acc_words * 8);
+        cudaMemset(dec->d_ll, 0, 2 * kAccSlots * 8);
         cudaMemcpy(dec->d_state, &rs, sizeof(rs), cudaMemcpyHostToDevice);
         return -1;
     }
