@@ -149,13 +149,14 @@ static float warp_tree(const float *v32) {
     }
     return v[0];
 }
-/* LayerNorm as the engine's 8 consumer warps compute it: the formula of
- * rust/npu-asr-host/src/lib.rs:79-110; warp w owns the 32-wide blocks [w*D/256, (w+1)*D/256),
- * lane l sums its elements 32*kb + l in kb order, each warp adds its lanes with the butterfly,
- * and the 8 warp sums are added in warp order; output rounded to bf16. */
-static float lane_tree(const float *x, int D, float sub_mean, int squares) {
-    /* warp w owns blocks [w*nkb/8, (w+1)*nkb/8): the engine's split for D = 256 and 768, and
-     * a defined tree for the narrower models the HuggingFace goldens use */
+/* LayerNorm as the engine's 8 consumer warps compute it: warp w owns the 32-wide blocks
+ * [w*nkb/8, (w+1)*nkb/8) (nkb = D/32: the engine's split for D = 256 and 768, and a defined
+ * tree for the narrower models the HuggingFace goldens use); lane l adds its elements
+ * 32*kb + l in kb order (sum and sum of squares in the same pass), each warp adds its lanes
+ * with the butterfly, and the 8 warp totals are added in warp order; mean = S1 / D,
+ * var = max(S2 / D - mean^2, 0), y = bf16((x - mean) * (1 / sqrt(var + eps)) * g + b)
+ * (rust/npu-asr-host/src/lib.rs:79-110 in single-pass form). */
+static float lane_tree(const float *x, int D, int squares) {
     int nkb = D / 32;
     float tot = 0.0f;
     for (int w = 0; w < 8; w++) {
@@ -164,8 +165,7 @@ static float lane_tree(const float *x, int D, float sub_mean, int squares) {
             float s = 0.0f;
             for (int kb = w * nkb / 8; kb < (w + 1) * nkb / 8; kb++) {
                 float v = x[32 * kb + l];
-                if (squares) { float c = v - sub_mean; s = s + c * c; }
-                else s = s + v;
+                s = squares ? s + v * v : s + v;
             }
             part[l] = s;
         }
@@ -174,8 +174,9 @@ static float lane_tree(const float *x, int D, float sub_mean, int squares) {
     return tot;
 }
 static void ln_dev_bf16(const float *x, const float *g, const float *b, int D, float eps, float *y) {
-    float mean = lane_tree(x, D, 0.0f, 0) / (float)D;
-    float var = lane_tree(x, D, mean, 1) / (float)D;
+    float mean = lane_tree(x, D, 0) / (float)D;
+    float var = lane_tree(x, D, 1) / (float)D - mean * mean;
+    var = fmaxf(var, 0.0f);
     float inv = 1.0f / sqrtf(var + eps);
     for (int i = 0; i < D; i++) {
         float t0 = (x[i] - mean) * inv;
@@ -186,17 +187,18 @@ static void ln_dev_bf16(const float *x, const float *g, const float *b, int D, f
 
 /* ---- 29-bit fixed point (the engine's GEMV input) ---------------------------------- */
 #define FIX_BITS 29
-/* exponent s with max|x| * 2^s < 2^29 (29 when max|x| < 2^-96) */
-static int fix_of_max(float m) {
-    uint32_t u;
-    memcpy(&u, &m, 4);
-    int E = m >= 0x1p-96f ? (int)((u >> 23) & 0xff) - 126 : 0;
+/* data-independent exponent of a LayerNorm output: |y_k| <= sqrt(D) |g_k| + |b_k| (1% margin);
+ * the same double arithmetic as the engine */
+static int fix_of_ln(const float *g, const float *b, int D) {
+    double B = 0.0;
+    for (int k = 0; k < D; k++) {
+        double v = (sqrt((double)D) * fabs((double)g[k]) + fabs((double)b[k])) * 1.01;
+        if (v > B) B = v;
+    }
+    if (!(B > 0.0)) return FIX_BITS;
+    int E = 0;
+    frexp(B, &E);
     return FIX_BITS - E;
-}
-static int fix_of_vec(const float *x, int n) {
-    float m = 0.0f;
-    for (int i = 0; i < n; i++) m = fmaxf(m, fabsf(x[i]));
-    return fix_of_max(m);
 }
 /* X = rint(x * 2^s), clamped to +-(2^30 - 64) */
 static int32_t to_fix(float x, int s) {
@@ -343,7 +345,7 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
         lin_t *lin = m->lins + l * 6;
         if (dev) ln_dev_bf16(x, ly->ln1_w, ly->ln1_b, D, c->eps, h);
         else or_layer_norm(x, ly->ln1_w, ly->ln1_b, 1, D, c->eps, h);
-        int sx = dev ? fix_of_vec(h, D) : 0;
+        int sx = dev ? fix_of_ln(ly->ln1_w, ly->ln1_b, D) : 0;
         lin_apply(m, &lin[0], h, sx, q);
         lin_apply(m, &lin[1], h, sx, kn);
         lin_apply(m, &lin[2], h, sx, vn);
@@ -380,7 +382,7 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
         trace_x(m, pos, 2 * l, xr);
         if (dev) ln_dev_bf16(xr, ly->ln2_w, ly->ln2_b, D, c->eps, h);
         else or_layer_norm(xr, ly->ln2_w, ly->ln2_b, 1, D, c->eps, h);
-        lin_apply(m, &lin[4], h, dev ? fix_of_vec(h, D) : 0, f);
+        lin_apply(m, &lin[4], h, dev ? fix_of_ln(ly->ln2_w, ly->ln2_b, D) : 0, f);
         for (int i = 0; i < F; i++) f[i] = f[i] > 0.0f ? f[i] : 0.0f;
         if (dev) or_bf16_round_n(f, f, (size_t)F);
         lin_apply(m, &lin[5], f, dev ? m->fix_h[l] : 0, o);
@@ -392,7 +394,7 @@ static void opt_step(or_opt *m, int64_t id, int pos, float *logits, int want_log
         else or_layer_norm(x, m->w.lnf_w, m->w.lnf_b, 1, D, c->eps, h);
         if (dev) {
             trace_x(m, pos, 2 * c->n_layers, h);
-            gemv_fix(m, m->lm_q, m->lm_scale, NULL, D, V, h, fix_of_vec(h, D), logits);
+            gemv_fix(m, m->lm_q, m->lm_scale, NULL, D, V, h, fix_of_ln(m->w.lnf_w, m->w.lnf_b, D), logits);
         } else {
 #pragma omp parallel for num_threads(m->nthreads) schedule(static)
             for (int v = 0; v < V; v++) {

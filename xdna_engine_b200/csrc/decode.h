@@ -33,6 +33,7 @@ constexpr int kMaxPages = kMaxCtx / kPageTokens;
 constexpr int kStageKeys = 256;                   // cached keys staged once per layer (fast path)
 constexpr int kChunkKeys = 512;                   // keys per staged chunk beyond that
 constexpr int kAccSlots = 4;                      // token ring of the accumulator words
+constexpr int kMaxSubs = 8;                       // accumulator sub-words per output
 constexpr int kLimbs = 4;                         // X = a*2^24 + b*2^16 + c*2^8 + d
 constexpr int kLimbStride = kFmax + 16;           // bytes per limb row (bank offset 4 words)
 constexpr int kTile = 16;                         // output rows of one MMA m-tile
@@ -103,14 +104,18 @@ struct DecodeParams {
     const float *f2sb;         // [L][2][D]: fc2 scale, bias
     const int *fix_ctx;        // [L] fixed-point exponent of the attention context (out-proj input)
     const int *fix_h;          // [L] fixed-point exponent of the fc1 output (fc2 input)
+    const int *fix_ln1;        // [L] fixed-point exponents of the LayerNorm outputs (q|k|v input)
+    const int *fix_ln2;        // [L] (fc1 input)
+    int fix_lnf;               // final LayerNorm (LM-head input)
     int o_bias_shift, f2_bias_shift;
     // paged KV cache: [L][phys_page][H][2 halves][K|V][64 positions][32 dims] bf16
     uint16_t *kv;
     const int *page_table;     // logical page -> physical page
     int n_phys_pages;
     // exchange
-    unsigned long long *acc;   // [kAccSlots][L][2: out-proj, fc2][D * acc_stride] accumulator words
-    int acc_stride;            // words between consecutive outputs' accumulators (spreads atomics)
+    unsigned long long *acc;   // [kAccSlots][L][2: out-proj, fc2][kMaxSubs][D] accumulator words
+    int o_subs, f2_subs;       // sub-words per output (contributor i adds into sub-word i % subs,
+                               // so fewer atomics meet on one address; readers add the sub-words)
     int poll_ns;               // sleep between polls of incomplete words
     unsigned long long *lm_words; // [kAccSlots][2]: per token the max LM-head key, the CTAs counted in
     int lm_prefetch_layer;     // layer during which the LM-head rows go to L2 (< 0: never)

@@ -280,11 +280,6 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
 }
 
 // ---------------------------------------------------------------- fixed point and limbs
-// exponent s so that |x| * 2^s < 2^29 for max |x| = m (s = 29 when m < 2^-96)
-__device__ __forceinline__ int fix_exponent(float m) {
-    const int E = m >= 0x1p-96f ? (int)((__float_as_uint(m) >> 23) & 0xff) - 126 : 0;   // m < 2^E
-    return kFixBits - E;
-}
 // X = rint(x * 2^s) clamped to +-(2^30 - 64), split into four int8 limbs at column k
 __device__ __forceinline__ void put_limbs4(int8_t *L, int k, float x, float sc) {
     float v = __fmul_rn(x, sc);
@@ -321,69 +316,57 @@ __device__ __forceinline__ long long limb_dot(int a, int b, int c, int d) {
     return (long long)hi * 65536 + lo;
 }
 
-// LayerNorm of the D-vector x by the 8 consumer warps together, the formula of
-// rust/npu-asr-host/src/lib.rs:79-110 (population variance, each op rounded), with this tree:
-// warp w owns the 32-wide blocks [w*D/256, (w+1)*D/256) (the K range of its GEMV share), lane l
-// sums its elements 32*kb + l in kb order, the warp adds its lanes with the xor butterfly, and
-// the 8 warp sums are added in warp order.  Output rounded to bf16; the fixed-point exponent
-// comes from the max over the whole output; each warp writes the limbs of its own blocks and,
-// if `out` is given, those outputs.  Three consumer barriers; every consumer thread calls it.
+// LayerNorm of the D-vector x by the 8 consumer warps together: warp w owns the 32-wide
+// blocks [w*D/256, (w+1)*D/256) (the K range of its GEMV share); one pass gives the sum and
+// the sum of squares (lane l adds its elements 32*kb + l in kb order, the warp adds its lanes
+// with the xor butterfly, the 8 warp totals are added in warp order); mean = S1 / D,
+// var = max(S2 / D - mean^2, 0) (population variance, the engine's single-pass form of
+// rust/npu-asr-host/src/lib.rs:79-110), y = bf16((x - mean) * (1 / sqrt(var + eps)) * g + b).
+// The GEMV input is y in fixed point 2^fix, an exponent derived from the LayerNorm
+// parameters (|y_k| <= sqrt(D) |g_k| + |b_k|), so no max reduction is needed.  Each warp
+// writes the limbs of its own blocks and, if `out` is given, those outputs.  One consumer
+// barrier; every consumer thread calls it.
 template <int D>
-__device__ __noinline__ int ln_limbs(const float *g, const float *b, float eps, float *out) {
+__device__ __forceinline__ void ln_limbs(const float *g, const float *b, float eps, int fix, float *out) {
     constexpr int KBW = D / 32 / kConsumerWarps;
     const Cta S = make_cta();
     const int lane = S.lane, kb0 = S.warp * KBW;
-    float *red = S.red + 32;                      // [3][8]
+    float *red = S.red + 32;                      // [2][8]
     float v[KBW];
-    float s = 0.0f;
+    float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
     for (int kk = 0; kk < KBW; kk++) {
         v[kk] = S.x[32 * (kb0 + kk) + lane];
-        s = __fadd_rn(s, v[kk]);
+        s1 = __fadd_rn(s1, v[kk]);
+        s2 = __fadd_rn(s2, __fmul_rn(v[kk], v[kk]));
     }
-    s = warp_sum(s);
-    if (lane == 0) red[S.warp] = s;
-    cbar();
-    s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) s = __fadd_rn(s, red[w]);
-    const float mean = __fdiv_rn(s, (float)D);
-    float q = 0.0f;
-#pragma unroll
-    for (int kk = 0; kk < KBW; kk++) {
-        const float c = __fsub_rn(v[kk], mean);
-        q = __fadd_rn(q, __fmul_rn(c, c));
+    for (int o = 16; o; o >>= 1) {
+        s1 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, o));
+        s2 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, o));
     }
-    q = warp_sum(q);
-    if (lane == 0) red[8 + S.warp] = q;
+    if (lane == 0) { red[S.warp] = s1; red[8 + S.warp] = s2; }
     cbar();
-    q = 0.0f;
+    s1 = 0.0f;
+    s2 = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) q = __fadd_rn(q, red[8 + w]);
-    const float var = __fdiv_rn(q, (float)D);
+    for (int w = 0; w < kConsumerWarps; w++) {
+        s1 = __fadd_rn(s1, red[w]);
+        s2 = __fadd_rn(s2, red[8 + w]);
+    }
+    const float mean = __fdiv_rn(s1, (float)D);
+    const float var = fmaxf(__fsub_rn(__fdiv_rn(s2, (float)D), __fmul_rn(mean, mean)), 0.0f);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-    float m = 0.0f;
+    const float sc = exp2i(fix);
 #pragma unroll
     for (int kk = 0; kk < KBW; kk++) {
         const int i = 32 * (kb0 + kk) + lane;
         const float t = __fmul_rn(__fsub_rn(v[kk], mean), inv);
-        v[kk] = bf16r(__fadd_rn(__fmul_rn(t, g[i]), b[i]));
-        m = fmaxf(m, fabsf(v[kk]));
-    }
-    m = warp_max_nonneg(m);
-    if (lane == 0) red[16 + S.warp] = m;
-    cbar();
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; w++) m = fmaxf(m, red[16 + w]);
-    const int e = fix_exponent(m);
-    const float sc = exp2i(e);
-#pragma unroll
-    for (int kk = 0; kk < KBW; kk++) {
-        put_limbs4(S.limbs, 32 * (kb0 + kk) + lane, v[kk], sc);
-        if (out) out[32 * (kb0 + kk) + lane] = v[kk];
+        const float y = bf16r(__fadd_rn(__fmul_rn(t, g[i]), b[i]));
+        put_limbs4(S.limbs, i, y, sc);
+        if (out) out[i] = y;
     }
     __syncwarp();
-    return e;
 }
 
 // ------------------------------------------------------------------------------ GEMVs
@@ -420,7 +403,7 @@ __device__ __forceinline__ void tile_dot(const Cta &S, const uint8_t *ch, long l
 // 16w + g + 8: float(exact dot) * 2^-s * scale + bias.  No cross-warp partial sums.  The
 // slots stay owned until release_tiles.
 template <int NKB>
-__device__ __noinline__ bool rowtile_warp(const DecodeParams &p, uint32_t ctr, int nt, int s, uint32_t where,
+__device__ __forceinline__ bool rowtile_warp(const DecodeParams &p, uint32_t ctr, int nt, int s, uint32_t where,
                                           float *y) {
     const Cta S = make_cta();
     if (S.warp >= nt) return true;
@@ -449,7 +432,7 @@ __device__ __forceinline__ void release_tiles(const Cta &S, uint32_t ctr, int nt
 // columns kSlimbOff + 32 kb), the slice chunks of D outputs; warp w owns the m-tiles w, w+8, ...
 // Each output's exact partial is added as (partial + 2^bshift + 2^56) into words[n].
 template <int D>
-__device__ __noinline__ bool slice_mma_red(const DecodeParams &p, uint32_t ctr, int nkb,
+__device__ __forceinline__ bool slice_mma_red(const DecodeParams &p, uint32_t ctr, int nkb,
                                            unsigned long long *words, int bshift, uint32_t where,
                                            unsigned long long *clk = nullptr) {
     const Cta S = make_cta();
@@ -494,7 +477,7 @@ __device__ __noinline__ bool slice_mma_red(const DecodeParams &p, uint32_t ctr, 
         const int2 lo2 = reinterpret_cast<const int2 *>(scr + i * 32 + 4 * gg)[hi];       // limbs 0, 1
         const int2 hi2 = reinterpret_cast<const int2 *>(scr + i * 32 + 4 * gg + 1)[hi];   // limbs 2, 3
         const int n = (S.warp + kConsumerWarps * i) * kTile + r;
-        red_add_u64(words + (size_t)n * p.acc_stride, (unsigned long long)limb_dot(lo2.x, lo2.y, hi2.x, hi2.y) + add);
+        red_add_u64(words + n, (unsigned long long)limb_dot(lo2.x, lo2.y, hi2.x, hi2.y) + add);
     }
     __syncwarp();
     return true;
@@ -505,44 +488,53 @@ __device__ __noinline__ bool slice_mma_red(const DecodeParams &p, uint32_t ctr, 
 // Thread t owns n = t + 256 i.  Returns false on timeout / abort.  The caller follows with a
 // barrier.
 template <int D>
-__device__ __noinline__ bool gather_acc(const DecodeParams &p, const unsigned long long *words, int cnt, int bshift,
-                                        int fix, const float *sb, uint32_t where) {
+__device__ __forceinline__ bool gather_acc(const DecodeParams &p, const unsigned long long *words, int cnt, int subs,
+                                           int bshift, int fix, const float *sb, uint32_t where) {
     const Cta S = make_cta();
     constexpr int PER = D / kConsumerThreads;
     float sc[PER], bi[PER];
-    unsigned long long v[PER];
+    unsigned long long v[PER][kMaxSubs];
+    unsigned want[kMaxSubs];
+#pragma unroll
+    for (int k = 0; k < kMaxSubs; k++) want[k] = k < subs ? (unsigned)((cnt + subs - 1 - k) / subs) : 0u;
 #pragma unroll
     for (int i = 0; i < PER; i++) {
         const int n = S.tid + kConsumerThreads * i;
         sc[i] = sb[n];
         bi[i] = sb[D + n];
-        v[i] = ld_relaxed_u64(words + (size_t)n * p.acc_stride);
+#pragma unroll
+        for (int k = 0; k < kMaxSubs; k++) v[i][k] = k < subs ? ld_relaxed_u64(words + (size_t)k * D + n) : 0ull;
     }
-    const unsigned want = (unsigned)cnt;
     uint64_t t0 = 0;
     uint32_t it = 0;
     bool ok = true;
     while (true) {
         bool all = true;
 #pragma unroll
-        for (int i = 0; i < PER; i++) all &= (unsigned)(v[i] >> kCountShift) == want;
+        for (int i = 0; i < PER; i++)
+#pragma unroll
+            for (int k = 0; k < kMaxSubs; k++) all &= (unsigned)(v[i][k] >> kCountShift) == want[k];
         if (all) break;
         __nanosleep(p.poll_ns);
 #pragma unroll
         for (int i = 0; i < PER; i++)
-            if ((unsigned)(v[i] >> kCountShift) != want)
-                v[i] = ld_relaxed_u64(words + (size_t)(S.tid + kConsumerThreads * i) * p.acc_stride);
+#pragma unroll
+            for (int k = 0; k < kMaxSubs; k++)
+                if ((unsigned)(v[i][k] >> kCountShift) != want[k])
+                    v[i][k] = ld_relaxed_u64(words + (size_t)k * D + S.tid + kConsumerThreads * i);
         if ((++it & 31) == 0 && wait_expired(p.state, p.timeout_ns, S.flag, &t0, ERR_TIMEOUT_FLAG, where)) {
             ok = false;
             break;
         }
     }
-    const long long off = (long long)cnt << bshift;
     const float inv = exp2i(-fix);
 #pragma unroll
     for (int i = 0; i < PER; i++) {
         const int n = S.tid + kConsumerThreads * i;
-        const long long Y = (long long)(v[i] & ((1ull << kCountShift) - 1)) - off;
+        long long Y = 0;
+#pragma unroll
+        for (int k = 0; k < kMaxSubs; k++)
+            Y += (long long)(v[i][k] & ((1ull << kCountShift) - 1)) - ((long long)want[k] << bshift);
         const float val = __fadd_rn(__fmul_rn(__fmul_rn(__ll2float_rn(Y), inv), sc[i]), bi[i]);
         S.x[n] = __fadd_rn(S.x[n], val);
     }
@@ -601,7 +593,7 @@ __device__ __forceinline__ float part_score(const float *qf, const uint16_t *kro
 // ctx limbs (fixed point 2^fix) land at limb column kSlimbOff + d.  `xu` counts the pair
 // exchanges of this launch (mbarrier buffer and parity).  Returns false on timeout / abort;
 // the caller follows with a barrier.
-__device__ __noinline__ bool attention(const DecodeParams &p, int layer, int head, int half, int pos, bool staged,
+__device__ __forceinline__ bool attention(const DecodeParams &p, int layer, int head, int half, int pos, bool staged,
                                        uint32_t xu, int fix, int t) {
     const Cta S = make_cta();
     const int tk = pos + 1;
@@ -738,7 +730,7 @@ __device__ __forceinline__ void ln_prefetch(const Cta &S, int buf, const float *
 // reads all CTAs' keys and leaves the winning id in S.flag[1] (CTA 0 also stores it in the
 // token array).  Returns false on timeout / abort (uniform over the CTA).
 template <int D>
-__device__ __noinline__ bool lm_head(const DecodeParams &p, uint32_t ctr, int t, int pos, uint32_t tau, int lm_t0,
+__device__ __forceinline__ bool lm_head(const DecodeParams &p, uint32_t ctr, int t, int pos, uint32_t tau, int lm_t0,
                                      int lm_nt, int s) {
     const Cta S = make_cta();
     constexpr int NKB_D = D / 32;
@@ -886,7 +878,6 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
     const int head = c >> 1, half = c & 1;
     const int fci = c - 2 * H;
     const bool is_fc = !is_head && fci < p.n_fc;
-    constexpr int NKB_D = D / 32;
     const int fc_kb_begin = is_fc ? fc_kb0(fci, F / 32, p.n_fc) : 0;
     const int fc_nkb = is_fc ? fc_kb0(fci + 1, F / 32, p.n_fc) - fc_kb_begin : 0;
     const uint32_t tok0 = p.state->tok_base;
@@ -901,7 +892,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
     for (int t = 0; t < p.n_steps; t++) {
         const int pos = p.start_pos + t;
         const uint32_t tau = tok0 + (uint32_t)t;
-        const size_t XW = (size_t)D * p.acc_stride;        // words of one exchange
+        const size_t XW = (size_t)D * kMaxSubs;            // words of one exchange
         unsigned long long *acc_tok = p.acc + (size_t)(tau % kAccSlots) * L * 2 * XW;
         const int64_t id = (t == 0 || pos < p.n_prompt) ? p.tokens[pos] : next_id;
         bool bad = false;
@@ -916,7 +907,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             // A spare CTA has no work in a token without an LM head, but it still waits for
             // the token's last fc2 words: that keeps it from running ahead into the slot of a
             // later token while the words there still hold an older token's complete sums.
-            const bool ok = gather_acc<D>(p, acc_tok + (size_t)((L - 1) * 2 + 1) * XW, p.n_fc, p.f2_bias_shift,
+            const bool ok = gather_acc<D>(p, acc_tok + (size_t)((L - 1) * 2 + 1) * XW, p.n_fc, p.f2_subs, p.f2_bias_shift,
                                           p.fix_h[L - 1], p.f2sb + (size_t)(L - 1) * 2 * D, 0x88u);
             if (cbar_or(!ok)) return;
             next_id = p.tokens[pos + 1];
@@ -960,7 +951,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 cp_async_commit();
                 bool ok = true;
                 if (l > 0)
-                    ok = gather_acc<D>(p, acc_tok + (size_t)((l - 1) * 2 + 1) * XW, p.n_fc, p.f2_bias_shift,
+                    ok = gather_acc<D>(p, acc_tok + (size_t)((l - 1) * 2 + 1) * XW, p.n_fc, p.f2_subs, p.f2_bias_shift,
                                        p.fix_h[l - 1], p.f2sb + (size_t)(l - 1) * 2 * D, 0x10u + l);
                 cp_async_wait_group<2>();          // this layer's LN parameters
                 if (cbar_or(!ok)) return;
@@ -968,7 +959,8 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 stamp(p, S, t, 1 + 4 * l);
                 const float *lg = S.lnp + (l & 1) * 2 * kDmax;
                 if (l == 1) stamp_clk(p, S, t, 1);
-                const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                const int s = p.fix_ln1[l];
+                ln_limbs<D>(lg, lg + kDmax, p.eps, s, nullptr);
                 cbar();                            // every warp's GEMV reads all limbs
                 if (l == 1) stamp_clk(p, S, t, 2);
                 if (l == 1) stamp(p, S, t, 57);
@@ -1005,13 +997,13 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 if (cbar_or(!ok)) return;
                 if (l == 1) stamp(p, S, t, 60);
                 if (l == 1) stamp_clk(p, S, t, 10);
-                ok = slice_mma_red<D>(p, ctr, 1, acc_o, p.o_bias_shift, 0x30u + l,
+                ok = slice_mma_red<D>(p, ctr, 1, acc_o + (size_t)(c % p.o_subs) * D, p.o_bias_shift, 0x30u + l,
                                       (p.timing && l == 1 && t < 2) ? p.timing + ((size_t)t * p.grid + blockIdx.x) * 128 + 75 : nullptr);
                 if (l == 1) stamp_clk(p, S, t, 13);
                 ctr += slice_chunks(D);
                 stamp(p, S, t, 3 + 4 * l);
                 // ---------------- x += out projection
-                ok = ok && gather_acc<D>(p, acc_o, 2 * H, p.o_bias_shift, p.fix_ctx[l],
+                ok = ok && gather_acc<D>(p, acc_o, 2 * H, p.o_subs, p.o_bias_shift, p.fix_ctx[l],
                                          p.osb + (size_t)l * 2 * D, 0x40u + l);
                 if (cbar_or(!ok)) return;
                 trace_x(p, S, t, 2 * l, S.x);
@@ -1019,7 +1011,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             } else {
                 // ---------------- x += out projection; LN2; fc1 rows; ReLU; K-split fc2
                 cp_async_commit();                 // (keeps the group count of the head path)
-                bool ok = gather_acc<D>(p, acc_o, 2 * H, p.o_bias_shift, p.fix_ctx[l],
+                bool ok = gather_acc<D>(p, acc_o, 2 * H, p.o_subs, p.o_bias_shift, p.fix_ctx[l],
                                         p.osb + (size_t)l * 2 * D, 0x40u + l);
                 cp_async_wait_group<2>();
                 if (cbar_or(!ok)) return;
@@ -1027,7 +1019,8 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                 stamp(p, S, t, 1 + 4 * l);
                 if (is_fc) {
                     const float *lg = S.lnp + (l & 1) * 2 * kDmax;
-                    const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, nullptr);
+                    const int s = p.fix_ln2[l];
+                    ln_limbs<D>(lg, lg + kDmax, p.eps, s, nullptr);
                     cbar();                        // every warp's GEMV reads all limbs
                     if (l == 1) stamp(p, S, t, 57);
                     const float hsc = exp2i(p.fix_h[l]);
@@ -1049,12 +1042,12 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
                     }
                     stamp(p, S, t, 2 + 4 * l);
                     if (l == 1) stamp(p, S, t, 60);
-                    ok = slice_mma_red<D>(p, ctr, fc_nkb, acc_f, p.f2_bias_shift, 0x60u + l);
+                    ok = slice_mma_red<D>(p, ctr, fc_nkb, acc_f + (size_t)(fci % p.f2_subs) * D, p.f2_bias_shift, 0x60u + l);
                     ctr += fc_nkb * slice_chunks(D);
                     stamp(p, S, t, 3 + 4 * l);
                 }
                 // ---------------- x += fc2
-                ok = ok && gather_acc<D>(p, acc_f, p.n_fc, p.f2_bias_shift, p.fix_h[l],
+                ok = ok && gather_acc<D>(p, acc_f, p.n_fc, p.f2_subs, p.f2_bias_shift, p.fix_h[l],
                                          p.f2sb + (size_t)l * 2 * D, 0x70u + l);
                 if (cbar_or(!ok)) return;
                 trace_x(p, S, t, 2 * l + 1, S.x);
@@ -1067,7 +1060,7 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             }
         }
         if (is_head) {
-            const bool ok = gather_acc<D>(p, acc_tok + (size_t)((L - 1) * 2 + 1) * XW, p.n_fc, p.f2_bias_shift,
+            const bool ok = gather_acc<D>(p, acc_tok + (size_t)((L - 1) * 2 + 1) * XW, p.n_fc, p.f2_subs, p.f2_bias_shift,
                                           p.fix_h[L - 1], p.f2sb + (size_t)(L - 1) * 2 * D, 0x80u);
             if (cbar_or(!ok)) return;
             trace_x(p, S, t, 2 * L - 1, S.x);
@@ -1079,7 +1072,8 @@ __device__ __forceinline__ void consumer(const DecodeParams &p, Cta &S) {
             cbar();
             const float *lg = S.lnp + (L & 1) * 2 * kDmax;
             float *tr = (p.trace && c == 0) ? p.trace + ((size_t)t * (2 * L + 1) + 2 * L) * D : nullptr;
-            const int s = ln_limbs<D>(lg, lg + kDmax, p.eps, tr);
+            const int s = p.fix_lnf;
+            ln_limbs<D>(lg, lg + kDmax, p.eps, s, tr);
             cbar();
             if (!lm_head<D>(p, ctr, t, pos, tau, lm_t0, lm_nt, s)) return;
             ctr += lm_nt;

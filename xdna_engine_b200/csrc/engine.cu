@@ -194,6 +194,13 @@ int fix_from_bound(double B) {
     std::frexp(B, &E);                     // B < 2^E
     return kFixBits - E;
 }
+// a LayerNorm output: |y_k| <= sqrt(D) |g_k| + |b_k| (1% for the roundings)
+double ln_bound(const float *g, const float *b, int D) {
+    double B = 0.0;
+    for (int k = 0; k < D; k++)
+        B = std::max(B, (std::sqrt((double)D) * std::fabs((double)g[k]) + std::fabs((double)b[k])) * 1.01);
+    return B;
+}
 double rows_bound(const QMat &m, int n0, int n1, const float *g, const float *b, int D) {
     std::vector<double> lnmax(D);
     for (int k = 0; k < D; k++)
@@ -249,7 +256,8 @@ struct XdnaOptDecoder {
     XdnaDevice *dev = nullptr;
     XdnaOptConfig cfg{};
     int grid = 0, n_fc = 0, max_ctx = 0, n_pages = 0, vocab_tiles = 0;
-    int o_bias_shift = 0, f2_bias_shift = 0, acc_stride = 1, poll_ns = 20, lm_prefetch_layer = 0;
+    int fix_lnf = 0;
+    int o_bias_shift = 0, f2_bias_shift = 0, o_subs = 2, f2_subs = 8, poll_ns = 20, lm_prefetch_layer = 0;
     size_t stream_bytes = 0, token_bytes = 0;
     uint8_t *d_stream = nullptr;
     ChunkRef *d_chunks = nullptr;
@@ -257,7 +265,7 @@ struct XdnaOptDecoder {
     int chunk_stride = 0;
     float *d_emb = nullptr, *d_pos = nullptr, *d_ln = nullptr, *d_lnf = nullptr, *d_osb = nullptr,
           *d_f2sb = nullptr;
-    int *d_fix = nullptr;                  // [2][L]: context, fc1-output exponents
+    int *d_fix = nullptr;                  // [4][L]: context, fc1-output, LN1, LN2 exponents
     uint16_t *d_kv = nullptr;
     int *d_pt = nullptr;
     unsigned long long *d_acc = nullptr;
@@ -443,7 +451,7 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
 
         // quantise every linear (Lin::load rule)
         std::vector<QMat> q(L), k(L), v(L), o(L), f1(L), f2(L);
-        std::vector<int> fix(2 * L);
+        std::vector<int> fix(4 * L);
         for (int l = 0; l < L; l++) {
             const XdnaOptLayer &ly = w->layers[l];
             q[l] = quant_linear(ly.wq, ly.bq, D, D);
@@ -454,6 +462,8 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
             f2[l] = quant_linear(ly.w2, ly.b2, F, D);
             fix[l] = fix_from_bound(rows_bound(v[l], 0, D, ly.ln1_w, ly.ln1_b, D));
             fix[L + l] = fix_from_bound(rows_bound(f1[l], 0, F, ly.ln2_w, ly.ln2_b, D));
+            fix[2 * L + l] = fix_from_bound(ln_bound(ly.ln1_w, ly.ln1_b, D));
+            fix[3 * L + l] = fix_from_bound(ln_bound(ly.ln2_w, ly.ln2_b, D));
         }
         QMat lm;
         lm.K = D;
@@ -543,8 +553,9 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         std::copy(w->lnf_w, w->lnf_w + D, lnf.begin());
         std::copy(w->lnf_b, w->lnf_b + D, lnf.begin() + D);
         upload(lnf, &dec->d_lnf, "upload lnf");
-        dec->d_fix = dmalloc<int>(2 * L);
-        ck(cudaMemcpy(dec->d_fix, fix.data(), 2 * L * sizeof(int), cudaMemcpyHostToDevice), "upload exponents");
+        dec->fix_lnf = fix_from_bound(ln_bound(w->lnf_w, w->lnf_b, D));
+        dec->d_fix = dmalloc<int>(4 * L);
+        ck(cudaMemcpy(dec->d_fix, fix.data(), 4 * L * sizeof(int), cudaMemcpyHostToDevice), "upload exponents");
 
         // paged KV: pages in reverse physical order so the page table is exercised
         dec->n_pages = (max_ctx + kPageTokens - 1) / kPageTokens;
@@ -557,11 +568,12 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         ck(cudaMemset(dec->d_kv, 0, kv_elems * 2), "clear kv");
 
         // exchange: accumulator words (zero) and the LM-head key words (epoch 0)
-        dec->acc_stride = env_int("XDNA_OPT_ACC_STRIDE", 1);
+        dec->o_subs = std::min(kMaxSubs, env_int("XDNA_OPT_O_SUBS", 2));
+        dec->f2_subs = std::min(kMaxSubs, env_int("XDNA_OPT_F2_SUBS", 8));
         dec->poll_ns = env_int("XDNA_OPT_POLL_NS", 20);
         dec->lm_prefetch_layer = std::max(0, L - 4);
         if (const char *e = std::getenv("XDNA_OPT_LM_PREFETCH_LAYER")) dec->lm_prefetch_layer = std::atoi(e);
-        dec->acc_words = (size_t)kAccSlots * L * 2 * D * dec->acc_stride;
+        dec->acc_words = (size_t)kAccSlots * L * 2 * D * kMaxSubs;
         dec->d_acc = dmalloc<unsigned long long>(dec->acc_words);
         ck(cudaMemset(dec->d_acc, 0, dec->acc_words * 8), "clear accumulators");
         dec->d_ll = dmalloc<unsigned long long>(2 * kAccSlots);
@@ -651,13 +663,17 @@ int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_promp
     p.f2sb = dec->d_f2sb;
     p.fix_ctx = dec->d_fix;
     p.fix_h = dec->d_fix + c.n_layers;
+    p.fix_ln1 = dec->d_fix + 2 * c.n_layers;
+    p.fix_ln2 = dec->d_fix + 3 * c.n_layers;
+    p.fix_lnf = dec->fix_lnf;
     p.o_bias_shift = dec->o_bias_shift;
     p.f2_bias_shift = dec->f2_bias_shift;
     p.kv = dec->d_kv;
     p.page_table = dec->d_pt;
     p.n_phys_pages = dec->n_pages;
     p.acc = dec->d_acc;
-    p.acc_stride = dec->acc_stride;
+    p.o_subs = dec->o_subs;
+    p.f2_subs = dec->f2_subs;
     p.poll_ns = dec->poll_ns;
     p.lm_words = dec->d_ll;
     p.lm_prefetch_layer = dec->lm_prefetch_layer;
