@@ -84,7 +84,7 @@ static void rope(float *x, int hd, int pos, float theta) {
 }
 
 int or_gemma_decode(const or_gemma_cfg *c, const or_gemma_weights *w, const int64_t *prompt, int n_prompt, int n_new,
-                    int64_t *out_tokens, float *logits, int nt) {
+                    int64_t *out_tokens, float *logits, int nt, const int64_t *force) {
     const int D = c->d_model, HQ = c->n_q_heads, HD = c->head_dim, F = c->ffn, V = c->vocab, L = c->n_layers;
     const int S = n_prompt + n_new, QD = HQ * HD;
     if (nt < 1) nt = 1;
@@ -168,7 +168,7 @@ int or_gemma_decode(const or_gemma_cfg *c, const or_gemma_weights *w, const int6
         const int step = pos + 1 - n_prompt;
         out_tokens[step] = best;
         if (logits) memcpy(logits + (size_t)step * V, lg, sizeof(float) * V);
-        tok = best;
+        tok = force ? force[step] : best;       /* teacher forcing */
     }
     for (int i = 0; i < L * 7; i++) glin_free(&lins[i]);
     glin_free(&lm);

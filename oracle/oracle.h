@@ -219,10 +219,11 @@ typedef struct {
     const or_whisper_dec_layer *layers;
 } or_whisper_dec_weights;
 /* enc [B][n_enc][d_model]; the same prompt for every stream; out_tokens [B][n_new],
- * logits (nullable) [B][n_new][vocab] */
+ * logits (nullable) [B][n_new][vocab]; force (nullable, [B][n_new]): feed force[b][g] after
+ * step g instead of the argmax (teacher forcing), so logits stay comparable across numerics */
 int or_whisper_decode(const or_whisper_dec_cfg *c, const or_whisper_dec_weights *w, const float *enc, int B,
                       const int64_t *prompt, int n_prompt, int n_new, int64_t *out_tokens, float *logits,
-                      int nthreads);
+                      int nthreads, const int64_t *force);
 
 /* ---- Gemma-3 text decoder (npu-gemma pieces + the HF Gemma-3 model they port) ---- */
 typedef struct {
@@ -238,8 +239,9 @@ typedef struct {
     const float *embed, *final_norm;      /* embed [V, D], tied LM head */
     const or_gemma_layer *layers;
 } or_gemma_weights;
+/* force (nullable, [n_new]): teacher forcing as for or_whisper_decode */
 int or_gemma_decode(const or_gemma_cfg *c, const or_gemma_weights *w, const int64_t *prompt, int n_prompt,
-                    int n_new, int64_t *out_tokens, float *logits, int nthreads);
+                    int n_new, int64_t *out_tokens, float *logits, int nthreads, const int64_t *force);
 float or_gelu_tanh_gemma(float x);
 
 #ifdef __cplusplus

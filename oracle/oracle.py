@@ -86,10 +86,10 @@ def lib():
         L.or_rel_shift.argtypes = [F32P, C.c_int, C.c_int, F32P]
         L.or_rel_pos_encoding.argtypes = [C.c_int, C.c_int, F32P]
         L.or_whisper_decode.argtypes = [C.c_void_p, C.c_void_p, F32P, C.c_int, C.c_void_p, C.c_int, C.c_int,
-                                        C.c_void_p, C.c_void_p, C.c_int]
+                                        C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
         L.or_whisper_decode.restype = C.c_int
         L.or_gemma_decode.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
-                                      C.c_void_p, C.c_int]
+                                      C.c_void_p, C.c_int, C.c_void_p]
         L.or_gemma_decode.restype = C.c_int
         L.or_opt_step.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_void_p]
         L.or_opt_step.restype = C.c_int64
@@ -520,8 +520,9 @@ class _WDecWeights(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in _WDEC_TOP + ("layers",)]
 
 
-def whisper_decode(cfg, w, enc, prompt, n_new, want_logits=False, nthreads=None):
-    """or_whisper_decode: greedy decode of B streams (enc [B, n_enc, D]) after a shared prompt."""
+def whisper_decode(cfg, w, enc, prompt, n_new, want_logits=False, nthreads=None, force=None):
+    """or_whisper_decode: greedy decode of B streams (enc [B, n_enc, D]) after a shared prompt;
+    force ([B, n_new], optional) feeds those tokens instead of the argmaxes (teacher forcing)."""
     keep = []
 
     def p(a):
@@ -538,11 +539,12 @@ def whisper_decode(cfg, w, enc, prompt, n_new, want_logits=False, nthreads=None)
     enc = _f32(enc)
     B = enc.shape[0]
     pr = np.ascontiguousarray(prompt, np.int64)
+    fc = None if force is None else np.ascontiguousarray(force, np.int64).reshape(B, n_new)
     toks = np.empty((B, n_new), np.int64)
     lg = np.empty((B, n_new, cfg.vocab), np.float32) if want_logits else None
     rc = lib().or_whisper_decode(C.addressof(c), C.addressof(ww), enc.ravel(), B, pr.ctypes.data, len(pr), n_new,
                                  toks.ctypes.data, lg.ctypes.data if lg is not None else None,
-                                 nthreads or os.cpu_count() or 1)
+                                 nthreads or os.cpu_count() or 1, _ptr(fc))
     if rc != 0:
         raise ValueError("or_whisper_decode: prompt + new tokens beyond max_tgt")
     return (toks, lg) if want_logits else toks
@@ -568,8 +570,9 @@ class _GmWeights(C.Structure):
     _fields_ = [("embed", C.c_void_p), ("final_norm", C.c_void_p), ("layers", C.c_void_p)]
 
 
-def gemma_decode(cfg, w, prompt, n_new, int8=True, want_logits=False, nthreads=None):
-    """or_gemma_decode: greedy decode of one stream after the prompt."""
+def gemma_decode(cfg, w, prompt, n_new, int8=True, want_logits=False, nthreads=None, force=None):
+    """or_gemma_decode: greedy decode of one stream after the prompt; force ([n_new], optional)
+    feeds those tokens instead of the argmaxes (teacher forcing)."""
     keep = []
 
     def p(a):
@@ -587,6 +590,7 @@ def gemma_decode(cfg, w, prompt, n_new, int8=True, want_logits=False, nthreads=N
     pr = np.ascontiguousarray(prompt, np.int64)
     toks = np.empty(n_new, np.int64)
     lg = np.empty((n_new, cfg.vocab), np.float32) if want_logits else None
+    fc = None if force is None else np.ascontiguousarray(force, np.int64)
     lib().or_gemma_decode(C.addressof(c), C.addressof(ww), pr.ctypes.data, len(pr), n_new, toks.ctypes.data,
-                          lg.ctypes.data if lg is not None else None, nthreads or os.cpu_count() or 1)
+                          lg.ctypes.data if lg is not None else None, nthreads or os.cpu_count() or 1, _ptr(fc))
     return (toks, lg) if want_logits else toks

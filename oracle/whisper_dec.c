@@ -57,7 +57,8 @@ static void attend(const float *q, const float *kf, const float *vf, int s, int 
 }
 
 int or_whisper_decode(const or_whisper_dec_cfg *c, const or_whisper_dec_weights *w, const float *enc, int B,
-                      const int64_t *prompt, int n_prompt, int n_new, int64_t *out_tokens, float *logits, int nt) {
+                      const int64_t *prompt, int n_prompt, int n_new, int64_t *out_tokens, float *logits, int nt,
+                      const int64_t *force) {
     const int D = c->d_model, H = c->n_heads, hd = D / H, F = c->ffn, V = c->vocab, L = c->n_layers, TE = c->n_enc;
     const int S = n_prompt + n_new;
     if (nt < 1) nt = 1;
@@ -111,7 +112,7 @@ int or_whisper_decode(const or_whisper_dec_cfg *c, const or_whisper_dec_weights 
             const int step = pos + 1 - n_prompt;
             out_tokens[(size_t)b * n_new + step] = best;
             if (logits) memcpy(logits + ((size_t)b * n_new + step) * V, lg, sizeof(float) * V);
-            tok = best;
+            tok = force ? force[(size_t)b * n_new + step] : best;   /* teacher forcing */
         }
     }
     free(ck); free(cv); free(sk); free(sv); free(x); free(ln); free(q); free(ctx); free(a); free(h1); free(lg); free(sc);

@@ -73,3 +73,19 @@ def test_bert_rejects_bad_input(X):
     out = m.embed(np.array([1500, 2000], np.int32), np.array([2], np.int32))
     assert out.shape == (1, 768)
     m.close()
+
+
+def test_bge_base_config_long_sequences(X):
+    """The BGE-base config at its length range: a batch of 6 drawn from U[32, 512] plus a
+    512-token and a 511-token sequence (all 8 key tiles of the attention, ragged tails), cos >=
+    0.999 against the oracle (bert/encoder.rs:43-57, head.rs:20-47)."""
+    w = make_bert_weights(BGE_BASE, seed=1)
+    ids, lens = make_bge_batch(6, seed=1)
+    rng = np.random.default_rng(11)
+    lens = np.concatenate([lens, np.array([512, 511], np.int32)])
+    ids = np.concatenate([ids, rng.integers(1000, 30000, 1023).astype(np.int32)])
+    m = X.BertEmbedder(X.Device(0), BGE_BASE, w, max_tokens=int(lens.sum()), max_seqs=8)
+    got = m.embed(ids, lens)
+    m.close()
+    c = cosines(got, O.bert_embed(BGE_BASE, w, ids, lens))
+    assert c.min() >= 0.999, c

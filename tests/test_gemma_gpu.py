@@ -44,6 +44,9 @@ def test_gemma_single_gpu_vs_oracle(X):
     got = dec.generate(np.array([PROMPT]), 12)[0]
     n = agree_until_close(got, wt, wl)
     assert n >= 4, (got, wt)
+    # all 12 tokens, teacher-forced: each GPU choice within 0.15 logit-rms of the oracle's best
+    gaps, _ = tf_gaps(cfg, w, PROMPT, got)
+    assert gaps.max() <= 0.15, gaps
     # three streams with different prompts: each equals its own single-stream run
     prompts = np.array([PROMPT, list(range(20, 30)), list(range(40, 50))])
     batch = dec.generate(prompts, 12)
@@ -70,6 +73,39 @@ def test_gemma_many_streams_vs_oracle(X, B):
         lens.append(agree_until_close(got[b], wt, wl))     # any earlier split is a near-tie
     assert sum(n >= 4 for n in lens) >= 0.9 * B, lens
     dec.close()
+
+
+def tf_gaps(cfg, w, prompt, toks):
+    """The oracle teacher-forced on the GPU's tokens: per step, how far below the oracle's best
+    logit the GPU's choice lies, in units of that step's logit rms (0 where they agree)."""
+    from oracle import oracle as O
+    wt, wl = O.gemma_decode(cfg, w, list(prompt), len(toks), int8=True, want_logits=True, force=toks)
+    gaps = []
+    for s in range(len(toks)):
+        l = wl[s].astype(np.float64)
+        gaps.append(float((l.max() - l[int(toks[s])]) / np.sqrt((l * l).mean())))
+    return np.array(gaps), wt
+
+
+def test_gemma_baseline_config_long_prompt(X):
+    """The BASELINE shapes (26 layers, d 1152, vocab 262,144, window 512, 5 local : 1 global) with
+    a 600-token prompt, so the local layers' 512-slot ring wraps and the global layers attend
+    past the window, then 16 greedy tokens.  The GPU never stores the 262,144 logits (the argmax
+    is fused into the LM-head GEMV), so the logits are compared through the oracle teacher-forced
+    on the GPU's tokens: every GPU token's oracle logit is within 0.05 logit-rms of the oracle's
+    best (f16 activations and a bf16 KV cache against f32), and most tokens are the oracle's own
+    argmax."""
+    cfg = X.GEMMA3_1B
+    w = X.make_gemma_weights(cfg, seed=2)
+    rng = np.random.default_rng(2)
+    prompt = rng.integers(2, cfg.vocab, 600)
+    dec = X.GemmaDecoder(X.Device(0), cfg, w, max_batch=1, max_ctx=640)
+    got = dec.generate(prompt[None, :], 16)[0]
+    dec.close()
+    gaps, wt = tf_gaps(cfg, w, prompt, got)
+    print("gemma 1B gaps (logit rms):", np.round(gaps, 4).tolist())
+    assert gaps.max() <= 0.05, gaps
+    assert (gaps == 0).sum() >= 12, gaps
 
 
 def test_gemma_rejects_bad_input(X):
@@ -123,8 +159,10 @@ def test_gemma_tensor_parallel_2gpu(X):
     for p in ps:
         p.join(timeout=60)
     assert np.array_equal(res[0], res[1]), "ranks disagree"
+    # all 12 tokens of both streams: the tensor-parallel sums add the ranks' partials in rank
+    # order (not the single GPU's order), so a token may differ from the single-GPU run only
+    # at a near tie; checked against the oracle teacher-forced on the TP tokens
     cfg, w = model(X)
-    single = X.GemmaDecoder(X.Device(0), cfg, w, max_batch=2, max_ctx=64)
-    ref = single.generate(np.array([PROMPT, list(range(20, 30))]), 12)
-    assert (res[0][:, :4] == ref[:, :4]).all(), (res[0], ref)
-    single.close()
+    for b, pr in enumerate([PROMPT, list(range(20, 30))]):
+        gaps, _ = tf_gaps(cfg, w, pr, res[0][b])
+        assert gaps.max() <= 0.15, (b, gaps)

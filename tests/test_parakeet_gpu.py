@@ -130,3 +130,19 @@ def test_parakeet_rejects_bad_shapes(X):
     with pytest.raises(X.XdnaError):
         enc.encode(X.make_parakeet_mel(cfg, 2))
     enc.close()
+
+
+def test_parakeet_encoder_baseline_config(X):
+    """The BASELINE config: all 24 blocks on a 10 s clip (128 x 1000 mel -> 125 x 1024) against
+    the oracle's int8-engine restatement of encoder.rs:572-654 at cos >= 0.999, and the same clip
+    inside a batch of 64 gives the same bits as alone (per-clip activation scales)."""
+    from oracle import oracle as O
+    cfg = X.ParakeetConfig()
+    w = X.make_parakeet_weights(cfg, seed=5)
+    mel = X.make_parakeet_mel(cfg, 64, seed=5)
+    enc = X.ParakeetEncoder(X.Device(0), cfg, w, max_batch=64)
+    batch = enc.encode(mel)
+    one = enc.encode(mel[:1])
+    enc.close()
+    assert np.array_equal(one[0], batch[0])
+    print("baseline", _compare(one, O.parakeet_encode(cfg, w, mel[:1], int8=True), cos_min=0.999))

@@ -87,3 +87,16 @@ def test_whisper_encoder_rejects_bad_shapes(X):
     with pytest.raises(X.XdnaError):
         enc.encode(X.make_mel(cfg, batch=2))
     enc.close()
+
+
+def test_whisper_encoder_baseline_config(X):
+    """The BASELINE config: all 12 layers over a full 30 s clip (80 x 3000 mel -> 1500 x 768),
+    one clip, against the oracle's restatement of encoder.rs:236-337 at cos >= 0.999."""
+    from oracle import oracle as O
+    cfg = X.WhisperEncConfig()
+    w = X.make_whisper_enc_weights(cfg, seed=3)
+    mel = X.make_mel(cfg, batch=1, seed=3)
+    enc = X.WhisperEncoder(X.Device(0), cfg, w, max_batch=1)
+    got = enc.encode(mel)
+    enc.close()
+    compare(got, O.whisper_encode(cfg, engine_weights(w), mel))
