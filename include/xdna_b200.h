@@ -369,6 +369,60 @@ int xdna_parakeet_encode(XdnaParakeet *m, const float *mel, int B, float *out);
 /* device-resident form: asynchronous on `stream` */
 int xdna_parakeet_encode_device(XdnaParakeet *m, const float *mel_dev, int B, float *out_dev, void *stream);
 
+
+/* ------------------------------------------- device layer, op by op (npu-xrt shim + CtxDecode) */
+/* The ordinal an open device was opened with (-1 for NULL). */
+int xdna_device_ordinal(const XdnaDevice *dev);
+
+/* Device buffers.  Replace shim_bo_alloc / shim_bo_free / shim_bo_write / shim_bo_read
+ * (rust/npu-xrt/shim/xrt_shim.h:26-30): device memory has no host mirror, so the reference's
+ * sync_to/from_device pair (xrt_shim.h:31-32) is folded into write / read.  write and read
+ * return 0, or -1 with xdna_last_error() set (a NULL pointer, or a range past the end). */
+typedef struct XdnaBuffer XdnaBuffer;
+XdnaBuffer *xdna_buffer_alloc(XdnaDevice *dev, size_t bytes);
+void xdna_buffer_free(XdnaBuffer *b);
+void *xdna_buffer_device_ptr(XdnaBuffer *b);
+int xdna_buffer_write(XdnaBuffer *b, const void *src, size_t bytes, size_t offset);
+int xdna_buffer_read(XdnaBuffer *b, void *dst, size_t bytes, size_t offset);
+
+/* Asynchronous runs.  Replace shim_run_matmul8_start / shim_run_elf_start + shim_run_wait +
+ * shim_run_free (xrt_shim.h:51-54, 75): a run marks all work enqueued on `stream` (a
+ * cudaStream_t; NULL = the legacy default stream) so far; xdna_run_wait returns 0 when it has
+ * completed, 1 if it has not within timeout_ms (< 0: wait without limit), -1 on a device
+ * error.  The reference's wait has no limit and folds "not completed" into -1. */
+typedef struct XdnaRun XdnaRun;
+XdnaRun *xdna_run_start(XdnaDevice *dev, void *stream);
+int xdna_run_wait(XdnaRun *r, int timeout_ms);
+void xdna_run_free(XdnaRun *r);
+
+/* Resident bf16 GEMV with an optional fused pre-norm.  Replaces CtxDecode::register_weight +
+ * gemv (rust/npu-asr/src/ctx_decode.rs:269-369) for norm = 0 and register_fused +
+ * fused_norm_gemv (ctx_decode.rs:566-643) for norm = 1 (RMSNorm, gamma) and norm = 2
+ * (LayerNorm, gamma and beta).  w is [K, N] f32 row-major, bias length N or NULL.  The
+ * fold: W'' = bf16(gamma[k] * W[k][n]); LayerNorm's bias' = sum_k beta[k] W[k][n] (f32, k
+ * ascending) + bias[n].  1 <= K <= 12288. */
+typedef struct XdnaGemvBf16 XdnaGemvBf16;
+XdnaGemvBf16 *xdna_gemv_bf16_register(XdnaDevice *dev, const float *w, int K, int N, const float *bias, int norm,
+                                      const float *gamma, const float *beta, float eps);
+void xdna_gemv_bf16_free(XdnaGemvBf16 *h);
+/* Host x[K] -> host y[N]: the input statistics in f64 on the host (RMS: x / sqrt(mean(x^2)
+ * + eps); LN: (x - mean) / sqrt(var + eps)), x rounded to bf16, f32 accumulation over
+ * bf16 products on the GPU, + bias'.  Synchronous; 0 or -1. */
+int xdna_gemv_bf16(XdnaGemvBf16 *h, const float *x, float *y);
+/* Device form of the dot product alone (x already normalised): y_dev = bf16(x_dev) . W'' +
+ * bias', asynchronous on `stream`. */
+int xdna_gemv_bf16_device(XdnaGemvBf16 *h, const float *x_dev, float *y_dev, void *stream);
+
+/* Single-query multi-head decode attention over the reference's packed K/V tiles.  Replaces
+ * the mha_decode kernel (route_b_kernels/mha_decode/mha_decode.cc:90-168) as CtxDecode
+ * dispatches it (ctx_decode.rs:464-555).  q_dev: [n_heads][64] bf16; kv_dev: per head
+ * n_tiles tiles of [K 64x64 | V 64x64 | int32 key count as 2 bf16] bf16 (16,388 bytes); the
+ * count is > 0 for a full or partial tile, < 0 (-count) for the last non-empty tile, 0 for an
+ * empty one.  ctx_dev: [n_heads][64] f32 = softmax(q.K^T / 8) V over the real keys.  Device
+ * pointers on the current device; asynchronous on `stream`. */
+int xdna_mha_decode_paged(const uint16_t *q_dev, const uint16_t *kv_dev, int n_heads, int n_tiles, float *ctx_dev,
+                          void *stream);
+
 #ifdef __cplusplus
 }
 #endif

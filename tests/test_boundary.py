@@ -96,3 +96,20 @@ def test_bfp16_quantize_matches_oracle():
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
     with pytest.raises(X.XdnaError):
         X.bfp16_quantize(x[:12])
+
+
+def test_op_layer_null_errors(xl):
+    """The op-by-op entries refuse NULL handles with an error message, no device needed."""
+    L = xl.lib()
+    assert L.xdna_device_ordinal(None) == -1
+    assert L.xdna_buffer_alloc(None, 64) is None
+    assert "null" in xl.last_error()
+    assert L.xdna_buffer_write(None, None, 0, 0) == -1
+    assert L.xdna_run_start(None, None) is None
+    assert L.xdna_run_wait(None, 0) == -1
+    assert L.xdna_gemv_bf16_register(None, None, 8, 8, None, 0, None, None, 1e-5) is None
+    assert L.xdna_gemv_bf16(None, None, None) == -1
+    assert L.xdna_mha_decode_paged(None, None, 12, 7, None, None) == -1
+    L.xdna_buffer_free(None)
+    L.xdna_run_free(None)
+    L.xdna_gemv_bf16_free(None)

@@ -149,6 +149,31 @@ def lib():
         L.xdna_opt_set_timing.restype = i
         L.xdna_opt_set_trace.argtypes = [vp, vp]
         L.xdna_opt_set_trace.restype = i
+        L.xdna_device_ordinal.argtypes = [vp]
+        L.xdna_device_ordinal.restype = i
+        L.xdna_buffer_alloc.argtypes = [vp, sz]
+        L.xdna_buffer_alloc.restype = vp
+        L.xdna_buffer_free.argtypes = [vp]
+        L.xdna_buffer_device_ptr.argtypes = [vp]
+        L.xdna_buffer_device_ptr.restype = vp
+        L.xdna_buffer_write.argtypes = [vp, vp, sz, sz]
+        L.xdna_buffer_write.restype = i
+        L.xdna_buffer_read.argtypes = [vp, vp, sz, sz]
+        L.xdna_buffer_read.restype = i
+        L.xdna_run_start.argtypes = [vp, vp]
+        L.xdna_run_start.restype = vp
+        L.xdna_run_wait.argtypes = [vp, i]
+        L.xdna_run_wait.restype = i
+        L.xdna_run_free.argtypes = [vp]
+        L.xdna_gemv_bf16_register.argtypes = [vp, vp, i, i, vp, i, vp, vp, C.c_float]
+        L.xdna_gemv_bf16_register.restype = vp
+        L.xdna_gemv_bf16_free.argtypes = [vp]
+        L.xdna_gemv_bf16.argtypes = [vp, vp, vp]
+        L.xdna_gemv_bf16.restype = i
+        L.xdna_gemv_bf16_device.argtypes = [vp, vp, vp, vp]
+        L.xdna_gemv_bf16_device.restype = i
+        L.xdna_mha_decode_paged.argtypes = [vp, vp, i, i, vp, vp]
+        L.xdna_mha_decode_paged.restype = i
         _LIB = L
     return _LIB
 
@@ -216,6 +241,47 @@ class Device:
         if self.handle:
             lib().xdna_device_close(self.handle)
             self.handle = None
+
+
+class GemvBf16:
+    """A resident bf16 weight with an optional fused pre-norm: CtxDecode::register_weight / gemv
+    (norm None) and register_fused / fused_norm_gemv (norm "rms" or "ln"),
+    rust/npu-asr/src/ctx_decode.rs:269-369, 566-643.  w is [K, N] (in, out)."""
+
+    _NORMS = {None: 0, "rms": 1, "ln": 2}
+
+    def __init__(self, dev: Device, w, bias=None, norm=None, gamma=None, beta=None, eps=1e-5):
+        w = np.ascontiguousarray(w, np.float32)
+        self.K, self.N = w.shape
+        keep = [np.ascontiguousarray(a, np.float32) if a is not None else None for a in (bias, gamma, beta)]
+        ptr = [None if a is None else _addr(a) for a in keep]
+        h = lib().xdna_gemv_bf16_register(dev.handle, _addr(w), self.K, self.N, ptr[0], self._NORMS[norm],
+                                          ptr[1], ptr[2], eps)
+        if not h:
+            raise XdnaError(last_error())
+        self.handle = h
+
+    def __call__(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        if x.shape != (self.K,):
+            raise ValueError(f"x has shape {x.shape}, want ({self.K},)")
+        y = np.empty(self.N, np.float32)
+        _check(lib().xdna_gemv_bf16(self.handle, _addr(x), _addr(y)))
+        return y
+
+    def device(self, x_dev: int, y_dev: int, stream: int = 0):
+        """y_dev[N] = bf16(x_dev[K]) . W'' + bias' (x already normalised), async on `stream`."""
+        _check(lib().xdna_gemv_bf16_device(self.handle, x_dev, y_dev, stream or None))
+
+    def free(self):
+        if self.handle:
+            lib().xdna_gemv_bf16_free(self.handle)
+            self.handle = None
+
+
+def mha_decode_paged(q_dev: int, kv_dev: int, n_heads: int, n_tiles: int, ctx_dev: int, stream: int = 0):
+    """The mha_decode kernel's contract over packed K/V tiles (mha_decode.cc:90-168)."""
+    _check(lib().xdna_mha_decode_paged(q_dev, kv_dev, n_heads, n_tiles, ctx_dev, stream or None))
 
 
 class OptDecoder:

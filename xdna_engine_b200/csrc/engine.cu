@@ -329,6 +329,7 @@ XdnaDevice *xdna_device_open(int ordinal) {
 }
 
 void xdna_device_close(XdnaDevice *dev) { delete dev; }
+int xdna_device_ordinal(const XdnaDevice *dev) { return dev ? dev->ordinal : -1; }
 
 int xdna_quant_i8_cols(const float *w, int K, int N, int8_t *q_nk, float *scale) {
     if (!w || !q_nk || !scale || K <= 0 || N <= 0) {

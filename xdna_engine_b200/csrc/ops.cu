@@ -1,0 +1,328 @@
+// ops.cu -- op-level entry points of the device layer (the npu-xrt replacement, one call per
+// reference dispatch), for hosts that drive the decode op by op the way CtxDecode does:
+//
+//  * device buffers        shim_bo_alloc / _write / _read / _free (rust/npu-xrt/shim/xrt_shim.h:16-40)
+//  * asynchronous runs      shim_run_matmul8_start / shim_run_wait / shim_run_free (xrt_shim.h:45-55):
+//                           a run marks the work enqueued on a stream so far; the wait is bounded
+//  * bf16 GEMV              CtxDecode::register_weight + gemv (rust/npu-asr/src/ctx_decode.rs:260-369)
+//  * fused norm + GEMV      CtxDecode::register_fused + fused_norm_gemv (ctx_decode.rs:566-643): the
+//                           norm's gamma folded into the weight (W'' = diag(gamma) W), LN's beta into
+//                           the bias (bias' = beta . W + bias), the input statistics in f64 on the host
+//  * paged decode attention the mha_tile kernel (route_b_kernels/mha_decode/mha_decode.cc:90-168) over
+//                           the reference's packed K/V tiles (ctx_decode.rs:468-555)
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/xdna_b200.h"
+
+namespace xdna {
+void set_last_error_message(const std::string &m);
+}
+using xdna::set_last_error_message;
+
+struct XdnaDevice;   // defined in engine.cu; only its ordinal is needed here
+extern "C" int xdna_device_ordinal(const XdnaDevice *dev);
+
+struct XdnaBuffer {
+    int ordinal = 0;
+    void *ptr = nullptr;
+    size_t bytes = 0;
+};
+struct XdnaRun {
+    int ordinal = 0;
+    cudaEvent_t ev = nullptr;
+};
+struct XdnaGemvBf16 {
+    int ordinal = 0;
+    int K = 0, N = 0, Kp = 0;
+    int norm = 0;                   // 0 none, 1 RMSNorm, 2 LayerNorm
+    float eps = 0.0f;
+    uint16_t *w = nullptr;          // [N][Kp] bf16 of W'' (gamma folded), K padded to 8
+    float *bias = nullptr;          // [N] bias' (folded) or bias
+    float *x = nullptr, *y = nullptr;   // staging for the host-in / host-out call
+};
+
+namespace {
+
+bool ck(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return true;
+    set_last_error_message(std::string(what) + ": " + cudaGetErrorString(e));
+    return false;
+}
+
+uint16_t bf16_rne(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);   // quiet NaN
+    return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+
+// ---- y[n] = sum_k bf16(x[k]) * W''[n][k] (f32 accumulation) + bias[n]
+// One warp per output row; lane l covers k in 8-wide groups l, l + 32, ...  (fma chain, then
+// the xor butterfly).  x is staged in shared memory as bf16-rounded f32.
+__global__ void gemv_bf16_kernel(const uint16_t *__restrict__ w, const float *__restrict__ x,
+                                 const float *__restrict__ bias, float *__restrict__ y, int N, int K, int Kp) {
+    extern __shared__ float xs[];
+    for (int k = threadIdx.x; k < Kp; k += blockDim.x)
+        xs[k] = k < K ? __bfloat162float(__float2bfloat16_rn(x[k])) : 0.0f;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (n >= N) return;
+    const uint4 *row = reinterpret_cast<const uint4 *>(w + (size_t)n * Kp);
+    float acc = 0.0f;
+    for (int g = lane; g < Kp / 8; g += 32) {
+        const uint4 v = row[g];
+        const float *xv = xs + 8 * g;
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            acc = fmaf(__uint_as_float(u[i] << 16), xv[2 * i], acc);
+            acc = fmaf(__uint_as_float(u[i] & 0xffff0000u), xv[2 * i + 1], acc);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) y[n] = acc + (bias ? bias[n] : 0.0f);
+}
+
+// ---- mha_tile over the packed tiles of every head: one CTA of 64 threads per head.
+// kv: [H][n_tiles][K 64x64 | V 64x64 | int32 header as 2 bf16] bf16; header > 0: that many keys,
+// < 0: the last non-empty tile with |h| keys, 0: empty.  Per tile the scores q.k * 1/8, the tile's
+// max and exp-weights update the running (max, sum, acc) in f32 (the online softmax of mha_tile,
+// applied per tile); ctx = acc / sum after the last tile.
+constexpr int kTkv = 64, kHd = 64;
+__global__ void mha_decode_paged_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ kv,
+                                        int n_tiles, float *__restrict__ ctx) {
+    __shared__ float qs[kHd], ps[kTkv], red[2];
+    const int h = blockIdx.x, t = threadIdx.x;
+    qs[t] = __uint_as_float((uint32_t)q[h * kHd + t] << 16);
+    float m = -3.0e38f, l = 0.0f, acc = 0.0f;
+    __syncthreads();
+    const size_t tile_elems = 2 * kTkv * kHd + 2;
+    for (int ti = 0; ti < n_tiles; ti++) {
+        const uint16_t *tile = kv + ((size_t)h * n_tiles + ti) * tile_elems;
+        const int32_t hdr = *reinterpret_cast<const int32_t *>(tile + 2 * kTkv * kHd);   // 4-byte aligned
+        const int s = hdr < 0 ? -hdr : hdr;
+        if (s == 0) continue;
+        float sc = -INFINITY;
+        if (t < s) {
+            // the packed tiles are 16,388 bytes apart, so only 4-byte alignment holds: 32-bit loads
+            const uint32_t *kr = reinterpret_cast<const uint32_t *>(tile + t * kHd);
+            float a = 0.0f;
+#pragma unroll 8
+            for (int c = 0; c < kHd / 2; c++) {
+                const uint32_t u = kr[c];
+                a = fmaf(qs[2 * c], __uint_as_float(u << 16), a);
+                a = fmaf(qs[2 * c + 1], __uint_as_float(u & 0xffff0000u), a);
+            }
+            sc = a * 0.125f;
+        }
+        float tm = sc;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o));
+        if ((t & 31) == 0) red[t >> 5] = tm;
+        __syncthreads();
+        const float m_new = fmaxf(m, fmaxf(red[0], red[1]));
+        const float p = t < s ? expf(sc - m_new) : 0.0f;
+        ps[t] = p;
+        __syncthreads();
+        const float corr = expf(m - m_new);
+        float psum = 0.0f, a = 0.0f;
+        const uint16_t *V = tile + kTkv * kHd;
+        for (int j = 0; j < s; j++) {
+            psum += ps[j];
+            a = fmaf(ps[j], __uint_as_float((uint32_t)V[j * kHd + t] << 16), a);
+        }
+        l = l * corr + psum;
+        acc = acc * corr + a;
+        m = m_new;
+        __syncthreads();
+        if (hdr < 0) break;
+    }
+    ctx[h * kHd + t] = l > 0.0f ? acc / l : 0.0f;
+}
+
+}  // namespace
+
+extern "C" {
+
+// ------------------------------------------------------------------------------- buffers
+XdnaBuffer *xdna_buffer_alloc(XdnaDevice *dev, size_t bytes) {
+    if (!dev || bytes == 0) { set_last_error_message("xdna_buffer_alloc: null device or zero size"); return nullptr; }
+    auto *b = new XdnaBuffer();
+    b->ordinal = xdna_device_ordinal(dev);
+    b->bytes = bytes;
+    if (!ck(cudaSetDevice(b->ordinal), "xdna_buffer_alloc") || !ck(cudaMalloc(&b->ptr, bytes), "xdna_buffer_alloc")) {
+        delete b;
+        return nullptr;
+    }
+    return b;
+}
+void xdna_buffer_free(XdnaBuffer *b) {
+    if (!b) return;
+    cudaSetDevice(b->ordinal);
+    cudaFree(b->ptr);
+    delete b;
+}
+void *xdna_buffer_device_ptr(XdnaBuffer *b) { return b ? b->ptr : nullptr; }
+int xdna_buffer_write(XdnaBuffer *b, const void *src, size_t bytes, size_t offset) {
+    if (!b || (!src && bytes)) { set_last_error_message("xdna_buffer_write: null pointer"); return -1; }
+    if (offset > b->bytes || bytes > b->bytes - offset) { set_last_error_message("xdna_buffer_write: range beyond the buffer"); return -1; }
+    if (!ck(cudaSetDevice(b->ordinal), "xdna_buffer_write")) return -1;
+    return ck(cudaMemcpy(static_cast<char *>(b->ptr) + offset, src, bytes, cudaMemcpyHostToDevice), "xdna_buffer_write") ? 0 : -1;
+}
+int xdna_buffer_read(XdnaBuffer *b, void *dst, size_t bytes, size_t offset) {
+    if (!b || (!dst && bytes)) { set_last_error_message("xdna_buffer_read: null pointer"); return -1; }
+    if (offset > b->bytes || bytes > b->bytes - offset) { set_last_error_message("xdna_buffer_read: range beyond the buffer"); return -1; }
+    if (!ck(cudaSetDevice(b->ordinal), "xdna_buffer_read")) return -1;
+    return ck(cudaMemcpy(dst, static_cast<const char *>(b->ptr) + offset, bytes, cudaMemcpyDeviceToHost), "xdna_buffer_read") ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------------- runs
+XdnaRun *xdna_run_start(XdnaDevice *dev, void *stream) {
+    if (!dev) { set_last_error_message("xdna_run_start: null device"); return nullptr; }
+    auto *r = new XdnaRun();
+    r->ordinal = xdna_device_ordinal(dev);
+    if (!ck(cudaSetDevice(r->ordinal), "xdna_run_start") ||
+        !ck(cudaEventCreateWithFlags(&r->ev, cudaEventDisableTiming), "xdna_run_start") ||
+        !ck(cudaEventRecord(r->ev, static_cast<cudaStream_t>(stream)), "xdna_run_start")) {
+        if (r->ev) cudaEventDestroy(r->ev);
+        delete r;
+        return nullptr;
+    }
+    return r;
+}
+int xdna_run_wait(XdnaRun *r, int timeout_ms) {
+    if (!r) { set_last_error_message("xdna_run_wait: null run"); return -1; }
+    cudaSetDevice(r->ordinal);
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        const cudaError_t e = cudaEventQuery(r->ev);
+        if (e == cudaSuccess) return 0;
+        if (e != cudaErrorNotReady) { ck(e, "xdna_run_wait"); return -1; }
+        if (timeout_ms >= 0 && std::chrono::steady_clock::now() - t0 >= std::chrono::milliseconds(timeout_ms)) {
+            set_last_error_message("xdna_run_wait: not completed within the timeout");
+            return 1;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+void xdna_run_free(XdnaRun *r) {
+    if (!r) return;
+    cudaSetDevice(r->ordinal);
+    cudaEventDestroy(r->ev);
+    delete r;
+}
+
+// ------------------------------------------------------------------------ bf16 GEMV (+ norm)
+XdnaGemvBf16 *xdna_gemv_bf16_register(XdnaDevice *dev, const float *w, int K, int N, const float *bias, int norm,
+                                      const float *gamma, const float *beta, float eps) {
+    if (!dev || !w || K < 1 || K > 12288 || N < 1 || norm < 0 || norm > 2 || (norm && !gamma) || (norm == 2 && !beta)) {
+        set_last_error_message("xdna_gemv_bf16_register: null pointer, shape outside 1 <= K <= 12288, N >= 1, or bad "
+                               "norm (0 none, 1 RMS, 2 LN)");
+        return nullptr;
+    }
+    auto *h = new XdnaGemvBf16();
+    h->ordinal = xdna_device_ordinal(dev);
+    h->K = K;
+    h->N = N;
+    h->Kp = (K + 7) & ~7;
+    h->norm = norm;
+    h->eps = eps;
+    // fold (ctx_decode.rs:566-603): W''[k][n] = gamma[k] * W[k][n]; LN bias'[n] = sum_k beta[k] W[k][n]
+    // (f32, k ascending) + bias[n]
+    std::vector<uint16_t> wt((size_t)N * h->Kp, 0);
+    for (int k = 0; k < K; k++) {
+        const float g = norm ? gamma[k] : 1.0f;
+        for (int n = 0; n < N; n++) wt[(size_t)n * h->Kp + k] = bf16_rne(g * w[(size_t)k * N + n]);
+    }
+    std::vector<float> bp(N, 0.0f);
+    for (int n = 0; n < N; n++) {
+        float s = 0.0f;
+        if (norm == 2)
+            for (int k = 0; k < K; k++) s += beta[k] * w[(size_t)k * N + n];
+        bp[n] = s + (bias ? bias[n] : 0.0f);
+    }
+    bool ok = ck(cudaSetDevice(h->ordinal), "xdna_gemv_bf16_register") &&
+              ck(cudaMalloc(&h->w, wt.size() * 2), "xdna_gemv_bf16_register") &&
+              ck(cudaMalloc(&h->bias, (size_t)N * 4), "xdna_gemv_bf16_register") &&
+              ck(cudaMalloc(&h->x, (size_t)h->Kp * 4), "xdna_gemv_bf16_register") &&
+              ck(cudaMalloc(&h->y, (size_t)N * 4), "xdna_gemv_bf16_register") &&
+              ck(cudaMemcpy(h->w, wt.data(), wt.size() * 2, cudaMemcpyHostToDevice), "xdna_gemv_bf16_register") &&
+              ck(cudaMemcpy(h->bias, bp.data(), (size_t)N * 4, cudaMemcpyHostToDevice), "xdna_gemv_bf16_register");
+    if (!ok) {
+        xdna_gemv_bf16_free(h);
+        return nullptr;
+    }
+    return h;
+}
+
+void xdna_gemv_bf16_free(XdnaGemvBf16 *h) {
+    if (!h) return;
+    cudaSetDevice(h->ordinal);
+    cudaFree(h->w);
+    cudaFree(h->bias);
+    cudaFree(h->x);
+    cudaFree(h->y);
+    delete h;
+}
+
+int xdna_gemv_bf16_device(XdnaGemvBf16 *h, const float *x_dev, float *y_dev, void *stream) {
+    if (!h || !x_dev || !y_dev) { set_last_error_message("xdna_gemv_bf16_device: null pointer"); return -1; }
+    if (!ck(cudaSetDevice(h->ordinal), "xdna_gemv_bf16_device")) return -1;
+    const int warps = 8;
+    gemv_bf16_kernel<<<(h->N + warps - 1) / warps, warps * 32, (size_t)h->Kp * 4, static_cast<cudaStream_t>(stream)>>>(
+        h->w, x_dev, h->bias, y_dev, h->N, h->K, h->Kp);
+    return ck(cudaGetLastError(), "xdna_gemv_bf16_device") ? 0 : -1;
+}
+
+int xdna_gemv_bf16(XdnaGemvBf16 *h, const float *x, float *y) {
+    if (!h || !x || !y) { set_last_error_message("xdna_gemv_bf16: null pointer"); return -1; }
+    // the input normalisation in f64 on the host (ctx_decode.rs:617-640)
+    std::vector<float> xn(h->K);
+    if (h->norm == 1) {
+        double ms = 0.0;
+        for (int k = 0; k < h->K; k++) ms += (double)x[k] * (double)x[k];
+        ms /= h->K;
+        const double inv = 1.0 / std::sqrt(ms + (double)h->eps);
+        for (int k = 0; k < h->K; k++) xn[k] = (float)((double)x[k] * inv);
+    } else if (h->norm == 2) {
+        double mean = 0.0, var = 0.0;
+        for (int k = 0; k < h->K; k++) mean += (double)x[k];
+        mean /= h->K;
+        for (int k = 0; k < h->K; k++) var += ((double)x[k] - mean) * ((double)x[k] - mean);
+        var /= h->K;
+        const double inv = 1.0 / std::sqrt(var + (double)h->eps);
+        for (int k = 0; k < h->K; k++) xn[k] = (float)(((double)x[k] - mean) * inv);
+    } else {
+        std::copy(x, x + h->K, xn.begin());
+    }
+    if (!ck(cudaSetDevice(h->ordinal), "xdna_gemv_bf16") ||
+        !ck(cudaMemcpy(h->x, xn.data(), (size_t)h->K * 4, cudaMemcpyHostToDevice), "xdna_gemv_bf16"))
+        return -1;
+    if (xdna_gemv_bf16_device(h, h->x, h->y, nullptr) != 0) return -1;
+    return ck(cudaMemcpy(y, h->y, (size_t)h->N * 4, cudaMemcpyDeviceToHost), "xdna_gemv_bf16") ? 0 : -1;
+}
+
+// ------------------------------------------------------------------- paged decode attention
+int xdna_mha_decode_paged(const uint16_t *q_dev, const uint16_t *kv_dev, int n_heads, int n_tiles, float *ctx_dev,
+                          void *stream) {
+    if (!q_dev || !kv_dev || !ctx_dev || n_heads < 1 || n_tiles < 1) {
+        set_last_error_message("xdna_mha_decode_paged: null pointer or empty shape");
+        return -1;
+    }
+    mha_decode_paged_kernel<<<n_heads, kHd, 0, static_cast<cudaStream_t>(stream)>>>(q_dev, kv_dev, n_tiles, ctx_dev);
+    return ck(cudaGetLastError(), "xdna_mha_decode_paged") ? 0 : -1;
+}
+
+}  // extern "C"
