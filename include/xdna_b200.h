@@ -423,6 +423,38 @@ int xdna_gemv_bf16_device(XdnaGemvBf16 *h, const float *x_dev, float *y_dev, voi
 int xdna_mha_decode_paged(const uint16_t *q_dev, const uint16_t *kv_dev, int n_heads, int n_tiles, float *ctx_dev,
                           void *stream);
 
+
+/* Conformer bricks, op by op (the on-NPU kernels NpuMatmul dispatches, npu-parakeet/src/npu.rs).
+ * All pointers are device pointers on the current device; asynchronous on `stream`.
+ *
+ * Rel-pos multi-head attention, Parakeet shapes (H = 8, d_k = 128, D = 1024, T <= 128): the
+ * relpos_mha brick (route_b_kernels/relpos_mha/relpos_mha.cc:1-60, 193-280) with attention_core's
+ * math (rust/npu-parakeet/src/encoder.rs:285-414): per head AC = (q + u) k^T, BD = (q + v) p^T
+ * read at the rel_shift index BD[i][T - 1 - i + j] (ops.rs:113-133), softmax((AC + BD) / sqrt(128))
+ * over the T keys, ctx = P V.  qkv: [B][T][3 * 1024] f32 (q | k | v per row); pm: the projected
+ * positions [2T - 1][1024] f32, row p for relative position T - 1 - p; pos_u, pos_v: [1024] f32;
+ * ctx: [B][T][1024] f32.  Operands are rounded to bf16 for the tensor cores, f32 accumulation. */
+int xdna_relpos_mha(const float *qkv_dev, const float *pm_dev, const float *pos_u_dev, const float *pos_v_dev, int T,
+                    int B, float *ctx_dev, void *stream);
+/* The conv module's middle (encoder.rs conv_module; ops.rs:92-110; dwconv1d.cc): x = the
+ * pointwise-1 output [B][T][2C] f32 (values in channels 0..C-1, gates in C..2C-1);
+ * g = x_val * sigmoid(x_gate); y[b][t][c] = silu(bias[c] + sum_j taps[c][j] g[t + j - (k-1)/2][c])
+ * over the taps inside [0, T) ('same' zero padding, BatchNorm folded into taps and bias);
+ * y: [B][T][C] f32, ready for pointwise-2.  taps: [C][k] f32, k one of 3, 5, 7, 9, 15, 31. */
+int xdna_dwconv1d_glu_silu(const float *x_dev, int B, int T, int C, const float *taps_dev, int k,
+                           const float *bias_dev, float *y_dev, void *stream);
+/* One conv2d of the /8 subsample front end (route_b_kernels/subsample_conv2d/
+ * subsample_patch_embed.cc: bf16 operands, f32 accumulation, optional ReLU, bf16 out):
+ * x [B][ci][hin][win] bf16, w [co][ci/groups][kh][kw] bf16, bias [co] f32 (nullable) ->
+ * out [B][co][hout][wout] bf16, hout = (hin + 2 pad - kh) / stride + 1 (likewise wout).
+ * Covers conv.0 (1 -> 256, k3 s2 p1, ReLU), the depthwise conv.2/.5 (groups = ci) and the
+ * pointwise conv.3/.6 (k1, ReLU).  The accumulation starts at the bias and adds the taps in
+ * (input channel, row, column) order, as conv2d of ops.rs:38-89; a pointwise conv (k1 s1 p0,
+ * groups 1) sums the taps first and adds the bias last, as that function's matmul path. */
+int xdna_subsample_conv2d(const uint16_t *x_dev, int B, int ci, int hin, int win, const uint16_t *w_dev,
+                          const float *bias_dev, int co, int kh, int kw, int stride, int pad, int groups, int relu,
+                          uint16_t *out_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

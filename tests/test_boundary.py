@@ -110,6 +110,9 @@ def test_op_layer_null_errors(xl):
     assert L.xdna_gemv_bf16_register(None, None, 8, 8, None, 0, None, None, 1e-5) is None
     assert L.xdna_gemv_bf16(None, None, None) == -1
     assert L.xdna_mha_decode_paged(None, None, 12, 7, None, None) == -1
+    assert L.xdna_relpos_mha(None, None, None, None, 125, 1, None, None) == -1
+    assert L.xdna_dwconv1d_glu_silu(None, 1, 125, 1024, None, 9, None, None, None) == -1
+    assert L.xdna_subsample_conv2d(None, 1, 1, 8, 8, None, None, 4, 3, 3, 2, 1, 1, 1, None, None) == -1
     L.xdna_buffer_free(None)
     L.xdna_run_free(None)
     L.xdna_gemv_bf16_free(None)

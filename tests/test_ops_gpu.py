@@ -228,3 +228,119 @@ def test_run_wait_is_bounded(X, dev):
         assert L.xdna_run_wait(r, 0) == 0
     finally:
         L.xdna_run_free(r)
+
+
+# ------------------------------------------------------------------ conformer bricks
+
+
+def _conv_case(seed, ci, h, w, co, k, stride, pad, groups, B=2, zero_frac=0.1):
+    rng = np.random.default_rng(seed)
+    x = bf16(rng.standard_normal((B, ci, h, w)).astype(np.float32))
+    wt = bf16((rng.standard_normal((co, ci // groups, k, k)) * 0.3).astype(np.float32))
+    wt[rng.random(wt.shape) < zero_frac] = 0.0
+    b = rng.standard_normal(co).astype(np.float32)
+    return x, wt, b
+
+
+@pytest.mark.parametrize("case", [
+    dict(ci=1, h=125, w=80, co=256, k=3, stride=2, pad=1, groups=1, relu=1),     # conv.0 (odd frames)
+    dict(ci=256, h=63, w=40, co=256, k=3, stride=2, pad=1, groups=256, relu=0),  # conv.2 depthwise
+    dict(ci=256, h=32, w=20, co=256, k=1, stride=1, pad=0, groups=1, relu=1),    # conv.3 pointwise
+    dict(ci=8, h=9, w=7, co=12, k=3, stride=1, pad=1, groups=4, relu=0),         # grouped, stride 1
+])
+def test_subsample_conv2d_bit_exact_with_oracle(X, case):
+    """Bit-exact against the oracle's conv2d (ops.rs:38-89, pinned to golden_subsample.py's
+    im2col == conv gate) on bf16 operands: bf16 x bf16 products are exact in f32, the adds
+    follow the same order, one bf16 rounding of the result."""
+    import torch
+    from oracle import oracle as O
+    c = dict(case)
+    relu = c.pop("relu")
+    x, wt, b = _conv_case(sum(c.values()), **c)
+    B = x.shape[0]
+    ho = (c["h"] + 2 * c["pad"] - c["k"]) // c["stride"] + 1
+    wo = (c["w"] + 2 * c["pad"] - c["k"]) // c["stride"] + 1
+    xd = torch.from_numpy(bf16_bits(x).view(np.int16)).cuda()
+    wd = torch.from_numpy(bf16_bits(wt).view(np.int16)).cuda()
+    bd = torch.from_numpy(b).cuda()
+    out = torch.zeros((B, c["co"], ho, wo), dtype=torch.int16, device="cuda")
+    rc = X.lib().xdna_subsample_conv2d(xd.data_ptr(), B, c["ci"], c["h"], c["w"], wd.data_ptr(), bd.data_ptr(),
+                                       c["co"], c["k"], c["k"], c["stride"], c["pad"], c["groups"], relu,
+                                       out.data_ptr(), None)
+    assert rc == 0, X.last_error()
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint16)
+    for bi in range(B):
+        ref = O.conv2d(x[bi], wt, b, c["stride"], c["pad"], c["groups"])
+        if relu:
+            ref = np.maximum(ref, 0.0)
+        np.testing.assert_array_equal(got[bi], bf16_bits(ref))
+
+
+def test_subsample_conv2d_rejects_bad_groups(X):
+    assert X.lib().xdna_subsample_conv2d(1, 1, 6, 4, 4, 1, None, 4, 3, 3, 1, 1, 4, 0, 1, None) == -1
+    assert "groups" in X.last_error()
+
+
+@pytest.mark.parametrize("k,T,C,B", [(9, 125, 1024, 2), (9, 1, 1024, 1), (5, 77, 512, 3), (3, 40, 100, 1),
+                                     (31, 64, 256, 2)])
+def test_dwconv1d_glu_silu_matches_conv_module(X, k, T, C, B):
+    """GLU -> dwconv1d (the oracle's, ops.rs:92-110, pinned to golden_dwconv1d_k9.py) -> SiLU,
+    as the conv module runs them, within f32 rounding (the exp of CUDA and of the host libm
+    may differ by an ulp, so the bar is relative 1e-5 of the term magnitudes)."""
+    import torch
+    from oracle import oracle as O
+    rng = np.random.default_rng(k * 1000 + T)
+    x = rng.standard_normal((B, T, 2 * C)).astype(np.float32)
+    taps = (rng.standard_normal((C, k)) * 0.3).astype(np.float32)
+    bias = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    xd, td, bd = (torch.from_numpy(a).cuda() for a in (x, taps, bias))
+    yd = torch.full((B, T, C), float("nan"), dtype=torch.float32, device="cuda")
+    rc = X.lib().xdna_dwconv1d_glu_silu(xd.data_ptr(), B, T, C, td.data_ptr(), k, bd.data_ptr(), yd.data_ptr(), None)
+    assert rc == 0, X.last_error()
+    got = yd.cpu().numpy()
+    for bi in range(B):
+        g = (x[bi, :, :C] * (1.0 / (1.0 + np.exp(-x[bi, :, C:].astype(np.float64))))).astype(np.float32)
+        dw = O.dwconv1d(np.ascontiguousarray(g.T), taps, bias).astype(np.float64)
+        ref = (dw * (1.0 / (1.0 + np.exp(-dw)))).T
+        scale = np.abs(bias)[None, :] + sum(np.abs(np.roll(g, -(j - (k - 1) // 2), axis=0)) * np.abs(taps[:, j])
+                                            for j in range(k)) + 1e-30
+        np.testing.assert_array_less(np.abs(got[bi] - ref), 1e-5 * scale + 1e-6)
+    assert X.lib().xdna_dwconv1d_glu_silu(xd.data_ptr(), B, T, C, td.data_ptr(), 4, bd.data_ptr(), yd.data_ptr(),
+                                          None) == -1
+
+
+@pytest.mark.parametrize("T,B", [(125, 2), (128, 1), (1, 1), (37, 3)])
+def test_relpos_mha_matches_attention_core(X, T, B):
+    """The rel-pos attention brick against attention_core restated in f64 (rel_shift through the
+    oracle's, pinned bit-exact to the reference golden): bf16 tensor-core operands put the bar at
+    rel-L2 1e-2 per clip and head."""
+    import torch
+    from oracle import oracle as O
+    H, DK, D = 8, 128, 1024
+    rng = np.random.default_rng(T * 10 + B)
+    qkv = (rng.standard_normal((B, T, 3 * D)) * 0.5).astype(np.float32)
+    pm = (rng.standard_normal((2 * T - 1, D)) * 0.5).astype(np.float32)
+    pu = (rng.standard_normal(D) * 0.1).astype(np.float32)
+    pv = (rng.standard_normal(D) * 0.1).astype(np.float32)
+    qd, pmd, pud, pvd = (torch.from_numpy(a).cuda() for a in (qkv, pm, pu, pv))
+    ctx = torch.full((B, T, D), float("nan"), dtype=torch.float32, device="cuda")
+    rc = X.lib().xdna_relpos_mha(qd.data_ptr(), pmd.data_ptr(), pud.data_ptr(), pvd.data_ptr(), T, B,
+                                 ctx.data_ptr(), None)
+    assert rc == 0, X.last_error()
+    got = ctx.cpu().numpy()
+    for bi in range(B):
+        q, k, v = (qkv[bi, :, i * D:(i + 1) * D].astype(np.float64) for i in range(3))
+        bd = np.stack([(q[:, h * DK:(h + 1) * DK] + pv[h * DK:(h + 1) * DK]) @ pm[:, h * DK:(h + 1) * DK].T
+                       for h in range(H)]).astype(np.float32)
+        bds = O.rel_shift(bd).astype(np.float64)
+        for h in range(H):
+            sl = slice(h * DK, (h + 1) * DK)
+            ac = (q[:, sl] + pu[sl]) @ k[:, sl].T
+            s = (ac + bds[h]) / np.sqrt(DK)
+            p = np.exp(s - s.max(axis=1, keepdims=True))
+            ref = (p / p.sum(axis=1, keepdims=True)) @ v[:, sl]
+            rel = np.linalg.norm(got[bi, :, sl] - ref) / np.linalg.norm(ref)
+            assert rel < 1e-2, (bi, h, rel)
+    assert X.lib().xdna_relpos_mha(qd.data_ptr(), pmd.data_ptr(), pud.data_ptr(), pvd.data_ptr(), 129, B,
+                                   ctx.data_ptr(), None) == -1

@@ -174,6 +174,12 @@ def lib():
         L.xdna_gemv_bf16_device.restype = i
         L.xdna_mha_decode_paged.argtypes = [vp, vp, i, i, vp, vp]
         L.xdna_mha_decode_paged.restype = i
+        L.xdna_relpos_mha.argtypes = [vp, vp, vp, vp, i, i, vp, vp]
+        L.xdna_relpos_mha.restype = i
+        L.xdna_dwconv1d_glu_silu.argtypes = [vp, i, i, i, vp, i, vp, vp, vp]
+        L.xdna_dwconv1d_glu_silu.restype = i
+        L.xdna_subsample_conv2d.argtypes = [vp, i, i, i, i, vp, vp, i, i, i, i, i, i, i, vp, vp]
+        L.xdna_subsample_conv2d.restype = i
         _LIB = L
     return _LIB
 

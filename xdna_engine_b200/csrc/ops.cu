@@ -8,6 +8,10 @@
 //  * fused norm + GEMV      CtxDecode::register_fused + fused_norm_gemv (ctx_decode.rs:566-643): the
 //                           norm's gamma folded into the weight (W'' = diag(gamma) W), LN's beta into
 //                           the bias (bias' = beta . W + bias), the input statistics in f64 on the host
+//  * conformer bricks       dwconv1d_glu_silu: GLU -> depthwise conv1d k 'same' -> SiLU (the conv
+//                           module's middle, encoder.rs conv_module + ops.rs:92-110, the dwconv1d.cc
+//                           brick); subsample_conv2d: one conv2d of the /8 subsample with bf16
+//                           operands, f32 accumulation, optional ReLU, bf16 out (subsample_patch_embed.cc)
 //  * paged decode attention the mha_tile kernel (route_b_kernels/mha_decode/mha_decode.cc:90-168) over
 //                           the reference's packed K/V tiles (ctx_decode.rs:468-555)
 #include <cuda_runtime.h>
@@ -150,6 +154,90 @@ __global__ void mha_decode_paged_kernel(const uint16_t *__restrict__ q, const ui
         if (hdr < 0) break;
     }
     ctx[h * kHd + t] = l > 0.0f ? acc / l : 0.0f;
+}
+
+
+// ---- conv module middle: y[b][t][c] = silu(bias[c] + sum_j taps[c][j] * glu[b][t + j - pad][c])
+// with glu[t][c] = x[t][c] * sigmoid(x[t][C + c]) (x = pw1 output [B][T][2C]); taps skipped where
+// t + j - pad falls outside [0, T) (ops.rs:92-110: the sum starts at the bias and adds the valid
+// taps in order).  One thread per channel walks kRows rows of one clip with the last k GLU
+// values in a register window; loads and stores are coalesced across channels.
+constexpr int kDwRows = 32;
+__device__ __forceinline__ float sigmoid_f(float v) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))); }
+template <int k>
+__global__ void __launch_bounds__(128) dwconv1d_glu_silu_kernel(const float *__restrict__ x, int T, int C,
+                                                                const float *__restrict__ taps,
+                                                                const float *__restrict__ bias, float *__restrict__ y) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.z;
+    if (c >= C) return;
+    constexpr int pad = (k - 1) / 2;
+    const int t0 = blockIdx.y * kDwRows;
+    const float *xb = x + (size_t)b * T * 2 * C;
+    float tp[k];
+#pragma unroll
+    for (int j = 0; j < k; j++) tp[j] = taps[(size_t)c * k + j];
+    const float bc = bias[c];
+    auto glu = [&](int s) -> float {
+        const float *r = xb + (size_t)s * 2 * C;
+        return __fmul_rn(r[c], sigmoid_f(r[C + c]));
+    };
+    float win[k];                             // win[j] = glu(t + j - pad) for the current t
+#pragma unroll
+    for (int j = 0; j < k - 1; j++) {
+        const int s = t0 + j - pad;
+        win[j + 1] = (s >= 0 && s < T) ? glu(s) : 0.0f;
+    }
+    const int t_end = min(T, t0 + kDwRows);
+    for (int t = t0; t < t_end; t++) {
+#pragma unroll
+        for (int j = 0; j < k - 1; j++) win[j] = win[j + 1];
+        const int s_new = t + k - 1 - pad;
+        win[k - 1] = s_new < T ? glu(s_new) : 0.0f;
+        float acc = bc;
+#pragma unroll
+        for (int j = 0; j < k; j++) {
+            const int s = t + j - pad;
+            if (s < 0 || s >= T) continue;
+            acc = __fadd_rn(acc, __fmul_rn(tp[j], win[j]));
+        }
+        y[((size_t)b * T + t) * C + c] = __fmul_rn(acc, sigmoid_f(acc));
+    }
+}
+
+// ---- conv2d of the subsample (ops.rs:38-89 order): out[b][o][oh][ow] = bias[o] + sum over the
+// group's input channels ic and taps (i, j), in that order, of w[o][ic][i][j] * x[b][g*gci+ic][ih][iw]
+// (zero-weight taps and taps outside the padded image skipped; a pointwise conv adds the bias
+// after the sum, as the reference's matmul fast path does); ReLU optional; x, w bf16, the
+// products exact in f32, every add rounded to f32, the result rounded once to bf16.  NCHW; one
+// thread per output position, consecutive threads on consecutive ow.
+__global__ void __launch_bounds__(256) conv2d_bf16_kernel(const uint16_t *__restrict__ x, int ci, int hin, int win,
+                                                          const uint16_t *__restrict__ w,
+                                                          const float *__restrict__ bias, int co, int kh, int kw,
+                                                          int stride, int pad, int groups, int relu, int hout,
+                                                          int wout, uint16_t *__restrict__ out) {
+    const int p = blockIdx.x * blockDim.x + threadIdx.x, o = blockIdx.y, b = blockIdx.z;
+    if (p >= hout * wout) return;
+    const int oh = p / wout, ow = p % wout;
+    const int gci = ci / groups, g = o / (co / groups);
+    // the pointwise case is conv2d's matmul fast path: the dot product first, then + bias
+    const bool pointwise = kh == 1 && kw == 1 && groups == 1 && stride == 1 && pad == 0;
+    float acc = bias && !pointwise ? bias[o] : 0.0f;
+    const uint16_t *wo = w + (size_t)o * gci * kh * kw;
+    for (int ic = 0; ic < gci; ic++) {
+        const uint16_t *xp = x + ((size_t)b * ci + g * gci + ic) * hin * win;
+        for (int i = 0; i < kh; i++) {
+            const int ih = oh * stride + i - pad;
+            for (int j = 0; j < kw; j++) {
+                const float wv = __uint_as_float((uint32_t)wo[(ic * kh + i) * kw + j] << 16);
+                const int iw = ow * stride + j - pad;
+                if (wv == 0.0f || ih < 0 || ih >= hin || iw < 0 || iw >= win) continue;
+                acc = __fadd_rn(acc, __fmul_rn(wv, __uint_as_float((uint32_t)xp[(size_t)ih * win + iw] << 16)));
+            }
+        }
+    }
+    if (bias && pointwise) acc = __fadd_rn(acc, bias[o]);
+    if (relu) acc = fmaxf(acc, 0.0f);
+    out[(((size_t)b * co + o) * hout + oh) * wout + ow] = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
 }
 
 }  // namespace
@@ -323,6 +411,47 @@ int xdna_mha_decode_paged(const uint16_t *q_dev, const uint16_t *kv_dev, int n_h
     }
     mha_decode_paged_kernel<<<n_heads, kHd, 0, static_cast<cudaStream_t>(stream)>>>(q_dev, kv_dev, n_tiles, ctx_dev);
     return ck(cudaGetLastError(), "xdna_mha_decode_paged") ? 0 : -1;
+}
+
+// ------------------------------------------------------------------------- conformer bricks
+int xdna_dwconv1d_glu_silu(const float *x_dev, int B, int T, int C, const float *taps_dev, int k,
+                           const float *bias_dev, float *y_dev, void *stream) {
+    if (!x_dev || !taps_dev || !bias_dev || !y_dev || B < 1 || B > 65535 || T < 1 || C < 1 ||
+        (k != 3 && k != 5 && k != 7 && k != 9 && k != 15 && k != 31)) {
+        set_last_error_message("xdna_dwconv1d_glu_silu: null pointer, empty shape, or k not one of 3 5 7 9 15 31");
+        return -1;
+    }
+    const dim3 grid((C + 127) / 128, (T + kDwRows - 1) / kDwRows, B);
+    auto st = static_cast<cudaStream_t>(stream);
+    switch (k) {
+    case 3: dwconv1d_glu_silu_kernel<3><<<grid, 128, 0, st>>>(x_dev, T, C, taps_dev, bias_dev, y_dev); break;
+    case 5: dwconv1d_glu_silu_kernel<5><<<grid, 128, 0, st>>>(x_dev, T, C, taps_dev, bias_dev, y_dev); break;
+    case 7: dwconv1d_glu_silu_kernel<7><<<grid, 128, 0, st>>>(x_dev, T, C, taps_dev, bias_dev, y_dev); break;
+    case 9: dwconv1d_glu_silu_kernel<9><<<grid, 128, 0, st>>>(x_dev, T, C, taps_dev, bias_dev, y_dev); break;
+    case 15: dwconv1d_glu_silu_kernel<15><<<grid, 128, 0, st>>>(x_dev, T, C, taps_dev, bias_dev, y_dev); break;
+    default: dwconv1d_glu_silu_kernel<31><<<grid, 128, 0, st>>>(x_dev, T, C, taps_dev, bias_dev, y_dev); break;
+    }
+    return ck(cudaGetLastError(), "xdna_dwconv1d_glu_silu") ? 0 : -1;
+}
+
+int xdna_subsample_conv2d(const uint16_t *x_dev, int B, int ci, int hin, int win, const uint16_t *w_dev,
+                          const float *bias_dev, int co, int kh, int kw, int stride, int pad, int groups, int relu,
+                          uint16_t *out_dev, void *stream) {
+    if (!x_dev || !w_dev || !out_dev || B < 1 || B > 65535 || ci < 1 || hin < 1 || win < 1 || co < 1 || co > 65535 ||
+        kh < 1 || kw < 1 || stride < 1 || pad < 0 || groups < 1 || ci % groups || co % groups) {
+        set_last_error_message("xdna_subsample_conv2d: null pointer, empty shape, or groups not dividing ci and co");
+        return -1;
+    }
+    const int hout = (hin + 2 * pad - kh) / stride + 1, wout = (win + 2 * pad - kw) / stride + 1;
+    if (hout < 1 || wout < 1) {
+        set_last_error_message("xdna_subsample_conv2d: kernel larger than the padded image");
+        return -1;
+    }
+    const dim3 grid((hout * wout + 255) / 256, co, B);
+    conv2d_bf16_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x_dev, ci, hin, win, w_dev, bias_dev, co,
+                                                                            kh, kw, stride, pad, groups, relu, hout,
+                                                                            wout, out_dev);
+    return ck(cudaGetLastError(), "xdna_subsample_conv2d") ? 0 : -1;
 }
 
 }  // extern "C"

@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
     }
     m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
-    if (lane == 0) atomicMax(amax + clip, __float_as_uint(m));
+    if (lane == 0 && amax) atomicMax(amax + clip, __float_as_uint(m));
 }
 
 }  // namespace parakeet
@@ -843,6 +843,29 @@ static int parakeet_enqueue(XdnaParakeet *m, const float *mel_dev, int B, float 
 }
 
 extern "C" {
+
+// The rel-pos attention brick alone (relpos_mha.cc's contract; attention_core, encoder.rs:285-414)
+int xdna_relpos_mha(const float *qkv_dev, const float *pm_dev, const float *pos_u_dev, const float *pos_v_dev, int T,
+                    int B, float *ctx_dev, void *stream) {
+    if (!qkv_dev || !pm_dev || !pos_u_dev || !pos_v_dev || !ctx_dev || T < 1 || T > parakeet::MAX_T || B < 1 ||
+        B > 65535) {
+        set_last_error_message("xdna_relpos_mha: null pointer, or T outside 1..128, or B outside 1..65535");
+        return -1;
+    }
+    cudaError_t e = cudaFuncSetAttribute(parakeet::relpos_attention_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, parakeet::ATT_SMEM);
+    if (e == cudaSuccess) {
+        parakeet::relpos_attention_kernel<<<dim3(parakeet::H, B), parakeet::ATT_THREADS, parakeet::ATT_SMEM,
+                                            static_cast<cudaStream_t>(stream)>>>(qkv_dev, pm_dev, pos_u_dev,
+                                                                                  pos_v_dev, T, ctx_dev, nullptr);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) {
+        set_last_error_message(std::string("xdna_relpos_mha: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
 
 // The second call with the same (batch, input, output) captures the forward into a CUDA graph
 // on a private stream; that call and later ones replay it on `stream` (one launch instead of
