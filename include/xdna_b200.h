@@ -249,6 +249,8 @@ int xdna_opt_sync(XdnaOptDecoder *dec, void *stream);
 /* Bytes of weights one decoded token streams from HBM (int8 rows + per-row scale/bias). */
 size_t xdna_opt_stream_bytes_per_token(const XdnaOptDecoder *dec);
 int xdna_opt_grid(const XdnaOptDecoder *dec);
+/* the configuration the decoder was created with (for one made by xdna_opt_load) */
+int xdna_opt_config(const XdnaOptDecoder *dec, XdnaOptConfig *out);
 /* Debugging aid: when trace_dev (device, [n_steps][2*n_layers+1][d_model] f32) is non-NULL,
  * later launches record the residual stream after each attention and each FFN residual add,
  * then the final LayerNorm output, per step of the launch.  NULL turns it off. */
@@ -385,6 +387,19 @@ void *xdna_buffer_device_ptr(XdnaBuffer *b);
 int xdna_buffer_write(XdnaBuffer *b, const void *src, size_t bytes, size_t offset);
 int xdna_buffer_read(XdnaBuffer *b, void *dst, size_t bytes, size_t offset);
 
+/* Fused arenas: FusedArena (rust/npu-xrt/src/lib.rs:641-744), the three resident regions a
+ * fused dispatch reads and writes -- 0 input (written per call), 1 output (read back), 2
+ * scratch (weights, KV caches, intermediates) -- each a device buffer addressed by byte offset
+ * (write_at / read_at).  A zero-size region is allocated with 2 bytes, as the reference does.
+ * xdna_arena_region hands out a region as an XdnaBuffer (owned by the arena) for its device
+ * pointer.  write/read return 0, or -1 with xdna_last_error() set. */
+typedef struct XdnaArena XdnaArena;
+XdnaArena *xdna_arena_create(XdnaDevice *dev, size_t input_bytes, size_t output_bytes, size_t scratch_bytes);
+void xdna_arena_free(XdnaArena *a);
+XdnaBuffer *xdna_arena_region(XdnaArena *a, int which);
+int xdna_arena_write(XdnaArena *a, int which, size_t offset, const void *src, size_t bytes);
+int xdna_arena_read(XdnaArena *a, int which, size_t offset, void *dst, size_t bytes);
+
 /* Asynchronous runs.  Replace shim_run_matmul8_start / shim_run_elf_start + shim_run_wait +
  * shim_run_free (xrt_shim.h:51-54, 75): a run marks all work enqueued on `stream` (a
  * cudaStream_t; NULL = the legacy default stream) so far; xdna_run_wait returns 0 when it has
@@ -454,6 +469,35 @@ int xdna_dwconv1d_glu_silu(const float *x_dev, int B, int T, int C, const float 
 int xdna_subsample_conv2d(const uint16_t *x_dev, int B, int ci, int hin, int win, const uint16_t *w_dev,
                           const float *bias_dev, int co, int kh, int kw, int stride, int pad, int groups, int relu,
                           uint16_t *out_dev, void *stream);
+
+
+/* ------------------------------------------------- weight stores (npu-weights arena, npy dirs) */
+/* A baked weight arena: one safetensors file (rust/npu-weights/src/arena.rs:13-100) --
+ * tensors BF16 or F32, "__metadata__" {format_version, arch, source_ref, source_fingerprint}.
+ * xdna_weights_open memory-maps it and checks arch == expect_arch (NULL: any) and
+ * format_version == 1, failing with the reference's messages ("arena arch ... != expected ...",
+ * "arena format_version N != 1 (rebake)").  NULL on error. */
+typedef struct XdnaWeightArena XdnaWeightArena;
+XdnaWeightArena *xdna_weights_open(const char *path, const char *expect_arch);
+void xdna_weights_close(XdnaWeightArena *a);
+/* number of tensors; name i in sorted order (NULL out of range) */
+int xdna_weights_count(const XdnaWeightArena *a);
+const char *xdna_weights_name(const XdnaWeightArena *a, int i);
+/* a metadata string, or NULL */
+const char *xdna_weights_meta(const XdnaWeightArena *a, const char *key);
+/* dtype (0 F32, 1 BF16) and up to max_dims extents of tensor `name`; returns its rank, -1 if absent */
+int xdna_weights_info(const XdnaWeightArena *a, const char *name, int *dtype, int64_t *shape, int max_dims);
+/* tensor_f32 (arena.rs:62-78): n values upcast to f32; 0, or -1 (absent, or n not its size) */
+int xdna_weights_read_f32(const XdnaWeightArena *a, const char *name, float *out, size_t n);
+/* tensor_bf16 (arena.rs:86-100): the raw bf16 bits; 0, 1 for an F32 tensor (nothing copied), -1 */
+int xdna_weights_read_bf16(const XdnaWeightArena *a, const char *name, uint16_t *out, size_t n);
+
+/* Opt::load (opt125m_decode.rs:155-180) from a baked arena of arch "opt" (a file) or from the
+ * npy directory it was baked from (a directory; names + ".npy"), with the names of
+ * rust/npu-weights/src/arch/opt.rs:7-16; the configuration comes from the shapes (head_dim 64,
+ * eps 1e-5).  lm_head.weight must be embed_tokens transposed (OPT ties them).  Then as
+ * xdna_opt_create (max_ctx <= 0: min(max_pos, 2048)).  NULL on error. */
+XdnaOptDecoder *xdna_opt_load(XdnaDevice *dev, const char *path, int max_ctx, int grid);
 
 #ifdef __cplusplus
 }

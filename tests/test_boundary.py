@@ -105,6 +105,12 @@ def test_op_layer_null_errors(xl):
     assert L.xdna_buffer_alloc(None, 64) is None
     assert "null" in xl.last_error()
     assert L.xdna_buffer_write(None, None, 0, 0) == -1
+    assert L.xdna_arena_create(None, 8, 8, 8) is None
+    assert L.xdna_arena_write(None, 0, 0, None, 0) == -1
+    L.xdna_arena_free(None)
+    assert L.xdna_weights_open(None, None) is None
+    assert L.xdna_weights_count(None) == -1
+    assert L.xdna_opt_config(None, None) == -1
     assert L.xdna_run_start(None, None) is None
     assert L.xdna_run_wait(None, 0) == -1
     assert L.xdna_gemv_bf16_register(None, None, 8, 8, None, 0, None, None, 1e-5) is None

@@ -344,3 +344,27 @@ def test_relpos_mha_matches_attention_core(X, T, B):
             assert rel < 1e-2, (bi, h, rel)
     assert X.lib().xdna_relpos_mha(qd.data_ptr(), pmd.data_ptr(), pud.data_ptr(), pvd.data_ptr(), 129, B,
                                    ctx.data_ptr(), None) == -1
+
+
+def test_fused_arena_regions(X, dev):
+    """FusedArena (lib.rs:641-744): three regions, byte-offset write_at / read_at, a zero-size
+    region rounded up to 2 bytes, region index checked."""
+    L = X.lib()
+    a = L.xdna_arena_create(dev.handle, 4096, 0, 1 << 16)
+    assert a, X.last_error()
+    try:
+        regs = [L.xdna_arena_region(a, i) for i in range(3)]
+        ptrs = [L.xdna_buffer_device_ptr(r) for r in regs]
+        assert all(ptrs) and len(set(ptrs)) == 3
+        assert L.xdna_arena_region(a, 3) is None
+        x = np.arange(256, dtype=np.uint8)
+        assert L.xdna_arena_write(a, 2, 1000, x.ctypes.data, 256) == 0
+        y = np.zeros(256, np.uint8)
+        assert L.xdna_arena_read(a, 2, 1000, y.ctypes.data, 256) == 0
+        np.testing.assert_array_equal(x, y)
+        two = np.array([7, 9], np.uint8)
+        assert L.xdna_arena_write(a, 1, 0, two.ctypes.data, 2) == 0
+        assert L.xdna_arena_write(a, 1, 1, two.ctypes.data, 2) == -1
+        assert L.xdna_arena_write(a, 0, 4095, x.ctypes.data, 2) == -1
+    finally:
+        L.xdna_arena_free(a)

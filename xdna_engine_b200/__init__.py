@@ -145,6 +145,8 @@ def lib():
         L.xdna_opt_stream_bytes_per_token.restype = sz
         L.xdna_opt_grid.argtypes = [vp]
         L.xdna_opt_grid.restype = i
+        L.xdna_opt_config.argtypes = [vp, vp]
+        L.xdna_opt_config.restype = i
         L.xdna_opt_set_timing.argtypes = [vp, vp]
         L.xdna_opt_set_timing.restype = i
         L.xdna_opt_set_trace.argtypes = [vp, vp]
@@ -160,6 +162,15 @@ def lib():
         L.xdna_buffer_write.restype = i
         L.xdna_buffer_read.argtypes = [vp, vp, sz, sz]
         L.xdna_buffer_read.restype = i
+        L.xdna_arena_create.argtypes = [vp, sz, sz, sz]
+        L.xdna_arena_create.restype = vp
+        L.xdna_arena_free.argtypes = [vp]
+        L.xdna_arena_region.argtypes = [vp, i]
+        L.xdna_arena_region.restype = vp
+        L.xdna_arena_write.argtypes = [vp, i, sz, vp, sz]
+        L.xdna_arena_write.restype = i
+        L.xdna_arena_read.argtypes = [vp, i, sz, vp, sz]
+        L.xdna_arena_read.restype = i
         L.xdna_run_start.argtypes = [vp, vp]
         L.xdna_run_start.restype = vp
         L.xdna_run_wait.argtypes = [vp, i]
@@ -180,6 +191,23 @@ def lib():
         L.xdna_dwconv1d_glu_silu.restype = i
         L.xdna_subsample_conv2d.argtypes = [vp, i, i, i, i, vp, vp, i, i, i, i, i, i, i, vp, vp]
         L.xdna_subsample_conv2d.restype = i
+        L.xdna_weights_open.argtypes = [C.c_char_p, C.c_char_p]
+        L.xdna_weights_open.restype = vp
+        L.xdna_weights_close.argtypes = [vp]
+        L.xdna_weights_count.argtypes = [vp]
+        L.xdna_weights_count.restype = i
+        L.xdna_weights_name.argtypes = [vp, i]
+        L.xdna_weights_name.restype = C.c_char_p
+        L.xdna_weights_meta.argtypes = [vp, C.c_char_p]
+        L.xdna_weights_meta.restype = C.c_char_p
+        L.xdna_weights_info.argtypes = [vp, C.c_char_p, vp, vp, i]
+        L.xdna_weights_info.restype = i
+        L.xdna_weights_read_f32.argtypes = [vp, C.c_char_p, vp, sz]
+        L.xdna_weights_read_f32.restype = i
+        L.xdna_weights_read_bf16.argtypes = [vp, C.c_char_p, vp, sz]
+        L.xdna_weights_read_bf16.restype = i
+        L.xdna_opt_load.argtypes = [vp, C.c_char_p, i, i]
+        L.xdna_opt_load.restype = vp
         _LIB = L
     return _LIB
 
@@ -316,9 +344,29 @@ class OptDecoder:
         h = lib().xdna_opt_create(device.handle, C.byref(c), C.byref(w), self.max_ctx, grid)
         if not h:
             raise XdnaError(last_error())
+        self._adopt(h)
+
+    def _adopt(self, h):
         self.handle = h
         self.grid = lib().xdna_opt_grid(h)
         self.stream_bytes_per_token = lib().xdna_opt_stream_bytes_per_token(h)
+
+    @classmethod
+    def load(cls, device: Device, path: str, max_ctx: int | None = None, grid: int = 0):
+        """Opt::load from a baked arena (a .safetensors file of arch "opt") or the npy directory
+        it was baked from; the configuration comes from the tensor shapes."""
+        h = lib().xdna_opt_load(device.handle, os.fsencode(path), max_ctx or 0, grid)
+        if not h:
+            raise XdnaError(last_error())
+        c = _OptConfig()
+        _check(lib().xdna_opt_config(h, C.byref(c)))
+        self = cls.__new__(cls)
+        self.cfg = OptConfig(c.n_layers, c.d_model, c.n_heads, c.head_dim, c.ffn, c.vocab, c.max_pos,
+                             float(np.float32(c.eps)))
+        self.device = device
+        self.max_ctx = max_ctx or min(c.max_pos, 2048)
+        self._adopt(h)
+        return self
 
     def generate(self, prompt, n_new: int, want_logits: bool = False):
         """Greedy decode (host in, host out)."""

@@ -43,6 +43,10 @@
 #include "../../include/npu_engine.h"
 #include "../../include/xdna_b200.h"
 
+namespace xdna {
+void read_npy_f32(const std::string &path, std::vector<size_t> &shape, std::vector<float> &data);   // weights.cu
+}
+
 namespace {
 
 thread_local std::string g_npu_err;
@@ -212,45 +216,8 @@ struct Npy {
     std::vector<float> data;
 };
 Npy read_npy(const std::string &path) {
-    std::ifstream f(path, std::ios::binary);
-    if (!f) throw std::runtime_error("read " + path + ": No such file or directory");
-    char magic[6];
-    f.read(magic, 6);
-    if (!f || std::memcmp(magic, "\x93NUMPY", 6) != 0) throw std::runtime_error("read " + path + ": not an npy file");
-    unsigned char ver[2];
-    f.read(reinterpret_cast<char *>(ver), 2);
-    uint32_t hlen = 0;
-    if (ver[0] == 1) {
-        unsigned char b[2];
-        f.read(reinterpret_cast<char *>(b), 2);
-        hlen = b[0] | (b[1] << 8);
-    } else {
-        unsigned char b[4];
-        f.read(reinterpret_cast<char *>(b), 4);
-        hlen = b[0] | (b[1] << 8) | (b[2] << 16) | ((uint32_t)b[3] << 24);
-    }
-    std::string h(hlen, '\0');
-    f.read(&h[0], hlen);
-    if (h.find("'descr': '<f4'") == std::string::npos)
-        throw std::runtime_error("read " + path + ": expected little-endian f32 data");
-    if (h.find("'fortran_order': False") == std::string::npos)
-        throw std::runtime_error("read " + path + ": Fortran order is not supported");
-    const size_t a = h.find("'shape': ("), b = h.find(')', a);
-    if (a == std::string::npos || b == std::string::npos) throw std::runtime_error("read " + path + ": bad header");
     Npy n;
-    std::string dims = h.substr(a + 10, b - a - 10);
-    size_t count = 1;
-    std::stringstream ds(dims);
-    std::string tok;
-    while (std::getline(ds, tok, ',')) {
-        tok = Toml::trim(tok);
-        if (tok.empty()) continue;
-        n.shape.push_back(std::stoul(tok));
-        count *= n.shape.back();
-    }
-    n.data.resize(count);
-    f.read(reinterpret_cast<char *>(n.data.data()), count * 4);
-    if (!f) throw std::runtime_error("read " + path + ": file shorter than its shape");
+    xdna::read_npy_f32(path, n.shape, n.data);
     return n;
 }
 

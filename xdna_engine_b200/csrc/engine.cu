@@ -620,6 +620,11 @@ int xdna_opt_get_tokens(XdnaOptDecoder *dec, int64_t *host, size_t off, size_t n
     return copy_tokens(dec, host, off, n, stream, false);
 }
 int xdna_opt_grid(const XdnaOptDecoder *dec) { return dec ? dec->grid : 0; }
+int xdna_opt_config(const XdnaOptDecoder *dec, XdnaOptConfig *out) {
+    if (!dec || !out) { set_err("xdna_opt_config: null decoder or output"); return -1; }
+    *out = dec->cfg;
+    return 0;
+}
 int xdna_opt_set_timing(XdnaOptDecoder *dec, unsigned long long *timing_dev) {
     if (!dec) { set_err("xdna_opt_set_timing: decoder is null"); return -1; }
     dec->timing = timing_dev;

@@ -2,6 +2,8 @@
 // reference dispatch), for hosts that drive the decode op by op the way CtxDecode does:
 //
 //  * device buffers        shim_bo_alloc / _write / _read / _free (rust/npu-xrt/shim/xrt_shim.h:16-40)
+//  * fused arenas           FusedArena (rust/npu-xrt/src/lib.rs:641-744): input / output / scratch
+//                           regions addressed by byte offset
 //  * asynchronous runs      shim_run_matmul8_start / shim_run_wait / shim_run_free (xrt_shim.h:45-55):
 //                           a run marks the work enqueued on a stream so far; the wait is bounded
 //  * bf16 GEMV              CtxDecode::register_weight + gemv (rust/npu-asr/src/ctx_decode.rs:260-369)
@@ -40,6 +42,10 @@ struct XdnaBuffer {
     int ordinal = 0;
     void *ptr = nullptr;
     size_t bytes = 0;
+};
+// the three resident regions of a fused dispatch: input, output, scratch (FusedArena)
+struct XdnaArena {
+    XdnaBuffer *part[3] = {nullptr, nullptr, nullptr};
 };
 struct XdnaRun {
     int ordinal = 0;
@@ -274,6 +280,42 @@ int xdna_buffer_read(XdnaBuffer *b, void *dst, size_t bytes, size_t offset) {
     if (offset > b->bytes || bytes > b->bytes - offset) { set_last_error_message("xdna_buffer_read: range beyond the buffer"); return -1; }
     if (!ck(cudaSetDevice(b->ordinal), "xdna_buffer_read")) return -1;
     return ck(cudaMemcpy(dst, static_cast<const char *>(b->ptr) + offset, bytes, cudaMemcpyDeviceToHost), "xdna_buffer_read") ? 0 : -1;
+}
+
+// ----------------------------------------------------------------- arenas (FusedArena)
+XdnaArena *xdna_arena_create(XdnaDevice *dev, size_t input_bytes, size_t output_bytes, size_t scratch_bytes) {
+    if (!dev) { set_last_error_message("xdna_arena_create: null device"); return nullptr; }
+    auto *a = new XdnaArena();
+    const size_t sz[3] = {input_bytes, output_bytes, scratch_bytes};
+    for (int i = 0; i < 3; i++) {
+        // a zero-size region still gets an allocation (lib.rs:663-667 rounds it up to 2 bytes)
+        a->part[i] = xdna_buffer_alloc(dev, std::max<size_t>(sz[i], 2));
+        if (!a->part[i]) {
+            xdna_arena_free(a);
+            return nullptr;
+        }
+    }
+    return a;
+}
+void xdna_arena_free(XdnaArena *a) {
+    if (!a) return;
+    for (auto *b : a->part) xdna_buffer_free(b);
+    delete a;
+}
+XdnaBuffer *xdna_arena_region(XdnaArena *a, int which) {
+    if (!a || which < 0 || which > 2) {
+        set_last_error_message("xdna_arena_region: null arena or region not 0 (input), 1 (output), 2 (scratch)");
+        return nullptr;
+    }
+    return a->part[which];
+}
+int xdna_arena_write(XdnaArena *a, int which, size_t offset, const void *src, size_t bytes) {
+    XdnaBuffer *b = xdna_arena_region(a, which);
+    return b ? xdna_buffer_write(b, src, bytes, offset) : -1;
+}
+int xdna_arena_read(XdnaArena *a, int which, size_t offset, void *dst, size_t bytes) {
+    XdnaBuffer *b = xdna_arena_region(a, which);
+    return b ? xdna_buffer_read(b, dst, bytes, offset) : -1;
 }
 
 // ---------------------------------------------------------------------------------- runs
