@@ -499,6 +499,22 @@ int xdna_weights_read_bf16(const XdnaWeightArena *a, const char *name, uint16_t 
  * xdna_opt_create (max_ctx <= 0: min(max_pos, 2048)).  NULL on error. */
 XdnaOptDecoder *xdna_opt_load(XdnaDevice *dev, const char *path, int max_ctx, int grid);
 
+
+/* ------------------------------------------------------------ Whisper log-mel front end */
+/* What the reference runs through preprocessor.onnx (rust/npu-engine/src/asr/whisper.rs:686-705),
+ * the Whisper feature extractor: 480,000 samples (30 s at 16 kHz) -> input_features [80][3000]:
+ * reflect-padded 400-sample frames every 160 samples, periodic Hann window, power spectrum, 80
+ * Slaney mel filters over 0..8 kHz, log10(max(., 1e-10)), clamped below at the clip maximum - 8,
+ * then (x + 4) / 4. */
+typedef struct XdnaLogMel XdnaLogMel;
+XdnaLogMel *xdna_log_mel_create(XdnaDevice *dev);
+void xdna_log_mel_free(XdnaLogMel *h);
+/* wav_dev [B][480000] f32 -> mel_dev [B][80][3000] f32, asynchronous on `stream` */
+int xdna_log_mel_device(XdnaLogMel *h, const float *wav_dev, int B, float *mel_dev, void *stream);
+/* the reference's host step: pcm i16 / 32768, zero-padded or truncated to 480,000 samples ->
+ * mel [80][3000] f32 (host).  Synchronous. */
+int xdna_log_mel(XdnaLogMel *h, const int16_t *pcm, size_t n, float *mel);
+
 #ifdef __cplusplus
 }
 #endif

@@ -191,6 +191,13 @@ def lib():
         L.xdna_dwconv1d_glu_silu.restype = i
         L.xdna_subsample_conv2d.argtypes = [vp, i, i, i, i, vp, vp, i, i, i, i, i, i, i, vp, vp]
         L.xdna_subsample_conv2d.restype = i
+        L.xdna_log_mel_create.argtypes = [vp]
+        L.xdna_log_mel_create.restype = vp
+        L.xdna_log_mel_free.argtypes = [vp]
+        L.xdna_log_mel_device.argtypes = [vp, vp, i, vp, vp]
+        L.xdna_log_mel_device.restype = i
+        L.xdna_log_mel.argtypes = [vp, vp, sz, vp]
+        L.xdna_log_mel.restype = i
         L.xdna_weights_open.argtypes = [C.c_char_p, C.c_char_p]
         L.xdna_weights_open.restype = vp
         L.xdna_weights_close.argtypes = [vp]
@@ -362,7 +369,7 @@ class OptDecoder:
         _check(lib().xdna_opt_config(h, C.byref(c)))
         self = cls.__new__(cls)
         self.cfg = OptConfig(c.n_layers, c.d_model, c.n_heads, c.head_dim, c.ffn, c.vocab, c.max_pos,
-                             float(np.float32(c.eps)))
+                             float(str(np.float32(c.eps))))   # the shortest decimal of the f32
         self.device = device
         self.max_ctx = max_ctx or min(c.max_pos, 2048)
         self._adopt(h)
