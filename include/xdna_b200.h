@@ -93,6 +93,18 @@ int xdna_gemm_i8(const int8_t *A, const int8_t *B, const float *sa, int rows_per
 /* After the stream has finished: -1 (with xdna_last_error) if a GEMM's bounded wait expired
  * since the last check, else 0. */
 int xdna_gemm_check(void);
+/* The fused two-GEMM FFN with the hidden activations kept on chip (ffn_gemm2,
+ * route_b_kernels/ffn_gemm2/ffn_gemm2_iron.py:1-30, with the encoder FFN's bias and activation
+ * between the GEMMs): out[M, N] = act(A[M, K] . W1[P, K]^T + b1) . W2[N, P]^T (+ b2) (+ residual).
+ * bf16 operands (row-major, K-major weights as nn.Linear stores them), f32 accumulation, the
+ * hidden rounded to bf16 on chip (as the unfused path rounds it in HBM).  act: 0 none, 1
+ * exact-erf GELU (the reference's Abramowitz-Stegun form), 2 ReLU.  b1, b2, residual ([M, N]
+ * bf16) nullable; exactly one of out_bf16 / out_f32.  K % 64 == 0, P % 256 == 0, N % 64 == 0,
+ * N <= 768.  Asynchronous on `stream`; xdna_ffn_fused_check reports a bounded wait that expired. */
+int xdna_ffn_fused_bf16(const uint16_t *A, const uint16_t *W1, const float *b1, int act, const uint16_t *W2,
+                        const float *b2, const uint16_t *residual, uint16_t *out_bf16, float *out_f32, int M, int K,
+                        int P, int N, void *stream);
+int xdna_ffn_fused_check(void);
 
 /* ------------------------------------------------ BGE / BERT embeddings (EmbedPipeline) */
 typedef struct {
