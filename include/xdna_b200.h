@@ -105,6 +105,9 @@ int xdna_ffn_fused_bf16(const uint16_t *A, const uint16_t *W1, const float *b1, 
                         const float *b2, const uint16_t *residual, uint16_t *out_bf16, float *out_f32, int M, int K,
                         int P, int N, void *stream);
 int xdna_ffn_fused_check(void);
+/* diagnostics: globaltimer stamps of the first cluster's two CTAs into trace_dev ([2][1024] u64,
+ * slot 16 c + k for chunk c), or NULL (the default) for none */
+void xdna_ffn_fused_set_trace(unsigned long long *trace_dev);
 
 /* ------------------------------------------------ BGE / BERT embeddings (EmbedPipeline) */
 typedef struct {

@@ -76,6 +76,7 @@ def lib():
         L.xdna_ffn_fused_bf16.argtypes = [vp, vp, vp, i, vp, vp, vp, vp, vp, i, i, i, i, vp]
         L.xdna_ffn_fused_bf16.restype = i
         L.xdna_ffn_fused_check.restype = i
+        L.xdna_ffn_fused_set_trace.argtypes = [vp]
         L.xdna_gemm_i8.argtypes = [vp, vp, vp, i, vp, vp, i, vp, C.c_float, vp, vp, i, i, i, vp]
         L.xdna_gemm_i8.restype = i
         L.xdna_bert_create.argtypes = [vp, vp, vp, i, i]

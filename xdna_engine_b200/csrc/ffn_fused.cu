@@ -16,7 +16,8 @@
 //      output half, chunk columns]^T.
 // H never touches HBM.  TMEM: acc2 in columns [0, 384), H in [384, 512).  The MMA thread issues
 // GEMM1 of chunk c while the epilogue is still turning chunk c-1 into bf16, then GEMM2 of
-// chunk c-1; one 3-stage ring of 48 KB stages carries both GEMMs' operands in issue order.
+// chunk c-1; one 5-stage ring of 32 KB stages (A + W1 k-block, or one output half of a W2
+// k-block) carries both GEMMs' operands in issue order.
 // The chunk buffer is single: before overwriting it for chunk c, a CTA waits until both CTAs'
 // GEMM2 of chunk c-1 has completed (each CTA's epilogue arrives on its own and its peer's
 // "free" barrier after seeing its own GEMM2 commit).  Every wait is bounded (an error code in
@@ -35,6 +36,7 @@
 #include "../../include/xdna_b200.h"
 #include "ptx.cuh"
 #include "tc.cuh"
+#include "gelu.cuh"
 
 namespace xdna {
 void set_last_error_message(const std::string &m);
@@ -44,12 +46,13 @@ bool make_tmap(CUtensorMap *tm, const void *base, int rows, int K, int ld, int b
 
 namespace ffn2 {
 
-constexpr int BM = 128, BK = 64, PC = 256, HALF = PC / 2, STAGES = 3, STAGE_BYTES = 48 * 1024;
+constexpr int BM = 128, BK = 64, PC = 256, HALF = PC / 2, STAGES = 5, STAGE_BYTES = 32 * 1024;
 constexpr int A_BYTES = BM * BK * 2, W1_BYTES = HALF * BK * 2;            // 16 KB each
 constexpr int HBLK = BM * 128, HBUF = 4 * HBLK;                            // 16 KB per K block, 64 KB per chunk
 constexpr int H_COL = 384;                                                  // acc2 in [0, 384)
-constexpr int THREADS = 192;                                               // producer, MMA, 4 epilogue warps
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + HBUF + 256;
+constexpr int EPI = 256;                                                   // 8 epilogue warps
+constexpr int THREADS = 64 + EPI;                                          // + producer, MMA
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + HBUF + HALF * 4 + 256;
 constexpr uint64_t TIMEOUT_NS = 2000000000ull;
 
 __device__ unsigned int g_ffn_error;
@@ -90,12 +93,12 @@ __device__ __forceinline__ void bulk_s2peer(uint32_t dst_cluster, uint32_t src_c
         "r"(src_cta), "r"(bytes), "r"(bar_cluster)
         : "memory");
 }
-// barrier over the 128 epilogue threads (id 1) that also ORs a flag across them, so a decision
+// barrier over the 256 epilogue threads (id 1) that also ORs a flag across them, so a decision
 // taken after a bounded wait is the same in every epilogue thread
 __device__ __forceinline__ bool epi_bar_or(bool v) {
     uint32_t r;
     asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 128, p;\n"
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n"
         " selp.u32 %0, 1, 0, q;\n}\n"
         : "=r"(r)
         : "r"((uint32_t)v)
@@ -106,19 +109,6 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// the reference's GELU: 0.5 x (1 + erf(x / sqrt 2)), Abramowitz-Stegun 7.1.26 erf
-// (rust/npu-asr-host/src/lib.rs:464-495); the same function the unfused GEMM epilogue applies
-__device__ __forceinline__ float gelu_erf_as(float v) {
-    const float x = v * 0.70710678118654752440f;
-    const float ax = fabsf(x);
-    const float t = __frcp_rn(fmaf(0.3275911f, ax, 1.0f));
-    float p = fmaf(1.061405429f, t, -1.453152027f);
-    p = fmaf(p, t, 1.421413741f);
-    p = fmaf(p, t, -0.284496736f);
-    p = fmaf(p, t, 0.254829592f);
-    const float y = fmaf(-p * t, __expf(-ax * ax), 1.0f);
-    return 0.5f * v * (1.0f + copysignf(y, x));
-}
 
 struct Params {
     int M, K, P, N;
@@ -128,6 +118,7 @@ struct Params {
     const uint16_t *residual;   // [M, N] bf16 or null
     uint16_t *out_bf16;         // [M, N] or null
     float *out_f32;             // [M, N] or null
+    unsigned long long *trace;  // null, or [2][1024] globaltimer stamps of cluster 0 (diagnostics)
 };
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
@@ -137,10 +128,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *ring = smem;                                   // [STAGES][48 KB]
     uint8_t *hbuf = smem + STAGES * STAGE_BYTES;            // [4 K blocks][128 rows][128 B], swizzled
-    uint64_t *full = reinterpret_cast<uint64_t *>(hbuf + HBUF);
+    float *sb1 = reinterpret_cast<float *>(hbuf + HBUF);       // [HALF] this chunk's b1 slice
+    uint64_t *full = reinterpret_cast<uint64_t *>(sb1 + HALF);
     uint64_t *empty = full + STAGES;
     uint64_t *hacc_full = empty + STAGES;   // GEMM1 of a chunk done (MMA commit)
-    uint64_t *tm_free = hacc_full + 1;      // TMEM H drained (4 epilogue warps)
+    uint64_t *tm_free = hacc_full + 1;      // TMEM H drained (8 epilogue warps)
     uint64_t *hready = tm_free + 1;         // chunk in shared memory: own half (1 arrival) + peer's copy (tx)
     uint64_t *g2done = hready + 1;          // GEMM2 of a chunk done (MMA commit)
     uint64_t *hfree = g2done + 1;           // both CTAs' GEMM2 of the previous chunk done (2 arrivals)
@@ -151,11 +143,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint32_t r = cluster_rank(), peer = r ^ 1u;
     const int m0 = (blockIdx.x >> 1) * BM;
     const int N2 = p.N / 2, nk = p.K / BK, nc = p.P / PC;
+    unsigned long long *tr = (p.trace && blockIdx.x < 2) ? p.trace + blockIdx.x * 1024 : nullptr;
+    auto stamp = [&](int slot) {
+        if (tr && slot < 1024) tr[slot] = globaltimer_ns();
+    };
 
     if (threadIdx.x == 0) {
+        stamp(1002);
         for (int s = 0; s < STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_init(hacc_full, 1);
-        mbar_init(tm_free, 4);
+        mbar_init(tm_free, EPI / 32);
         mbar_init(hready, 1);
         mbar_init(g2done, 1);
         mbar_init(hfree, 2);
@@ -180,14 +177,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             return true;
         };
         auto gemm2_loads = [&](int c) {
-            for (int j = 0; j < PC / BK && ok; j++) {
-                int s;
-                if (!(ok = acquire(s))) break;
-                uint8_t *st = ring + s * STAGE_BYTES;
-                mbar_arrive_expect_tx(&full[s], (uint32_t)N2 * 128);
-                tc::tma_load_2d(st, &tmW2, c * PC + BK * j, (int)r * N2, &full[s]);
-                tc::tma_load_2d(st + (N2 / 2) * 128, &tmW2, c * PC + BK * j, (int)r * N2 + N2 / 2, &full[s]);
-            }
+            for (int j = 0; j < PC / BK && ok; j++)
+                for (int h = 0; h < 2 && ok; h++) {
+                    int s;
+                    if (!(ok = acquire(s))) break;
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)(N2 / 2) * 128);
+                    tc::tma_load_2d(ring + s * STAGE_BYTES, &tmW2, c * PC + BK * j, (int)r * N2 + h * (N2 / 2), &full[s]);
+                }
         };
         for (int c = 0; c < nc && ok; c++) {
             for (int kb = 0; kb < nk && ok; kb++) {
@@ -198,7 +194,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 tc::tma_load_2d(st, &tmA, kb * BK, m0, &full[s]);
                 tc::tma_load_2d(st + A_BYTES, &tmW1, kb * BK, c * PC + HALF * (int)r, &full[s]);
             }
+            stamp(16 * c + 12);
             if (c >= 1) gemm2_loads(c - 1);
+            stamp(16 * c + 13);
         }
         if (ok) gemm2_loads(nc - 1);
         // the loads in flight land before the CTA moves on
@@ -212,26 +210,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         bool ok = true;
         auto gemm2 = [&](int c) {
             if (!(ok = ok && wait_b(hready, c & 1, 4u))) return;
+            stamp(16 * c + 4);
             tc::fence_after_sync();
-            for (int j = 0; j < PC / BK; j++, c_ring++) {
-                const int s = c_ring % STAGES;
-                if (!(ok = wait_b(&full[s], (c_ring / STAGES) & 1, 5u))) return;
-                tc::fence_after_sync();
-                const uint64_t da = tc::desc_k_sw128(smem_u32(hbuf + j * HBLK));
-                const uint64_t db0 = tc::desc_k_sw128(smem_u32(ring + s * STAGE_BYTES));
-                const uint64_t db1 = tc::desc_k_sw128(smem_u32(ring + s * STAGE_BYTES + (N2 / 2) * 128));
+            for (int j = 0; j < PC / BK; j++)
+                for (int h = 0; h < 2; h++, c_ring++) {
+                    const int s = c_ring % STAGES;
+                    if (!(ok = wait_b(&full[s], (c_ring / STAGES) & 1, 5u))) return;
+                    tc::fence_after_sync();
+                    const uint64_t da = tc::desc_k_sw128(smem_u32(hbuf + j * HBLK));
+                    const uint64_t db = tc::desc_k_sw128(smem_u32(ring + s * STAGE_BYTES));
 #pragma unroll
-                for (int k = 0; k < BK / 16; k++) {
-                    const uint32_t accum = (c > 0 || j > 0 || k > 0) ? 1u : 0u;
-                    tc::mma_bf16(tmem, da + 2 * k, db0 + 2 * k, id2, accum);
-                    tc::mma_bf16(tmem + (uint32_t)(N2 / 2), da + 2 * k, db1 + 2 * k, id2, accum);
+                    for (int k = 0; k < BK / 16; k++)
+                        tc::mma_bf16(tmem + (uint32_t)(h * (N2 / 2)), da + 2 * k, db + 2 * k, id2,
+                                     (c > 0 || j > 0 || k > 0) ? 1u : 0u);
+                    tc::commit(&empty[s]);
                 }
-                tc::commit(&empty[s]);
-            }
             tc::commit(g2done);
         };
         for (int c = 0; c < nc && ok; c++) {
+            stamp(16 * c + 0);
             if (c >= 1 && !(ok = wait_b(tm_free, (c - 1) & 1, 3u))) break;
+            stamp(16 * c + 1);
             tc::fence_after_sync();
             for (int kb = 0; kb < nk; kb++, c_ring++) {
                 const int s = c_ring % STAGES;
@@ -245,41 +244,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 tc::commit(&empty[s]);
             }
             tc::commit(hacc_full);       // always signalled, so the epilogue never waits forever
+            stamp(16 * c + 2);
             if (ok && c >= 1) gemm2(c - 1);
+            stamp(16 * c + 3);
         }
         if (ok) gemm2(nc - 1);
         tc::commit(acc_full);
     } else if (warp >= 2) {
-        // ------------------------------------------------------------ epilogue (4 warps)
-        // TMEM lane quarter (warp & 3) = rows 32 (warp & 3) + lane of the tile
-        const int q = warp & 3, et = threadIdx.x - 64;
+        // ------------------------------------------------------------ epilogue (8 warps)
+        // TMEM lane quarter (warp & 3) = rows 32 (warp & 3) + lane of the tile; warp half
+        // hh = (warp - 2) / 4 takes H columns [64 hh, 64 hh + 64), i.e. K block 2r + hh
+        const int q = warp & 3, hh = (warp - 2) >> 2, et = threadIdx.x - 64;
         const int row_l = 32 * q + lane, row = m0 + row_l;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-        // every exit from this loop is taken by all 128 threads together (epi_bar_or), so no
-        // thread is ever left waiting at a barrier the others skipped
+        // every exit from this loop is taken by all epilogue threads together (epi_bar_or), so
+        // no thread is ever left waiting at a barrier the others skipped
         bool ok = true;
         for (int c = 0; c < nc; c++) {
+            const int col0 = c * PC + HALF * (int)r;
+            if (et < HALF) sb1[et] = p.b1 ? p.b1[col0 + et] : 0.0f;   // read after the barrier below
             if (epi_bar_or(!wait_b(hacc_full, c & 1, 6u))) { ok = false; break; }
+            if (et == 0) stamp(16 * c + 8);
             tc::fence_after_sync();
-            uint32_t hv[HALF];
-#pragma unroll
-            for (int b = 0; b < HALF / 32; b++)
-                tc::tmem_ld32(tmem + lane_base + H_COL + 32 * b, *reinterpret_cast<uint32_t(*)[32]>(&hv[32 * b]));
+            uint32_t hv[64];
+            tc::tmem_ld32(tmem + lane_base + H_COL + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&hv[0]));
+            tc::tmem_ld32(tmem + lane_base + H_COL + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&hv[32]));
             tc::tmem_ld_wait();
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(tm_free);
             // bias + activation + bf16, packed in pairs
-            const int col0 = c * PC + HALF * (int)r;
-            uint32_t pk[HALF / 2];
+            const float *bb = sb1 + 64 * hh;
+            uint32_t pk[32];
 #pragma unroll
-            for (int j = 0; j < HALF / 2; j++) {
-                float a = __uint_as_float(hv[2 * j]), b = __uint_as_float(hv[2 * j + 1]);
-                if (p.b1) { a += p.b1[col0 + 2 * j]; b += p.b1[col0 + 2 * j + 1]; }
+            for (int j = 0; j < 32; j++) {
+                float a = __uint_as_float(hv[2 * j]) + bb[2 * j], b = __uint_as_float(hv[2 * j + 1]) + bb[2 * j + 1];
                 if (p.act == 1) { a = gelu_erf_as(a); b = gelu_erf_as(b); }
                 else if (p.act == 2) { a = fmaxf(a, 0.0f); b = fmaxf(b, 0.0f); }
                 pk[j] = bf16bits(a) | (bf16bits(b) << 16);
             }
+            if (et == 0) stamp(16 * c + 9);
             // the chunk buffer is free once both CTAs' GEMM2 of chunk c-1 completed
             if (c >= 1) {
                 bool good = true;
@@ -293,20 +297,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 good = wait_b(hfree, (c - 1) & 1, 8u) && good;
                 if (epi_bar_or(!good)) { ok = false; break; }
             }
-            // this CTA's half = K blocks 2r, 2r+1; row_l's 16-byte chunk j of a block sits at
-            // chunk (j ^ (row_l & 7)) of its 128-byte row
+            // K block 2r + hh; row_l's 16-byte chunk j of a block sits at chunk (j ^ (row_l & 7))
+            // of its 128-byte row
+            uint8_t *blk = hbuf + (2 * r + hh) * HBLK + row_l * 128;
 #pragma unroll
-            for (int b = 0; b < 2; b++) {
-                uint8_t *blk = hbuf + (2 * r + b) * HBLK + row_l * 128;
-#pragma unroll
-                for (int j = 0; j < 8; j++)
-                    *reinterpret_cast<uint4 *>(blk + ((j ^ (row_l & 7)) << 4)) =
-                        make_uint4(pk[32 * b + 4 * j], pk[32 * b + 4 * j + 1], pk[32 * b + 4 * j + 2],
-                                   pk[32 * b + 4 * j + 3]);
-            }
+            for (int j = 0; j < 8; j++)
+                *reinterpret_cast<uint4 *>(blk + ((j ^ (row_l & 7)) << 4)) =
+                    make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            if (et == 0) stamp(16 * c + 10);
             tc::fence_proxy_async_smem();
-            named_bar(1, 128);
+            named_bar(1, EPI);
             if (et == 0) {
+                stamp(16 * c + 11);
                 mbar_arrive_expect_tx(hready, 2 * HBLK);                  // own half + the peer's 32 KB
                 const uint32_t src = smem_u32(hbuf + 2 * r * HBLK);
                 bulk_s2peer(mapa(src, peer), src, 2 * HBLK, mapa(smem_u32(hready), peer));
@@ -314,8 +316,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
         // ---- final epilogue: acc2 columns [0, N/2) = output columns [r N/2, r N/2 + N/2)
         if (ok && !epi_bar_or(!wait_b(acc_full, 0, 9u))) {
+            if (et == 0) stamp(1000);
             tc::fence_after_sync();
-            for (int c0 = 0; c0 < N2; c0 += 32) {
+            for (int c0 = 32 * hh; c0 < N2; c0 += 64) {
                 uint32_t v[32];
                 tc::tmem_ld32(tmem + lane_base + c0, v);
                 tc::tmem_ld_wait();
@@ -352,12 +355,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
     tc::fence_before_sync();
     __syncthreads();
+    if (threadIdx.x == 0) stamp(1001);
     if (warp == 1) tc::tmem_dealloc(tmem, 512);
     cluster_sync();                 // no copy or arrive from the peer is still aimed at this CTA
 }
 
 }  // namespace ffn2
 }  // namespace xdna
+
+static unsigned long long *g_ffn_trace = nullptr;
+// diagnostics: globaltimer stamps of the first cluster's CTAs into trace_dev ([2][1024] u64), or off
+extern "C" void xdna_ffn_fused_set_trace(unsigned long long *trace_dev) { g_ffn_trace = trace_dev; }
 
 extern "C" int xdna_ffn_fused_bf16(const uint16_t *A, const uint16_t *W1, const float *b1, int act, const uint16_t *W2,
                                    const float *b2, const uint16_t *residual, uint16_t *out_bf16, float *out_f32, int M,
@@ -380,7 +388,7 @@ extern "C" int xdna_ffn_fused_bf16(const uint16_t *A, const uint16_t *W1, const 
     }
     cudaError_t e = cudaFuncSetAttribute(ffn2::ffn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ffn2::SMEM);
     if (e == cudaSuccess) {
-        ffn2::Params prm{M, K, P, N, b1, act, b2, residual, out_bf16, out_f32};
+        ffn2::Params prm{M, K, P, N, b1, act, b2, residual, out_bf16, out_f32, g_ffn_trace};
         const int tiles = (M + ffn2::BM - 1) / ffn2::BM;
         ffn2::ffn_fused_kernel<<<2 * tiles, ffn2::THREADS, ffn2::SMEM, static_cast<cudaStream_t>(stream)>>>(ta, t1, t2,
                                                                                                          prm);

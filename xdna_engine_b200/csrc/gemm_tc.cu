@@ -25,6 +25,7 @@
 #include "../../include/xdna_b200.h"
 #include "ptx.cuh"
 #include "tc.cuh"
+#include "gelu.cuh"
 
 namespace xdna {
 void set_last_error_message(const std::string &m);
@@ -56,19 +57,6 @@ __device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, uns
     return true;
 }
 
-// the reference's GELU: 0.5 x (1 + erf(x / sqrt 2)) with the Abramowitz-Stegun 7.1.26 erf
-// (rust/npu-asr-host/src/lib.rs:464-495)
-__device__ __forceinline__ float gelu_erf_as(float v) {
-    const float x = v * 0.70710678118654752440f;
-    const float ax = fabsf(x);
-    const float t = __frcp_rn(fmaf(0.3275911f, ax, 1.0f));
-    float p = fmaf(1.061405429f, t, -1.453152027f);
-    p = fmaf(p, t, 1.421413741f);
-    p = fmaf(p, t, -0.284496736f);
-    p = fmaf(p, t, 0.254829592f);
-    const float y = fmaf(-p * t, __expf(-ax * ax), 1.0f);
-    return 0.5f * v * (1.0f + copysignf(y, x));
-}
 
 // bf16 operands, f32 accumulators: C = act(acc + bias) (+ residual), bf16 or f32 out
 struct EpiBf16 {
