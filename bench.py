@@ -976,15 +976,118 @@ def run_gemma_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_gemma_case(args):
-    """One xdna_gemma generate of B streams x ctx-token prompts + 4 tokens (ncu captures of the
-    step at a chosen context; nothing timed)."""
+def run_gemma_case(B, ctx):
+    """One xdna_gemma generate of B streams x ctx-token prompts + 4 tokens."""
     import xdna_engine_b200 as X
     from xdna_engine_b200.synth import GEMMA3_1B as cfg, make_gemma_weights
-    B, ctx = (int(v) for v in args.case.split(","))
     dec = X.GemmaDecoder(X.Device(0), cfg, make_gemma_weights(cfg, seed=0), max_batch=B, max_ctx=ctx + 8)
     prompts = np.random.default_rng(0).integers(2, cfg.vocab, (B, ctx)).astype(np.int64)
     print(dec.generate(prompts, 4)[0], flush=True)
+
+
+def run_case(args):
+    """Profiling cases: a small, fixed piece of one workload run a few times on cuda:0 and nothing
+    timed, so that an ncu capture (-k <kernel> -s <skip> -c <count>) of it is reproducible from
+    committed code.  NAME:ARGS --
+      gemm_bf16:M,N,K,act   three xdna_gemm_bf16 launches (act 0 none, 1 GELU)
+      gemm_i8:M,N,K,act     three xdna_gemm_i8 launches (act 0 none, 1 SiLU, 3 GLU)
+      ffn_fused:M           three xdna_ffn_fused_bf16 launches at the BGE FFN shape (768, 3072, 768)
+      bge:S                 two BERT-base forwards of S sequences of lengths U[32,512]
+      whisper:B             two Whisper-small encoder forwards of B clips
+      parakeet:B            two Parakeet encoder forwards of B clips (eager, then the graph)
+      whisper_dec:B         two Whisper-small decoder runs of B streams x 4 tokens
+      decode:N              one opt-125m generation of N tokens after a 32-token prompt
+      gemma:B,ctx           one Gemma-3-1B generate (B streams, ctx-token prompts, + 4 tokens)
+      (a bare "B,ctx" is the gemma case)"""
+    import torch
+    name, _, rest = args.case.partition(":") if ":" in args.case else ("gemma", "", args.case)
+    vals = [int(v) for v in rest.split(",") if v]
+    torch.cuda.set_device(0)
+    import xdna_engine_b200 as X
+    L = X.lib()
+    st = torch.cuda.current_stream()
+    sp = st.cuda_stream
+    if name == "gemma":
+        run_gemma_case(*vals)
+    elif name in ("gemm_bf16", "gemm_i8"):
+        M, N, K, act = vals
+        if name == "gemm_bf16":
+            A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+            B = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+            C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            bias = torch.zeros(N, device="cuda")
+            for _ in range(3):
+                assert L.xdna_gemm_bf16(A.data_ptr(), B.data_ptr(), bias.data_ptr(), None, C.data_ptr(), M, N, K,
+                                        act, sp) == 0, X.last_error()
+        else:
+            A = torch.randint(-127, 128, (M, K), device="cuda", dtype=torch.int8)
+            B = torch.randint(-127, 128, (N, K), device="cuda", dtype=torch.int8)
+            sa = torch.full((1,), 1e-3, device="cuda")
+            ws = torch.full((N,), 1e-3, device="cuda")
+            C = torch.empty(M, N // 2 if act == 3 else N, device="cuda")
+            for _ in range(3):
+                assert L.xdna_gemm_i8(A.data_ptr(), B.data_ptr(), sa.data_ptr(), M, ws.data_ptr(), None, act, None,
+                                      1.0, C.data_ptr(), None, M, N, K, sp) == 0, X.last_error()
+        torch.cuda.synchronize()
+        assert L.xdna_gemm_check() == 0, X.last_error()
+    elif name == "ffn_fused":
+        M, = vals
+        K, P, N = 768, 3072, 768
+        A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        W1 = (torch.randn(P, K, device="cuda") * 0.03).to(torch.bfloat16)
+        W2 = (torch.randn(N, P, device="cuda") * 0.02).to(torch.bfloat16)
+        b1, b2 = torch.zeros(P, device="cuda"), torch.zeros(N, device="cuda")
+        C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        for _ in range(3):
+            assert L.xdna_ffn_fused_bf16(A.data_ptr(), W1.data_ptr(), b1.data_ptr(), 1, W2.data_ptr(), b2.data_ptr(),
+                                         None, C.data_ptr(), None, M, K, P, N, sp) == 0, X.last_error()
+        torch.cuda.synchronize()
+        assert L.xdna_ffn_fused_check() == 0, X.last_error()
+    elif name == "bge":
+        S, = vals
+        from xdna_engine_b200.synth import BGE_BASE, make_bert_weights, make_bge_batch
+        ids, lens = make_bge_batch(S, seed=0)
+        m = X.BertEmbedder(X.Device(0), BGE_BASE, make_bert_weights(BGE_BASE, seed=0), max_tokens=int(lens.sum()),
+                           max_seqs=S)
+        for _ in range(2):
+            m.embed(ids, lens)
+    elif name == "whisper":
+        B, = vals
+        from xdna_engine_b200.synth import WHISPER_SMALL_ENC as cfg, make_whisper_enc_weights, make_mel
+        enc = X.WhisperEncoder(X.Device(0), cfg, make_whisper_enc_weights(cfg, seed=0), max_batch=B)
+        d_mel = torch.from_numpy(make_mel(cfg, batch=B, seed=0)).cuda()
+        out = torch.empty(B, 1500, 768, device="cuda", dtype=torch.bfloat16)
+        for _ in range(2):
+            enc.encode_device(d_mel.data_ptr(), B, out.data_ptr(), sp)
+    elif name == "parakeet":
+        B, = vals
+        from xdna_engine_b200.synth import PARAKEET_V3 as cfg, make_parakeet_weights, make_parakeet_mel
+        enc = X.ParakeetEncoder(X.Device(0), cfg, make_parakeet_weights(cfg, seed=0), max_batch=B)
+        d_mel = torch.from_numpy(make_parakeet_mel(cfg, B, seed=0)).cuda()
+        out = torch.empty(B, enc.frames_out, 1024, device="cuda")
+        for _ in range(2):
+            enc.encode_device(d_mel.data_ptr(), B, out.data_ptr(), sp)
+    elif name == "whisper_dec":
+        B, = vals
+        from xdna_engine_b200.synth import WHISPER_SMALL_DEC as cfg, WHISPER_PROMPT, make_whisper_dec_weights, \
+            make_encoder_states
+        dec = X.WhisperDecoder(X.Device(0), cfg, make_whisper_dec_weights(cfg, seed=0), max_batch=B)
+        d_enc = torch.from_numpy(make_encoder_states(cfg, B, seed=0)).cuda()
+        toks = torch.empty(B, 4, dtype=torch.int64, device="cuda")
+        prompt = np.array(WHISPER_PROMPT, np.int64)
+        assert L.xdna_whisper_dec_set_encoder(dec.handle, d_enc.data_ptr(), B, sp) == 0, X.last_error()
+        for _ in range(2):
+            assert L.xdna_whisper_dec_run(dec.handle, B, prompt.ctypes.data, len(prompt), 4, toks.data_ptr(), None,
+                                          sp) == 0, X.last_error()
+    elif name == "decode":
+        N, = vals
+        from xdna_engine_b200.synth import OPT_125M, make_opt_weights, make_prompt
+        dec = X.OptDecoder(X.Device(0), OPT_125M, make_opt_weights(OPT_125M, seed=0), max_ctx=32 + N + 1)
+        print(dec.generate(make_prompt(OPT_125M, 32, seed=0), N)[:8], flush=True)
+    else:
+        raise SystemExit(f"unknown case {name!r}")
+    torch.cuda.synchronize()
+    print(f"case {args.case}: ok", flush=True)
 
 
 def run_gemma(args):
@@ -1095,11 +1198,10 @@ def main():
                     "(default: as many as fit in about one second, so the clock sampler sees them)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode", "bge", "whisper", "parakeet", "whisper_dec", "gemma"], default="decode")
-    ap.add_argument("--case", default="", help="gemma only: 'B,ctx' runs one small generate (B streams, ctx-token "
-                    "prompts, ctx - 1 prefill steps + 4 tokens) and prints its tokens: the profiling case")
+    ap.add_argument("--case", default="", help="a profiling case NAME:ARGS (see run_case); nothing is timed")
     args = ap.parse_args()
     if args.case:
-        run_gemma_case(args)
+        run_case(args)
         return
     if args.warmup < 3:
         args.warmup = 3
