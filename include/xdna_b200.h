@@ -105,6 +105,17 @@ int xdna_ffn_fused_bf16(const uint16_t *A, const uint16_t *W1, const float *b1, 
                         const float *b2, const uint16_t *residual, uint16_t *out_bf16, float *out_f32, int M, int K,
                         int P, int N, void *stream);
 int xdna_ffn_fused_check(void);
+/* Encoder self-attention, 12 heads of 64, on the tcgen05 tensor cores: the reference's `mha`
+ * with valid_len (rust/npu-asr-host/src/lib.rs:189-326) over packed sequences.  qkv
+ * [T_total, 2304] bf16 (q | k | v per row, head h at columns 64 h of each), cu [n_seqs + 1]
+ * int32 device offsets of the sequences, max_len >= the longest; ctx [T_total, 768] bf16 =
+ * softmax(q k^T / 8) v over each sequence's own keys.  Asynchronous on `stream`;
+ * xdna_attention_check reports a bounded wait that expired. */
+int xdna_attention_bf16(const uint16_t *qkv, int T_total, const int32_t *cu, int n_seqs, int max_len, uint16_t *ctx,
+                        void *stream);
+int xdna_attention_check(void);
+/* diagnostics: globaltimer stamps of the first CTA into trace_dev ([512] u64), NULL for none */
+void xdna_attention_set_trace(unsigned long long *trace_dev);
 /* diagnostics: globaltimer stamps of the first cluster's two CTAs into trace_dev ([2][1024] u64,
  * slot 16 c + k for chunk c), or NULL (the default) for none */
 void xdna_ffn_fused_set_trace(unsigned long long *trace_dev);
@@ -529,6 +540,13 @@ int xdna_log_mel_device(XdnaLogMel *h, const float *wav_dev, int B, float *mel_d
 /* the reference's host step: pcm i16 / 32768, zero-padded or truncated to 480,000 samples ->
  * mel [80][3000] f32 (host).  Synchronous. */
 int xdna_log_mel(XdnaLogMel *h, const int16_t *pcm, size_t n, float *mel);
+
+/* Detokenizer of the ASR front end: ids -> text with a byte-level BPE tokenizer.json (Whisper's),
+ * as the HuggingFace tokenizers library decodes (whisper.rs:671-679): added tokens, then the BPE
+ * vocabulary; special tokens dropped when skip_special; bytes through the inverse GPT-2
+ * byte-to-unicode table; invalid UTF-8 replaced by U+FFFD.  Writes up to cap - 1 bytes + NUL to
+ * out (nullable); returns the full length, or -1 with xdna_last_error() set. */
+int xdna_bpe_decode(const char *tokenizer_path, const int64_t *ids, size_t n, int skip_special, char *out, size_t cap);
 
 #ifdef __cplusplus
 }

@@ -83,8 +83,8 @@ def test_scenario_errors(lib, tmp_path):
     asr = tmp_path / "asr.toml"
     asr.write_text('[scenario]\nkind = "asr"\nname = "whisper-small"\n[model]\nhidden = 768\nff = 3072\n'
                    'n_heads = 12\nhead_dim = 64\nn_layers = 12\nmax_seq = 1500\n')
-    assert lib.npu_model_load(str(asr).encode()) is None
-    assert lib.npu_last_error().startswith(b"unsupported: ")
+    assert lib.npu_model_load(str(asr).encode()) is None      # no artifacts.weights directory
+    assert lib.npu_last_error().startswith(b"load failed: ")
     odd = tmp_path / "odd.toml"
     odd.write_text(asr.read_text().replace('"asr"', '"speech"'))
     assert lib.npu_model_load(str(odd).encode()) is None

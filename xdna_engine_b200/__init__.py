@@ -77,6 +77,10 @@ def lib():
         L.xdna_ffn_fused_bf16.restype = i
         L.xdna_ffn_fused_check.restype = i
         L.xdna_ffn_fused_set_trace.argtypes = [vp]
+        L.xdna_attention_bf16.argtypes = [vp, i, vp, i, i, vp, vp]
+        L.xdna_attention_bf16.restype = i
+        L.xdna_attention_check.restype = i
+        L.xdna_attention_set_trace.argtypes = [vp]
         L.xdna_gemm_i8.argtypes = [vp, vp, vp, i, vp, vp, i, vp, C.c_float, vp, vp, i, i, i, vp]
         L.xdna_gemm_i8.restype = i
         L.xdna_bert_create.argtypes = [vp, vp, vp, i, i]
@@ -202,6 +206,8 @@ def lib():
         L.xdna_log_mel_device.restype = i
         L.xdna_log_mel.argtypes = [vp, vp, sz, vp]
         L.xdna_log_mel.restype = i
+        L.xdna_bpe_decode.argtypes = [C.c_char_p, vp, sz, i, vp, sz]
+        L.xdna_bpe_decode.restype = i
         L.xdna_weights_open.argtypes = [C.c_char_p, C.c_char_p]
         L.xdna_weights_open.restype = vp
         L.xdna_weights_close.argtypes = [vp]

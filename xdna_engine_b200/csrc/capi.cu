@@ -24,6 +24,7 @@
 //   tokenizer decode) is wired behind npu_transcribe.
 #include <cuda_runtime.h>
 
+#include <sys/stat.h>
 #include <unistd.h>
 
 #include <algorithm>
@@ -392,13 +393,22 @@ struct WordPiece {
 }  // namespace
 
 // --------------------------------------------------------------------------- model handle
+namespace xdna {
+struct AsrState;   // asr.cu: the Whisper pipeline behind npu_transcribe
+AsrState *asr_load(XdnaDevice *dev, const std::string &wdir, const std::string &tokenizer, int n_layers);
+void asr_free(AsrState *a);
+std::string asr_transcribe(AsrState *a, const int16_t *pcm, size_t n);
+}  // namespace xdna
+
 struct NpuModel {
     ScenarioCfg cfg;
     XdnaDevice *dev = nullptr;
     XdnaBert *bert = nullptr;
+    xdna::AsrState *asr = nullptr;
     WordPiece tok;
     ~NpuModel() {
         if (bert) xdna_bert_free(bert);
+        if (asr) xdna::asr_free(asr);
         if (dev) xdna_device_close(dev);
     }
 };
@@ -465,6 +475,36 @@ NpuModel *load_embed(const ScenarioCfg &c, const std::string &path) {
     return m.release();
 }
 
+// ASR scenarios: Whisper-small (hidden 768, 12 heads of 64, ff 3072) from the npy layout of
+// artifacts.weights; the tokenizer is artifacts.tokenizer, else tokenizer.json beside the weights
+NpuModel *load_asr(const ScenarioCfg &c, const std::string &path) {
+    if (c.name.find("whisper") == std::string::npos)
+        throw std::runtime_error(err_unsupported("ASR model \"" + c.name + "\": only Whisper scenarios are wired "
+                                                 "behind npu_transcribe"));
+    if (c.hidden != 768 || c.ff != 3072 || c.n_heads != 12 || c.head_dim != 64)
+        throw std::runtime_error(err_unsupported("ASR models with hidden 768, ff 3072, 12 heads of 64 (Whisper-small)"));
+    if (!c.source.empty())
+        throw std::runtime_error(err_unsupported("artifacts.source (weight arenas); give the npy directory in artifacts.weights"));
+    std::unique_ptr<NpuModel> m(new NpuModel());
+    m->cfg = c;
+    char cwd[4096];
+    const std::string root = getcwd(cwd, sizeof cwd) ? std::string(cwd) : std::string(".");
+    const std::string wdir = root + "/" + c.weights;
+    const std::string tok = c.tokenizer.empty() ? wdir + "/tokenizer.json" : root + "/" + c.tokenizer;
+    struct stat st;
+    if (c.weights.empty() || stat(wdir.c_str(), &st) != 0 || !S_ISDIR(st.st_mode))
+        throw std::runtime_error(err_load("asr weights load " + wdir + ": No such file or directory"));
+    m->dev = xdna_device_open(0);
+    if (!m->dev) throw std::runtime_error(err_device(xdna_last_error()));
+    try {
+        m->asr = xdna::asr_load(m->dev, wdir, tok, c.n_layers);
+    } catch (const std::exception &e) {
+        throw std::runtime_error(err_load("asr weights load " + wdir + ": " + e.what()));
+    }
+    (void)path;
+    return m.release();
+}
+
 }  // namespace
 
 extern "C" {
@@ -491,11 +531,7 @@ NpuModel *npu_model_load(const char *scenario_path) {
             return nullptr;
         }
         if (c.kind == "embeddings") return load_embed(c, path);
-        if (c.kind == "asr") {
-            npu_set_err(err_unsupported("ASR scenarios: no ASR front end (log-mel, tokenizer decode) is wired "
-                                        "behind npu_transcribe in this backend"));
-            return nullptr;
-        }
+        if (c.kind == "asr") return load_asr(c, path);
         npu_set_err(err_load("unknown scenario kind \"" + c.kind + "\""));
         return nullptr;
     } catch (const std::exception &e) {
@@ -519,8 +555,27 @@ char *npu_transcribe(NpuModel *m, const int16_t *pcm, uintptr_t n, uint32_t samp
         npu_set_err(err_unsupported("sample_rate " + std::to_string(sample_rate) + " (need 16000)"));
         return nullptr;
     }
-    npu_set_err("wrong model kind: wanted asr, got embed");
-    return nullptr;
+    if (!m->asr) {
+        npu_set_err("wrong model kind: wanted asr, got embed");
+        return nullptr;
+    }
+    try {
+        const std::string text = xdna::asr_transcribe(m->asr, pcm, (size_t)n);
+        if (text.find('\0') != std::string::npos) {
+            npu_set_err("transcript contained a NUL byte");
+            return nullptr;
+        }
+        char *r = static_cast<char *>(std::malloc(text.size() + 1));
+        if (!r) { npu_set_err("out of host memory"); return nullptr; }
+        std::memcpy(r, text.c_str(), text.size() + 1);
+        return r;
+    } catch (const std::exception &e) {
+        npu_set_err(err_device(e.what()));
+        return nullptr;
+    } catch (...) {
+        npu_set_err("panic in npu_transcribe");
+        return nullptr;
+    }
 }
 
 int npu_embed(NpuModel *m, const char *text, float *out, uintptr_t out_cap) {

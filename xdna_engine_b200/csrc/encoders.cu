@@ -7,7 +7,7 @@
 //   BertBlock::forward   q/k/v/o, ffn1 (+GELU), ffn2 on the NPU GEMM engine, host MHA with
 //                        the key mask j >= valid_len, post-LN (bert/encoder.rs:43-57)
 //                        -> xdna_gemm_bf16 (tcgen05, fused bias/GELU/residual),
-//                           attention_kernel, ln_kernel
+//                           attention_tc (tcgen05), ln_kernel
 //   EmbedHead::run       CLS or mean pooling over valid rows, L2 with norm clamp 1e-12
 //                        (bert/head.rs:20-47)                     -> pool_kernel
 // Packing sequences (instead of padding each to 512 and masking keys) gives the same result
@@ -31,6 +31,9 @@ cudaError_t gemm_bf16(const uint16_t *A, int lda, const uint16_t *B, int ldb, in
                       const float *bias, const uint16_t *residual, int ldr, int act, uint16_t *C, int ldc,
                       cudaStream_t st, int res_mod = 0, float *C_f32 = nullptr);
 unsigned gemm_error_and_clear();
+cudaError_t attention_tc(const uint16_t *qkv, int T_total, const int32_t *cu, int n_seqs, int max_len, uint16_t *ctx,
+                         cudaStream_t st);
+unsigned attention_tc_error_and_clear();
 
 namespace bert {
 
@@ -113,182 +116,8 @@ __global__ void ln_kernel(const uint16_t *xin, int T, const float *g, const floa
 }
 
 // ---------------------------------------------------------------------------- attention
-// softmax(q k^T / 8) v per (sequence, head, 128-query tile) over the sequence's own keys
-// (the valid_len key mask of npu-asr-host mha, lib.rs:189-326).  Tensor cores via
-// mma.sync m16n8k16 bf16 (f32 accumulate), flash-style online softmax over 64-key tiles.
-// Shared tiles [64 rows][64 bf16] with 16-byte chunks XOR-swizzled by (row & 7).
-__device__ __forceinline__ uint32_t swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                               uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) { return bf16bits(lo) | (bf16bits(hi) << 16); }
-
-// load a 64 x 64 bf16 tile (row stride ld elements) with cp.async into a swizzled tile;
-// rows >= nrows are zero-filled
-template <int ROWS, int NT>
-__device__ __forceinline__ void load_tile(uint8_t *tile, const uint16_t *src, int ld, int nrows, int tid) {
-    for (int c = tid; c < ROWS * 8; c += NT) {
-        const int r = c >> 3, ch = c & 7;
-        uint8_t *dst = tile + swz(r, ch);
-        if (r < nrows) cp_async16(dst, src + (size_t)r * ld + ch * 8);
-        else *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
-    }
-}
-
-constexpr int AQ = 128;             // queries per CTA (8 warps x 16 rows)
-constexpr int ATHREADS = 256;
-__global__ void __launch_bounds__(ATHREADS) attention_kernel(const uint16_t *qkv, const int32_t *cu, uint16_t *ctx) {
-    __shared__ __align__(128) uint8_t sQ[AQ * 128];
-    __shared__ __align__(128) uint8_t sK[2][64 * 128];
-    __shared__ __align__(128) uint8_t sV[2][64 * 128];
-    const int qt = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
-    const int s0 = cu[sq], L = cu[sq + 1] - s0;
-    const int q0 = qt * AQ;
-    if (q0 >= L) return;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr int LD = 3 * D;
-    const uint16_t *Qg = qkv + (size_t)(s0 + q0) * LD + h * HD;
-    const uint16_t *Kg = qkv + (size_t)s0 * LD + D + h * HD;
-    const uint16_t *Vg = qkv + (size_t)s0 * LD + 2 * D + h * HD;
-    const int nq = min(AQ, L - q0);
-    const int nkt = (L + 63) / 64;
-    load_tile<AQ, ATHREADS>(sQ, Qg, LD, nq, tid);
-    load_tile<64, ATHREADS>(sK[0], Kg, LD, min(64, L), tid);
-    load_tile<64, ATHREADS>(sV[0], Vg, LD, min(64, L), tid);
-    cp_async_commit();
-
-    const uint32_t q_base = smem_u32(sQ);
-    float o[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
-    const float scale_log2 = 0.125f * 1.4426950408889634f;
-    uint32_t qa[4][4];
-
-    for (int kt = 0; kt < nkt; kt++) {
-        const int buf = kt & 1;
-        if (kt + 1 < nkt) {
-            const int r0 = (kt + 1) * 64;
-            load_tile<64, ATHREADS>(sK[buf ^ 1], Kg + (size_t)r0 * LD, LD, min(64, L - r0), tid);
-            load_tile<64, ATHREADS>(sV[buf ^ 1], Vg + (size_t)r0 * LD, LD, min(64, L - r0), tid);
-        }
-        cp_async_commit();
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-        __syncthreads();
-        if (kt == 0) {
-            // Q fragments for this warp's 16 rows, 4 k-chunks of 16 dims
-#pragma unroll
-            for (int kc = 0; kc < 4; kc++) {
-                const int r = warp * 16 + (lane & 15), ch = kc * 2 + (lane >> 4);
-                ldsm_x4(q_base + swz(r, ch), qa[kc][0], qa[kc][1], qa[kc][2], qa[kc][3]);
-            }
-        }
-        const uint32_t k_base = smem_u32(sK[buf]), v_base = smem_u32(sV[buf]);
-        float sc[8][4];
-#pragma unroll
-        for (int n = 0; n < 8; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
-#pragma unroll
-        for (int kc = 0; kc < 4; kc++) {
-#pragma unroll
-            for (int np = 0; np < 4; np++) {   // two 8-key n-tiles per ldmatrix.x4
-                const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
-                const int ch = kc * 2 + ((lane >> 3) & 1);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4(k_base + swz(key, ch), b0, b1, b2, b3);
-                mma_bf16_16816(sc[2 * np], qa[kc][0], qa[kc][1], qa[kc][2], qa[kc][3], b0, b1);
-                mma_bf16_16816(sc[2 * np + 1], qa[kc][0], qa[kc][1], qa[kc][2], qa[kc][3], b2, b3);
-            }
-        }
-        // mask keys beyond the sequence, online softmax (rows g and g + 8 of the warp)
-        const int kbase = kt * 64;
-        float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-        for (int n = 0; n < 8; n++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int key = kbase + n * 8 + 2 * (lane & 3) + (e & 1);
-                if (key >= L) sc[n][e] = -INFINITY;
-                mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
-            }
-        float corr[2], mnew[2];
-#pragma unroll
-        for (int r = 0; r < 2; r++) {
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-            mnew[r] = fmaxf(m_r[r], mx[r]);
-            corr[r] = exp2f((m_r[r] - mnew[r]) * scale_log2);
-            m_r[r] = mnew[r];
-        }
-        float ls[2] = {0.0f, 0.0f};
-        uint32_t pa[4][4];   // P as A fragments: 4 k-chunks (16 keys each)
-#pragma unroll
-        for (int n = 0; n < 8; n++) {
-            float p[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                p[e] = exp2f((sc[n][e] - mnew[e >> 1]) * scale_log2);
-                ls[e >> 1] += p[e];
-            }
-            const int kc = n >> 1, hi = n & 1;
-            pa[kc][hi * 2 + 0] = pack_bf16x2(p[0], p[1]);
-            pa[kc][hi * 2 + 1] = pack_bf16x2(p[2], p[3]);
-        }
-#pragma unroll
-        for (int r = 0; r < 2; r++) {
-            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
-            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
-            l_r[r] = l_r[r] * corr[r] + ls[r];
-        }
-#pragma unroll
-        for (int n = 0; n < 8; n++) {
-            o[n][0] *= corr[0]; o[n][1] *= corr[0];
-            o[n][2] *= corr[1]; o[n][3] *= corr[1];
-        }
-        // O += P V: k = keys (4 chunks of 16), n = dims (8 tiles of 8); V^T fragments by ldmatrix.trans
-#pragma unroll
-        for (int kc = 0; kc < 4; kc++) {
-            // A fragment order for m16n8k16: a0 (rows g, k 0-7), a1 (rows g+8, k 0-7),
-            // a2 (rows g, k 8-15), a3 (rows g+8, k 8-15)
-            const uint32_t a0 = pa[kc][0], a1 = pa[kc][1], a2 = pa[kc][2], a3 = pa[kc][3];
-#pragma unroll
-            for (int np = 0; np < 4; np++) {
-                const int key = kc * 16 + (lane & 15);
-                const int ch = np * 2 + (lane >> 4);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(v_base + swz(key, ch), b0, b1, b2, b3);
-                mma_bf16_16816(o[2 * np], a0, a1, a2, a3, b0, b1);
-                mma_bf16_16816(o[2 * np + 1], a0, a1, a2, a3, b2, b3);
-            }
-        }
-        __syncthreads();
-    }
-    // write ctx rows (bf16)
-    const int g = lane >> 2, c2 = 2 * (lane & 3);
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-        const int qi = warp * 16 + g + 8 * r;
-        if (qi < nq) {
-            const float inv = 1.0f / l_r[r];
-            uint16_t *dst = ctx + (size_t)(s0 + q0 + qi) * D + h * HD;
-#pragma unroll
-            for (int n = 0; n < 8; n++)
-                *reinterpret_cast<uint32_t *>(dst + n * 8 + c2) = pack_bf16x2(o[n][2 * r] * inv, o[n][2 * r + 1] * inv);
-        }
-    }
-}
+// softmax(q k^T / 8) v per (sequence, head) over the sequence's own keys (the valid_len key
+// mask of npu-asr-host mha, lib.rs:189-326): the tcgen05 kernel of attention_tc.cu.
 
 // out[b] = l2norm(pool(x rows of sequence b)); pooling bit 0: 0 = CLS (row 0), 1 = mean;
 // bit 1 set: no L2 normalisation (EmbedHead with normalize = false, bert/head.rs:20-47)
@@ -496,7 +325,7 @@ int xdna_bert_encode_device(XdnaBert *m, const int32_t *ids, const int32_t *tok_
                                                  m->emb_ln + D, eps, m->x);
     for (const auto &L : m->layers) {
         if ((e = gemm_bf16(m->x, D, L.wqkv, D, T, 3 * D, D, L.bqkv, nullptr, 0, 0, m->qkv, 3 * D, st))) break;
-        attention_kernel<<<dim3((max_len + AQ - 1) / AQ, H, n_seqs), ATHREADS, 0, st>>>(m->qkv, cu, m->ctx);
+        if ((e = attention_tc(m->qkv, T, cu, n_seqs, max_len, m->ctx, st))) break;
         if ((e = gemm_bf16(m->ctx, D, L.wo, D, T, D, D, L.bo, m->x, D, 0, m->y, D, st))) break;
         ln_kernel<<<(T + 7) / 8, 256, 0, st>>>(m->y, T, L.ln1, L.ln1 + D, eps, m->x);
         if ((e = gemm_bf16(m->x, D, L.w1, D, T, F, D, L.b1, nullptr, 0, 1, m->hbuf, F, st))) break;
@@ -536,8 +365,8 @@ int xdna_bert_embed(XdnaBert *m, const int32_t *ids, const int32_t *seq_lens, in
         ck(cudaMemcpy(m->cu, cu.data(), (n_seqs + 1) * 4, cudaMemcpyHostToDevice), "copy offsets");
         if (xdna_bert_encode_device(m, m->ids, m->tokpos, m->cu, T, n_seqs, max_len, m->out, nullptr) != 0) return -1;
         ck(cudaMemcpy(out, m->out, (size_t)n_seqs * bert::D * 4, cudaMemcpyDeviceToHost), "copy embeddings");
-        if (gemm_error_and_clear()) {
-            set_last_error_message("xdna_bert_embed: a tensor-core GEMM wait expired");
+        if (gemm_error_and_clear() | attention_tc_error_and_clear()) {
+            set_last_error_message("xdna_bert_embed: a tensor-core wait expired");
             return -1;
         }
         return 0;
@@ -766,7 +595,7 @@ int xdna_whisper_encode_device(XdnaWhisperEnc *m, const float *mel_dev, int B, u
         const auto &L = m->layers[li];
         bert::ln_kernel<<<(R2 + 7) / 8, 256, 0, st>>>(m->x, R2, L.ln1, L.ln1 + D, eps, m->y);
         if ((e = gemm_bf16(m->y, D, L.wqkv, D, R2, 3 * D, D, L.bqkv, nullptr, 0, 0, m->qkv, 3 * D, st))) break;
-        bert::attention_kernel<<<dim3((To + bert::AQ - 1) / bert::AQ, 12, B), bert::ATHREADS, 0, st>>>(m->qkv, m->cu, m->ctx);
+        if ((e = attention_tc(m->qkv, R2, m->cu, B, To, m->ctx, st))) break;
         if ((e = gemm_bf16(m->ctx, D, L.wo, D, R2, D, D, L.bo, m->x, D, 0, m->y, D, st))) break;
         std::swap(m->x, m->y);   // x <- x + attn
         bert::ln_kernel<<<(R2 + 7) / 8, 256, 0, st>>>(m->x, R2, L.ln2, L.ln2 + D, eps, m->y);
@@ -798,7 +627,10 @@ int xdna_whisper_encode(XdnaWhisperEnc *m, const float *mel, int B, float *out) 
             const uint32_t u = (uint32_t)hbuf[i] << 16;
             std::memcpy(out + i, &u, 4);
         }
-        if (gemm_error_and_clear()) { set_last_error_message("xdna_whisper_encode: a GEMM wait expired"); return -1; }
+        if (gemm_error_and_clear() | attention_tc_error_and_clear()) {
+            set_last_error_message("xdna_whisper_encode: a tensor-core wait expired");
+            return -1;
+        }
         return 0;
     } catch (const std::exception &ex) {
         set_last_error_message(std::string("xdna_whisper_encode: ") + ex.what());

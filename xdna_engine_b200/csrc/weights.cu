@@ -31,130 +31,17 @@
 #include <vector>
 
 #include "../../include/xdna_b200.h"
+#include "json.h"
 
 namespace xdna {
 void set_last_error_message(const std::string &m);
 }
 using xdna::set_last_error_message;
 
+using xdna::json::Json;
+using xdna::json::JsonParser;
+
 namespace {
-
-// --------------------------------------------------------------------------- JSON subset
-// Objects, arrays, strings (with \u escapes), numbers, true / false / null: what a safetensors
-// header holds.
-struct Json {
-    enum Kind { Null, Bool, Num, Str, Arr, Obj } kind = Null;
-    double num = 0;
-    bool b = false;
-    std::string str;
-    std::vector<Json> arr;
-    std::map<std::string, Json> obj;
-};
-
-struct JsonParser {
-    const char *p, *end;
-    [[noreturn]] void fail(const char *what) { throw std::runtime_error(std::string("safetensors header: ") + what); }
-    void ws() {
-        while (p < end && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) p++;
-    }
-    void put_utf8(std::string &o, uint32_t cp) {
-        if (cp < 0x80) o += (char)cp;
-        else if (cp < 0x800) { o += (char)(0xc0 | (cp >> 6)); o += (char)(0x80 | (cp & 0x3f)); }
-        else if (cp < 0x10000) {
-            o += (char)(0xe0 | (cp >> 12)); o += (char)(0x80 | ((cp >> 6) & 0x3f)); o += (char)(0x80 | (cp & 0x3f));
-        } else {
-            o += (char)(0xf0 | (cp >> 18)); o += (char)(0x80 | ((cp >> 12) & 0x3f));
-            o += (char)(0x80 | ((cp >> 6) & 0x3f)); o += (char)(0x80 | (cp & 0x3f));
-        }
-    }
-    uint32_t hex4() {
-        if (end - p < 4) fail("short \\u escape");
-        uint32_t v = 0;
-        for (int i = 0; i < 4; i++, p++) {
-            const char c = *p;
-            v = v * 16 + (c >= '0' && c <= '9' ? c - '0' : c >= 'a' && c <= 'f' ? c - 'a' + 10
-                          : c >= 'A' && c <= 'F' ? c - 'A' + 10 : (fail("bad \\u escape"), 0));
-        }
-        return v;
-    }
-    std::string string() {
-        if (p >= end || *p != '"') fail("expected a string");
-        p++;
-        std::string o;
-        while (p < end && *p != '"') {
-            if (*p != '\\') { o += *p++; continue; }
-            if (++p >= end) fail("bad escape");
-            const char c = *p++;
-            switch (c) {
-            case 'n': o += '\n'; break;
-            case 't': o += '\t'; break;
-            case 'r': o += '\r'; break;
-            case 'b': o += '\b'; break;
-            case 'f': o += '\f'; break;
-            case 'u': {
-                uint32_t cp = hex4();
-                if (cp >= 0xd800 && cp < 0xdc00 && end - p >= 6 && p[0] == '\\' && p[1] == 'u') {
-                    p += 2;
-                    cp = 0x10000 + ((cp - 0xd800) << 10) + (hex4() - 0xdc00);
-                }
-                put_utf8(o, cp);
-                break;
-            }
-            default: o += c;
-            }
-        }
-        if (p >= end) fail("unterminated string");
-        p++;
-        return o;
-    }
-    Json value(int depth = 0) {
-        if (depth > 16) fail("nested too deeply");
-        ws();
-        if (p >= end) fail("unexpected end");
-        Json j;
-        if (*p == '{') {
-            j.kind = Json::Obj;
-            p++;
-            ws();
-            if (p < end && *p == '}') { p++; return j; }
-            while (true) {
-                ws();
-                std::string k = string();
-                ws();
-                if (p >= end || *p != ':') fail("expected ':'");
-                p++;
-                j.obj[k] = value(depth + 1);
-                ws();
-                if (p < end && *p == ',') { p++; continue; }
-                if (p < end && *p == '}') { p++; return j; }
-                fail("expected ',' or '}'");
-            }
-        }
-        if (*p == '[') {
-            j.kind = Json::Arr;
-            p++;
-            ws();
-            if (p < end && *p == ']') { p++; return j; }
-            while (true) {
-                j.arr.push_back(value(depth + 1));
-                ws();
-                if (p < end && *p == ',') { p++; continue; }
-                if (p < end && *p == ']') { p++; return j; }
-                fail("expected ',' or ']'");
-            }
-        }
-        if (*p == '"') { j.kind = Json::Str; j.str = string(); return j; }
-        if (end - p >= 4 && !std::strncmp(p, "true", 4)) { p += 4; j.kind = Json::Bool; j.b = true; return j; }
-        if (end - p >= 5 && !std::strncmp(p, "false", 5)) { p += 5; j.kind = Json::Bool; return j; }
-        if (end - p >= 4 && !std::strncmp(p, "null", 4)) { p += 4; return j; }
-        const char *s = p;
-        while (p < end && (std::strchr("+-.eE", *p) || (*p >= '0' && *p <= '9'))) p++;
-        if (p == s) fail("unexpected character");
-        j.kind = Json::Num;
-        j.num = std::stod(std::string(s, p));
-        return j;
-    }
-};
 
 uint64_t as_u64(const Json &j, const char *what) {
     if (j.kind != Json::Num || j.num < 0 || j.num != (double)(uint64_t)j.num)
@@ -264,7 +151,8 @@ XdnaWeightArena *open_arena(const std::string &path, const char *expect_arch) {
     uint64_t hlen = 0;
     for (int i = 7; i >= 0; i--) hlen = (hlen << 8) | base[i];
     if (hlen > a->map_bytes - 8) throw std::runtime_error(path + ": header length beyond the file");
-    JsonParser jp{reinterpret_cast<const char *>(base + 8), reinterpret_cast<const char *>(base + 8 + hlen)};
+    JsonParser jp{reinterpret_cast<const char *>(base + 8), reinterpret_cast<const char *>(base + 8 + hlen),
+                  "safetensors header"};
     const Json h = jp.value();
     if (h.kind != Json::Obj) throw std::runtime_error(path + ": safetensors header is not an object");
     a->data = base + 8 + hlen;
