@@ -9,9 +9,10 @@
 //   S   = Q . K_j^T      (M 128, N 128, K 64; both operands K-major in 128-byte swizzle)
 //   O_j = P_j . V_j      (M 128, N 64, K 128; P K-major from shared memory, V MN-major: the
 //                         [key][dim] tile exactly as TMA wrote it, no transpose)
-// and S_{j+1} is issued before waiting for P_j, so it overlaps the softmax of tile j.  Warps 2-5
-// (one thread per query row; TMEM lane quarter = warp % 4) read S 32 columns at a time (twice),
-// mask keys at or past the sequence length, keep the running maximum and sum in f32, write
+// and S_{j+1} is issued before waiting for P_j, so it overlaps the softmax of tile j.  Warps 2-9
+// (two threads per query row, each half of the keys and half of the output dims; TMEM lane
+// quarter = warp % 4) read S 32 columns at a time (twice), swap partial row maxima through a
+// TMEM column, mask keys at or past the sequence length, keep the running maximum and sum in f32, write
 // P_j = exp2((s - m) * log2(e) / 8) as bf16 into the swizzled P buffer, and fold each O_j into
 // an f32 register accumulator with the running correction, so O never needs a
 // read-modify-write in TMEM.  The output row is acc / sum in bf16.  Numerics match the
@@ -34,14 +35,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
 namespace attn_tc {
 
 constexpr int D = 768, HD = 64, LD = 3 * D;
-constexpr int BQ = 128, BKV = 128, THREADS = 192;
+constexpr int BQ = 128, BKV = 128, SOFTMAX = 256, THREADS = 64 + SOFTMAX;
 constexpr int TILE = 128 * 128;                         // one 128-row x 128-byte swizzled tile
 // 7 tiles + 128 B of barriers + up to 896 B to reach a 1024-byte boundary: 115,712 B, so two CTAs
 // (plus the 1 KB each reserves) fit in an SM's 228 KB.  A base less than 128-byte aligned would
 // need more padding; the kernel checks and refuses to run rather than overrun.
 constexpr int PAD = 896;
 constexpr int SMEM = PAD + 7 * TILE + 128;
-constexpr uint32_t S_COL = 0, O_COL = 128;
+constexpr uint32_t S_COL = 0, O_COL = 128, X_COL = 192;   // X: the row partners' exchange columns
 constexpr uint64_t TIMEOUT_NS = 2000000000ull;
 
 __device__ unsigned int g_attn_error;
@@ -59,11 +60,38 @@ __device__ __forceinline__ bool wait_b(uint64_t *bar, uint32_t parity, unsigned 
     return true;
 }
 
-// barrier over the 128 softmax threads (id 1) that ORs a flag across them
+// one 32-bit TMEM column of the warp's 32 lanes: store / load (thread t <-> lane base + t)
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(__float_as_uint(v)) : "memory");
+}
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+    return __uint_as_float(r);
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 2^x by the hardware approximation (results below 2^-126 flush to zero: far below a bf16
+// softmax weight's resolution, and exactly 0 for the masked -inf)
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// two finite floats -> bf16x2 (round to nearest even) with integer ops: the same bits as
+// cvt.rn.bf16x2.f32, kept off the conversion pipe that the exponentials already load
+__device__ __forceinline__ uint32_t pack_bf16_rne(float a, float b) {
+    const uint32_t x = __float_as_uint(a), y = __float_as_uint(b);
+    const uint32_t xr = x + 0x7fffu + ((x >> 16) & 1u), yr = y + 0x7fffu + ((y >> 16) & 1u);
+    return __byte_perm(xr, yr, 0x7632);
+}
+
+// barrier over the 256 softmax threads (id 1) that ORs a flag across them
 __device__ __forceinline__ bool sm_bar_or(bool v) {
     uint32_t r;
     asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 128, p;\n"
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n"
         " selp.u32 %0, 1, 0, q;\n}\n"
         : "=r"(r)
         : "r"((uint32_t)v)
@@ -117,8 +145,8 @@ __global__ void __launch_bounds__(THREADS, 2)
         mbar_init(q_full, 1);
         for (int s = 0; s < 2; s++) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
         mbar_init(s_full, 1);
-        mbar_init(s_free, 4);
-        mbar_init(p_full, 4);
+        mbar_init(s_free, SOFTMAX / 32);
+        mbar_init(p_full, SOFTMAX / 32);
         mbar_init(o_full, 1);
         mbar_fence_init();
     }
@@ -179,46 +207,47 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
         // every path ends with the softmax threads released (their waits are bounded anyway)
     } else if (warp >= 2) {
-        // ------------------------------------------------------------ softmax (one thread per row)
-        // Tile j: pass 1 (row maximum of S_j), then the fold of O_{j-1} (its MMA ran during pass 1),
-        // then pass 2 (P_j) -- so the O MMA's latency hides behind the next tile's maximum.
-        const int q = warp & 3, row = 32 * q + lane;
+        // ------------------------------------------------------------ softmax (two threads per row)
+        // Warps 2-9: TMEM lane quarter q = warp % 4 holds rows 32 q + lane; warp half hf = (warp-2)/4
+        // takes keys [64 hf, 64 hf + 64) of every tile (K block hf of P) and output dims
+        // [32 hf, 32 hf + 32).  The two threads of a row share lane (32 q + lane), so they swap
+        // their partial maxima (and, at the end, sums) through TMEM columns X_COL + hf.
+        // Tile j: pass 1 (row maximum of S_j), the fold of O_{j-1} (its MMA ran meanwhile), pass 2
+        // (P_j) -- so the O MMA's latency hides behind the next tile's maximum.
+        const int q = warp & 3, hf = (warp - 2) >> 2, row = 32 * q + lane;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         const float c = 0.125f * 1.4426950408889634f;     // 1/sqrt(64) * log2(e)
         float m = -INFINITY, l = 0.0f, corr_pending = 0.0f;
-        float o[HD];
+        float o[32];
 #pragma unroll
-        for (int d = 0; d < HD; d++) o[d] = 0.0f;
+        for (int d = 0; d < 32; d++) o[d] = 0.0f;
         bool ok = true;
-        // o = o * corr + O_t, t = the tile whose P.V the MMA thread last committed
+        // o = o * corr + O_t (this thread's 32 dims), t = the tile whose P.V was last committed
         auto fold = [&](int t, float corr) -> bool {
             if (sm_bar_or(!wait_b(o_full, t & 1, 8u))) return false;
-            if (row == 0) stamp(16 * t + 5);
+            if (row == 0 && hf == 0) stamp(16 * t + 5);
             tc::fence_after_sync();
+            uint32_t ov[32];
+            tc::tmem_ld32(tmem + lane_base + O_COL + 32 * hf, ov);
+            tc::tmem_ld_wait();
 #pragma unroll
-            for (int hf = 0; hf < 2; hf++) {
-                uint32_t ov[32];
-                tc::tmem_ld32(tmem + lane_base + O_COL + 32 * hf, ov);
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int d = 0; d < 32; d++) o[32 * hf + d] = fmaf(o[32 * hf + d], corr, __uint_as_float(ov[d]));
-            }
+            for (int d = 0; d < 32; d++) o[d] = fmaf(o[d], corr, __uint_as_float(ov[d]));
             tc::fence_before_sync();
-            if (row == 0) stamp(16 * t + 6);
+            if (row == 0 && hf == 0) stamp(16 * t + 6);
             return true;
         };
         for (int j = 0; j < nkv; j++) {
             if (sm_bar_or(!wait_b(s_full, j & 1, 7u))) { ok = false; break; }
-            if (row == 0) stamp(16 * j + 2);
+            if (row == 0 && hf == 0) stamp(16 * j + 2);
             tc::fence_after_sync();
-            const int kbase = j * BKV;
-            const bool full = kbase + BKV <= L;                // uniform: no key of the tile is masked
-            // pass 1: the row maximum over the tile's valid keys, 32 columns at a time
+            const int kbase = j * BKV + 64 * hf;
+            const bool full = j * BKV + BKV <= L;             // uniform: no key of the tile is masked
+            // pass 1: the maximum over this thread's 64 keys, then over the row's 128
             float mx = -INFINITY;
 #pragma unroll 1
-            for (int qc = 0; qc < 4; qc++) {
+            for (int qc = 0; qc < 2; qc++) {
                 uint32_t v[32];
-                tc::tmem_ld32(tmem + lane_base + S_COL + 32 * qc, v);
+                tc::tmem_ld32(tmem + lane_base + S_COL + 64 * hf + 32 * qc, v);
                 tc::tmem_ld_wait();
                 if (full) {
                     float m2 = __uint_as_float(v[1]);
@@ -235,23 +264,31 @@ __global__ void __launch_bounds__(THREADS, 2)
                         if (kbase + 32 * qc + i < L) mx = fmaxf(mx, __uint_as_float(v[i]));
                 }
             }
-            if (row == 0) stamp(16 * j + 3);
+            tmem_st1(tmem + lane_base + X_COL + hf, mx);
+            tmem_st_wait();
+            tc::fence_before_sync();
+            named_bar(1, SOFTMAX);
+            tc::fence_after_sync();
+            mx = fmaxf(mx, tmem_ld1(tmem + lane_base + X_COL + (hf ^ 1)));
+            tc::tmem_ld_wait();
+            if (row == 0 && hf == 0) stamp(16 * j + 3);
             const float m_new = fmaxf(m, mx);
             const float corr = exp2f((m - m_new) * c);
             const float mc = m_new * c;
             m = m_new;
-            // P_{j-1} has been read by its MMA once O_{j-1} is complete: fold it, then overwrite P
+            // P_{j-1} has been read by its MMA once O_{j-1} is complete: fold it, then overwrite P.
+            // (A thread rewrites its X_COL only after the next tile's s_full barrier, which its
+            // partner reaches after reading it.)
             if (j >= 1 && !fold(j - 1, corr_pending)) { ok = false; break; }
             corr_pending = corr;
-            // pass 2: P = 2^(s c - m c) as bf16 into the swizzled P buffer: keys [32 qc, 32 qc + 32)
-            // are 16-byte chunks 4 (qc & 1) .. + 3 of K block qc / 2
+            // pass 2: P = 2^(s c - m c) as bf16 into K block hf of the swizzled P buffer
             float ls = 0.0f;
 #pragma unroll 1
-            for (int qc = 0; qc < 4; qc++) {
+            for (int qc = 0; qc < 2; qc++) {
                 uint32_t v[32];
-                tc::tmem_ld32(tmem + lane_base + S_COL + 32 * qc, v);
+                tc::tmem_ld32(tmem + lane_base + S_COL + 64 * hf + 32 * qc, v);
                 tc::tmem_ld_wait();
-                if (qc == 3) {
+                if (qc == 1) {
                     tc::fence_before_sync();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(s_free);           // S may be overwritten by S_{j+1}
@@ -266,14 +303,14 @@ __global__ void __launch_bounds__(THREADS, 2)
                         x0 = k0 < L ? x0 : -INFINITY;
                         x1 = k0 + 1 < L ? x1 : -INFINITY;
                     }
-                    const float p0 = exp2f(x0), p1 = exp2f(x1);
+                    const float p0 = ex2(x0), p1 = ex2(x1);
                     ls += p0 + p1;
-                    pk[i] = bf16bits(p0) | (bf16bits(p1) << 16);
+                    pk[i] = pack_bf16_rne(p0, p1);
                 }
-                uint8_t *prow = sP + (qc >> 1) * TILE + row * 128;
+                uint8_t *prow = sP + hf * TILE + row * 128;
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    const int ch = 4 * (qc & 1) + u;
+                    const int ch = 4 * qc + u;
                     *reinterpret_cast<uint4 *>(prow + ((ch ^ (row & 7)) << 4)) =
                         make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
                 }
@@ -282,14 +319,24 @@ __global__ void __launch_bounds__(THREADS, 2)
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
-            if (row == 0) stamp(16 * j + 4);
+            if (row == 0 && hf == 0) stamp(16 * j + 4);
         }
         if (ok && !fold(nkv - 1, corr_pending)) ok = false;
+        if (ok) {
+            // the row's sum = the two threads' partial sums (same running maximum)
+            tmem_st1(tmem + lane_base + X_COL + hf, l);
+            tmem_st_wait();
+            tc::fence_before_sync();
+            named_bar(1, SOFTMAX);
+            tc::fence_after_sync();
+            l += tmem_ld1(tmem + lane_base + X_COL + (hf ^ 1));
+            tc::tmem_ld_wait();
+        }
         if (ok && q0 + row < L) {
             const float inv = 1.0f / l;
-            uint4 *dst = reinterpret_cast<uint4 *>(ctx + (size_t)(s0 + q0 + row) * D + h * HD);
+            uint4 *dst = reinterpret_cast<uint4 *>(ctx + (size_t)(s0 + q0 + row) * D + h * HD + 32 * hf);
 #pragma unroll
-            for (int u = 0; u < 8; u++)
+            for (int u = 0; u < 4; u++)
                 dst[u] = make_uint4(bf16bits(o[8 * u] * inv) | (bf16bits(o[8 * u + 1] * inv) << 16),
                                     bf16bits(o[8 * u + 2] * inv) | (bf16bits(o[8 * u + 3] * inv) << 16),
                                     bf16bits(o[8 * u + 4] * inv) | (bf16bits(o[8 * u + 5] * inv) << 16),
