@@ -1192,6 +1192,76 @@ def run_gemma(args):
         torch.distributed.destroy_process_group()
 
 
+def _time_ms(fn, st, reps=10, warm=3):
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record(st)
+    for _ in range(reps):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def run_kernel_bench(args):
+    """Op-level timings behind the design notes (one GPU, CUDA events, inputs larger than L2):
+      ffn_fused  -- the BGE FFN at M = 69,632 rows (K 768, P 3072, N 768, GELU): the fused
+                    kernel against the unfused pair and each of its GEMMs
+      attention  -- tcgen05 encoder attention for 32 Whisper clips (1500 positions) and a
+                    256-sequence BGE batch (lengths U[32, 512])"""
+    import torch
+    torch.cuda.set_device(0)
+    import xdna_engine_b200 as X
+    L = X.lib()
+    st = torch.cuda.current_stream()
+    sp = st.cuda_stream
+    reps = max(args.steps, 3) if args.steps > 0 else 10
+    out = {}
+    if args.workload == "ffn_fused":
+        M, K, P, N = 69632, 768, 3072, 768
+        A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        W1 = (torch.randn(P, K, device="cuda") * 0.03).to(torch.bfloat16)
+        W2 = (torch.randn(N, P, device="cuda") * 0.02).to(torch.bfloat16)
+        b1, b2 = torch.zeros(P, device="cuda"), torch.zeros(N, device="cuda")
+        R = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+        H = torch.empty(M, P, device="cuda", dtype=torch.bfloat16)
+        C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        up = lambda: L.xdna_gemm_bf16(A.data_ptr(), W1.data_ptr(), b1.data_ptr(), None, H.data_ptr(), M, P, K, 1, sp)
+        down = lambda: L.xdna_gemm_bf16(H.data_ptr(), W2.data_ptr(), b2.data_ptr(), R.data_ptr(), C.data_ptr(), M, N,
+                                        P, 0, sp)
+        fused = lambda: L.xdna_ffn_fused_bf16(A.data_ptr(), W1.data_ptr(), b1.data_ptr(), 1, W2.data_ptr(),
+                                              b2.data_ptr(), R.data_ptr(), C.data_ptr(), None, M, K, P, N, sp)
+        fl = 2.0 * M * K * P
+        t = {"fused": _time_ms(fused, st, reps), "up": _time_ms(up, st, reps), "down": _time_ms(down, st, reps),
+             "unfused": _time_ms(lambda: (up(), down()), st, reps)}
+        assert L.xdna_ffn_fused_check() == 0 and L.xdna_gemm_check() == 0, X.last_error()
+        out = {"metric": "BGE FFN (M 69,632, K 768, P 3072, N 768, GELU) time", "value": t["fused"], "unit": "ms",
+               "higher_is_better": False, "unfused_ms": t["unfused"], "up_ms": t["up"], "down_ms": t["down"],
+               "fused_tflops": 2 * fl / t["fused"] / 1e9, "unfused_tflops": 2 * fl / t["unfused"] / 1e9,
+               "up_tflops": fl / t["up"] / 1e9, "down_tflops": fl / t["down"] / 1e9}
+    else:
+        res = {}
+        for name, lens in (("whisper32", [1500] * 32),
+                           ("bge256", [int(v) for v in np.random.default_rng(0).integers(32, 513, 256)])):
+            T = int(sum(lens))
+            qkv = torch.randn(T, 2304, device="cuda").to(torch.bfloat16)
+            cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device="cuda")
+            ctx = torch.empty(T, 768, device="cuda", dtype=torch.bfloat16)
+            ms = _time_ms(lambda: L.xdna_attention_bf16(qkv.data_ptr(), T, cu.data_ptr(), len(lens), max(lens),
+                                                        ctx.data_ptr(), sp), st, reps)
+            res[name] = (ms, sum(4.0 * l * l * 64 * 12 for l in lens) / ms / 1e9)
+        assert L.xdna_attention_check() == 0, X.last_error()
+        out = {"metric": "encoder attention time per layer (32 Whisper clips x 1500)", "value": res["whisper32"][0],
+               "unit": "ms", "higher_is_better": False, "whisper32_tflops": res["whisper32"][1],
+               "bge256_ms": res["bge256"][0], "bge256_tflops": res["bge256"][1]}
+    out.update({"n_gpus": 1, "steps": reps, "warmup": 3, "dtype": "bf16", "data": "synthetic (random)",
+                "config": {"workload": args.workload}})
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1200,7 +1270,8 @@ def main():
     ap.add_argument("--reps", type=int, default=0, help="decode: repetitions of the K-step timed region "
                     "(default: as many as fit in about one second, so the clock sampler sees them)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "bge", "whisper", "parakeet", "whisper_dec", "gemma"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "bge", "whisper", "parakeet", "whisper_dec", "gemma", "ffn_fused",
+                                           "attention"], default="decode")
     ap.add_argument("--case", default="", help="a profiling case NAME:ARGS (see run_case); nothing is timed")
     args = ap.parse_args()
     if args.case:
@@ -1208,7 +1279,13 @@ def main():
         return
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload == "gemma":
+    if args.workload in ("ffn_fused", "attention"):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "op-level timing of this backend's kernels; "
+                              "the reference has no counterpart to time"}))
+            return
+        run_kernel_bench(args)
+    elif args.workload == "gemma":
         run_gemma_reference(args) if args.impl == "reference" else run_gemma(args)
     elif args.workload == "whisper_dec":
         if args.steps <= 0:

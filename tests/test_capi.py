@@ -200,3 +200,71 @@ def test_npu_embed_end_to_end(lib, tmp_path, monkeypatch, pooling):
         assert lib.npu_last_error() == b"wrong model kind: wanted asr, got embed"
     finally:
         lib.npu_model_free(m)
+
+
+def _bf16(a):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return u.astype(np.uint32).view(np.float32).reshape(np.shape(a))
+
+
+@pytest.mark.gpu
+def test_npu_embed_from_baked_arena(lib, tmp_path, monkeypatch):
+    """artifacts.source + arch + arena (BertWeights::load_for, bert/weights.rs:41-53): the same
+    model baked into an npu-weights arena (linear weights and embeddings bf16, biases and norms
+    f32, arch/bert.rs:121-125 names) embeds exactly as the npy directory holding the same
+    (bf16-rounded) values."""
+    from xdna_engine_b200 import arena
+    from xdna_engine_b200.synth import BGE_BASE, make_bert_weights
+    cfg = dataclasses.replace(BGE_BASE, n_layers=2, vocab=len(VOCAB), pooling=1)
+    w = make_bert_weights(cfg, seed=9, bias_std=0.02, ln_std=0.05)
+    names = {"o_w": "attn_out_w", "o_b": "attn_out_b"}
+    t = {f"emb/{k}": (w[k], k in ("word_emb", "pos_emb", "type_emb"))
+         for k in ("word_emb", "pos_emb", "type_emb", "emb_ln_w", "emb_ln_b")}
+    for i, ly in enumerate(w["layers"]):
+        for k, v in ly.items():
+            n = names.get(k, k)
+            t[f"L{i}/{n}"] = (v, n.endswith("_w") and "ln" not in n)
+    arena.bake(str(tmp_path / "bge.safetensors"), t, arch="bert", source_ref="synthetic")
+    wq = {k: (_bf16(v) if bf else v) for k, (v, bf) in
+          ((k, (w[k], k in ("word_emb", "pos_emb", "type_emb"))) for k in ("word_emb", "pos_emb", "type_emb",
+                                                                              "emb_ln_w", "emb_ln_b"))}
+    wq["layers"] = [{k: (_bf16(v) if names.get(k, k).endswith("_w") and "ln" not in names.get(k, k) else v)
+                     for k, v in ly.items()} for ly in w["layers"]]
+    scen = _write_scenario(tmp_path, cfg, wq, "mean")
+    arena_scen = tmp_path / "bge_arena.toml"
+    arena_scen.write_text(scen.read_text().replace('[artifacts]\n',
+                          '[artifacts]\nsource = "path:/models/bge"\narch = "bert"\narena = "bge.safetensors"\n'))
+    monkeypatch.chdir(tmp_path)
+    a = lib.npu_model_load(str(arena_scen).encode())
+    assert a, lib.npu_last_error()
+    b = lib.npu_model_load(str(scen).encode())
+    assert b, lib.npu_last_error()
+    try:
+        for text in ("Hello, world!", "unaffable GPU B200 embeddings"):
+            va, vb = np.zeros(768, np.float32), np.zeros(768, np.float32)
+            assert lib.npu_embed(a, text.encode(), va.ctypes.data, 768) == 768, lib.npu_last_error()
+            assert lib.npu_embed(b, text.encode(), vb.ctypes.data, 768) == 768
+            np.testing.assert_array_equal(va, vb)
+    finally:
+        lib.npu_model_free(a)
+        lib.npu_model_free(b)
+
+
+def test_arena_scenario_errors(lib, tmp_path, monkeypatch):
+    """No arena path -> unsupported (baking is not part of the backend); wrong arch -> the
+    arena's own error; source without arch -> the reference's message."""
+    from xdna_engine_b200 import arena
+    monkeypatch.chdir(tmp_path)
+    (tmp_path / "vocab.txt").write_text("\n".join(VOCAB) + "\n")
+    arena.bake(str(tmp_path / "x.safetensors"), {"emb/word_emb": (np.zeros((4, 768), np.float32), True)}, arch="opt")
+    base = ('[scenario]\nkind = "embeddings"\nname = "bge"\n[model]\nhidden = 768\nff = 3072\nn_heads = 12\n'
+            'head_dim = 64\nn_layers = 2\nmax_seq = 512\n[artifacts]\ntokenizer = "vocab.txt"\n')
+    cases = [('source = "hf:BAAI/bge-base-en-v1.5"\narch = "bert"\n', b"unsupported: baking a weight arena"),
+             ('source = "hf:BAAI/bge-base-en-v1.5"\n', b"artifacts.arch is empty"),
+             ('source = "path:/m"\narch = "bert"\narena = "x.safetensors"\n', b'arena arch "opt" != expected "bert"')]
+    for extra, msg in cases:
+        p = tmp_path / "s.toml"
+        p.write_text(base + extra)
+        assert lib.npu_model_load(str(p).encode()) is None
+        assert msg in lib.npu_last_error(), lib.npu_last_error()

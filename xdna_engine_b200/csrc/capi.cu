@@ -178,7 +178,7 @@ struct ScenarioCfg {
     std::string kind, name;
     int hidden = 0, ff = 0, n_heads = 0, head_dim = 0, n_layers = 0, max_seq = 0;
     std::string precision = "bf16";
-    std::string weights, tokenizer, source;
+    std::string weights, tokenizer, source, arch, arena;
     std::string pooling = "mean";
     bool normalize = false;
 };
@@ -206,6 +206,8 @@ ScenarioCfg parse_scenario(const std::string &path) {
     c.weights = t.str("artifacts.weights");
     c.tokenizer = t.str("artifacts.tokenizer");
     c.source = t.str("artifacts.source");
+    c.arch = t.str("artifacts.arch");
+    c.arena = t.str("artifacts.arena");
     c.pooling = t.str("embeddings.pooling", "mean");
     c.normalize = t.boolean("embeddings.normalize", false);
     return c;
@@ -221,6 +223,33 @@ Npy read_npy(const std::string &path) {
     xdna::read_npy_f32(path, n.shape, n.data);
     return n;
 }
+
+// tensors by name from the legacy npy directory (name + ".npy") or from a baked weight arena
+// (the same names, npu-weights/src/arch/bert.rs:121-125 + L{i}/...; bf16 upcast to f32)
+struct TensorStore {
+    std::string dir;
+    XdnaWeightArena *arena = nullptr;
+    ~TensorStore() {
+        if (arena) xdna_weights_close(arena);
+    }
+    Npy get(const std::string &name) const {
+        if (!arena) return read_npy(dir + "/" + name + ".npy");
+        int dt = 0;
+        int64_t shape[8];
+        const int nd = xdna_weights_info(arena, name.c_str(), &dt, shape, 8);
+        if (nd < 0) throw std::runtime_error(std::string("arena: ") + xdna_last_error());
+        Npy n;
+        size_t count = 1;
+        for (int d = 0; d < nd; d++) {
+            n.shape.push_back((size_t)shape[d]);
+            count *= (size_t)shape[d];
+        }
+        n.data.resize(count);
+        if (xdna_weights_read_f32(arena, name.c_str(), n.data.data(), count) != 0)
+            throw std::runtime_error(std::string("arena: ") + xdna_last_error());
+        return n;
+    }
+};
 
 // ------------------------------------------------------------------- WordPiece tokenizer
 struct WordPiece {
@@ -421,24 +450,40 @@ namespace {
 NpuModel *load_embed(const ScenarioCfg &c, const std::string &path) {
     if (c.hidden != 768 || c.ff != 3072 || c.n_heads != 12 || c.head_dim != 64)
         throw std::runtime_error(err_unsupported("embedding models with hidden 768, ff 3072, 12 heads of 64 (BERT-base)"));
-    if (!c.source.empty())
-        throw std::runtime_error(err_unsupported("artifacts.source (weight arenas); give the npy directory in artifacts.weights"));
     if (c.n_layers < 1 || c.max_seq < 1) throw std::runtime_error(err_load("scenario " + path + ": bad model sizes"));
     std::unique_ptr<NpuModel> m(new NpuModel());
     m->cfg = c;
     char cwd[4096];
     const std::string root = getcwd(cwd, sizeof cwd) ? std::string(cwd) : std::string(".");
     m->tok.load(root + "/" + c.tokenizer);
-    const std::string wdir = root + "/" + c.weights;
+    // weights: a baked arena when artifacts.source is set (BertWeights::load_for,
+    // bert/weights.rs:41-53), else the legacy npy directory artifacts.weights
+    TensorStore store;
+    std::string wdir = root + "/" + c.weights;
+    if (!c.source.empty()) {
+        if (c.arch.empty())
+            throw std::runtime_error(err_load("artifacts.source is set but artifacts.arch is empty (need "
+                                              "bert|esm|vit|opt|whisper|fastconformer|gigaam)"));
+        if (c.source.rfind("hf:", 0) != 0 && c.source.rfind("path:", 0) != 0)
+            throw std::runtime_error(err_load("artifacts.source \"" + c.source + "\": expected hf:<repo>[@rev] or path:/abs"));
+        if (c.arena.empty())
+            throw std::runtime_error(err_unsupported("baking a weight arena from artifacts.source (npu-weights bake); "
+                                                     "set artifacts.arena to a baked arena"));
+        wdir = c.arena[0] == '/' ? c.arena : root + "/" + c.arena;
+        store.arena = xdna_weights_open(wdir.c_str(), c.arch.c_str());
+        if (!store.arena) throw std::runtime_error(err_load(xdna_last_error()));
+    } else {
+        store.dir = wdir;
+    }
     std::map<std::string, Npy> emb;
     for (const char *k : {"word_emb", "pos_emb", "type_emb", "emb_ln_w", "emb_ln_b"})
-        emb[k] = read_npy(wdir + "/emb/" + k + ".npy");
+        emb[k] = store.get(std::string("emb/") + k);
     static const char *names[] = {"q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "attn_out_w", "attn_out_b",
                                   "attn_ln_w", "attn_ln_b", "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b", "out_ln_w",
                                   "out_ln_b"};
     std::vector<std::map<std::string, Npy>> layers(c.n_layers);
     for (int l = 0; l < c.n_layers; l++)
-        for (const char *k : names) layers[l][k] = read_npy(wdir + "/L" + std::to_string(l) + "/" + k + ".npy");
+        for (const char *k : names) layers[l][k] = store.get("L" + std::to_string(l) + "/" + k);
     const Npy &we = emb["word_emb"], &pe = emb["pos_emb"];
     if (we.shape.size() != 2 || we.shape[1] != 768 || pe.shape.size() != 2 || pe.shape[1] != 768)
         throw std::runtime_error(err_load("bert weights load " + wdir + ": embedding tables must be [n, 768]"));
