@@ -102,17 +102,54 @@ __global__ void embed_ln_kernel(const int32_t *ids, const int32_t *tok_pos, int 
 }
 
 // y = LN(x) row-wise, bf16 in / bf16 out; one warp per row
-__global__ void ln_kernel(const uint16_t *xin, int T, const float *g, const float *b, float eps, uint16_t *y) {
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+// y = LN(x) row-wise, bf16 in / bf16 out.  Each warp walks rows w, w + W, w + 2W, ... (W = warps
+// in the grid, a few per SM) and loads its next row while it normalises the current one, so
+// every SM keeps ~2 rows per warp in flight; gamma and beta are staged in shared memory once
+// per block.  The arithmetic is ln_row's, in the same order.
+constexpr int LN_BLOCKS_PER_SM = 3;
+__global__ void __launch_bounds__(256, LN_BLOCKS_PER_SM) ln_kernel(const uint16_t *__restrict__ xin, int T,
+                                                                   const float *__restrict__ g,
+                                                                   const float *__restrict__ b, float eps,
+                                                                   uint16_t *__restrict__ y) {
+    __shared__ float sg[D], sb[D];
+    for (int i = threadIdx.x; i < D; i += blockDim.x) { sg[i] = g[i]; sb[i] = b[i]; }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, nw = gridDim.x * 8;
+    int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (row >= T) return;
-    float v[24];
+    uint4 cur[3];
 #pragma unroll
-    for (int j = 0; j < 3; j++)
-        unpack8(*reinterpret_cast<const uint4 *>(xin + (size_t)row * D + 8 * lane + 256 * j), v + 8 * j);
-    ln_row(v, g, b, eps, lane);
+    for (int j = 0; j < 3; j++) cur[j] = *reinterpret_cast<const uint4 *>(xin + (size_t)row * D + 8 * lane + 256 * j);
+    while (row < T) {
+        const int nrow = row + nw;
+        uint4 nxt[3];
+        if (nrow < T)
 #pragma unroll
-    for (int j = 0; j < 3; j++)
-        *reinterpret_cast<uint4 *>(y + (size_t)row * D + 8 * lane + 256 * j) = pack8(v + 8 * j);
+            for (int j = 0; j < 3; j++) nxt[j] = *reinterpret_cast<const uint4 *>(xin + (size_t)nrow * D + 8 * lane + 256 * j);
+        float v[24];
+#pragma unroll
+        for (int j = 0; j < 3; j++) unpack8(cur[j], v + 8 * j);
+        ln_row(v, sg, sb, eps, lane);
+#pragma unroll
+        for (int j = 0; j < 3; j++)
+            *reinterpret_cast<uint4 *>(y + (size_t)row * D + 8 * lane + 256 * j) = pack8(v + 8 * j);
+        if (nrow < T)
+#pragma unroll
+            for (int j = 0; j < 3; j++) cur[j] = nxt[j];
+        row = nrow;
+    }
+}
+
+// the row LayerNorm over T rows: a grid of LN_BLOCKS_PER_SM blocks per SM (or fewer for short inputs)
+void launch_ln(const uint16_t *x, int T, const float *g, const float *b, float eps, uint16_t *y, cudaStream_t st) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const int blocks = std::min((T + 7) / 8, sms * LN_BLOCKS_PER_SM);
+    ln_kernel<<<blocks, 256, 0, st>>>(x, T, g, b, eps, y);
 }
 
 // ---------------------------------------------------------------------------- attention
@@ -327,10 +364,10 @@ int xdna_bert_encode_device(XdnaBert *m, const int32_t *ids, const int32_t *tok_
         if ((e = gemm_bf16(m->x, D, L.wqkv, D, T, 3 * D, D, L.bqkv, nullptr, 0, 0, m->qkv, 3 * D, st))) break;
         if ((e = attention_tc(m->qkv, T, cu, n_seqs, max_len, m->ctx, st))) break;
         if ((e = gemm_bf16(m->ctx, D, L.wo, D, T, D, D, L.bo, m->x, D, 0, m->y, D, st))) break;
-        ln_kernel<<<(T + 7) / 8, 256, 0, st>>>(m->y, T, L.ln1, L.ln1 + D, eps, m->x);
+        launch_ln(m->y, T, L.ln1, L.ln1 + D, eps, m->x, st);
         if ((e = gemm_bf16(m->x, D, L.w1, D, T, F, D, L.b1, nullptr, 0, 1, m->hbuf, F, st))) break;
         if ((e = gemm_bf16(m->hbuf, F, L.w2, F, T, D, F, L.b2, m->x, D, 0, m->y, D, st))) break;
-        ln_kernel<<<(T + 7) / 8, 256, 0, st>>>(m->y, T, L.ln2, L.ln2 + D, eps, m->x);
+        launch_ln(m->y, T, L.ln2, L.ln2 + D, eps, m->x, st);
     }
     pool_kernel<<<n_seqs, 32, 0, st>>>(m->x, cu, m->cfg.pooling, out_dev);
     e = cudaGetLastError();
@@ -593,17 +630,17 @@ int xdna_whisper_encode_device(XdnaWhisperEnc *m, const float *mel_dev, int B, u
     if (!e) e = gemm_bf16(m->cols, 3 * D, m->c2w, 3 * D, R2, D, 3 * D, m->c2b, m->pos, D, 1, m->x, D, st, To);
     for (size_t li = 0; li < m->layers.size() && !e; li++) {
         const auto &L = m->layers[li];
-        bert::ln_kernel<<<(R2 + 7) / 8, 256, 0, st>>>(m->x, R2, L.ln1, L.ln1 + D, eps, m->y);
+        bert::launch_ln(m->x, R2, L.ln1, L.ln1 + D, eps, m->y, st);
         if ((e = gemm_bf16(m->y, D, L.wqkv, D, R2, 3 * D, D, L.bqkv, nullptr, 0, 0, m->qkv, 3 * D, st))) break;
         if ((e = attention_tc(m->qkv, R2, m->cu, B, To, m->ctx, st))) break;
         if ((e = gemm_bf16(m->ctx, D, L.wo, D, R2, D, D, L.bo, m->x, D, 0, m->y, D, st))) break;
         std::swap(m->x, m->y);   // x <- x + attn
-        bert::ln_kernel<<<(R2 + 7) / 8, 256, 0, st>>>(m->x, R2, L.ln2, L.ln2 + D, eps, m->y);
+        bert::launch_ln(m->x, R2, L.ln2, L.ln2 + D, eps, m->y, st);
         if ((e = gemm_bf16(m->y, D, L.w1, D, R2, F, D, L.b1, nullptr, 0, 1, m->hb, F, st))) break;
         if ((e = gemm_bf16(m->hb, F, L.w2, F, R2, D, F, L.b2, m->x, D, 0, m->y, D, st))) break;
         std::swap(m->x, m->y);   // x <- x + ffn
     }
-    if (!e) bert::ln_kernel<<<(R2 + 7) / 8, 256, 0, st>>>(m->x, R2, m->lnpost, m->lnpost + D, eps, out_dev);
+    if (!e) bert::launch_ln(m->x, R2, m->lnpost, m->lnpost + D, eps, out_dev, st);
     if (!e) e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_last_error_message(std::string("xdna_whisper_encode_device: ") + cudaGetErrorString(e));
