@@ -142,12 +142,9 @@ __global__ void __launch_bounds__(256, LN_BLOCKS_PER_SM) ln_kernel(const uint16_
 
 // the row LayerNorm over T rows: a grid of LN_BLOCKS_PER_SM blocks per SM (or fewer for short inputs)
 void launch_ln(const uint16_t *x, int T, const float *g, const float *b, float eps, uint16_t *y, cudaStream_t st) {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    }
+    int dev = 0, sms = 148;            // queried per call: cheap, and right on any current device
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int blocks = std::min((T + 7) / 8, sms * LN_BLOCKS_PER_SM);
     ln_kernel<<<blocks, 256, 0, st>>>(x, T, g, b, eps, y);
 }
