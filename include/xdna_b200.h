@@ -446,7 +446,10 @@ typedef struct XdnaGemvBf16 XdnaGemvBf16;
 XdnaGemvBf16 *xdna_gemv_bf16_register(XdnaDevice *dev, const float *w, int K, int N, const float *bias, int norm,
                                       const float *gamma, const float *beta, float eps);
 void xdna_gemv_bf16_free(XdnaGemvBf16 *h);
-/* Host x[K] -> host y[N]: the input statistics in f64 on the host (RMS: x / sqrt(mean(x^2)
+/* Handles with staging buffers (XdnaGemvBf16, XdnaLogMel) serve one call at a time: calls on
+ * one handle from several threads must be serialised by the caller (as the reference's device
+ * objects, which are neither Send nor Sync).
+ * Host x[K] -> host y[N]: the input statistics in f64 on the host (RMS: x / sqrt(mean(x^2)
  * + eps); LN: (x - mean) / sqrt(var + eps)), x rounded to bf16, f32 accumulation over
  * bf16 products on the GPU, + bias'.  Synchronous; 0 or -1. */
 int xdna_gemv_bf16(XdnaGemvBf16 *h, const float *x, float *y);
