@@ -917,7 +917,7 @@ def run_wdec(args):
         "ms_per_token_b32": ms_token, "ms_per_token_b1": ms_token_b1,
         # bfp16 blocks whose mantissas needed both +128 and -128 (stored with +128 as 127): the
         # one place the weight storage can differ from the reference's block rule
-        "bfp16_clamped_blocks": int(dec.clamped_blocks()),
+        "bfp16_clamped_blocks": int(dec.clamped_blocks),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_token": bytes_step,

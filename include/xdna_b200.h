@@ -311,7 +311,8 @@ typedef struct XdnaWhisperDec XdnaWhisperDec;
 XdnaWhisperDec *xdna_whisper_dec_create(XdnaDevice *dev, const XdnaWhisperDecConfig *cfg,
                                         const XdnaWhisperDecWeights *w, int max_batch);
 void xdna_whisper_dec_free(XdnaWhisperDec *m);
-/* bfp16 blocks that held both mantissa +128 and -128 (stored with +128 as 127; 0 in practice) */
+/* bfp16 blocks that held both mantissa +128 and -128 (stored with +128 as 127): 251 of the
+ * ~15.6 million blocks of the random-init N(0, 0.02) Whisper-small decoder */
 long long xdna_whisper_dec_clamped_blocks(const XdnaWhisperDec *m);
 /* cross K/V of every layer from encoder states enc_dev [B][n_enc][768] f32 (device); async */
 int xdna_whisper_dec_set_encoder(XdnaWhisperDec *m, const float *enc_dev, int B, void *stream);

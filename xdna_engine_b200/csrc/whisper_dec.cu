@@ -337,17 +337,19 @@ __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const 
 // with this layer's K at column koff + h*64 and V at koff + D + h*64.  The chunk's K and V
 // rows are staged in shared memory with 16-byte loads first.
 constexpr int XCH = 128;
-__global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const uint16_t *kv, int T, int ldkv,
-                                                         int koff, float *part, int nsplit) {
+// The cross K/V of one layer, head-major: ckl[b][h][K | V][T][64] bf16 (cross_relayout_kernel), so
+// a split's 128 keys are one contiguous 16 KB block of K and one of V.
+__global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const uint16_t *ckl, int T, float *part,
+                                                         int nsplit) {
     __shared__ __align__(16) uint16_t ks[XCH * HD], vs[XCH * HD];
     __shared__ float qs[HD], sc[XCH], red[4], pacc[2][HD];
     const int h = blockIdx.x, b = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
     const int jn = min(XCH, T - s * XCH);
-    const uint16_t *base = kv + ((size_t)b * T + (size_t)s * XCH) * ldkv + koff + h * HD;
+    const uint4 *kb = reinterpret_cast<const uint4 *>(ckl + (((size_t)b * H + h) * 2 * T + (size_t)s * XCH) * HD);
+    const uint4 *vb = kb + (size_t)T * HD / 8;
     for (int i = tid; i < jn * 8; i += 128) {
-        const int row = i >> 3, c = i & 7;
-        reinterpret_cast<uint4 *>(ks)[i] = *reinterpret_cast<const uint4 *>(base + (size_t)row * ldkv + 8 * c);
-        reinterpret_cast<uint4 *>(vs)[i] = *reinterpret_cast<const uint4 *>(base + (size_t)row * ldkv + D + 8 * c);
+        reinterpret_cast<uint4 *>(ks)[i] = kb[i];
+        reinterpret_cast<uint4 *>(vs)[i] = vb[i];
     }
     if (tid < HD) qs[tid] = q[(size_t)b * D + h * HD + tid];
     __syncthreads();
@@ -388,6 +390,19 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const u
     if (tid < HD) pp[2 + tid] = pacc[0][tid] + pacc[1][tid];
     if (tid == 0) { pp[0] = mx; pp[1] = red[0] + red[1] + red[2] + red[3]; }
 }
+// ckv [B * T][L][K | V][768] (the cross K/V GEMM's output) -> ckh [L][B][12 heads][K | V][T][64]:
+// 16-byte chunks, reads coalesced along a row, writes in 128-byte head rows
+__global__ void cross_relayout_kernel(const uint16_t *__restrict__ ckv, int B, int T, int L, uint16_t *__restrict__ ckh) {
+    const size_t row_chunks = (size_t)L * 2 * D / 8, n = (size_t)B * T * row_chunks;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t bt = i / row_chunks, r = i % row_chunks;
+        const int b = (int)(bt / T), t = (int)(bt % T);
+        const int l = (int)(r / (2 * D / 8)), kv = (int)((r / (D / 8)) & 1), h = (int)((r % (D / 8)) / 8), c = (int)(r % 8);
+        const size_t dst = (((((size_t)l * B + b) * H + h) * 2 + kv) * T + t) * HD + 8 * c;
+        *reinterpret_cast<uint4 *>(ckh + dst) = *reinterpret_cast<const uint4 *>(ckv + i * 8);
+    }
+}
+
 __global__ void cross_merge_kernel(const float *__restrict__ part, int nsplit, uint16_t *__restrict__ ctx) {
     griddep_launch();                                 // the next GEMV may start its weight fetch
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
@@ -526,6 +541,7 @@ struct XdnaWhisperDec {
     // state
     float *x = nullptr, *qkv = nullptr, *q = nullptr, *logits = nullptr, *xpart = nullptr;
     uint16_t *xn = nullptr, *ctx = nullptr, *h = nullptr, *kcache = nullptr, *vcache = nullptr, *ckv = nullptr,
+             *ckh = nullptr,
              *enc_bf = nullptr;
     float *enc_f = nullptr;
     unsigned *done = nullptr;
@@ -690,8 +706,8 @@ cudaError_t step(XdnaWhisperDec *m, int B, int n_prompt, int n_new, float *lrec,
         if ((e = gemv(m, L.out, m->ctx, B, OUT_RESID, m->x, nullptr, D, st))) break;
         ln_kernel<<<(B + 7) / 8, 256, 0, st>>>(m->x, B, L.ln + 2 * D, L.ln + 3 * D, m->xn);
         if ((e = gemv(m, L.cq, m->xn, B, OUT_F32, m->q, nullptr, D, st))) break;
-        cross_attn_kernel<<<dim3(H, B, nsplit), 128, 0, st>>>(m->q, m->ckv, c.n_enc, c.n_layers * 2 * D, l * 2 * D,
-                                                               m->xpart, nsplit);
+        cross_attn_kernel<<<dim3(H, B, nsplit), 128, 0, st>>>(m->q, m->ckh + (size_t)l * B * H * 2 * c.n_enc * HD,
+                                                               c.n_enc, m->xpart, nsplit);
         cross_merge_kernel<<<dim3(H, B), HD, 0, st>>>(m->xpart, nsplit, m->ctx);
         if ((e = gemv(m, L.cout, m->ctx, B, OUT_RESID, m->x, nullptr, D, st))) break;
         ln_kernel<<<(B + 7) / 8, 256, 0, st>>>(m->x, B, L.ln + 4 * D, L.ln + 5 * D, m->xn);
@@ -804,6 +820,7 @@ XdnaWhisperDec *xdna_whisper_dec_create(XdnaDevice *dev_unused, const XdnaWhispe
         m->kcache = static_cast<uint16_t *>(keep(dalloc<uint16_t>(L * B * H * c.max_tgt * HD)));
         m->vcache = static_cast<uint16_t *>(keep(dalloc<uint16_t>(L * B * H * c.max_tgt * HD)));
         m->ckv = static_cast<uint16_t *>(keep(dalloc<uint16_t>(B * c.n_enc * L * 2 * D)));
+        m->ckh = static_cast<uint16_t *>(keep(dalloc<uint16_t>(B * c.n_enc * L * 2 * D)));
         m->enc_bf = static_cast<uint16_t *>(keep(dalloc<uint16_t>(B * c.n_enc * D)));
         m->enc_f = static_cast<float *>(keep(dalloc<float>(B * c.n_enc * D)));
         m->done = static_cast<unsigned *>(keep(dalloc<unsigned>(1)));
@@ -846,6 +863,10 @@ int xdna_whisper_dec_set_encoder(XdnaWhisperDec *m, const float *enc_dev, int B,
     cudaError_t e = cudaGetLastError();
     if (!e) e = gemm_bf16(m->enc_bf, wdec::D, m->ckv_w, wdec::D, B * c.n_enc, NKV, wdec::D, m->ckv_b, nullptr, 0, 0,
                           m->ckv, NKV, st);
+    if (!e) {
+        wdec::cross_relayout_kernel<<<148 * 8, 256, 0, st>>>(m->ckv, B, c.n_enc, c.n_layers, m->ckh);
+        e = cudaGetLastError();
+    }
     if (e) { set_last_error_message(std::string("xdna_whisper_dec_set_encoder: ") + cudaGetErrorString(e)); return -1; }
     m->B_enc = B;
     return 0;
