@@ -326,6 +326,19 @@ int xdna_whisper_dec_run(XdnaWhisperDec *m, int B, const int64_t *prompt_host, i
  * nullable, [B][n_new][vocab]).  Synchronous. */
 int xdna_whisper_dec_generate(XdnaWhisperDec *m, const float *enc_host, int B, const int64_t *prompt, int n_prompt,
                               int n_new, int64_t *tokens_host, float *logits_host);
+/* Continuous batching (per-stream positions; the batched decode with per-stream positions and
+ * masks that gen_decode_batched.py:3-12 defers): the decoder holds max_batch slots, each with its
+ * own cross K/V and self-attention cache.  A stream joins by loading its encoder states into a
+ * free slot (set_encoder_slot: enc_dev [n_enc][768] f32 device, asynchronous on `stream`) and
+ * feeding its prompt from position 0; every step_slots call runs one decoder step for slots
+ * 0 .. n_slots-1, slot b feeding tokens[b] at positions[b] (its own K/V row is written there and
+ * its self-attention spans positions 0 .. positions[b]; a negative position marks an empty slot)
+ * and returning its greedy next token (first maximum; -1 for an empty slot) in next[b], with the
+ * logits rows in logits [n_slots][vocab] when not NULL.  Host arrays; synchronous; the first step
+ * of each width is recorded as a CUDA graph.  A stream leaves by simply not being fed. */
+int xdna_whisper_dec_set_encoder_slot(XdnaWhisperDec *m, int slot, const float *enc_dev, void *stream);
+int xdna_whisper_dec_step_slots(XdnaWhisperDec *m, int n_slots, const int64_t *tokens, const int *positions,
+                                int64_t *next, float *logits);
 
 /* ------------------------------------------------------------ Gemma-3 text decoder */
 /* The reference has no Gemma decode step (rust/npu-gemma/src/lib.rs:30-43 maps what to reuse:

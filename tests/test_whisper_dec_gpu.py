@@ -140,3 +140,61 @@ def test_whisper_decoder_baseline_config(X):
                 srt = np.sort(r)
                 assert srt[-1] - srt[-2] < np.abs(g - r).max(), (b, s, "flip with a clear margin")
     print("whisper dec worst rel-L2", worst)
+
+
+def test_continuous_batching_matches_single_streams(X):
+    """Continuous batching (xdna_whisper_dec_set_encoder_slot / step_slots): four streams with
+    their own prompts and encoder states join three slots at different steps, run at their own
+    positions (each self-attention spans only its own tokens), leave when done, and a later
+    stream reuses a freed slot.  Every stream's greedy tokens equal its own single-stream run
+    (xdna_whisper_dec_generate, batch 1) bit for bit, and so do its logits."""
+    from xdna_engine_b200.synth import WhisperDecConfig, make_encoder_states, make_whisper_dec_weights
+    cfg = WhisperDecConfig(n_layers=2)
+    w = make_whisper_dec_weights(cfg, seed=6, bias_std=0.02, ln_std=0.05)
+    encs = make_encoder_states(cfg, 4, seed=6)
+    prompts = [[50258, 50259, 50359, 50363], [50258, 50260, 50359], [50258, 50261, 50359, 50363], [50258, 50262]]
+    n_new = 10
+    single = X.WhisperDecoder(X.Device(0), cfg, w, max_batch=1)
+    want, want_lg = [], []
+    for s in range(4):
+        t, lg = single.generate(encs[s:s + 1], prompts[s], n_new, want_logits=True)
+        want.append(t[0].tolist())
+        want_lg.append(lg[0])
+    single.close()
+
+    dec = X.WhisperDecoder(X.Device(0), cfg, w, max_batch=3)
+    joins = {0: (0, 0), 3: (1, 1), 5: (2, 2)}           # step -> (stream, slot)
+    slot_of = {}
+    state = {}                                          # stream -> [pos, generated, logits rows]
+    free_after = {}
+    step = 0
+    while len(state) < 4 or any(len(v[1]) < n_new for v in state.values()):
+        if step in joins:
+            s, slot = joins[step]
+            dec.set_encoder_slot(slot, encs[s])
+            slot_of[slot] = s
+            state[s] = [0, [], []]
+        tokens = np.zeros(3, np.int64)
+        positions = np.full(3, -1, np.int32)
+        for slot, s in slot_of.items():
+            pos, gen, _ = state[s]
+            tokens[slot] = prompts[s][pos] if pos < len(prompts[s]) else gen[-1]
+            positions[slot] = pos
+        nxt, lg = dec.step_slots(tokens, positions, want_logits=True)
+        for slot, s in list(slot_of.items()):
+            st_ = state[s]
+            if st_[0] >= len(prompts[s]) - 1:
+                st_[1].append(int(nxt[slot]))
+                st_[2].append(lg[slot].copy())
+            st_[0] += 1
+            if len(st_[1]) == n_new:                   # done: the slot is free again
+                del slot_of[slot]
+                if 3 not in state:                     # stream 3 joins the first freed slot
+                    joins[step + 1] = (3, slot)
+        assert all(nxt[b] == -1 for b in range(3) if positions[b] < 0)
+        step += 1
+        assert step < 200
+    dec.close()
+    for s in range(4):
+        assert state[s][1] == want[s], (s, state[s][1], want[s])
+        np.testing.assert_array_equal(np.stack(state[s][2]), want_lg[s])

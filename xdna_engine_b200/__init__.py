@@ -119,6 +119,10 @@ def lib():
         L.xdna_whisper_dec_run.restype = i
         L.xdna_whisper_dec_generate.argtypes = [vp, vp, i, vp, i, i, vp, vp]
         L.xdna_whisper_dec_generate.restype = i
+        L.xdna_whisper_dec_set_encoder_slot.argtypes = [vp, i, vp, vp]
+        L.xdna_whisper_dec_set_encoder_slot.restype = i
+        L.xdna_whisper_dec_step_slots.argtypes = [vp, i, vp, vp, vp, vp]
+        L.xdna_whisper_dec_step_slots.restype = i
         L.xdna_gemma_create.argtypes = [vp, vp, vp, i, i, i, i]
         L.xdna_gemma_create.restype = vp
         L.xdna_gemma_free.argtypes = [vp]
@@ -678,6 +682,24 @@ class WhisperDecoder:
     @property
     def clamped_blocks(self) -> int:
         return lib().xdna_whisper_dec_clamped_blocks(self.handle)
+
+    # ---- continuous batching
+    def set_encoder_slot(self, slot: int, enc):
+        """Load one stream's encoder states enc [n_enc, 768] (host) into `slot`."""
+        import torch
+        d = torch.from_numpy(np.ascontiguousarray(enc, np.float32)).cuda()
+        _check(lib().xdna_whisper_dec_set_encoder_slot(self.handle, slot, d.data_ptr(), None))
+        torch.cuda.synchronize()
+
+    def step_slots(self, tokens, positions, want_logits=False):
+        """One step for slots 0 .. len(tokens)-1 at their own positions (negative: empty slot)."""
+        t = np.ascontiguousarray(tokens, np.int64)
+        p = np.ascontiguousarray(positions, np.int32)
+        nxt = np.empty(t.size, np.int64)
+        lg = np.empty((t.size, self.cfg.vocab), np.float32) if want_logits else None
+        _check(lib().xdna_whisper_dec_step_slots(self.handle, t.size, _addr(t), _addr(p), _addr(nxt),
+                                                  None if lg is None else _addr(lg)))
+        return (nxt, lg) if want_logits else nxt
 
     def generate(self, enc, prompt, n_new, want_logits=False):
         enc = np.ascontiguousarray(enc, np.float32)

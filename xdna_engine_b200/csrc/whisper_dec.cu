@@ -230,10 +230,14 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) bfp_gemv_kernel(GemvArgs a
     }
 }
 
-__global__ void embed_kernel(const int64_t *tok, const int *pos, const float *et, const float *ep, float *x) {
-    const int b = blockIdx.x, p = *pos;
+// positions: pos[b * pos_stride] (stride 0: one shared position; 1: per stream); a negative
+// position marks an empty slot, which gets a zero row
+__global__ void embed_kernel(const int64_t *tok, const int *pos, int pos_stride, const float *et, const float *ep,
+                             float *x) {
+    const int b = blockIdx.x, p = pos[b * pos_stride];
     const int64_t id = tok[b];
-    for (int d = threadIdx.x; d < D; d += blockDim.x) x[(size_t)b * D + d] = et[(size_t)id * D + d] + ep[(size_t)p * D + d];
+    for (int d = threadIdx.x; d < D; d += blockDim.x)
+        x[(size_t)b * D + d] = p < 0 ? 0.0f : et[(size_t)id * D + d] + ep[(size_t)p * D + d];
 }
 
 // y = bf16(LN(x)) per stream row (ln_row: population variance, eps 1e-5); one warp per row
@@ -273,12 +277,16 @@ __global__ void ln_kernel(const float *__restrict__ x, int B, const float *__res
 // [B][3D]; cache [B][H][max_tgt][64] (K) and the same for V; ctx bf16 [B][D].
 constexpr int SA_MAX = 448;
 constexpr int SA_SMEM = 2 * SA_MAX * HD * 2;
-__global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const int *posp, int max_tgt,
+__global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const int *posp, int pos_stride, int max_tgt,
                                                         uint16_t *kc, uint16_t *vc, uint16_t *ctx) {
     griddep_launch();                                 // the next GEMV may start its weight fetch
     extern __shared__ __align__(16) uint16_t kvs[];        // K rows then V rows
     __shared__ float q[HD], sc[SA_MAX], red[8], part[2][HD];
-    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, pos = *posp;
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, pos = posp[b * pos_stride];
+    if (pos < 0) {                                    // an empty slot: no cache row, zero context
+        if (tid < HD) ctx[(size_t)b * D + h * HD + tid] = 0;
+        return;
+    }
     const float *r = qkv + (size_t)b * 3 * D + h * HD;
     const size_t cb = ((size_t)b * H + h) * max_tgt * HD;
     const int S = pos + 1;
@@ -390,16 +398,49 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const u
     if (tid < HD) pp[2 + tid] = pacc[0][tid] + pacc[1][tid];
     if (tid == 0) { pp[0] = mx; pp[1] = red[0] + red[1] + red[2] + red[3]; }
 }
+// continuous batching: each slot's greedy next token (first maximum), -1 for an empty slot;
+// the logits rows optionally copied to logits_out [B][V]
+__global__ void __launch_bounds__(1024) slot_argmax_kernel(const float *logits, int V, int ldl, const int *pos,
+                                                           int64_t *next, float *logits_out) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const float *lr = logits + (size_t)b * ldl;
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = tid; i < V; i += blockDim.x) {
+        const float v = lr[i];
+        if (v > best) { best = v; idx = i; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    if ((tid & 31) == 0) { bv[tid >> 5] = best; bi[tid >> 5] = idx; }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
+        next[b] = pos[b] < 0 ? -1 : idx;
+    }
+    if (logits_out)
+        for (int i = tid; i < V; i += blockDim.x) logits_out[(size_t)b * V + i] = lr[i];
+}
+
 // ckv [B * T][L][K | V][768] (the cross K/V GEMM's output) -> ckh [L][B][12 heads][K | V][T][64]:
 // 16-byte chunks, reads coalesced along a row, writes in 128-byte head rows
-__global__ void cross_relayout_kernel(const uint16_t *__restrict__ ckv, int B, int T, int L, uint16_t *__restrict__ ckh) {
+// (streams b0 .. b0 + B - 1 of ckv's rows, into a layout of BL streams)
+__global__ void cross_relayout_kernel(const uint16_t *__restrict__ ckv, int b0, int B, int BL, int T, int L,
+                                      uint16_t *__restrict__ ckh) {
     const size_t row_chunks = (size_t)L * 2 * D / 8, n = (size_t)B * T * row_chunks;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const size_t bt = i / row_chunks, r = i % row_chunks;
-        const int b = (int)(bt / T), t = (int)(bt % T);
+        const int b = b0 + (int)(bt / T), t = (int)(bt % T);
         const int l = (int)(r / (2 * D / 8)), kv = (int)((r / (D / 8)) & 1), h = (int)((r % (D / 8)) / 8), c = (int)(r % 8);
-        const size_t dst = (((((size_t)l * B + b) * H + h) * 2 + kv) * T + t) * HD + 8 * c;
-        *reinterpret_cast<uint4 *>(ckh + dst) = *reinterpret_cast<const uint4 *>(ckv + i * 8);
+        const size_t dst = (((((size_t)l * BL + b) * H + h) * 2 + kv) * T + t) * HD + 8 * c;
+        *reinterpret_cast<uint4 *>(ckh + dst) = *reinterpret_cast<const uint4 *>(ckv + ((size_t)b0 * T) * (row_chunks * 8) + i * 8);
     }
 }
 
@@ -547,6 +588,11 @@ struct XdnaWhisperDec {
     unsigned *done = nullptr;
     int *pos = nullptr;
     int64_t *tok = nullptr, *prompt = nullptr, *out_tok = nullptr, *tok_out = nullptr;
+    // continuous batching: per-slot token, position and next token; logits rows [max_batch][V]
+    int *spos = nullptr;
+    int64_t *stok = nullptr, *snext = nullptr;
+    float *slog = nullptr;
+    std::vector<std::pair<int, cudaGraphExec_t>> slot_graphs[2];   // [with logits] (n_slots, graph)
     float *lrec = nullptr;                  // logits record of xdna_whisper_dec_generate
     size_t lrec_n = 0;
     int B_enc = 0;
@@ -560,6 +606,8 @@ struct XdnaWhisperDec {
     cudaStream_t cap = nullptr;
     ~XdnaWhisperDec() {
         if (lrec) cudaFree(lrec);
+        for (auto &v : slot_graphs)
+            for (auto &g : v) cudaGraphExecDestroy(g.second);
         for (auto &g : graphs)
             if (g.exec) cudaGraphExecDestroy(g.exec);
         if (cap) cudaStreamDestroy(cap);
@@ -689,24 +737,28 @@ cudaError_t gemv(XdnaWhisperDec *m, const BfpMat &w, const uint16_t *x, int B, i
     return cudaLaunchKernelEx(&lc, wdec::bfp_gemv_kernel<4>, a);
 }
 
-// one token for B streams (reads *pos and tok on the device, advances both)
-cudaError_t step(XdnaWhisperDec *m, int B, int n_prompt, int n_new, float *lrec, cudaStream_t st) {
+// one token for B streams.  Lockstep (slots == false): reads *pos and tok on the device and
+// advances both.  Slots: stream b feeds stok[b] at its own position spos[b] (< 0: empty slot) and
+// writes its greedy next token to snext[b] (logits rows to slog when not null).
+cudaError_t step(XdnaWhisperDec *m, int B, int n_prompt, int n_new, float *lrec, cudaStream_t st, bool slots = false) {
     using namespace wdec;
     const auto &c = m->cfg;
     const int nsplit = (c.n_enc + XCH - 1) / XCH;
+    const int *posp = slots ? m->spos : m->pos;
+    const int pstride = slots ? 1 : 0;
     cudaError_t e = cudaSuccess;
-    embed_kernel<<<B, 256, 0, st>>>(m->tok, m->pos, m->et, m->ep, m->x);
+    embed_kernel<<<B, 256, 0, st>>>(slots ? m->stok : m->tok, posp, pstride, m->et, m->ep, m->x);
     for (int l = 0; l < c.n_layers && !e; l++) {
         const auto &L = m->layers[l];
         ln_kernel<<<(B + 7) / 8, 256, 0, st>>>(m->x, B, L.ln, L.ln + D, m->xn);
         if ((e = gemv(m, L.qkv, m->xn, B, OUT_F32, m->qkv, nullptr, 3 * D, st))) break;
-        self_attn_kernel<<<dim3(H, B), 128, SA_SMEM, st>>>(m->qkv, m->pos, c.max_tgt,
+        self_attn_kernel<<<dim3(H, B), 128, SA_SMEM, st>>>(m->qkv, posp, pstride, c.max_tgt,
                                                      m->kcache + (size_t)l * m->max_batch * H * c.max_tgt * HD,
                                                      m->vcache + (size_t)l * m->max_batch * H * c.max_tgt * HD, m->ctx);
         if ((e = gemv(m, L.out, m->ctx, B, OUT_RESID, m->x, nullptr, D, st))) break;
         ln_kernel<<<(B + 7) / 8, 256, 0, st>>>(m->x, B, L.ln + 2 * D, L.ln + 3 * D, m->xn);
         if ((e = gemv(m, L.cq, m->xn, B, OUT_F32, m->q, nullptr, D, st))) break;
-        cross_attn_kernel<<<dim3(H, B, nsplit), 128, 0, st>>>(m->q, m->ckh + (size_t)l * B * H * 2 * c.n_enc * HD,
+        cross_attn_kernel<<<dim3(H, B, nsplit), 128, 0, st>>>(m->q, m->ckh + (size_t)l * m->max_batch * H * 2 * c.n_enc * HD,
                                                                c.n_enc, m->xpart, nsplit);
         cross_merge_kernel<<<dim3(H, B), HD, 0, st>>>(m->xpart, nsplit, m->ctx);
         if ((e = gemv(m, L.cout, m->ctx, B, OUT_RESID, m->x, nullptr, D, st))) break;
@@ -718,8 +770,11 @@ cudaError_t step(XdnaWhisperDec *m, int B, int n_prompt, int n_new, float *lrec,
     ln_kernel<<<(B + 7) / 8, 256, 0, st>>>(m->x, B, m->lnpost, m->lnpost + D, m->xn);
     const int ldl = (c.vocab + 15) / 16 * 16;
     if ((e = gemv(m, m->lm, m->xn, B, OUT_F32, m->logits, nullptr, ldl, st))) return e;
-    argmax_kernel<<<B, 1024, 0, st>>>(m->logits, c.vocab, ldl, B, m->prompt, n_prompt, m->pos, m->tok, m->out_tok,
-                                      n_new, lrec, m->done);
+    if (slots)
+        slot_argmax_kernel<<<B, 1024, 0, st>>>(m->logits, c.vocab, ldl, m->spos, m->snext, lrec);
+    else
+        argmax_kernel<<<B, 1024, 0, st>>>(m->logits, c.vocab, ldl, B, m->prompt, n_prompt, m->pos, m->tok, m->out_tok,
+                                          n_new, lrec, m->done);
     return cudaGetLastError();
 }
 }  // namespace
@@ -829,6 +884,10 @@ XdnaWhisperDec *xdna_whisper_dec_create(XdnaDevice *dev_unused, const XdnaWhispe
         m->prompt = static_cast<int64_t *>(keep(dalloc<int64_t>(c.max_tgt)));
         m->out_tok = static_cast<int64_t *>(keep(dalloc<int64_t>(B * c.max_tgt)));
         m->tok_out = static_cast<int64_t *>(keep(dalloc<int64_t>(B * c.max_tgt)));
+        m->spos = static_cast<int *>(keep(dalloc<int>(B)));
+        m->stok = static_cast<int64_t *>(keep(dalloc<int64_t>(B)));
+        m->snext = static_cast<int64_t *>(keep(dalloc<int64_t>(B)));
+        m->slog = static_cast<float *>(keep(dalloc<float>(B * (size_t)c.vocab)));
         ck(cudaMemset(m->done, 0, sizeof(unsigned)), "memset");
         ck(cudaFuncSetAttribute(self_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SA_SMEM), "smem");
         const int gsm = (int)kGemvSmemCap;
@@ -864,11 +923,80 @@ int xdna_whisper_dec_set_encoder(XdnaWhisperDec *m, const float *enc_dev, int B,
     if (!e) e = gemm_bf16(m->enc_bf, wdec::D, m->ckv_w, wdec::D, B * c.n_enc, NKV, wdec::D, m->ckv_b, nullptr, 0, 0,
                           m->ckv, NKV, st);
     if (!e) {
-        wdec::cross_relayout_kernel<<<148 * 8, 256, 0, st>>>(m->ckv, B, c.n_enc, c.n_layers, m->ckh);
+        wdec::cross_relayout_kernel<<<148 * 8, 256, 0, st>>>(m->ckv, 0, B, m->max_batch, c.n_enc, c.n_layers, m->ckh);
         e = cudaGetLastError();
     }
     if (e) { set_last_error_message(std::string("xdna_whisper_dec_set_encoder: ") + cudaGetErrorString(e)); return -1; }
     m->B_enc = B;
+    return 0;
+}
+
+// ---- continuous batching: streams join and leave slots; every slot runs at its own position
+int xdna_whisper_dec_set_encoder_slot(XdnaWhisperDec *m, int slot, const float *enc_dev, void *stream) {
+    if (!m || !enc_dev) { set_last_error_message("xdna_whisper_dec_set_encoder_slot: null pointer"); return -1; }
+    if (slot < 0 || slot >= m->max_batch) {
+        set_last_error_message("xdna_whisper_dec_set_encoder_slot: slot outside 0 .. max_batch - 1");
+        return -1;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const auto &c = m->cfg;
+    const size_t n = (size_t)c.n_enc * wdec::D;
+    const int NKV = c.n_layers * 2 * wdec::D;
+    uint16_t *enc_bf = m->enc_bf + (size_t)slot * n, *ckv = m->ckv + (size_t)slot * c.n_enc * NKV;
+    wdec::to_bf16_kernel<<<1184, 256, 0, st>>>(enc_dev, n, enc_bf);
+    cudaError_t e = cudaGetLastError();
+    if (!e) e = gemm_bf16(enc_bf, wdec::D, m->ckv_w, wdec::D, c.n_enc, NKV, wdec::D, m->ckv_b, nullptr, 0, 0, ckv, NKV, st);
+    if (!e) {
+        wdec::cross_relayout_kernel<<<148 * 8, 256, 0, st>>>(m->ckv, slot, 1, m->max_batch, c.n_enc, c.n_layers, m->ckh);
+        e = cudaGetLastError();
+    }
+    if (e) { set_last_error_message(std::string("xdna_whisper_dec_set_encoder_slot: ") + cudaGetErrorString(e)); return -1; }
+    return 0;
+}
+
+int xdna_whisper_dec_step_slots(XdnaWhisperDec *m, int n_slots, const int64_t *tokens, const int *positions,
+                                int64_t *next, float *logits) {
+    if (!m || !tokens || !positions || !next) { set_last_error_message("xdna_whisper_dec_step_slots: null pointer"); return -1; }
+    const auto &c = m->cfg;
+    if (n_slots < 1 || n_slots > m->max_batch) {
+        set_last_error_message("xdna_whisper_dec_step_slots: n_slots outside 1 .. max_batch");
+        return -1;
+    }
+    for (int b = 0; b < n_slots; b++)
+        if (positions[b] >= 0 && (positions[b] >= c.max_tgt || tokens[b] < 0 || tokens[b] >= c.vocab)) {
+            set_last_error_message("xdna_whisper_dec_step_slots: slot " + std::to_string(b) +
+                                   ": position beyond max_tgt or token out of range");
+            return -1;
+        }
+    cudaStream_t st = nullptr;
+    cudaError_t e = cudaMemcpy(m->stok, tokens, sizeof(int64_t) * n_slots, cudaMemcpyHostToDevice);
+    if (!e) e = cudaMemcpy(m->spos, positions, sizeof(int) * n_slots, cudaMemcpyHostToDevice);
+    auto &graphs = m->slot_graphs[logits ? 1 : 0];
+    cudaGraphExec_t exec = nullptr;
+    for (auto &g : graphs)
+        if (g.first == n_slots) exec = g.second;
+    if (!e && exec) e = cudaGraphLaunch(exec, st);
+    else if (!e) {
+        // the first step of a width runs eagerly (kernel attributes set before any capture), then
+        // the width is recorded as a graph for the following steps
+        e = step(m, n_slots, 0, 0, logits ? m->slog : nullptr, st, true);
+        if (!e && !m->cap) e = cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking);
+        cudaGraph_t graph = nullptr;
+        if (!e) e = cudaStreamSynchronize(st);
+        if (!e) e = cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal);
+        if (!e) {
+            const cudaError_t e2 = step(m, n_slots, 0, 0, logits ? m->slog : nullptr, m->cap, true);
+            e = cudaStreamEndCapture(m->cap, &graph);
+            if (!e) e = e2;
+        }
+        cudaGraphExec_t g = nullptr;
+        if (!e) e = cudaGraphInstantiate(&g, graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+        if (!e) graphs.push_back({n_slots, g});
+    }
+    if (!e) e = cudaMemcpy(next, m->snext, sizeof(int64_t) * n_slots, cudaMemcpyDeviceToHost);
+    if (!e && logits) e = cudaMemcpy(logits, m->slog, sizeof(float) * n_slots * (size_t)c.vocab, cudaMemcpyDeviceToHost);
+    if (e) { set_last_error_message(std::string("xdna_whisper_dec_step_slots: ") + cudaGetErrorString(e)); return -1; }
     return 0;
 }
 
