@@ -434,12 +434,13 @@ def run_bge(args):
     gemm_tflops = (14155776.0 * T) / (gemm_ms_layer * 1e-3) / 1e12
     # end to end through xdna_bert_embed: host ids in, host embeddings out
     e2e = []
-    host_out = np.empty((B, 768), np.float32)
+    host_out = pinned_like(shape=(B, 768), dtype=np.float32)
+    host_ids, host_lens = pinned_like(ids), pinned_like(lens)
     for _ in range(3):
         a, b = torch.cuda.Event(True), torch.cuda.Event(True)
         torch.cuda.synchronize()
         a.record(torch.cuda.default_stream())
-        rc = X.lib().xdna_bert_embed(m.handle, ids.ctypes.data, lens.ctypes.data, B, host_out.ctypes.data)
+        rc = X.lib().xdna_bert_embed(m.handle, host_ids.ctypes.data, host_lens.ctypes.data, B, host_out.ctypes.data)
         b.record(torch.cuda.default_stream())
         torch.cuda.synchronize()
         assert rc == 0, X.last_error()
@@ -577,13 +578,14 @@ def run_whisper(args):
     gemm_tflops = (2.0 * M * 768 * 9216) / (g0.elapsed_time(g1) * 1e-3) / 1e12
     del A, Bw, Cb
     # end to end through xdna_whisper_encode: host mel in, host f32 encodings out
-    host_out = np.empty((B, 1500, 768), np.float32)
+    host_out = pinned_like(shape=(B, 1500, 768), dtype=np.float32)
+    host_mel = pinned_like(mel)
     e2e = []
     for _ in range(3):
         a, b = torch.cuda.Event(True), torch.cuda.Event(True)
         torch.cuda.synchronize()
         a.record(torch.cuda.default_stream())
-        rc = X.lib().xdna_whisper_encode(enc.handle, mel.ctypes.data, B, host_out.ctypes.data)
+        rc = X.lib().xdna_whisper_encode(enc.handle, host_mel.ctypes.data, B, host_out.ctypes.data)
         b.record(torch.cuda.default_stream())
         torch.cuda.synchronize()
         assert rc == 0, X.last_error()
@@ -744,13 +746,14 @@ def run_parakeet(args):
     peak = int8_peak_tops()
     del A, Wt, Cf
     # end to end through xdna_parakeet_encode: host mel in, host encodings out
-    host_out = np.empty((B, T, 1024), np.float32)
+    host_out = pinned_like(shape=(B, T, 1024), dtype=np.float32)
+    host_mel = pinned_like(mel)
     e2e = []
     for _ in range(3):
         a, b = torch.cuda.Event(True), torch.cuda.Event(True)
         torch.cuda.synchronize()
         a.record(torch.cuda.default_stream())
-        rc = X.lib().xdna_parakeet_encode(enc.handle, mel.ctypes.data, B, host_out.ctypes.data)
+        rc = X.lib().xdna_parakeet_encode(enc.handle, host_mel.ctypes.data, B, host_out.ctypes.data)
         b.record(torch.cuda.default_stream())
         torch.cuda.synchronize()
         assert rc == 0, X.last_error()
@@ -884,13 +887,14 @@ def run_wdec(args):
     torch.cuda.synchronize()
     ms_token_b1 = a.elapsed_time(b) / (len(prompt) - 1 + 64)
     # end to end: host encoder states in (cross K/V precompute included), host tokens out
-    host_tok = np.empty((B, n_new), np.int64)
+    host_tok = pinned_like(shape=(B, n_new), dtype=np.int64)
+    host_enc = pinned_like(enc)
     e2e = []
     for _ in range(2):
         a, b = torch.cuda.Event(True), torch.cuda.Event(True)
         torch.cuda.synchronize()
         a.record(torch.cuda.default_stream())
-        assert L.xdna_whisper_dec_generate(dec.handle, enc.ctypes.data, B, prompt.ctypes.data, len(prompt), n_new,
+        assert L.xdna_whisper_dec_generate(dec.handle, host_enc.ctypes.data, B, prompt.ctypes.data, len(prompt), n_new,
                                            host_tok.ctypes.data, None) == 0, X.last_error()
         b.record(torch.cuda.default_stream())
         torch.cuda.synchronize()
@@ -1190,6 +1194,23 @@ def run_gemma(args):
     print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def pinned_like(a=None, shape=None, dtype=None):
+    """A numpy view of page-locked host memory (the e2e legs copy from and to pinned buffers),
+    filled with `a` when given."""
+    import torch
+    if a is not None:
+        shape, dtype = a.shape, a.dtype
+    t = torch.empty(tuple(shape), dtype=torch.from_numpy(np.empty(0, dtype)).dtype, pin_memory=True)
+    out = t.numpy()
+    if a is not None:
+        out[...] = a
+    pinned_like.keep.append(t)
+    return out
+
+
+pinned_like.keep = []
 
 
 def _time_ms(fn, st, reps=10, warm=3):

@@ -149,6 +149,12 @@ void launch_ln(const uint16_t *x, int T, const float *g, const float *b, float e
     ln_kernel<<<blocks, 256, 0, st>>>(x, T, g, b, eps, y);
 }
 
+// bf16 -> f32 (exact), grid-stride
+__global__ void bf16_to_f32_kernel(const uint16_t *__restrict__ x, size_t n, float *__restrict__ y) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __uint_as_float((uint32_t)x[i] << 16);
+}
+
 // ---------------------------------------------------------------------------- attention
 // softmax(q k^T / 8) v per (sequence, head) over the sequence's own keys (the valid_len key
 // mask of npu-asr-host mha, lib.rs:189-326): the tcgen05 kernel of attention_tc.cu.
@@ -653,14 +659,15 @@ int xdna_whisper_encode(XdnaWhisperEnc *m, const float *mel, int B, float *out) 
     const int C = m->cfg.n_mels, T = m->cfg.n_frames, To = T / 2;
     try {
         ck(cudaMemcpy(m->mel, mel, sizeof(float) * (size_t)B * C * T, cudaMemcpyHostToDevice), "copy mel");
-        uint16_t *enc = m->hb;   // reuse the FFN buffer for the bf16 result
+        // the FFN buffer ([B * To][3072] bf16) holds the bf16 result and, after it, its f32 widening
+        // (2 + 4 bytes per value <= 2 * 3072 / 768), which is copied straight into `out`
+        const size_t n = (size_t)B * To * whisper::D;
+        uint16_t *enc = m->hb;
+        float *encf = reinterpret_cast<float *>(m->hb + n);
         if (xdna_whisper_encode_device(m, m->mel, B, enc, nullptr) != 0) return -1;
-        std::vector<uint16_t> hbuf((size_t)B * To * whisper::D);
-        ck(cudaMemcpy(hbuf.data(), enc, hbuf.size() * 2, cudaMemcpyDeviceToHost), "copy encoded");
-        for (size_t i = 0; i < hbuf.size(); i++) {
-            const uint32_t u = (uint32_t)hbuf[i] << 16;
-            std::memcpy(out + i, &u, 4);
-        }
+        bert::bf16_to_f32_kernel<<<148 * 8, 256>>>(enc, n, encf);
+        ck(cudaGetLastError(), "widen");
+        ck(cudaMemcpy(out, encf, n * sizeof(float), cudaMemcpyDeviceToHost), "copy encoded");
         if (gemm_error_and_clear() | attention_tc_error_and_clear()) {
             set_last_error_message("xdna_whisper_encode: a tensor-core wait expired");
             return -1;
