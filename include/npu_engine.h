@@ -41,15 +41,26 @@ void npu_model_free(NpuModel *m);
 /* Thread-local last error ("" if none).  (lib.rs:114-119) */
 const char *npu_last_error(void);
 
-/* Control plane (rust/npu-capi/src/lib.rs:129-214).  Exported for link compatibility; the
- * control plane itself is not part of this backend, so these report an error. */
+/* Control plane (rust/npu-capi/src/lib.rs:125-214 over rust/npu-runtime): one worker thread per
+ * GPU, each holding a replica of every configured model; requests go to the least-busy worker.
+ * Config TOML as npu-runtime's config.rs ([server], [defaults], [[model]] name / scenario) plus
+ * `[server] gpus = N`; a missing file is the empty config.  All calls are thread safe. */
+/* Start from a config path (loads its models on every GPU).  NULL on error.  (lib.rs:129-144) */
 NpuRuntime *npu_runtime_start(const char *config_path);
+/* ASR through the control plane (model name or NULL for the default).  Caller frees.
+ * (lib.rs:146-160) */
 char *npu_runtime_transcribe(NpuRuntime *rt, const char *model, const int16_t *pcm, uintptr_t n,
                              uint32_t sample_rate);
+/* Embedding through the control plane: copies min(dim, out_cap) floats, returns dim; -1 on
+ * error.  (lib.rs:162-182) */
 int npu_runtime_embed(NpuRuntime *rt, const char *model, const char *text, float *out,
                       uintptr_t out_cap);
+/* Re-read the config file and reconcile every GPU.  0 / -1.  (lib.rs:184-192) */
 int npu_runtime_reload(NpuRuntime *rt);
+/* Model statuses as JSON (http.rs:55-66 plus "replicas" and "devices"); free with
+ * npu_string_free.  (lib.rs:194-203) */
 char *npu_runtime_models_json(NpuRuntime *rt);
+/* Stop the workers (their models are freed on their GPUs) and free the handle.  (lib.rs:205-214) */
 void npu_runtime_stop(NpuRuntime *rt);
 
 #ifdef __cplusplus

@@ -50,7 +50,15 @@ int main(void) {
     printf("kind_null=%s\n", npu_last_error());
     if (npu_embed(NULL, "x", NULL, 0) != -1) return 5;
     if (npu_transcribe(NULL, NULL, 0, 16000) != NULL) return 6;
-    if (npu_runtime_start("cfg.toml") != NULL) return 7;
+    NpuRuntime *rt = npu_runtime_start("/nonexistent/engine.toml");   /* missing: empty config */
+    if (rt == NULL) return 7;
+    char *js = npu_runtime_models_json(rt);
+    if (js == NULL) return 8;
+    printf("models=%s\n", js);
+    npu_string_free(js);
+    if (npu_runtime_embed(rt, NULL, "x", NULL, 0) != -1) return 9;
+    printf("rt_embed=%s\n", npu_last_error());
+    npu_runtime_stop(rt);
     npu_string_free(NULL);
     npu_model_free(NULL);
     npu_runtime_stop(NULL);
@@ -73,6 +81,8 @@ def test_c_program_links_and_reports_errors(lib, tmp_path):
     assert "null_path=scenario_path is null" in out.stdout
     assert "missing=load failed: scenario /nonexistent/scenario.toml" in out.stdout
     assert "kind_null=model is null" in out.stdout
+    assert 'models={"object":"list","data":[]}' in out.stdout
+    assert "rt_embed=unsupported: no embed model loaded" in out.stdout
 
 
 def test_scenario_errors(lib, tmp_path):

@@ -9,8 +9,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libxdna_b200.so")
-SOURCES = ["decode_kernel.cu", "gemv_op.cu", "engine.cu", "noalloc.cu", "capi.cu", "ops.cu", "weights.cu", "asr.cu", "logmel.cu", "ffn_fused.cu", "attention_tc.cu", "gemm_tc.cu", "encoders.cu", "parakeet.cu", "whisper_dec.cu", "gemma.cu"]
-HEADERS = ["decode.h", "gemv_op.h", "ptx.cuh", "tc.cuh", "gelu.cuh", "json.h"]
+SOURCES = ["decode_kernel.cu", "gemv_op.cu", "engine.cu", "noalloc.cu", "capi.cu", "runtime.cu", "ops.cu", "weights.cu", "asr.cu", "logmel.cu", "ffn_fused.cu", "attention_tc.cu", "gemm_tc.cu", "encoders.cu", "parakeet.cu", "whisper_dec.cu", "gemma.cu"]
+HEADERS = ["decode.h", "gemv_op.h", "ptx.cuh", "tc.cuh", "gelu.cuh", "json.h", "toml.h", "capi_internal.h"]
 
 
 def nvcc():

@@ -19,9 +19,10 @@
 //   longest-match-first WordPiece with "##" continuations (max 100 characters per word, else
 //   [UNK]); [CLS] ... [SEP]; truncated to model.max_seq.  Lower-casing and accent stripping
 //   cover ASCII and Latin-1; other code points pass through unchanged.
-// * The encoder and head run on the GPU (xdna_bert_*).  ASR scenarios are rejected at load:
-//   the Whisper kernels are reachable through xdna_whisper_* but no ASR front end (log-mel,
-//   tokenizer decode) is wired behind npu_transcribe.
+// * The encoder and head run on the GPU (xdna_bert_*).  ASR scenarios whose name contains
+//   "whisper" run the Whisper pipeline of asr.cu behind npu_transcribe.
+// * The control plane (npu_runtime_*) lives in runtime.cu and loads models through
+//   npu_model_load_on, one replica per GPU.
 #include <cuda_runtime.h>
 
 #include <sys/stat.h>
@@ -43,6 +44,8 @@
 
 #include "../../include/npu_engine.h"
 #include "../../include/xdna_b200.h"
+#include "capi_internal.h"
+#include "toml.h"
 
 namespace xdna {
 void read_npy_f32(const std::string &path, std::vector<size_t> &shape, std::vector<float> &data);   // weights.cu
@@ -50,6 +53,7 @@ void read_npy_f32(const std::string &path, std::vector<size_t> &shape, std::vect
 
 namespace {
 
+using xdna::Toml;
 thread_local std::string g_npu_err;
 void npu_set_err(const std::string &m) { g_npu_err = m; }
 
@@ -95,84 +99,6 @@ void utf8_append(std::string &o, uint32_t cp) {
         o += (char)(0x80 | ((cp >> 6) & 0x3f)); o += (char)(0x80 | (cp & 0x3f));
     }
 }
-
-// ------------------------------------------------------------------------ TOML subset
-struct Toml {
-    std::map<std::string, std::string> kv;   // "table.key" -> value (strings unquoted)
-    std::map<std::string, bool> is_str;
-
-    static std::string trim(const std::string &s) {
-        size_t a = s.find_first_not_of(" \t\r"), b = s.find_last_not_of(" \t\r");
-        return a == std::string::npos ? "" : s.substr(a, b - a + 1);
-    }
-    // parse; returns "" or an error message
-    std::string parse(const std::string &text) {
-        std::istringstream in(text);
-        std::string line, table;
-        int ln = 0;
-        while (std::getline(in, line)) {
-            ln++;
-            // strip a comment that is not inside a string
-            bool q = false;
-            for (size_t i = 0; i < line.size(); i++) {
-                if (line[i] == '"' && (i == 0 || line[i - 1] != '\\')) q = !q;
-                if (line[i] == '#' && !q) { line.resize(i); break; }
-            }
-            line = trim(line);
-            if (line.empty()) continue;
-            if (line[0] == '[') {
-                if (line.back() != ']' || line.size() < 3 || line[1] == '[')
-                    return "line " + std::to_string(ln) + ": unsupported table header";
-                table = trim(line.substr(1, line.size() - 2));
-                continue;
-            }
-            const size_t eq = line.find('=');
-            if (eq == std::string::npos) return "line " + std::to_string(ln) + ": expected key = value";
-            const std::string key = trim(line.substr(0, eq));
-            std::string val = trim(line.substr(eq + 1));
-            const std::string full = table.empty() ? key : table + "." + key;
-            if (!val.empty() && val[0] == '"') {
-                std::string out;
-                size_t i = 1;
-                for (; i < val.size() && val[i] != '"'; i++) {
-                    if (val[i] == '\\' && i + 1 < val.size()) {
-                        const char e = val[++i];
-                        out += e == 'n' ? '\n' : e == 't' ? '\t' : e;
-                    } else {
-                        out += val[i];
-                    }
-                }
-                if (i >= val.size()) return "line " + std::to_string(ln) + ": unterminated string";
-                kv[full] = out;
-                is_str[full] = true;
-            } else {
-                kv[full] = val;
-                is_str[full] = false;
-            }
-        }
-        return "";
-    }
-    bool has(const std::string &k) const { return kv.count(k) != 0; }
-    std::string str(const std::string &k, const std::string &dflt = "") const {
-        auto it = kv.find(k);
-        return it == kv.end() ? dflt : it->second;
-    }
-    long integer(const std::string &k) const {
-        auto it = kv.find(k);
-        if (it == kv.end()) throw std::runtime_error("missing field `" + k.substr(k.find('.') + 1) + "`");
-        char *end = nullptr;
-        const long v = std::strtol(it->second.c_str(), &end, 10);
-        if (is_str.at(k) || !end || *end) throw std::runtime_error("invalid type for `" + k + "`: expected an integer");
-        return v;
-    }
-    bool boolean(const std::string &k, bool dflt) const {
-        auto it = kv.find(k);
-        if (it == kv.end()) return dflt;
-        if (it->second == "true") return true;
-        if (it->second == "false") return false;
-        throw std::runtime_error("invalid type for `" + k + "`: expected a boolean");
-    }
-};
 
 struct ScenarioCfg {
     std::string kind, name;
@@ -441,13 +367,10 @@ struct NpuModel {
         if (dev) xdna_device_close(dev);
     }
 };
-struct NpuRuntime {
-    int unused;
-};
 
 namespace {
 
-NpuModel *load_embed(const ScenarioCfg &c, const std::string &path) {
+NpuModel *load_embed(const ScenarioCfg &c, const std::string &path, int ordinal) {
     if (c.hidden != 768 || c.ff != 3072 || c.n_heads != 12 || c.head_dim != 64)
         throw std::runtime_error(err_unsupported("embedding models with hidden 768, ff 3072, 12 heads of 64 (BERT-base)"));
     if (c.n_layers < 1 || c.max_seq < 1) throw std::runtime_error(err_load("scenario " + path + ": bad model sizes"));
@@ -511,7 +434,7 @@ NpuModel *load_embed(const ScenarioCfg &c, const std::string &path) {
     }
     XdnaBertWeights bw{we.data.data(), pe.data.data(), emb["type_emb"].data.data(), emb["emb_ln_w"].data.data(),
                        emb["emb_ln_b"].data.data(), ly.data()};
-    m->dev = xdna_device_open(0);
+    m->dev = xdna_device_open(ordinal);
     if (!m->dev) throw std::runtime_error(err_device(xdna_last_error()));
     const int max_len = std::min(c.max_seq, bc.max_pos);
     m->cfg.max_seq = max_len;
@@ -522,7 +445,7 @@ NpuModel *load_embed(const ScenarioCfg &c, const std::string &path) {
 
 // ASR scenarios: Whisper-small (hidden 768, 12 heads of 64, ff 3072) from the npy layout of
 // artifacts.weights; the tokenizer is artifacts.tokenizer, else tokenizer.json beside the weights
-NpuModel *load_asr(const ScenarioCfg &c, const std::string &path) {
+NpuModel *load_asr(const ScenarioCfg &c, const std::string &path, int ordinal) {
     if (c.name.find("whisper") == std::string::npos)
         throw std::runtime_error(err_unsupported("ASR model \"" + c.name + "\": only Whisper scenarios are wired "
                                                  "behind npu_transcribe"));
@@ -539,7 +462,7 @@ NpuModel *load_asr(const ScenarioCfg &c, const std::string &path) {
     struct stat st;
     if (c.weights.empty() || stat(wdir.c_str(), &st) != 0 || !S_ISDIR(st.st_mode))
         throw std::runtime_error(err_load("asr weights load " + wdir + ": No such file or directory"));
-    m->dev = xdna_device_open(0);
+    m->dev = xdna_device_open(ordinal);
     if (!m->dev) throw std::runtime_error(err_device(xdna_last_error()));
     try {
         m->asr = xdna::asr_load(m->dev, wdir, tok, c.n_layers);
@@ -552,17 +475,10 @@ NpuModel *load_asr(const ScenarioCfg &c, const std::string &path) {
 
 }  // namespace
 
-extern "C" {
+void npu_set_last_error(const std::string &msg) { npu_set_err(msg); }
 
-int npu_available(void) {
-    try {
-        return xdna_device_count() > 0 ? 1 : 0;
-    } catch (...) {
-        return 0;
-    }
-}
-
-NpuModel *npu_model_load(const char *scenario_path) {
+// npu_model_load on a given CUDA device (the control plane loads one replica per GPU)
+NpuModel *npu_model_load_on(const char *scenario_path, int ordinal) {
     try {
         if (!scenario_path) { npu_set_err("scenario_path is null"); return nullptr; }
         const std::string path(scenario_path);
@@ -575,8 +491,8 @@ NpuModel *npu_model_load(const char *scenario_path) {
             npu_set_err(err_load("scenario " + path + ": " + e.what()));
             return nullptr;
         }
-        if (c.kind == "embeddings") return load_embed(c, path);
-        if (c.kind == "asr") return load_asr(c, path);
+        if (c.kind == "embeddings") return load_embed(c, path, ordinal);
+        if (c.kind == "asr") return load_asr(c, path, ordinal);
         npu_set_err(err_load("unknown scenario kind \"" + c.kind + "\""));
         return nullptr;
     } catch (const std::exception &e) {
@@ -587,6 +503,18 @@ NpuModel *npu_model_load(const char *scenario_path) {
         return nullptr;
     }
 }
+
+extern "C" {
+
+int npu_available(void) {
+    try {
+        return xdna_device_count() > 0 ? 1 : 0;
+    } catch (...) {
+        return 0;
+    }
+}
+
+NpuModel *npu_model_load(const char *scenario_path) { return npu_model_load_on(scenario_path, 0); }
 
 int npu_model_kind(const NpuModel *m) {
     if (!m) { npu_set_err("model is null"); return -1; }
@@ -664,29 +592,6 @@ void npu_model_free(NpuModel *m) {
 }
 
 const char *npu_last_error(void) { return g_npu_err.c_str(); }
-
-static const char *kNoRuntime = "unsupported: the control plane (npu-runtime) is not part of the B200 backend";
-NpuRuntime *npu_runtime_start(const char *config_path) {
-    npu_set_err(config_path ? kNoRuntime : "config_path is null");
-    return nullptr;
-}
-char *npu_runtime_transcribe(NpuRuntime *rt, const char *, const int16_t *, uintptr_t, uint32_t) {
-    npu_set_err(rt ? kNoRuntime : "runtime is null");
-    return nullptr;
-}
-int npu_runtime_embed(NpuRuntime *rt, const char *, const char *, float *, uintptr_t) {
-    npu_set_err(rt ? kNoRuntime : "runtime is null");
-    return -1;
-}
-int npu_runtime_reload(NpuRuntime *rt) {
-    npu_set_err(rt ? kNoRuntime : "runtime is null");
-    return -1;
-}
-char *npu_runtime_models_json(NpuRuntime *rt) {
-    npu_set_err(rt ? kNoRuntime : "runtime is null");
-    return nullptr;
-}
-void npu_runtime_stop(NpuRuntime *) {}
 
 // WordPiece front end on its own (host only): the ids npu_embed feeds the encoder for `text`.
 int xdna_wordpiece_encode(const char *tokenizer_path, const char *text, int max_len, int32_t *ids, int cap) {
