@@ -1004,6 +1004,7 @@ def run_case(args):
       parakeet:B            two Parakeet encoder forwards of B clips (eager, then the graph)
       whisper_dec:B         two Whisper-small decoder runs of B streams x 4 tokens
       decode:N              one opt-125m generation of N tokens after a 32-token prompt
+      prefill:N             three batched prefills of N opt-125m prompt positions (prints the last's time)
       gemma:B,ctx           one Gemma-3-1B generate (B streams, ctx-token prompts, + 4 tokens)
       (a bare "B,ctx" is the gemma case)"""
     import torch
@@ -1091,6 +1092,20 @@ def run_case(args):
         from xdna_engine_b200.synth import OPT_125M, make_opt_weights, make_prompt
         dec = X.OptDecoder(X.Device(0), OPT_125M, make_opt_weights(OPT_125M, seed=0), max_ctx=32 + N + 1)
         print(dec.generate(make_prompt(OPT_125M, 32, seed=0), N)[:8], flush=True)
+    elif name == "prefill":
+        N, = vals
+        from xdna_engine_b200.synth import OPT_125M, make_opt_weights, make_prompt
+        dec = X.OptDecoder(X.Device(0), OPT_125M, make_opt_weights(OPT_125M, seed=0), max_ctx=N + 1)
+        prompt = make_prompt(OPT_125M, N, seed=0)
+        dec.set_tokens(prompt, 0, sp)
+        for _ in range(3):
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record(st)
+            dec.prefill(0, N, sp)
+            b.record(st)
+            torch.cuda.synchronize()
+        dec.sync(sp)
+        print(f"prefill of {N} positions: {a.elapsed_time(b):.3f} ms", flush=True)
     else:
         raise SystemExit(f"unknown case {name!r}")
     torch.cuda.synchronize()

@@ -269,6 +269,15 @@ int xdna_opt_set_tokens(XdnaOptDecoder *dec, const int64_t *host, size_t off, si
 int xdna_opt_get_tokens(XdnaOptDecoder *dec, int64_t *host, size_t off, size_t n, void *stream);
 int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_prompt,
                     float *logits_dev, void *stream);
+/* Prompt prefill as a batch (replaces stepping the prompt through Opt::step,
+ * rust/npu-whisper/src/bin/opt125m_decode.rs:296-315): writes the K / V rows of positions
+ * start_pos .. start_pos + n - 1 for tokens[] already on the device, up to 32 positions per
+ * launch sequence, with exactly the decode kernel's arithmetic (the cache, and every later
+ * token, are bit-identical to launching those positions).  No LM head: follow with
+ * xdna_opt_launch from start_pos + n.  Asynchronous on `stream`; bad token ids are reported by
+ * xdna_opt_sync.  xdna_opt_generate uses it for all prompt positions but the last.  Returns 0,
+ * or -1 (also when the decoder was created with XDNA_OPT_PREFILL=0). */
+int xdna_opt_prefill(XdnaOptDecoder *dec, int start_pos, int n, void *stream);
 /* Wait for the decoder's launches on `stream` and report a device-side failure (bounded
  * waits that expired).  Returns 0, or -1 with xdna_last_error() set. */
 int xdna_opt_sync(XdnaOptDecoder *dec, void *stream);

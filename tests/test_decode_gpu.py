@@ -99,6 +99,49 @@ def test_decode_prompt_of_one_and_long_context(X, dev, n_prompt, n_new, grid):
     np.testing.assert_array_equal(lg, olg)
 
 
+@pytest.mark.parametrize("n_prompt", [2, 33, 97])
+def test_batched_prefill_equals_stepping(X, dev, monkeypatch, n_prompt):
+    """The batched prompt prefill (xdna_opt_prefill, used by generate for all prompt positions but
+    the last) leaves the cache exactly as stepping every prompt position through the decode
+    kernel: tokens and logits of the two decoders are identical bit for bit (33 and 97 positions
+    take two and four launch sequences of at most 32, and cross a 64-position page)."""
+    w = make_opt_weights(SMALL, seed=6, std=0.2, bias_std=0.05, ln_std=0.1)
+    prompt = make_prompt(SMALL, n_prompt, seed=6)
+    n_new = 24
+    dec = X.OptDecoder(dev, SMALL, w, max_ctx=n_prompt + n_new)
+    ids, lg = dec.generate(prompt, n_new, want_logits=True)
+    # the public entry, then the decode kernel from the last prompt position
+    dec.set_tokens(prompt)
+    dec.prefill(0, n_prompt - 1)
+    dec.launch(n_prompt - 1, n_new, n_prompt)
+    dec.sync()
+    out = np.empty(n_new, np.int64)
+    dec.get_tokens(out, n_prompt)
+    dec.sync()
+    dec.close()
+    np.testing.assert_array_equal(out, ids)
+    monkeypatch.setenv("XDNA_OPT_PREFILL", "0")
+    ref = X.OptDecoder(dev, SMALL, w, max_ctx=n_prompt + n_new)
+    rids, rlg = ref.generate(prompt, n_new, want_logits=True)
+    with pytest.raises(X.XdnaError):
+        ref.prefill(0, 1)                                   # not built for this decoder
+    ref.close()
+    np.testing.assert_array_equal(ids, rids)
+    np.testing.assert_array_equal(lg, rlg)
+
+
+def test_prefill_reports_bad_token(X, dev):
+    w = make_opt_weights(SMALL, seed=6, std=0.2)
+    dec = X.OptDecoder(dev, SMALL, w, max_ctx=16)
+    dec.set_tokens(np.array([5, SMALL.vocab + 3, 7], np.int64))
+    dec.prefill(0, 2)
+    with pytest.raises(X.XdnaError, match="token id out of range"):
+        dec.sync()
+    with pytest.raises(X.XdnaError):
+        dec.prefill(10, 7)                                  # beyond max_ctx
+    dec.close()
+
+
 def test_launch_split_equals_single_launch(X, dev):
     """Per-token launches on device-resident tokens give the same stream as one launch."""
     w = make_opt_weights(SMALL, seed=5, std=0.2)

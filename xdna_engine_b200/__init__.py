@@ -152,6 +152,8 @@ def lib():
         L.xdna_opt_launch.argtypes = [vp, i, i, i, vp, vp]
         L.xdna_opt_launch.restype = i
         L.xdna_opt_sync.argtypes = [vp, vp]
+        L.xdna_opt_prefill.argtypes = [vp, i, i, vp]
+        L.xdna_opt_prefill.restype = i
         L.xdna_opt_sync.restype = i
         L.xdna_opt_stream_bytes_per_token.argtypes = [vp]
         L.xdna_opt_stream_bytes_per_token.restype = sz
@@ -413,6 +415,10 @@ class OptDecoder:
                stream: int = 0):
         _check(lib().xdna_opt_launch(self.handle, start_pos, n_steps, n_prompt,
                                      logits_ptr or None, stream or None))
+
+    def prefill(self, start_pos: int, n: int, stream: int = 0):
+        """K / V rows of prompt positions [start_pos, start_pos + n) as a batch (no LM head)."""
+        _check(lib().xdna_opt_prefill(self.handle, start_pos, n, stream or None))
 
     def set_timing(self, timing_ptr: int):
         _check(lib().xdna_opt_set_timing(self.handle, timing_ptr or None))

@@ -130,4 +130,31 @@ struct DecodeParams {
     unsigned long long *timing; // optional [2][grid][128] globaltimer / clock stamps (first 2 steps)
 };
 
+// ---------------------------------------------------------------- batched prompt prefill
+constexpr int kPrefillTokens = 32;                // positions per prefill launch sequence
+enum { PF_QKV = 0, PF_FC1 = 1, PF_RESID = 2 };
+
+struct PrefillGemv {
+    const int8_t *w;            // [N][K] row-major int8
+    const float *sc, *bi;       // [N] row scale, bias
+    const int8_t *limbs;        // [T][4][K] input limbs (fixed point 2^fix)
+    int T, K, N, fix, mode;
+    // PF_QKV: q out [T][D] (bf16 values of y / 8), K / V rows into the paged cache
+    float *q;
+    uint16_t *kv;
+    const int *pt;
+    int layer, n_phys, n_heads, pos0, D;
+    // PF_FC1: limbs of bf16(relu(y)) at 2^fix_out into [T][4][N]
+    int8_t *limbs_out;
+    int fix_out;
+    // PF_RESID: x[t][n] += y
+    float *x;
+    // K split: nsplit CTAs per 16-row tile add exact partials into acc[t][n] (int64, zero
+    // between uses); the last of a tile's CTAs to finish (cnt[tile]) applies the epilogue and
+    // clears its words and counter
+    int nsplit;
+    unsigned long long *acc;
+    unsigned int *cnt;
+};
+
 }  // namespace xdna

@@ -34,6 +34,7 @@
 #include <cuda_bf16.h>
 #include <cstdint>
 #include <cmath>
+#include <algorithm>
 
 #include "decode.h"
 #include "ptx.cuh"
@@ -1112,6 +1113,333 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) opt_dec
         if (S.tid == 0) *(volatile int *)S.flag = 1;
     }
     cluster_sync_all();                      // neither CTA leaves while its pair may write into it
+}
+
+
+// ------------------------------------------------------------------------------ prefill
+// The prompt's positions before the last one need no LM head, only their K / V rows, and their
+// layers do not depend on one another within a layer's linear maps: so they run as a batch of
+// up to kPrefillTokens positions per launch sequence instead of one decode step each
+// (rust/npu-whisper/src/bin/opt125m_decode.rs:296-315 steps the prompt one token at a time).
+// Every number is the decode kernel's: the same LayerNorm reduction order, the same fixed-point
+// inputs and exact integer dots (the int8 MMA over the four limbs, combined in 64 bits), the same
+// epilogue roundings, the same partial-score chains, softmax sums and P.V chains; so the K / V
+// rows written here, and every later token, are bit-identical to a run that steps the prompt.
+__global__ void prefill_embed_kernel(const int64_t *tokens, int pos0, int D, int V, const float *emb_tok,
+                                     const float *emb_pos, float *x, RunState *state) {
+    const int t = blockIdx.x, pos = pos0 + t;
+    int64_t id = tokens[pos];
+    if (id < 0 || id >= V) {                       // reported like the decode kernel; row 0 stands in
+        if (threadIdx.x == 0) set_error_st(state, ERR_BAD_TOKEN, pos);
+        id = 0;
+    }
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+        x[(size_t)t * D + i] = __fadd_rn(emb_tok[(size_t)id * D + i], emb_pos[(size_t)(pos + 2) * D + i]);
+}
+
+// limbs of rint(x * sc) (put_limbs4's rule) into [4][K] rows at column k
+__device__ __forceinline__ void put_limbs_rows(int8_t *L, int K, int k, float x, float sc) {
+    float v = __fmul_rn(x, sc);
+    v = fminf(fmaxf(v, -1073741760.0f), 1073741760.0f);
+    const int X = __float2int_rn(v);
+    const int d = ((X + 128) & 255) - 128;
+    const int X1 = (X - d) >> 8;
+    const int c = ((X1 + 128) & 255) - 128;
+    const int X2 = (X1 - c) >> 8;
+    const int b = ((X2 + 128) & 255) - 128;
+    const int a = (X2 - b) >> 8;
+    L[k] = (int8_t)a;
+    L[K + k] = (int8_t)b;
+    L[2 * K + k] = (int8_t)c;
+    L[3 * K + k] = (int8_t)d;
+}
+
+// ln_limbs for one position per CTA (256 threads): same per-lane sums, butterfly, warp order
+template <int D>
+__global__ void __launch_bounds__(256) prefill_ln_kernel(const float *x, const float *g, const float *b, float eps,
+                                                         int fix, int8_t *limbs) {
+    constexpr int KBW = D / 32 / kConsumerWarps;
+    __shared__ float red[16];
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, kb0 = warp * KBW;
+    const float *xr = x + (size_t)t * D;
+    float v[KBW];
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < KBW; kk++) {
+        v[kk] = xr[32 * (kb0 + kk) + lane];
+        s1 = __fadd_rn(s1, v[kk]);
+        s2 = __fadd_rn(s2, __fmul_rn(v[kk], v[kk]));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        s1 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, o));
+        s2 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, o));
+    }
+    if (lane == 0) { red[warp] = s1; red[8 + warp] = s2; }
+    __syncthreads();
+    s1 = 0.0f;
+    s2 = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) {
+        s1 = __fadd_rn(s1, red[w]);
+        s2 = __fadd_rn(s2, red[8 + w]);
+    }
+    const float mean = __fdiv_rn(s1, (float)D);
+    const float var = fmaxf(__fsub_rn(__fdiv_rn(s2, (float)D), __fmul_rn(mean, mean)), 0.0f);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    const float sc = exp2i(fix);
+    int8_t *L = limbs + (size_t)t * 4 * D;
+#pragma unroll
+    for (int kk = 0; kk < KBW; kk++) {
+        const int i = 32 * (kb0 + kk) + lane;
+        const float tt = __fmul_rn(__fsub_rn(v[kk], mean), inv);
+        put_limbs_rows(L, D, i, bf16r(__fadd_rn(__fmul_rn(tt, g[i]), b[i])), sc);
+    }
+}
+
+// One CTA per (16-row tile, K slice), its 8 warps splitting the slice again, all positions at
+// once.  The slice's input limbs of every position are staged in shared memory first (rows padded
+// by 16 bytes, so a fragment load hits 32 distinct banks) and each warp holds its weight
+// fragments in registers before the MMAs, so no load waits inside the MMA chain.  B columns =
+// (position pair, limb): one m16n8k32 covers two positions' four limbs; limb sums are exact in
+// 32 bits (|sum| <= K * 128 * 127 < 2^31 for K <= 3072) and combine exactly in 64 bits.  The
+// warps' partials are added in shared memory, the slices' in 64-bit integer atomics (any order
+// gives the same sum); the tile's last slice applies the epilogue.
+constexpr int kPfWarps = 8;
+constexpr int kPfMaxKbWarp = 4;                   // k-blocks per warp at most
+
+__global__ void __launch_bounds__(kPfWarps * 32) prefill_gemv_kernel(const PrefillGemv a) {
+    constexpr int NCG = kPrefillTokens / 2;
+    extern __shared__ __align__(16) uint8_t pf_smem[];
+    __shared__ unsigned last_s;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    const int tile = blockIdx.x, n0 = tile * kTile;
+    const int nkb = a.K / 32;
+    const int kbA = blockIdx.y * nkb / a.nsplit, kbB = (blockIdx.y + 1) * nkb / a.nsplit;
+    const int ks = (kbB - kbA) * 32, stride = ks + 16;
+    // this warp's k-blocks and their weight fragments (requested before the staging wait)
+    const int w0k = kbA + warp * (kbB - kbA) / kPfWarps, w1k = kbA + (warp + 1) * (kbB - kbA) / kPfWarps;
+    const int nk = w1k - w0k;
+    uint32_t af[kPfMaxKbWarp][4];
+    {
+        const int8_t *r0 = a.w + (size_t)(n0 + g) * a.K + tig * 4, *r1 = r0 + (size_t)8 * a.K;
+#pragma unroll
+        for (int i = 0; i < kPfMaxKbWarp; i++)
+            if (i < nk) {
+                const int kb = w0k + i;
+                af[i][0] = __ldg(reinterpret_cast<const unsigned int *>(r0 + kb * 32));
+                af[i][1] = __ldg(reinterpret_cast<const unsigned int *>(r1 + kb * 32));
+                af[i][2] = __ldg(reinterpret_cast<const unsigned int *>(r0 + kb * 32 + 16));
+                af[i][3] = __ldg(reinterpret_cast<const unsigned int *>(r1 + kb * 32 + 16));
+            }
+    }
+    // stage limbs [position][limb][slice] (positions >= T as zeros)
+    {
+        const int vec = ks / 16, rows = kPrefillTokens * 4;
+        for (int i = threadIdx.x; i < rows * vec; i += kPfWarps * 32) {
+            const int row = i / vec, c = i - row * vec, t = row >> 2;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (t < a.T)
+                v = __ldg(reinterpret_cast<const uint4 *>(a.limbs + (size_t)row * a.K + (size_t)kbA * 32) + c);
+            *reinterpret_cast<uint4 *>(pf_smem + (size_t)row * stride + c * 16) = v;
+        }
+    }
+    __syncthreads();
+    int acc[NCG][4];
+#pragma unroll
+    for (int i = 0; i < NCG; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0;
+    // column g of a pair tile: position 2 cg + (g >> 2), limb g & 3 -> staged row 8 cg + g
+#pragma unroll
+    for (int i = 0; i < kPfMaxKbWarp; i++) {
+        if (i >= nk) break;
+        const uint8_t *bb = pf_smem + (size_t)g * stride + (w0k + i - kbA) * 32 + tig * 4;
+#pragma unroll
+        for (int cg = 0; cg < NCG; cg++) {
+            const uint8_t *r = bb + (size_t)(8 * cg) * stride;
+            const uint32_t b0 = *reinterpret_cast<const uint32_t *>(r);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t *>(r + 16);
+            mma_s8_16832(acc[cg], af[i][0], af[i][1], af[i][2], af[i][3], b0, b1);
+        }
+    }
+    __syncthreads();                        // the staged limbs are dead: their space holds partials
+    long long(*part)[kPrefillTokens][kTile] = reinterpret_cast<long long(*)[kPrefillTokens][kTile]>(pf_smem);
+    // lanes with even tig hold rows g, g + 8 of position 2 cg + tig / 2
+    const bool owner = (tig & 1) == 0;
+#pragma unroll
+    for (int cg = 0; cg < NCG; cg++) {
+        const int x0 = __shfl_down_sync(0xffffffffu, acc[cg][0], 1);
+        const int x1 = __shfl_down_sync(0xffffffffu, acc[cg][1], 1);
+        const int x2 = __shfl_down_sync(0xffffffffu, acc[cg][2], 1);
+        const int x3 = __shfl_down_sync(0xffffffffu, acc[cg][3], 1);
+        const int t = 2 * cg + (tig >> 1);
+        if (owner) {
+            part[warp][t][g] = ((long long)acc[cg][0] << 24) + ((long long)acc[cg][1] << 16) + ((long long)x0 << 8) + x1;
+            part[warp][t][g + 8] =
+                ((long long)acc[cg][2] << 24) + ((long long)acc[cg][3] << 16) + ((long long)x2 << 8) + x3;
+        }
+    }
+    __syncthreads();
+    // thread i of the CTA: items (position, row) i, i + 256, ...
+    const int items = a.T * kTile;
+    auto warp_total = [&](int t, int r) {
+        long long y = 0;
+#pragma unroll
+        for (int w = 0; w < kPfWarps; w++) y += part[w][t][r];
+        return y;
+    };
+    if (a.nsplit > 1) {
+        for (int i = threadIdx.x; i < items; i += kPfWarps * 32) {
+            const int t = i / kTile, r = i % kTile;
+            atomicAdd(a.acc + (size_t)t * a.N + n0 + r, (unsigned long long)warp_total(t, r));
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) last_s = atomicAdd(a.cnt + tile, 1u) == (unsigned)(a.nsplit - 1);
+        __syncthreads();
+        if (!last_s) return;
+        __threadfence();
+    }
+    const float inv = exp2i(-a.fix);
+    for (int i = threadIdx.x; i < items; i += kPfWarps * 32) {
+        const int t = i / kTile, r = i % kTile, n = n0 + r;
+        const long long Y = a.nsplit > 1 ? (long long)atomicExch(a.acc + (size_t)t * a.N + n, 0ull) : warp_total(t, r);
+        const float y = __fadd_rn(__fmul_rn(__fmul_rn(__ll2float_rn(Y), inv), a.sc[n]), a.bi[n]);
+        if (a.mode == PF_QKV) {
+            const int part_i = n / a.D, rr = n - part_i * a.D;
+            const int pos = a.pos0 + t;
+            if (part_i == 0) {
+                a.q[(size_t)t * a.D + rr] = bf16r(__fmul_rn(y, 0.125f));
+            } else {
+                const int head = rr / kHeadDim, half = (rr % kHeadDim) / kHalfDim, k = rr % kHalfDim;
+                const size_t idx =
+                    (((((size_t)a.layer * a.n_phys + a.pt[pos / kPageTokens]) * a.n_heads + head) * 2 + half) * 2 +
+                     (part_i - 1)) * (size_t)(kPageTokens * kHalfDim) + (size_t)(pos % kPageTokens) * kHalfDim + k;
+                a.kv[idx] = (uint16_t)bf16bits(y);
+            }
+        } else if (a.mode == PF_FC1) {
+            put_limbs_rows(a.limbs_out + (size_t)t * 4 * a.N, a.N, n, bf16r(fmaxf(y, 0.0f)), exp2i(a.fix_out));
+        } else {
+            float *xr = a.x + (size_t)t * a.N + n;
+            *xr = __fadd_rn(*xr, y);
+        }
+    }
+    if (a.nsplit > 1 && threadIdx.x == 0) a.cnt[tile] = 0u;
+}
+
+// partial score over 32 dims of an unswizzled cache row: part_score's four fma chains
+__device__ __forceinline__ float part_score_row(const float *qf, const uint16_t *krow) {
+    const uint4 *kr = reinterpret_cast<const uint4 *>(krow);
+    float c[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint4 w = kr[i];
+        const float *qq = qf + 8 * i;
+        float a = 0.0f;
+        a = fmaf(qq[0], bf16lo(w.x), a);
+        a = fmaf(qq[1], bf16hi(w.x), a);
+        a = fmaf(qq[2], bf16lo(w.y), a);
+        a = fmaf(qq[3], bf16hi(w.y), a);
+        a = fmaf(qq[4], bf16lo(w.z), a);
+        a = fmaf(qq[5], bf16hi(w.z), a);
+        a = fmaf(qq[6], bf16lo(w.w), a);
+        a = fmaf(qq[7], bf16hi(w.w), a);
+        c[i] = a;
+    }
+    return __fadd_rn(__fadd_rn(c[0], c[1]), __fadd_rn(c[2], c[3]));
+}
+
+// attention() for one (position, head) per CTA of 256 threads, both halves of the head:
+// s_j = part_0 + part_1, the max, fast_exp, the per-thread / butterfly / warp-order sum,
+// P.V chains over keys j = g mod 8 per half, ctx limbs at 2^fix
+__global__ void __launch_bounds__(256) prefill_attn_kernel(const float *q, const uint16_t *kv, const int *pt,
+                                                           int layer, int n_phys, int n_heads, int pos0, int D,
+                                                           int fix, int8_t *limbs) {
+    __shared__ float sp[kMaxCtx];
+    __shared__ __align__(16) float qf[kHeadDim];
+    __shared__ float red[16], accg[8 * kHalfDim];
+    const int t = blockIdx.x, head = blockIdx.y, pos = pos0 + t, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    if (tid < kHeadDim) qf[tid] = q[(size_t)t * D + head * kHeadDim + tid];
+    __syncthreads();
+    auto row = [&](int j, int half, int kvsel) {
+        return kv + (((((size_t)layer * n_phys + pt[j / kPageTokens]) * n_heads + head) * 2 + half) * 2 + kvsel) *
+                        (size_t)(kPageTokens * kHalfDim) +
+               (size_t)(j % kPageTokens) * kHalfDim;
+    };
+    float m = -INFINITY;
+    for (int j = tid; j <= pos; j += 256) {
+        const float s = __fadd_rn(part_score_row(qf, row(j, 0, 0)), part_score_row(qf + kHalfDim, row(j, 1, 0)));
+        sp[j] = s;
+        m = fmaxf(m, s);
+    }
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) m = fmaxf(m, red[w]);
+    float l = 0.0f;
+    for (int j = tid; j <= pos; j += 256) {
+        const float pj = fast_exp_nonpos(__fsub_rn(sp[j], m));
+        sp[j] = pj;
+        l = __fadd_rn(l, pj);
+    }
+    l = warp_sum(l);
+    __syncthreads();                       // every red[] max read before the sums overwrite
+    if (lane == 0) red[8 + warp] = l;
+    __syncthreads();
+    l = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) l = __fadd_rn(l, red[8 + w]);
+    const int d = tid & 31, g = tid >> 5;
+    int8_t *L = limbs + (size_t)t * 4 * D;
+    for (int half = 0; half < 2; half++) {
+        float a = 0.0f;
+        for (int j = g; j <= pos; j += 8) {
+            const uint16_t vv = row(j, half, 1)[d];
+            a = fmaf(sp[j], __uint_as_float((uint32_t)vv << 16), a);
+        }
+        accg[g * 32 + d] = a;
+        __syncthreads();
+        if (tid < kHalfDim) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int gg = 0; gg < 8; gg++) tot = __fadd_rn(tot, accg[gg * 32 + tid]);
+            put_limbs_rows(L, D, head * kHeadDim + half * kHalfDim + tid, bf16r(__fdiv_rn(tot, l)), exp2i(fix));
+        }
+        __syncthreads();
+    }
+}
+
+cudaError_t launch_prefill_embed(const int64_t *tokens, int pos0, int T, int D, int V, const float *emb_tok,
+                                 const float *emb_pos, float *x, RunState *state, cudaStream_t st) {
+    prefill_embed_kernel<<<T, 256, 0, st>>>(tokens, pos0, D, V, emb_tok, emb_pos, x, state);
+    return cudaGetLastError();
+}
+cudaError_t launch_prefill_ln(const float *x, int T, int D, const float *g, const float *b, float eps, int fix,
+                              int8_t *limbs, cudaStream_t st) {
+    if (D == 768) prefill_ln_kernel<768><<<T, 256, 0, st>>>(x, g, b, eps, fix, limbs);
+    else if (D == 256) prefill_ln_kernel<256><<<T, 256, 0, st>>>(x, g, b, eps, fix, limbs);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+cudaError_t launch_prefill_gemv(const PrefillGemv &a, cudaStream_t st) {
+    const int nkb = a.K / 32;
+    if (a.T < 1 || a.T > kPrefillTokens || a.K % 32 || a.N % kTile || a.nsplit < 1 || a.nsplit > nkb ||
+        (nkb + a.nsplit - 1) / a.nsplit > kPfWarps * kPfMaxKbWarp)
+        return cudaErrorInvalidValue;
+    // the largest slice's staged limbs, or the warps' partials, whichever is larger
+    const int ks = (nkb + a.nsplit - 1) / a.nsplit * 32;
+    const size_t smem = std::max((size_t)kPrefillTokens * 4 * (ks + 16),
+                                 (size_t)kPfWarps * kPrefillTokens * kTile * sizeof(long long));
+    cudaError_t e = cudaFuncSetAttribute(prefill_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    prefill_gemv_kernel<<<dim3(a.N / kTile, a.nsplit), kPfWarps * 32, smem, st>>>(a);
+    return cudaGetLastError();
+}
+cudaError_t launch_prefill_attn(const float *q, const uint16_t *kv, const int *pt, int layer, int n_phys, int n_heads,
+                                int pos0, int T, int D, int fix, int8_t *limbs, cudaStream_t st) {
+    prefill_attn_kernel<<<dim3(T, n_heads), 256, 0, st>>>(q, kv, pt, layer, n_phys, n_heads, pos0, D, fix, limbs);
+    return cudaGetLastError();
 }
 
 // model widths the decode kernel is compiled for (d_model, ffn)

@@ -26,6 +26,13 @@ int decode_smem_bytes();
 cudaError_t launch_opt_decode(const DecodeParams &p, cudaStream_t st);
 cudaError_t max_coresident_ctas(int d, int f, int *out);
 bool decode_shape_supported(int d, int f);
+cudaError_t launch_prefill_embed(const int64_t *tokens, int pos0, int T, int D, int V, const float *emb_tok,
+                                 const float *emb_pos, float *x, RunState *state, cudaStream_t st);
+cudaError_t launch_prefill_ln(const float *x, int T, int D, const float *g, const float *b, float eps, int fix,
+                              int8_t *limbs, cudaStream_t st);
+cudaError_t launch_prefill_gemv(const PrefillGemv &a, cudaStream_t st);
+cudaError_t launch_prefill_attn(const float *q, const uint16_t *kv, const int *pt, int layer, int n_phys, int n_heads,
+                                int pos0, int T, int D, int fix, int8_t *limbs, cudaStream_t st);
 }  // namespace xdna
 
 using namespace xdna;
@@ -277,9 +284,21 @@ struct XdnaOptDecoder {
     float *trace = nullptr;         // optional residual-stream record (xdna_opt_set_trace)
     unsigned long long *timing = nullptr;  // optional phase stamps (xdna_opt_set_timing)
     size_t logits_cap = 0;
+    // batched prompt prefill: row-major int8 weights per layer (q|k|v, o, fc1, fc2), the q|k|v
+    // and fc1 row scale / bias, scratch for kPrefillTokens positions
+    bool prefill = false;
+    std::vector<int> h_fix;                // [4][L] as d_fix
+    int8_t *d_pfw = nullptr;
+    float *d_pfsb = nullptr;
+    size_t pf_w_layer = 0, pf_sb_layer = 0;
+    float *d_pfx = nullptr, *d_pfq = nullptr;
+    int8_t *d_pfa = nullptr, *d_pfh = nullptr;
+    unsigned long long *d_pfacc = nullptr;  // [kPrefillTokens][max(3D, F)] K-split sums (zero between uses)
+    unsigned int *d_pfcnt = nullptr;        // per 16-row tile: K-slice CTAs finished
     ~XdnaOptDecoder() {
         void *ptrs[] = {d_stream, d_chunks, d_nl, d_nlm, d_emb, d_pos, d_ln, d_lnf, d_osb, d_f2sb, d_fix,
-                        d_kv, d_pt, d_acc, d_ll, d_tokens, d_state, d_logits};
+                        d_kv, d_pt, d_acc, d_ll, d_tokens, d_state, d_logits, d_pfw, d_pfsb, d_pfx, d_pfq,
+                        d_pfa, d_pfh, d_pfacc, d_pfcnt};
         for (void *p : ptrs)
             if (p) cudaFree(p);
     }
@@ -557,6 +576,54 @@ XdnaOptDecoder *xdna_opt_create(XdnaDevice *dev, const XdnaOptConfig *cfg, const
         dec->fix_lnf = fix_from_bound(ln_bound(w->lnf_w, w->lnf_b, D));
         dec->d_fix = dmalloc<int>(4 * L);
         ck(cudaMemcpy(dec->d_fix, fix.data(), 4 * L * sizeof(int), cudaMemcpyHostToDevice), "upload exponents");
+        dec->h_fix = fix;
+
+        // batched prompt prefill (XDNA_OPT_PREFILL=0 steps the prompt through the decode kernel)
+        {
+            const char *pf = std::getenv("XDNA_OPT_PREFILL");
+            dec->prefill = !(pf && pf[0] == '0');
+        }
+        if (dec->prefill) {
+            dec->pf_w_layer = (size_t)3 * D * D + (size_t)D * D + 2 * (size_t)F * D;
+            dec->pf_sb_layer = (size_t)2 * 3 * D + 2 * (size_t)F;
+            std::vector<int8_t> wl(dec->pf_w_layer);
+            std::vector<float> sbl(dec->pf_sb_layer);
+            dec->d_pfw = dmalloc<int8_t>(dec->pf_w_layer * L);
+            dec->d_pfsb = dmalloc<float>(dec->pf_sb_layer * L);
+            for (int l = 0; l < L; l++) {
+                int8_t *o8 = wl.data();
+                const QMat *qkv3[3] = {&q[l], &k[l], &v[l]};
+                for (const QMat *m : qkv3) { std::copy(m->q.begin(), m->q.end(), o8); o8 += m->q.size(); }
+                std::copy(o[l].q.begin(), o[l].q.end(), o8); o8 += o[l].q.size();
+                std::copy(f1[l].q.begin(), f1[l].q.end(), o8); o8 += f1[l].q.size();
+                std::copy(f2[l].q.begin(), f2[l].q.end(), o8);
+                float *sb = sbl.data();                // qkv scale [3D], qkv bias [3D], fc1 scale [F], bias [F]
+                for (int i = 0; i < 3; i++)
+                    for (int n = 0; n < D; n++) {
+                        const RowRef r = row_of(*qkv3[i], n);
+                        sb[i * D + n] = r.scale;
+                        sb[3 * D + i * D + n] = r.bias;
+                    }
+                for (int n = 0; n < F; n++) {
+                    const RowRef r = row_of(f1[l], n);
+                    sb[6 * D + n] = r.scale;
+                    sb[6 * D + F + n] = r.bias;
+                }
+                ck(cudaMemcpy(dec->d_pfw + dec->pf_w_layer * l, wl.data(), wl.size(), cudaMemcpyHostToDevice),
+                   "upload prefill weights");
+                ck(cudaMemcpy(dec->d_pfsb + dec->pf_sb_layer * l, sbl.data(), sbl.size() * 4, cudaMemcpyHostToDevice),
+                   "upload prefill scales");
+            }
+            dec->d_pfx = dmalloc<float>((size_t)kPrefillTokens * D);
+            dec->d_pfq = dmalloc<float>((size_t)kPrefillTokens * D);
+            dec->d_pfa = dmalloc<int8_t>((size_t)kPrefillTokens * 4 * D);
+            dec->d_pfh = dmalloc<int8_t>((size_t)kPrefillTokens * 4 * F);
+            const int nmax = std::max(3 * D, F);
+            dec->d_pfacc = dmalloc<unsigned long long>((size_t)kPrefillTokens * nmax);
+            ck(cudaMemset(dec->d_pfacc, 0, (size_t)kPrefillTokens * nmax * 8), "clear prefill sums");
+            dec->d_pfcnt = dmalloc<unsigned int>(nmax / kTile);
+            ck(cudaMemset(dec->d_pfcnt, 0, (size_t)(nmax / kTile) * 4), "clear prefill counters");
+        }
 
         // paged KV: pages in reverse physical order so the page table is exercised
         dec->n_pages = (max_ctx + kPageTokens - 1) / kPageTokens;
@@ -701,6 +768,78 @@ int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_promp
     return 0;
 }
 
+// K slices (CTAs) per 16-row tile: about 256 CTAs per GEMV, a slice at most 32 k-blocks (4 per
+// warp) and, where the shape allows, at least 16 (two per warp)
+static PrefillGemv with_split(PrefillGemv g) {
+    const int tiles = g.N / kTile, nkb = g.K / 32;
+    const int lo = (nkb + 31) / 32;
+    g.nsplit = std::max(lo, std::min(std::max(1, nkb / 16), 256 / tiles));
+    return g;
+}
+
+int xdna_opt_prefill(XdnaOptDecoder *dec, int start_pos, int n, void *stream) {
+    if (!dec) { set_err("xdna_opt_prefill: decoder is null"); return -1; }
+    if (!dec->prefill) { set_err("xdna_opt_prefill: the decoder was created with XDNA_OPT_PREFILL=0"); return -1; }
+    if (start_pos < 0 || n < 0 || start_pos + n > dec->max_ctx) {
+        set_err("xdna_opt_prefill: positions out of range (start_pos + n must be <= max_ctx)");
+        return -1;
+    }
+    const XdnaOptConfig &c = dec->cfg;
+    const int D = c.d_model, F = c.ffn, L = c.n_layers, H = c.n_heads;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSetDevice(dec->dev->ordinal);
+    for (int p0 = start_pos; e == cudaSuccess && p0 < start_pos + n; p0 += kPrefillTokens) {
+        const int T = std::min(kPrefillTokens, start_pos + n - p0);
+        e = launch_prefill_embed(dec->d_tokens, p0, T, D, c.vocab, dec->d_emb, dec->d_pos, dec->d_pfx, dec->d_state, st);
+        for (int l = 0; l < L && e == cudaSuccess; l++) {
+            const int8_t *wl = dec->d_pfw + dec->pf_w_layer * l;
+            const float *sb = dec->d_pfsb + dec->pf_sb_layer * l;
+            const float *ln = dec->d_ln + (size_t)l * 4 * D;
+            PrefillGemv g{};
+            g.acc = dec->d_pfacc;
+            g.cnt = dec->d_pfcnt;
+            g.T = T;
+            g.x = dec->d_pfx;
+            g.q = dec->d_pfq;
+            g.kv = dec->d_kv;
+            g.pt = dec->d_pt;
+            g.layer = l;
+            g.n_phys = dec->n_pages;
+            g.n_heads = H;
+            g.pos0 = p0;
+            g.D = D;
+            // LN1 -> q | k | v (K / V rows into the cache)
+            e = launch_prefill_ln(dec->d_pfx, T, D, ln, ln + D, c.eps, dec->h_fix[2 * L + l], dec->d_pfa, st);
+            g.w = wl; g.sc = sb; g.bi = sb + 3 * D; g.limbs = dec->d_pfa;
+            g.K = D; g.N = 3 * D; g.fix = dec->h_fix[2 * L + l]; g.mode = PF_QKV;
+            if (e == cudaSuccess) e = launch_prefill_gemv(with_split(g), st);
+            // attention -> context limbs -> x += out projection
+            if (e == cudaSuccess)
+                e = launch_prefill_attn(dec->d_pfq, dec->d_kv, dec->d_pt, l, dec->n_pages, H, p0, T, D, dec->h_fix[l],
+                                        dec->d_pfa, st);
+            g.w = wl + (size_t)3 * D * D; g.sc = dec->d_osb + (size_t)l * 2 * D; g.bi = g.sc + D;
+            g.K = D; g.N = D; g.fix = dec->h_fix[l]; g.mode = PF_RESID;
+            if (e == cudaSuccess) e = launch_prefill_gemv(with_split(g), st);
+            // LN2 -> fc1 + ReLU -> x += fc2
+            if (e == cudaSuccess)
+                e = launch_prefill_ln(dec->d_pfx, T, D, ln + 2 * D, ln + 3 * D, c.eps, dec->h_fix[3 * L + l],
+                                      dec->d_pfa, st);
+            g.w = wl + (size_t)4 * D * D; g.sc = sb + 6 * D; g.bi = sb + 6 * D + F; g.limbs = dec->d_pfa;
+            g.K = D; g.N = F; g.fix = dec->h_fix[3 * L + l]; g.mode = PF_FC1;
+            g.limbs_out = dec->d_pfh; g.fix_out = dec->h_fix[L + l];
+            if (e == cudaSuccess) e = launch_prefill_gemv(with_split(g), st);
+            g.w = wl + (size_t)4 * D * D + (size_t)F * D; g.sc = dec->d_f2sb + (size_t)l * 2 * D; g.bi = g.sc + D;
+            g.limbs = dec->d_pfh; g.K = F; g.N = D; g.fix = dec->h_fix[L + l]; g.mode = PF_RESID;
+            if (e == cudaSuccess) e = launch_prefill_gemv(with_split(g), st);
+        }
+    }
+    if (e != cudaSuccess) {
+        set_err(std::string("xdna_opt_prefill: ") + cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
 int xdna_opt_sync(XdnaOptDecoder *dec, void *stream) {
     if (!dec) { set_err("xdna_opt_sync: decoder is null"); return -1; }
     cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
@@ -755,8 +894,13 @@ int xdna_opt_generate(XdnaOptDecoder *dec, const int64_t *prompt, size_t n_promp
         cudaStream_t st = nullptr;
         ck(cudaMemcpyAsync(dec->d_tokens, prompt, n_prompt * sizeof(int64_t), cudaMemcpyHostToDevice, st),
            "copy prompt");
-        const int n_steps = (int)(n_prompt + n_new - 1);
-        if (xdna_opt_launch(dec, 0, n_steps, (int)n_prompt, out_logits ? dec->d_logits : nullptr, st) != 0)
+        // the prompt's positions before the last one as a batch (their K / V rows only), then the
+        // decode kernel from the last prompt position; without the batched path every position
+        // is a decode step
+        const int start = dec->prefill ? (int)n_prompt - 1 : 0;
+        if (start > 0 && xdna_opt_prefill(dec, 0, start, st) != 0) return -1;
+        const int n_steps = (int)(n_prompt + n_new - 1) - start;
+        if (xdna_opt_launch(dec, start, n_steps, (int)n_prompt, out_logits ? dec->d_logits : nullptr, st) != 0)
             return -1;
         ck(cudaMemcpyAsync(out_ids, dec->d_tokens + n_prompt, n_new * sizeof(int64_t), cudaMemcpyDeviceToHost, st),
            "copy ids");
