@@ -345,22 +345,44 @@ __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const 
 // with this layer's K at column koff + h*64 and V at koff + D + h*64.  The chunk's K and V
 // rows are staged in shared memory with 16-byte loads first.
 constexpr int XCH = 128;
+// set by a kernel whose bounded wait expired; read and cleared by the synchronous entry points
+__device__ unsigned int g_wdec_error;
 // The cross K/V of one layer, head-major: ckl[b][h][K | V][T][64] bf16 (cross_relayout_kernel), so
 // a split's 128 keys are one contiguous 16 KB block of K and one of V.
 __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const uint16_t *ckl, int T, float *part,
                                                          int nsplit) {
-    __shared__ __align__(16) uint16_t ks[XCH * HD], vs[XCH * HD];
+    __shared__ __align__(128) uint16_t ks[XCH * HD], vs[XCH * HD];
     __shared__ float qs[HD], sc[XCH], red[4], pacc[2][HD];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int ok_s;
     const int h = blockIdx.x, b = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
     const int jn = min(XCH, T - s * XCH);
-    const uint4 *kb = reinterpret_cast<const uint4 *>(ckl + (((size_t)b * H + h) * 2 * T + (size_t)s * XCH) * HD);
-    const uint4 *vb = kb + (size_t)T * HD / 8;
-    for (int i = tid; i < jn * 8; i += 128) {
-        reinterpret_cast<uint4 *>(ks)[i] = kb[i];
-        reinterpret_cast<uint4 *>(vs)[i] = vb[i];
+    const uint16_t *kb = ckl + (((size_t)b * H + h) * 2 * T + (size_t)s * XCH) * HD;
+    const uint16_t *vb = kb + (size_t)T * HD;
+    // the chunk's K and V rows are contiguous (head-major relayout): two bulk copies
+    // (cp.async.bulk, no multicast) complete on one mbarrier while q is read
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        const uint32_t bytes = (uint32_t)jn * HD * 2;
+        mbar_arrive_expect_tx(&bar, 2 * bytes);
+        bulk_g2s(ks, kb, bytes, &bar);
+        bulk_g2s(vs, vb, bytes, &bar);
+        ok_s = 1;
     }
     if (tid < HD) qs[tid] = q[(size_t)b * D + h * HD + tid];
     __syncthreads();
+    if (!mbar_try_wait(&bar, 0)) {          // bounded: 1 s, then the launch is reported failed
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&bar, 0))
+            if (globaltimer_ns() - t0 > 1000000000ull) {
+                atomicCAS(&g_wdec_error, 0u, 1u);
+                ok_s = 0;
+                break;
+            }
+    }
+    __syncthreads();
+    if (!ok_s) return;
     float v = -INFINITY;
     if (tid < jn) {
         const uint4 *kr = reinterpret_cast<const uint4 *>(ks + tid * HD);
@@ -779,6 +801,15 @@ cudaError_t step(XdnaWhisperDec *m, int B, int n_prompt, int n_new, float *lrec,
 }
 }  // namespace
 
+// true (and cleared) if a decoder kernel's bounded wait expired since the last check
+static bool wdec_error_and_clear() {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, wdec::g_wdec_error, sizeof v) != cudaSuccess || !v) return false;
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(wdec::g_wdec_error, &z, sizeof z);
+    return true;
+}
+
 extern "C" {
 
 XdnaWhisperDec *xdna_whisper_dec_create(XdnaDevice *dev_unused, const XdnaWhisperDecConfig *cfg,
@@ -995,6 +1026,10 @@ int xdna_whisper_dec_step_slots(XdnaWhisperDec *m, int n_slots, const int64_t *t
         if (!e) graphs.push_back({n_slots, g});
     }
     if (!e) e = cudaMemcpy(next, m->snext, sizeof(int64_t) * n_slots, cudaMemcpyDeviceToHost);
+    if (!e && wdec_error_and_clear()) {
+        set_last_error_message("xdna_whisper_dec_step_slots: a cross-attention copy wait expired");
+        return -1;
+    }
     if (!e && logits) e = cudaMemcpy(logits, m->slog, sizeof(float) * n_slots * (size_t)c.vocab, cudaMemcpyDeviceToHost);
     if (e) { set_last_error_message(std::string("xdna_whisper_dec_step_slots: ") + cudaGetErrorString(e)); return -1; }
     return 0;
@@ -1083,6 +1118,10 @@ int xdna_whisper_dec_generate(XdnaWhisperDec *m, const float *enc_host, int B, c
         ck(cudaMemcpy(tokens_host, m->tok_out, sizeof(int64_t) * B * n_new, cudaMemcpyDeviceToHost), "copy tokens");
         if (lg) ck(cudaMemcpy(logits_host, lg, sizeof(float) * B * n_new * m->cfg.vocab, cudaMemcpyDeviceToHost), "copy logits");
         if (gemm_error_and_clear()) { set_last_error_message("xdna_whisper_dec_generate: a GEMM wait expired"); return -1; }
+        if (wdec_error_and_clear()) {
+            set_last_error_message("xdna_whisper_dec_generate: a cross-attention copy wait expired");
+            return -1;
+        }
         return 0;
     } catch (const std::exception &ex) {
         set_last_error_message(std::string("xdna_whisper_dec_generate: ") + ex.what());
