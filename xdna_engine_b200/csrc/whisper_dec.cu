@@ -275,6 +275,19 @@ __global__ void ln_kernel(const float *__restrict__ x, int B, const float *__res
 // 242-278): appends this position's k, v (bf16) to the cache, stages the head's cached K and V
 // in shared memory with 16-byte loads, then scores / softmax / P.V from there.  qkv f32
 // [B][3D]; cache [B][H][max_tgt][64] (K) and the same for V; ctx bf16 [B][D].
+// set by a kernel whose bounded wait expired; read and cleared by the synchronous entry points
+__device__ unsigned int g_wdec_error;
+// bounded wait on a bulk-copy mbarrier (1 s): false, with the error word set, when it expires
+__device__ __forceinline__ bool wait_copy(uint64_t *bar) {
+    if (mbar_try_wait(bar, 0)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, 0))
+        if (globaltimer_ns() - t0 > 1000000000ull) {
+            atomicCAS(&g_wdec_error, 0u, 1u);
+            return false;
+        }
+    return true;
+}
 constexpr int SA_MAX = 448;
 constexpr int SA_SMEM = 2 * SA_MAX * HD * 2;
 __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const int *posp, int pos_stride, int max_tgt,
@@ -291,11 +304,22 @@ __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const 
     const size_t cb = ((size_t)b * H + h) * max_tgt * HD;
     const int S = pos + 1;
     uint16_t *ks = kvs, *vs = kvs + SA_MAX * HD;
-    // cached rows 0 .. pos-1 (16-byte pieces), and this position's row from the projection
-    for (int i = tid; i < pos * (HD / 8); i += 128) {
-        reinterpret_cast<uint4 *>(ks)[i] = reinterpret_cast<const uint4 *>(kc + cb)[i];
-        reinterpret_cast<uint4 *>(vs)[i] = reinterpret_cast<const uint4 *>(vc + cb)[i];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int ok_s;
+    // cached rows 0 .. pos-1 (contiguous: two bulk copies on one mbarrier), and this position's
+    // row from the projection
+    if (tid == 0) {
+        ok_s = 1;
+        if (pos > 0) {
+            mbar_init(&bar, 1);
+            mbar_fence_init();
+            const uint32_t bytes = (uint32_t)pos * HD * 2;
+            mbar_arrive_expect_tx(&bar, 2 * bytes);
+            bulk_g2s(ks, kc + cb, bytes, &bar);
+            bulk_g2s(vs, vc + cb, bytes, &bar);
+        }
     }
+    __syncthreads();
     if (tid < HD) {
         q[tid] = r[tid];
         const uint16_t kb = (uint16_t)bf16bits(r[D + tid]), vb = (uint16_t)bf16bits(r[2 * D + tid]);
@@ -304,7 +328,9 @@ __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const 
         ks[pos * HD + tid] = kb;
         vs[pos * HD + tid] = vb;
     }
+    if (pos > 0 && !wait_copy(&bar)) ok_s = 0;
     __syncthreads();
+    if (!ok_s) return;
     float mx = -INFINITY;
     for (int j = tid; j < S; j += 128) {
         const uint4 *kr = reinterpret_cast<const uint4 *>(ks + j * HD);
@@ -343,10 +369,8 @@ __global__ void __launch_bounds__(128) self_attn_kernel(const float *qkv, const 
 // Cross attention, split: block (h, b, s) takes encoder positions [128 s, 128 s + 128) and
 // writes (max, sum, acc[64]); cross_merge folds the splits in order.  kv rows: [B][T_enc][ldkv]
 // with this layer's K at column koff + h*64 and V at koff + D + h*64.  The chunk's K and V
-// rows are staged in shared memory with 16-byte loads first.
+// rows are staged in shared memory by bulk copies first.
 constexpr int XCH = 128;
-// set by a kernel whose bounded wait expired; read and cleared by the synchronous entry points
-__device__ unsigned int g_wdec_error;
 // The cross K/V of one layer, head-major: ckl[b][h][K | V][T][64] bf16 (cross_relayout_kernel), so
 // a split's 128 keys are one contiguous 16 KB block of K and one of V.
 __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const uint16_t *ckl, int T, float *part,
@@ -372,15 +396,7 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const float *q, const u
     }
     if (tid < HD) qs[tid] = q[(size_t)b * D + h * HD + tid];
     __syncthreads();
-    if (!mbar_try_wait(&bar, 0)) {          // bounded: 1 s, then the launch is reported failed
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&bar, 0))
-            if (globaltimer_ns() - t0 > 1000000000ull) {
-                atomicCAS(&g_wdec_error, 0u, 1u);
-                ok_s = 0;
-                break;
-            }
-    }
+    if (!wait_copy(&bar)) ok_s = 0;          // bounded: 1 s, then the launch is reported failed
     __syncthreads();
     if (!ok_s) return;
     float v = -INFINITY;
@@ -1027,7 +1043,7 @@ int xdna_whisper_dec_step_slots(XdnaWhisperDec *m, int n_slots, const int64_t *t
     }
     if (!e) e = cudaMemcpy(next, m->snext, sizeof(int64_t) * n_slots, cudaMemcpyDeviceToHost);
     if (!e && wdec_error_and_clear()) {
-        set_last_error_message("xdna_whisper_dec_step_slots: a cross-attention copy wait expired");
+        set_last_error_message("xdna_whisper_dec_step_slots: an attention copy wait expired");
         return -1;
     }
     if (!e && logits) e = cudaMemcpy(logits, m->slog, sizeof(float) * n_slots * (size_t)c.vocab, cudaMemcpyDeviceToHost);
@@ -1119,7 +1135,7 @@ int xdna_whisper_dec_generate(XdnaWhisperDec *m, const float *enc_host, int B, c
         if (lg) ck(cudaMemcpy(logits_host, lg, sizeof(float) * B * n_new * m->cfg.vocab, cudaMemcpyDeviceToHost), "copy logits");
         if (gemm_error_and_clear()) { set_last_error_message("xdna_whisper_dec_generate: a GEMM wait expired"); return -1; }
         if (wdec_error_and_clear()) {
-            set_last_error_message("xdna_whisper_dec_generate: a cross-attention copy wait expired");
+            set_last_error_message("xdna_whisper_dec_generate: an attention copy wait expired");
             return -1;
         }
         return 0;
