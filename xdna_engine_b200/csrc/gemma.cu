@@ -911,9 +911,10 @@ struct XdnaGemma {
     uint32_t *ebase = nullptr;             // device: epoch base of this step's exchanges
     struct Graph {
         int B, n_prompt, n_new;
+        bool lm;                          // false: a prompt step (no LM head)
         cudaGraphExec_t exec;
     };
-    std::vector<Graph> graphs;            // one decode step per staged shape
+    std::vector<Graph> graphs;            // one decode step per staged shape and step kind
     cudaStream_t cap = nullptr;
     std::vector<void *> owned;
     ~XdnaGemma() {
@@ -1116,7 +1117,10 @@ cudaError_t allreduce(XdnaGemma *m, const float *y, int B, float *out, uint32_t 
     return cudaGetLastError();
 }
 
-cudaError_t step(XdnaGemma *m, int B, int n_prompt, int n_new, cudaStream_t st) {
+// One decode step of B streams.  A step at a position before the prompt's last needs no LM head
+// (the pick kernel takes the prompt's next token), so with lm == false the LM-head GEMV and the
+// argmax exchange are left out.
+cudaError_t step(XdnaGemma *m, int B, int n_prompt, int n_new, cudaStream_t st, bool lm = true) {
     using namespace gm;
     const auto &c = m->cfg;
     const float eps = c.eps;
@@ -1149,12 +1153,14 @@ cudaError_t step(XdnaGemma *m, int B, int n_prompt, int n_new, cudaStream_t st) 
         post_add_norm_kernel<kNPL><<<(B + 3) / 4, 128, 0, st>>>(yin, B, nrm + 3 * kD + 2 * HD, wnext, eps, m->x, m->xn);
     }
     if (e) return e;
-    if ((e = gemv(m, m->lm, m->xn, B, OUT_ARGMAX, nullptr, nullptr, 0, st))) return e;
-    unpack_best_kernel<<<1, MAXB, 0, st>>>(m->lmbest, B, m->bestv + m->rank * MAXB,
-                                            m->besti + m->rank * MAXB);
-    if (m->tp > 1)
-        tp_gather_best_kernel<<<1, 2 * MAXB, 0, st>>>(B, m->dbufs, m->tp, m->rank, m->ebase, ++ex, m->bestv, m->besti,
-                                                     m->err);
+    if (lm) {
+        if ((e = gemv(m, m->lm, m->xn, B, OUT_ARGMAX, nullptr, nullptr, 0, st))) return e;
+        unpack_best_kernel<<<1, MAXB, 0, st>>>(m->lmbest, B, m->bestv + m->rank * MAXB,
+                                                m->besti + m->rank * MAXB);
+        if (m->tp > 1)
+            tp_gather_best_kernel<<<1, 2 * MAXB, 0, st>>>(B, m->dbufs, m->tp, m->rank, m->ebase, ++ex, m->bestv,
+                                                         m->besti, m->err);
+    }
     pick_kernel<<<1, MAXB, 0, st>>>(m->bestv, m->besti, m->tp == 1 ? 1 : m->tp, B, m->prompt, n_prompt, m->pos, m->tok,
                                     m->out, n_new, m->done, m->ebase, ex);
     return cudaGetLastError();
@@ -1418,23 +1424,25 @@ int xdna_gemma_steps(XdnaGemma *m, int n_steps, void *stream) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // the first step of a staged shape runs eagerly and is then recorded as a graph (positions,
     // tokens and exchange epochs live on the device); later steps replay the graph
-    XdnaGemma::Graph *g = nullptr;
-    for (auto &x : m->graphs)
-        if (x.B == m->run_B && x.n_prompt == m->run_prompt && x.n_new == m->run_new) g = &x;
     for (int s = 0; s < n_steps; s++) {
         cudaError_t e;
+        // positions before the prompt's last skip the LM head (the host counts the steps)
+        const bool lm = m->run_done >= m->run_prompt - 1;
+        XdnaGemma::Graph *g = nullptr;
+        for (auto &x : m->graphs)
+            if (x.B == m->run_B && x.n_prompt == m->run_prompt && x.n_new == m->run_new && x.lm == lm) g = &x;
         if (g) {
             e = cudaGraphLaunch(g->exec, st);
         } else {
-            e = step(m, m->run_B, m->run_prompt, m->run_new, st);
+            e = step(m, m->run_B, m->run_prompt, m->run_new, st, lm);
             if (!e) {
-                m->graphs.push_back({m->run_B, m->run_prompt, m->run_new, nullptr});
+                m->graphs.push_back({m->run_B, m->run_prompt, m->run_new, lm, nullptr});
                 g = &m->graphs.back();
                 if (!m->cap) e = cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking);
                 cudaGraph_t graph = nullptr;
                 if (!e) e = cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal);
                 if (!e) {
-                    const cudaError_t e2 = step(m, m->run_B, m->run_prompt, m->run_new, m->cap);
+                    const cudaError_t e2 = step(m, m->run_B, m->run_prompt, m->run_new, m->cap, lm);
                     e = cudaStreamEndCapture(m->cap, &graph);
                     if (!e) e = e2;
                 }
