@@ -273,7 +273,7 @@ __global__ void ln_kernel(const float *__restrict__ x, int B, const float *__res
 
 // Self attention of (head h, stream b) over positions 0..pos (attend_one, whisper_decoder.rs:
 // 242-278): appends this position's k, v (bf16) to the cache, stages the head's cached K and V
-// in shared memory with 16-byte loads, then scores / softmax / P.V from there.  qkv f32
+// in shared memory by bulk copies, then scores / softmax / P.V from there.  qkv f32
 // [B][3D]; cache [B][H][max_tgt][64] (K) and the same for V; ctx bf16 [B][D].
 // set by a kernel whose bounded wait expired; read and cleared by the synchronous entry points
 __device__ unsigned int g_wdec_error;
