@@ -275,8 +275,10 @@ int xdna_opt_launch(XdnaOptDecoder *dec, int start_pos, int n_steps, int n_promp
  * launch sequence, with exactly the decode kernel's arithmetic (the cache, and every later
  * token, are bit-identical to launching those positions).  No LM head: follow with
  * xdna_opt_launch from start_pos + n.  Asynchronous on `stream`; bad token ids are reported by
- * xdna_opt_sync.  xdna_opt_generate uses it for all prompt positions but the last.  Returns 0,
- * or -1 (also when the decoder was created with XDNA_OPT_PREFILL=0). */
+ * xdna_opt_sync.  xdna_opt_generate uses it for all prompt positions but the last.  It uses the
+ * decoder's own scratch (split-K sums, counters), so a decoder takes one prefill or launch at a
+ * time, on one stream.  Returns 0, or -1 (also when the decoder was created with
+ * XDNA_OPT_PREFILL=0). */
 int xdna_opt_prefill(XdnaOptDecoder *dec, int start_pos, int n, void *stream);
 /* Wait for the decoder's launches on `stream` and report a device-side failure (bounded
  * waits that expired).  Returns 0, or -1 with xdna_last_error() set. */
